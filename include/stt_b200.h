@@ -1,0 +1,226 @@
+/*
+ * stt_b200.h — C ABI of the B200-native (sm_100a) STT-1B decode step.
+ *
+ * This library replaces the GPU half of the stt-wasm crate of stt-web: the Q4 weight
+ * store and loader (crates/stt-wasm/src/gguf.rs), the transformer step
+ * (crates/stt-wasm/src/model.rs) and the delayed-streams step loop
+ * (crates/stt-wasm/src/stream.rs).  Every entry point below names the reference
+ * interface it replaces (path:line inside the stt-web project).
+ *
+ * Conventions
+ *  - Every call returns an int status: STT_OK (0) or a negative STT_E_* code.  The text of
+ *    the last error on the calling thread is available from stt_last_error().
+ *  - No C++ exception crosses this boundary.  Host buffers are owned by the caller and are
+ *    only read/written during the call.  Pointers documented as "device" must be CUDA device
+ *    pointers on the model's device.
+ *  - A model handle is bound to one CUDA device.  Calls on one handle (and on the stream
+ *    sets created from it) are not thread-safe: the caller serialises them.  The multi-GPU
+ *    pattern is one host thread per device, each with its own model.
+ *  - Sizes are those of the loaded GGUF file; the defaults match kyutai/stt-1b-en_fr.
+ */
+#ifndef STT_B200_H
+#define STT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (the reference reports anyhow::Result errors at load, gguf.rs:204-310,
+ *      and panics on shape, launch and index errors, gguf.rs:521-529, 562-568, 620-621) ---- */
+#define STT_OK 0
+#define STT_E_INVALID_ARG (-1)  /* bad pointer, size, stream id or token id              */
+#define STT_E_FORMAT (-2)       /* malformed or unsupported GGUF content                 */
+#define STT_E_OOM (-3)          /* host or device allocation failed                      */
+#define STT_E_CUDA (-4)         /* a CUDA runtime call failed                            */
+#define STT_E_DEVICE_FLAG (-5)  /* a kernel raised its error word (bad index / timeout)  */
+#define STT_E_STATE (-6)        /* call not valid in the current state (e.g. position    */
+                                /* past max_seq_len, which panics in the reference)      */
+
+/* Model hyper-parameters.  Mirrors SttConfig (crates/stt-wasm/src/lib.rs:27-58) field by
+ * field; stt_config_default() gives the values of SttConfig::default() (lib.rs:60-80). */
+typedef struct stt_config {
+    int32_t num_layers;          /* 16 */
+    int32_t hidden_size;         /* 2048 */
+    int32_t num_heads;           /* 16 */
+    int32_t num_kv_heads;        /* 16 (MHA) */
+    int32_t intermediate_size;   /* 5632: unused, as in the reference; FFN width comes from
+                                    the linear_in shape (model.rs:517-524) */
+    int32_t vocab_size;          /* 8000: text_linear rows */
+    int32_t text_in_vocab_size;  /* 8001: text_emb rows */
+    int32_t num_codebooks;       /* 32 */
+    int32_t audio_vocab_size;    /* 2049 */
+    int32_t text_delay;          /* 6 */
+    double rope_theta;           /* 100000.0 */
+    int32_t max_seq_len;         /* 4096: RoPE table length; positions beyond it are an error */
+    int32_t sliding_window;      /* 750: the KV ring holds sliding_window + 1 slots */
+    uint32_t text_padding_id;    /* 3 */
+    uint32_t text_start_token;   /* 8000 */
+} stt_config;
+
+/* Fills *cfg with SttConfig::default() (crates/stt-wasm/src/lib.rs:60-80). */
+void stt_config_default(stt_config* cfg);
+
+/* Storage type of the KV ring on the device. */
+#define STT_KV_BF16 0   /* default: bf16 K and V (half the bytes of the reference's f32)    */
+#define STT_KV_F32 1    /* f32 K and V, the reference's own precision (model.rs:185-192)    */
+
+typedef struct stt_model stt_model;      /* loaded weights on one device                    */
+typedef struct stt_streams stt_streams;  /* N independent streams: KV rings + step state    */
+typedef struct stt_q4_tensor stt_q4_tensor; /* one Q4_0 matrix in the device layout         */
+
+/* Read-only description of a loaded model. */
+typedef struct stt_model_info {
+    int32_t num_layers, hidden_size, num_heads, head_dim, ffn_hidden;
+    int32_t vocab_size, text_in_vocab_size, num_codebooks, audio_vocab_size;
+    int32_t embedding_dtype;     /* GGML dtype code of the embedding tables (0,1,2 or 30)  */
+    int32_t device;
+    uint64_t q4_weight_bytes;    /* Q4_0 bytes one decode step reads (all linear layers)   */
+    uint64_t device_bytes;       /* total device memory held by the model                  */
+} stt_model_info;
+
+/* ---------------------------------------------------------------------------------------
+ * Loading — replaces Q4ModelLoader::from_shards (gguf.rs:752-755) + load_deferred
+ * (gguf.rs:763-826) + Q4ModelParts::finalize (gguf.rs:658-692).
+ * The GGUF bytes may be split over several shards (ShardedCursor, gguf.rs:321-397).
+ * Tensor names, the dims-reversal rule (gguf.rs:83-85), the dtype checks (gguf.rs:880-882,
+ * 906-916) and the 32-byte data alignment (gguf.rs:34, 273-274) follow the reference.
+ * Embedding tables may be Q4_0 (the reference format, gguf.rs:616-633) or, as an
+ * extension, F32 / F16 / BF16 (GGML type 30).  cfg == NULL means stt_config_default().
+ * ------------------------------------------------------------------------------------- */
+int stt_model_load_gguf(const uint8_t* const* shards, const size_t* shard_lens, int n_shards,
+                        int device, const stt_config* cfg, stt_model** out);
+int stt_model_destroy(stt_model* model);
+int stt_model_get_info(const stt_model* model, stt_model_info* out);
+
+/* ---------------------------------------------------------------------------------------
+ * Streams — replaces SttModel::create_cache (model.rs:728-738) plus one SttStream::new
+ * (stream.rs:53-64) per stream.  Each stream owns a ring of sliding_window + 1 K/V slots per
+ * layer (model.rs:130-153) and the stream-loop state of stream.rs:20-41.
+ * kv_dtype is STT_KV_BF16 or STT_KV_F32.
+ * ------------------------------------------------------------------------------------- */
+int stt_streams_create(stt_model* model, int n_streams, int kv_dtype, stt_streams** out);
+int stt_streams_destroy(stt_streams* streams);
+
+/* Raw decode step over a batch — replaces SttModel::forward (model.rs:631-664) followed by
+ * logits.argmax(2) (stream.rs:104).  For each i < n, stream stream_ids[i] consumes
+ * audio_tokens[i*num_codebooks .. +num_codebooks] and text_tokens[i]; its KV ring and
+ * position advance by one.  Host buffers.  logits_out (n*vocab_size floats) and argmax_out
+ * (n values, lowest index on ties) may each be NULL.  Stream ids in one call are distinct. */
+int stt_forward(stt_streams* streams, const int32_t* stream_ids, int n,
+                const uint32_t* audio_tokens, const uint32_t* text_tokens,
+                float* logits_out, uint32_t* argmax_out);
+
+/* One frame of the delayed-streams loop — replaces SttStream::feed_frame (stream.rs:70-81):
+ * submit_frame (stream.rs:90-107) then resolve_pending_as_token (stream.rs:231-266),
+ * including the delay gating and the limit-cycle breaker.  *token_out is the emitted token,
+ * or -1 for the reference's None (a frame inside the text delay). */
+int stt_stream_feed_frame(stt_streams* streams, int stream_id, const uint32_t* audio_tokens,
+                          int32_t* token_out);
+
+/* The same frame step for n streams at once (one batched decode step).  tokens_out[i] is the
+ * token emitted by stream_ids[i] or -1. */
+int stt_streams_feed_frame(stt_streams* streams, const int32_t* stream_ids, int n,
+                           const uint32_t* audio_tokens, int32_t* tokens_out);
+
+/* n_frames consecutive feed_frame calls on one stream, run back to back on the device with
+ * the greedy token fed back on the device (the goal of submit_frame_gpu, stream.rs:117-138,
+ * with the exact feed_frame semantics).  audio_tokens holds n_frames*num_codebooks ids;
+ * tokens_out receives n_frames values (-1 = None).  Host buffers. */
+int stt_stream_feed_frames(stt_streams* streams, int stream_id, int n_frames,
+                           const uint32_t* audio_tokens, int32_t* tokens_out);
+
+/* Device-pointer variant of stt_stream_feed_frames: d_audio and d_tokens are device buffers,
+ * the work is queued on cuda_stream (a cudaStream_t, NULL = legacy default stream) and the
+ * call returns without synchronising.  The stream's host-side mirror of its state is
+ * refreshed by the next synchronous call on that stream. */
+int stt_stream_feed_frames_device(stt_streams* streams, int stream_id, int n_frames,
+                                  const uint32_t* d_audio, int32_t* d_tokens,
+                                  void* cuda_stream);
+
+/* Batched device-pointer frame step: stream_ids are host values, d_audio holds
+ * n*num_codebooks ids and d_tokens n outputs, both on the device; queued on cuda_stream. */
+int stt_streams_feed_frame_device(stt_streams* streams, const int32_t* stream_ids, int n,
+                                  const uint32_t* d_audio, int32_t* d_tokens,
+                                  void* cuda_stream);
+
+/* Replaces SttStream::flush (stream.rs:315-338): text_delay frames of zero audio through
+ * feed_frame, collecting the emitted tokens (at most text_delay).  *n_tokens receives the
+ * count written to tokens_out (capacity entries available). */
+int stt_stream_flush(stt_streams* streams, int stream_id, uint32_t* tokens_out, int capacity,
+                     int* n_tokens);
+
+/* Replaces SttStream::reset (stream.rs:341-349) when keep_buffers == 0 and
+ * SttStream::reset_keep_buffers (stream.rs:354-362) otherwise.  Both zero the state; the
+ * device ring is kept allocated in either case and zeroed when keep_buffers != 0. */
+int stt_stream_reset(stt_streams* streams, int stream_id, int keep_buffers);
+
+/* Replaces SttStream::set_last_text_token (stream.rs:190-192). */
+int stt_stream_set_last_text_token(stt_streams* streams, int stream_id, uint32_t token);
+
+/* Stream-loop state of one stream (stream.rs:20-41 and KVCache counters, model.rs:139-153). */
+typedef struct stt_stream_state {
+    int32_t offset;          /* absolute position (tokens seen), RoPE offset              */
+    int32_t len;             /* valid ring entries, <= sliding_window + 1                 */
+    int32_t write_pos;       /* next ring slot                                             */
+    int32_t frame_count;     /* frames submitted since reset                               */
+    uint32_t last_text_token;
+    uint32_t delay_prev[2];  /* limit-cycle history, 0xFFFFFFFF = none (stream.rs:62)       */
+} stt_stream_state;
+int stt_stream_get_state(stt_streams* streams, int stream_id, stt_stream_state* out);
+
+/* ---------------------------------------------------------------------------------------
+ * Isolated Q4_0 matmul — replaces Q4Tensor::from_q4_bytes (gguf.rs:418-451) and
+ * q4_matmul (gguf.rs:517-578, shader crates/stt-wasm/src/wgsl/shader_naive.wgsl:30-98).
+ * ------------------------------------------------------------------------------------- */
+/* Uploads raw Q4_0 bytes of an [n, k] matrix ((n*k/32)*18 bytes, k % 32 == 0) and repacks
+ * them into the device layout. */
+int stt_q4_tensor_create(const uint8_t* q4_bytes, size_t n_bytes, int n, int k, int device,
+                         stt_q4_tensor** out);
+int stt_q4_tensor_destroy(stt_q4_tensor* t);
+/* out[rows, n] = input[rows, k] x W^T with f32 host buffers (rows = B*M of the reference). */
+int stt_q4_matmul(const stt_q4_tensor* w, const float* input, int rows, float* out);
+/* Device variant: d_input is f32 [rows, k] (in_dtype 0) or bf16 [rows, k] (in_dtype 1);
+ * d_out is f32 [rows, n].  Queued on cuda_stream, no synchronisation. */
+int stt_q4_matmul_device(const stt_q4_tensor* w, const void* d_input, int in_dtype, int rows,
+                         float* d_out, void* cuda_stream);
+/* Dequantises the whole matrix to f32 on the device and copies it to out_host (n*k floats):
+ * out[r*k + j] = (nibble - 8) * f16_to_f32(scale), bit-exact with gguf.rs:616-633. */
+int stt_q4_tensor_dequant(const stt_q4_tensor* w, float* out_host);
+
+/* ---------------------------------------------------------------------------------------
+ * Synthetic model and inputs (no counterpart in the reference, which downloads the real
+ * checkpoint).  Weights are drawn N(mean, std) from Philox-4x32-10 keyed by (seed, tensor
+ * index) with a Box-Muller transform in f64, rounded to bf16, and Q4_0-quantised with the
+ * exact rules of scripts/quantize.py:65-116; the file layout follows quantize.py:119-199.
+ * ------------------------------------------------------------------------------------- */
+typedef struct stt_synth_params {
+    uint64_t seed;
+    int32_t num_layers, hidden_size, num_heads, ffn_hidden;
+    int32_t vocab_size, text_in_vocab_size, num_codebooks, audio_vocab_size;
+    int32_t embedding_dtype;     /* 30 = BF16 (default), 2 = Q4_0, 0 = F32                  */
+    float weight_std;            /* 0.02 */
+    float norm_mean, norm_std;   /* 1.0, 0.02 (alphas rounded to bf16, stored F32)          */
+    int32_t n_threads;           /* 0 = all host cores                                      */
+} stt_synth_params;
+void stt_synth_default(stt_synth_params* p);
+/* Writes a whole GGUF v3 file into a buffer allocated by the library (*out_buf, *out_len);
+ * release it with stt_synth_free. */
+int stt_synth_gguf(const stt_synth_params* p, uint8_t** out_buf, size_t* out_len);
+void stt_synth_free(uint8_t* buf);
+/* Q4_0-quantises n floats (n % 32 == 0) with the rules of scripts/quantize.py:65-116. */
+int stt_synth_quantize_q4_0(const float* x, size_t n, uint8_t* out);
+/* Seeded uniform audio tokens in [0, 2048): out[f*num_codebooks + c] for frames
+ * first_frame .. first_frame+n_frames-1 of stream `stream`. */
+int stt_synth_audio_tokens(uint64_t seed, int32_t stream, int32_t first_frame, int32_t n_frames,
+                           int32_t num_codebooks, uint32_t* out);
+
+/* Text of the last error on the calling thread ("" if none). */
+const char* stt_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* STT_B200_H */

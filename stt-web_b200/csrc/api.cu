@@ -1,0 +1,1018 @@
+// C ABI of libsttb200: model loading, stream sets, decode steps and the isolated Q4 matmul.
+// The entry points and the reference interfaces they replace are listed in include/stt_b200.h.
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "gguf.h"
+#include "kernels.h"
+#include "mega.h"
+
+namespace stt {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+void clear_error() { g_last_error.clear(); }
+
+#define CUDA_TRY(expr)                                                                              \
+    do {                                                                                            \
+        cudaError_t e_ = (expr);                                                                    \
+        if (e_ != cudaSuccess)                                                                      \
+            return set_error(STT_E_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_),    \
+                             __FILE__, __LINE__);                                                   \
+    } while (0)
+
+#define TRY(expr)                  \
+    do {                           \
+        int rc_ = (expr);          \
+        if (rc_ != STT_OK) return rc_; \
+    } while (0)
+
+// Restores the calling thread's current device on scope exit.
+struct DeviceScope {
+    int prev = 0;
+    bool ok = false;
+    explicit DeviceScope(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) ok = true;
+    }
+    ~DeviceScope() {
+        if (ok) cudaSetDevice(prev);
+    }
+};
+
+// Device buffer that grows on demand.
+struct DevBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+    int ensure(size_t bytes) {
+        if (bytes <= cap) return STT_OK;
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        CUDA_TRY(cudaMalloc(&p, bytes));
+        cap = bytes;
+        return STT_OK;
+    }
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+};
+
+// Pinned host buffer that grows on demand.
+struct HostBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    void release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+    }
+    int ensure(size_t bytes) {
+        if (bytes <= cap) return STT_OK;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        cap = 0;
+        CUDA_TRY(cudaHostAlloc(&p, bytes, cudaHostAllocDefault));
+        cap = bytes;
+        return STT_OK;
+    }
+    ~HostBuf() {
+        if (p) cudaFreeHost(p);
+    }
+};
+
+}  // namespace stt
+
+using namespace stt;
+
+// ------------------------------------------------------------------------------------ model
+
+struct stt_model {
+    int device = 0;
+    int num_sms = 148;
+    stt_config cfg{};
+    int32_t L = 0, D = 0, H = 0, HD = 0, F = 0, V = 0, TV = 0, AV = 0, NC = 0, ML = 0;
+    int32_t emb_type = 0, emb_row_bytes = 0;
+    void* d_mem = nullptr;  // weights, norms, embeddings, rope table
+    size_t device_bytes = 0;
+    uint64_t q4_bytes = 0;
+    std::vector<LayerDev> h_layers;
+    LayerDev* d_layers = nullptr;
+    Q4Dev head{};
+    const float* out_norm = nullptr;
+    const float2* rope = nullptr;
+    const uint8_t* emb_audio = nullptr;
+    const uint8_t* emb_text = nullptr;
+    float attn_scale = 0.0f;
+};
+
+extern "C" void stt_config_default(stt_config* c) {
+    if (!c) return;
+    c->num_layers = 16;
+    c->hidden_size = 2048;
+    c->num_heads = 16;
+    c->num_kv_heads = 16;
+    c->intermediate_size = 5632;
+    c->vocab_size = 8000;
+    c->text_in_vocab_size = 8001;
+    c->num_codebooks = 32;
+    c->audio_vocab_size = 2049;
+    c->text_delay = 6;
+    c->rope_theta = 100000.0;
+    c->max_seq_len = 4096;
+    c->sliding_window = 750;
+    c->text_padding_id = 3;
+    c->text_start_token = 8000;
+}
+
+extern "C" const char* stt_last_error(void) { return g_last_error.c_str(); }
+
+namespace {
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int require(const GgufFile& g, const std::string& name, const GgufTensor** out) {
+    *out = g.find(name);
+    if (!*out) return set_error(STT_E_FORMAT, "Tensor '%s' not found", name.c_str());
+    return STT_OK;
+}
+
+// Q4Linear checks of load_q4_linear (gguf.rs:873-888) and Q4Tensor::from_q4_bytes (gguf.rs:418-432),
+// plus the shape this build's kernels need.
+int check_q4(const GgufTensor* t, uint64_t rows, uint64_t cols) {
+    if (t->dtype != GGML_Q4_0)
+        return set_error(STT_E_FORMAT, "Expected Q4_0 for '%s', got dtype %u", t->name.c_str(), t->dtype);
+    if (t->dims.size() != 2)
+        return set_error(STT_E_FORMAT, "'%s' must be 2-D, has %zu dims", t->name.c_str(), t->dims.size());
+    const auto s = t->shape();
+    if (t->numel % 32 != 0)
+        return set_error(STT_E_FORMAT, "Q4_0 requires element count divisible by 32, got %llu",
+                         (unsigned long long)t->numel);
+    if (s[0] != rows || s[1] != cols)
+        return set_error(STT_E_FORMAT, "'%s' has shape [%llu, %llu], expected [%llu, %llu]", t->name.c_str(),
+                         (unsigned long long)s[0], (unsigned long long)s[1], (unsigned long long)rows,
+                         (unsigned long long)cols);
+    if (cols % 32 != 0 || cols > (uint64_t)kMaxGemvK)
+        return set_error(STT_E_FORMAT, "'%s': in_features %llu unsupported (multiple of 32, at most %d)",
+                         t->name.c_str(), (unsigned long long)cols, kMaxGemvK);
+    return STT_OK;
+}
+
+// load_rms_norm (gguf.rs:890-925): F32 or F16 (converted with gguf.rs f16_to_f32), Q4_0 rejected.
+int load_norm(const GgufFile& g, const GgufTensor* t, int32_t D, std::vector<float>& out) {
+    if (t->dtype == GGML_Q4_0)
+        return set_error(STT_E_FORMAT, "Cannot load Q4_0 tensor '%s' as norm weight", t->name.c_str());
+    if (t->dtype != GGML_F32 && t->dtype != GGML_F16)
+        return set_error(STT_E_FORMAT, "norm weight '%s' has unsupported dtype %u", t->name.c_str(), t->dtype);
+    if (t->numel != (uint64_t)D)
+        return set_error(STT_E_FORMAT, "norm weight '%s' has %llu elements, expected %d", t->name.c_str(),
+                         (unsigned long long)t->numel, D);
+    std::vector<uint8_t> scratch;
+    const uint8_t* p = g.tensor_data(*t, scratch);
+    if (!p) return STT_E_FORMAT;
+    out.resize(D);
+    for (int32_t i = 0; i < D; ++i) {
+        if (t->dtype == GGML_F32) std::memcpy(&out[i], p + 4 * i, 4);
+        else out[i] = f16_bits_to_f32_gguf((uint16_t)(p[2 * i] | (p[2 * i + 1] << 8)));
+    }
+    return STT_OK;
+}
+
+}  // namespace
+
+extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* shard_lens, int n_shards,
+                                   int device, const stt_config* cfg_in, stt_model** out) {
+    clear_error();
+    if (!out) return set_error(STT_E_INVALID_ARG, "out is NULL");
+    *out = nullptr;
+    stt_config cfg;
+    if (cfg_in) cfg = *cfg_in; else stt_config_default(&cfg);
+    if (cfg.num_layers <= 0 || cfg.num_layers > kMaxLayers || cfg.num_heads <= 0 || cfg.hidden_size <= 0 ||
+        cfg.num_codebooks <= 0 || cfg.num_codebooks > kMaxCodebooks || cfg.sliding_window < 0 ||
+        cfg.max_seq_len <= 0 || cfg.text_delay < 0)
+        return set_error(STT_E_INVALID_ARG, "invalid stt_config");
+    if (cfg.num_kv_heads != cfg.num_heads)
+        return set_error(STT_E_INVALID_ARG, "num_kv_heads (%d) != num_heads (%d): only MHA is supported",
+                         cfg.num_kv_heads, cfg.num_heads);
+    GgufFile g;
+    TRY(g.open(shards, shard_lens, n_shards));
+
+    auto m = std::make_unique<stt_model>();
+    m->device = device;
+    m->cfg = cfg;
+    m->L = cfg.num_layers;
+    m->H = cfg.num_heads;
+    m->NC = cfg.num_codebooks;
+    m->ML = cfg.sliding_window + 1;  // model.rs:730
+
+    // embeddings (gguf.rs:770-793): shape from the file, one dtype for all tables
+    const GgufTensor* text_emb;
+    TRY(require(g, "text_emb.weight", &text_emb));
+    if (text_emb->dims.size() != 2) return set_error(STT_E_FORMAT, "text_emb.weight must be 2-D");
+    m->TV = (int32_t)text_emb->shape()[0];
+    m->D = (int32_t)text_emb->shape()[1];
+    if (m->D != cfg.hidden_size)
+        return set_error(STT_E_FORMAT, "text_emb.weight width %d != hidden_size %d", m->D, cfg.hidden_size);
+    if (m->D % m->H != 0 || m->D / m->H != 128)
+        return set_error(STT_E_FORMAT, "head_dim %d unsupported (this build needs 128)", m->D / m->H);
+    m->HD = m->D / m->H;
+    m->emb_type = (int32_t)text_emb->dtype;
+    if (m->D % 32 != 0) return set_error(STT_E_FORMAT, "hidden size %d not a multiple of 32", m->D);
+    switch (m->emb_type) {
+        case GGML_Q4_0: m->emb_row_bytes = m->D / 32 * 18; break;
+        case GGML_F32: m->emb_row_bytes = m->D * 4; break;
+        default: m->emb_row_bytes = m->D * 2; break;
+    }
+    std::vector<const GgufTensor*> audio(m->NC);
+    for (int i = 0; i < m->NC; ++i) {
+        TRY(require(g, "emb." + std::to_string(i) + ".weight", &audio[i]));
+        const auto s = audio[i]->shape();
+        if (audio[i]->dims.size() != 2 || s[1] != (uint64_t)m->D || audio[i]->dtype != (uint32_t)m->emb_type)
+            return set_error(STT_E_FORMAT, "emb.%d.weight: shape/dtype differs from text_emb.weight", i);
+        if (i == 0) m->AV = (int32_t)s[0];
+        else if (s[0] != (uint64_t)m->AV) return set_error(STT_E_FORMAT, "emb.%d.weight has %llu rows, emb.0 has %d", i, (unsigned long long)s[0], m->AV);
+    }
+
+    // layers
+    struct LayerT { const GgufTensor *n1, *qkv, *out, *n2, *fin, *fout; };
+    std::vector<LayerT> lt(m->L);
+    for (int l = 0; l < m->L; ++l) {
+        const std::string p = "transformer.layers." + std::to_string(l) + ".";
+        TRY(require(g, p + "norm1.alpha", &lt[l].n1));
+        TRY(require(g, p + "self_attn.in_proj_weight", &lt[l].qkv));
+        TRY(require(g, p + "self_attn.out_proj.weight", &lt[l].out));
+        TRY(require(g, p + "norm2.alpha", &lt[l].n2));
+        TRY(require(g, p + "gating.linear_in.weight", &lt[l].fin));
+        TRY(require(g, p + "gating.linear_out.weight", &lt[l].fout));
+        if (l == 0) {
+            if (lt[0].fin->dims.size() != 2 || lt[0].fin->shape()[0] % 2 != 0)
+                return set_error(STT_E_FORMAT, "linear_in must have an even number of rows");
+            m->F = (int32_t)(lt[0].fin->shape()[0] / 2);  // model.rs:519-520
+        }
+        TRY(check_q4(lt[l].qkv, 3ull * m->D, m->D));
+        TRY(check_q4(lt[l].out, m->D, m->D));
+        TRY(check_q4(lt[l].fin, 2ull * m->F, m->D));
+        TRY(check_q4(lt[l].fout, m->D, m->F));
+    }
+    const GgufTensor *out_norm_t, *head_t;
+    TRY(require(g, "out_norm.alpha", &out_norm_t));
+    TRY(require(g, "text_linear.weight", &head_t));
+    if (head_t->dims.size() != 2) return set_error(STT_E_FORMAT, "text_linear.weight must be 2-D");
+    m->V = (int32_t)head_t->shape()[0];
+    TRY(check_q4(head_t, m->V, m->D));
+    if ((uint32_t)m->TV <= cfg.text_start_token || (uint32_t)m->TV <= cfg.text_padding_id)
+        return set_error(STT_E_FORMAT, "text_emb rows (%d) do not cover start/padding tokens", m->TV);
+
+    // norms (converted on the host)
+    std::vector<float> norms((size_t)(2 * m->L + 1) * m->D);
+    for (int l = 0; l < m->L; ++l) {
+        std::vector<float> a, b;
+        TRY(load_norm(g, lt[l].n1, m->D, a));
+        TRY(load_norm(g, lt[l].n2, m->D, b));
+        std::copy(a.begin(), a.end(), norms.begin() + (size_t)(2 * l) * m->D);
+        std::copy(b.begin(), b.end(), norms.begin() + (size_t)(2 * l + 1) * m->D);
+    }
+    {
+        std::vector<float> a;
+        TRY(load_norm(g, out_norm_t, m->D, a));
+        std::copy(a.begin(), a.end(), norms.begin() + (size_t)(2 * m->L) * m->D);
+    }
+
+    // RoPE table (RoPE::new, model.rs:34-59): f32 inverse frequencies, f32 angle, cos/sin.
+    const int half = m->HD / 2;
+    std::vector<float2> rope((size_t)cfg.max_seq_len * half);
+    {
+        std::vector<float> inv_freq(half);
+        for (int i = 0; i < half; ++i)
+            inv_freq[i] = 1.0f / std::pow((float)cfg.rope_theta, (float)(2 * i) / (float)m->HD);
+        for (int p = 0; p < cfg.max_seq_len; ++p)
+            for (int j = 0; j < half; ++j) {
+                const float f = (float)p * inv_freq[j];
+                rope[(size_t)p * half + j] = make_float2(std::cos(f), std::sin(f));
+            }
+    }
+    m->attn_scale = std::pow((float)m->HD, -0.5f);  // model.rs:411
+
+    // device memory plan
+    std::vector<const GgufTensor*> q4s;
+    for (int l = 0; l < m->L; ++l) {
+        q4s.push_back(lt[l].qkv);
+        q4s.push_back(lt[l].out);
+        q4s.push_back(lt[l].fin);
+        q4s.push_back(lt[l].fout);
+    }
+    q4s.push_back(head_t);
+    size_t off = 0;
+    std::vector<size_t> off_nib(q4s.size()), off_sc(q4s.size());
+    size_t max_raw = 0;
+    for (size_t i = 0; i < q4s.size(); ++i) {
+        const size_t nblk = q4s[i]->numel / 32;
+        off_nib[i] = off;
+        off = align_up(off + nblk * 16, 256);
+        off_sc[i] = off;
+        off = align_up(off + nblk * 2, 256);
+        m->q4_bytes += q4s[i]->nbytes;
+        max_raw = std::max<size_t>(max_raw, q4s[i]->nbytes);
+    }
+    const size_t off_norms = off;
+    off = align_up(off + norms.size() * sizeof(float), 256);
+    const size_t off_rope = off;
+    off = align_up(off + rope.size() * sizeof(float2), 256);
+    const size_t audio_table = (size_t)m->AV * m->emb_row_bytes;
+    const size_t off_emb = off;
+    off = align_up(off + audio_table * m->NC, 256);
+    const size_t off_text = off;
+    off = align_up(off + (size_t)m->TV * m->emb_row_bytes, 256);
+    const size_t off_layers = off;
+    off = align_up(off + sizeof(LayerDev) * m->L, 256);
+    m->device_bytes = off;
+
+    // Every tensor's bytes must lie inside the input (tensor_data, gguf.rs:298-310).
+    {
+        std::vector<const GgufTensor*> used(audio.begin(), audio.end());
+        used.push_back(text_emb);
+        used.push_back(out_norm_t);
+        used.push_back(head_t);
+        for (const auto& t : lt) {
+            used.push_back(t.n1); used.push_back(t.qkv); used.push_back(t.out);
+            used.push_back(t.n2); used.push_back(t.fin); used.push_back(t.fout);
+        }
+        for (const GgufTensor* t : used) {
+            const uint64_t abs = g.data_offset() + t->offset;
+            if (abs < g.data_offset() || abs > g.total_bytes() || t->nbytes > g.total_bytes() - abs)
+                return set_error(STT_E_FORMAT, "tensor '%s' data (%llu bytes at %llu) runs past the end of the file (%llu bytes)",
+                                 t->name.c_str(), (unsigned long long)t->nbytes, (unsigned long long)abs,
+                                 (unsigned long long)g.total_bytes());
+        }
+    }
+
+    // The file is fully validated above; only now touch the device.
+    int ndev = 0;
+    CUDA_TRY(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return set_error(STT_E_INVALID_ARG, "device %d out of range (%d devices)", device, ndev);
+    DeviceScope ds(device);
+    if (!ds.ok) return set_error(STT_E_CUDA, "cudaSetDevice(%d) failed", device);
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    m->num_sms = prop.multiProcessorCount;
+    if (cudaMalloc(&m->d_mem, off) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(STT_E_OOM, "cannot allocate %zu bytes on device %d", off, device);
+    }
+    uint8_t* base = static_cast<uint8_t*>(m->d_mem);
+    struct Cleanup {
+        stt_model* m;
+        bool armed = true;
+        ~Cleanup() {
+            if (armed && m->d_mem) cudaFree(m->d_mem);
+        }
+    } cleanup{m.get()};
+
+    // Q4 matrices: raw bytes -> staging -> repack into the two planes
+    {
+        DevBuf staging;
+        TRY(staging.ensure(max_raw));
+        std::vector<uint8_t> scratch;
+        std::vector<Q4Dev> qd(q4s.size());
+        for (size_t i = 0; i < q4s.size(); ++i) {
+            const uint8_t* src = g.tensor_data(*q4s[i], scratch);
+            if (!src) return STT_E_FORMAT;
+            CUDA_TRY(cudaMemcpy(staging.p, src, q4s[i]->nbytes, cudaMemcpyHostToDevice));
+            const auto s = q4s[i]->shape();
+            qd[i].nib = reinterpret_cast<const uint4*>(base + off_nib[i]);
+            qd[i].scale = reinterpret_cast<const uint16_t*>(base + off_sc[i]);
+            qd[i].n = (int32_t)s[0];
+            qd[i].k = (int32_t)s[1];
+            CUDA_TRY(launch_repack_q4(static_cast<const uint8_t*>(staging.p), (int64_t)(q4s[i]->numel / 32),
+                                      const_cast<uint4*>(qd[i].nib), const_cast<uint16_t*>(qd[i].scale), 0));
+            CUDA_TRY(cudaDeviceSynchronize());
+        }
+        m->h_layers.resize(m->L);
+        const float* dn = reinterpret_cast<const float*>(base + off_norms);
+        for (int l = 0; l < m->L; ++l) {
+            LayerDev& L = m->h_layers[l];
+            L.qkv = qd[4 * l + 0];
+            L.out = qd[4 * l + 1];
+            L.fin = qd[4 * l + 2];
+            L.fout = qd[4 * l + 3];
+            L.norm1 = dn + (size_t)(2 * l) * m->D;
+            L.norm2 = dn + (size_t)(2 * l + 1) * m->D;
+        }
+        m->head = qd.back();
+        m->out_norm = dn + (size_t)(2 * m->L) * m->D;
+    }
+    CUDA_TRY(cudaMemcpy(base + off_norms, norms.data(), norms.size() * sizeof(float), cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(base + off_rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    {
+        std::vector<uint8_t> scratch;
+        for (int i = 0; i < m->NC; ++i) {
+            const uint8_t* src = g.tensor_data(*audio[i], scratch);
+            if (!src) return STT_E_FORMAT;
+            CUDA_TRY(cudaMemcpy(base + off_emb + audio_table * i, src, audio_table, cudaMemcpyHostToDevice));
+        }
+        const uint8_t* src = g.tensor_data(*text_emb, scratch);
+        if (!src) return STT_E_FORMAT;
+        CUDA_TRY(cudaMemcpy(base + off_text, src, (size_t)m->TV * m->emb_row_bytes, cudaMemcpyHostToDevice));
+    }
+    CUDA_TRY(cudaMemcpy(base + off_layers, m->h_layers.data(), sizeof(LayerDev) * m->L, cudaMemcpyHostToDevice));
+    m->d_layers = reinterpret_cast<LayerDev*>(base + off_layers);
+    m->rope = reinterpret_cast<const float2*>(base + off_rope);
+    m->emb_audio = base + off_emb;
+    m->emb_text = base + off_text;
+    CUDA_TRY(configure_kernels());
+    CUDA_TRY(configure_mega());
+    CUDA_TRY(cudaDeviceSynchronize());
+    cleanup.armed = false;
+    *out = m.release();
+    return STT_OK;
+}
+
+extern "C" int stt_model_destroy(stt_model* m) {
+    if (!m) return STT_OK;
+    {
+        DeviceScope ds(m->device);
+        if (m->d_mem) cudaFree(m->d_mem);
+    }
+    delete m;
+    return STT_OK;
+}
+
+extern "C" int stt_model_get_info(const stt_model* m, stt_model_info* o) {
+    if (!m || !o) return set_error(STT_E_INVALID_ARG, "NULL argument");
+    o->num_layers = m->L;
+    o->hidden_size = m->D;
+    o->num_heads = m->H;
+    o->head_dim = m->HD;
+    o->ffn_hidden = m->F;
+    o->vocab_size = m->V;
+    o->text_in_vocab_size = m->TV;
+    o->num_codebooks = m->NC;
+    o->audio_vocab_size = m->AV;
+    o->embedding_dtype = m->emb_type;
+    o->device = m->device;
+    o->q4_weight_bytes = m->q4_bytes;
+    o->device_bytes = m->device_bytes;
+    return STT_OK;
+}
+
+// ------------------------------------------------------------------------------------ streams
+
+struct stt_streams {
+    stt_model* m = nullptr;
+    int S = 0;
+    int kv_f32 = 0;
+    void* d_kv = nullptr;
+    size_t kv_stream_bytes = 0;
+    StreamState* d_state = nullptr;
+    std::vector<StreamState> h_state;
+    bool state_stale = false;
+    // scratch, sized for S batch rows
+    float *d_x = nullptr, *d_qkv = nullptr, *d_attn = nullptr, *d_hid = nullptr, *d_logits = nullptr, *d_part = nullptr;
+    uint32_t* d_tickets = nullptr;
+    int32_t* d_ids = nullptr;
+    StepDesc* d_desc = nullptr;
+    DevBuf in_audio, in_text, out_tokens, out_logits;
+    HostBuf h_stage, h_tokens;
+    void* d_scratch = nullptr;
+    cudaStream_t stream = nullptr;
+    std::map<int, cudaGraphExec_t> graphs;
+    MegaState mega;
+};
+
+namespace {
+
+int nsplit_for(const stt_model* m, int n) {
+    const int want = (2 * m->num_sms + n * m->H - 1) / (n * m->H);
+    return std::max(1, std::min(32, want));
+}
+
+StreamState fresh_state(const stt_model* m) {
+    StreamState s{};
+    s.last_text = m->cfg.text_start_token;
+    s.prev0 = s.prev1 = 0xFFFFFFFFu;
+    return s;
+}
+
+Ctx make_ctx(stt_streams* s, int n) {
+    stt_model* m = s->m;
+    Ctx c{};
+    c.layers = m->d_layers;
+    c.head = m->head;
+    c.out_norm = m->out_norm;
+    c.rope = m->rope;
+    c.emb_audio = m->emb_audio;
+    c.emb_text = m->emb_text;
+    c.emb_type = m->emb_type;
+    c.emb_row_bytes = m->emb_row_bytes;
+    c.L = m->L; c.D = m->D; c.H = m->H; c.HD = m->HD; c.F = m->F; c.V = m->V; c.TV = m->TV; c.AV = m->AV;
+    c.NC = m->NC; c.ML = m->ML; c.max_seq_len = m->cfg.max_seq_len;
+    c.attn_scale = m->attn_scale;
+    c.pad_id = m->cfg.text_padding_id;
+    c.text_delay = m->cfg.text_delay;
+    c.kv = s->d_kv;
+    c.kv_f32 = s->kv_f32;
+    c.kv_half_stride = (int64_t)m->H * m->ML * m->HD;
+    c.kv_layer_stride = 2 * c.kv_half_stride;
+    c.kv_stream_stride = (int64_t)m->L * c.kv_layer_stride;
+    c.state = s->d_state;
+    c.ids = s->d_ids;
+    c.n = n;
+    c.desc = s->d_desc;
+    c.x = s->d_x; c.qkv = s->d_qkv; c.attn = s->d_attn; c.hid = s->d_hid; c.logits = s->d_logits;
+    c.part = s->d_part;
+    c.tickets = s->d_tickets;
+    c.nsplit = nsplit_for(m, n);
+    c.chunk = (m->ML + c.nsplit - 1) / c.nsplit;
+    return c;
+}
+
+// Enqueues one decode step for batch size n on stream st.
+int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
+    stt_model* m = s->m;
+    const Ctx c = make_ctx(s, n);
+    const int grid = 2 * m->num_sms;
+    CUDA_TRY(launch_embed(c, st));
+    for (int l = 0; l < m->L; ++l) {
+        const LayerDev& L = m->h_layers[l];
+        GemvArgs a{};
+        a.W = L.qkv; a.in = s->d_x; a.norm = L.norm1; a.out = s->d_qkv; a.ldo = 3 * m->D; a.layer = l;
+        a.n_units = 3 * m->D / 2;
+        CUDA_TRY(launch_gemv(c, a, EPI_QKV, n, grid, st));
+        CUDA_TRY(launch_attention(c, l, st));
+        a = GemvArgs{};
+        a.W = L.out; a.in = s->d_attn; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
+        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, grid, st));
+        a = GemvArgs{};
+        a.W = L.fin; a.in = s->d_x; a.norm = L.norm2; a.out = s->d_hid; a.ldo = m->F; a.n_units = m->F;
+        a.half_n = m->F;
+        CUDA_TRY(launch_gemv(c, a, EPI_GATE, n, grid, st));
+        a = GemvArgs{};
+        a.W = L.fout; a.in = s->d_hid; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
+        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, grid, st));
+    }
+    GemvArgs a{};
+    a.W = m->head; a.in = s->d_x; a.norm = m->out_norm; a.out = s->d_logits; a.ldo = m->V;
+    a.n_units = (m->V + 1) / 2;
+    CUDA_TRY(launch_gemv(c, a, EPI_LOGITS, n, grid, st));
+    CUDA_TRY(launch_finish(c, st));
+    return STT_OK;
+}
+
+int graph_for(stt_streams* s, int n, cudaGraphExec_t* out) {
+    auto it = s->graphs.find(n);
+    if (it != s->graphs.end()) {
+        *out = it->second;
+        return STT_OK;
+    }
+    cudaGraph_t graph;
+    CUDA_TRY(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(s, n, s->stream);
+    cudaError_t e = cudaStreamEndCapture(s->stream, &graph);
+    if (rc != STT_OK) {
+        if (e == cudaSuccess) cudaGraphDestroy(graph);
+        return rc;
+    }
+    CUDA_TRY(e);
+    cudaGraphExec_t exec;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    CUDA_TRY(e);
+    s->graphs[n] = exec;
+    *out = exec;
+    return STT_OK;
+}
+
+// Brings the host copy of every stream state up to date.  Asynchronous calls may have queued
+// steps on caller streams, so this waits for the whole device.
+int refresh_state(stt_streams* s) {
+    if (!s->state_stale) return STT_OK;
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(s->h_state.data(), s->d_state, sizeof(StreamState) * s->S, cudaMemcpyDeviceToHost));
+    s->state_stale = false;
+    return STT_OK;
+}
+
+int check_ids(stt_streams* s, const int32_t* ids, int n) {
+    if (!ids || n <= 0 || n > s->S) return set_error(STT_E_INVALID_ARG, "need 1..%d stream ids, got %d", s->S, n);
+    std::vector<uint8_t> seen(s->S, 0);
+    for (int i = 0; i < n; ++i) {
+        if (ids[i] < 0 || ids[i] >= s->S) return set_error(STT_E_INVALID_ARG, "stream id %d out of range [0, %d)", ids[i], s->S);
+        if (seen[ids[i]]) return set_error(STT_E_INVALID_ARG, "stream id %d repeated in one call", ids[i]);
+        seen[ids[i]] = 1;
+    }
+    return STT_OK;
+}
+
+// Host-side checks the reference makes by panicking: token ids index the embedding tables
+// (gguf.rs:620-621) and positions index the RoPE table (model.rs:72-79).
+int check_tokens(const stt_model* m, const uint32_t* audio, size_t n_audio, const uint32_t* text, size_t n_text) {
+    for (size_t i = 0; i < n_audio; ++i)
+        if (audio[i] >= (uint32_t)m->AV)
+            return set_error(STT_E_INVALID_ARG, "audio token %u (index %zu) >= audio vocab %d", audio[i], i, m->AV);
+    for (size_t i = 0; text && i < n_text; ++i)
+        if (text[i] >= (uint32_t)m->TV)
+            return set_error(STT_E_INVALID_ARG, "text token %u (index %zu) >= text vocab %d", text[i], i, m->TV);
+    return STT_OK;
+}
+
+// Offsets advance by one per queued step, so the host copy of the offsets is always current
+// even while other state fields are stale.
+int check_positions(stt_streams* s, const int32_t* ids, int n, int steps) {
+    for (int i = 0; i < n; ++i) {
+        const StreamState& st = s->h_state[ids[i]];
+        if ((int64_t)st.offset + steps > s->m->cfg.max_seq_len)
+            return set_error(STT_E_STATE, "stream %d: position %d + %d steps exceeds max_seq_len %d", ids[i],
+                             st.offset, steps, s->m->cfg.max_seq_len);
+    }
+    return STT_OK;
+}
+
+// Queues `steps` decode steps for the batch `ids` with device-resident inputs and outputs.
+int run_steps(stt_streams* s, const int32_t* ids, int n, int steps, const uint32_t* d_audio, const uint32_t* d_text,
+              int32_t* d_tokens, float* d_logits, int mode, cudaStream_t user_stream) {
+    stt_model* m = s->m;
+    cudaStream_t st = user_stream ? user_stream : s->stream;
+    if (n > kMaxBatch) return set_error(STT_E_INVALID_ARG, "batch of %d streams exceeds %d", n, kMaxBatch);
+    static DescInit init;  // large; filled under the caller's serialisation of this handle
+    init.desc = StepDesc{d_audio, d_text, d_tokens, d_logits, 0, mode, 0, 0};
+    init.n = n;
+    std::memcpy(init.ids, ids, sizeof(int32_t) * n);
+    const bool use_mega = n == 1 && mega_supported(m->L, m->D, m->F, m->HD) && d_text == nullptr &&
+                          d_logits == nullptr && std::getenv("STT_DISABLE_MEGA") == nullptr;
+    cudaGraphExec_t exec = nullptr;
+    if (!use_mega) TRY(graph_for(s, n, &exec));
+    CUDA_TRY(launch_set_desc(s->d_desc, s->d_ids, init, st));
+    if (use_mega) {
+        // single-stream steps go through the persistent step kernel
+        CUDA_TRY(launch_mega_steps(s->mega, make_ctx(s, 1), m->h_layers.data(), steps, st));
+    } else {
+        for (int t = 0; t < steps; ++t) CUDA_TRY(cudaGraphLaunch(exec, st));
+    }
+    for (int i = 0; i < n; ++i) s->h_state[ids[i]].offset += steps;
+    s->state_stale = true;
+    return STT_OK;
+}
+
+// Synchronous wrapper: host inputs in, host outputs out.
+int run_host(stt_streams* s, const int32_t* ids, int n, int steps, const uint32_t* audio, const uint32_t* text,
+             int32_t* tokens_out, float* logits_out, int mode) {
+    stt_model* m = s->m;
+    DeviceScope ds(m->device);
+    TRY(check_ids(s, ids, n));
+    const size_t n_audio = (size_t)steps * n * m->NC;
+    TRY(check_tokens(m, audio, n_audio, text, (size_t)steps * n));
+    TRY(check_positions(s, ids, n, steps));
+    TRY(s->in_audio.ensure(n_audio * 4));
+    TRY(s->out_tokens.ensure((size_t)steps * n * 4));
+    if (text) TRY(s->in_text.ensure((size_t)steps * n * 4));
+    if (logits_out) TRY(s->out_logits.ensure((size_t)steps * n * m->V * 4));
+    // one pinned staging area for the inputs: audio then text
+    const size_t in_bytes = n_audio * 4 + (text ? (size_t)steps * n * 4 : 0);
+    HostBuf& hb = s->h_tokens;  // reused as the input stage before the outputs arrive
+    TRY(hb.ensure(std::max(in_bytes, (size_t)steps * n * 4)));
+    std::memcpy(hb.p, audio, n_audio * 4);
+    if (text) std::memcpy(static_cast<uint8_t*>(hb.p) + n_audio * 4, text, (size_t)steps * n * 4);
+    CUDA_TRY(cudaMemcpyAsync(s->in_audio.p, hb.p, n_audio * 4, cudaMemcpyHostToDevice, s->stream));
+    if (text)
+        CUDA_TRY(cudaMemcpyAsync(s->in_text.p, static_cast<uint8_t*>(hb.p) + n_audio * 4, (size_t)steps * n * 4,
+                                 cudaMemcpyHostToDevice, s->stream));
+    TRY(run_steps(s, ids, n, steps, static_cast<uint32_t*>(s->in_audio.p),
+                  text ? static_cast<uint32_t*>(s->in_text.p) : nullptr, static_cast<int32_t*>(s->out_tokens.p),
+                  logits_out ? static_cast<float*>(s->out_logits.p) : nullptr, mode, s->stream));
+    CUDA_TRY(cudaMemcpyAsync(hb.p, s->out_tokens.p, (size_t)steps * n * 4, cudaMemcpyDeviceToHost, s->stream));
+    StepDesc desc_back;
+    CUDA_TRY(cudaMemcpyAsync(&desc_back, s->d_desc, sizeof(StepDesc), cudaMemcpyDeviceToHost, s->stream));
+    CUDA_TRY(cudaStreamSynchronize(s->stream));
+    if (tokens_out) std::memcpy(tokens_out, hb.p, (size_t)steps * n * 4);
+    // run_steps advanced the host offsets; the device copy below is the same state
+    if (logits_out)
+        CUDA_TRY(cudaMemcpy(logits_out, s->out_logits.p, (size_t)steps * n * m->V * 4, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(s->h_state.data(), s->d_state, sizeof(StreamState) * s->S, cudaMemcpyDeviceToHost));
+    s->state_stale = false;
+    if (desc_back.error != 0)
+        return set_error(desc_back.error == STT_E_INVALID_ARG ? STT_E_INVALID_ARG : STT_E_DEVICE_FLAG,
+                         "a kernel raised error %d", desc_back.error);
+    return STT_OK;
+}
+
+}  // namespace
+
+extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt_streams** out) {
+    clear_error();
+    if (!m || !out || n_streams <= 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    if (kv_dtype != STT_KV_BF16 && kv_dtype != STT_KV_F32) return set_error(STT_E_INVALID_ARG, "kv_dtype must be 0 or 1");
+    *out = nullptr;
+    DeviceScope ds(m->device);
+    auto s = std::make_unique<stt_streams>();
+    s->m = m;
+    s->S = n_streams;
+    s->kv_f32 = kv_dtype == STT_KV_F32;
+    const size_t elem = s->kv_f32 ? 4 : 2;
+    s->kv_stream_bytes = (size_t)m->L * 2 * m->H * m->ML * m->HD * elem;
+    int max_np = 0;
+    for (int n = 1; n <= n_streams; ++n) max_np = std::max(max_np, n * nsplit_for(m, n));
+    const size_t S = (size_t)n_streams;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off = (off + bytes + 255) / 256 * 256; return o; };
+    const size_t o_state = take(sizeof(StreamState) * S);
+    const size_t o_x = take(S * m->D * 4), o_qkv = take(S * 3 * m->D * 4), o_attn = take(S * m->D * 4);
+    const size_t o_hid = take(S * m->F * 4), o_logits = take(S * m->V * 4);
+    const size_t o_part = take((size_t)max_np * m->H * (m->HD + 4) * 4);
+    const size_t o_tick = take((S * m->H + 1) * 4);
+    const size_t o_desc = take(sizeof(StepDesc) + S * 4 + 64);
+    const size_t o_mega = take(mega_scratch_bytes(m->num_sms, m->D, m->F, m->V, m->H, m->HD));
+    if (cudaMalloc(&s->d_scratch, off) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(STT_E_OOM, "cannot allocate %zu bytes of step scratch", off);
+    }
+    if (cudaMalloc(&s->d_kv, s->kv_stream_bytes * S) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(s->d_scratch);
+        return set_error(STT_E_OOM, "cannot allocate the KV rings (%zu bytes)", s->kv_stream_bytes * S);
+    }
+    uint8_t* b = static_cast<uint8_t*>(s->d_scratch);
+    s->d_state = reinterpret_cast<StreamState*>(b + o_state);
+    s->d_x = reinterpret_cast<float*>(b + o_x);
+    s->d_qkv = reinterpret_cast<float*>(b + o_qkv);
+    s->d_attn = reinterpret_cast<float*>(b + o_attn);
+    s->d_hid = reinterpret_cast<float*>(b + o_hid);
+    s->d_logits = reinterpret_cast<float*>(b + o_logits);
+    s->d_part = reinterpret_cast<float*>(b + o_part);
+    s->d_tickets = reinterpret_cast<uint32_t*>(b + o_tick);
+    s->d_desc = reinterpret_cast<StepDesc*>(b + o_desc);
+    s->d_ids = reinterpret_cast<int32_t*>(b + o_desc + sizeof(StepDesc));
+    s->mega.scratch = b + o_mega;
+    s->mega.scratch_bytes = mega_scratch_bytes(m->num_sms, m->D, m->F, m->V, m->H, m->HD);
+    CUDA_TRY(cudaMemset(s->d_scratch, 0, off));
+    CUDA_TRY(cudaMemset(s->d_kv, 0, s->kv_stream_bytes * S));
+    s->h_state.assign(S, fresh_state(m));
+    CUDA_TRY(cudaMemcpy(s->d_state, s->h_state.data(), sizeof(StreamState) * S, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+    *out = s.release();
+    return STT_OK;
+}
+
+extern "C" int stt_streams_destroy(stt_streams* s) {
+    if (!s) return STT_OK;
+    {
+        DeviceScope ds(s->m->device);
+        if (s->stream) cudaStreamSynchronize(s->stream);
+        for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+        s->graphs.clear();
+        if (s->stream) cudaStreamDestroy(s->stream);
+        if (s->d_kv) cudaFree(s->d_kv);
+        if (s->d_scratch) cudaFree(s->d_scratch);
+        s->in_audio.release();
+        s->in_text.release();
+        s->out_tokens.release();
+        s->out_logits.release();
+        s->h_stage.release();
+        s->h_tokens.release();
+    }
+    delete s;
+    return STT_OK;
+}
+
+extern "C" int stt_forward(stt_streams* s, const int32_t* ids, int n, const uint32_t* audio, const uint32_t* text,
+                           float* logits_out, uint32_t* argmax_out) {
+    clear_error();
+    if (!s || !audio || !text) return set_error(STT_E_INVALID_ARG, "NULL argument");
+    std::vector<int32_t> tok(n > 0 ? n : 1);
+    TRY(run_host(s, ids, n, 1, audio, text, tok.data(), logits_out, 0));
+    if (argmax_out)
+        for (int i = 0; i < n; ++i) argmax_out[i] = (uint32_t)tok[i];
+    return STT_OK;
+}
+
+extern "C" int stt_stream_feed_frame(stt_streams* s, int stream_id, const uint32_t* audio, int32_t* token_out) {
+    clear_error();
+    if (!s || !audio || !token_out) return set_error(STT_E_INVALID_ARG, "NULL argument");
+    const int32_t id = stream_id;
+    return run_host(s, &id, 1, 1, audio, nullptr, token_out, nullptr, 1);
+}
+
+extern "C" int stt_streams_feed_frame(stt_streams* s, const int32_t* ids, int n, const uint32_t* audio,
+                                      int32_t* tokens_out) {
+    clear_error();
+    if (!s || !audio || !tokens_out) return set_error(STT_E_INVALID_ARG, "NULL argument");
+    return run_host(s, ids, n, 1, audio, nullptr, tokens_out, nullptr, 1);
+}
+
+extern "C" int stt_stream_feed_frames(stt_streams* s, int stream_id, int n_frames, const uint32_t* audio,
+                                      int32_t* tokens_out) {
+    clear_error();
+    if (!s || !audio || !tokens_out || n_frames < 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    if (n_frames == 0) return STT_OK;
+    const int32_t id = stream_id;
+    return run_host(s, &id, 1, n_frames, audio, nullptr, tokens_out, nullptr, 1);
+}
+
+extern "C" int stt_stream_feed_frames_device(stt_streams* s, int stream_id, int n_frames, const uint32_t* d_audio,
+                                             int32_t* d_tokens, void* cuda_stream) {
+    clear_error();
+    if (!s || !d_audio || !d_tokens || n_frames < 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    if (n_frames == 0) return STT_OK;
+    DeviceScope ds(s->m->device);
+    const int32_t id = stream_id;
+    TRY(check_ids(s, &id, 1));
+    TRY(check_positions(s, &id, 1, n_frames));
+    TRY(run_steps(s, &id, 1, n_frames, d_audio, nullptr, d_tokens, nullptr, 1, static_cast<cudaStream_t>(cuda_stream)));
+    s->state_stale = true;
+    return STT_OK;
+}
+
+extern "C" int stt_streams_feed_frame_device(stt_streams* s, const int32_t* ids, int n, const uint32_t* d_audio,
+                                             int32_t* d_tokens, void* cuda_stream) {
+    clear_error();
+    if (!s || !d_audio || !d_tokens) return set_error(STT_E_INVALID_ARG, "NULL argument");
+    DeviceScope ds(s->m->device);
+    TRY(check_ids(s, ids, n));
+    TRY(check_positions(s, ids, n, 1));
+    TRY(run_steps(s, ids, n, 1, d_audio, nullptr, d_tokens, nullptr, 1, static_cast<cudaStream_t>(cuda_stream)));
+    s->state_stale = true;
+    return STT_OK;
+}
+
+extern "C" int stt_stream_flush(stt_streams* s, int stream_id, uint32_t* tokens_out, int capacity, int* n_tokens) {
+    clear_error();
+    if (!s || !n_tokens || capacity < 0 || (capacity > 0 && !tokens_out)) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    *n_tokens = 0;
+    const int steps = s->m->cfg.text_delay;
+    if (steps == 0) return STT_OK;
+    std::vector<uint32_t> zero((size_t)steps * s->m->NC, 0u);
+    std::vector<int32_t> tok(steps);
+    // text_delay frames of zero audio through feed_frame (stream.rs:329-335)
+    TRY(stt_stream_feed_frames(s, stream_id, steps, zero.data(), tok.data()));
+    for (int i = 0; i < steps; ++i)
+        if (tok[i] >= 0 && *n_tokens < capacity) tokens_out[(*n_tokens)++] = (uint32_t)tok[i];
+    return STT_OK;
+}
+
+extern "C" int stt_stream_reset(stt_streams* s, int stream_id, int keep_buffers) {
+    clear_error();
+    if (!s || stream_id < 0 || stream_id >= s->S) return set_error(STT_E_INVALID_ARG, "bad stream id");
+    DeviceScope ds(s->m->device);
+    TRY(refresh_state(s));
+    s->h_state[stream_id] = fresh_state(s->m);
+    CUDA_TRY(cudaMemcpy(s->d_state + stream_id, &s->h_state[stream_id], sizeof(StreamState),
+                        cudaMemcpyHostToDevice));
+    if (keep_buffers)
+        CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t*>(s->d_kv) + s->kv_stream_bytes * stream_id, 0,
+                                 s->kv_stream_bytes, s->stream));
+    CUDA_TRY(cudaStreamSynchronize(s->stream));
+    return STT_OK;
+}
+
+extern "C" int stt_stream_set_last_text_token(stt_streams* s, int stream_id, uint32_t token) {
+    clear_error();
+    if (!s || stream_id < 0 || stream_id >= s->S) return set_error(STT_E_INVALID_ARG, "bad stream id");
+    if (token >= (uint32_t)s->m->TV) return set_error(STT_E_INVALID_ARG, "token %u >= text vocab %d", token, s->m->TV);
+    DeviceScope ds(s->m->device);
+    TRY(refresh_state(s));
+    s->h_state[stream_id].last_text = token;
+    CUDA_TRY(cudaMemcpy(s->d_state + stream_id, &s->h_state[stream_id], sizeof(StreamState),
+                        cudaMemcpyHostToDevice));
+    return STT_OK;
+}
+
+extern "C" int stt_stream_get_state(stt_streams* s, int stream_id, stt_stream_state* out) {
+    clear_error();
+    if (!s || !out || stream_id < 0 || stream_id >= s->S) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    DeviceScope ds(s->m->device);
+    s->state_stale = true;
+    TRY(refresh_state(s));
+    const StreamState& st = s->h_state[stream_id];
+    out->offset = st.offset;
+    out->len = st.len;
+    out->write_pos = st.write_pos;
+    out->frame_count = st.frame_count;
+    out->last_text_token = st.last_text;
+    out->delay_prev[0] = st.prev0;
+    out->delay_prev[1] = st.prev1;
+    return STT_OK;
+}
+
+// ------------------------------------------------------------------------------------ Q4 matmul
+
+struct stt_q4_tensor {
+    int device = 0;
+    int num_sms = 148;
+    Q4Dev w{};
+    void* mem = nullptr;
+};
+
+extern "C" int stt_q4_tensor_create(const uint8_t* bytes, size_t n_bytes, int n, int k, int device, stt_q4_tensor** out) {
+    clear_error();
+    if (!bytes || !out || n <= 0 || k <= 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    *out = nullptr;
+    const uint64_t numel = (uint64_t)n * (uint64_t)k;
+    // Q4Tensor::from_q4_bytes (gguf.rs:418-432)
+    if (numel % 32 != 0) return set_error(STT_E_FORMAT, "Q4_0 requires element count divisible by 32, got %llu", (unsigned long long)numel);
+    const uint64_t nblk = numel / 32;
+    if (n_bytes != nblk * 18)
+        return set_error(STT_E_FORMAT, "Q4_0 byte count mismatch: expected %llu for %llu blocks, got %zu",
+                         (unsigned long long)(nblk * 18), (unsigned long long)nblk, n_bytes);
+    if (k % 32 != 0 || k > kMaxGemvK)
+        return set_error(STT_E_INVALID_ARG, "in_features %d unsupported (multiple of 32, at most %d)", k, kMaxGemvK);
+    DeviceScope ds(device);
+    if (!ds.ok) return set_error(STT_E_INVALID_ARG, "cannot select device %d", device);
+    auto t = std::make_unique<stt_q4_tensor>();
+    t->device = device;
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    t->num_sms = prop.multiProcessorCount;
+    const size_t nib_bytes = (nblk * 16 + 255) / 256 * 256;
+    if (cudaMalloc(&t->mem, nib_bytes + nblk * 2) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(STT_E_OOM, "cannot allocate Q4 tensor");
+    }
+    t->w.nib = static_cast<const uint4*>(t->mem);
+    t->w.scale = reinterpret_cast<const uint16_t*>(static_cast<uint8_t*>(t->mem) + nib_bytes);
+    t->w.n = n;
+    t->w.k = k;
+    DevBuf staging;
+    TRY(staging.ensure(n_bytes));
+    CUDA_TRY(cudaMemcpy(staging.p, bytes, n_bytes, cudaMemcpyHostToDevice));
+    CUDA_TRY(launch_repack_q4(static_cast<const uint8_t*>(staging.p), (int64_t)nblk, const_cast<uint4*>(t->w.nib),
+                              const_cast<uint16_t*>(t->w.scale), 0));
+    CUDA_TRY(configure_kernels());
+    CUDA_TRY(cudaDeviceSynchronize());
+    *out = t.release();
+    return STT_OK;
+}
+
+extern "C" int stt_q4_tensor_destroy(stt_q4_tensor* t) {
+    if (!t) return STT_OK;
+    {
+        DeviceScope ds(t->device);
+        if (t->mem) cudaFree(t->mem);
+    }
+    delete t;
+    return STT_OK;
+}
+
+extern "C" int stt_q4_matmul_device(const stt_q4_tensor* t, const void* d_in, int in_dtype, int rows, float* d_out,
+                                    void* cuda_stream) {
+    if (!t || !d_in || !d_out || rows < 0 || (in_dtype != 0 && in_dtype != 1))
+        return set_error(STT_E_INVALID_ARG, "bad arguments");
+    if (rows == 0) return STT_OK;
+    DeviceScope ds(t->device);
+    Ctx c{};
+    GemvArgs a{};
+    a.W = t->w;
+    if (in_dtype == 0) a.in = static_cast<const float*>(d_in);
+    else a.in_bf16 = static_cast<const __nv_bfloat16*>(d_in);
+    a.out = d_out;
+    a.ldo = t->w.n;
+    a.n_units = (t->w.n + 1) / 2;
+    CUDA_TRY(launch_gemv(c, a, EPI_PLAIN, rows, 2 * t->num_sms, static_cast<cudaStream_t>(cuda_stream)));
+    return STT_OK;
+}
+
+extern "C" int stt_q4_matmul(const stt_q4_tensor* t, const float* input, int rows, float* out) {
+    clear_error();
+    if (!t || !input || !out || rows < 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    if (rows == 0) return STT_OK;
+    DeviceScope ds(t->device);
+    DevBuf din, dout;
+    TRY(din.ensure((size_t)rows * t->w.k * 4));
+    TRY(dout.ensure((size_t)rows * t->w.n * 4));
+    CUDA_TRY(cudaMemcpy(din.p, input, (size_t)rows * t->w.k * 4, cudaMemcpyHostToDevice));
+    TRY(stt_q4_matmul_device(t, din.p, 0, rows, static_cast<float*>(dout.p), nullptr));
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(out, dout.p, (size_t)rows * t->w.n * 4, cudaMemcpyDeviceToHost));
+    return STT_OK;
+}
+
+extern "C" int stt_q4_tensor_dequant(const stt_q4_tensor* t, float* out_host) {
+    clear_error();
+    if (!t || !out_host) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    DeviceScope ds(t->device);
+    DevBuf d;
+    const size_t bytes = (size_t)t->w.n * t->w.k * 4;
+    TRY(d.ensure(bytes));
+    CUDA_TRY(launch_dequant_q4(t->w, static_cast<float*>(d.p), nullptr));
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(out_host, d.p, bytes, cudaMemcpyDeviceToHost));
+    return STT_OK;
+}

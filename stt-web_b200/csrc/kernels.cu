@@ -1,0 +1,590 @@
+// Step kernels of the STT-1B decode step for sm_100a.
+//
+// One decode step for a batch of n streams is
+//   embed -> 16 x [qkv, attention, out_proj, linear_in, linear_out] -> head -> finish
+// where each Q4 matmul is the dequant-fused GEMV of gemv_kernel with its neighbours fused in:
+//   qkv        RMSNorm(norm1) prologue; RoPE + K/V ring write epilogue   (model.rs:426-449)
+//   attention  split-KV softmax(q.k^T * scale).v, last split combines     (model.rs:450-472)
+//   out_proj   residual-add epilogue                                       (model.rs:565)
+//   linear_in  RMSNorm(norm2) prologue; silu(gate) * value epilogue        (model.rs:517-524)
+//   linear_out residual-add epilogue                                       (model.rs:570)
+//   head       RMSNorm(out_norm) prologue                                  (model.rs:662-663)
+//   finish     argmax (lowest index on ties) and the stream-loop state update (stream.rs:90-107,
+//              231-266)
+#include <cfloat>
+
+#include "device.cuh"
+#include "kernels.h"
+
+namespace stt {
+
+// ------------------------------------------------------------------------------------ Q4 layout
+
+// Splits raw Q4_0 blocks (18 bytes: f16 scale, 16 nibble bytes) into the two device planes.
+__global__ void repack_q4_kernel(const uint8_t* __restrict__ raw, int64_t nblocks, uint4* __restrict__ nib,
+                                 uint16_t* __restrict__ scale) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    const uint8_t* p = raw + b * 18;
+    scale[b] = (uint16_t)(p[0] | (p[1] << 8));
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        w[i] = (uint32_t)p[2 + 4 * i] | ((uint32_t)p[3 + 4 * i] << 8) | ((uint32_t)p[4 + 4 * i] << 16) |
+               ((uint32_t)p[5 + 4 * i] << 24);
+    nib[b] = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// out[r*k + j] = (nibble - 8) * scale, the value the reference shader uses (shader_naive.wgsl:64-81).
+__global__ void dequant_q4_kernel(Q4Dev w, float* __restrict__ out) {
+    const int64_t nb = w.k / 32;
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= (int64_t)w.n * nb) return;
+    const uint4 q = w.nib[b];
+    const float d = f16_to_f32_ieee(w.scale[b]);
+    float* o = out + b * 32;
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t byte = (words[wi] >> (8 * i)) & 0xFFu;
+            o[4 * wi + i] = __fmul_rn(nib_m8(byte & 0xFu), d);
+            o[16 + 4 * wi + i] = __fmul_rn(nib_m8(byte >> 4), d);
+        }
+}
+
+// ------------------------------------------------------------------------------------ embed
+
+__device__ __forceinline__ float emb_value(const Ctx& c, const uint8_t* table, uint32_t row, int j) {
+    const uint8_t* r = table + (int64_t)row * c.emb_row_bytes;
+    switch (c.emb_type) {
+        case EMB_BF16: return bf16_to_f32_dev(reinterpret_cast<const uint16_t*>(r)[j]);
+        case EMB_F32: return reinterpret_cast<const float*>(r)[j];
+        case EMB_F16: return f16_to_f32_ieee(reinterpret_cast<const uint16_t*>(r)[j]);
+        default: {  // Q4_0 row, gguf.rs:616-633
+            const uint8_t* blk = r + (j >> 5) * 18;
+            const float d = f16_to_f32_gguf((uint16_t)(blk[0] | (blk[1] << 8)));
+            const int w = j & 31;
+            const uint32_t byte = blk[2 + (w & 15)];
+            const uint32_t nib = w < 16 ? (byte & 0xFu) : (byte >> 4);
+            return __fmul_rn(nib_m8(nib), d);
+        }
+    }
+}
+
+// x = sum of the 32 audio rows (codebook order) then the text row (model.rs:640-646), f32.
+__global__ void __launch_bounds__(256) embed_kernel(Ctx c) {
+    const int i = blockIdx.x;
+    const int sid = c.ids[i];
+    StepDesc* desc = c.desc;
+    const int step = desc->step;
+    const uint32_t* audio = desc->audio + ((int64_t)step * c.n + i) * c.NC;
+    uint32_t text = desc->text ? desc->text[(int64_t)step * c.n + i] : c.state[sid].last_text;
+    if (text >= (uint32_t)c.TV) {
+        raise_error(desc, -1);
+        text = 0;
+    }
+    __shared__ uint32_t toks[kMaxCodebooks];
+    if (threadIdx.x < c.NC) {
+        uint32_t t = audio[threadIdx.x];
+        if (t >= (uint32_t)c.AV) {
+            raise_error(desc, -1);
+            t = 0;
+        }
+        toks[threadIdx.x] = t;
+    }
+    __syncthreads();
+    const int64_t table_bytes = (int64_t)c.AV * c.emb_row_bytes;
+    for (int j = threadIdx.x; j < c.D; j += blockDim.x) {
+        float acc = 0.0f;
+        for (int cb = 0; cb < c.NC; ++cb) acc = __fadd_rn(acc, emb_value(c, c.emb_audio + cb * table_bytes, toks[cb], j));
+        acc = __fadd_rn(acc, emb_value(c, c.emb_text, text, j));
+        c.x[(int64_t)i * c.D + j] = acc;
+    }
+}
+
+// ------------------------------------------------------------------------------------ GEMV
+
+// Input vector layout in shared memory: element j of batch row m sits at
+//   m*K + ((q*NB + b) << 2) + e,   b = j/32, q = (j%32)/4, e = j%4
+// so lane l reading quad q of block b = l + 32t touches consecutive 16-byte chunks.
+__device__ __forceinline__ int xs_index(int j, int NB) {
+    const int b = j >> 5, w = j & 31;
+    return (((w >> 2) * NB + b) << 2) + (w & 3);
+}
+
+// Deterministic block reduction (fixed order) of one value per thread; all threads get the sum.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = 0.0f;
+    for (int w = 0; w < nw; ++w) s += red[w];
+    return s;
+}
+
+// Loads batch rows [row0, row0+mb) of `in` into the shared layout above, applying RMSNorm
+// (burn::nn::RmsNorm: (x / sqrt(mean(x^2) + 1e-8)) * alpha) when alpha != NULL.
+__device__ void load_vectors(const float* __restrict__ in, const __nv_bfloat16* __restrict__ in_bf16, int K,
+                             int row0, int mb, const float* __restrict__ alpha, float* xs, float* red) {
+    const int NB = K >> 5;
+    for (int m = 0; m < mb; ++m) {
+        const int64_t base = (int64_t)(row0 + m) * K;
+        float rms = 1.0f;
+        if (alpha) {
+            float ss = 0.0f;
+            for (int j = threadIdx.x; j < K; j += blockDim.x) {
+                const float v = in[base + j];
+                ss = __fmaf_rn(v, v, ss);
+            }
+            ss = block_sum(ss, red);
+            rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-8f));
+        }
+        for (int j = threadIdx.x; j < K; j += blockDim.x) {
+            float v = in_bf16 ? __bfloat162float(in_bf16[base + j]) : in[base + j];
+            if (alpha) v = __fmul_rn(__fdiv_rn(v, rms), alpha[j]);
+            xs[m * K + xs_index(j, NB)] = v;
+        }
+    }
+}
+
+// Sum over one 32-element block of (nibble - 8) * x for the 4 words of a Q4_0 payload.
+__device__ __forceinline__ float block_dot(const uint4 q, const float4* __restrict__ xq, int NB) {
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+        const float4 lo = xq[wi * NB];
+        const float4 hi = xq[(4 + wi) * NB];
+        const uint32_t w = words[wi];
+        s0 = __fmaf_rn(nib_m8(w & 0xFu), lo.x, s0);
+        s1 = __fmaf_rn(nib_m8((w >> 4) & 0xFu), hi.x, s1);
+        s0 = __fmaf_rn(nib_m8((w >> 8) & 0xFu), lo.y, s0);
+        s1 = __fmaf_rn(nib_m8((w >> 12) & 0xFu), hi.y, s1);
+        s0 = __fmaf_rn(nib_m8((w >> 16) & 0xFu), lo.z, s0);
+        s1 = __fmaf_rn(nib_m8((w >> 20) & 0xFu), hi.z, s1);
+        s0 = __fmaf_rn(nib_m8((w >> 24) & 0xFu), lo.w, s0);
+        s1 = __fmaf_rn(nib_m8(w >> 28), hi.w, s1);
+    }
+    return s0 + s1;
+}
+
+template <int EPI>
+__device__ __forceinline__ void unit_rows(const GemvArgs& a, int u, int* ra, int* rb) {
+    if (EPI == EPI_GATE) {
+        *ra = u;
+        *rb = u + a.half_n;
+    } else {
+        *ra = 2 * u;
+        *rb = 2 * u + 1 < a.W.n ? 2 * u + 1 : -1;
+    }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue(const Ctx& c, const GemvArgs& a, int bm, int ra, int rb, float va, float vb) {
+    if (EPI == EPI_PLAIN || EPI == EPI_LOGITS) {
+        float* o = a.out + (int64_t)bm * a.ldo;
+        o[ra] = va;
+        if (rb >= 0) o[rb] = vb;
+    } else if (EPI == EPI_RESID) {
+        float* o = a.out + (int64_t)bm * a.ldo;
+        o[ra] = __fadd_rn(va, o[ra]);
+        if (rb >= 0) o[rb] = __fadd_rn(vb, o[rb]);
+    } else if (EPI == EPI_GATE) {
+        // silu(gate) * value, silu(x) = x * (1 / (1 + exp(-x)))
+        const float sg = __fmul_rn(va, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-va))));
+        a.out[(int64_t)bm * a.ldo + ra] = __fmul_rn(sg, vb);
+    } else {  // EPI_QKV
+        const int sid = c.ids[bm];
+        const StreamState st = c.state[sid];
+        const int D = c.D, HD = c.HD;
+        float* o = a.out + (int64_t)bm * a.ldo;
+        int part = ra / D;            // 0 q, 1 k, 2 v
+        const int within = ra - part * D;
+        const int h = within / HD, d = within - h * HD;
+        if (part < 2) {
+            // RoPE::apply_rotation (model.rs:114-116) on the pair (2i, 2i+1), no fma contraction
+            const float2 cs = c.rope[(int64_t)st.offset * (HD >> 1) + (d >> 1)];
+            const float r = __fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y));
+            const float im = __fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x));
+            va = r;
+            vb = im;
+        }
+        o[ra] = va;
+        o[rb] = vb;
+        if (part >= 1) {
+            const int64_t off = (int64_t)sid * c.kv_stream_stride + (int64_t)a.layer * c.kv_layer_stride +
+                                (part == 2 ? c.kv_half_stride : 0) + ((int64_t)h * c.ML + st.write_pos) * HD + d;
+            if (c.kv_f32) {
+                float* kv = reinterpret_cast<float*>(c.kv) + off;
+                kv[0] = va;
+                kv[1] = vb;
+            } else {
+                __nv_bfloat162* kv = reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(c.kv) + off);
+                *kv = __floats2bfloat162_rn(va, vb);
+            }
+        }
+    }
+}
+
+template <int MB, int EPI>
+__global__ void __launch_bounds__(256) gemv_kernel(Ctx c, GemvArgs a, int row0, int mb) {
+    extern __shared__ float4 smem4[];
+    float* xs = reinterpret_cast<float*>(smem4);
+    __shared__ float red[32];
+    const int K = a.W.k, NB = K >> 5;
+    load_vectors(a.in, a.in_bf16, K, row0, mb, a.norm, xs, red);
+    __syncthreads();
+    const int64_t u0 = (int64_t)a.n_units * blockIdx.x / gridDim.x;
+    const int64_t u1 = (int64_t)a.n_units * (blockIdx.x + 1) / gridDim.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const float4* xq = reinterpret_cast<const float4*>(xs);
+    for (int64_t u = u0 + warp; u < u1; u += nwarps) {
+        int ra, rb;
+        unit_rows<EPI>(a, (int)u, &ra, &rb);
+        float acc[2][MB];
+#pragma unroll
+        for (int m = 0; m < MB; ++m) acc[0][m] = acc[1][m] = 0.0f;
+        const uint4* na = a.W.nib + (int64_t)ra * NB;
+        const uint4* nb_ = a.W.nib + (int64_t)(rb >= 0 ? rb : ra) * NB;
+        const uint16_t* sa = a.W.scale + (int64_t)ra * NB;
+        const uint16_t* sb = a.W.scale + (int64_t)(rb >= 0 ? rb : ra) * NB;
+        for (int b0 = lane; b0 < NB; b0 += 64) {
+            const int b1 = b0 + 32;
+            const bool has1 = b1 < NB;
+            const uint4 qa0 = __ldg(na + b0), qb0 = __ldg(nb_ + b0);
+            const uint4 qa1 = has1 ? __ldg(na + b1) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+            const uint4 qb1 = has1 ? __ldg(nb_ + b1) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+            const float da0 = f16_to_f32_ieee(__ldg(sa + b0)), db0 = f16_to_f32_ieee(__ldg(sb + b0));
+            const float da1 = has1 ? f16_to_f32_ieee(__ldg(sa + b1)) : 0.0f;
+            const float db1 = has1 ? f16_to_f32_ieee(__ldg(sb + b1)) : 0.0f;
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                if (m < mb) {
+                    const float4* x0 = xq + (m * K >> 2) + b0;
+                    acc[0][m] = __fmaf_rn(da0, block_dot(qa0, x0, NB), acc[0][m]);
+                    acc[1][m] = __fmaf_rn(db0, block_dot(qb0, x0, NB), acc[1][m]);
+                    if (has1) {
+                        const float4* x1 = xq + (m * K >> 2) + b1;
+                        acc[0][m] = __fmaf_rn(da1, block_dot(qa1, x1, NB), acc[0][m]);
+                        acc[1][m] = __fmaf_rn(db1, block_dot(qb1, x1, NB), acc[1][m]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            if (m < mb) {
+                const float va = warp_sum(acc[0][m]);
+                const float vb = warp_sum(acc[1][m]);
+                if (lane == 0) epilogue<EPI>(c, a, row0 + m, ra, rb, va, vb);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------ attention
+
+// One (split, head, batch row): keys [split*chunk, min(len, (split+1)*chunk)) of the ring.
+// Partial = (max score, sum exp, sum exp * v).  The CTA finishing last for a (row, head)
+// combines the partials in split order and writes attn[row][head].
+template <typename KT>
+__global__ void __launch_bounds__(128) attn_kernel(Ctx c, int layer) {
+    const int s = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sid = c.ids[i];
+    const StreamState st = c.state[sid];
+    const int len = min(st.len + 1, c.ML);
+    const int j0 = s * c.chunk, j1 = min(len, j0 + c.chunk);
+    const int HD = c.HD;  // 128: 4 dims per lane
+    const float4 q = reinterpret_cast<const float4*>(c.qkv + (int64_t)i * 3 * c.D + h * HD)[lane];
+    const KT* kbase = reinterpret_cast<const KT*>(c.kv) + (int64_t)sid * c.kv_stream_stride +
+                      (int64_t)layer * c.kv_layer_stride + (int64_t)h * c.ML * HD;
+    const KT* vbase = kbase + c.kv_half_stride;
+    float m = -FLT_MAX, l = 0.0f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool any = false;
+    for (int j = j0 + warp; j < j1; j += 4) {
+        float4 k, v;
+        if (sizeof(KT) == 4) {
+            k = reinterpret_cast<const float4*>(kbase + (int64_t)j * HD)[lane];
+            v = reinterpret_cast<const float4*>(vbase + (int64_t)j * HD)[lane];
+        } else {
+            const uint2 kr = reinterpret_cast<const uint2*>(kbase + (int64_t)j * HD)[lane];
+            const uint2 vr = reinterpret_cast<const uint2*>(vbase + (int64_t)j * HD)[lane];
+            k = make_float4(__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xFFFF0000u),
+                            __uint_as_float(kr.y << 16), __uint_as_float(kr.y & 0xFFFF0000u));
+            v = make_float4(__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xFFFF0000u),
+                            __uint_as_float(vr.y << 16), __uint_as_float(vr.y & 0xFFFF0000u));
+        }
+        float dot = __fmul_rn(q.x, k.x);
+        dot = __fmaf_rn(q.y, k.y, dot);
+        dot = __fmaf_rn(q.z, k.z, dot);
+        dot = __fmaf_rn(q.w, k.w, dot);
+        dot = warp_sum(dot);
+        const float score = __fmul_rn(dot, c.attn_scale);
+        const float mn = fmaxf(m, score);
+        const float corr = any ? expf(m - mn) : 0.0f;
+        const float p = expf(score - mn);
+        l = __fmaf_rn(l, corr, p);
+        o.x = __fmaf_rn(o.x, corr, __fmul_rn(p, v.x));
+        o.y = __fmaf_rn(o.y, corr, __fmul_rn(p, v.y));
+        o.z = __fmaf_rn(o.z, corr, __fmul_rn(p, v.z));
+        o.w = __fmaf_rn(o.w, corr, __fmul_rn(p, v.w));
+        m = mn;
+        any = true;
+    }
+    // combine the 4 warps in warp order
+    __shared__ float sm_m[4], sm_l[4];
+    __shared__ float4 sm_o[4][32];
+    if (lane == 0) {
+        sm_m[warp] = any ? m : -FLT_MAX;
+        sm_l[warp] = l;
+    }
+    sm_o[warp][lane] = o;
+    __syncthreads();
+    const int NS = c.nsplit;
+    float* part = c.part + (((int64_t)i * c.H + h) * NS + s) * (HD + 4);
+    if (warp == 0) {
+        float M = -FLT_MAX;
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w]);
+        float L = 0.0f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < 4; ++w) {
+            if (sm_l[w] == 0.0f) continue;
+            const float f = expf(sm_m[w] - M);
+            L = __fmaf_rn(sm_l[w], f, L);
+            const float4 ow = sm_o[w][lane];
+            O.x = __fmaf_rn(ow.x, f, O.x);
+            O.y = __fmaf_rn(ow.y, f, O.y);
+            O.z = __fmaf_rn(ow.z, f, O.z);
+            O.w = __fmaf_rn(ow.w, f, O.w);
+        }
+        if (lane == 0) {
+            part[0] = M;
+            part[1] = L;
+        }
+        reinterpret_cast<float4*>(part + 4)[lane] = O;
+    }
+    // last CTA of this (row, head) combines the splits
+    __shared__ uint32_t last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(&c.tickets[i * c.H + h], 1u);
+        last = (prev == (uint32_t)NS - 1u);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (warp == 0) {
+        const float* pb = c.part + ((int64_t)i * c.H + h) * NS * (HD + 4);
+        float M = -FLT_MAX;
+        for (int t = 0; t < NS; ++t) M = fmaxf(M, __ldcg(pb + t * (HD + 4)));
+        float L = 0.0f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t = 0; t < NS; ++t) {
+            const float lt = __ldcg(pb + t * (HD + 4) + 1);
+            if (lt == 0.0f) continue;
+            const float f = expf(__ldcg(pb + t * (HD + 4)) - M);
+            L = __fmaf_rn(lt, f, L);
+            const float4 ot = __ldcg(reinterpret_cast<const float4*>(pb + t * (HD + 4) + 4) + lane);
+            O.x = __fmaf_rn(ot.x, f, O.x);
+            O.y = __fmaf_rn(ot.y, f, O.y);
+            O.z = __fmaf_rn(ot.z, f, O.z);
+            O.w = __fmaf_rn(ot.w, f, O.w);
+        }
+        float4 r = make_float4(__fdiv_rn(O.x, L), __fdiv_rn(O.y, L), __fdiv_rn(O.z, L), __fdiv_rn(O.w, L));
+        reinterpret_cast<float4*>(c.attn + (int64_t)i * c.D + h * HD)[lane] = r;
+        if (lane == 0) c.tickets[i * c.H + h] = 0u;
+    }
+}
+
+// ------------------------------------------------------------------------------------ finish
+
+// Greedy argmax of the logits (lowest index among equal maxima), then the end-of-step state
+// update: KVCache ring counters (model.rs:204-207) and, in feed_frame mode, the delay gating
+// and limit-cycle breaker of resolve_pending_as_token (stream.rs:231-266).
+__global__ void __launch_bounds__(1024) finish_kernel(Ctx c) {
+    const int i = blockIdx.x;
+    const float* lg = c.logits + (int64_t)i * c.V;
+    float best = -FLT_MAX;
+    int bi = 0x7FFFFFFF;
+    for (int j = threadIdx.x; j < c.V; j += blockDim.x) {
+        const float v = lg[j];
+        if (v > best || (v == best && j < bi)) {
+            best = v;
+            bi = j;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    __shared__ float wv[32];
+    __shared__ int wi[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        wv[warp] = best;
+        wi[warp] = bi;
+    }
+    StepDesc* desc = c.desc;
+    const int step = desc->step;
+    __syncthreads();
+    if (desc->logits) {
+        float* dst = desc->logits + ((int64_t)step * c.n + i) * c.V;
+        for (int j = threadIdx.x; j < c.V; j += blockDim.x) dst[j] = lg[j];
+    }
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (wv[w] > best || (wv[w] == best && wi[w] < bi)) {
+                best = wv[w];
+                bi = wi[w];
+            }
+        const uint32_t token = (uint32_t)(bi == 0x7FFFFFFF ? 0 : bi);
+        const int sid = c.ids[i];
+        StreamState st = c.state[sid];
+        st.write_pos = (st.write_pos + 1) % c.ML;
+        st.offset += 1;
+        st.len = min(st.len + 1, c.ML);
+        int32_t out = (int32_t)token;
+        if (desc->mode == 1) {
+            st.frame_count += 1;
+            if (st.frame_count >= c.text_delay) {
+                st.last_text = token;
+            } else {
+                const uint32_t p0 = st.prev0, p1 = st.prev1;
+                st.prev0 = p1;
+                st.prev1 = token;
+                st.last_text = (token != c.pad_id && token != 0u && token == p0 && token != p1) ? c.pad_id : token;
+                out = -1;
+            }
+        }
+        c.state[sid] = st;
+        desc->tokens[(int64_t)step * c.n + i] = out;
+        __threadfence();
+        const uint32_t done = atomicAdd(&c.tickets[c.n * c.H], 1u);
+        if (done == (uint32_t)c.n - 1u) {
+            desc->step = step + 1;
+            c.tickets[c.n * c.H] = 0u;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------ launchers
+
+template <int N>
+struct DescParams {
+    StepDesc desc;
+    int32_t n;
+    int32_t ids[N];
+};
+
+template <int N>
+__global__ void set_desc_kernel(StepDesc* d_desc, int32_t* d_ids, const __grid_constant__ DescParams<N> p) {
+    if (threadIdx.x == 0) *d_desc = p.desc;
+    for (int i = threadIdx.x; i < p.n; i += blockDim.x) d_ids[i] = p.ids[i];
+}
+
+cudaError_t launch_set_desc(StepDesc* d_desc, int32_t* d_ids, const DescInit& p, cudaStream_t st) {
+    if (p.n <= kSmallBatch) {
+        DescParams<kSmallBatch> q;
+        q.desc = p.desc;
+        q.n = p.n;
+        for (int i = 0; i < p.n; ++i) q.ids[i] = p.ids[i];
+        set_desc_kernel<kSmallBatch><<<1, 64, 0, st>>>(d_desc, d_ids, q);
+    } else {
+        set_desc_kernel<kMaxBatch><<<1, 256, 0, st>>>(d_desc, d_ids, *reinterpret_cast<const DescParams<kMaxBatch>*>(&p));
+    }
+    return cudaGetLastError();
+}
+
+template <int MB, int EPI>
+static cudaError_t configure_gemv_t() {
+    return cudaFuncSetAttribute(gemv_kernel<MB, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(MB * kMaxGemvK * sizeof(float)));
+}
+
+template <int EPI>
+static cudaError_t configure_gemv_e() {
+    cudaError_t e = configure_gemv_t<1, EPI>();
+    if (e == cudaSuccess) e = configure_gemv_t<2, EPI>();
+    if (e == cudaSuccess) e = configure_gemv_t<4, EPI>();
+    return e;
+}
+
+// Raises the dynamic shared memory limit of every GEMV instantiation (call once per device).
+cudaError_t configure_kernels() {
+    cudaError_t e = configure_gemv_e<EPI_PLAIN>();
+    if (e == cudaSuccess) e = configure_gemv_e<EPI_QKV>();
+    if (e == cudaSuccess) e = configure_gemv_e<EPI_GATE>();
+    if (e == cudaSuccess) e = configure_gemv_e<EPI_RESID>();
+    if (e == cudaSuccess) e = configure_gemv_e<EPI_LOGITS>();
+    return e;
+}
+
+template <int MB, int EPI>
+static cudaError_t launch_gemv_t(const Ctx& c, const GemvArgs& a, int rows, int grid, cudaStream_t st) {
+    const size_t smem = (size_t)MB * a.W.k * sizeof(float);
+    for (int r0 = 0; r0 < rows; r0 += MB) {
+        const int mb = rows - r0 < MB ? rows - r0 : MB;
+        gemv_kernel<MB, EPI><<<grid, 256, smem, st>>>(c, a, r0, mb);
+    }
+    return cudaGetLastError();
+}
+
+template <int EPI>
+static cudaError_t launch_gemv_e(const Ctx& c, const GemvArgs& a, int rows, int grid, cudaStream_t st) {
+    if (rows <= 1) return launch_gemv_t<1, EPI>(c, a, rows, grid, st);
+    if (rows == 2) return launch_gemv_t<2, EPI>(c, a, rows, grid, st);
+    return launch_gemv_t<4, EPI>(c, a, rows, grid, st);
+}
+
+cudaError_t launch_gemv(const Ctx& c, const GemvArgs& a, int epi, int rows, int grid, cudaStream_t st) {
+    switch (epi) {
+        case EPI_PLAIN: return launch_gemv_e<EPI_PLAIN>(c, a, rows, grid, st);
+        case EPI_QKV: return launch_gemv_e<EPI_QKV>(c, a, rows, grid, st);
+        case EPI_GATE: return launch_gemv_e<EPI_GATE>(c, a, rows, grid, st);
+        case EPI_RESID: return launch_gemv_e<EPI_RESID>(c, a, rows, grid, st);
+        default: return launch_gemv_e<EPI_LOGITS>(c, a, rows, grid, st);
+    }
+}
+
+cudaError_t launch_repack_q4(const uint8_t* raw, int64_t nblocks, uint4* nib, uint16_t* scale, cudaStream_t st) {
+    const int64_t grid = (nblocks + 255) / 256;
+    repack_q4_kernel<<<(unsigned)grid, 256, 0, st>>>(raw, nblocks, nib, scale);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_q4(const Q4Dev& w, float* out, cudaStream_t st) {
+    const int64_t nblocks = (int64_t)w.n * (w.k / 32);
+    dequant_q4_kernel<<<(unsigned)((nblocks + 255) / 256), 256, 0, st>>>(w, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_embed(const Ctx& c, cudaStream_t st) {
+    embed_kernel<<<c.n, 256, 0, st>>>(c);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const Ctx& c, int layer, cudaStream_t st) {
+    dim3 grid(c.nsplit, c.H, c.n);
+    if (c.kv_f32) attn_kernel<float><<<grid, 128, 0, st>>>(c, layer);
+    else attn_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(c, layer);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_finish(const Ctx& c, cudaStream_t st) {
+    finish_kernel<<<c.n, 1024, 0, st>>>(c);
+    return cudaGetLastError();
+}
+
+}  // namespace stt

@@ -1,0 +1,44 @@
+// Host-side launchers of the step kernels (kernels.cu).
+#pragma once
+
+#include "device.cuh"
+
+namespace stt {
+
+constexpr int kMaxGemvK = 8448;  // largest reduction length the GEMV stages in shared memory
+
+enum Epi : int { EPI_PLAIN = 0, EPI_QKV = 1, EPI_GATE = 2, EPI_RESID = 3, EPI_LOGITS = 4 };
+
+// One Q4 matmul of the step: out = W . vec for each batch row, with the epilogue `epi`.
+struct GemvArgs {
+    Q4Dev W;
+    const float* in;                 // [rows][K] f32 input (ignored when in_bf16 != NULL)
+    const __nv_bfloat16* in_bf16;    // [rows][K] bf16 input or NULL
+    const float* norm;               // RMSNorm alpha applied to the input, or NULL
+    float* out;                      // destination (see Epi)
+    int64_t ldo;                     // destination row stride in floats
+    int32_t layer;                   // layer of the K/V ring (EPI_QKV)
+    int32_t n_units;                 // pairs of output rows
+    int32_t half_n;                  // EPI_GATE: value rows start here (= ffn width)
+};
+
+// Per-call descriptor and batch ids, written on the device from launch parameters so that
+// back-to-back asynchronous calls never race on a host staging buffer.
+constexpr int kMaxBatch = 4096;
+constexpr int kSmallBatch = 64;  // batches up to this size use a 300-byte parameter block
+struct DescInit {
+    StepDesc desc;
+    int32_t n;
+    int32_t ids[kMaxBatch];
+};
+
+cudaError_t configure_kernels();
+cudaError_t launch_set_desc(StepDesc* d_desc, int32_t* d_ids, const DescInit& p, cudaStream_t st);
+cudaError_t launch_repack_q4(const uint8_t* raw, int64_t nblocks, uint4* nib, uint16_t* scale, cudaStream_t st);
+cudaError_t launch_dequant_q4(const Q4Dev& w, float* out, cudaStream_t st);
+cudaError_t launch_gemv(const Ctx& c, const GemvArgs& a, int epi, int rows, int grid, cudaStream_t st);
+cudaError_t launch_embed(const Ctx& c, cudaStream_t st);
+cudaError_t launch_attention(const Ctx& c, int layer, cudaStream_t st);
+cudaError_t launch_finish(const Ctx& c, cudaStream_t st);
+
+}  // namespace stt
