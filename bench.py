@@ -233,6 +233,32 @@ def main():
     e2e_s = max_over_ranks(e2e_s)
     e2e = world * args.steps * FRAMES / e2e_s
 
+    # ---- diagnostics: grid-barrier latency and a per-phase breakdown of one late frame
+    diag = {}
+    ns = C.c_double()
+    if lib().stt_debug_barrier_ns(local, 2000, C.byref(ns)) == 0:
+        diag["grid_barrier_ns"] = ns.value
+    lib().stt_debug_trace_frame(cache._h, FRAMES - 10)
+    utterance_device()
+    torch.cuda.synchronize()
+    buf = (C.c_uint64 * 1024)()
+    nt = C.c_int()
+    if lib().stt_debug_get_trace(cache._h, buf, 1024, C.byref(nt)) == 0 and nt.value > 3:
+        t = [buf[i] for i in range(nt.value)]
+        names = ["qkv", "attention", "out_proj", "linear_in", "linear_out"] * 16 + ["head"]
+        work = {k: 0.0 for k in set(names)}
+        wait = {k: 0.0 for k in set(names)}
+        prev = t[0]
+        for k, name in enumerate(names[: (len(t) - 1) // 2]):
+            work[name] += (t[1 + 2 * k] - prev) / 1e3
+            wait[name] += (t[2 + 2 * k] - t[1 + 2 * k]) / 1e3
+            prev = t[2 + 2 * k]
+        diag["traced_frame"] = FRAMES - 10
+        diag["frame_us"] = (t[-1] - t[0]) / 1e3
+        diag["phase_work_us"] = {k: round(v, 2) for k, v in work.items()}
+        diag["phase_barrier_us"] = {k: round(v, 2) for k, v in wait.items()}
+    lib().stt_debug_trace_frame(cache._h, -1)
+
     # ---- roofline of the decode step (every kernel of a frame, device-timed above)
     pk, pk_kind = peaks()
     algo = algorithmic_bytes_per_utterance()
@@ -252,6 +278,7 @@ def main():
         "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": FRAMES * 32 * 4,
                 "d2h_bytes_per_step": FRAMES * (4 + 32)},
         "clocks": clocks,
+        "diagnostics": diag,
         "tokens_checksum": int(np.int64(dev_tokens.astype(np.int64).sum())),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

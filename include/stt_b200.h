@@ -217,6 +217,19 @@ int stt_synth_quantize_q4_0(const float* x, size_t n, uint8_t* out);
 int stt_synth_audio_tokens(uint64_t seed, int32_t stream, int32_t first_frame, int32_t n_frames,
                            int32_t num_codebooks, uint32_t* out);
 
+/* ---------------------------------------------------------------------------------------
+ * Diagnostics (no counterpart in the reference): timing probes of the persistent
+ * single-stream step kernel, used by the benchmarks and profiles of this library.
+ * ------------------------------------------------------------------------------------- */
+/* Records the device clock (%globaltimer, ns) at the start of frame `frame` and at the entry
+ * and exit of every grid barrier of that frame, on later single-stream calls; -1 disables. */
+int stt_debug_trace_frame(stt_streams* streams, int frame);
+/* Copies the timestamps of the last traced frame (at most cap); *n receives the count. */
+int stt_debug_get_trace(stt_streams* streams, uint64_t* out, int cap, int* n);
+/* Mean time of one grid barrier of the persistent kernel over `iters` back-to-back barriers on
+ * device `device`, in nanoseconds. */
+int stt_debug_barrier_ns(int device, int iters, double* ns_per_barrier);
+
 /* Text of the last error on the calling thread ("" if none). */
 const char* stt_last_error(void);
 

@@ -26,7 +26,12 @@ int set_error(int code, const char* fmt, ...) {
     g_last_error = buf;
     return code;
 }
-void clear_error() { g_last_error.clear(); }
+// Resets the thread's error text and any stale, non-sticky CUDA runtime error left by a call whose
+// failure was already handled (e.g. in a destructor), so it cannot surface in a later launch check.
+void clear_error() {
+    g_last_error.clear();
+    (void)cudaGetLastError();
+}
 
 #define CUDA_TRY(expr)                                                                              \
     do {                                                                                            \
@@ -500,6 +505,8 @@ struct stt_streams {
 
 namespace {
 
+constexpr int kTraceCap = 1024;
+
 int nsplit_for(const stt_model* m, int n) {
     const int want = (2 * m->num_sms + n * m->H - 1) / (n * m->H);
     return std::max(1, std::min(32, want));
@@ -656,13 +663,14 @@ int run_steps(stt_streams* s, const int32_t* ids, int n, int steps, const uint32
     init.desc = StepDesc{d_audio, d_text, d_tokens, d_logits, 0, mode, 0, 0};
     init.n = n;
     std::memcpy(init.ids, ids, sizeof(int32_t) * n);
-    const bool use_mega = n == 1 && mega_supported(m->L, m->D, m->F, m->HD) && d_text == nullptr &&
-                          d_logits == nullptr && std::getenv("STT_DISABLE_MEGA") == nullptr;
+    const bool use_mega = n == 1 && mega_supported(m->L, m->D, m->F, m->HD);
     cudaGraphExec_t exec = nullptr;
     if (!use_mega) TRY(graph_for(s, n, &exec));
     CUDA_TRY(launch_set_desc(s->d_desc, s->d_ids, init, st));
     if (use_mega) {
         // single-stream steps go through the persistent step kernel
+        if (s->mega.trace_frame >= 0)
+            CUDA_TRY(cudaMemsetAsync(s->mega.trace, 0, sizeof(unsigned long long) * s->mega.trace_cap, st));
         CUDA_TRY(launch_mega_steps(s->mega, make_ctx(s, 1), m->h_layers.data(), steps, st));
     } else {
         for (int t = 0; t < steps; ++t) CUDA_TRY(cudaGraphLaunch(exec, st));
@@ -737,10 +745,14 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     const size_t o_state = take(sizeof(StreamState) * S);
     const size_t o_x = take(S * m->D * 4), o_qkv = take(S * 3 * m->D * 4), o_attn = take(S * m->D * 4);
     const size_t o_hid = take(S * m->F * 4), o_logits = take(S * m->V * 4);
-    const size_t o_part = take((size_t)max_np * m->H * (m->HD + 4) * 4);
+    // attention partials: the graph path uses n * nsplit_for(n) rows per head, the persistent
+    // kernel one row per CTA (num_sms / H splits per head)
+    const size_t part_rows = std::max<size_t>((size_t)max_np * m->H, (size_t)m->num_sms);
+    const size_t o_part = take(part_rows * (m->HD + 4) * 4);
     const size_t o_tick = take((S * m->H + 1) * 4);
     const size_t o_desc = take(sizeof(StepDesc) + S * 4 + 64);
     const size_t o_mega = take(mega_scratch_bytes(m->num_sms, m->D, m->F, m->V, m->H, m->HD));
+    const size_t o_trace = take(kTraceCap * sizeof(unsigned long long));
     if (cudaMalloc(&s->d_scratch, off) != cudaSuccess) {
         cudaGetLastError();
         return set_error(STT_E_OOM, "cannot allocate %zu bytes of step scratch", off);
@@ -763,6 +775,8 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     s->d_ids = reinterpret_cast<int32_t*>(b + o_desc + sizeof(StepDesc));
     s->mega.scratch = b + o_mega;
     s->mega.scratch_bytes = mega_scratch_bytes(m->num_sms, m->D, m->F, m->V, m->H, m->HD);
+    s->mega.trace = reinterpret_cast<unsigned long long*>(b + o_trace);
+    s->mega.trace_cap = kTraceCap;
     CUDA_TRY(cudaMemset(s->d_scratch, 0, off));
     CUDA_TRY(cudaMemset(s->d_kv, 0, s->kv_stream_bytes * S));
     s->h_state.assign(S, fresh_state(m));
@@ -1014,5 +1028,41 @@ extern "C" int stt_q4_tensor_dequant(const stt_q4_tensor* t, float* out_host) {
     CUDA_TRY(launch_dequant_q4(t->w, static_cast<float*>(d.p), nullptr));
     CUDA_TRY(cudaDeviceSynchronize());
     CUDA_TRY(cudaMemcpy(out_host, d.p, bytes, cudaMemcpyDeviceToHost));
+    return STT_OK;
+}
+
+// ------------------------------------------------------------------------------------ diagnostics
+
+extern "C" int stt_debug_trace_frame(stt_streams* s, int frame) {
+    clear_error();
+    if (!s) return set_error(STT_E_INVALID_ARG, "NULL streams");
+    s->mega.trace_frame = frame < 0 ? -1 : frame;
+    return STT_OK;
+}
+
+extern "C" int stt_debug_get_trace(stt_streams* s, uint64_t* out, int cap, int* n) {
+    clear_error();
+    if (!s || !out || !n || cap < 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    DeviceScope ds(s->m->device);
+    std::vector<unsigned long long> t(s->mega.trace_cap);
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(t.data(), s->mega.trace, sizeof(unsigned long long) * t.size(), cudaMemcpyDeviceToHost));
+    int k = 0;
+    while (k < (int)t.size() && t[k] != 0) ++k;
+    *n = std::min(k, cap);
+    for (int i = 0; i < *n; ++i) out[i] = t[i];
+    return STT_OK;
+}
+
+extern "C" int stt_debug_barrier_ns(int device, int iters, double* ns) {
+    clear_error();
+    if (!ns || iters <= 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    DeviceScope ds(device);
+    if (!ds.ok) return set_error(STT_E_INVALID_ARG, "cannot select device %d", device);
+    DevBuf b;
+    TRY(b.ensure(256));
+    float ms = 0.0f;
+    CUDA_TRY(mega_barrier_probe(b.p, iters, &ms));
+    *ns = (double)ms * 1e6 / iters;
     return STT_OK;
 }

@@ -74,8 +74,9 @@ __device__ __forceinline__ float emb_value(const Ctx& c, const uint8_t* table, u
 }
 
 // x = sum of the 32 audio rows (codebook order) then the text row (model.rs:640-646), f32.
+// grid (ceil(D/256), n): each CTA sums a 256-element slice of one batch row.
 __global__ void __launch_bounds__(256) embed_kernel(Ctx c) {
-    const int i = blockIdx.x;
+    const int i = blockIdx.y;
     const int sid = c.ids[i];
     StepDesc* desc = c.desc;
     const int step = desc->step;
@@ -96,12 +97,12 @@ __global__ void __launch_bounds__(256) embed_kernel(Ctx c) {
     }
     __syncthreads();
     const int64_t table_bytes = (int64_t)c.AV * c.emb_row_bytes;
-    for (int j = threadIdx.x; j < c.D; j += blockDim.x) {
-        float acc = 0.0f;
-        for (int cb = 0; cb < c.NC; ++cb) acc = __fadd_rn(acc, emb_value(c, c.emb_audio + cb * table_bytes, toks[cb], j));
-        acc = __fadd_rn(acc, emb_value(c, c.emb_text, text, j));
-        c.x[(int64_t)i * c.D + j] = acc;
-    }
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= c.D) return;
+    float acc = 0.0f;
+    for (int cb = 0; cb < c.NC; ++cb) acc = __fadd_rn(acc, emb_value(c, c.emb_audio + cb * table_bytes, toks[cb], j));
+    acc = __fadd_rn(acc, emb_value(c, c.emb_text, text, j));
+    c.x[(int64_t)i * c.D + j] = acc;
 }
 
 // ------------------------------------------------------------------------------------ GEMV
@@ -571,7 +572,7 @@ cudaError_t launch_dequant_q4(const Q4Dev& w, float* out, cudaStream_t st) {
 }
 
 cudaError_t launch_embed(const Ctx& c, cudaStream_t st) {
-    embed_kernel<<<c.n, 256, 0, st>>>(c);
+    embed_kernel<<<dim3((c.D + 255) / 256, c.n), 256, 0, st>>>(c);
     return cudaGetLastError();
 }
 

@@ -8,11 +8,15 @@ namespace stt {
 struct MegaState {
     void* scratch = nullptr;  // device scratch owned by the stream set
     size_t scratch_bytes = 0;
+    unsigned long long* trace = nullptr;  // device buffer for phase timestamps (diagnostics)
+    int trace_frame = -1;
+    int trace_cap = 0;
 };
 
 bool mega_supported(int L, int D, int F, int HD);
 size_t mega_scratch_bytes(int num_sms, int D, int F, int V, int H, int HD);
 cudaError_t configure_mega();
+cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out);
 cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_layers, int steps, cudaStream_t st);
 
 }  // namespace stt

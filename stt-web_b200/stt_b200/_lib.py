@@ -128,6 +128,9 @@ SIGNATURES = {
     "stt_synth_free": (None, [U8P]),
     "stt_synth_quantize_q4_0": (C.c_int, [F32P, C.c_size_t, U8P]),
     "stt_synth_audio_tokens": (C.c_int, [C.c_uint64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, U32P]),
+    "stt_debug_trace_frame": (C.c_int, [P, C.c_int]),
+    "stt_debug_get_trace": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int, I32P]),
+    "stt_debug_barrier_ns": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "stt_last_error": (C.c_char_p, []),
 }
 

@@ -183,14 +183,18 @@ def full_model():
     model.close()
 
 
-def test_full_size_model_parity(full_model):
+@pytest.mark.parametrize("kv,bound", [("f32", 1e-3), ("bf16", LOGIT_TOL)])
+def test_full_size_model_parity(full_model, kv, bound):
+    """Raw steps (n = 1: the persistent kernel) against the oracle at the full model size.  With
+    bf16 K/V a 1e-6 difference can flip a bf16 rounding of K or V, so that mode is held to the
+    2e-2 bound; f32 K/V is held to 1e-3."""
     g, model = full_model
     assert model.info.q4_weight_bytes == 627_351_552
-    cache = model.create_cache(1, "bf16")
+    cache = model.create_cache(1, kv)
     om = oracle_for(g.array, SttConfig())
     frames = stt_b200.audio_tokens(1, 0, 6)
-    worst = compare_steps(model, cache, om, O.KV_BF16, frames, 0)
-    assert worst < 1e-3, worst
+    worst = compare_steps(model, cache, om, 0 if kv == "f32" else O.KV_BF16, frames, 0)
+    assert worst < bound, worst
 
 
 def test_full_size_feed_frame_tokens_identical(full_model):
@@ -201,3 +205,39 @@ def test_full_size_feed_frame_tokens_identical(full_model):
     ref = oracle_for(g.array, cfg).stream(O.KV_BF16)
     frames = stt_b200.audio_tokens(2, 0, 10)
     assert st.feed_frames(frames) == [ref.feed_frame(f) for f in frames]
+
+
+def test_persistent_kernel_and_graph_path_agree(full_model, monkeypatch):
+    """The single-stream persistent kernel and the multi-kernel graph path decode the same
+    utterance to the same tokens."""
+    g, model = full_model
+    cfg = SttConfig()
+    frames = stt_b200.audio_tokens(3, 0, 40)
+    a = model.create_cache(1, "bf16")
+    toks_mega = stt_b200.SttStream(cfg, a).feed_frames(frames)
+    monkeypatch.setenv("STT_DISABLE_MEGA", "1")
+    b = model.create_cache(1, "bf16")
+    toks_graph = stt_b200.SttStream(cfg, b).feed_frames(frames)
+    monkeypatch.delenv("STT_DISABLE_MEGA")
+    assert toks_mega == toks_graph
+    sa, sb = a.state(0), b.state(0)
+    assert sa == sb and sa["offset"] == 40
+
+
+def test_persistent_kernel_barrier_and_trace(full_model):
+    import ctypes as C
+    from stt_b200._lib import lib
+    ns = C.c_double()
+    assert lib().stt_debug_barrier_ns(0, 2000, C.byref(ns)) == 0
+    assert 50 < ns.value < 20000, ns.value
+    g, model = full_model
+    cache = model.create_cache(1, "bf16")
+    assert lib().stt_debug_trace_frame(cache._h, 1) == 0
+    stt_b200.SttStream(SttConfig(), cache).feed_frames(stt_b200.audio_tokens(4, 0, 3))
+    buf = (C.c_uint64 * 1024)()
+    n = C.c_int()
+    assert lib().stt_debug_get_trace(cache._h, buf, 1024, C.byref(n)) == 0
+    # frame start + 2 marks per barrier: 5 per layer and one after the head
+    assert n.value == 1 + 2 * (5 * 16 + 1), n.value
+    t = np.array(buf[:n.value], dtype=np.int64)
+    assert np.all(np.diff(t) >= 0)
