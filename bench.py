@@ -193,7 +193,7 @@ def main():
     ts = torch.cuda.current_stream()
 
     def utterance_device():
-        cache.reset(0)
+        check(lib().stt_stream_reset_async(cache._h, 0, 0, C.c_void_p(ts.cuda_stream)), "reset_async")
         check(lib().stt_stream_feed_frames_device(cache._h, 0, FRAMES, C.c_void_p(d_audio.data_ptr()),
                                                   C.c_void_p(d_tokens.data_ptr()), C.c_void_p(ts.cuda_stream)),
               "feed_frames_device")

@@ -157,6 +157,10 @@ int stt_stream_flush(stt_streams* streams, int stream_id, uint32_t* tokens_out, 
  * device ring is kept allocated in either case and zeroed when keep_buffers != 0. */
 int stt_stream_reset(stt_streams* streams, int stream_id, int keep_buffers);
 
+/* Asynchronous reset: the same state change as stt_stream_reset, queued on cuda_stream (NULL =
+ * legacy default stream) behind work already queued there, without waiting for the device. */
+int stt_stream_reset_async(stt_streams* streams, int stream_id, int keep_buffers, void* cuda_stream);
+
 /* Replaces SttStream::set_last_text_token (stream.rs:190-192). */
 int stt_stream_set_last_text_token(stt_streams* streams, int stream_id, uint32_t token);
 

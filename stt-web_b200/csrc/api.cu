@@ -655,15 +655,14 @@ int check_positions(stt_streams* s, const int32_t* ids, int n, int steps) {
 
 // Queues `steps` decode steps for the batch `ids` with device-resident inputs and outputs.
 int run_steps(stt_streams* s, const int32_t* ids, int n, int steps, const uint32_t* d_audio, const uint32_t* d_text,
-              int32_t* d_tokens, float* d_logits, int mode, cudaStream_t user_stream) {
+              int32_t* d_tokens, float* d_logits, int mode, cudaStream_t st) {
     stt_model* m = s->m;
-    cudaStream_t st = user_stream ? user_stream : s->stream;
     if (n > kMaxBatch) return set_error(STT_E_INVALID_ARG, "batch of %d streams exceeds %d", n, kMaxBatch);
     static DescInit init;  // large; filled under the caller's serialisation of this handle
     init.desc = StepDesc{d_audio, d_text, d_tokens, d_logits, 0, mode, 0, 0};
     init.n = n;
     std::memcpy(init.ids, ids, sizeof(int32_t) * n);
-    const bool use_mega = n == 1 && mega_supported(m->L, m->D, m->F, m->HD);
+    const bool use_mega = n == 1 && mega_supported(m->L, m->D, m->F, m->HD, m->V, m->num_sms);
     cudaGraphExec_t exec = nullptr;
     if (!use_mega) TRY(graph_for(s, n, &exec));
     CUDA_TRY(launch_set_desc(s->d_desc, s->d_ids, init, st));
@@ -894,6 +893,22 @@ extern "C" int stt_stream_reset(stt_streams* s, int stream_id, int keep_buffers)
         CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t*>(s->d_kv) + s->kv_stream_bytes * stream_id, 0,
                                  s->kv_stream_bytes, s->stream));
     CUDA_TRY(cudaStreamSynchronize(s->stream));
+    return STT_OK;
+}
+
+extern "C" int stt_stream_reset_async(stt_streams* s, int stream_id, int keep_buffers, void* cuda_stream) {
+    clear_error();
+    if (!s || stream_id < 0 || stream_id >= s->S) return set_error(STT_E_INVALID_ARG, "bad stream id");
+    DeviceScope ds(s->m->device);
+    cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+    const StreamState fresh = fresh_state(s->m);
+    CUDA_TRY(launch_set_state(s->d_state + stream_id, fresh, st));
+    if (keep_buffers)
+        CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t*>(s->d_kv) + s->kv_stream_bytes * stream_id, 0,
+                                 s->kv_stream_bytes, st));
+    // the offset mirror is exact; the other host fields are refreshed on the next synchronous call
+    s->h_state[stream_id] = fresh;
+    s->state_stale = true;
     return STT_OK;
 }
 

@@ -495,6 +495,13 @@ __global__ void set_desc_kernel(StepDesc* d_desc, int32_t* d_ids, const __grid_c
     for (int i = threadIdx.x; i < p.n; i += blockDim.x) d_ids[i] = p.ids[i];
 }
 
+__global__ void set_state_kernel(StreamState* dst, StreamState v) { *dst = v; }
+
+cudaError_t launch_set_state(StreamState* dst, const StreamState& value, cudaStream_t st) {
+    set_state_kernel<<<1, 1, 0, st>>>(dst, value);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_set_desc(StepDesc* d_desc, int32_t* d_ids, const DescInit& p, cudaStream_t st) {
     if (p.n <= kSmallBatch) {
         DescParams<kSmallBatch> q;

@@ -33,6 +33,7 @@ struct DescInit {
 };
 
 cudaError_t configure_kernels();
+cudaError_t launch_set_state(StreamState* dst, const StreamState& value, cudaStream_t st);
 cudaError_t launch_set_desc(StepDesc* d_desc, int32_t* d_ids, const DescInit& p, cudaStream_t st);
 cudaError_t launch_repack_q4(const uint8_t* raw, int64_t nblocks, uint4* nib, uint16_t* scale, cudaStream_t st);
 cudaError_t launch_dequant_q4(const Q4Dev& w, float* out, cudaStream_t st);

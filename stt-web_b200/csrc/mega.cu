@@ -3,18 +3,23 @@
 // One cooperative launch of one 512-thread CTA per SM runs `steps` whole frames of one stream:
 //   per layer   QKV -> attention -> out_proj -> linear_in -> linear_out, a grid barrier after each
 //   per frame   head GEMV + per-CTA argmax -> barrier -> every CTA reduces the argmax, applies the
-//               stream rule, and builds the next frame's input from the audio sum precomputed in
-//               the head phase plus the text row.
-// The weight bytes (627 MB per frame) dwarf everything else, so the kernel is organised around
-// keeping HBM streaming:
-//   - each CTA owns fixed row ranges of every matrix and issues cp.async.bulk.prefetch.L2 for the
-//     ranges of the coming phases (and the KV slots its attention split will read), keeping a byte
-//     budget in flight ahead of its consumption, so the HBM queue never drains during barriers;
-//   - the GEMV consumes those bytes at about 1.5 instructions per weight: the input vector is
-//     turned into 24-bit fixed point per 32-element block (three byte limbs, shared exponent) and
-//     every nibble goes through dp4a, which keeps the dot product of a block exact in integers;
-//   - every spin (grid barrier) is bounded: on timeout the kernel raises STT_E_DEVICE_FLAG in the
-//     step descriptor, sets an abort word that releases the other CTAs, and returns.
+//               stream rule, and builds the next frame's input from the audio-embedding sum
+//               (computed in the head phase) plus the text row.
+// A single stream reads 627 MB of Q4_0 weights per frame but each phase is a few MB, so the
+// design is about keeping the dependent chain of 81 phases short while HBM keeps streaming:
+//   - every CTA owns fixed row ranges of every matrix.  Right after a phase's GEMV, before the
+//     grid barrier, one thread bulk-copies (cp.async.bulk + mbarrier) the CTA's rows of the
+//     NEXT phase into shared memory, so after the barrier only the activation vector has to be
+//     fetched; the same thread issues cp.async.bulk.prefetch.L2 for the phases beyond, keeping
+//     a byte budget of look-ahead in flight so HBM never idles during barriers;
+//   - the GEMV reads weights from shared memory at about 1.5 instructions per weight: the input
+//     vector becomes 24-bit fixed point per 32-element block (three byte limbs, shared
+//     exponent) and every nibble goes through dp4a, so each block's dot product is exact;
+//   - the grid barrier is a release add + acquire poll on one counter;
+//   - every wait is bounded: a timed-out barrier or copy raises STT_E_DEVICE_FLAG in the step
+//     descriptor, sets an abort word that releases the other CTAs, waits (bounded) for its own
+//     copies in flight, and returns.
+#include <algorithm>
 #include <cfloat>
 #include <cstdlib>
 
@@ -27,9 +32,11 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kNBMax = 264;             // K / 32 for K <= 8448
+constexpr int kNBMax = 264;                // K / 32 for K <= 8448
 constexpr int kMaxK = kNBMax * 32;
-constexpr uint32_t kSpinLimit = 1u << 26;  // ~ seconds with the nanosleep back-off
+constexpr int kWBuf = 144 * 1024;          // staged weight rows of one phase per CTA
+constexpr int kMaxL = 32;                  // layers held in the shared layer table
+constexpr uint32_t kSpinLimit = 1u << 26;  // bounded waits (~ seconds)
 
 struct MegaArgs {
     Ctx c;
@@ -39,32 +46,65 @@ struct MegaArgs {
     float* xa;             // [D] audio-embedding sum of the next frame
     float* amax_v;         // [grid] per-CTA best logit
     int32_t* amax_i;       // [grid] and its index
-    uint32_t pf_budget;    // L2 lookahead per CTA in bytes
-    unsigned long long* trace;  // optional: globaltimer at every barrier entry/exit of one frame
+    uint32_t pf_budget;    // L2 look-ahead per CTA in bytes
+    unsigned long long* trace;  // optional: %globaltimer at each barrier of one frame
     int32_t trace_frame;
     int32_t trace_cap;
 };
 
 struct Smem {
-    uint4 limbs[6 * kNBMax];   // [vec][block]: L0,L1,L2 of element groups 0-3, then of groups 4-7
-    float xs[kNBMax];          // 2^(e_b - 27): block scale of the fixed-point input (incl. 1/16)
-    float xf[kMaxK];           // the input vector in f32
+    alignas(128) uint8_t wbuf[kWBuf];  // this CTA's weight rows of the current phase
+    uint4 limbs[6 * kNBMax];           // [vec][block]: L0,L1,L2 of groups 0-3, then of groups 4-7
+    float xs[kNBMax];                  // 2^(e_b - 27): block scale of the fixed-point input
+    float xf[kMaxK];                   // the input vector in f32 / attention scratch
+    LayerDev layers[kMaxL];
     float red[kWarps];
     float wv[kWarps];
     int32_t wi[kWarps];
+    alignas(8) unsigned long long mbar;
+    uint32_t staged, waited;  // staged copies issued / waited for (thread 0's bookkeeping)
     int32_t flag;
 };
+
+// ------------------------------------------------------------------------------ primitives
 
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
-
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* m, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(m)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* m, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(m)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* m, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(m)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, unsigned long long* m) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(m))
+        : "memory");
+}
 __device__ __forceinline__ int dp4a_su(int a, uint32_t b, int c) {
     int d;
     asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -75,12 +115,9 @@ __device__ __forceinline__ int dp4a_ss(int a, uint32_t b, int c) {
     asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
     return d;
 }
-
 // exact int -> float for |v| < 2^22
 __device__ __forceinline__ float i2f(int v) { return __int_as_float(0x4B400000 + v) - 12582912.0f; }
 
-// Grid barrier: arrival counter with release/acquire and a bounded spin.  Returns false when the
-// kernel must stop (timeout here or elsewhere).
 __device__ __forceinline__ unsigned long long globaltimer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -95,28 +132,32 @@ struct Tracer {
     }
 };
 
+__device__ __forceinline__ int64_t split_lo(int64_t total, int part, int parts) { return total * part / parts; }
+
+// Grid barrier.  Returns false when the kernel must stop (a timeout here or in another CTA).
 __device__ bool grid_sync(const MegaArgs& P, uint32_t& epoch, Smem& sm, Tracer& tr) {
-    __threadfence();
     __syncthreads();
     tr.mark(P);
     ++epoch;
     if (threadIdx.x == 0) {
         const uint32_t target = epoch * gridDim.x;
-        atomicAdd(P.bar, 1u);
+        red_release_add(P.bar, 1u);  // release: this CTA's writes, ordered by the barrier above
         int ok = 1;
         uint32_t spins = 0;
         for (;;) {
             if ((int32_t)(ld_acquire(P.bar) - target) >= 0) break;
-            if (*(volatile uint32_t*)(P.bar + 1)) { ok = 0; break; }
+            if (*(volatile uint32_t*)(P.bar + 1)) {
+                ok = 0;
+                break;
+            }
             if (++spins > kSpinLimit) {
                 atomicExch(P.bar + 1, 1u);
                 raise_error(P.c.desc, -5);
                 ok = 0;
                 break;
             }
-            if (spins > 32) __nanosleep(64);
+            if (spins > 2048) __nanosleep(32);
         }
-        __threadfence();
         sm.flag = ok;
     }
     __syncthreads();
@@ -124,101 +165,179 @@ __device__ bool grid_sync(const MegaArgs& P, uint32_t& epoch, Smem& sm, Tracer& 
     return sm.flag != 0;
 }
 
-__device__ __forceinline__ int64_t split_lo(int64_t total, int part, int parts) { return total * part / parts; }
-
 // ------------------------------------------------------------------------------ phase geometry
 
-enum Phase : int { PH_QKV = 0, PH_ATT = 1, PH_OUT = 2, PH_IN = 3, PH_DOWN = 4 };
+enum Kind : int { K_QKV = 0, K_ATT = 1, K_OUT = 2, K_IN = 3, K_DOWN = 4, K_HEAD = 5 };
 
-struct Range {
-    const void* p;
+// The rows of one phase this CTA reads: one or two contiguous row ranges of one matrix.
+struct Rows {
+    const Q4Dev* W;
+    int32_t r0[2];
+    int32_t n[2];
+    int32_t nr;  // number of ranges
+};
+
+__device__ __forceinline__ Kind kind_of(int p, int L) { return p == 5 * L ? K_HEAD : (Kind)(p % 5); }
+
+__device__ Rows rows_of(const Smem& sm, const Ctx& c, int p, int cta, int ncta) {
+    Rows r{};
+    const Kind k = kind_of(p, c.L);
+    if (k == K_HEAD) {
+        const int64_t U = (c.V + 1) / 2;
+        const int64_t a = 2 * split_lo(U, cta, ncta), b = min((int64_t)c.V, 2 * split_lo(U, cta + 1, ncta));
+        r.W = &c.head;
+        r.r0[0] = (int)a;
+        r.n[0] = (int)max((int64_t)0, b - a);
+        r.nr = 1;
+        return r;
+    }
+    const LayerDev& L = sm.layers[p / 5];
+    switch (k) {
+        case K_QKV:
+        case K_OUT:
+        case K_DOWN: {
+            const Q4Dev* W = k == K_QKV ? &L.qkv : (k == K_OUT ? &L.out : &L.fout);
+            const int64_t U = W->n / 2;
+            r.W = W;
+            r.r0[0] = (int)(2 * split_lo(U, cta, ncta));
+            r.n[0] = (int)(2 * split_lo(U, cta + 1, ncta)) - r.r0[0];
+            r.nr = 1;
+            break;
+        }
+        case K_IN: {
+            const int u0 = (int)split_lo(c.F, cta, ncta), u1 = (int)split_lo(c.F, cta + 1, ncta);
+            r.W = &L.fin;
+            r.r0[0] = u0;
+            r.r0[1] = c.F + u0;
+            r.n[0] = r.n[1] = u1 - u0;
+            r.nr = 2;
+            break;
+        }
+        default:
+            r.nr = 0;
+            break;
+    }
+    return r;
+}
+
+// Shared-memory layout of a staged phase: for each range, nibbles then scales (16-byte aligned).
+struct Staged {
+    uint32_t nib[2];
+    uint32_t sc[2];
     uint32_t bytes;
 };
 
-// Byte ranges a CTA reads in global phase `gp` (frame-relative index gp % per_frame): at most 4.
-__device__ int phase_ranges(const MegaArgs& P, int gp, int cta, int ncta, int len_next, Range* out) {
-    const Ctx& c = P.c;
-    const int per_frame = 5 * c.L + 1;
-    const int p = gp % per_frame;
-    int n = 0;
-    auto q4 = [&](const Q4Dev& W, int64_t r0, int64_t r1) {
-        if (r1 <= r0) return;
-        const int64_t nb = W.k / 32;
-        out[n++] = Range{W.nib + r0 * nb, (uint32_t)((r1 - r0) * nb * 16)};
-        out[n++] = Range{W.scale + r0 * nb, (uint32_t)((r1 - r0) * nb * 2)};
-    };
-    if (p == 5 * c.L) {  // head
-        const int64_t U = (c.V + 1) / 2;
-        const int64_t r1 = 2 * split_lo(U, cta + 1, ncta);
-        q4(c.head, 2 * split_lo(U, cta, ncta), r1 < c.V ? r1 : (int64_t)c.V);
-        return n;
+__device__ __forceinline__ Staged staged_layout(const Rows& r) {
+    Staged s{};
+    uint32_t off = 0;
+    const uint32_t NB = r.nr ? (uint32_t)(r.W->k >> 5) : 0;
+    for (int i = 0; i < r.nr; ++i) {
+        s.nib[i] = off;
+        off += (uint32_t)r.n[i] * NB * 16;
+        s.sc[i] = off;
+        off += ((uint32_t)r.n[i] * NB * 2 + 15) & ~15u;
     }
-    const int l = p / 5, k = p % 5;
-    const LayerDev& L = c.layers[l];
-    switch (k) {
-        case PH_QKV: {
-            const int64_t U = 3 * c.D / 2;
-            q4(L.qkv, 2 * split_lo(U, cta, ncta), 2 * split_lo(U, cta + 1, ncta));
-            break;
-        }
-        case PH_OUT: {
-            const int64_t U = c.D / 2;
-            q4(L.out, 2 * split_lo(U, cta, ncta), 2 * split_lo(U, cta + 1, ncta));
-            break;
-        }
-        case PH_IN: {
-            const int64_t u0 = split_lo(c.F, cta, ncta), u1 = split_lo(c.F, cta + 1, ncta);
-            q4(L.fin, u0, u1);
-            q4(L.fin, c.F + u0, c.F + u1);
-            break;
-        }
-        case PH_DOWN: {
-            const int64_t U = c.D / 2;
-            q4(L.fout, 2 * split_lo(U, cta, ncta), 2 * split_lo(U, cta + 1, ncta));
-            break;
-        }
-        default: {  // attention: K and V slots of this CTA's split (bf16 rings only)
-            const int h = cta / P.nsplit, s = cta % P.nsplit;
-            if (h >= c.H || c.kv_f32) break;
-            const int chunk = (len_next + P.nsplit - 1) / P.nsplit;
-            const int j0 = s * chunk, j1 = min(len_next, j0 + chunk);
-            if (j1 <= j0) break;
-            const int sid = c.ids[0];
-            const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(c.kv) + (int64_t)sid * c.kv_stream_stride +
-                                      (int64_t)l * c.kv_layer_stride + (int64_t)h * c.ML * c.HD;
-            out[n++] = Range{kb + (int64_t)j0 * c.HD, (uint32_t)((j1 - j0) * c.HD * 2)};
-            out[n++] = Range{kb + c.kv_half_stride + (int64_t)j0 * c.HD, (uint32_t)((j1 - j0) * c.HD * 2)};
-            break;
-        }
-    }
-    return n;
+    s.bytes = off;
+    return s;
 }
 
-// Issues L2 prefetches for whole phases after `cur` until `budget` bytes are ahead.
-struct Prefetcher {
-    int next;          // next global phase to prefetch
-    int limit;         // one past the last global phase of the launch
-    __device__ void run(const MegaArgs& P, int cur, int cta, int ncta, int len_next_of_frame) {
-        if (threadIdx.x != 0) return;
-        uint32_t ahead = 0;
-        Range r[4];
-        // bytes already requested beyond the current phase
-        for (int g = cur + 1; g < next; ++g) {
-            const int n = phase_ranges(P, g, cta, ncta, len_next_of_frame, r);
-            for (int i = 0; i < n; ++i) ahead += r[i].bytes;
-        }
-        while (next < limit && ahead < P.pf_budget) {
-            const int n = phase_ranges(P, next, cta, ncta, len_next_of_frame, r);
-            for (int i = 0; i < n; ++i) {
-                const uint8_t* p = static_cast<const uint8_t*>(r[i].p);
-                for (uint32_t o = 0; o < r[i].bytes; o += 65536u)
-                    prefetch_l2(p + o, min(65536u, r[i].bytes - o));
-                ahead += r[i].bytes;
-            }
-            ++next;
+// Bytes a phase reads from HBM for this CTA (weights, or the K/V slots of its attention split).
+__device__ uint32_t phase_bytes(const Smem& sm, const MegaArgs& P, int p, int cta, int ncta, int len) {
+    const Ctx& c = P.c;
+    if (kind_of(p, c.L) == K_ATT) {
+        const int h = cta / P.nsplit, s = cta % P.nsplit;
+        if (h >= c.H) return 0;
+        const int chunk = (len + P.nsplit - 1) / P.nsplit;
+        const int j0 = s * chunk, j1 = min(len, j0 + chunk);
+        return j1 > j0 ? (uint32_t)(j1 - j0) * c.HD * 2 * (c.kv_f32 ? 4 : 2) : 0u;
+    }
+    const Rows r = rows_of(sm, c, p, cta, ncta);
+    uint32_t b = 0;
+    for (int i = 0; i < r.nr; ++i) b += (uint32_t)r.n[i] * (uint32_t)(r.W->k >> 5) * 18u;
+    return b;
+}
+
+// L2 prefetch of one phase's ranges.
+__device__ void prefetch_phase(const Smem& sm, const MegaArgs& P, int p, int cta, int ncta, int len) {
+    const Ctx& c = P.c;
+    if (kind_of(p, c.L) == K_ATT) {
+        const int h = cta / P.nsplit, s = cta % P.nsplit;
+        if (h >= c.H) return;
+        const int chunk = (len + P.nsplit - 1) / P.nsplit;
+        const int j0 = s * chunk, j1 = min(len, j0 + chunk);
+        if (j1 <= j0) return;
+        const int es = c.kv_f32 ? 4 : 2;
+        const uint8_t* kb = static_cast<const uint8_t*>(c.kv) +
+                            ((int64_t)c.ids[0] * c.kv_stream_stride + (int64_t)(p / 5) * c.kv_layer_stride +
+                             (int64_t)h * c.ML * c.HD + (int64_t)j0 * c.HD) * es;
+        const uint32_t bytes = (uint32_t)(j1 - j0) * c.HD * es;
+        prefetch_l2(kb, bytes);
+        prefetch_l2(kb + c.kv_half_stride * es, bytes);
+        return;
+    }
+    const Rows r = rows_of(sm, c, p, cta, ncta);
+    for (int i = 0; i < r.nr; ++i) {
+        if (r.n[i] <= 0) continue;
+        const int64_t NB = r.W->k >> 5;
+        const uint8_t* nb = reinterpret_cast<const uint8_t*>(r.W->nib + (int64_t)r.r0[i] * NB);
+        const uint32_t nbytes = (uint32_t)(r.n[i] * NB * 16);
+        for (uint32_t o = 0; o < nbytes; o += 65536u) prefetch_l2(nb + o, min(65536u, nbytes - o));
+        const uint32_t sbytes = (uint32_t)(r.n[i] * NB * 2) & ~15u;
+        if (sbytes) prefetch_l2(r.W->scale + (int64_t)r.r0[i] * NB, sbytes);
+    }
+}
+
+// Thread 0: bulk-copies phase p's rows of this CTA into wbuf; completion on sm.mbar.
+__device__ void stage_phase(Smem& sm, const Ctx& c, int p, int cta, int ncta) {
+    const Rows r = rows_of(sm, c, p, cta, ncta);
+    const Staged s = staged_layout(r);
+    ++sm.staged;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    uint32_t tx = 0;
+    for (int i = 0; i < r.nr; ++i)
+        if (r.n[i] > 0) tx += (uint32_t)r.n[i] * (uint32_t)(r.W->k >> 5) * 16u + (((uint32_t)r.n[i] * (uint32_t)(r.W->k >> 5) * 2u) & ~15u);
+    mbar_expect_tx(&sm.mbar, tx);
+    for (int i = 0; i < r.nr; ++i) {
+        if (r.n[i] <= 0) continue;
+        const int64_t NB = r.W->k >> 5;
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(r.W->nib + (int64_t)r.r0[i] * NB);
+        const uint32_t nbytes = (uint32_t)(r.n[i] * NB * 16);
+        for (uint32_t o = 0; o < nbytes; o += 32768u)
+            bulk_g2s(sm.wbuf + s.nib[i] + o, src + o, min(32768u, nbytes - o), &sm.mbar);
+        const uint32_t sbytes = (uint32_t)(r.n[i] * NB * 2);
+        const uint32_t sfull = sbytes & ~15u;
+        if (sfull) bulk_g2s(sm.wbuf + s.sc[i], r.W->scale + (int64_t)r.r0[i] * NB, sfull, &sm.mbar);
+        if (sbytes != sfull) {
+            // scale bytes not a multiple of 16 (rows * K/32 * 2): the tail is copied by this thread;
+            // the consumers read it after the same barrier that publishes the bulk copies
+            const uint16_t* tail = r.W->scale + (int64_t)r.r0[i] * NB + sfull / 2;
+            uint16_t* dst = reinterpret_cast<uint16_t*>(sm.wbuf + s.sc[i] + sfull);
+            for (uint32_t t = 0; t < (sbytes - sfull) / 2; ++t) dst[t] = tail[t];
         }
     }
-};
+}
+
+// Waits (bounded) for the staged copy of the current phase; the parity flips per staging.
+__device__ bool wait_stage(Smem& sm, const MegaArgs& P, uint32_t& parity) {
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        uint32_t spins = 0;
+        while (!mbar_try_wait(&sm.mbar, parity)) {
+            if (++spins > kSpinLimit || *(volatile uint32_t*)(P.bar + 1)) {
+                if (!*(volatile uint32_t*)(P.bar + 1)) raise_error(P.c.desc, -5);
+                atomicExch(P.bar + 1, 1u);
+                ok = 0;
+                break;
+            }
+        }
+        if (ok) ++sm.waited;
+        sm.flag = ok;
+    }
+    __syncthreads();
+    const bool ok = sm.flag != 0;
+    if (ok) parity ^= 1u;
+    return ok;
+}
 
 // ------------------------------------------------------------------------------ input vectors
 
@@ -261,32 +380,37 @@ __device__ float block_reduce_sum(float v, Smem& sm) {
     if (lane == 0) sm.red[warp] = v;
     __syncthreads();
     float s = 0.0f;
+#pragma unroll
     for (int w = 0; w < kWarps; ++w) s += sm.red[w];
     __syncthreads();
     return s;
 }
 
-// xf = RMSNorm(src) with alpha (or a plain copy when alpha == NULL); src is read through L2.
-__device__ void load_vector(Smem& sm, const float* src, int K, const float* alpha) {
+// RMSNorm of the vector in xf, in place (burn::nn::RmsNorm: (x / sqrt(mean(x^2) + 1e-8)) * alpha).
+__device__ void norm_in_place(Smem& sm, int K, const float* alpha) {
     float ss = 0.0f;
-    for (int j = threadIdx.x; j < K; j += kThreads) {
-        const float v = __ldcg(src + j);
-        sm.xf[j] = v;
-        ss = __fmaf_rn(v, v, ss);
-    }
-    if (alpha) {
-        ss = block_reduce_sum(ss, sm);
-        const float rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-8f));
-        for (int j = threadIdx.x; j < K; j += kThreads) sm.xf[j] = __fmul_rn(__fdiv_rn(sm.xf[j], rms), alpha[j]);
-    }
+    for (int j = threadIdx.x; j < K; j += kThreads) ss = __fmaf_rn(sm.xf[j], sm.xf[j], ss);
+    ss = block_reduce_sum(ss, sm);
+    const float rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-8f));
+    for (int j = threadIdx.x; j < K; j += kThreads) sm.xf[j] = __fmul_rn(__fdiv_rn(sm.xf[j], rms), __ldg(alpha + j));
+}
+
+// xf = src (read through L2), optionally normalised, then its limbs.
+__device__ void load_vector(Smem& sm, const float* src, int K, const float* alpha) {
+    for (int q = threadIdx.x; q < (K >> 2); q += kThreads)
+        reinterpret_cast<float4*>(sm.xf)[q] = __ldcg(reinterpret_cast<const float4*>(src) + q);
     __syncthreads();
+    if (alpha) {
+        norm_in_place(sm, K, alpha);
+        __syncthreads();
+    }
     build_limbs(sm, K);
     __syncthreads();
 }
 
 // ------------------------------------------------------------------------------ GEMV
 
-// sum over one Q4_0 block of (nibble - 8) * x, as 16 * sum in fixed point (S0 + 256 S1 + 65536 S2)
+// 16 * sum over one Q4_0 block of (nibble - 8) * X in fixed point (S0 + 256 S1 + 65536 S2)
 __device__ __forceinline__ float block_dp4a(const uint4 q, const uint4* L) {
     const uint32_t words[4] = {q.x, q.y, q.z, q.w};
     const uint32_t l0[4] = {L[0].x, L[0].y, L[0].z, L[0].w}, l1[4] = {L[1].x, L[1].y, L[1].z, L[1].w};
@@ -308,61 +432,56 @@ __device__ __forceinline__ float block_dp4a(const uint4 q, const uint4* L) {
     return __fmaf_rn(i2f(s2), 65536.0f, __fmaf_rn(i2f(s1), 256.0f, i2f(s0)));
 }
 
-template <int EPI>
-__device__ __forceinline__ void unit_rows_m(const Ctx& c, int u, int* ra, int* rb, int N) {
-    if (EPI == EPI_GATE) {
-        *ra = u;
-        *rb = u + c.F;
-    } else {
-        *ra = 2 * u;
-        *rb = 2 * u + 1 < N ? 2 * u + 1 : -1;
-    }
-}
-
 struct HeadBest {
     float v;
     int i;
 };
 
+// One GEMV phase over the rows staged in wbuf.  Units are row pairs (2u, 2u+1) or, for
+// linear_in, (gate row u, value row u + F); a warp takes one unit, its lanes split the blocks.
 template <int EPI>
-__device__ void gemv_phase(const MegaArgs& P, Smem& sm, const Q4Dev& W, int layer, const StreamState& st,
-                           int cta, int ncta, HeadBest* best, int frame) {
+__device__ void gemv_phase(const MegaArgs& P, Smem& sm, const Rows& r, int layer, const StreamState& st,
+                           HeadBest* best, int frame) {
     const Ctx& c = P.c;
-    const int NB = W.k >> 5;
-    const int64_t U = EPI == EPI_GATE ? c.F : (W.n + 1) / 2;
-    const int64_t u0 = split_lo(U, cta, ncta), u1 = split_lo(U, cta + 1, ncta);
+    if (r.nr == 0 || r.n[0] <= 0) return;
+    const Staged s = staged_layout(r);
+    const int NB = r.W->k >> 5;
+    const int units = EPI == EPI_GATE ? r.n[0] : (r.n[0] + 1) / 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int64_t u = u0 + warp; u < u1; u += kWarps) {
-        int ra, rb;
-        unit_rows_m<EPI>(c, (int)u, &ra, &rb, W.n);
-        const int rb_ = rb >= 0 ? rb : ra;
-        const uint4* na = W.nib + (int64_t)ra * NB;
-        const uint4* nb = W.nib + (int64_t)rb_ * NB;
-        const uint16_t* sa = W.scale + (int64_t)ra * NB;
-        const uint16_t* sb = W.scale + (int64_t)rb_ * NB;
+    const uint4* nibs = reinterpret_cast<const uint4*>(sm.wbuf);
+    const uint16_t* scs = reinterpret_cast<const uint16_t*>(sm.wbuf);
+    for (int u = warp; u < units; u += kWarps) {
+        int ra, rb;  // global rows (rb < 0: unit has one row)
+        uint32_t na, nb, sa, sb;  // wbuf offsets in uint4 / uint16 units
+        if (EPI == EPI_GATE) {
+            ra = r.r0[0] + u;
+            rb = r.r0[1] + u;
+            na = s.nib[0] / 16 + (uint32_t)u * NB;
+            nb = s.nib[1] / 16 + (uint32_t)u * NB;
+            sa = s.sc[0] / 2 + (uint32_t)u * NB;
+            sb = s.sc[1] / 2 + (uint32_t)u * NB;
+        } else {
+            const int la = 2 * u;
+            const bool two = 2 * u + 1 < r.n[0];
+            const int lb = two ? la + 1 : la;
+            ra = r.r0[0] + la;
+            rb = two ? r.r0[0] + lb : -1;
+            na = s.nib[0] / 16 + (uint32_t)la * NB;
+            nb = s.nib[0] / 16 + (uint32_t)lb * NB;
+            sa = s.sc[0] / 2 + (uint32_t)la * NB;
+            sb = s.sc[0] / 2 + (uint32_t)lb * NB;
+        }
         float acc_a = 0.0f, acc_b = 0.0f;
-        for (int b0 = lane; b0 < NB; b0 += 64) {
-            const int b1 = b0 + 32;
-            const bool has1 = b1 < NB;
-            const uint4 qa0 = __ldg(na + b0), qb0 = __ldg(nb + b0);
-            const uint4 qa1 = has1 ? __ldg(na + b1) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-            const uint4 qb1 = has1 ? __ldg(nb + b1) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-            const float da0 = f16_to_f32_ieee(__ldg(sa + b0)), db0 = f16_to_f32_ieee(__ldg(sb + b0));
-            const float da1 = has1 ? f16_to_f32_ieee(__ldg(sa + b1)) : 0.0f;
-            const float db1 = has1 ? f16_to_f32_ieee(__ldg(sb + b1)) : 0.0f;
+        for (int b = lane; b < NB; b += 32) {
+            const uint4 qa = nibs[na + b], qb = nibs[nb + b];
+            const float x = sm.xs[b];
+            const float da = __fmul_rn(f16_to_f32_ieee(scs[sa + b]), x);
+            const float db = __fmul_rn(f16_to_f32_ieee(scs[sb + b]), x);
             uint4 L[6];
 #pragma unroll
-            for (int v = 0; v < 6; ++v) L[v] = sm.limbs[v * NB + b0];
-            const float x0 = sm.xs[b0];
-            acc_a = __fmaf_rn(block_dp4a(qa0, L), __fmul_rn(da0, x0), acc_a);
-            acc_b = __fmaf_rn(block_dp4a(qb0, L), __fmul_rn(db0, x0), acc_b);
-            if (has1) {
-#pragma unroll
-                for (int v = 0; v < 6; ++v) L[v] = sm.limbs[v * NB + b1];
-                const float x1 = sm.xs[b1];
-                acc_a = __fmaf_rn(block_dp4a(qa1, L), __fmul_rn(da1, x1), acc_a);
-                acc_b = __fmaf_rn(block_dp4a(qb1, L), __fmul_rn(db1, x1), acc_b);
-            }
+            for (int v = 0; v < 6; ++v) L[v] = sm.limbs[v * NB + b];
+            acc_a = __fmaf_rn(block_dp4a(qa, L), da, acc_a);
+            acc_b = __fmaf_rn(block_dp4a(qb, L), db, acc_b);
         }
         float va = warp_sum(acc_a), vb = warp_sum(acc_b);
         if (lane != 0) continue;
@@ -375,26 +494,32 @@ __device__ void gemv_phase(const MegaArgs& P, Smem& sm, const Q4Dev& W, int laye
         } else if (EPI == EPI_LOGITS) {
             c.logits[ra] = va;
             if (c.desc->logits) c.desc->logits[(int64_t)frame * c.V + ra] = va;
-            if (va > best->v || (va == best->v && ra < best->i)) { best->v = va; best->i = ra; }
+            if (va > best->v || (va == best->v && ra < best->i)) {
+                best->v = va;
+                best->i = ra;
+            }
             if (rb >= 0) {
                 c.logits[rb] = vb;
                 if (c.desc->logits) c.desc->logits[(int64_t)frame * c.V + rb] = vb;
-                if (vb > best->v || (vb == best->v && rb < best->i)) { best->v = vb; best->i = rb; }
+                if (vb > best->v || (vb == best->v && rb < best->i)) {
+                    best->v = vb;
+                    best->i = rb;
+                }
             }
-        } else {  // EPI_QKV: RoPE on q and k pairs, K/V ring write
+        } else {  // EPI_QKV: RoPE on q and k pairs, K/V ring write (row pairs are always complete)
             const int D = c.D, HD = c.HD;
             const int part = ra / D;
             const int within = ra - part * D;
             const int h = within / HD, d = within - h * HD;
             if (part < 2) {
                 const float2 cs = c.rope[(int64_t)st.offset * (HD >> 1) + (d >> 1)];
-                const float r = __fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y));
+                const float re = __fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y));
                 const float im = __fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x));
-                va = r;
+                va = re;
                 vb = im;
             }
             c.qkv[ra] = va;
-            c.qkv[rb] = vb;
+            c.qkv[ra + 1] = vb;
             if (part >= 1) {
                 const int64_t off = (int64_t)c.ids[0] * c.kv_stream_stride + (int64_t)layer * c.kv_layer_stride +
                                     (part == 2 ? c.kv_half_stride : 0) + ((int64_t)h * c.ML + st.write_pos) * HD + d;
@@ -413,6 +538,25 @@ __device__ void gemv_phase(const MegaArgs& P, Smem& sm, const Q4Dev& W, int laye
 
 // ------------------------------------------------------------------------------ attention
 
+constexpr int kKeysPerBatch = 4;  // keys a warp loads before computing
+
+template <typename KT>
+__device__ __forceinline__ void load_kv(const KT* kp, const KT* vp, int lane, float4& k, float4& v) {
+    if (sizeof(KT) == 4) {
+        k = __ldcg(reinterpret_cast<const float4*>(kp) + lane);
+        v = __ldcg(reinterpret_cast<const float4*>(vp) + lane);
+    } else {
+        const uint2 kr = __ldcg(reinterpret_cast<const uint2*>(kp) + lane);
+        const uint2 vr = __ldcg(reinterpret_cast<const uint2*>(vp) + lane);
+        k = make_float4(__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xFFFF0000u), __uint_as_float(kr.y << 16),
+                        __uint_as_float(kr.y & 0xFFFF0000u));
+        v = make_float4(__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xFFFF0000u), __uint_as_float(vr.y << 16),
+                        __uint_as_float(vr.y & 0xFFFF0000u));
+    }
+}
+
+// Split-KV attention of head h = cta / nsplit over keys [s*chunk, min(len, (s+1)*chunk)).  The
+// CTA finishing last for a head combines the splits in split order.
 template <typename KT>
 __device__ void attention_phase(const MegaArgs& P, Smem& sm, int layer, const StreamState& st, int cta) {
     const Ctx& c = P.c;
@@ -430,39 +574,38 @@ __device__ void attention_phase(const MegaArgs& P, Smem& sm, int layer, const St
     const KT* vbase = kbase + c.kv_half_stride;
     float m = -FLT_MAX, l = 0.0f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = j0 + warp; j < j1; j += kWarps) {
-        float4 k, v;
-        if (sizeof(KT) == 4) {
-            k = __ldcg(reinterpret_cast<const float4*>(kbase + (int64_t)j * HD) + lane);
-            v = __ldcg(reinterpret_cast<const float4*>(vbase + (int64_t)j * HD) + lane);
-        } else {
-            const uint2 kr = __ldcg(reinterpret_cast<const uint2*>(kbase + (int64_t)j * HD) + lane);
-            const uint2 vr = __ldcg(reinterpret_cast<const uint2*>(vbase + (int64_t)j * HD) + lane);
-            k = make_float4(__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xFFFF0000u),
-                            __uint_as_float(kr.y << 16), __uint_as_float(kr.y & 0xFFFF0000u));
-            v = make_float4(__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xFFFF0000u),
-                            __uint_as_float(vr.y << 16), __uint_as_float(vr.y & 0xFFFF0000u));
+    for (int base = j0 + warp; base < j1; base += kWarps * kKeysPerBatch) {
+        float4 kk[kKeysPerBatch], vv[kKeysPerBatch];
+#pragma unroll
+        for (int t = 0; t < kKeysPerBatch; ++t) {
+            const int j = base + t * kWarps;
+            if (j < j1) load_kv<KT>(kbase + (int64_t)j * HD, vbase + (int64_t)j * HD, lane, kk[t], vv[t]);
         }
-        float dot = __fmul_rn(q.x, k.x);
-        dot = __fmaf_rn(q.y, k.y, dot);
-        dot = __fmaf_rn(q.z, k.z, dot);
-        dot = __fmaf_rn(q.w, k.w, dot);
-        dot = warp_sum(dot);
-        const float score = __fmul_rn(dot, c.attn_scale);
-        const float mn = fmaxf(m, score);
-        const float corr = expf(m - mn);
-        const float p = expf(score - mn);
-        l = __fmaf_rn(l, corr, p);
-        o.x = __fmaf_rn(o.x, corr, __fmul_rn(p, v.x));
-        o.y = __fmaf_rn(o.y, corr, __fmul_rn(p, v.y));
-        o.z = __fmaf_rn(o.z, corr, __fmul_rn(p, v.z));
-        o.w = __fmaf_rn(o.w, corr, __fmul_rn(p, v.w));
-        m = mn;
+#pragma unroll
+        for (int t = 0; t < kKeysPerBatch; ++t) {
+            const int j = base + t * kWarps;
+            if (j >= j1) break;
+            float dot = __fmul_rn(q.x, kk[t].x);
+            dot = __fmaf_rn(q.y, kk[t].y, dot);
+            dot = __fmaf_rn(q.z, kk[t].z, dot);
+            dot = __fmaf_rn(q.w, kk[t].w, dot);
+            dot = warp_sum(dot);
+            const float score = __fmul_rn(dot, c.attn_scale);
+            const float mn = fmaxf(m, score);
+            const float corr = expf(m - mn);
+            const float p = expf(score - mn);
+            l = __fmaf_rn(l, corr, p);
+            o.x = __fmaf_rn(o.x, corr, __fmul_rn(p, vv[t].x));
+            o.y = __fmaf_rn(o.y, corr, __fmul_rn(p, vv[t].y));
+            o.z = __fmaf_rn(o.z, corr, __fmul_rn(p, vv[t].z));
+            o.w = __fmaf_rn(o.w, corr, __fmul_rn(p, vv[t].w));
+            m = mn;
+        }
     }
-    // combine the warps in warp order through shared memory (reuses xf as scratch)
-    float* wm = sm.xf;              // [kWarps]
-    float* wl = sm.xf + kWarps;     // [kWarps]
-    float4* wo = reinterpret_cast<float4*>(sm.xf + 2 * kWarps);  // [kWarps][32]
+    // combine the warps in warp order through shared memory (xf as scratch)
+    float* wm = sm.xf;
+    float* wl = sm.xf + kWarps;
+    float4* wo = reinterpret_cast<float4*>(sm.xf + 2 * kWarps);
     if (lane == 0) {
         wm[warp] = m;
         wl[warp] = l;
@@ -538,7 +681,7 @@ __device__ __forceinline__ float emb_val(const Ctx& c, const uint8_t* table, uin
     }
 }
 
-// xa[j] for this CTA's slice of j: sum of the 32 audio rows of `frame` in codebook order.
+// xa[j] for this CTA's slice of j: sum of the audio rows of `frame` in codebook order.
 __device__ void audio_sum_slice(const MegaArgs& P, int frame, int cta, int ncta) {
     const Ctx& c = P.c;
     const uint32_t* audio = c.desc->audio + (int64_t)frame * c.NC;
@@ -560,145 +703,205 @@ __device__ void audio_sum_slice(const MegaArgs& P, int frame, int cta, int ncta)
 
 // ------------------------------------------------------------------------------ kernel
 
+struct Look {
+    int next;  // next global phase to L2-prefetch
+    int end;   // one past the last global phase of the launch
+};
+
+// Thread 0, after staging global phase `staged`: L2-prefetch later phases until pf_budget bytes
+// are requested beyond it.
+__device__ void look_ahead(const Smem& sm, const MegaArgs& P, Look& lk, int staged, int per_frame, int cta, int ncta,
+                           int len) {
+    if (lk.next <= staged) lk.next = staged + 1;
+    uint32_t ahead = 0;
+    for (int g = staged + 1; g < lk.next; ++g) ahead += phase_bytes(sm, P, g % per_frame, cta, ncta, len);
+    while (lk.next < lk.end && ahead < P.pf_budget) {
+        const int p = lk.next % per_frame;
+        prefetch_phase(sm, P, p, cta, ncta, len);
+        ahead += phase_bytes(sm, P, p, cta, ncta, len);
+        ++lk.next;
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant__ MegaArgs P) {
     extern __shared__ uint4 smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
     const Ctx& c = P.c;
     const int cta = blockIdx.x, ncta = gridDim.x;
-    uint32_t epoch = 0;
+    const int per_frame = 5 * c.L + 1;
+    uint32_t epoch = 0, parity = 0;
+    Tracer tr;
+    Look lk{0, per_frame * P.steps};
+
+    for (int i = threadIdx.x; i < c.L; i += kThreads) sm.layers[i] = c.layers[i];
+    if (threadIdx.x == 0) {
+        mbar_init(&sm.mbar, 1);
+        sm.staged = sm.waited = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
     const int sid = c.ids[0];
     StreamState st = c.state[sid];
     StepDesc* desc = c.desc;
-    const int per_frame = 5 * c.L + 1;
-    Prefetcher pf{0, per_frame * P.steps};
-    Tracer tr;
-
-    // prologue: audio sum of frame 0
+    if (threadIdx.x == 0) {
+        stage_phase(sm, c, 0, cta, ncta);
+        look_ahead(sm, P, lk, 0, per_frame, cta, ncta, min(st.len + 1, c.ML));
+    }
     audio_sum_slice(P, 0, cta, ncta);
-    if (!grid_sync(P, epoch, sm, tr)) return;
+    if (!grid_sync(P, epoch, sm, tr)) goto drain;
 
     for (int f = 0; f < P.steps; ++f) {
         tr.on = P.trace != nullptr && cta == 0 && f == P.trace_frame;
         tr.mark(P);
-        const int len_now = min(st.len + 1, c.ML);
-        // text token of this frame
-        uint32_t text = desc->text ? __ldcg(desc->text + f) : st.last_text;
-        if (text >= (uint32_t)c.TV) {
-            raise_error(desc, -1);
-            text = 0;
-        }
-        // x = audio sum + text row (model.rs:640-646); every CTA builds it, CTA slices are stored
-        for (int j = threadIdx.x; j < c.D; j += kThreads) {
-            const float v = __fadd_rn(__ldcg(P.xa + j), emb_val(c, c.emb_text, text, j));
-            sm.xf[j] = v;
-        }
-        __syncthreads();
         {
-            const int j0 = (int)split_lo(c.D, cta, ncta), j1 = (int)split_lo(c.D, cta + 1, ncta);
-            for (int j = j0 + (int)threadIdx.x; j < j1; j += kThreads) c.x[j] = sm.xf[j];
-        }
-        for (int l = 0; l < c.L; ++l) {
-            const LayerDev& Lw = c.layers[l];
-            const int gp = f * per_frame + 5 * l;
-            // ---- QKV
-            pf.run(P, gp + PH_QKV, cta, ncta, len_now);
-            if (l == 0) {
-                // norm1 of the frame input already staged in xf
-                float ss = 0.0f;
-                for (int j = threadIdx.x; j < c.D; j += kThreads) ss = __fmaf_rn(sm.xf[j], sm.xf[j], ss);
-                ss = block_reduce_sum(ss, sm);
-                const float rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)c.D), 1e-8f));
-                for (int j = threadIdx.x; j < c.D; j += kThreads)
-                    sm.xf[j] = __fmul_rn(__fdiv_rn(sm.xf[j], rms), Lw.norm1[j]);
-                __syncthreads();
-                build_limbs(sm, c.D);
-                __syncthreads();
-            } else {
-                load_vector(sm, c.x, c.D, Lw.norm1);
+            const int len_now = min(st.len + 1, c.ML);
+            uint32_t text = desc->text ? __ldcg(desc->text + f) : st.last_text;
+            if (text >= (uint32_t)c.TV) {
+                raise_error(desc, -1);
+                text = 0;
             }
-            gemv_phase<EPI_QKV>(P, sm, Lw.qkv, l, st, cta, ncta, nullptr, f);
-            if (!grid_sync(P, epoch, sm, tr)) return;
-            // ---- attention
-            pf.run(P, gp + PH_ATT, cta, ncta, len_now);
-            if (c.kv_f32) attention_phase<float>(P, sm, l, st, cta);
-            else attention_phase<__nv_bfloat16>(P, sm, l, st, cta);
-            if (!grid_sync(P, epoch, sm, tr)) return;
-            // ---- out_proj + residual
-            pf.run(P, gp + PH_OUT, cta, ncta, len_now);
-            load_vector(sm, c.attn, c.D, nullptr);
-            gemv_phase<EPI_RESID>(P, sm, Lw.out, l, st, cta, ncta, nullptr, f);
-            if (!grid_sync(P, epoch, sm, tr)) return;
-            // ---- linear_in + silu gate
-            pf.run(P, gp + PH_IN, cta, ncta, len_now);
-            load_vector(sm, c.x, c.D, Lw.norm2);
-            gemv_phase<EPI_GATE>(P, sm, Lw.fin, l, st, cta, ncta, nullptr, f);
-            if (!grid_sync(P, epoch, sm, tr)) return;
-            // ---- linear_out + residual
-            pf.run(P, gp + PH_DOWN, cta, ncta, len_now);
-            load_vector(sm, c.hid, c.F, nullptr);
-            gemv_phase<EPI_RESID>(P, sm, Lw.fout, l, st, cta, ncta, nullptr, f);
-            if (!grid_sync(P, epoch, sm, tr)) return;
-        }
-        // ---- head + argmax partials; audio sum of the next frame
-        pf.run(P, f * per_frame + 5 * c.L, cta, ncta, min(st.len + 2, c.ML));
-        load_vector(sm, c.x, c.D, c.out_norm);
-        HeadBest best{-FLT_MAX, 0x7FFFFFFF};
-        gemv_phase<EPI_LOGITS>(P, sm, c.head, 0, st, cta, ncta, &best, f);
-        {
-            const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-            if (lane == 0) {
-                sm.wv[warp] = best.v;
-                sm.wi[warp] = best.i;
-            }
+            // x = audio sum + text row (model.rs:640-646); every CTA builds all of it and stores its slice
+            for (int j = threadIdx.x; j < c.D; j += kThreads)
+                sm.xf[j] = __fadd_rn(__ldcg(P.xa + j), emb_val(c, c.emb_text, text, j));
             __syncthreads();
-            if (threadIdx.x == 0) {
-                float bv = -FLT_MAX;
-                int bi = 0x7FFFFFFF;
-                for (int w = 0; w < kWarps; ++w)
-                    if (sm.wv[w] > bv || (sm.wv[w] == bv && sm.wi[w] < bi)) {
-                        bv = sm.wv[w];
-                        bi = sm.wi[w];
+            {
+                const int j0 = (int)split_lo(c.D, cta, ncta), j1 = (int)split_lo(c.D, cta + 1, ncta);
+                for (int j = j0 + (int)threadIdx.x; j < j1; j += kThreads) c.x[j] = sm.xf[j];
+            }
+            for (int l = 0; l < c.L; ++l) {
+                const LayerDev& Lw = sm.layers[l];
+                const int p0 = 5 * l, gp0 = f * per_frame + p0;
+                // ---- QKV (its weights were staged before the previous barrier)
+                if (l == 0) {
+                    norm_in_place(sm, c.D, Lw.norm1);
+                    __syncthreads();
+                    build_limbs(sm, c.D);
+                    __syncthreads();
+                } else {
+                    load_vector(sm, c.x, c.D, Lw.norm1);
+                }
+                if (!wait_stage(sm, P, parity)) goto drain;
+                gemv_phase<EPI_QKV>(P, sm, rows_of(sm, c, p0 + K_QKV, cta, ncta), l, st, nullptr, f);
+                __syncthreads();
+                if (threadIdx.x == 0) {  // out_proj rows: attention does not use the staging buffer
+                    stage_phase(sm, c, p0 + K_OUT, cta, ncta);
+                    look_ahead(sm, P, lk, gp0 + K_OUT, per_frame, cta, ncta, len_now);
+                }
+                if (!grid_sync(P, epoch, sm, tr)) goto drain;
+                // ---- attention
+                if (c.kv_f32) attention_phase<float>(P, sm, l, st, cta);
+                else attention_phase<__nv_bfloat16>(P, sm, l, st, cta);
+                if (!grid_sync(P, epoch, sm, tr)) goto drain;
+                // ---- out_proj + residual
+                load_vector(sm, c.attn, c.D, nullptr);
+                if (!wait_stage(sm, P, parity)) goto drain;
+                gemv_phase<EPI_RESID>(P, sm, rows_of(sm, c, p0 + K_OUT, cta, ncta), l, st, nullptr, f);
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    stage_phase(sm, c, p0 + K_IN, cta, ncta);
+                    look_ahead(sm, P, lk, gp0 + K_IN, per_frame, cta, ncta, len_now);
+                }
+                if (!grid_sync(P, epoch, sm, tr)) goto drain;
+                // ---- linear_in + silu gate
+                load_vector(sm, c.x, c.D, Lw.norm2);
+                if (!wait_stage(sm, P, parity)) goto drain;
+                gemv_phase<EPI_GATE>(P, sm, rows_of(sm, c, p0 + K_IN, cta, ncta), l, st, nullptr, f);
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    stage_phase(sm, c, p0 + K_DOWN, cta, ncta);
+                    look_ahead(sm, P, lk, gp0 + K_DOWN, per_frame, cta, ncta, len_now);
+                }
+                if (!grid_sync(P, epoch, sm, tr)) goto drain;
+                // ---- linear_out + residual
+                load_vector(sm, c.hid, c.F, nullptr);
+                if (!wait_stage(sm, P, parity)) goto drain;
+                gemv_phase<EPI_RESID>(P, sm, rows_of(sm, c, p0 + K_DOWN, cta, ncta), l, st, nullptr, f);
+                __syncthreads();
+                if (threadIdx.x == 0) {  // next: QKV of layer l+1, or the head
+                    const int pn = l + 1 < c.L ? p0 + 5 : 5 * c.L;
+                    stage_phase(sm, c, pn, cta, ncta);
+                    look_ahead(sm, P, lk, f * per_frame + pn, per_frame, cta, ncta, len_now);
+                }
+                if (!grid_sync(P, epoch, sm, tr)) goto drain;
+            }
+            // ---- head + argmax partials; audio sum of the next frame
+            load_vector(sm, c.x, c.D, c.out_norm);
+            if (!wait_stage(sm, P, parity)) goto drain;
+            HeadBest best{-FLT_MAX, 0x7FFFFFFF};
+            gemv_phase<EPI_LOGITS>(P, sm, rows_of(sm, c, 5 * c.L, cta, ncta), 0, st, &best, f);
+            {
+                const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+                if (lane == 0) {
+                    sm.wv[warp] = best.v;
+                    sm.wi[warp] = best.i;
+                }
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    float bv = -FLT_MAX;
+                    int bi = 0x7FFFFFFF;
+                    for (int w = 0; w < kWarps; ++w)
+                        if (sm.wv[w] > bv || (sm.wv[w] == bv && sm.wi[w] < bi)) {
+                            bv = sm.wv[w];
+                            bi = sm.wi[w];
+                        }
+                    P.amax_v[cta] = bv;
+                    P.amax_i[cta] = bi;
+                    if (f + 1 < P.steps) {  // the next frame starts with layer 0's QKV
+                        stage_phase(sm, c, 0, cta, ncta);
+                        look_ahead(sm, P, lk, (f + 1) * per_frame, per_frame, cta, ncta, min(st.len + 2, c.ML));
                     }
-                P.amax_v[cta] = bv;
-                P.amax_i[cta] = bi;
+                }
             }
+            if (f + 1 < P.steps) audio_sum_slice(P, f + 1, cta, ncta);
+            if (!grid_sync(P, epoch, sm, tr)) goto drain;
         }
-        if (f + 1 < P.steps) audio_sum_slice(P, f + 1, cta, ncta);
-        if (!grid_sync(P, epoch, sm, tr)) return;
         // every CTA reduces the partials identically
-        float bv = -FLT_MAX;
-        int bi = 0x7FFFFFFF;
-        for (int t = 0; t < ncta; ++t) {
-            const float v = __ldcg(P.amax_v + t);
-            const int i = __ldcg(P.amax_i + t);
-            if (v > bv || (v == bv && i < bi)) {
-                bv = v;
-                bi = i;
+        {
+            float bv = -FLT_MAX;
+            int bi = 0x7FFFFFFF;
+            for (int t = 0; t < ncta; ++t) {
+                const float v = __ldcg(P.amax_v + t);
+                const int i = __ldcg(P.amax_i + t);
+                if (v > bv || (v == bv && i < bi)) {
+                    bv = v;
+                    bi = i;
+                }
             }
-        }
-        const uint32_t token = (uint32_t)(bi == 0x7FFFFFFF ? 0 : bi);
-        st.write_pos = (st.write_pos + 1) % c.ML;
-        st.offset += 1;
-        st.len = min(st.len + 1, c.ML);
-        int32_t out = (int32_t)token;
-        if (desc->mode == 1) {
-            st.frame_count += 1;
-            if (st.frame_count >= c.text_delay) {
-                st.last_text = token;
-            } else {
-                const uint32_t p0 = st.prev0, p1 = st.prev1;
-                st.prev0 = p1;
-                st.prev1 = token;
-                st.last_text = (token != c.pad_id && token != 0u && token == p0 && token != p1) ? c.pad_id : token;
-                out = -1;
+            const uint32_t token = (uint32_t)(bi == 0x7FFFFFFF ? 0 : bi);
+            st.write_pos = (st.write_pos + 1) % c.ML;
+            st.offset += 1;
+            st.len = min(st.len + 1, c.ML);
+            int32_t out = (int32_t)token;
+            if (desc->mode == 1) {
+                st.frame_count += 1;
+                if (st.frame_count >= c.text_delay) {
+                    st.last_text = token;
+                } else {
+                    const uint32_t p0 = st.prev0, p1 = st.prev1;
+                    st.prev0 = p1;
+                    st.prev1 = token;
+                    st.last_text = (token != c.pad_id && token != 0u && token == p0 && token != p1) ? c.pad_id : token;
+                    out = -1;
+                }
             }
-        }
-        if (cta == 0 && threadIdx.x == 0) {
-            desc->tokens[f] = out;
-            c.state[sid] = st;
-            if (f + 1 == P.steps) desc->step = P.steps;
+            if (cta == 0 && threadIdx.x == 0) {
+                desc->tokens[f] = out;
+                c.state[sid] = st;
+                if (f + 1 == P.steps) desc->step = P.steps;
+            }
         }
     }
+    return;
+drain:
+    // stopping early: a staged copy that was issued but not yet waited for (stages and waits
+    // alternate, so one is pending exactly when the issue count exceeds the wait count) must land
+    // before the CTA's shared memory goes away
+    if (threadIdx.x == 0 && sm.staged != sm.waited) {
+        uint32_t spins = 0;
+        while (!mbar_try_wait(&sm.mbar, parity) && ++spins < kSpinLimit) {
+        }
+    }
+    __syncthreads();
 }
 
 // Grid-barrier latency probe: `iters` back-to-back barriers of the persistent kernel.
@@ -711,13 +914,28 @@ __global__ void __launch_bounds__(kThreads, 1) barrier_probe_kernel(const __grid
         if (!grid_sync(P, epoch, sm, tr)) return;
 }
 
+// Largest staged phase of one CTA in bytes (must fit kWBuf).
+size_t max_stage_bytes(int D, int F, int V, int ncta) {
+    auto rows_max = [&](int64_t units, int rows_per_unit) { return (units + ncta - 1) / ncta * rows_per_unit; };
+    auto bytes = [](int64_t rows, int k) {
+        return (size_t)rows * (k / 32) * 16 + (((size_t)rows * (k / 32) * 2 + 15) & ~(size_t)15);
+    };
+    size_t m = bytes(rows_max(3 * D / 2, 2), D);
+    m = std::max(m, bytes(rows_max(D / 2, 2), D));
+    m = std::max(m, 2 * bytes(rows_max(F, 1), D));
+    m = std::max(m, bytes(rows_max(D / 2, 2), F));
+    m = std::max(m, bytes(rows_max((V + 1) / 2, 2), D));
+    return m;
+}
+
 }  // namespace
 
 cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out) {
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(barrier_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(barrier_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
     if (e != cudaSuccess) return e;
     MegaArgs P{};
     P.bar = static_cast<uint32_t*>(scratch);
@@ -727,7 +945,8 @@ cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out) {
     e = cudaMemset(P.bar, 0, 256);
     void* args[] = {(void*)&P, (void*)&iters};
     if (e == cudaSuccess) e = cudaEventRecord(a, 0);
-    if (e == cudaSuccess) e = cudaLaunchCooperativeKernel((const void*)barrier_probe_kernel, dim3(sms), dim3(kThreads), args, sizeof(Smem), 0);
+    if (e == cudaSuccess)
+        e = cudaLaunchCooperativeKernel((const void*)barrier_probe_kernel, dim3(sms), dim3(kThreads), args, sizeof(Smem), 0);
     if (e == cudaSuccess) e = cudaEventRecord(b, 0);
     if (e == cudaSuccess) e = cudaEventSynchronize(b);
     if (e == cudaSuccess) e = cudaEventElapsedTime(ms_out, a, b);
@@ -736,9 +955,10 @@ cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out) {
     return e;
 }
 
-bool mega_supported(int L, int D, int F, int HD) {
-    // head tickets live in the 64-word barrier block: 2 + H <= 64
-    return HD == 128 && D % 256 == 0 && D <= kMaxK && F % 128 == 0 && F <= kMaxK && L > 0 && D / HD <= 60 &&
+bool mega_supported(int L, int D, int F, int HD, int V, int num_sms) {
+    // head tickets live in the 64-word barrier block (2 + H <= 64); the layer table holds kMaxL
+    return HD == 128 && D % 256 == 0 && D <= kMaxK && F % 128 == 0 && F <= kMaxK && L > 0 && L <= kMaxL &&
+           D / HD <= 60 && max_stage_bytes(D, F, V, num_sms) <= (size_t)kWBuf &&
            std::getenv("STT_DISABLE_MEGA") == nullptr;
 }
 
@@ -754,8 +974,7 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
     int dev = 0, sms = 0, occ = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess)
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, mega_kernel, kThreads, sizeof(Smem));
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, mega_kernel, kThreads, sizeof(Smem));
     if (e != cudaSuccess) return e;
     if (occ < 1) return cudaErrorCooperativeLaunchTooLarge;
     uint8_t* s = static_cast<uint8_t*>(ms.scratch);
@@ -767,7 +986,7 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
     P.xa = reinterpret_cast<float*>(s + 256);
     P.amax_v = reinterpret_cast<float*>(s + 256 + (size_t)c.D * 4);
     P.amax_i = reinterpret_cast<int32_t*>(s + 256 + (size_t)c.D * 4 + (size_t)sms * 4);
-    P.pf_budget = 256u * 1024u;
+    P.pf_budget = 384u * 1024u;
     if (const char* pb = std::getenv("STT_MEGA_PF_KB")) P.pf_budget = (uint32_t)std::atoi(pb) * 1024u;
     P.trace = nullptr;
     P.trace_frame = -1;

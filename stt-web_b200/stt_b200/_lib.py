@@ -116,6 +116,7 @@ SIGNATURES = {
     "stt_streams_feed_frame_device": (C.c_int, [P, I32P, C.c_int, P, P, P]),
     "stt_stream_flush": (C.c_int, [P, C.c_int, U32P, C.c_int, I32P]),
     "stt_stream_reset": (C.c_int, [P, C.c_int, C.c_int]),
+    "stt_stream_reset_async": (C.c_int, [P, C.c_int, C.c_int, P]),
     "stt_stream_set_last_text_token": (C.c_int, [P, C.c_int, C.c_uint32]),
     "stt_stream_get_state": (C.c_int, [P, C.c_int, C.POINTER(stt_stream_state)]),
     "stt_q4_tensor_create": (C.c_int, [U8P, C.c_size_t, C.c_int, C.c_int, C.c_int, C.POINTER(P)]),
