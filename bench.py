@@ -48,6 +48,23 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
+TRACE_NAMES = {1: "frame_start", 2: "barrier_arrive", 3: "barrier_wait", 10: "qkv_prologue", 11: "qkv_stage_wait",
+               12: "qkv_gemv", 22: "attention", 30: "out_proj_prologue", 31: "out_proj_stage_wait",
+               32: "out_proj_gemv", 40: "linear_in_prologue", 41: "linear_in_stage_wait", 42: "linear_in_gemv",
+               50: "linear_out_prologue", 51: "linear_out_stage_wait", 52: "linear_out_gemv",
+               60: "head_prologue", 61: "head_stage_wait", 62: "head_gemv"}
+
+
+def trace_breakdown(raw):
+    """(tag, ns) pairs of one traced frame -> microseconds spent reaching each kind of mark."""
+    pairs = [(raw[i], raw[i + 1]) for i in range(0, len(raw) - 1, 2)]
+    out = {}
+    for (t0, a), (t1, b) in zip(pairs, pairs[1:]):
+        k = TRACE_NAMES.get(t1, str(t1))
+        out[k] = out.get(k, 0.0) + (b - a) / 1e3
+    return {"frame_us": (pairs[-1][1] - pairs[0][1]) / 1e3, "trace_us": {k: round(v, 2) for k, v in out.items()}}
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -243,20 +260,9 @@ def main():
     torch.cuda.synchronize()
     buf = (C.c_uint64 * 1024)()
     nt = C.c_int()
-    if lib().stt_debug_get_trace(cache._h, buf, 1024, C.byref(nt)) == 0 and nt.value > 3:
-        t = [buf[i] for i in range(nt.value)]
-        names = ["qkv", "attention", "out_proj", "linear_in", "linear_out"] * 16 + ["head"]
-        work = {k: 0.0 for k in set(names)}
-        wait = {k: 0.0 for k in set(names)}
-        prev = t[0]
-        for k, name in enumerate(names[: (len(t) - 1) // 2]):
-            work[name] += (t[1 + 2 * k] - prev) / 1e3
-            wait[name] += (t[2 + 2 * k] - t[1 + 2 * k]) / 1e3
-            prev = t[2 + 2 * k]
+    if lib().stt_debug_get_trace(cache._h, buf, 1024, C.byref(nt)) == 0 and nt.value > 4:
+        diag.update(trace_breakdown([buf[i] for i in range(nt.value)]))
         diag["traced_frame"] = FRAMES - 10
-        diag["frame_us"] = (t[-1] - t[0]) / 1e3
-        diag["phase_work_us"] = {k: round(v, 2) for k, v in work.items()}
-        diag["phase_barrier_us"] = {k: round(v, 2) for k, v in wait.items()}
     lib().stt_debug_trace_frame(cache._h, -1)
 
     # ---- roofline of the decode step (every kernel of a frame, device-timed above)

@@ -47,6 +47,7 @@ struct MegaArgs {
     float* amax_v;         // [grid] per-CTA best logit
     int32_t* amax_i;       // [grid] and its index
     uint32_t pf_budget;    // L2 look-ahead per CTA in bytes
+    int32_t pf_lines;      // 1: warp 0 prefetches 128-byte lines; 0: bulk prefetch (TMA queue)
     unsigned long long* trace;  // optional: %globaltimer at each barrier of one frame
     int32_t trace_frame;
     int32_t trace_cap;
@@ -78,6 +79,18 @@ __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
 }
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void prefetch_line(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+// Called by all 32 lanes of warp 0: bulk prefetch by lane 0, or line prefetches spread over lanes.
+__device__ __forceinline__ void prefetch_range(const void* p, uint32_t bytes, bool lines, int lane) {
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    if (lines) {
+        for (uint32_t o = (uint32_t)lane * 128u; o < bytes; o += 32u * 128u) prefetch_line(b + o);
+    } else if (lane == 0) {
+        for (uint32_t o = 0; o < bytes; o += 65536u) prefetch_l2(b + o, min(65536u, bytes - o));
+    }
 }
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -124,11 +137,18 @@ __device__ __forceinline__ unsigned long long globaltimer() {
     return t;
 }
 
+// Trace points of one frame of CTA 0: (tag, %globaltimer) pairs.  Tags: 1 frame start,
+// 2 barrier entry, 3 barrier exit, 10*k + {0 prologue done, 1 staged copy landed, 2 compute done}
+// for phase kinds k = 1 qkv, 2 attention, 3 out_proj, 4 linear_in, 5 linear_out, 6 head.
 struct Tracer {
     int slot = 0;
     bool on = false;
-    __device__ void mark(const MegaArgs& P) {
-        if (on && threadIdx.x == 0 && slot < P.trace_cap) P.trace[slot++] = globaltimer();
+    __device__ void mark(const MegaArgs& P, unsigned long long tag) {
+        if (on && threadIdx.x == 0 && slot + 1 < P.trace_cap) {
+            P.trace[slot] = tag;
+            P.trace[slot + 1] = globaltimer();
+            slot += 2;
+        }
     }
 };
 
@@ -137,7 +157,7 @@ __device__ __forceinline__ int64_t split_lo(int64_t total, int part, int parts) 
 // Grid barrier.  Returns false when the kernel must stop (a timeout here or in another CTA).
 __device__ bool grid_sync(const MegaArgs& P, uint32_t& epoch, Smem& sm, Tracer& tr) {
     __syncthreads();
-    tr.mark(P);
+    tr.mark(P, 2);
     ++epoch;
     if (threadIdx.x == 0) {
         const uint32_t target = epoch * gridDim.x;
@@ -161,7 +181,7 @@ __device__ bool grid_sync(const MegaArgs& P, uint32_t& epoch, Smem& sm, Tracer& 
         sm.flag = ok;
     }
     __syncthreads();
-    tr.mark(P);
+    tr.mark(P, 3);
     return sm.flag != 0;
 }
 
@@ -257,9 +277,10 @@ __device__ uint32_t phase_bytes(const Smem& sm, const MegaArgs& P, int p, int ct
     return b;
 }
 
-// L2 prefetch of one phase's ranges.
-__device__ void prefetch_phase(const Smem& sm, const MegaArgs& P, int p, int cta, int ncta, int len) {
+// L2 prefetch of one phase's ranges (all lanes of warp 0).
+__device__ void prefetch_phase(const Smem& sm, const MegaArgs& P, int p, int cta, int ncta, int len, int lane) {
     const Ctx& c = P.c;
+    const bool lines = P.pf_lines != 0;
     if (kind_of(p, c.L) == K_ATT) {
         const int h = cta / P.nsplit, s = cta % P.nsplit;
         if (h >= c.H) return;
@@ -271,19 +292,17 @@ __device__ void prefetch_phase(const Smem& sm, const MegaArgs& P, int p, int cta
                             ((int64_t)c.ids[0] * c.kv_stream_stride + (int64_t)(p / 5) * c.kv_layer_stride +
                              (int64_t)h * c.ML * c.HD + (int64_t)j0 * c.HD) * es;
         const uint32_t bytes = (uint32_t)(j1 - j0) * c.HD * es;
-        prefetch_l2(kb, bytes);
-        prefetch_l2(kb + c.kv_half_stride * es, bytes);
+        prefetch_range(kb, bytes, lines, lane);
+        prefetch_range(kb + c.kv_half_stride * es, bytes, lines, lane);
         return;
     }
     const Rows r = rows_of(sm, c, p, cta, ncta);
     for (int i = 0; i < r.nr; ++i) {
         if (r.n[i] <= 0) continue;
         const int64_t NB = r.W->k >> 5;
-        const uint8_t* nb = reinterpret_cast<const uint8_t*>(r.W->nib + (int64_t)r.r0[i] * NB);
-        const uint32_t nbytes = (uint32_t)(r.n[i] * NB * 16);
-        for (uint32_t o = 0; o < nbytes; o += 65536u) prefetch_l2(nb + o, min(65536u, nbytes - o));
+        prefetch_range(r.W->nib + (int64_t)r.r0[i] * NB, (uint32_t)(r.n[i] * NB * 16), lines, lane);
         const uint32_t sbytes = (uint32_t)(r.n[i] * NB * 2) & ~15u;
-        if (sbytes) prefetch_l2(r.W->scale + (int64_t)r.r0[i] * NB, sbytes);
+        if (sbytes) prefetch_range(r.W->scale + (int64_t)r.r0[i] * NB, sbytes, lines, lane);
     }
 }
 
@@ -708,16 +727,17 @@ struct Look {
     int end;   // one past the last global phase of the launch
 };
 
-// Thread 0, after staging global phase `staged`: L2-prefetch later phases until pf_budget bytes
-// are requested beyond it.
+// Warp 0, after staging global phase `staged`: L2-prefetch later phases until pf_budget bytes
+// are requested beyond it.  Every lane keeps the same Look state.
 __device__ void look_ahead(const Smem& sm, const MegaArgs& P, Look& lk, int staged, int per_frame, int cta, int ncta,
                            int len) {
+    const int lane = threadIdx.x & 31;
     if (lk.next <= staged) lk.next = staged + 1;
     uint32_t ahead = 0;
     for (int g = staged + 1; g < lk.next; ++g) ahead += phase_bytes(sm, P, g % per_frame, cta, ncta, len);
     while (lk.next < lk.end && ahead < P.pf_budget) {
         const int p = lk.next % per_frame;
-        prefetch_phase(sm, P, p, cta, ncta, len);
+        prefetch_phase(sm, P, p, cta, ncta, len, lane);
         ahead += phase_bytes(sm, P, p, cta, ncta, len);
         ++lk.next;
     }
@@ -743,16 +763,14 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
     const int sid = c.ids[0];
     StreamState st = c.state[sid];
     StepDesc* desc = c.desc;
-    if (threadIdx.x == 0) {
-        stage_phase(sm, c, 0, cta, ncta);
-        look_ahead(sm, P, lk, 0, per_frame, cta, ncta, min(st.len + 1, c.ML));
-    }
+    if (threadIdx.x == 0) stage_phase(sm, c, 0, cta, ncta);
+    if (threadIdx.x < 32) look_ahead(sm, P, lk, 0, per_frame, cta, ncta, min(st.len + 1, c.ML));
     audio_sum_slice(P, 0, cta, ncta);
     if (!grid_sync(P, epoch, sm, tr)) goto drain;
 
     for (int f = 0; f < P.steps; ++f) {
         tr.on = P.trace != nullptr && cta == 0 && f == P.trace_frame;
-        tr.mark(P);
+        tr.mark(P, 1);
         {
             const int len_now = min(st.len + 1, c.ML);
             uint32_t text = desc->text ? __ldcg(desc->text + f) : st.last_text;
@@ -780,53 +798,64 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 } else {
                     load_vector(sm, c.x, c.D, Lw.norm1);
                 }
+                tr.mark(P, 10);
                 if (!wait_stage(sm, P, parity)) goto drain;
+                tr.mark(P, 11);
                 gemv_phase<EPI_QKV>(P, sm, rows_of(sm, c, p0 + K_QKV, cta, ncta), l, st, nullptr, f);
                 __syncthreads();
-                if (threadIdx.x == 0) {  // out_proj rows: attention does not use the staging buffer
-                    stage_phase(sm, c, p0 + K_OUT, cta, ncta);
-                    look_ahead(sm, P, lk, gp0 + K_OUT, per_frame, cta, ncta, len_now);
-                }
+                tr.mark(P, 12);
+                // out_proj rows (attention does not use the staging buffer)
+                if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_OUT, cta, ncta);
+                if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_OUT, per_frame, cta, ncta, len_now);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- attention
                 if (c.kv_f32) attention_phase<float>(P, sm, l, st, cta);
                 else attention_phase<__nv_bfloat16>(P, sm, l, st, cta);
+                __syncthreads();
+                tr.mark(P, 22);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- out_proj + residual
                 load_vector(sm, c.attn, c.D, nullptr);
+                tr.mark(P, 30);
                 if (!wait_stage(sm, P, parity)) goto drain;
+                tr.mark(P, 31);
                 gemv_phase<EPI_RESID>(P, sm, rows_of(sm, c, p0 + K_OUT, cta, ncta), l, st, nullptr, f);
                 __syncthreads();
-                if (threadIdx.x == 0) {
-                    stage_phase(sm, c, p0 + K_IN, cta, ncta);
-                    look_ahead(sm, P, lk, gp0 + K_IN, per_frame, cta, ncta, len_now);
-                }
+                tr.mark(P, 32);
+                if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_IN, cta, ncta);
+                if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_IN, per_frame, cta, ncta, len_now);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- linear_in + silu gate
                 load_vector(sm, c.x, c.D, Lw.norm2);
+                tr.mark(P, 40);
                 if (!wait_stage(sm, P, parity)) goto drain;
+                tr.mark(P, 41);
                 gemv_phase<EPI_GATE>(P, sm, rows_of(sm, c, p0 + K_IN, cta, ncta), l, st, nullptr, f);
                 __syncthreads();
-                if (threadIdx.x == 0) {
-                    stage_phase(sm, c, p0 + K_DOWN, cta, ncta);
-                    look_ahead(sm, P, lk, gp0 + K_DOWN, per_frame, cta, ncta, len_now);
-                }
+                tr.mark(P, 42);
+                if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_DOWN, cta, ncta);
+                if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_DOWN, per_frame, cta, ncta, len_now);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- linear_out + residual
                 load_vector(sm, c.hid, c.F, nullptr);
+                tr.mark(P, 50);
                 if (!wait_stage(sm, P, parity)) goto drain;
+                tr.mark(P, 51);
                 gemv_phase<EPI_RESID>(P, sm, rows_of(sm, c, p0 + K_DOWN, cta, ncta), l, st, nullptr, f);
                 __syncthreads();
-                if (threadIdx.x == 0) {  // next: QKV of layer l+1, or the head
+                tr.mark(P, 52);
+                {  // next: QKV of layer l+1, or the head
                     const int pn = l + 1 < c.L ? p0 + 5 : 5 * c.L;
-                    stage_phase(sm, c, pn, cta, ncta);
-                    look_ahead(sm, P, lk, f * per_frame + pn, per_frame, cta, ncta, len_now);
+                    if (threadIdx.x == 0) stage_phase(sm, c, pn, cta, ncta);
+                    if (threadIdx.x < 32) look_ahead(sm, P, lk, f * per_frame + pn, per_frame, cta, ncta, len_now);
                 }
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
             }
             // ---- head + argmax partials; audio sum of the next frame
             load_vector(sm, c.x, c.D, c.out_norm);
+            tr.mark(P, 60);
             if (!wait_stage(sm, P, parity)) goto drain;
+            tr.mark(P, 61);
             HeadBest best{-FLT_MAX, 0x7FFFFFFF};
             gemv_phase<EPI_LOGITS>(P, sm, rows_of(sm, c, 5 * c.L, cta, ncta), 0, st, &best, f);
             {
@@ -846,13 +875,14 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                         }
                     P.amax_v[cta] = bv;
                     P.amax_i[cta] = bi;
-                    if (f + 1 < P.steps) {  // the next frame starts with layer 0's QKV
-                        stage_phase(sm, c, 0, cta, ncta);
-                        look_ahead(sm, P, lk, (f + 1) * per_frame, per_frame, cta, ncta, min(st.len + 2, c.ML));
-                    }
+                    if (f + 1 < P.steps) stage_phase(sm, c, 0, cta, ncta);  // next frame: layer 0's QKV
                 }
+                if (f + 1 < P.steps && threadIdx.x < 32)
+                    look_ahead(sm, P, lk, (f + 1) * per_frame, per_frame, cta, ncta, min(st.len + 2, c.ML));
             }
             if (f + 1 < P.steps) audio_sum_slice(P, f + 1, cta, ncta);
+            __syncthreads();
+            tr.mark(P, 62);
             if (!grid_sync(P, epoch, sm, tr)) goto drain;
         }
         // every CTA reduces the partials identically
@@ -986,8 +1016,10 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
     P.xa = reinterpret_cast<float*>(s + 256);
     P.amax_v = reinterpret_cast<float*>(s + 256 + (size_t)c.D * 4);
     P.amax_i = reinterpret_cast<int32_t*>(s + 256 + (size_t)c.D * 4 + (size_t)sms * 4);
-    P.pf_budget = 384u * 1024u;
+    P.pf_budget = 128u * 1024u;
     if (const char* pb = std::getenv("STT_MEGA_PF_KB")) P.pf_budget = (uint32_t)std::atoi(pb) * 1024u;
+    P.pf_lines = 1;
+    if (const char* pm = std::getenv("STT_MEGA_PF_BULK")) P.pf_lines = std::atoi(pm) ? 0 : 1;
     P.trace = nullptr;
     P.trace_frame = -1;
     P.trace_cap = 0;
