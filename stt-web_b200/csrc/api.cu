@@ -495,7 +495,7 @@ struct stt_streams {
     uint32_t* d_tickets = nullptr;
     int32_t* d_ids = nullptr;
     StepDesc* d_desc = nullptr;
-    DevBuf in_audio, in_text, out_tokens, out_logits;
+    DevBuf in_audio, in_text, out_tokens, out_logits, mega_xa;
     HostBuf h_stage, h_tokens;
     void* d_scratch = nullptr;
     cudaStream_t stream = nullptr;
@@ -670,6 +670,12 @@ int run_steps(stt_streams* s, const int32_t* ids, int n, int steps, const uint32
         // single-stream steps go through the persistent step kernel
         if (s->mega.trace_frame >= 0)
             CUDA_TRY(cudaMemsetAsync(s->mega.trace, 0, sizeof(unsigned long long) * s->mega.trace_cap, st));
+        if ((size_t)steps * m->D * 4 > s->mega_xa.cap) {
+            // growing reallocates: work still queued on another stream may read the old buffer
+            CUDA_TRY(cudaDeviceSynchronize());
+            TRY(s->mega_xa.ensure((size_t)steps * m->D * 4));
+        }
+        s->mega.xa_all = static_cast<float*>(s->mega_xa.p);
         CUDA_TRY(launch_mega_steps(s->mega, make_ctx(s, 1), m->h_layers.data(), steps, st));
     } else {
         for (int t = 0; t < steps; ++t) CUDA_TRY(cudaGraphLaunch(exec, st));
@@ -799,6 +805,7 @@ extern "C" int stt_streams_destroy(stt_streams* s) {
         s->in_text.release();
         s->out_tokens.release();
         s->out_logits.release();
+        s->mega_xa.release();
         s->h_stage.release();
         s->h_tokens.release();
     }

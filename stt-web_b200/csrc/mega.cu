@@ -36,6 +36,8 @@ constexpr int kNBMax = 264;                // K / 32 for K <= 8448
 constexpr int kMaxK = kNBMax * 32;
 constexpr int kWBuf = 144 * 1024;          // staged weight rows of one phase per CTA
 constexpr int kMaxL = 32;                  // layers held in the shared layer table
+constexpr int kMaxOwnRows = 256;           // rows of x one CTA owns (out_proj / linear_out rows)
+constexpr int kQMax = (kMaxK / 4 + kThreads - 1) / kThreads;  // input quads per thread
 constexpr uint32_t kSpinLimit = 1u << 26;  // bounded waits (~ seconds)
 
 struct MegaArgs {
@@ -43,7 +45,7 @@ struct MegaArgs {
     int32_t steps;
     int32_t nsplit;        // attention splits per head
     uint32_t* bar;         // [0] arrivals (monotonic), [1] abort, [2..2+H) head tickets
-    float* xa;             // [D] audio-embedding sum of the next frame
+    const float* xa;       // [steps][D] audio-embedding sums of every frame (audio_sum_kernel)
     float* amax_v;         // [grid] per-CTA best logit
     int32_t* amax_i;       // [grid] and its index
     uint32_t pf_budget;    // L2 look-ahead per CTA in bytes
@@ -59,7 +61,9 @@ struct Smem {
     float xs[kNBMax];                  // 2^(e_b - 27): block scale of the fixed-point input
     float xf[kMaxK];                   // the input vector in f32 / attention scratch
     LayerDev layers[kMaxL];
-    float red[kWarps];
+    float xown[kMaxOwnRows];           // this CTA's rows of the residual stream x
+    float2 rope[64];                   // (cos, sin) of this frame's position, HD / 2 pairs
+    float red[2][kWarps];
     float wv[kWarps];
     int32_t wi[kWarps];
     alignas(8) unsigned long long mbar;
@@ -360,71 +364,106 @@ __device__ bool wait_stage(Smem& sm, const MegaArgs& P, uint32_t& parity) {
 
 // ------------------------------------------------------------------------------ input vectors
 
-// Builds the dp4a limbs of xf[0..K) (already in shared memory) for every 32-element block.
-__device__ void build_limbs(Smem& sm, int K) {
-    const int NB = K >> 5;
-    for (int q = threadIdx.x; q < (K >> 2); q += kThreads) {  // quad q: elements 4q .. 4q+3
-        const int b = q >> 3, g = q & 7;
-        const float4 v = reinterpret_cast<const float4*>(sm.xf)[q];
-        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
-        m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
-        // max < 2^e with e = biased exponent - 126; scale the block by 2^(23 - e)
-        int e = m > 0.0f ? (int)((__float_as_uint(m) >> 23) & 0xFF) - 126 : 0;
-        e = max(-96, min(e, 120));
-        const float up = __uint_as_float((uint32_t)(127 + 23 - e) << 23);
-        const float vals[4] = {v.x, v.y, v.z, v.w};
-        uint32_t w0 = 0, w1 = 0, w2 = 0;
+// dp4a limbs of one quad (elements 4q .. 4q+3) of block b = q / 8; called by all 32 lanes of a
+// warp with 8 consecutive lanes holding the 8 quads of a block.
+__device__ __forceinline__ void quad_limbs(Smem& sm, int q, int NB, float4 v) {
+    const int b = q >> 3, g = q & 7;
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
+    // max < 2^e with e = biased exponent - 126; scale the block by 2^(23 - e)
+    int e = m > 0.0f ? (int)((__float_as_uint(m) >> 23) & 0xFF) - 126 : 0;
+    e = max(-96, min(e, 120));
+    const float up = __uint_as_float((uint32_t)(127 + 23 - e) << 23);
+    const float vals[4] = {v.x, v.y, v.z, v.w};
+    uint32_t w0 = 0, w1 = 0, w2 = 0;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            int X = __float2int_rn(vals[i] * up);
-            X = max(-(1 << 23), min(X, (1 << 23) - 1));
-            w0 |= (uint32_t)(X & 0xFF) << (8 * i);
-            w1 |= (uint32_t)((X >> 8) & 0xFF) << (8 * i);
-            w2 |= (uint32_t)((X >> 16) & 0xFF) << (8 * i);
-        }
-        uint32_t* L = reinterpret_cast<uint32_t*>(sm.limbs);
-        const int base = g < 4 ? 0 : 3;
-        L[((base + 0) * NB + b) * 4 + (g & 3)] = w0;
-        L[((base + 1) * NB + b) * 4 + (g & 3)] = w1;
-        L[((base + 2) * NB + b) * 4 + (g & 3)] = w2;
-        if (g == 0) sm.xs[b] = __uint_as_float((uint32_t)(127 + e - 27) << 23);
+    for (int i = 0; i < 4; ++i) {
+        int X = __float2int_rn(vals[i] * up);
+        X = max(-(1 << 23), min(X, (1 << 23) - 1));
+        w0 |= (uint32_t)(X & 0xFF) << (8 * i);
+        w1 |= (uint32_t)((X >> 8) & 0xFF) << (8 * i);
+        w2 |= (uint32_t)((X >> 16) & 0xFF) << (8 * i);
     }
+    uint32_t* L = reinterpret_cast<uint32_t*>(sm.limbs);
+    const int base = g < 4 ? 0 : 3;
+    L[((base + 0) * NB + b) * 4 + (g & 3)] = w0;
+    L[((base + 1) * NB + b) * 4 + (g & 3)] = w1;
+    L[((base + 2) * NB + b) * 4 + (g & 3)] = w2;
+    if (g == 0) sm.xs[b] = __uint_as_float((uint32_t)(127 + e - 27) << 23);
 }
 
-__device__ float block_reduce_sum(float v, Smem& sm) {
+// Block sum in a fixed order with one __syncthreads; `rb` alternates the two scratch rows so
+// back-to-back reductions need no second barrier.
+__device__ __forceinline__ float block_sum(float v, Smem& sm, uint32_t& rb) {
     v = warp_sum(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) sm.red[warp] = v;
+    if (lane == 0) sm.red[rb][warp] = v;
     __syncthreads();
     float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) s += sm.red[w];
-    __syncthreads();
+    for (int w = 0; w < kWarps; ++w) s += sm.red[rb][w];
+    rb ^= 1u;
     return s;
 }
 
-// RMSNorm of the vector in xf, in place (burn::nn::RmsNorm: (x / sqrt(mean(x^2) + 1e-8)) * alpha).
-__device__ void norm_in_place(Smem& sm, int K, const float* alpha) {
-    float ss = 0.0f;
-    for (int j = threadIdx.x; j < K; j += kThreads) ss = __fmaf_rn(sm.xf[j], sm.xf[j], ss);
-    ss = block_reduce_sum(ss, sm);
-    const float rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-8f));
-    for (int j = threadIdx.x; j < K; j += kThreads) sm.xf[j] = __fmul_rn(__fdiv_rn(sm.xf[j], rms), __ldg(alpha + j));
+// The GEMV input of a phase: K floats from `src` (global, read through L2) or, when src is NULL,
+// from xf; RMSNorm with `alpha` when NORM (burn::nn::RmsNorm: (x / sqrt(mean(x^2) + 1e-8)) *
+// alpha); then the dp4a limbs.  QN = quads per thread; a thread's x and alpha loads are all in
+// flight together.
+template <int QN, bool NORM>
+__device__ __noinline__ void prep_vector_t(Smem& sm, const float* src, int K, const float* alpha, uint32_t& rb) {
+    const int nq = K >> 2, NB = K >> 5;
+    float4 v[QN], a[NORM ? QN : 1];
+#pragma unroll
+    for (int i = 0; i < QN; ++i) {
+        const int q = threadIdx.x + i * kThreads;
+        if (q < nq) {
+            v[i] = src ? __ldcg(reinterpret_cast<const float4*>(src) + q) : reinterpret_cast<const float4*>(sm.xf)[q];
+            if (NORM) a[i] = __ldg(reinterpret_cast<const float4*>(alpha) + q);
+        }
+    }
+    if (NORM) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < QN; ++i) {
+            const int q = threadIdx.x + i * kThreads;
+            if (q < nq) {
+                ss = __fmaf_rn(v[i].x, v[i].x, ss);
+                ss = __fmaf_rn(v[i].y, v[i].y, ss);
+                ss = __fmaf_rn(v[i].z, v[i].z, ss);
+                ss = __fmaf_rn(v[i].w, v[i].w, ss);
+            }
+        }
+        ss = block_sum(ss, sm, rb);
+        const float rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-8f));
+#pragma unroll
+        for (int i = 0; i < QN; ++i) {
+            v[i].x = __fmul_rn(__fdiv_rn(v[i].x, rms), a[NORM ? i : 0].x);
+            v[i].y = __fmul_rn(__fdiv_rn(v[i].y, rms), a[NORM ? i : 0].y);
+            v[i].z = __fmul_rn(__fdiv_rn(v[i].z, rms), a[NORM ? i : 0].z);
+            v[i].w = __fmul_rn(__fdiv_rn(v[i].w, rms), a[NORM ? i : 0].w);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < QN; ++i) {
+        const int q = threadIdx.x + i * kThreads;
+        if (q < nq) quad_limbs(sm, q, NB, v[i]);  // nq is a multiple of 32: whole warps
+    }
+    __syncthreads();
 }
 
-// xf = src (read through L2), optionally normalised, then its limbs.
-__device__ void load_vector(Smem& sm, const float* src, int K, const float* alpha) {
-    for (int q = threadIdx.x; q < (K >> 2); q += kThreads)
-        reinterpret_cast<float4*>(sm.xf)[q] = __ldcg(reinterpret_cast<const float4*>(src) + q);
-    __syncthreads();
+__device__ __forceinline__ void prep_vector(Smem& sm, const float* src, int K, const float* alpha, uint32_t& rb) {
+    const int qn = (K / 4 + kThreads - 1) / kThreads;
     if (alpha) {
-        norm_in_place(sm, K, alpha);
-        __syncthreads();
+        if (qn <= 1) prep_vector_t<1, true>(sm, src, K, alpha, rb);
+        else prep_vector_t<2, true>(sm, src, K, alpha, rb);  // D <= 4096
+    } else {
+        if (qn <= 1) prep_vector_t<1, false>(sm, src, K, alpha, rb);
+        else if (qn <= 2) prep_vector_t<2, false>(sm, src, K, alpha, rb);
+        else prep_vector_t<kQMax, false>(sm, src, K, alpha, rb);
     }
-    build_limbs(sm, K);
-    __syncthreads();
 }
 
 // ------------------------------------------------------------------------------ GEMV
@@ -459,7 +498,7 @@ struct HeadBest {
 // One GEMV phase over the rows staged in wbuf.  Units are row pairs (2u, 2u+1) or, for
 // linear_in, (gate row u, value row u + F); a warp takes one unit, its lanes split the blocks.
 template <int EPI>
-__device__ void gemv_phase(const MegaArgs& P, Smem& sm, const Rows& r, int layer, const StreamState& st,
+__device__ __noinline__ void gemv_phase(const MegaArgs& P, Smem& sm, const Rows& r, int layer, const StreamState& st,
                            HeadBest* best, int frame) {
     const Ctx& c = P.c;
     if (r.nr == 0 || r.n[0] <= 0) return;
@@ -504,9 +543,16 @@ __device__ void gemv_phase(const MegaArgs& P, Smem& sm, const Rows& r, int layer
         }
         float va = warp_sum(acc_a), vb = warp_sum(acc_b);
         if (lane != 0) continue;
-        if (EPI == EPI_RESID) {
-            c.x[ra] = __fadd_rn(va, __ldcg(c.x + ra));
-            if (rb >= 0) c.x[rb] = __fadd_rn(vb, __ldcg(c.x + rb));
+        if (EPI == EPI_RESID) {  // rows of this CTA: the residual lives in xown
+            const int o = ra - r.r0[0];
+            const float xa_ = __fadd_rn(va, sm.xown[o]);
+            sm.xown[o] = xa_;
+            c.x[ra] = xa_;
+            if (rb >= 0) {
+                const float xb_ = __fadd_rn(vb, sm.xown[o + 1]);
+                sm.xown[o + 1] = xb_;
+                c.x[rb] = xb_;
+            }
         } else if (EPI == EPI_GATE) {
             const float sg = __fmul_rn(va, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-va))));
             c.hid[ra] = __fmul_rn(sg, vb);
@@ -531,7 +577,7 @@ __device__ void gemv_phase(const MegaArgs& P, Smem& sm, const Rows& r, int layer
             const int within = ra - part * D;
             const int h = within / HD, d = within - h * HD;
             if (part < 2) {
-                const float2 cs = c.rope[(int64_t)st.offset * (HD >> 1) + (d >> 1)];
+                const float2 cs = sm.rope[d >> 1];
                 const float re = __fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y));
                 const float im = __fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x));
                 va = re;
@@ -577,7 +623,7 @@ __device__ __forceinline__ void load_kv(const KT* kp, const KT* vp, int lane, fl
 // Split-KV attention of head h = cta / nsplit over keys [s*chunk, min(len, (s+1)*chunk)).  The
 // CTA finishing last for a head combines the splits in split order.
 template <typename KT>
-__device__ void attention_phase(const MegaArgs& P, Smem& sm, int layer, const StreamState& st, int cta) {
+__device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& sm, int layer, const StreamState& st, int cta) {
     const Ctx& c = P.c;
     const int NS = P.nsplit;
     const int h = cta / NS, s = cta % NS;
@@ -700,26 +746,6 @@ __device__ __forceinline__ float emb_val(const Ctx& c, const uint8_t* table, uin
     }
 }
 
-// xa[j] for this CTA's slice of j: sum of the audio rows of `frame` in codebook order.
-__device__ void audio_sum_slice(const MegaArgs& P, int frame, int cta, int ncta) {
-    const Ctx& c = P.c;
-    const uint32_t* audio = c.desc->audio + (int64_t)frame * c.NC;
-    const int j0 = (int)split_lo(c.D, cta, ncta), j1 = (int)split_lo(c.D, cta + 1, ncta);
-    const int64_t table = (int64_t)c.AV * c.emb_row_bytes;
-    for (int j = j0 + (int)threadIdx.x; j < j1; j += kThreads) {
-        float acc = 0.0f;
-        for (int cb = 0; cb < c.NC; ++cb) {
-            uint32_t t = __ldcg(audio + cb);
-            if (t >= (uint32_t)c.AV) {
-                raise_error(c.desc, -1);
-                t = 0;
-            }
-            acc = __fadd_rn(acc, emb_val(c, c.emb_audio + cb * table, t, j));
-        }
-        P.xa[j] = acc;
-    }
-}
-
 // ------------------------------------------------------------------------------ kernel
 
 struct Look {
@@ -749,9 +775,12 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
     const Ctx& c = P.c;
     const int cta = blockIdx.x, ncta = gridDim.x;
     const int per_frame = 5 * c.L + 1;
-    uint32_t epoch = 0, parity = 0;
+    uint32_t epoch = 0, parity = 0, rb = 0;
     Tracer tr;
     Look lk{0, per_frame * P.steps};
+    // rows of x this CTA owns: the out_proj / linear_out row range
+    const int own0 = (int)(2 * split_lo(c.D / 2, cta, ncta));
+    const int own1 = (int)(2 * split_lo(c.D / 2, cta + 1, ncta));
 
     for (int i = threadIdx.x; i < c.L; i += kThreads) sm.layers[i] = c.layers[i];
     if (threadIdx.x == 0) {
@@ -765,8 +794,6 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
     StepDesc* desc = c.desc;
     if (threadIdx.x == 0) stage_phase(sm, c, 0, cta, ncta);
     if (threadIdx.x < 32) look_ahead(sm, P, lk, 0, per_frame, cta, ncta, min(st.len + 1, c.ML));
-    audio_sum_slice(P, 0, cta, ncta);
-    if (!grid_sync(P, epoch, sm, tr)) goto drain;
 
     for (int f = 0; f < P.steps; ++f) {
         tr.on = P.trace != nullptr && cta == 0 && f == P.trace_frame;
@@ -778,26 +805,24 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 raise_error(desc, -1);
                 text = 0;
             }
-            // x = audio sum + text row (model.rs:640-646); every CTA builds all of it and stores its slice
-            for (int j = threadIdx.x; j < c.D; j += kThreads)
-                sm.xf[j] = __fadd_rn(__ldcg(P.xa + j), emb_val(c, c.emb_text, text, j));
-            __syncthreads();
-            {
-                const int j0 = (int)split_lo(c.D, cta, ncta), j1 = (int)split_lo(c.D, cta + 1, ncta);
-                for (int j = j0 + (int)threadIdx.x; j < j1; j += kThreads) c.x[j] = sm.xf[j];
+            // x = audio sum + text row (model.rs:640-646): built whole by every CTA; the CTA keeps
+            // its own rows in xown and publishes them
+            const float* xa = P.xa + (int64_t)f * c.D;
+            for (int j = threadIdx.x; j < c.D; j += kThreads) {
+                const float v = __fadd_rn(__ldcg(xa + j), emb_val(c, c.emb_text, text, j));
+                sm.xf[j] = v;
+                if (j >= own0 && j < own1) {
+                    sm.xown[j - own0] = v;
+                    c.x[j] = v;
+                }
             }
+            if (threadIdx.x < (c.HD >> 1)) sm.rope[threadIdx.x] = c.rope[(int64_t)st.offset * (c.HD >> 1) + threadIdx.x];
+            __syncthreads();
             for (int l = 0; l < c.L; ++l) {
                 const LayerDev& Lw = sm.layers[l];
                 const int p0 = 5 * l, gp0 = f * per_frame + p0;
                 // ---- QKV (its weights were staged before the previous barrier)
-                if (l == 0) {
-                    norm_in_place(sm, c.D, Lw.norm1);
-                    __syncthreads();
-                    build_limbs(sm, c.D);
-                    __syncthreads();
-                } else {
-                    load_vector(sm, c.x, c.D, Lw.norm1);
-                }
+                prep_vector(sm, l == 0 ? nullptr : c.x, c.D, Lw.norm1, rb);
                 tr.mark(P, 10);
                 if (!wait_stage(sm, P, parity)) goto drain;
                 tr.mark(P, 11);
@@ -806,7 +831,9 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 tr.mark(P, 12);
                 // out_proj rows (attention does not use the staging buffer)
                 if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_OUT, cta, ncta);
+                tr.mark(P, 70);
                 if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_OUT, per_frame, cta, ncta, len_now);
+                tr.mark(P, 71);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- attention
                 if (c.kv_f32) attention_phase<float>(P, sm, l, st, cta);
@@ -815,7 +842,7 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 tr.mark(P, 22);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- out_proj + residual
-                load_vector(sm, c.attn, c.D, nullptr);
+                prep_vector(sm, c.attn, c.D, nullptr, rb);
                 tr.mark(P, 30);
                 if (!wait_stage(sm, P, parity)) goto drain;
                 tr.mark(P, 31);
@@ -823,10 +850,12 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 __syncthreads();
                 tr.mark(P, 32);
                 if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_IN, cta, ncta);
+                tr.mark(P, 70);
                 if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_IN, per_frame, cta, ncta, len_now);
+                tr.mark(P, 71);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- linear_in + silu gate
-                load_vector(sm, c.x, c.D, Lw.norm2);
+                prep_vector(sm, c.x, c.D, Lw.norm2, rb);
                 tr.mark(P, 40);
                 if (!wait_stage(sm, P, parity)) goto drain;
                 tr.mark(P, 41);
@@ -834,10 +863,12 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 __syncthreads();
                 tr.mark(P, 42);
                 if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_DOWN, cta, ncta);
+                tr.mark(P, 70);
                 if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_DOWN, per_frame, cta, ncta, len_now);
+                tr.mark(P, 71);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- linear_out + residual
-                load_vector(sm, c.hid, c.F, nullptr);
+                prep_vector(sm, c.hid, c.F, nullptr, rb);
                 tr.mark(P, 50);
                 if (!wait_stage(sm, P, parity)) goto drain;
                 tr.mark(P, 51);
@@ -847,12 +878,14 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 {  // next: QKV of layer l+1, or the head
                     const int pn = l + 1 < c.L ? p0 + 5 : 5 * c.L;
                     if (threadIdx.x == 0) stage_phase(sm, c, pn, cta, ncta);
+                    tr.mark(P, 70);
                     if (threadIdx.x < 32) look_ahead(sm, P, lk, f * per_frame + pn, per_frame, cta, ncta, len_now);
+                    tr.mark(P, 71);
                 }
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
             }
-            // ---- head + argmax partials; audio sum of the next frame
-            load_vector(sm, c.x, c.D, c.out_norm);
+            // ---- head + argmax partials
+            prep_vector(sm, c.x, c.D, c.out_norm, rb);
             tr.mark(P, 60);
             if (!wait_stage(sm, P, parity)) goto drain;
             tr.mark(P, 61);
@@ -880,8 +913,6 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 if (f + 1 < P.steps && threadIdx.x < 32)
                     look_ahead(sm, P, lk, (f + 1) * per_frame, per_frame, cta, ncta, min(st.len + 2, c.ML));
             }
-            if (f + 1 < P.steps) audio_sum_slice(P, f + 1, cta, ncta);
-            __syncthreads();
             tr.mark(P, 62);
             if (!grid_sync(P, epoch, sm, tr)) goto drain;
         }
@@ -932,6 +963,29 @@ drain:
         }
     }
     __syncthreads();
+}
+
+// Audio-embedding sums of every frame of the call: xa[f][j] = sum over codebooks (in order) of
+// the audio rows of frame f (model.rs:640-644), computed before the persistent kernel starts.
+__global__ void __launch_bounds__(256) audio_sum_kernel(Ctx c, float* __restrict__ xa) {
+    const int f = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    __shared__ uint32_t toks[kMaxCodebooks];
+    const uint32_t* audio = c.desc->audio + (int64_t)f * c.NC;
+    if (threadIdx.x < c.NC) {
+        uint32_t t = audio[threadIdx.x];
+        if (t >= (uint32_t)c.AV) {
+            raise_error(c.desc, -1);
+            t = 0;
+        }
+        toks[threadIdx.x] = t;
+    }
+    __syncthreads();
+    if (j >= c.D) return;
+    const int64_t table = (int64_t)c.AV * c.emb_row_bytes;
+    float acc = 0.0f;
+    for (int cb = 0; cb < c.NC; ++cb) acc = __fadd_rn(acc, emb_val(c, c.emb_audio + cb * table, toks[cb], j));
+    xa[(int64_t)f * c.D + j] = acc;
 }
 
 // Grid-barrier latency probe: `iters` back-to-back barriers of the persistent kernel.
@@ -986,14 +1040,16 @@ cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out) {
 }
 
 bool mega_supported(int L, int D, int F, int HD, int V, int num_sms) {
-    // head tickets live in the 64-word barrier block (2 + H <= 64); the layer table holds kMaxL
-    return HD == 128 && D % 256 == 0 && D <= kMaxK && F % 128 == 0 && F <= kMaxK && L > 0 && L <= kMaxL &&
+    // head tickets live in the 64-word barrier block (2 + H <= 64); the layer table holds kMaxL;
+    // a CTA keeps its x rows (2 * ceil(D/2 / num_sms)) in xown
+    return HD == 128 && D % 256 == 0 && D <= 4096 && F % 128 == 0 && F <= kMaxK && L > 0 && L <= kMaxL &&
+           2 * ((D / 2 + num_sms - 1) / num_sms) <= kMaxOwnRows &&
            D / HD <= 60 && max_stage_bytes(D, F, V, num_sms) <= (size_t)kWBuf &&
            std::getenv("STT_DISABLE_MEGA") == nullptr;
 }
 
 size_t mega_scratch_bytes(int num_sms, int D, int F, int V, int H, int HD) {
-    return 256 + (size_t)D * 4 + (size_t)num_sms * 8 + 64 * 4;
+    return 256 + (size_t)D * 4 + (size_t)num_sms * 8 + 64 * 4;  // bar | (unused) | amax_v | amax_i
 }
 
 cudaError_t configure_mega() {
@@ -1013,7 +1069,7 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
     P.steps = steps;
     P.nsplit = sms / c.H;  // the stream set sizes its partials buffer for num_sms rows
     P.bar = reinterpret_cast<uint32_t*>(s);
-    P.xa = reinterpret_cast<float*>(s + 256);
+    P.xa = ms.xa_all;
     P.amax_v = reinterpret_cast<float*>(s + 256 + (size_t)c.D * 4);
     P.amax_i = reinterpret_cast<int32_t*>(s + 256 + (size_t)c.D * 4 + (size_t)sms * 4);
     P.pf_budget = 128u * 1024u;
@@ -1030,6 +1086,9 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
     }
     if (P.nsplit < 1) return cudaErrorInvalidConfiguration;
     e = cudaMemsetAsync(P.bar, 0, 256, st);
+    if (e != cudaSuccess) return e;
+    audio_sum_kernel<<<dim3((c.D + 255) / 256, steps), 256, 0, st>>>(c, ms.xa_all);
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     void* args[] = {(void*)&P};
     return cudaLaunchCooperativeKernel((const void*)mega_kernel, dim3(sms), dim3(kThreads), args, sizeof(Smem), st);

@@ -8,6 +8,7 @@ namespace stt {
 struct MegaState {
     void* scratch = nullptr;  // device scratch owned by the stream set
     size_t scratch_bytes = 0;
+    float* xa_all = nullptr;              // [steps][D] audio sums of the call (grown by the caller)
     unsigned long long* trace = nullptr;  // device buffer for phase timestamps (diagnostics)
     int trace_frame = -1;
     int trace_cap = 0;
