@@ -49,10 +49,11 @@ def peaks():
 
 
 TRACE_NAMES = {1: "frame_start", 2: "barrier_arrive", 3: "barrier_wait", 10: "qkv_prologue", 11: "qkv_stage_wait",
-               12: "qkv_gemv", 22: "attention", 30: "out_proj_prologue", 31: "out_proj_stage_wait",
+               12: "qkv_gemv", 21: "attention_stage_wait", 22: "attention", 30: "out_proj_prologue",
                32: "out_proj_gemv", 40: "linear_in_prologue", 41: "linear_in_stage_wait", 42: "linear_in_gemv",
                50: "linear_out_prologue", 51: "linear_out_stage_wait", 52: "linear_out_gemv",
-               60: "head_prologue", 61: "head_stage_wait", 62: "head_gemv"}
+               60: "head_prologue", 61: "head_stage_wait", 62: "head_gemv", 70: "stage_issue",
+               71: "l2_prefetch_issue"}
 
 
 def trace_breakdown(raw):

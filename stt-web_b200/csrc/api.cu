@@ -662,7 +662,7 @@ int run_steps(stt_streams* s, const int32_t* ids, int n, int steps, const uint32
     init.desc = StepDesc{d_audio, d_text, d_tokens, d_logits, 0, mode, 0, 0};
     init.n = n;
     std::memcpy(init.ids, ids, sizeof(int32_t) * n);
-    const bool use_mega = n == 1 && mega_supported(m->L, m->D, m->F, m->HD, m->V, m->num_sms);
+    const bool use_mega = n == 1 && mega_supported(m->L, m->D, m->F, m->HD, m->V, m->num_sms, m->ML, s->kv_f32);
     cudaGraphExec_t exec = nullptr;
     if (!use_mega) TRY(graph_for(s, n, &exec));
     CUDA_TRY(launch_set_desc(s->d_desc, s->d_ids, init, st));

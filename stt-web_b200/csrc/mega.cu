@@ -244,14 +244,25 @@ __device__ Rows rows_of(const Smem& sm, const Ctx& c, int p, int cta, int ncta) 
     return r;
 }
 
-// Shared-memory layout of a staged phase: for each range, nibbles then scales (16-byte aligned).
+// Shared-memory layout of a staged phase: for each range, nibbles then scales (16-byte aligned),
+// then the phase's norm weight (D floats) when it has one.
 struct Staged {
     uint32_t nib[2];
     uint32_t sc[2];
+    uint32_t alpha;  // offset of the norm weight, or ~0u
     uint32_t bytes;
 };
 
-__device__ __forceinline__ Staged staged_layout(const Rows& r) {
+// The norm weight applied to a phase's input: norm1 (QKV), norm2 (linear_in), out_norm (head).
+__device__ __forceinline__ const float* phase_alpha(const Smem& sm, const Ctx& c, int p) {
+    const Kind k = kind_of(p, c.L);
+    if (k == K_HEAD) return c.out_norm;
+    if (k == K_QKV) return sm.layers[p / 5].norm1;
+    if (k == K_IN) return sm.layers[p / 5].norm2;
+    return nullptr;
+}
+
+__device__ __forceinline__ Staged staged_layout(const Rows& r, bool alpha, int D) {
     Staged s{};
     uint32_t off = 0;
     const uint32_t NB = r.nr ? (uint32_t)(r.W->k >> 5) : 0;
@@ -261,8 +272,34 @@ __device__ __forceinline__ Staged staged_layout(const Rows& r) {
         s.sc[i] = off;
         off += ((uint32_t)r.n[i] * NB * 2 + 15) & ~15u;
     }
+    s.alpha = ~0u;
+    if (alpha) {
+        s.alpha = off;
+        off += (uint32_t)D * 4;
+    }
     s.bytes = off;
     return s;
+}
+
+// Slots [j0, j1) of the attention split handled by this CTA (empty when h >= H).
+struct Split {
+    int h, s, j0, j1;
+};
+__device__ __forceinline__ Split split_of(const MegaArgs& P, int cta, int len) {
+    Split r;
+    r.h = cta / P.nsplit;
+    r.s = cta % P.nsplit;
+    const int chunk = (len + P.nsplit - 1) / P.nsplit;
+    r.j0 = r.s * chunk;
+    r.j1 = r.h < P.c.H ? min(len, r.j0 + chunk) : r.j0;
+    if (r.j1 < r.j0) r.j1 = r.j0;
+    return r;
+}
+
+// wbuf offset of the staged K/V slots: after the out_proj rows, which are staged with them.
+__device__ __forceinline__ uint32_t kv_offset(const Smem& sm, const Ctx& c, int layer, int cta, int ncta) {
+    const Staged so = staged_layout(rows_of(sm, c, 5 * layer + K_OUT, cta, ncta), false, c.D);
+    return (so.bytes + 127u) & ~127u;
 }
 
 // Bytes a phase reads from HBM for this CTA (weights, or the K/V slots of its attention split).
@@ -310,32 +347,69 @@ __device__ void prefetch_phase(const Smem& sm, const MegaArgs& P, int p, int cta
     }
 }
 
-// Thread 0: bulk-copies phase p's rows of this CTA into wbuf; completion on sm.mbar.
-__device__ void stage_phase(Smem& sm, const Ctx& c, int p, int cta, int ncta) {
-    const Rows r = rows_of(sm, c, p, cta, ncta);
-    const Staged s = staged_layout(r);
-    ++sm.staged;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+// Bulk copy of one row range's nibbles and scales into wbuf (thread 0).
+__device__ __forceinline__ void stage_rows(Smem& sm, const Q4Dev* W, int r0, int n, uint32_t nib_off, uint32_t sc_off) {
+    if (n <= 0) return;
+    const int64_t NB = W->k >> 5;
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(W->nib + (int64_t)r0 * NB);
+    const uint32_t nbytes = (uint32_t)(n * NB * 16);
+    for (uint32_t o = 0; o < nbytes; o += 32768u)
+        bulk_g2s(sm.wbuf + nib_off + o, src + o, min(32768u, nbytes - o), &sm.mbar);
+    const uint32_t sbytes = (uint32_t)(n * NB * 2);
+    const uint32_t sfull = sbytes & ~15u;
+    if (sfull) bulk_g2s(sm.wbuf + sc_off, W->scale + (int64_t)r0 * NB, sfull, &sm.mbar);
+    if (sbytes != sfull) {
+        // scale bytes not a multiple of 16: the tail is copied by this thread; the consumers
+        // read it after the barrier that publishes the bulk copies
+        const uint16_t* tail = W->scale + (int64_t)r0 * NB + sfull / 2;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(sm.wbuf + sc_off + sfull);
+        for (uint32_t t = 0; t < (sbytes - sfull) / 2; ++t) dst[t] = tail[t];
+    }
+}
+
+__device__ __forceinline__ uint32_t rows_tx(const Rows& r) {
     uint32_t tx = 0;
     for (int i = 0; i < r.nr; ++i)
-        if (r.n[i] > 0) tx += (uint32_t)r.n[i] * (uint32_t)(r.W->k >> 5) * 16u + (((uint32_t)r.n[i] * (uint32_t)(r.W->k >> 5) * 2u) & ~15u);
-    mbar_expect_tx(&sm.mbar, tx);
-    for (int i = 0; i < r.nr; ++i) {
-        if (r.n[i] <= 0) continue;
-        const int64_t NB = r.W->k >> 5;
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(r.W->nib + (int64_t)r.r0[i] * NB);
-        const uint32_t nbytes = (uint32_t)(r.n[i] * NB * 16);
-        for (uint32_t o = 0; o < nbytes; o += 32768u)
-            bulk_g2s(sm.wbuf + s.nib[i] + o, src + o, min(32768u, nbytes - o), &sm.mbar);
-        const uint32_t sbytes = (uint32_t)(r.n[i] * NB * 2);
-        const uint32_t sfull = sbytes & ~15u;
-        if (sfull) bulk_g2s(sm.wbuf + s.sc[i], r.W->scale + (int64_t)r.r0[i] * NB, sfull, &sm.mbar);
-        if (sbytes != sfull) {
-            // scale bytes not a multiple of 16 (rows * K/32 * 2): the tail is copied by this thread;
-            // the consumers read it after the same barrier that publishes the bulk copies
-            const uint16_t* tail = r.W->scale + (int64_t)r.r0[i] * NB + sfull / 2;
-            uint16_t* dst = reinterpret_cast<uint16_t*>(sm.wbuf + s.sc[i] + sfull);
-            for (uint32_t t = 0; t < (sbytes - sfull) / 2; ++t) dst[t] = tail[t];
+        if (r.n[i] > 0) {
+            const uint32_t NB = (uint32_t)(r.W->k >> 5);
+            tx += (uint32_t)r.n[i] * NB * 16u + (((uint32_t)r.n[i] * NB * 2u) & ~15u);
+        }
+    return tx;
+}
+
+// Thread 0: bulk-copies phase p's rows of this CTA (and its norm weight) into wbuf; completion on
+// sm.mbar.  No proxy fence is needed before overwriting wbuf: it was only read by the generic
+// proxy, and every reader passed the __syncthreads that precedes this call.
+__device__ void stage_phase(Smem& sm, const Ctx& c, int p, int cta, int ncta) {
+    const Rows r = rows_of(sm, c, p, cta, ncta);
+    const float* alpha = phase_alpha(sm, c, p);
+    const Staged s = staged_layout(r, alpha != nullptr, c.D);
+    ++sm.staged;
+    mbar_expect_tx(&sm.mbar, rows_tx(r) + (alpha ? (uint32_t)c.D * 4u : 0u));
+    for (int i = 0; i < r.nr; ++i) stage_rows(sm, r.W, r.r0[i], r.n[i], s.nib[i], s.sc[i]);
+    if (alpha) bulk_g2s(sm.wbuf + s.alpha, alpha, (uint32_t)c.D * 4u, &sm.mbar);
+}
+
+// Thread 0, after the QKV GEMV of layer l: stages the out_proj rows and this CTA's K/V slots of
+// layer l (as of the previous frames: the slot written this frame is read from qkv instead).
+__device__ void stage_out_kv(Smem& sm, const MegaArgs& P, int l, int cta, int ncta, int len) {
+    const Ctx& c = P.c;
+    const Rows r = rows_of(sm, c, 5 * l + K_OUT, cta, ncta);
+    const Staged s = staged_layout(r, false, c.D);
+    const Split sp = split_of(P, cta, len);
+    const int es = c.kv_f32 ? 4 : 2;
+    const uint32_t kvb = (uint32_t)(sp.j1 - sp.j0) * c.HD * es;
+    const uint32_t koff = kv_offset(sm, c, l, cta, ncta);
+    ++sm.staged;
+    mbar_expect_tx(&sm.mbar, rows_tx(r) + 2u * kvb);
+    stage_rows(sm, r.W, r.r0[0], r.n[0], s.nib[0], s.sc[0]);
+    if (kvb) {
+        const uint8_t* kb = static_cast<const uint8_t*>(c.kv) +
+                            ((int64_t)c.ids[0] * c.kv_stream_stride + (int64_t)l * c.kv_layer_stride +
+                             (int64_t)sp.h * c.ML * c.HD + (int64_t)sp.j0 * c.HD) * es;
+        for (uint32_t o = 0; o < kvb; o += 32768u) {
+            bulk_g2s(sm.wbuf + koff + o, kb + o, min(32768u, kvb - o), &sm.mbar);
+            bulk_g2s(sm.wbuf + koff + kvb + o, kb + c.kv_half_stride * es + o, min(32768u, kvb - o), &sm.mbar);
         }
     }
 }
@@ -421,7 +495,7 @@ __device__ __noinline__ void prep_vector_t(Smem& sm, const float* src, int K, co
         const int q = threadIdx.x + i * kThreads;
         if (q < nq) {
             v[i] = src ? __ldcg(reinterpret_cast<const float4*>(src) + q) : reinterpret_cast<const float4*>(sm.xf)[q];
-            if (NORM) a[i] = __ldg(reinterpret_cast<const float4*>(alpha) + q);
+            if (NORM) a[i] = reinterpret_cast<const float4*>(alpha)[q];  // staged in shared memory
         }
     }
     if (NORM) {
@@ -502,7 +576,7 @@ __device__ __noinline__ void gemv_phase(const MegaArgs& P, Smem& sm, const Rows&
                            HeadBest* best, int frame) {
     const Ctx& c = P.c;
     if (r.nr == 0 || r.n[0] <= 0) return;
-    const Staged s = staged_layout(r);
+    const Staged s = staged_layout(r, false, c.D);
     const int NB = r.W->k >> 5;
     const int units = EPI == EPI_GATE ? r.n[0] : (r.n[0] + 1) / 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -620,52 +694,69 @@ __device__ __forceinline__ void load_kv(const KT* kp, const KT* vp, int lane, fl
     }
 }
 
-// Split-KV attention of head h = cta / nsplit over keys [s*chunk, min(len, (s+1)*chunk)).  The
-// CTA finishing last for a head combines the splits in split order.
+// Split-KV attention of head h over ring slots [j0, j1) of this CTA, from the staged K/V (the
+// slot written this frame, write_pos, comes from qkv).  Writes the partial (max, sum exp,
+// sum exp * v); the out_proj prologue of every CTA combines the partials of all splits.
 template <typename KT>
-__device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& sm, int layer, const StreamState& st, int cta) {
+__device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& sm, int layer, const StreamState& st, int cta,
+                                             int ncta) {
     const Ctx& c = P.c;
-    const int NS = P.nsplit;
-    const int h = cta / NS, s = cta % NS;
-    if (h >= c.H) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int len = min(st.len + 1, c.ML);
-    const int chunk = (len + NS - 1) / NS;
-    const int j0 = s * chunk, j1 = min(len, j0 + chunk);
-    const int HD = c.HD;
+    const Split sp = split_of(P, cta, len);
+    if (sp.h >= c.H) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int HD = c.HD, h = sp.h;
     const float4 q = __ldcg(reinterpret_cast<const float4*>(c.qkv + h * HD) + lane);
-    const KT* kbase = reinterpret_cast<const KT*>(c.kv) + (int64_t)c.ids[0] * c.kv_stream_stride +
-                      (int64_t)layer * c.kv_layer_stride + (int64_t)h * c.ML * HD;
-    const KT* vbase = kbase + c.kv_half_stride;
+    const float4 kcur = __ldcg(reinterpret_cast<const float4*>(c.qkv + c.D + h * HD) + lane);
+    const float4 vcur = __ldcg(reinterpret_cast<const float4*>(c.qkv + 2 * c.D + h * HD) + lane);
+    const uint32_t koff = kv_offset(sm, c, layer, cta, ncta);
+    const uint32_t kvb = (uint32_t)(sp.j1 - sp.j0) * HD * sizeof(KT);
+    const KT* ks = reinterpret_cast<const KT*>(sm.wbuf + koff);
+    const KT* vs = reinterpret_cast<const KT*>(sm.wbuf + koff + kvb);
     float m = -FLT_MAX, l = 0.0f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int base = j0 + warp; base < j1; base += kWarps * kKeysPerBatch) {
-        float4 kk[kKeysPerBatch], vv[kKeysPerBatch];
-#pragma unroll
-        for (int t = 0; t < kKeysPerBatch; ++t) {
-            const int j = base + t * kWarps;
-            if (j < j1) load_kv<KT>(kbase + (int64_t)j * HD, vbase + (int64_t)j * HD, lane, kk[t], vv[t]);
+    for (int j = sp.j0 + warp; j < sp.j1; j += kWarps) {
+        float4 k, v;
+        if (j == st.write_pos) {
+            // this frame's K/V (the ring copy stores them rounded to the ring type)
+            if (sizeof(KT) == 4) {
+                k = kcur;
+                v = vcur;
+            } else {
+                k = make_float4(__bfloat162float(__float2bfloat16_rn(kcur.x)), __bfloat162float(__float2bfloat16_rn(kcur.y)),
+                                __bfloat162float(__float2bfloat16_rn(kcur.z)), __bfloat162float(__float2bfloat16_rn(kcur.w)));
+                v = make_float4(__bfloat162float(__float2bfloat16_rn(vcur.x)), __bfloat162float(__float2bfloat16_rn(vcur.y)),
+                                __bfloat162float(__float2bfloat16_rn(vcur.z)), __bfloat162float(__float2bfloat16_rn(vcur.w)));
+            }
+        } else {
+            const int r = j - sp.j0;
+            if (sizeof(KT) == 4) {
+                k = reinterpret_cast<const float4*>(ks + (int64_t)r * HD)[lane];
+                v = reinterpret_cast<const float4*>(vs + (int64_t)r * HD)[lane];
+            } else {
+                const uint2 kr = reinterpret_cast<const uint2*>(ks + (int64_t)r * HD)[lane];
+                const uint2 vr = reinterpret_cast<const uint2*>(vs + (int64_t)r * HD)[lane];
+                k = make_float4(__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xFFFF0000u),
+                                __uint_as_float(kr.y << 16), __uint_as_float(kr.y & 0xFFFF0000u));
+                v = make_float4(__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xFFFF0000u),
+                                __uint_as_float(vr.y << 16), __uint_as_float(vr.y & 0xFFFF0000u));
+            }
         }
-#pragma unroll
-        for (int t = 0; t < kKeysPerBatch; ++t) {
-            const int j = base + t * kWarps;
-            if (j >= j1) break;
-            float dot = __fmul_rn(q.x, kk[t].x);
-            dot = __fmaf_rn(q.y, kk[t].y, dot);
-            dot = __fmaf_rn(q.z, kk[t].z, dot);
-            dot = __fmaf_rn(q.w, kk[t].w, dot);
-            dot = warp_sum(dot);
-            const float score = __fmul_rn(dot, c.attn_scale);
-            const float mn = fmaxf(m, score);
-            const float corr = expf(m - mn);
-            const float p = expf(score - mn);
-            l = __fmaf_rn(l, corr, p);
-            o.x = __fmaf_rn(o.x, corr, __fmul_rn(p, vv[t].x));
-            o.y = __fmaf_rn(o.y, corr, __fmul_rn(p, vv[t].y));
-            o.z = __fmaf_rn(o.z, corr, __fmul_rn(p, vv[t].z));
-            o.w = __fmaf_rn(o.w, corr, __fmul_rn(p, vv[t].w));
-            m = mn;
-        }
+        float dot = __fmul_rn(q.x, k.x);
+        dot = __fmaf_rn(q.y, k.y, dot);
+        dot = __fmaf_rn(q.z, k.z, dot);
+        dot = __fmaf_rn(q.w, k.w, dot);
+        dot = warp_sum(dot);
+        const float score = __fmul_rn(dot, c.attn_scale);
+        const float mn = fmaxf(m, score);
+        const float corr = expf(m - mn);
+        const float p = expf(score - mn);
+        l = __fmaf_rn(l, corr, p);
+        o.x = __fmaf_rn(o.x, corr, __fmul_rn(p, v.x));
+        o.y = __fmaf_rn(o.y, corr, __fmul_rn(p, v.y));
+        o.z = __fmaf_rn(o.z, corr, __fmul_rn(p, v.z));
+        o.w = __fmaf_rn(o.w, corr, __fmul_rn(p, v.w));
+        m = mn;
     }
     // combine the warps in warp order through shared memory (xf as scratch)
     float* wm = sm.xf;
@@ -677,7 +768,6 @@ __device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& sm, int la
     }
     wo[warp * 32 + lane] = o;
     __syncthreads();
-    float* part = c.part + ((int64_t)h * NS + s) * (HD + 4);
     if (warp == 0) {
         float M = -FLT_MAX;
         for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wm[w]);
@@ -693,39 +783,72 @@ __device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& sm, int la
             O.z = __fmaf_rn(ow.z, f, O.z);
             O.w = __fmaf_rn(ow.w, f, O.w);
         }
+        float* part = c.part + ((int64_t)h * P.nsplit + sp.s) * (HD + 4);
         if (lane == 0) {
             part[0] = M;
             part[1] = L;
         }
         reinterpret_cast<float4*>(part + 4)[lane] = O;
     }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) sm.flag = atomicAdd(P.bar + 2 + h, 1u) == (uint32_t)NS - 1u;
-    __syncthreads();
-    if (!sm.flag) return;
-    __threadfence();
-    if (warp == 0) {
+}
+
+// The out_proj input: every CTA combines, for each head, the partials of all its splits (in
+// split order) into softmax(q.k^T * scale).v, then builds the limbs.
+template <int NSMAX>
+__device__ __noinline__ void prep_attn(Smem& sm, const MegaArgs& P) {
+    const Ctx& c = P.c;
+    const int NS = P.nsplit, HD = c.HD, NB = c.D >> 5;
+    const int nq = c.D >> 2, qh = HD >> 2;
+    for (int q = threadIdx.x; q < nq; q += kThreads) {
+        const int h = q / qh, d4 = q - h * qh;
         const float* pb = c.part + (int64_t)h * NS * (HD + 4);
-        float M = -FLT_MAX;
-        for (int t = 0; t < NS; ++t) M = fmaxf(M, __ldcg(pb + t * (HD + 4)));
-        float L = 0.0f;
         float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int t = 0; t < NS; ++t) {
-            const float lt = __ldcg(pb + t * (HD + 4) + 1);
-            if (lt == 0.0f) continue;
-            const float f = expf(__ldcg(pb + t * (HD + 4)) - M);
-            L = __fmaf_rn(lt, f, L);
-            const float4 ot = __ldcg(reinterpret_cast<const float4*>(pb + t * (HD + 4) + 4) + lane);
-            O.x = __fmaf_rn(ot.x, f, O.x);
-            O.y = __fmaf_rn(ot.y, f, O.y);
-            O.z = __fmaf_rn(ot.z, f, O.z);
-            O.w = __fmaf_rn(ot.w, f, O.w);
+        float L = 0.0f;
+        if (NS <= NSMAX) {
+            float2 ml[NSMAX];
+            float4 os[NSMAX];
+#pragma unroll
+            for (int t = 0; t < NSMAX; ++t)
+                if (t < NS) {
+                    ml[t] = __ldcg(reinterpret_cast<const float2*>(pb + t * (HD + 4)));
+                    os[t] = __ldcg(reinterpret_cast<const float4*>(pb + t * (HD + 4) + 4) + d4);
+                }
+            float M = -FLT_MAX;
+#pragma unroll
+            for (int t = 0; t < NSMAX; ++t)
+                if (t < NS && ml[t].y != 0.0f) M = fmaxf(M, ml[t].x);
+#pragma unroll
+            for (int t = 0; t < NSMAX; ++t)
+                if (t < NS && ml[t].y != 0.0f) {
+                    const float f = expf(ml[t].x - M);
+                    L = __fmaf_rn(ml[t].y, f, L);
+                    O.x = __fmaf_rn(os[t].x, f, O.x);
+                    O.y = __fmaf_rn(os[t].y, f, O.y);
+                    O.z = __fmaf_rn(os[t].z, f, O.z);
+                    O.w = __fmaf_rn(os[t].w, f, O.w);
+                }
+        } else {
+            float M = -FLT_MAX;
+            for (int t = 0; t < NS; ++t) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2*>(pb + t * (HD + 4)));
+                if (ml.y != 0.0f) M = fmaxf(M, ml.x);
+            }
+            for (int t = 0; t < NS; ++t) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2*>(pb + t * (HD + 4)));
+                if (ml.y == 0.0f) continue;
+                const float4 ot = __ldcg(reinterpret_cast<const float4*>(pb + t * (HD + 4) + 4) + d4);
+                const float f = expf(ml.x - M);
+                L = __fmaf_rn(ml.y, f, L);
+                O.x = __fmaf_rn(ot.x, f, O.x);
+                O.y = __fmaf_rn(ot.y, f, O.y);
+                O.z = __fmaf_rn(ot.z, f, O.z);
+                O.w = __fmaf_rn(ot.w, f, O.w);
+            }
         }
-        reinterpret_cast<float4*>(c.attn + h * HD)[lane] =
-            make_float4(__fdiv_rn(O.x, L), __fdiv_rn(O.y, L), __fdiv_rn(O.z, L), __fdiv_rn(O.w, L));
-        if (lane == 0) P.bar[2 + h] = 0u;
+        const float4 a = make_float4(__fdiv_rn(O.x, L), __fdiv_rn(O.y, L), __fdiv_rn(O.z, L), __fdiv_rn(O.w, L));
+        quad_limbs(sm, q, NB, a);  // c.D / 4 is a multiple of 32: whole warps
     }
+    __syncthreads();
 }
 
 // ------------------------------------------------------------------------------ embedding
@@ -819,33 +942,36 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
             if (threadIdx.x < (c.HD >> 1)) sm.rope[threadIdx.x] = c.rope[(int64_t)st.offset * (c.HD >> 1) + threadIdx.x];
             __syncthreads();
             for (int l = 0; l < c.L; ++l) {
-                const LayerDev& Lw = sm.layers[l];
                 const int p0 = 5 * l, gp0 = f * per_frame + p0;
-                // ---- QKV (its weights were staged before the previous barrier)
-                prep_vector(sm, l == 0 ? nullptr : c.x, c.D, Lw.norm1, rb);
-                tr.mark(P, 10);
+                // ---- QKV: weights and norm1 were staged before the previous barrier
                 if (!wait_stage(sm, P, parity)) goto drain;
                 tr.mark(P, 11);
-                gemv_phase<EPI_QKV>(P, sm, rows_of(sm, c, p0 + K_QKV, cta, ncta), l, st, nullptr, f);
+                {
+                    const Rows r = rows_of(sm, c, p0 + K_QKV, cta, ncta);
+                    const Staged sg = staged_layout(r, true, c.D);
+                    prep_vector(sm, l == 0 ? nullptr : c.x, c.D, reinterpret_cast<const float*>(sm.wbuf + sg.alpha), rb);
+                    tr.mark(P, 10);
+                    gemv_phase<EPI_QKV>(P, sm, r, l, st, nullptr, f);
+                }
                 __syncthreads();
                 tr.mark(P, 12);
-                // out_proj rows (attention does not use the staging buffer)
-                if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_OUT, cta, ncta);
+                if (threadIdx.x == 0) stage_out_kv(sm, P, l, cta, ncta, len_now);
                 tr.mark(P, 70);
                 if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_OUT, per_frame, cta, ncta, len_now);
                 tr.mark(P, 71);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
-                // ---- attention
-                if (c.kv_f32) attention_phase<float>(P, sm, l, st, cta);
-                else attention_phase<__nv_bfloat16>(P, sm, l, st, cta);
+                // ---- attention over the staged K/V slots (staged together with out_proj's rows)
+                if (!wait_stage(sm, P, parity)) goto drain;
+                tr.mark(P, 21);
+                if (c.kv_f32) attention_phase<float>(P, sm, l, st, cta, ncta);
+                else attention_phase<__nv_bfloat16>(P, sm, l, st, cta, ncta);
                 __syncthreads();
                 tr.mark(P, 22);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
-                // ---- out_proj + residual
-                prep_vector(sm, c.attn, c.D, nullptr, rb);
+                // ---- out_proj + residual (input: the combined attention partials)
+                if (P.nsplit <= 10) prep_attn<10>(sm, P);
+                else prep_attn<1>(sm, P);
                 tr.mark(P, 30);
-                if (!wait_stage(sm, P, parity)) goto drain;
-                tr.mark(P, 31);
                 gemv_phase<EPI_RESID>(P, sm, rows_of(sm, c, p0 + K_OUT, cta, ncta), l, st, nullptr, f);
                 __syncthreads();
                 tr.mark(P, 32);
@@ -855,11 +981,15 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 tr.mark(P, 71);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- linear_in + silu gate
-                prep_vector(sm, c.x, c.D, Lw.norm2, rb);
-                tr.mark(P, 40);
                 if (!wait_stage(sm, P, parity)) goto drain;
                 tr.mark(P, 41);
-                gemv_phase<EPI_GATE>(P, sm, rows_of(sm, c, p0 + K_IN, cta, ncta), l, st, nullptr, f);
+                {
+                    const Rows r = rows_of(sm, c, p0 + K_IN, cta, ncta);
+                    const Staged sg = staged_layout(r, true, c.D);
+                    prep_vector(sm, c.x, c.D, reinterpret_cast<const float*>(sm.wbuf + sg.alpha), rb);
+                    tr.mark(P, 40);
+                    gemv_phase<EPI_GATE>(P, sm, r, l, st, nullptr, f);
+                }
                 __syncthreads();
                 tr.mark(P, 42);
                 if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_DOWN, cta, ncta);
@@ -868,10 +998,10 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 tr.mark(P, 71);
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
                 // ---- linear_out + residual
-                prep_vector(sm, c.hid, c.F, nullptr, rb);
-                tr.mark(P, 50);
                 if (!wait_stage(sm, P, parity)) goto drain;
                 tr.mark(P, 51);
+                prep_vector(sm, c.hid, c.F, nullptr, rb);
+                tr.mark(P, 50);
                 gemv_phase<EPI_RESID>(P, sm, rows_of(sm, c, p0 + K_DOWN, cta, ncta), l, st, nullptr, f);
                 __syncthreads();
                 tr.mark(P, 52);
@@ -885,12 +1015,16 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
                 if (!grid_sync(P, epoch, sm, tr)) goto drain;
             }
             // ---- head + argmax partials
-            prep_vector(sm, c.x, c.D, c.out_norm, rb);
-            tr.mark(P, 60);
             if (!wait_stage(sm, P, parity)) goto drain;
             tr.mark(P, 61);
             HeadBest best{-FLT_MAX, 0x7FFFFFFF};
-            gemv_phase<EPI_LOGITS>(P, sm, rows_of(sm, c, 5 * c.L, cta, ncta), 0, st, &best, f);
+            {
+                const Rows r = rows_of(sm, c, 5 * c.L, cta, ncta);
+                const Staged sg = staged_layout(r, true, c.D);
+                prep_vector(sm, c.x, c.D, reinterpret_cast<const float*>(sm.wbuf + sg.alpha), rb);
+                tr.mark(P, 60);
+                gemv_phase<EPI_LOGITS>(P, sm, r, 0, st, &best, f);
+            }
             {
                 const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
                 if (lane == 0) {
@@ -1039,7 +1173,16 @@ cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out) {
     return e;
 }
 
-bool mega_supported(int L, int D, int F, int HD, int V, int num_sms) {
+bool mega_supported(int L, int D, int F, int HD, int V, int num_sms, int ML, int kv_f32) {
+    const int H = D / HD;
+    const int nsplit = num_sms / (H > 0 ? H : 1);
+    if (nsplit < 1) return false;
+    // out_proj rows (plus alignment) and the K/V slots of one split share the staging buffer
+    const size_t kv = (size_t)((ML + nsplit - 1) / nsplit) * HD * (kv_f32 ? 4 : 2) * 2;
+    const size_t out_rows = (size_t)2 * ((D / 2 + num_sms - 1) / num_sms);
+    const size_t out_bytes = out_rows * (D / 32) * 16 + ((out_rows * (D / 32) * 2 + 15) & ~(size_t)15);
+    if (((out_bytes + 127) & ~(size_t)127) + kv > (size_t)kWBuf) return false;
+    if (max_stage_bytes(D, F, V, num_sms) + (size_t)D * 4 > (size_t)kWBuf) return false;
     // head tickets live in the 64-word barrier block (2 + H <= 64); the layer table holds kMaxL;
     // a CTA keeps its x rows (2 * ceil(D/2 / num_sms)) in xown
     return HD == 128 && D % 256 == 0 && D <= 4096 && F % 128 == 0 && F <= kMaxK && L > 0 && L <= kMaxL &&

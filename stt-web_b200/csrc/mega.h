@@ -14,7 +14,7 @@ struct MegaState {
     int trace_cap = 0;
 };
 
-bool mega_supported(int L, int D, int F, int HD, int V, int num_sms);
+bool mega_supported(int L, int D, int F, int HD, int V, int num_sms, int ML, int kv_f32);
 size_t mega_scratch_bytes(int num_sms, int D, int F, int V, int H, int HD);
 cudaError_t configure_mega();
 cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out);

@@ -237,10 +237,10 @@ def test_persistent_kernel_barrier_and_trace(full_model):
     buf = (C.c_uint64 * 1024)()
     n = C.c_int()
     assert lib().stt_debug_get_trace(cache._h, buf, 1024, C.byref(n)) == 0
-    # (tag, time) pairs: frame start, 2 per barrier (5 per layer + 1 after the head), the marks
-    # inside the phases (3 per GEMV phase, 1 per attention phase, 3 for the head) and 2 after
-    # each weight staging issued before a barrier (4 per layer)
+    # (tag, time) pairs: frame start; per layer 5 barriers (2 marks each), the phase marks (3 for
+    # qkv, linear_in and linear_out, 2 for attention and out_proj) and 2 after each of the 4
+    # stagings; the head's 3 marks and its barrier
     pairs = n.value // 2
-    assert pairs == 1 + 2 * (5 * 16 + 1) + 16 * (4 * 3 + 1) + 3 + 16 * 4 * 2, pairs
+    assert pairs == 1 + 16 * (5 * 2 + 3 * 3 + 2 * 2 + 4 * 2) + 3 + 2, pairs
     t = np.array(buf[1:n.value:2], dtype=np.int64)
     assert np.all(np.diff(t) >= 0)
