@@ -57,13 +57,20 @@ TRACE_NAMES = {1: "frame_start", 2: "barrier_arrive", 3: "barrier_wait", 10: "qk
 
 
 def trace_breakdown(raw):
-    """(tag, ns) pairs of one traced frame -> microseconds spent reaching each kind of mark."""
+    """(tag, cycles) pairs of one traced frame, bracketed by (0, globaltimer ns) pairs ->
+    microseconds spent reaching each kind of mark."""
     pairs = [(raw[i], raw[i + 1]) for i in range(0, len(raw) - 1, 2)]
+    walls = [v for t, v in pairs if t == 0]
+    marks = [(t, v) for t, v in pairs if t != 0]
+    frame_ns = walls[-1] - walls[0] if len(walls) >= 2 else None
+    cycles = marks[-1][1] - marks[0][1]
+    ns_per_cycle = frame_ns / cycles if frame_ns and cycles else 1.0 / 1.965
     out = {}
-    for (t0, a), (t1, b) in zip(pairs, pairs[1:]):
+    for (t0, a), (t1, b) in zip(marks, marks[1:]):
         k = TRACE_NAMES.get(t1, str(t1))
-        out[k] = out.get(k, 0.0) + (b - a) / 1e3
-    return {"frame_us": (pairs[-1][1] - pairs[0][1]) / 1e3, "trace_us": {k: round(v, 2) for k, v in out.items()}}
+        out[k] = out.get(k, 0.0) + (b - a) * ns_per_cycle / 1e3
+    return {"frame_us": frame_ns / 1e3 if frame_ns else None, "sm_ghz": 1.0 / ns_per_cycle,
+            "trace_us": {k: round(v, 2) for k, v in out.items()}}
 
 
 class ClockSampler:
@@ -254,8 +261,10 @@ def main():
     # ---- diagnostics: grid-barrier latency and a per-phase breakdown of one late frame
     diag = {}
     ns = C.c_double()
-    if lib().stt_debug_barrier_ns(local, 2000, C.byref(ns)) == 0:
+    if lib().stt_debug_barrier_ns(local, 2000, 0, C.byref(ns)) == 0:
         diag["grid_barrier_ns"] = ns.value
+    if lib().stt_debug_barrier_ns(local, 2000, 1, C.byref(ns)) == 0:
+        diag["grid_barrier_flag_ns"] = ns.value
     lib().stt_debug_trace_frame(cache._h, FRAMES - 10)
     utterance_device()
     torch.cuda.synchronize()

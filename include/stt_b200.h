@@ -225,14 +225,16 @@ int stt_synth_audio_tokens(uint64_t seed, int32_t stream, int32_t first_frame, i
  * Diagnostics (no counterpart in the reference): timing probes of the persistent
  * single-stream step kernel, used by the benchmarks and profiles of this library.
  * ------------------------------------------------------------------------------------- */
-/* Records the device clock (%globaltimer, ns) at the start of frame `frame` and at the entry
- * and exit of every grid barrier of that frame, on later single-stream calls; -1 disables. */
+/* Records (tag, SM clock cycles) pairs at the phase boundaries of frame `frame` of CTA 0, with
+ * (0, %globaltimer ns) pairs at the frame's start and end, on later single-stream calls;
+ * -1 disables. */
 int stt_debug_trace_frame(stt_streams* streams, int frame);
 /* Copies the timestamps of the last traced frame (at most cap); *n receives the count. */
 int stt_debug_get_trace(stt_streams* streams, uint64_t* out, int cap, int* n);
-/* Mean time of one grid barrier of the persistent kernel over `iters` back-to-back barriers on
- * device `device`, in nanoseconds. */
-int stt_debug_barrier_ns(int device, int iters, double* ns_per_barrier);
+/* Mean time of one grid barrier over `iters` back-to-back barriers on device `device`, in
+ * nanoseconds: mode 0 is the persistent kernel's barrier (release add, acquire poll of the
+ * counter), mode 1 a variant in which the last arriver publishes a flag that the others poll. */
+int stt_debug_barrier_ns(int device, int iters, int mode, double* ns_per_barrier);
 
 /* Text of the last error on the calling thread ("" if none). */
 const char* stt_last_error(void);

@@ -1076,7 +1076,7 @@ extern "C" int stt_debug_get_trace(stt_streams* s, uint64_t* out, int cap, int* 
     return STT_OK;
 }
 
-extern "C" int stt_debug_barrier_ns(int device, int iters, double* ns) {
+extern "C" int stt_debug_barrier_ns(int device, int iters, int mode, double* ns) {
     clear_error();
     if (!ns || iters <= 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
     DeviceScope ds(device);
@@ -1084,7 +1084,7 @@ extern "C" int stt_debug_barrier_ns(int device, int iters, double* ns) {
     DevBuf b;
     TRY(b.ensure(256));
     float ms = 0.0f;
-    CUDA_TRY(mega_barrier_probe(b.p, iters, &ms));
+    CUDA_TRY(mega_barrier_probe(b.p, iters, mode, &ms));
     *ns = (double)ms * 1e6 / iters;
     return STT_OK;
 }

@@ -141,7 +141,8 @@ __device__ __forceinline__ unsigned long long globaltimer() {
     return t;
 }
 
-// Trace points of one frame of CTA 0: (tag, %globaltimer) pairs.  Tags: 1 frame start,
+// Trace points of one frame of CTA 0: (tag, SM clock cycles) pairs, bracketed by (0, %globaltimer)
+// pairs at the frame's start and end so the host can convert cycles to time.  Tags: 1 frame start,
 // 2 barrier entry, 3 barrier exit, 10*k + {0 prologue done, 1 staged copy landed, 2 compute done}
 // for phase kinds k = 1 qkv, 2 attention, 3 out_proj, 4 linear_in, 5 linear_out, 6 head.
 struct Tracer {
@@ -150,6 +151,14 @@ struct Tracer {
     __device__ void mark(const MegaArgs& P, unsigned long long tag) {
         if (on && threadIdx.x == 0 && slot + 1 < P.trace_cap) {
             P.trace[slot] = tag;
+            P.trace[slot + 1] = clock64();
+            slot += 2;
+        }
+    }
+    // (tag 0, %globaltimer) pair: lets the host convert the cycle counts to nanoseconds
+    __device__ void wall(const MegaArgs& P) {
+        if (on && threadIdx.x == 0 && slot + 1 < P.trace_cap) {
+            P.trace[slot] = 0;
             P.trace[slot + 1] = globaltimer();
             slot += 2;
         }
@@ -919,7 +928,9 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
     if (threadIdx.x < 32) look_ahead(sm, P, lk, 0, per_frame, cta, ncta, min(st.len + 1, c.ML));
 
     for (int f = 0; f < P.steps; ++f) {
+        if (tr.on) tr.wall(P);  // end of the traced frame
         tr.on = P.trace != nullptr && cta == 0 && f == P.trace_frame;
+        tr.wall(P);
         tr.mark(P, 1);
         {
             const int len_now = min(st.len + 1, c.ML);
@@ -1122,14 +1133,37 @@ __global__ void __launch_bounds__(256) audio_sum_kernel(Ctx c, float* __restrict
     xa[(int64_t)f * c.D + j] = acc;
 }
 
-// Grid-barrier latency probe: `iters` back-to-back barriers of the persistent kernel.
-__global__ void __launch_bounds__(kThreads, 1) barrier_probe_kernel(const __grid_constant__ MegaArgs P, int iters) {
+// Grid-barrier latency probe: `iters` back-to-back barriers of the persistent kernel (mode 0),
+// or of a variant where the last arriver (atom.add.acq_rel) publishes a generation flag on a
+// separate line that the others poll (mode 1).
+__global__ void __launch_bounds__(kThreads, 1) barrier_probe_kernel(const __grid_constant__ MegaArgs P, int iters,
+                                                                    int mode) {
     extern __shared__ uint4 smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
     uint32_t epoch = 0;
     Tracer tr;
-    for (int i = 0; i < iters; ++i)
-        if (!grid_sync(P, epoch, sm, tr)) return;
+    if (mode == 0) {
+        for (int i = 0; i < iters; ++i)
+            if (!grid_sync(P, epoch, sm, tr)) return;
+        return;
+    }
+    uint32_t* flag = P.bar + 32;  // 128 bytes away from the counter
+    for (int i = 0; i < iters; ++i) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const uint32_t gen = (uint32_t)i + 1u;
+            uint32_t old;
+            asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(P.bar) : "memory");
+            if (old == gen * gridDim.x - 1u) {
+                asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(gen) : "memory");
+            } else {
+                uint32_t spins = 0;
+                while ((int32_t)(ld_acquire(flag) - gen) < 0 && ++spins < kSpinLimit) {
+                }
+            }
+        }
+        __syncthreads();
+    }
 }
 
 // Largest staged phase of one CTA in bytes (must fit kWBuf).
@@ -1148,7 +1182,7 @@ size_t max_stage_bytes(int D, int F, int V, int ncta) {
 
 }  // namespace
 
-cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out) {
+cudaError_t mega_barrier_probe(void* scratch, int iters, int mode, float* ms_out) {
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1161,7 +1195,7 @@ cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out) {
     cudaEventCreate(&a);
     cudaEventCreate(&b);
     e = cudaMemset(P.bar, 0, 256);
-    void* args[] = {(void*)&P, (void*)&iters};
+    void* args[] = {(void*)&P, (void*)&iters, (void*)&mode};
     if (e == cudaSuccess) e = cudaEventRecord(a, 0);
     if (e == cudaSuccess)
         e = cudaLaunchCooperativeKernel((const void*)barrier_probe_kernel, dim3(sms), dim3(kThreads), args, sizeof(Smem), 0);

@@ -17,7 +17,7 @@ struct MegaState {
 bool mega_supported(int L, int D, int F, int HD, int V, int num_sms, int ML, int kv_f32);
 size_t mega_scratch_bytes(int num_sms, int D, int F, int V, int H, int HD);
 cudaError_t configure_mega();
-cudaError_t mega_barrier_probe(void* scratch, int iters, float* ms_out);
+cudaError_t mega_barrier_probe(void* scratch, int iters, int mode, float* ms_out);
 cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_layers, int steps, cudaStream_t st);
 
 }  // namespace stt

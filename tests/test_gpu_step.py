@@ -228,8 +228,9 @@ def test_persistent_kernel_barrier_and_trace(full_model):
     import ctypes as C
     from stt_b200._lib import lib
     ns = C.c_double()
-    assert lib().stt_debug_barrier_ns(0, 2000, C.byref(ns)) == 0
-    assert 50 < ns.value < 20000, ns.value
+    for mode in (0, 1):
+        assert lib().stt_debug_barrier_ns(0, 2000, mode, C.byref(ns)) == 0
+        assert 50 < ns.value < 20000, ns.value
     g, model = full_model
     cache = model.create_cache(1, "bf16")
     assert lib().stt_debug_trace_frame(cache._h, 1) == 0
@@ -240,7 +241,9 @@ def test_persistent_kernel_barrier_and_trace(full_model):
     # (tag, time) pairs: frame start; per layer 5 barriers (2 marks each), the phase marks (3 for
     # qkv, linear_in and linear_out, 2 for attention and out_proj) and 2 after each of the 4
     # stagings; the head's 3 marks and its barrier
-    pairs = n.value // 2
-    assert pairs == 1 + 16 * (5 * 2 + 3 * 3 + 2 * 2 + 4 * 2) + 3 + 2, pairs
-    t = np.array(buf[1:n.value:2], dtype=np.int64)
+    tags = list(buf[0:n.value:2])
+    marks = [i for i, t in enumerate(tags) if t != 0]
+    assert len(marks) == 1 + 16 * (5 * 2 + 3 * 3 + 2 * 2 + 4 * 2) + 3 + 2, len(marks)
+    assert tags[0] == 0 and tags[-1] == 0  # wall-clock pairs around the frame
+    t = np.array([buf[2 * i + 1] for i in marks], dtype=np.int64)
     assert np.all(np.diff(t) >= 0)
