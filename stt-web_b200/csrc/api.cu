@@ -1069,9 +1069,10 @@ extern "C" int stt_debug_get_trace(stt_streams* s, uint64_t* out, int cap, int* 
     std::vector<unsigned long long> t(s->mega.trace_cap);
     CUDA_TRY(cudaDeviceSynchronize());
     CUDA_TRY(cudaMemcpy(t.data(), s->mega.trace, sizeof(unsigned long long) * t.size(), cudaMemcpyDeviceToHost));
+    // (tag, value) pairs up to the first pair whose value (a clock reading) is still zero
     int k = 0;
-    while (k < (int)t.size() && t[k] != 0) ++k;
-    *n = std::min(k, cap);
+    while (k + 1 < (int)t.size() && t[k + 1] != 0) k += 2;
+    *n = std::min(k, cap & ~1);
     for (int i = 0; i < *n; ++i) out[i] = t[i];
     return STT_OK;
 }
