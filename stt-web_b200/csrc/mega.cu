@@ -71,6 +71,12 @@ struct Smem {
     int32_t flag;
 };
 
+// The kernel's dynamic shared memory.  Functions that are not inlined recover the Smem through
+// this file-scope array instead of a reference parameter, so the compiler keeps emitting
+// shared-memory (LDS/STS) accesses rather than generic ones.
+extern __shared__ __align__(128) uint4 mega_smem[];
+__device__ __forceinline__ Smem& smem_ref() { return *reinterpret_cast<Smem*>(mega_smem); }
+
 // ------------------------------------------------------------------------------ primitives
 
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
@@ -496,7 +502,8 @@ __device__ __forceinline__ float block_sum(float v, Smem& sm, uint32_t& rb) {
 // alpha); then the dp4a limbs.  QN = quads per thread; a thread's x and alpha loads are all in
 // flight together.
 template <int QN, bool NORM>
-__device__ __noinline__ void prep_vector_t(Smem& sm, const float* src, int K, const float* alpha, uint32_t& rb) {
+__device__ __noinline__ void prep_vector_t(Smem& /*sm_param*/, const float* src, int K, const float* alpha, uint32_t& rb) {
+    Smem& sm = smem_ref();
     const int nq = K >> 2, NB = K >> 5;
     float4 v[QN], a[NORM ? QN : 1];
 #pragma unroll
@@ -520,13 +527,15 @@ __device__ __noinline__ void prep_vector_t(Smem& sm, const float* src, int K, co
             }
         }
         ss = block_sum(ss, sm, rb);
-        const float rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-8f));
+        // x * (1 / rms) instead of x / rms: within 1.5 ulp, below the 24-bit fixed-point step of
+        // the limbs that follow
+        const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-8f)));
 #pragma unroll
         for (int i = 0; i < QN; ++i) {
-            v[i].x = __fmul_rn(__fdiv_rn(v[i].x, rms), a[NORM ? i : 0].x);
-            v[i].y = __fmul_rn(__fdiv_rn(v[i].y, rms), a[NORM ? i : 0].y);
-            v[i].z = __fmul_rn(__fdiv_rn(v[i].z, rms), a[NORM ? i : 0].z);
-            v[i].w = __fmul_rn(__fdiv_rn(v[i].w, rms), a[NORM ? i : 0].w);
+            v[i].x = __fmul_rn(__fmul_rn(v[i].x, inv), a[NORM ? i : 0].x);
+            v[i].y = __fmul_rn(__fmul_rn(v[i].y, inv), a[NORM ? i : 0].y);
+            v[i].z = __fmul_rn(__fmul_rn(v[i].z, inv), a[NORM ? i : 0].z);
+            v[i].w = __fmul_rn(__fmul_rn(v[i].w, inv), a[NORM ? i : 0].w);
         }
     }
 #pragma unroll
@@ -581,8 +590,9 @@ struct HeadBest {
 // One GEMV phase over the rows staged in wbuf.  Units are row pairs (2u, 2u+1) or, for
 // linear_in, (gate row u, value row u + F); a warp takes one unit, its lanes split the blocks.
 template <int EPI>
-__device__ __noinline__ void gemv_phase(const MegaArgs& P, Smem& sm, const Rows& r, int layer, const StreamState& st,
-                           HeadBest* best, int frame) {
+__device__ __noinline__ void gemv_phase(const MegaArgs& P, Smem& /*sm_param*/, const Rows& r, int layer,
+                                        const StreamState& st, HeadBest* best, int frame) {
+    Smem& sm = smem_ref();
     const Ctx& c = P.c;
     if (r.nr == 0 || r.n[0] <= 0) return;
     const Staged s = staged_layout(r, false, c.D);
@@ -707,8 +717,9 @@ __device__ __forceinline__ void load_kv(const KT* kp, const KT* vp, int lane, fl
 // slot written this frame, write_pos, comes from qkv).  Writes the partial (max, sum exp,
 // sum exp * v); the out_proj prologue of every CTA combines the partials of all splits.
 template <typename KT>
-__device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& sm, int layer, const StreamState& st, int cta,
-                                             int ncta) {
+__device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& /*sm_param*/, int layer, const StreamState& st,
+                                             int cta, int ncta) {
+    Smem& sm = smem_ref();
     const Ctx& c = P.c;
     const int len = min(st.len + 1, c.ML);
     const Split sp = split_of(P, cta, len);
@@ -804,7 +815,8 @@ __device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& sm, int la
 // The out_proj input: every CTA combines, for each head, the partials of all its splits (in
 // split order) into softmax(q.k^T * scale).v, then builds the limbs.
 template <int NSMAX>
-__device__ __noinline__ void prep_attn(Smem& sm, const MegaArgs& P) {
+__device__ __noinline__ void prep_attn(Smem& /*sm_param*/, const MegaArgs& P) {
+    Smem& sm = smem_ref();
     const Ctx& c = P.c;
     const int NS = P.nsplit, HD = c.HD, NB = c.D >> 5;
     const int nq = c.D >> 2, qh = HD >> 2;
@@ -902,8 +914,7 @@ __device__ void look_ahead(const Smem& sm, const MegaArgs& P, Look& lk, int stag
 }
 
 __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant__ MegaArgs P) {
-    extern __shared__ uint4 smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+    Smem& sm = smem_ref();
     const Ctx& c = P.c;
     const int cta = blockIdx.x, ncta = gridDim.x;
     const int per_frame = 5 * c.L + 1;
@@ -1138,8 +1149,7 @@ __global__ void __launch_bounds__(256) audio_sum_kernel(Ctx c, float* __restrict
 // separate line that the others poll (mode 1).
 __global__ void __launch_bounds__(kThreads, 1) barrier_probe_kernel(const __grid_constant__ MegaArgs P, int iters,
                                                                     int mode) {
-    extern __shared__ uint4 smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+    Smem& sm = smem_ref();
     uint32_t epoch = 0;
     Tracer tr;
     if (mode == 0) {
