@@ -1259,7 +1259,7 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
     P.xa = ms.xa_all;
     P.amax_v = reinterpret_cast<float*>(s + 256 + (size_t)c.D * 4);
     P.amax_i = reinterpret_cast<int32_t*>(s + 256 + (size_t)c.D * 4 + (size_t)sms * 4);
-    P.pf_budget = 128u * 1024u;
+    P.pf_budget = 0;  // off by default: issuing the prefetches stalls warp 0 longer than it saves
     if (const char* pb = std::getenv("STT_MEGA_PF_KB")) P.pf_budget = (uint32_t)std::atoi(pb) * 1024u;
     P.pf_lines = 1;
     if (const char* pm = std::getenv("STT_MEGA_PF_BULK")) P.pf_lines = std::atoi(pm) ? 0 : 1;
