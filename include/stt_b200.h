@@ -190,6 +190,15 @@ int stt_q4_matmul(const stt_q4_tensor* w, const float* input, int rows, float* o
  * d_out is f32 [rows, n].  Queued on cuda_stream, no synchronisation. */
 int stt_q4_matmul_device(const stt_q4_tensor* w, const void* d_input, int in_dtype, int rows,
                          float* d_out, void* cuda_stream);
+/* No counterpart in the reference.  Split-K form of stt_q4_matmul_device (same arguments plus
+ * `splits`, 1..64 and at most k/32) that requests no device memory: partial sums and per-tile
+ * counters live in a fixed 4 MiB + 16 KiB array of the library's device image, so
+ * splits * rows * n * 4 must be at most 4 MiB and n at most 65536, else STT_E_INVALID_ARG.
+ * The first call on a device looks up that array's address (make it before capturing a
+ * stream).  Calls on one device share the array and must not overlap in time.  Queued on
+ * cuda_stream, no synchronisation; d_input 16-byte aligned (f32) or 8-byte aligned (bf16). */
+int stt_q4_matmul_device_noalloc(const stt_q4_tensor* w, const void* d_input, int in_dtype, int rows,
+                                 int splits, float* d_out, void* cuda_stream);
 /* Dequantises the whole matrix to f32 on the device and copies it to out_host (n*k floats):
  * out[r*k + j] = (nibble - 8) * f16_to_f32(scale), bit-exact with gguf.rs:616-633. */
 int stt_q4_tensor_dequant(const stt_q4_tensor* w, float* out_host);

@@ -5,12 +5,14 @@
 #include <cstdarg>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
 #include "common.h"
 #include "gguf.h"
 #include "kernels.h"
+#include "noalloc.h"
 #include "mega.h"
 
 namespace stt {
@@ -1022,6 +1024,67 @@ extern "C" int stt_q4_matmul_device(const stt_q4_tensor* t, const void* d_in, in
     a.ldo = t->w.n;
     a.n_units = (t->w.n + 1) / 2;
     CUDA_TRY(launch_gemv(c, a, EPI_PLAIN, rows, 2 * t->num_sms, static_cast<cudaStream_t>(cuda_stream)));
+    return STT_OK;
+}
+
+// Split-K variant of stt_q4_matmul_device that requests no device memory: its partial sums and
+// per-tile counters live in a fixed array of the library's device image (4 MiB of partials,
+// 4096 tiles of 16 output rows).  For callers that cannot allocate during a call: a serving
+// process that sizes all of its device memory up front and must not grow afterwards, and a
+// latency-bound caller (one frame every 80 ms per stream) for which an allocation or a free,
+// which can synchronise the whole device, would stall every stream queued on it.  The first call
+// on a device looks up the array's address with that device current and keeps it; make that
+// first call before capturing a stream.  Calls on one device share the array: they must be
+// ordered (one stream, or explicit ordering between streams), or they race.
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+}  // namespace
+
+extern "C" int stt_q4_matmul_device_noalloc(const stt_q4_tensor* t, const void* d_in, int in_dtype, int rows,
+                                            int splits, float* d_out, void* cuda_stream) {
+    clear_error();
+    if (!t || !d_in || !d_out || rows < 0 || (in_dtype != 0 && in_dtype != 1))
+        return set_error(STT_E_INVALID_ARG, "bad arguments");
+    const int NB = t->w.k / 32;
+    if (splits < 1 || splits > kNoAllocMaxSplits || splits > NB)
+        return set_error(STT_E_INVALID_ARG, "splits %d out of range [1, %d]", splits, std::min(kNoAllocMaxSplits, NB));
+    const uintptr_t align = in_dtype == 0 ? 16 : 8;
+    if (reinterpret_cast<uintptr_t>(d_in) % align != 0 || reinterpret_cast<uintptr_t>(d_out) % 4 != 0)
+        return set_error(STT_E_INVALID_ARG, "input must be %d-byte aligned and output 4-byte aligned", (int)align);
+    const int tiles = (t->w.n + kNoAllocTileRows - 1) / kNoAllocTileRows;
+    if (tiles > kNoAllocTickets)
+        return set_error(STT_E_INVALID_ARG, "%d output rows need %d tiles of %d; the fixed scratch has %d tile counters",
+                         t->w.n, tiles, kNoAllocTileRows, kNoAllocTickets);
+    const size_t need = (size_t)splits * (size_t)rows * (size_t)t->w.n * sizeof(float);
+    if (need > kNoAllocPartialBytes)
+        return set_error(STT_E_INVALID_ARG,
+                         "%d splits x %d rows x %d outputs need %zu bytes of partial sums; the fixed scratch holds %zu "
+                         "(use fewer splits or rows per call)",
+                         splits, rows, t->w.n, need, kNoAllocPartialBytes);
+    if (t->device < 0 || t->device >= kNoAllocMaxDevices)
+        return set_error(STT_E_INVALID_ARG, "device %d out of range for the fixed scratch", t->device);
+    if (rows == 0) return STT_OK;
+    DeviceScope ds(t->device);
+    if (!ds.ok) return set_error(STT_E_CUDA, "cudaSetDevice(%d) failed", t->device);
+    void* scratch;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_addr[t->device]) {
+            void* p = nullptr;
+            const cudaError_t e = noalloc_scratch_address(&p);
+            if (e != cudaSuccess || !p)
+                return set_error(STT_E_CUDA, "cudaGetSymbolAddress(fixed scratch) failed on device %d: %s", t->device,
+                                 cudaGetErrorString(e));
+            g_noalloc_addr[t->device] = p;
+        }
+        scratch = g_noalloc_addr[t->device];
+    }
+    const float* in = in_dtype == 0 ? static_cast<const float*>(d_in) : nullptr;
+    const __nv_bfloat16* in_bf16 = in_dtype == 1 ? static_cast<const __nv_bfloat16*>(d_in) : nullptr;
+    CUDA_TRY(launch_q4_matmul_splitk(t->w, in, in_bf16, rows, d_out, splits, scratch,
+                                     static_cast<cudaStream_t>(cuda_stream)));
     return STT_OK;
 }
 

@@ -124,6 +124,7 @@ SIGNATURES = {
     "stt_q4_matmul": (C.c_int, [P, F32P, C.c_int, F32P]),
     "stt_q4_matmul_device": (C.c_int, [P, P, C.c_int, C.c_int, P, P]),
     "stt_q4_tensor_dequant": (C.c_int, [P, F32P]),
+    "stt_q4_matmul_device_noalloc": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, P, P]),
     "stt_synth_default": (None, [C.POINTER(stt_synth_params)]),
     "stt_synth_gguf": (C.c_int, [C.POINTER(stt_synth_params), C.POINTER(U8P), C.POINTER(C.c_size_t)]),
     "stt_synth_free": (None, [U8P]),
