@@ -48,12 +48,11 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
-TRACE_NAMES = {1: "frame_start", 2: "barrier_arrive", 3: "barrier_wait", 10: "qkv_prologue", 11: "qkv_stage_wait",
-               12: "qkv_gemv", 21: "attention_stage_wait", 22: "attention", 30: "out_proj_prologue",
-               32: "out_proj_gemv", 40: "linear_in_prologue", 41: "linear_in_stage_wait", 42: "linear_in_gemv",
-               50: "linear_out_prologue", 51: "linear_out_stage_wait", 52: "linear_out_gemv",
-               60: "head_prologue", 61: "head_stage_wait", 62: "head_gemv", 70: "stage_issue",
-               71: "l2_prefetch_issue"}
+TRACE_NAMES = {1: "frame_start", 11: "qkv_inputs", 12: "qkv_gemv", 13: "qkv_end", 21: "attention_inputs",
+               22: "attention", 24: "attention_merge", 23: "attention_end", 31: "out_proj_inputs",
+               32: "out_proj_gemv", 33: "out_proj_end", 41: "linear_in_inputs", 42: "linear_in_gemv",
+               43: "linear_in_end", 51: "linear_out_inputs", 52: "linear_out_gemv", 53: "linear_out_end",
+               61: "head_inputs", 62: "head_gemv", 63: "head_partial", 7: "argmax"}
 
 
 def trace_breakdown(raw):

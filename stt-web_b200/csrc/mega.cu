@@ -1,24 +1,32 @@
 // Persistent single-stream decode step for sm_100a.
 //
-// One cooperative launch of one 512-thread CTA per SM runs `steps` whole frames of one stream:
-//   per layer   QKV -> attention -> out_proj -> linear_in -> linear_out, a grid barrier after each
-//   per frame   head GEMV + per-CTA argmax -> barrier -> every CTA reduces the argmax, applies the
-//               stream rule, and builds the next frame's input from the audio-embedding sum
-//               (computed in the head phase) plus the text row.
-// A single stream reads 627 MB of Q4_0 weights per frame but each phase is a few MB, so the
-// design is about keeping the dependent chain of 81 phases short while HBM keeps streaming:
-//   - every CTA owns fixed row ranges of every matrix.  Right after a phase's GEMV, before the
-//     grid barrier, one thread bulk-copies (cp.async.bulk + mbarrier) the CTA's rows of the
-//     NEXT phase into shared memory, so after the barrier only the activation vector has to be
-//     fetched; the same thread issues cp.async.bulk.prefetch.L2 for the phases beyond, keeping
-//     a byte budget of look-ahead in flight so HBM never idles during barriers;
-//   - the GEMV reads weights from shared memory at about 1.5 instructions per weight: the input
-//     vector becomes 24-bit fixed point per 32-element block (three byte limbs, shared
-//     exponent) and every nibble goes through dp4a, so each block's dot product is exact;
-//   - the grid barrier is a release add + acquire poll on one counter;
-//   - every wait is bounded: a timed-out barrier or copy raises STT_E_DEVICE_FLAG in the step
-//     descriptor, sets an abort word that releases the other CTAs, waits (bounded) for its own
-//     copies in flight, and returns.
+// One cooperative launch of one 512-thread CTA per SM runs `steps` whole frames of one stream.
+// A frame is 5 phases per layer (QKV, attention, out_proj, linear_in, linear_out), then the head
+// and the argmax: 82 dependent steps that together read 627 MB of Q4_0 weights.  A phase is a
+// few MB, so the kernel is built to keep that chain short while HBM keeps streaming:
+//
+//   - Warp 15 is a producer.  It walks the same phase sequence as the other 15 warps, one
+//     "segment" at a time (a norm weight vector, a run of whole weight rows, or the K/V slots of
+//     an attention split), and bulk-copies (cp.async.bulk) each segment into a 192 KB
+//     shared-memory ring with a full mbarrier per segment.  It runs ahead of the consumers,
+//     across phases and frames, as far as the ring allows; the consumers release a phase's
+//     segments through empty mbarriers when the phase ends.
+//   - Phases exchange activations through flagged buffers instead of grid barriers: every value
+//     is one 64-bit word (value bits | epoch << 32), and a reader polls the words it needs until
+//     each carries the epoch of the phase that wrote it.  A reader waits exactly for its own
+//     inputs, and one L2 round trip both synchronises and fetches.  Epochs are unique per
+//     (frame, phase) over a stream set's lifetime (a base word persists across launches), every
+//     buffer is double-buffered by layer or frame parity, and each phase's inputs depend on every
+//     CTA's outputs two phases back, so a reader never meets a value of a later epoch.
+//   - One release/acquire counter per frame orders the K/V ring writes of a frame (made by the
+//     QKV epilogues) before the producers' bulk copies of those slots in later frames.
+//   - The GEMV turns the input vector into 24-bit fixed point per 32-element block (three byte
+//     limbs, shared exponent) and puts every nibble through dp4a, so each block's dot product is
+//     exact; only the per-block scale and the f32 accumulation round.
+//   - Every wait is bounded.  A wait that gives up raises STT_E_DEVICE_FLAG in the step
+//     descriptor and sets an abort word; every other wait sees that word and returns, all
+//     consumer threads run on to the end of the layer with in-bounds garbage and stop together,
+//     the producer waits (bounded) for its copies in flight, and the CTA exits.
 #include <algorithm>
 #include <cfloat>
 #include <cstdlib>
@@ -32,48 +40,76 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
+constexpr int kCWarps = kWarps - 1;        // consumer warps; warp kCWarps is the producer
+constexpr int kCThreads = kCWarps * 32;
 constexpr int kNBMax = 264;                // K / 32 for K <= 8448
 constexpr int kMaxK = kNBMax * 32;
-constexpr int kWBuf = 144 * 1024;          // staged weight rows of one phase per CTA
-constexpr int kMaxL = 32;                  // layers held in the shared layer table
-constexpr int kMaxOwnRows = 256;           // rows of x one CTA owns (out_proj / linear_out rows)
-constexpr int kQMax = (kMaxK / 4 + kThreads - 1) / kThreads;  // input quads per thread
-constexpr uint32_t kSpinLimit = 1u << 26;  // bounded waits (~ seconds)
+constexpr uint32_t kRing = 192u * 1024u;   // weight / K-V ring
+constexpr uint32_t kSegMax = 32u * 1024u;  // target bytes of one weight segment
+constexpr int kNBar = 32;                  // segments in flight at most
+constexpr int kMaxL = 32;
+constexpr int kMaxOwnRows = 256;
+constexpr uint32_t kEpochsPerFrame = 256;  // steps of a frame: 5 L + 2 <= 256
+constexpr int kPartPairs = 132;            // attention partial: M, L, 2 unused, O[128]
+// Bounded waits: a legitimate wait lasts at most about a frame (milliseconds); these limits give
+// up after roughly a second.
+constexpr uint32_t kSpinLimit = 1u << 21;    // mbarrier / counter polls
+constexpr uint32_t kLLSpinLimit = 1u << 20;  // flagged-word polls (each with a short sleep)
+
+enum Kind : int { K_QKV = 0, K_ATT = 1, K_OUT = 2, K_IN = 3, K_DOWN = 4, K_HEAD = 5 };
+
+// Row ranges of one CTA in one kind of phase; the same for every layer.
+struct Range {
+    int32_t r0;     // first row (linear_in: first gate row)
+    int32_t n;      // rows (linear_in: units)
+    int32_t units;  // pairs of rows, or (gate, value) units
+    int32_t ups;    // units per weight segment
+};
 
 struct MegaArgs {
     Ctx c;
     int32_t steps;
     int32_t nsplit;        // attention splits per head
-    uint32_t* bar;         // [0] arrivals (monotonic), [1] abort, [2..2+H) head tickets
-    const float* xa;       // [steps][D] audio-embedding sums of every frame (audio_sum_kernel)
-    float* amax_v;         // [grid] per-CTA best logit
-    int32_t* amax_i;       // [grid] and its index
-    uint32_t pf_budget;    // L2 look-ahead per CTA in bytes
-    int32_t pf_lines;      // 1: warp 0 prefetches 128-byte lines; 0: bulk prefetch (TMA queue)
-    unsigned long long* trace;  // optional: %globaltimer at each barrier of one frame
+    uint32_t* bar;         // [0] frames finished (summed over CTAs), [1] abort
+    uint32_t* base;        // epoch base, persists across launches
+    const float* xa;       // [steps][D] audio-embedding sums (audio_sum_kernel)
+    uint64_t* xb[2][2];    // [layer parity][0 after out_proj, 1 after linear_out]: D words
+    uint64_t* qkvb[2];     // [layer parity]: 3D words (q, k rotated; v)
+    uint64_t* partb[2];    // [layer parity]: H * nsplit * kPartPairs words
+    uint64_t* attb[2];     // [layer parity]: D words (softmax(q.k^T * scale).v per head)
+    uint64_t* hidb[2];     // [layer parity]: F words
+    uint64_t* argb[2];     // [frame parity]: 2 words per CTA (best logit, its index)
+    unsigned long long* trace;  // optional: (tag, SM clock) pairs of one frame of CTA 0
     int32_t trace_frame;
     int32_t trace_cap;
 };
 
 struct Smem {
-    alignas(128) uint8_t wbuf[kWBuf];  // this CTA's weight rows of the current phase
-    uint4 limbs[6 * kNBMax];           // [vec][block]: L0,L1,L2 of groups 0-3, then of groups 4-7
-    float xs[kNBMax];                  // 2^(e_b - 27): block scale of the fixed-point input
-    float xf[kMaxK];                   // the input vector in f32 / attention scratch
+    alignas(128) uint8_t ring[kRing];
+    uint4 limbs[6 * kNBMax];  // [vec][block]: L0,L1,L2 of groups 0-3, then of groups 4-7; attention scratch
+    float xs[kNBMax];         // 2^(e_b - 27): block scale of the fixed-point input
     LayerDev layers[kMaxL];
-    float xown[kMaxOwnRows];           // this CTA's rows of the residual stream x
-    float2 rope[64];                   // (cos, sin) of this frame's position, HD / 2 pairs
+    float xown[kMaxOwnRows];  // this CTA's rows of the residual stream x
+    float2 rope[64];          // (cos, sin) of this frame's position
     float red[2][kWarps];
-    float wv[kWarps];
+    float wv[kWarps];         // head: best logit of each warp
     int32_t wi[kWarps];
-    alignas(8) unsigned long long mbar;
-    uint32_t staged, waited;  // staged copies issued / waited for (thread 0's bookkeeping)
-    int32_t flag;
+    float av[kWarps];         // argmax: best of each warp over the per-CTA words
+    int32_t ai[kWarps];
+    Range rg[6];              // per kind of phase; rg[K_ATT] unused
+    StreamState st;           // stream state at the start of the current frame
+    uint32_t text;            // text token of the current frame
+    uint32_t seg_off[kNBar];  // ring offset of an issued segment (producer writes, consumers read)
+    uint32_t seg_end[kNBar];  // its end in ring bytes since launch (producer only)
+    alignas(8) unsigned long long full[kNBar];
+    alignas(8) unsigned long long empty[kNBar];
+    int32_t stop[2];          // consumers: some thread saw an abort (by agreement parity)
+    int32_t tslot, tron;      // trace cursor (consumer thread 0)
 };
+static_assert(sizeof(Smem) <= 232448, "shared memory per CTA");
 
 // The kernel's dynamic shared memory.  Functions that are not inlined recover the Smem through
-// this file-scope array instead of a reference parameter, so the compiler keeps emitting
-// shared-memory (LDS/STS) accesses rather than generic ones.
+// this file-scope array so the compiler keeps emitting shared-memory accesses.
 extern __shared__ __align__(128) uint4 mega_smem[];
 __device__ __forceinline__ Smem& smem_ref() { return *reinterpret_cast<Smem*>(mega_smem); }
 
@@ -87,29 +123,15 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
 __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void prefetch_line(const void* p) {
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-// Called by all 32 lanes of warp 0: bulk prefetch by lane 0, or line prefetches spread over lanes.
-__device__ __forceinline__ void prefetch_range(const void* p, uint32_t bytes, bool lines, int lane) {
-    const uint8_t* b = static_cast<const uint8_t*>(p);
-    if (lines) {
-        for (uint32_t o = (uint32_t)lane * 128u; o < bytes; o += 32u * 128u) prefetch_line(b + o);
-    } else if (lane == 0) {
-        for (uint32_t o = 0; o < bytes; o += 65536u) prefetch_l2(b + o, min(65536u, bytes - o));
-    }
-}
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(unsigned long long* m, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(m)), "r"(count) : "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(unsigned long long* m, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(m)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* m) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(m)) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(unsigned long long* m, uint32_t parity) {
     uint32_t ok;
@@ -122,12 +144,26 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* m, uint32_t pa
         : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, unsigned long long* m) {
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, unsigned long long* m) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(m))
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst), "l"(src),
+        "r"(bytes), "r"(smem_addr(m))
         : "memory");
 }
+// flagged words: value bits in the low half, epoch in the high half
+__device__ __forceinline__ void ll_store(uint64_t* p, float v, uint32_t ep) {
+    const uint64_t w = ((uint64_t)ep << 32) | (uint64_t)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ void ll_load2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint32_t ll_ep(uint64_t w) { return (uint32_t)(w >> 32); }
+__device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
+
+// consumer-only CTA barrier (the producer warp never joins it)
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory"); }
+
 __device__ __forceinline__ int dp4a_su(int a, uint32_t b, int c) {
     int d;
     asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -147,129 +183,88 @@ __device__ __forceinline__ unsigned long long globaltimer() {
     return t;
 }
 
-// Trace points of one frame of CTA 0: (tag, SM clock cycles) pairs, bracketed by (0, %globaltimer)
-// pairs at the frame's start and end so the host can convert cycles to time.  Tags: 1 frame start,
-// 2 barrier entry, 3 barrier exit, 10*k + {0 prologue done, 1 staged copy landed, 2 compute done}
-// for phase kinds k = 1 qkv, 2 attention, 3 out_proj, 4 linear_in, 5 linear_out, 6 head.
-struct Tracer {
-    int slot = 0;
-    bool on = false;
-    __device__ void mark(const MegaArgs& P, unsigned long long tag) {
-        if (on && threadIdx.x == 0 && slot + 1 < P.trace_cap) {
-            P.trace[slot] = tag;
-            P.trace[slot + 1] = clock64();
-            slot += 2;
-        }
-    }
-    // (tag 0, %globaltimer) pair: lets the host convert the cycle counts to nanoseconds
-    __device__ void wall(const MegaArgs& P) {
-        if (on && threadIdx.x == 0 && slot + 1 < P.trace_cap) {
-            P.trace[slot] = 0;
-            P.trace[slot + 1] = globaltimer();
-            slot += 2;
-        }
-    }
-};
+__device__ __forceinline__ bool aborted(const MegaArgs& P) { return *(volatile const uint32_t*)(P.bar + 1) != 0u; }
+__device__ __noinline__ void give_up(const MegaArgs& P) {
+    raise_error(P.c.desc, -5);
+    atomicExch(P.bar + 1, 1u);
+}
 
-__device__ __forceinline__ int64_t split_lo(int64_t total, int part, int parts) { return total * part / parts; }
-
-// Grid barrier.  Returns false when the kernel must stop (a timeout here or in another CTA).
-__device__ bool grid_sync(const MegaArgs& P, uint32_t& epoch, Smem& sm, Tracer& tr) {
-    __syncthreads();
-    tr.mark(P, 2);
-    ++epoch;
-    if (threadIdx.x == 0) {
-        const uint32_t target = epoch * gridDim.x;
-        red_release_add(P.bar, 1u);  // release: this CTA's writes, ordered by the barrier above
-        int ok = 1;
-        uint32_t spins = 0;
-        for (;;) {
-            if ((int32_t)(ld_acquire(P.bar) - target) >= 0) break;
-            if (*(volatile uint32_t*)(P.bar + 1)) {
-                ok = 0;
-                break;
-            }
-            if (++spins > kSpinLimit) {
-                atomicExch(P.bar + 1, 1u);
-                raise_error(P.c.desc, -5);
-                ok = 0;
-                break;
-            }
-            if (spins > 2048) __nanosleep(32);
-        }
-        sm.flag = ok;
+// Trace of one frame of CTA 0: (tag, SM clock) pairs from consumer thread 0, bracketed by
+// (0, %globaltimer) pairs so the host can convert cycles to time.  Tags: 1 frame start, then per
+// kind of phase k (1 qkv, 2 attention, 3 out_proj, 4 linear_in, 5 linear_out, 6 head):
+// 10k+1 inputs ready, 10k+2 this thread's compute done, 10k+3 phase end; 24 the partials of the
+// other attention splits merged (split-0 CTAs); 7 argmax reduced.
+__device__ __forceinline__ void trace_mark(const MegaArgs& P, unsigned long long tag) {
+    Smem& sm = smem_ref();
+    if (threadIdx.x == 0 && sm.tron && sm.tslot + 1 < P.trace_cap) {
+        P.trace[sm.tslot] = tag;
+        P.trace[sm.tslot + 1] = clock64();
+        sm.tslot += 2;
     }
-    __syncthreads();
-    tr.mark(P, 3);
-    return sm.flag != 0;
+}
+__device__ __forceinline__ void trace_wall(const MegaArgs& P) {
+    Smem& sm = smem_ref();
+    if (threadIdx.x == 0 && sm.tron && sm.tslot + 1 < P.trace_cap) {
+        P.trace[sm.tslot] = 0;
+        P.trace[sm.tslot + 1] = globaltimer();
+        sm.tslot += 2;
+    }
+}
+
+// ------------------------------------------------------------------------------ waits
+
+// Consumer wait for segment i to land.  Returns false after an abort (seen or raised).
+__device__ __forceinline__ bool wait_seg(Smem& sm, const MegaArgs& P, uint32_t i) {
+    unsigned long long* m = &sm.full[i % kNBar];
+    const uint32_t par = (i / kNBar) & 1u;
+    uint32_t spins = 0;
+    while (!mbar_try_wait(m, par)) {
+        if ((++spins & 255u) == 0) {
+            if (aborted(P)) return false;
+            if (spins > kSpinLimit) {
+                give_up(P);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// Waits until the 2 * N words at p (16-byte aligned) all carry epoch ep.
+template <int N>
+__device__ __forceinline__ bool ll_wait(const MegaArgs& P, const uint64_t* p, uint32_t ep, uint64_t (&w)[2 * N]) {
+    uint32_t spins = 0;
+    for (;;) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) ll_load2(p + 2 * i, w[2 * i], w[2 * i + 1]);
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < 2 * N; ++i) ok = ok && ll_ep(w[i]) == ep;
+        if (ok) return true;
+        ++spins;
+        if ((spins & 63u) == 0) {
+            if (aborted(P)) return false;
+            if (spins > kLLSpinLimit) {
+                give_up(P);
+                return false;
+            }
+        }
+        __nanosleep(64);
+    }
 }
 
 // ------------------------------------------------------------------------------ phase geometry
 
-enum Kind : int { K_QKV = 0, K_ATT = 1, K_OUT = 2, K_IN = 3, K_DOWN = 4, K_HEAD = 5 };
-
-// The rows of one phase this CTA reads: one or two contiguous row ranges of one matrix.
-struct Rows {
-    const Q4Dev* W;
-    int32_t r0[2];
-    int32_t n[2];
-    int32_t nr;  // number of ranges
-};
-
 __device__ __forceinline__ Kind kind_of(int p, int L) { return p == 5 * L ? K_HEAD : (Kind)(p % 5); }
+__device__ __forceinline__ int64_t split_lo(int64_t total, int part, int parts) { return total * part / parts; }
 
-__device__ Rows rows_of(const Smem& sm, const Ctx& c, int p, int cta, int ncta) {
-    Rows r{};
+__device__ __forceinline__ const Q4Dev* matrix_of(const Smem& sm, const Ctx& c, int p) {
     const Kind k = kind_of(p, c.L);
-    if (k == K_HEAD) {
-        const int64_t U = (c.V + 1) / 2;
-        const int64_t a = 2 * split_lo(U, cta, ncta), b = min((int64_t)c.V, 2 * split_lo(U, cta + 1, ncta));
-        r.W = &c.head;
-        r.r0[0] = (int)a;
-        r.n[0] = (int)max((int64_t)0, b - a);
-        r.nr = 1;
-        return r;
-    }
+    if (k == K_HEAD) return &c.head;
     const LayerDev& L = sm.layers[p / 5];
-    switch (k) {
-        case K_QKV:
-        case K_OUT:
-        case K_DOWN: {
-            const Q4Dev* W = k == K_QKV ? &L.qkv : (k == K_OUT ? &L.out : &L.fout);
-            const int64_t U = W->n / 2;
-            r.W = W;
-            r.r0[0] = (int)(2 * split_lo(U, cta, ncta));
-            r.n[0] = (int)(2 * split_lo(U, cta + 1, ncta)) - r.r0[0];
-            r.nr = 1;
-            break;
-        }
-        case K_IN: {
-            const int u0 = (int)split_lo(c.F, cta, ncta), u1 = (int)split_lo(c.F, cta + 1, ncta);
-            r.W = &L.fin;
-            r.r0[0] = u0;
-            r.r0[1] = c.F + u0;
-            r.n[0] = r.n[1] = u1 - u0;
-            r.nr = 2;
-            break;
-        }
-        default:
-            r.nr = 0;
-            break;
-    }
-    return r;
+    return k == K_QKV ? &L.qkv : k == K_OUT ? &L.out : k == K_IN ? &L.fin : &L.fout;
 }
-
-// Shared-memory layout of a staged phase: for each range, nibbles then scales (16-byte aligned),
-// then the phase's norm weight (D floats) when it has one.
-struct Staged {
-    uint32_t nib[2];
-    uint32_t sc[2];
-    uint32_t alpha;  // offset of the norm weight, or ~0u
-    uint32_t bytes;
-};
-
-// The norm weight applied to a phase's input: norm1 (QKV), norm2 (linear_in), out_norm (head).
-__device__ __forceinline__ const float* phase_alpha(const Smem& sm, const Ctx& c, int p) {
+__device__ __forceinline__ const float* alpha_of(const Smem& sm, const Ctx& c, int p) {
     const Kind k = kind_of(p, c.L);
     if (k == K_HEAD) return c.out_norm;
     if (k == K_QKV) return sm.layers[p / 5].norm1;
@@ -277,178 +272,244 @@ __device__ __forceinline__ const float* phase_alpha(const Smem& sm, const Ctx& c
     return nullptr;
 }
 
-__device__ __forceinline__ Staged staged_layout(const Rows& r, bool alpha, int D) {
-    Staged s{};
-    uint32_t off = 0;
-    const uint32_t NB = r.nr ? (uint32_t)(r.W->k >> 5) : 0;
-    for (int i = 0; i < r.nr; ++i) {
-        s.nib[i] = off;
-        off += (uint32_t)r.n[i] * NB * 16;
-        s.sc[i] = off;
-        off += ((uint32_t)r.n[i] * NB * 2 + 15) & ~15u;
-    }
-    s.alpha = ~0u;
-    if (alpha) {
-        s.alpha = off;
-        off += (uint32_t)D * 4;
-    }
-    s.bytes = off;
-    return s;
-}
-
-// Slots [j0, j1) of the attention split handled by this CTA (empty when h >= H).
+// Attention split of this CTA: head h = cta / nsplit, split s; ring slots [j0, j1).
 struct Split {
     int h, s, j0, j1;
 };
-__device__ __forceinline__ Split split_of(const MegaArgs& P, int cta, int len) {
+__device__ __forceinline__ Split split_of(int cta, int nsplit, int H, int len) {
     Split r;
-    r.h = cta / P.nsplit;
-    r.s = cta % P.nsplit;
-    const int chunk = (len + P.nsplit - 1) / P.nsplit;
-    r.j0 = r.s * chunk;
-    r.j1 = r.h < P.c.H ? min(len, r.j0 + chunk) : r.j0;
-    if (r.j1 < r.j0) r.j1 = r.j0;
+    r.h = cta / nsplit;
+    r.s = cta % nsplit;
+    const int chunk = (len + nsplit - 1) / nsplit;
+    r.j0 = min(len, r.s * chunk);
+    r.j1 = r.h < H ? min(len, r.j0 + chunk) : r.j0;
     return r;
 }
 
-// wbuf offset of the staged K/V slots: after the out_proj rows, which are staged with them.
-__device__ __forceinline__ uint32_t kv_offset(const Smem& sm, const Ctx& c, int layer, int cta, int ncta) {
-    const Staged so = staged_layout(rows_of(sm, c, 5 * layer + K_OUT, cta, ncta), false, c.D);
-    return (so.bytes + 127u) & ~127u;
+// Segments of phase p for this CTA: [norm weight] + weight runs, or one K/V segment.
+__device__ __forceinline__ int weight_segs(const Range& r) { return r.units > 0 ? (r.units + r.ups - 1) / r.ups : 0; }
+__device__ __forceinline__ int phase_segs(const Smem& sm, const MegaArgs& P, int p, int cta) {
+    const Kind k = kind_of(p, P.c.L);
+    if (k == K_ATT) return cta / P.nsplit < P.c.H ? 1 : 0;
+    const int w = weight_segs(sm.rg[k]);
+    return w == 0 ? 0 : w + (alpha_of(sm, P.c, p) ? 1 : 0);
 }
 
-// Bytes a phase reads from HBM for this CTA (weights, or the K/V slots of its attention split).
-__device__ uint32_t phase_bytes(const Smem& sm, const MegaArgs& P, int p, int cta, int ncta, int len) {
-    const Ctx& c = P.c;
-    if (kind_of(p, c.L) == K_ATT) {
-        const int h = cta / P.nsplit, s = cta % P.nsplit;
-        if (h >= c.H) return 0;
-        const int chunk = (len + P.nsplit - 1) / P.nsplit;
-        const int j0 = s * chunk, j1 = min(len, j0 + chunk);
-        return j1 > j0 ? (uint32_t)(j1 - j0) * c.HD * 2 * (c.kv_f32 ? 4 : 2) : 0u;
-    }
-    const Rows r = rows_of(sm, c, p, cta, ncta);
-    uint32_t b = 0;
-    for (int i = 0; i < r.nr; ++i) b += (uint32_t)r.n[i] * (uint32_t)(r.W->k >> 5) * 18u;
-    return b;
+// Weight segment k of a phase: units [ua, ua + nu), nr rows in the first run (pairs: both rows
+// of every unit; linear_in: the gate rows, then as many value rows), scales after the nibbles.
+struct WSeg {
+    int ua, nu;
+    int nr;
+    uint32_t sc_base;
+};
+__device__ __forceinline__ WSeg wseg(const Range& r, bool gate, int k, int NB) {
+    WSeg s;
+    s.ua = k * r.ups;
+    s.nu = min(r.ups, r.units - s.ua);
+    s.nr = gate ? s.nu : min(2 * s.nu, r.n - 2 * s.ua);
+    s.sc_base = (uint32_t)(gate ? 2 * s.nu : s.nr) * NB * 16u;
+    return s;
 }
 
-// L2 prefetch of one phase's ranges (all lanes of warp 0).
-__device__ void prefetch_phase(const Smem& sm, const MegaArgs& P, int p, int cta, int ncta, int len, int lane) {
-    const Ctx& c = P.c;
-    const bool lines = P.pf_lines != 0;
-    if (kind_of(p, c.L) == K_ATT) {
-        const int h = cta / P.nsplit, s = cta % P.nsplit;
-        if (h >= c.H) return;
-        const int chunk = (len + P.nsplit - 1) / P.nsplit;
-        const int j0 = s * chunk, j1 = min(len, j0 + chunk);
-        if (j1 <= j0) return;
-        const int es = c.kv_f32 ? 4 : 2;
-        const uint8_t* kb = static_cast<const uint8_t*>(c.kv) +
-                            ((int64_t)c.ids[0] * c.kv_stream_stride + (int64_t)(p / 5) * c.kv_layer_stride +
-                             (int64_t)h * c.ML * c.HD + (int64_t)j0 * c.HD) * es;
-        const uint32_t bytes = (uint32_t)(j1 - j0) * c.HD * es;
-        prefetch_range(kb, bytes, lines, lane);
-        prefetch_range(kb + c.kv_half_stride * es, bytes, lines, lane);
-        return;
-    }
-    const Rows r = rows_of(sm, c, p, cta, ncta);
-    for (int i = 0; i < r.nr; ++i) {
-        if (r.n[i] <= 0) continue;
-        const int64_t NB = r.W->k >> 5;
-        prefetch_range(r.W->nib + (int64_t)r.r0[i] * NB, (uint32_t)(r.n[i] * NB * 16), lines, lane);
-        const uint32_t sbytes = (uint32_t)(r.n[i] * NB * 2) & ~15u;
-        if (sbytes) prefetch_range(r.W->scale + (int64_t)r.r0[i] * NB, sbytes, lines, lane);
-    }
-}
+// ------------------------------------------------------------------------------ producer
 
-// Bulk copy of one row range's nibbles and scales into wbuf (thread 0).
-__device__ __forceinline__ void stage_rows(Smem& sm, const Q4Dev* W, int r0, int n, uint32_t nib_off, uint32_t sc_off) {
-    if (n <= 0) return;
-    const int64_t NB = W->k >> 5;
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(W->nib + (int64_t)r0 * NB);
-    const uint32_t nbytes = (uint32_t)(n * NB * 16);
-    for (uint32_t o = 0; o < nbytes; o += 32768u)
-        bulk_g2s(sm.wbuf + nib_off + o, src + o, min(32768u, nbytes - o), &sm.mbar);
-    const uint32_t sbytes = (uint32_t)(n * NB * 2);
-    const uint32_t sfull = sbytes & ~15u;
-    if (sfull) bulk_g2s(sm.wbuf + sc_off, W->scale + (int64_t)r0 * NB, sfull, &sm.mbar);
-    if (sbytes != sfull) {
-        // scale bytes not a multiple of 16: the tail is copied by this thread; the consumers
-        // read it after the barrier that publishes the bulk copies
-        const uint16_t* tail = W->scale + (int64_t)r0 * NB + sfull / 2;
-        uint16_t* dst = reinterpret_cast<uint16_t*>(sm.wbuf + sc_off + sfull);
-        for (uint32_t t = 0; t < (sbytes - sfull) / 2; ++t) dst[t] = tail[t];
-    }
-}
+struct Prod {
+    uint32_t issued;    // segments issued
+    uint32_t released;  // segments known released
+    uint32_t head;      // ring bytes allocated since launch (monotonic)
+    uint32_t tail;      // end of the last released segment
+};
 
-__device__ __forceinline__ uint32_t rows_tx(const Rows& r) {
-    uint32_t tx = 0;
-    for (int i = 0; i < r.nr; ++i)
-        if (r.n[i] > 0) {
-            const uint32_t NB = (uint32_t)(r.W->k >> 5);
-            tx += (uint32_t)r.n[i] * NB * 16u + (((uint32_t)r.n[i] * NB * 2u) & ~15u);
-        }
-    return tx;
-}
-
-// Thread 0: bulk-copies phase p's rows of this CTA (and its norm weight) into wbuf; completion on
-// sm.mbar.  No proxy fence is needed before overwriting wbuf: it was only read by the generic
-// proxy, and every reader passed the __syncthreads that precedes this call.
-__device__ void stage_phase(Smem& sm, const Ctx& c, int p, int cta, int ncta) {
-    const Rows r = rows_of(sm, c, p, cta, ncta);
-    const float* alpha = phase_alpha(sm, c, p);
-    const Staged s = staged_layout(r, alpha != nullptr, c.D);
-    ++sm.staged;
-    mbar_expect_tx(&sm.mbar, rows_tx(r) + (alpha ? (uint32_t)c.D * 4u : 0u));
-    for (int i = 0; i < r.nr; ++i) stage_rows(sm, r.W, r.r0[i], r.n[i], s.nib[i], s.sc[i]);
-    if (alpha) bulk_g2s(sm.wbuf + s.alpha, alpha, (uint32_t)c.D * 4u, &sm.mbar);
-}
-
-// Thread 0, after the QKV GEMV of layer l: stages the out_proj rows and this CTA's K/V slots of
-// layer l (as of the previous frames: the slot written this frame is read from qkv instead).
-__device__ void stage_out_kv(Smem& sm, const MegaArgs& P, int l, int cta, int ncta, int len) {
-    const Ctx& c = P.c;
-    const Rows r = rows_of(sm, c, 5 * l + K_OUT, cta, ncta);
-    const Staged s = staged_layout(r, false, c.D);
-    const Split sp = split_of(P, cta, len);
-    const int es = c.kv_f32 ? 4 : 2;
-    const uint32_t kvb = (uint32_t)(sp.j1 - sp.j0) * c.HD * es;
-    const uint32_t koff = kv_offset(sm, c, l, cta, ncta);
-    ++sm.staged;
-    mbar_expect_tx(&sm.mbar, rows_tx(r) + 2u * kvb);
-    stage_rows(sm, r.W, r.r0[0], r.n[0], s.nib[0], s.sc[0]);
-    if (kvb) {
-        const uint8_t* kb = static_cast<const uint8_t*>(c.kv) +
-                            ((int64_t)c.ids[0] * c.kv_stream_stride + (int64_t)l * c.kv_layer_stride +
-                             (int64_t)sp.h * c.ML * c.HD + (int64_t)sp.j0 * c.HD) * es;
-        for (uint32_t o = 0; o < kvb; o += 32768u) {
-            bulk_g2s(sm.wbuf + koff + o, kb + o, min(32768u, kvb - o), &sm.mbar);
-            bulk_g2s(sm.wbuf + koff + kvb + o, kb + c.kv_half_stride * es + o, min(32768u, kvb - o), &sm.mbar);
-        }
-    }
-}
-
-// Waits (bounded) for the staged copy of the current phase; the parity flips per staging.
-__device__ bool wait_stage(Smem& sm, const MegaArgs& P, uint32_t& parity) {
-    if (threadIdx.x == 0) {
-        int ok = 1;
+// Lane 0 waits for the release of the oldest unreleased segment; every lane gets the answer.
+__device__ __forceinline__ bool prod_wait_release(Smem& sm, const MegaArgs& P, Prod& q) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) {
+        const uint32_t j = q.released;
+        unsigned long long* m = &sm.empty[j % kNBar];
+        const uint32_t par = (j / kNBar) & 1u;
         uint32_t spins = 0;
-        while (!mbar_try_wait(&sm.mbar, parity)) {
-            if (++spins > kSpinLimit || *(volatile uint32_t*)(P.bar + 1)) {
-                if (!*(volatile uint32_t*)(P.bar + 1)) raise_error(P.c.desc, -5);
-                atomicExch(P.bar + 1, 1u);
-                ok = 0;
-                break;
+        while (!mbar_try_wait(m, par)) {
+            if ((++spins & 255u) == 0) {
+                if (aborted(P)) {
+                    ok = 0;
+                    break;
+                }
+                if (spins > kSpinLimit) {
+                    give_up(P);
+                    ok = 0;
+                    break;
+                }
             }
         }
-        if (ok) ++sm.waited;
-        sm.flag = ok;
     }
-    __syncthreads();
-    const bool ok = sm.flag != 0;
-    if (ok) parity ^= 1u;
-    return ok;
+    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+    if (ok) {
+        q.tail = sm.seg_end[q.released % kNBar];
+        ++q.released;
+    }
+    return ok != 0;
+}
+
+// Allocates `bytes` (a multiple of 128, at most kRing) in the ring, waiting for releases as
+// needed; returns the offset, or ~0u after an abort.
+__device__ __forceinline__ uint32_t prod_alloc(Smem& sm, const MegaArgs& P, Prod& q, uint32_t bytes) {
+    uint32_t start = q.head;
+    uint32_t off = start % kRing;
+    if (off + bytes > kRing) {
+        start += kRing - off;
+        off = 0;
+    }
+    const uint32_t end = start + bytes;
+    while (q.issued - q.released >= (uint32_t)kNBar || end - q.tail > kRing)
+        if (!prod_wait_release(sm, P, q)) return ~0u;
+    q.head = end;
+    if ((threadIdx.x & 31) == 0) {
+        sm.seg_off[q.issued % kNBar] = off;
+        sm.seg_end[q.issued % kNBar] = end;
+    }
+    return off;
+}
+
+// One segment: up to 4 bulk copies (source, bytes, offset inside the segment).
+struct Copies {
+    const void* src[4];
+    uint32_t bytes[4];
+    uint32_t dst[4];
+    int n;
+    uint32_t total;
+    __device__ void add(const void* s, uint32_t b, uint32_t d) {
+        if (b == 0) return;
+        src[n] = s;
+        bytes[n] = b;
+        dst[n] = d;
+        ++n;
+        total = max(total, d + b);
+    }
+};
+
+__device__ __forceinline__ bool prod_issue(Smem& sm, const MegaArgs& P, Prod& q, const Copies& cp) {
+    const uint32_t off = prod_alloc(sm, P, q, (max(cp.total, 16u) + 127u) & ~127u);
+    if (off == ~0u) return false;
+    if ((threadIdx.x & 31) == 0) {
+        uint32_t tx = 0;
+        for (int i = 0; i < cp.n; ++i) tx += cp.bytes[i];
+        unsigned long long* m = &sm.full[q.issued % kNBar];
+        mbar_expect_tx(m, tx);  // the producer's arrival; the phase completes when tx bytes land
+        const uint32_t base = smem_addr(sm.ring) + off;
+        for (int i = 0; i < cp.n; ++i) bulk_g2s(base + cp.dst[i], cp.src[i], cp.bytes[i], m);
+    }
+    __syncwarp();
+    ++q.issued;
+    return true;
+}
+
+// The producer warp: every segment of every phase of every frame, in consumption order.
+// Returns the number of segments issued.
+__device__ __noinline__ uint32_t producer(const MegaArgs& P, int cta) {
+    Smem& sm = smem_ref();
+    const Ctx& c = P.c;
+    const int per_frame = 5 * c.L + 1;
+    Prod q{0, 0, 0, 0};
+    StreamState st = c.state[c.ids[0]];
+    const int es = c.kv_f32 ? 4 : 2;
+    const uint32_t slot_bytes = (uint32_t)c.HD * es;
+    for (int f = 0; f < P.steps; ++f) {
+        const int len = min(st.len + 1, c.ML);
+        const int wp = st.write_pos;
+        for (int p = 0; p < per_frame; ++p) {
+            const Kind k = kind_of(p, c.L);
+            if (k == K_ATT) {
+                const Split sp = split_of(cta, P.nsplit, c.H, len);
+                if (sp.h >= c.H) continue;
+                if (p == K_ATT && f > 0) {
+                    // the slots come from earlier frames: wait until every CTA has finished
+                    // frame f - 1 (its K/V writes are released with that count)
+                    int ok = 1;
+                    if ((threadIdx.x & 31) == 0) {
+                        const uint32_t target = (uint32_t)f * gridDim.x;
+                        uint32_t spins = 0;
+                        while ((int32_t)(ld_acquire(P.bar) - target) < 0) {
+                            if ((++spins & 63u) == 0) {
+                                if (aborted(P)) {
+                                    ok = 0;
+                                    break;
+                                }
+                                if (spins > kSpinLimit) {
+                                    give_up(P);
+                                    ok = 0;
+                                    break;
+                                }
+                            }
+                            __nanosleep(128);
+                        }
+                        // generic-proxy writes, now visible to this thread, before the bulk
+                        // copies (async proxy) read them
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                    }
+                    if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) return q.issued;
+                }
+                const uint8_t* kb = static_cast<const uint8_t*>(c.kv) +
+                                    ((int64_t)c.ids[0] * c.kv_stream_stride + (int64_t)(p / 5) * c.kv_layer_stride +
+                                     (int64_t)sp.h * c.ML * c.HD) * es;
+                const uint8_t* vb = kb + c.kv_half_stride * es;
+                const uint32_t n = (uint32_t)(sp.j1 - sp.j0);
+                Copies cp{};
+                // slot wp is this frame's: it is read from the QKV output, never copied, so the
+                // copies cannot race with its write
+                const bool in = wp >= sp.j0 && wp < sp.j1;
+                const int a1 = in ? wp : sp.j1;
+                const int b0 = in ? wp + 1 : sp.j1;
+                cp.add(kb + (int64_t)sp.j0 * slot_bytes, (uint32_t)(a1 - sp.j0) * slot_bytes, 0);
+                cp.add(kb + (int64_t)b0 * slot_bytes, (uint32_t)(sp.j1 - b0) * slot_bytes,
+                       (uint32_t)(b0 - sp.j0) * slot_bytes);
+                cp.add(vb + (int64_t)sp.j0 * slot_bytes, (uint32_t)(a1 - sp.j0) * slot_bytes, n * slot_bytes);
+                cp.add(vb + (int64_t)b0 * slot_bytes, (uint32_t)(sp.j1 - b0) * slot_bytes,
+                       n * slot_bytes + (uint32_t)(b0 - sp.j0) * slot_bytes);
+                cp.total = max(cp.total, 2 * n * slot_bytes);
+                if (!prod_issue(sm, P, q, cp)) return q.issued;
+                continue;
+            }
+            const Range r = sm.rg[k];
+            const int nw = weight_segs(r);
+            if (nw == 0) continue;
+            if (const float* alpha = alpha_of(sm, c, p)) {
+                Copies cp{};
+                cp.add(alpha, (uint32_t)c.D * 4u, 0);
+                if (!prod_issue(sm, P, q, cp)) return q.issued;
+            }
+            const Q4Dev* W = matrix_of(sm, c, p);
+            const int NB = W->k >> 5;
+            const bool gate = k == K_IN;
+            for (int s = 0; s < nw; ++s) {
+                const WSeg g = wseg(r, gate, s, NB);
+                Copies cp{};
+                const int ra = gate ? r.r0 + g.ua : r.r0 + 2 * g.ua;
+                cp.add(W->nib + (int64_t)ra * NB, (uint32_t)g.nr * NB * 16u, 0);
+                cp.add(W->scale + (int64_t)ra * NB, (uint32_t)g.nr * NB * 2u, g.sc_base);
+                if (gate) {
+                    const int rb = c.F + r.r0 + g.ua;
+                    cp.add(W->nib + (int64_t)rb * NB, (uint32_t)g.nu * NB * 16u, (uint32_t)g.nu * NB * 16u);
+                    cp.add(W->scale + (int64_t)rb * NB, (uint32_t)g.nu * NB * 2u, g.sc_base + (uint32_t)g.nu * NB * 2u);
+                }
+                if (!prod_issue(sm, P, q, cp)) return q.issued;
+            }
+        }
+        st.len = min(st.len + 1, c.ML);
+        st.write_pos = (st.write_pos + 1) % c.ML;
+    }
+    return q.issued;
+}
+
+// Every issued copy must land before the CTA's shared memory goes away: wait (bounded) for the
+// full barriers of the last kNBar segments issued (older ones were consumed or waited already).
+__device__ void producer_drain(Smem& sm, uint32_t issued) {
+    if ((threadIdx.x & 31) != 0) return;
+    const uint32_t first = issued > (uint32_t)kNBar ? issued - kNBar : 0u;
+    for (uint32_t i = first; i < issued; ++i) {
+        uint32_t spins = 0;
+        while (!mbar_try_wait(&sm.full[i % kNBar], (i / kNBar) & 1u) && ++spins < kSpinLimit) {
+        }
+    }
 }
 
 // ------------------------------------------------------------------------------ input vectors
@@ -483,48 +544,81 @@ __device__ __forceinline__ void quad_limbs(Smem& sm, int q, int NB, float4 v) {
     if (g == 0) sm.xs[b] = __uint_as_float((uint32_t)(127 + e - 27) << 23);
 }
 
-// Block sum in a fixed order with one __syncthreads; `rb` alternates the two scratch rows so
-// back-to-back reductions need no second barrier.
-__device__ __forceinline__ float block_sum(float v, Smem& sm, uint32_t& rb) {
+// Sum over the consumer threads in a fixed order; `rb` alternates the two scratch rows so
+// back-to-back sums need one barrier each.
+__device__ __forceinline__ float block_sum(float v, Smem& sm, uint32_t rb) {
     v = warp_sum(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) sm.red[rb][warp] = v;
-    __syncthreads();
+    csync();
     float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) s += sm.red[rb][w];
-    rb ^= 1u;
+    for (int w = 0; w < kCWarps; ++w) s += sm.red[rb][w];
     return s;
 }
 
-// The GEMV input of a phase: K floats from `src` (global, read through L2) or, when src is NULL,
-// from xf; RMSNorm with `alpha` when NORM (burn::nn::RmsNorm: (x / sqrt(mean(x^2) + 1e-8)) *
-// alpha); then the dp4a limbs.  QN = quads per thread; a thread's x and alpha loads are all in
-// flight together.
-template <int QN, bool NORM>
-__device__ __noinline__ void prep_vector_t(Smem& /*sm_param*/, const float* src, int K, const float* alpha, uint32_t& rb) {
-    Smem& sm = smem_ref();
-    const int nq = K >> 2, NB = K >> 5;
-    float4 v[QN], a[NORM ? QN : 1];
-#pragma unroll
-    for (int i = 0; i < QN; ++i) {
-        const int q = threadIdx.x + i * kThreads;
-        if (q < nq) {
-            v[i] = src ? __ldcg(reinterpret_cast<const float4*>(src) + q) : reinterpret_cast<const float4*>(sm.xf)[q];
-            if (NORM) a[i] = reinterpret_cast<const float4*>(alpha)[q];  // staged in shared memory
+__device__ __forceinline__ float emb_val(const Ctx& c, const uint8_t* table, uint32_t row, int j) {
+    const uint8_t* r = table + (int64_t)row * c.emb_row_bytes;
+    switch (c.emb_type) {
+        case EMB_BF16: return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(r)[j] << 16);
+        case EMB_F32: return reinterpret_cast<const float*>(r)[j];
+        case EMB_F16: return f16_to_f32_ieee(reinterpret_cast<const uint16_t*>(r)[j]);
+        default: {  // Q4_0 row, gguf.rs:616-633
+            const uint8_t* blk = r + (j >> 5) * 18;
+            const float d = f16_to_f32_gguf((uint16_t)(blk[0] | (blk[1] << 8)));
+            const int w = j & 31;
+            const uint32_t byte = blk[2 + (w & 15)];
+            return __fmul_rn(nib_m8(w < 16 ? (byte & 0xFu) : (byte >> 4)), d);
         }
     }
-    if (NORM) {
+}
+
+// The GEMV input of a phase, K floats, then RMSNorm with `alpha` (a ring segment) when alpha is
+// not NULL (burn::nn::RmsNorm: (x / sqrt(mean(x^2) + 1e-8)) * alpha), then the limbs.
+//   src == 0: the flagged buffer `ll` at epoch `ep`
+//   src == 1: the frame input x0 = audio sum (xa) + text row (model.rs:640-646); the CTA also
+//             keeps its own rows [own0, own1) in xown
+// QN = quads per thread.  Ends with a consumer barrier.  Returns false after an abort.
+template <int QN>
+__device__ __noinline__ bool prep_vector(const MegaArgs& P, const uint64_t* ll, uint32_t ep, int K,
+                                         const float* alpha, uint32_t rb, int src, const float* xa, uint32_t text,
+                                         int own0, int own1) {
+    Smem& sm = smem_ref();
+    const Ctx& c = P.c;
+    const int nq = K >> 2, NB = K >> 5;
+    float4 v[QN];
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < QN; ++i) {
+        const int q = threadIdx.x + i * kCThreads;
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q < nq) {
+            if (src == 0) {
+                uint64_t w[4];
+                ok = ll_wait<2>(P, ll + 4 * q, ep, w) && ok;
+                v[i] = make_float4(ll_val(w[0]), ll_val(w[1]), ll_val(w[2]), ll_val(w[3]));
+            } else {
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(xa) + q);
+                const int j = 4 * q;
+                v[i] = make_float4(__fadd_rn(a.x, emb_val(c, c.emb_text, text, j)),
+                                   __fadd_rn(a.y, emb_val(c, c.emb_text, text, j + 1)),
+                                   __fadd_rn(a.z, emb_val(c, c.emb_text, text, j + 2)),
+                                   __fadd_rn(a.w, emb_val(c, c.emb_text, text, j + 3)));
+                const float vv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t)
+                    if (j + t >= own0 && j + t < own1) sm.xown[j + t - own0] = vv[t];
+            }
+        }
+    }
+    if (alpha) {
         float ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < QN; ++i) {
-            const int q = threadIdx.x + i * kThreads;
-            if (q < nq) {
-                ss = __fmaf_rn(v[i].x, v[i].x, ss);
-                ss = __fmaf_rn(v[i].y, v[i].y, ss);
-                ss = __fmaf_rn(v[i].z, v[i].z, ss);
-                ss = __fmaf_rn(v[i].w, v[i].w, ss);
-            }
+            ss = __fmaf_rn(v[i].x, v[i].x, ss);
+            ss = __fmaf_rn(v[i].y, v[i].y, ss);
+            ss = __fmaf_rn(v[i].z, v[i].z, ss);
+            ss = __fmaf_rn(v[i].w, v[i].w, ss);
         }
         ss = block_sum(ss, sm, rb);
         // x * (1 / rms) instead of x / rms: within 1.5 ulp, below the 24-bit fixed-point step of
@@ -532,30 +626,31 @@ __device__ __noinline__ void prep_vector_t(Smem& /*sm_param*/, const float* src,
         const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-8f)));
 #pragma unroll
         for (int i = 0; i < QN; ++i) {
-            v[i].x = __fmul_rn(__fmul_rn(v[i].x, inv), a[NORM ? i : 0].x);
-            v[i].y = __fmul_rn(__fmul_rn(v[i].y, inv), a[NORM ? i : 0].y);
-            v[i].z = __fmul_rn(__fmul_rn(v[i].z, inv), a[NORM ? i : 0].z);
-            v[i].w = __fmul_rn(__fmul_rn(v[i].w, inv), a[NORM ? i : 0].w);
+            const int q = threadIdx.x + i * kCThreads;
+            if (q < nq) {
+                const float4 a = reinterpret_cast<const float4*>(alpha)[q];
+                v[i].x = __fmul_rn(__fmul_rn(v[i].x, inv), a.x);
+                v[i].y = __fmul_rn(__fmul_rn(v[i].y, inv), a.y);
+                v[i].z = __fmul_rn(__fmul_rn(v[i].z, inv), a.z);
+                v[i].w = __fmul_rn(__fmul_rn(v[i].w, inv), a.w);
+            }
         }
     }
 #pragma unroll
     for (int i = 0; i < QN; ++i) {
-        const int q = threadIdx.x + i * kThreads;
+        const int q = threadIdx.x + i * kCThreads;
         if (q < nq) quad_limbs(sm, q, NB, v[i]);  // nq is a multiple of 32: whole warps
     }
-    __syncthreads();
+    csync();
+    return ok;
 }
 
-__device__ __forceinline__ void prep_vector(Smem& sm, const float* src, int K, const float* alpha, uint32_t& rb) {
-    const int qn = (K / 4 + kThreads - 1) / kThreads;
-    if (alpha) {
-        if (qn <= 1) prep_vector_t<1, true>(sm, src, K, alpha, rb);
-        else prep_vector_t<2, true>(sm, src, K, alpha, rb);  // D <= 4096
-    } else {
-        if (qn <= 1) prep_vector_t<1, false>(sm, src, K, alpha, rb);
-        else if (qn <= 2) prep_vector_t<2, false>(sm, src, K, alpha, rb);
-        else prep_vector_t<kQMax, false>(sm, src, K, alpha, rb);
-    }
+__device__ __forceinline__ bool prep_any(const MegaArgs& P, const uint64_t* ll, uint32_t ep, int K, const float* alpha,
+                                         uint32_t rb, int src, const float* xa, uint32_t text, int own0, int own1) {
+    const int qn = (K / 4 + kCThreads - 1) / kCThreads;
+    if (qn <= 2) return prep_vector<2>(P, ll, ep, K, alpha, rb, src, xa, text, own0, own1);
+    if (qn <= 3) return prep_vector<3>(P, ll, ep, K, alpha, rb, src, xa, text, own0, own1);
+    return prep_vector<5>(P, ll, ep, K, alpha, rb, src, xa, text, own0, own1);
 }
 
 // ------------------------------------------------------------------------------ GEMV
@@ -582,45 +677,52 @@ __device__ __forceinline__ float block_dp4a(const uint4 q, const uint4* L) {
     return __fmaf_rn(i2f(s2), 65536.0f, __fmaf_rn(i2f(s1), 256.0f, i2f(s0)));
 }
 
-struct HeadBest {
-    float v;
-    int i;
-};
-
-// One GEMV phase over the rows staged in wbuf.  Units are row pairs (2u, 2u+1) or, for
-// linear_in, (gate row u, value row u + F); a warp takes one unit, its lanes split the blocks.
+// One GEMV phase: unit u of this CTA's rows goes to consumer warp u % 15, in segment order; a
+// warp waits for the segment of its unit, its lanes split the unit's blocks.  `seg0` is the
+// global index of the phase's first weight segment.  Returns false after an abort.
+//   EPI_QKV    RoPE on the q and k pairs, flagged qkv words, K/V ring write (model.rs:426-449)
+//   EPI_RESID  x rows += result (kept in xown), flagged x words               (model.rs:565, 570)
+//   EPI_GATE   silu(gate) * value, flagged hidden words                       (model.rs:517-524)
+//   EPI_LOGITS logits, this warp's best (value, lowest index) in wv / wi
 template <int EPI>
-__device__ __noinline__ void gemv_phase(const MegaArgs& P, Smem& /*sm_param*/, const Rows& r, int layer,
-                                        const StreamState& st, HeadBest* best, int frame) {
+__device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0, uint64_t* outb, uint32_t ep, int frame) {
     Smem& sm = smem_ref();
     const Ctx& c = P.c;
-    if (r.nr == 0 || r.n[0] <= 0) return;
-    const Staged s = staged_layout(r, false, c.D);
-    const int NB = r.W->k >> 5;
-    const int units = EPI == EPI_GATE ? r.n[0] : (r.n[0] + 1) / 2;
+    const Range r = sm.rg[kind_of(p, c.L)];
+    const Q4Dev* W = matrix_of(sm, c, p);
+    const int NB = W->k >> 5;
+    const bool gate = EPI == EPI_GATE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint4* nibs = reinterpret_cast<const uint4*>(sm.wbuf);
-    const uint16_t* scs = reinterpret_cast<const uint16_t*>(sm.wbuf);
-    for (int u = warp; u < units; u += kWarps) {
-        int ra, rb;  // global rows (rb < 0: unit has one row)
-        uint32_t na, nb, sa, sb;  // wbuf offsets in uint4 / uint16 units
-        if (EPI == EPI_GATE) {
-            ra = r.r0[0] + u;
-            rb = r.r0[1] + u;
-            na = s.nib[0] / 16 + (uint32_t)u * NB;
-            nb = s.nib[1] / 16 + (uint32_t)u * NB;
-            sa = s.sc[0] / 2 + (uint32_t)u * NB;
-            sb = s.sc[1] / 2 + (uint32_t)u * NB;
+    const uint4* nibs = reinterpret_cast<const uint4*>(sm.ring);
+    const uint16_t* scs = reinterpret_cast<const uint16_t*>(sm.ring);
+    float best_v = -FLT_MAX;
+    int best_i = 0x7FFFFFFF;
+    bool ok = true;
+    for (int u = warp; u < r.units; u += kCWarps) {
+        const int k = u / r.ups;
+        ok = wait_seg(sm, P, seg0 + (uint32_t)k) && ok;
+        const WSeg g = wseg(r, gate, k, NB);
+        const uint32_t base = sm.seg_off[(seg0 + (uint32_t)k) % kNBar];
+        const int lu = u - g.ua;
+        int ra, rb;
+        uint32_t na, nb, sa, sb;  // ring offsets in uint4 / uint16 units
+        if (gate) {
+            ra = r.r0 + u;
+            rb = c.F + r.r0 + u;
+            na = (base + (uint32_t)lu * NB * 16u) / 16u;
+            nb = (base + (uint32_t)(g.nu + lu) * NB * 16u) / 16u;
+            sa = (base + g.sc_base + (uint32_t)lu * NB * 2u) / 2u;
+            sb = (base + g.sc_base + (uint32_t)(g.nu + lu) * NB * 2u) / 2u;
         } else {
-            const int la = 2 * u;
-            const bool two = 2 * u + 1 < r.n[0];
+            const int la = 2 * lu;
+            const bool two = la + 1 < g.nr;
             const int lb = two ? la + 1 : la;
-            ra = r.r0[0] + la;
-            rb = two ? r.r0[0] + lb : -1;
-            na = s.nib[0] / 16 + (uint32_t)la * NB;
-            nb = s.nib[0] / 16 + (uint32_t)lb * NB;
-            sa = s.sc[0] / 2 + (uint32_t)la * NB;
-            sb = s.sc[0] / 2 + (uint32_t)lb * NB;
+            ra = r.r0 + 2 * u;
+            rb = two ? ra + 1 : -1;
+            na = (base + (uint32_t)la * NB * 16u) / 16u;
+            nb = (base + (uint32_t)lb * NB * 16u) / 16u;
+            sa = (base + g.sc_base + (uint32_t)la * NB * 2u) / 2u;
+            sb = (base + g.sc_base + (uint32_t)lb * NB * 2u) / 2u;
         }
         float acc_a = 0.0f, acc_b = 0.0f;
         for (int b = lane; b < NB; b += 32) {
@@ -636,51 +738,53 @@ __device__ __noinline__ void gemv_phase(const MegaArgs& P, Smem& /*sm_param*/, c
         }
         float va = warp_sum(acc_a), vb = warp_sum(acc_b);
         if (lane != 0) continue;
-        if (EPI == EPI_RESID) {  // rows of this CTA: the residual lives in xown
-            const int o = ra - r.r0[0];
+        if (EPI == EPI_RESID) {
+            const int o = ra - r.r0;
             const float xa_ = __fadd_rn(va, sm.xown[o]);
             sm.xown[o] = xa_;
-            c.x[ra] = xa_;
+            ll_store(outb + ra, xa_, ep);
             if (rb >= 0) {
                 const float xb_ = __fadd_rn(vb, sm.xown[o + 1]);
                 sm.xown[o + 1] = xb_;
-                c.x[rb] = xb_;
+                ll_store(outb + rb, xb_, ep);
             }
         } else if (EPI == EPI_GATE) {
+            // silu(x) = x * (1 / (1 + exp(-x)))
             const float sg = __fmul_rn(va, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-va))));
-            c.hid[ra] = __fmul_rn(sg, vb);
+            ll_store(outb + ra, __fmul_rn(sg, vb), ep);
         } else if (EPI == EPI_LOGITS) {
             c.logits[ra] = va;
             if (c.desc->logits) c.desc->logits[(int64_t)frame * c.V + ra] = va;
-            if (va > best->v || (va == best->v && ra < best->i)) {
-                best->v = va;
-                best->i = ra;
+            if (va > best_v || (va == best_v && ra < best_i)) {
+                best_v = va;
+                best_i = ra;
             }
             if (rb >= 0) {
                 c.logits[rb] = vb;
                 if (c.desc->logits) c.desc->logits[(int64_t)frame * c.V + rb] = vb;
-                if (vb > best->v || (vb == best->v && rb < best->i)) {
-                    best->v = vb;
-                    best->i = rb;
+                if (vb > best_v || (vb == best_v && rb < best_i)) {
+                    best_v = vb;
+                    best_i = rb;
                 }
             }
-        } else {  // EPI_QKV: RoPE on q and k pairs, K/V ring write (row pairs are always complete)
+        } else {  // EPI_QKV (row pairs are always complete: 3D is even)
             const int D = c.D, HD = c.HD;
             const int part = ra / D;
             const int within = ra - part * D;
             const int h = within / HD, d = within - h * HD;
             if (part < 2) {
+                // RoPE::apply_rotation (model.rs:114-116) on the pair (2i, 2i+1)
                 const float2 cs = sm.rope[d >> 1];
                 const float re = __fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y));
                 const float im = __fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x));
                 va = re;
                 vb = im;
             }
-            c.qkv[ra] = va;
-            c.qkv[ra + 1] = vb;
+            ll_store(outb + ra, va, ep);
+            ll_store(outb + ra + 1, vb, ep);
             if (part >= 1) {
-                const int64_t off = (int64_t)c.ids[0] * c.kv_stream_stride + (int64_t)layer * c.kv_layer_stride +
-                                    (part == 2 ? c.kv_half_stride : 0) + ((int64_t)h * c.ML + st.write_pos) * HD + d;
+                const int64_t off = (int64_t)c.ids[0] * c.kv_stream_stride + (int64_t)(p / 5) * c.kv_layer_stride +
+                                    (part == 2 ? c.kv_half_stride : 0) + ((int64_t)h * c.ML + sm.st.write_pos) * HD + d;
                 if (c.kv_f32) {
                     float* kv = reinterpret_cast<float*>(c.kv) + off;
                     kv[0] = va;
@@ -692,52 +796,89 @@ __device__ __noinline__ void gemv_phase(const MegaArgs& P, Smem& /*sm_param*/, c
             }
         }
     }
+    if (EPI == EPI_LOGITS && lane == 0) {
+        sm.wv[warp] = best_v;
+        sm.wi[warp] = best_i;
+    }
+    return ok;
 }
 
 // ------------------------------------------------------------------------------ attention
 
-constexpr int kKeysPerBatch = 4;  // keys a warp loads before computing
-
-template <typename KT>
-__device__ __forceinline__ void load_kv(const KT* kp, const KT* vp, int lane, float4& k, float4& v) {
-    if (sizeof(KT) == 4) {
-        k = __ldcg(reinterpret_cast<const float4*>(kp) + lane);
-        v = __ldcg(reinterpret_cast<const float4*>(vp) + lane);
-    } else {
-        const uint2 kr = __ldcg(reinterpret_cast<const uint2*>(kp) + lane);
-        const uint2 vr = __ldcg(reinterpret_cast<const uint2*>(vp) + lane);
-        k = make_float4(__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xFFFF0000u), __uint_as_float(kr.y << 16),
-                        __uint_as_float(kr.y & 0xFFFF0000u));
-        v = make_float4(__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xFFFF0000u), __uint_as_float(vr.y << 16),
-                        __uint_as_float(vr.y & 0xFFFF0000u));
+// Online-softmax state of a set of keys: max score, sum of exp, sum of exp * v (4 dims a lane).
+struct SoftAcc {
+    float m, l;
+    float4 o;
+};
+__device__ __forceinline__ void soft_merge(SoftAcc& a, float m, float l, float4 o) {
+    if (l == 0.0f) return;
+    if (a.l == 0.0f) {
+        a.m = m;
+        a.l = l;
+        a.o = o;
+        return;
     }
+    const float M = fmaxf(a.m, m);
+    const float fa = expf(a.m - M), fb = expf(m - M);
+    a.l = __fmaf_rn(a.l, fa, __fmul_rn(l, fb));
+    a.o.x = __fmaf_rn(a.o.x, fa, __fmul_rn(o.x, fb));
+    a.o.y = __fmaf_rn(a.o.y, fa, __fmul_rn(o.y, fb));
+    a.o.z = __fmaf_rn(a.o.z, fa, __fmul_rn(o.z, fb));
+    a.o.w = __fmaf_rn(a.o.w, fa, __fmul_rn(o.w, fb));
+    a.m = M;
 }
 
-// Split-KV attention of head h over ring slots [j0, j1) of this CTA, from the staged K/V (the
-// slot written this frame, write_pos, comes from qkv).  Writes the partial (max, sum exp,
-// sum exp * v); the out_proj prologue of every CTA combines the partials of all splits.
+// Merges the 15 per-warp states through shared memory in warp order; the result is valid in
+// warp 0.  Two consumer barriers.
+__device__ __forceinline__ SoftAcc merge_warps(Smem& sm, const SoftAcc& mine) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float4* wo = reinterpret_cast<float4*>(sm.limbs);
+    float* wm = reinterpret_cast<float*>(wo + kCWarps * 32);
+    float* wl = wm + kCWarps;
+    if (lane == 0) {
+        wm[warp] = mine.m;
+        wl[warp] = mine.l;
+    }
+    wo[warp * 32 + lane] = mine.o;
+    csync();
+    SoftAcc a{-FLT_MAX, 0.0f, make_float4(0.f, 0.f, 0.f, 0.f)};
+    if (warp == 0)
+        for (int w = 0; w < kCWarps; ++w) soft_merge(a, wm[w], wl[w], wo[w * 32 + lane]);
+    csync();  // the scratch may be rewritten after this
+    return a;
+}
+
+// Split-KV attention of head h over ring slots [j0, j1) (model.rs:450-472): the K/V slots come
+// from the ring segment `seg`, the slot of this frame (write_pos) from the flagged qkv words.
+// Split 0 of each head then merges the partials of all splits (split order, then warp order)
+// into softmax(q.k^T * scale).v and publishes it.  Returns false after an abort.
 template <typename KT>
-__device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& /*sm_param*/, int layer, const StreamState& st,
-                                             int cta, int ncta) {
+__device__ __noinline__ bool attention_phase(const MegaArgs& P, int layer, uint32_t seg, uint32_t ep, int cta) {
     Smem& sm = smem_ref();
     const Ctx& c = P.c;
-    const int len = min(st.len + 1, c.ML);
-    const Split sp = split_of(P, cta, len);
-    if (sp.h >= c.H) return;
+    const int len = min(sm.st.len + 1, c.ML);
+    const int wpos = sm.st.write_pos;
+    const Split sp = split_of(cta, P.nsplit, c.H, len);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int HD = c.HD, h = sp.h;
-    const float4 q = __ldcg(reinterpret_cast<const float4*>(c.qkv + h * HD) + lane);
-    const float4 kcur = __ldcg(reinterpret_cast<const float4*>(c.qkv + c.D + h * HD) + lane);
-    const float4 vcur = __ldcg(reinterpret_cast<const float4*>(c.qkv + 2 * c.D + h * HD) + lane);
-    const uint32_t koff = kv_offset(sm, c, layer, cta, ncta);
-    const uint32_t kvb = (uint32_t)(sp.j1 - sp.j0) * HD * sizeof(KT);
-    const KT* ks = reinterpret_cast<const KT*>(sm.wbuf + koff);
-    const KT* vs = reinterpret_cast<const KT*>(sm.wbuf + koff + kvb);
-    float m = -FLT_MAX, l = 0.0f;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = sp.j0 + warp; j < sp.j1; j += kWarps) {
+    const int HD = c.HD, h = sp.h, par = layer & 1;
+    bool ok = wait_seg(sm, P, seg);
+    uint64_t w[4];
+    const uint64_t* qb = P.qkvb[par];
+    ok = ll_wait<2>(P, qb + h * HD + 4 * lane, ep - 1u, w) && ok;
+    const float4 q = make_float4(ll_val(w[0]), ll_val(w[1]), ll_val(w[2]), ll_val(w[3]));
+    ok = ll_wait<2>(P, qb + c.D + h * HD + 4 * lane, ep - 1u, w) && ok;
+    const float4 kcur = make_float4(ll_val(w[0]), ll_val(w[1]), ll_val(w[2]), ll_val(w[3]));
+    ok = ll_wait<2>(P, qb + 2 * c.D + h * HD + 4 * lane, ep - 1u, w) && ok;
+    const float4 vcur = make_float4(ll_val(w[0]), ll_val(w[1]), ll_val(w[2]), ll_val(w[3]));
+    trace_mark(P, 21);
+    const uint32_t base = sm.seg_off[seg % kNBar];
+    const int n = sp.j1 - sp.j0;
+    const KT* ks = reinterpret_cast<const KT*>(sm.ring + base);
+    const KT* vs = reinterpret_cast<const KT*>(sm.ring + base + (uint32_t)n * HD * sizeof(KT));
+    SoftAcc acc{-FLT_MAX, 0.0f, make_float4(0.f, 0.f, 0.f, 0.f)};
+    for (int j = sp.j0 + warp; j < sp.j1; j += kCWarps) {
         float4 k, v;
-        if (j == st.write_pos) {
+        if (j == wpos) {
             // this frame's K/V (the ring copy stores them rounded to the ring type)
             if (sizeof(KT) == 4) {
                 k = kcur;
@@ -749,13 +890,13 @@ __device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& /*sm_param
                                 __bfloat162float(__float2bfloat16_rn(vcur.z)), __bfloat162float(__float2bfloat16_rn(vcur.w)));
             }
         } else {
-            const int r = j - sp.j0;
+            const int rr = j - sp.j0;
             if (sizeof(KT) == 4) {
-                k = reinterpret_cast<const float4*>(ks + (int64_t)r * HD)[lane];
-                v = reinterpret_cast<const float4*>(vs + (int64_t)r * HD)[lane];
+                k = reinterpret_cast<const float4*>(ks + (int64_t)rr * HD)[lane];
+                v = reinterpret_cast<const float4*>(vs + (int64_t)rr * HD)[lane];
             } else {
-                const uint2 kr = reinterpret_cast<const uint2*>(ks + (int64_t)r * HD)[lane];
-                const uint2 vr = reinterpret_cast<const uint2*>(vs + (int64_t)r * HD)[lane];
+                const uint2 kr = reinterpret_cast<const uint2*>(ks + (int64_t)rr * HD)[lane];
+                const uint2 vr = reinterpret_cast<const uint2*>(vs + (int64_t)rr * HD)[lane];
                 k = make_float4(__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xFFFF0000u),
                                 __uint_as_float(kr.y << 16), __uint_as_float(kr.y & 0xFFFF0000u));
                 v = make_float4(__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xFFFF0000u),
@@ -768,148 +909,302 @@ __device__ __noinline__ void attention_phase(const MegaArgs& P, Smem& /*sm_param
         dot = __fmaf_rn(q.w, k.w, dot);
         dot = warp_sum(dot);
         const float score = __fmul_rn(dot, c.attn_scale);
-        const float mn = fmaxf(m, score);
-        const float corr = expf(m - mn);
-        const float p = expf(score - mn);
-        l = __fmaf_rn(l, corr, p);
-        o.x = __fmaf_rn(o.x, corr, __fmul_rn(p, v.x));
-        o.y = __fmaf_rn(o.y, corr, __fmul_rn(p, v.y));
-        o.z = __fmaf_rn(o.z, corr, __fmul_rn(p, v.z));
-        o.w = __fmaf_rn(o.w, corr, __fmul_rn(p, v.w));
-        m = mn;
+        const float mn = fmaxf(acc.m, score);
+        const float corr = expf(acc.m - mn);
+        const float pr = expf(score - mn);
+        acc.l = __fmaf_rn(acc.l, corr, pr);
+        acc.o.x = __fmaf_rn(acc.o.x, corr, __fmul_rn(pr, v.x));
+        acc.o.y = __fmaf_rn(acc.o.y, corr, __fmul_rn(pr, v.y));
+        acc.o.z = __fmaf_rn(acc.o.z, corr, __fmul_rn(pr, v.z));
+        acc.o.w = __fmaf_rn(acc.o.w, corr, __fmul_rn(pr, v.w));
+        acc.m = mn;
     }
-    // combine the warps in warp order through shared memory (xf as scratch)
-    float* wm = sm.xf;
-    float* wl = sm.xf + kWarps;
-    float4* wo = reinterpret_cast<float4*>(sm.xf + 2 * kWarps);
-    if (lane == 0) {
-        wm[warp] = m;
-        wl[warp] = l;
+    const SoftAcc mine = merge_warps(sm, acc);
+    trace_mark(P, 22);
+    uint64_t* pb = P.partb[par] + (int64_t)h * P.nsplit * kPartPairs;
+    if (sp.s != 0) {
+        if (warp == 0) {
+            uint64_t* d = pb + (int64_t)sp.s * kPartPairs;
+            if (lane == 0) {
+                ll_store(d, mine.m, ep);
+                ll_store(d + 1, mine.l, ep);
+            }
+            ll_store(d + 4 + 4 * lane, mine.o.x, ep);
+            ll_store(d + 5 + 4 * lane, mine.o.y, ep);
+            ll_store(d + 6 + 4 * lane, mine.o.z, ep);
+            ll_store(d + 7 + 4 * lane, mine.o.w, ep);
+        }
+        return ok;
     }
-    wo[warp * 32 + lane] = o;
-    __syncthreads();
+    // split 0: warp w merges splits w, w + 15, ...; warp 0 starts from its own partial (split 0)
+    SoftAcc a{-FLT_MAX, 0.0f, make_float4(0.f, 0.f, 0.f, 0.f)};
+    if (warp == 0) a = mine;
+    for (int s = warp == 0 ? kCWarps : warp; s < P.nsplit; s += kCWarps) {
+        const uint64_t* d = pb + (int64_t)s * kPartPairs;
+        uint64_t ml[2], ov[4];
+        ok = ll_wait<1>(P, d, ep, ml) && ok;
+        ok = ll_wait<2>(P, d + 4 + 4 * lane, ep, ov) && ok;
+        soft_merge(a, ll_val(ml[0]), ll_val(ml[1]),
+                   make_float4(ll_val(ov[0]), ll_val(ov[1]), ll_val(ov[2]), ll_val(ov[3])));
+    }
+    const SoftAcc all = merge_warps(sm, a);
+    trace_mark(P, 24);
     if (warp == 0) {
-        float M = -FLT_MAX;
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wm[w]);
-        float L = 0.0f;
-        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int w = 0; w < kWarps; ++w) {
-            if (wl[w] == 0.0f) continue;
-            const float f = expf(wm[w] - M);
-            L = __fmaf_rn(wl[w], f, L);
-            const float4 ow = wo[w * 32 + lane];
-            O.x = __fmaf_rn(ow.x, f, O.x);
-            O.y = __fmaf_rn(ow.y, f, O.y);
-            O.z = __fmaf_rn(ow.z, f, O.z);
-            O.w = __fmaf_rn(ow.w, f, O.w);
-        }
-        float* part = c.part + ((int64_t)h * P.nsplit + sp.s) * (HD + 4);
-        if (lane == 0) {
-            part[0] = M;
-            part[1] = L;
-        }
-        reinterpret_cast<float4*>(part + 4)[lane] = O;
+        uint64_t* d = P.attb[par] + h * HD + 4 * lane;
+        ll_store(d, __fdiv_rn(all.o.x, all.l), ep);
+        ll_store(d + 1, __fdiv_rn(all.o.y, all.l), ep);
+        ll_store(d + 2, __fdiv_rn(all.o.z, all.l), ep);
+        ll_store(d + 3, __fdiv_rn(all.o.w, all.l), ep);
     }
+    return ok;
 }
 
-// The out_proj input: every CTA combines, for each head, the partials of all its splits (in
-// split order) into softmax(q.k^T * scale).v, then builds the limbs.
-template <int NSMAX>
-__device__ __noinline__ void prep_attn(Smem& /*sm_param*/, const MegaArgs& P) {
+// ------------------------------------------------------------------------------ consumers
+
+__device__ __forceinline__ void release_phase(Smem& sm, uint32_t first, int n) {
+    if (threadIdx.x == 0)
+        for (int i = 0; i < n; ++i) mbar_arrive(&sm.empty[(first + (uint32_t)i) % kNBar]);
+}
+
+// Makes an abort seen by any consumer thread CTA-uniform; returns false when the CTA must stop.
+// Agreement k uses slot k & 1, so a thread that is already writing agreement k + 1 can never
+// change what a slower thread reads for agreement k.
+__device__ __forceinline__ bool agree(Smem& sm, const MegaArgs& P, bool ok, uint32_t& k) {
+    const uint32_t s = k & 1u;
+    ++k;
+    if (!ok || (threadIdx.x == 0 && aborted(P))) sm.stop[s] = 1;
+    csync();
+    return sm.stop[s] == 0;
+}
+
+// A frame's last step: every CTA reduces the per-CTA (best logit, index) words identically
+// (lowest index on ties), applies the stream rule (stream.rs:90-107, 231-266) and advances the
+// state.  Returns false after an abort.
+__device__ __noinline__ bool argmax_phase(const MegaArgs& P, int f, uint32_t ep) {
     Smem& sm = smem_ref();
     const Ctx& c = P.c;
-    const int NS = P.nsplit, HD = c.HD, NB = c.D >> 5;
-    const int nq = c.D >> 2, qh = HD >> 2;
-    for (int q = threadIdx.x; q < nq; q += kThreads) {
-        const int h = q / qh, d4 = q - h * qh;
-        const float* pb = c.part + (int64_t)h * NS * (HD + 4);
-        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-        float L = 0.0f;
-        if (NS <= NSMAX) {
-            float2 ml[NSMAX];
-            float4 os[NSMAX];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t* ab = P.argb[f & 1];
+    bool ok = true;
+    float bv = -FLT_MAX;
+    int bi = 0x7FFFFFFF;
+    if ((int)threadIdx.x < (int)gridDim.x) {
+        uint64_t w[2];
+        ok = ll_wait<1>(P, ab + 2 * threadIdx.x, ep, w);
+        bv = ll_val(w[0]);
+        bi = (int)(uint32_t)w[1];
+    }
 #pragma unroll
-            for (int t = 0; t < NSMAX; ++t)
-                if (t < NS) {
-                    ml[t] = __ldcg(reinterpret_cast<const float2*>(pb + t * (HD + 4)));
-                    os[t] = __ldcg(reinterpret_cast<const float4*>(pb + t * (HD + 4) + 4) + d4);
-                }
-            float M = -FLT_MAX;
-#pragma unroll
-            for (int t = 0; t < NSMAX; ++t)
-                if (t < NS && ml[t].y != 0.0f) M = fmaxf(M, ml[t].x);
-#pragma unroll
-            for (int t = 0; t < NSMAX; ++t)
-                if (t < NS && ml[t].y != 0.0f) {
-                    const float f = expf(ml[t].x - M);
-                    L = __fmaf_rn(ml[t].y, f, L);
-                    O.x = __fmaf_rn(os[t].x, f, O.x);
-                    O.y = __fmaf_rn(os[t].y, f, O.y);
-                    O.z = __fmaf_rn(os[t].z, f, O.z);
-                    O.w = __fmaf_rn(os[t].w, f, O.w);
-                }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if (lane == 0) {
+        sm.av[warp] = bv;
+        sm.ai[warp] = bi;
+    }
+    csync();
+    bv = -FLT_MAX;
+    bi = 0x7FFFFFFF;
+    for (int w = 0; w < kCWarps; ++w)
+        if (sm.av[w] > bv || (sm.av[w] == bv && sm.ai[w] < bi)) {
+            bv = sm.av[w];
+            bi = sm.ai[w];
+        }
+    const uint32_t token = (uint32_t)(bi < 0 || bi >= c.V ? 0 : bi);
+    StreamState st = sm.st;
+    st.write_pos = (st.write_pos + 1) % c.ML;
+    st.offset += 1;
+    st.len = min(st.len + 1, c.ML);
+    int32_t out = (int32_t)token;
+    if (c.desc->mode == 1) {
+        st.frame_count += 1;
+        if (st.frame_count >= c.text_delay) {
+            st.last_text = token;
         } else {
-            float M = -FLT_MAX;
-            for (int t = 0; t < NS; ++t) {
-                const float2 ml = __ldcg(reinterpret_cast<const float2*>(pb + t * (HD + 4)));
-                if (ml.y != 0.0f) M = fmaxf(M, ml.x);
-            }
-            for (int t = 0; t < NS; ++t) {
-                const float2 ml = __ldcg(reinterpret_cast<const float2*>(pb + t * (HD + 4)));
-                if (ml.y == 0.0f) continue;
-                const float4 ot = __ldcg(reinterpret_cast<const float4*>(pb + t * (HD + 4) + 4) + d4);
-                const float f = expf(ml.x - M);
-                L = __fmaf_rn(ml.y, f, L);
-                O.x = __fmaf_rn(ot.x, f, O.x);
-                O.y = __fmaf_rn(ot.y, f, O.y);
-                O.z = __fmaf_rn(ot.z, f, O.z);
-                O.w = __fmaf_rn(ot.w, f, O.w);
-            }
-        }
-        const float4 a = make_float4(__fdiv_rn(O.x, L), __fdiv_rn(O.y, L), __fdiv_rn(O.z, L), __fdiv_rn(O.w, L));
-        quad_limbs(sm, q, NB, a);  // c.D / 4 is a multiple of 32: whole warps
-    }
-    __syncthreads();
-}
-
-// ------------------------------------------------------------------------------ embedding
-
-__device__ __forceinline__ float emb_val(const Ctx& c, const uint8_t* table, uint32_t row, int j) {
-    const uint8_t* r = table + (int64_t)row * c.emb_row_bytes;
-    switch (c.emb_type) {
-        case EMB_BF16: return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(r)[j] << 16);
-        case EMB_F32: return reinterpret_cast<const float*>(r)[j];
-        case EMB_F16: return f16_to_f32_ieee(reinterpret_cast<const uint16_t*>(r)[j]);
-        default: {
-            const uint8_t* blk = r + (j >> 5) * 18;
-            const float d = f16_to_f32_gguf((uint16_t)(blk[0] | (blk[1] << 8)));
-            const int w = j & 31;
-            const uint32_t byte = blk[2 + (w & 15)];
-            return __fmul_rn(nib_m8(w < 16 ? (byte & 0xFu) : (byte >> 4)), d);
+            const uint32_t p0 = st.prev0, p1 = st.prev1;
+            st.prev0 = p1;
+            st.prev1 = token;
+            st.last_text = (token != c.pad_id && token != 0u && token == p0 && token != p1) ? c.pad_id : token;
+            out = -1;
         }
     }
+    csync();  // every thread has read sm.st and sm.av
+    if (threadIdx.x == 0) {
+        sm.st = st;
+        if (blockIdx.x == 0) {
+            c.desc->tokens[f] = out;
+            c.state[c.ids[0]] = st;
+            if (f + 1 == P.steps) c.desc->step = P.steps;
+        }
+    }
+    return ok;
 }
 
-// ------------------------------------------------------------------------------ kernel
-
-struct Look {
-    int next;  // next global phase to L2-prefetch
-    int end;   // one past the last global phase of the launch
-};
-
-// Warp 0, after staging global phase `staged`: L2-prefetch later phases until pf_budget bytes
-// are requested beyond it.  Every lane keeps the same Look state.
-__device__ void look_ahead(const Smem& sm, const MegaArgs& P, Look& lk, int staged, int per_frame, int cta, int ncta,
-                           int len) {
-    const int lane = threadIdx.x & 31;
-    if (lk.next <= staged) lk.next = staged + 1;
-    uint32_t ahead = 0;
-    for (int g = staged + 1; g < lk.next; ++g) ahead += phase_bytes(sm, P, g % per_frame, cta, ncta, len);
-    while (lk.next < lk.end && ahead < P.pf_budget) {
-        const int p = lk.next % per_frame;
-        prefetch_phase(sm, P, p, cta, ncta, len, lane);
-        ahead += phase_bytes(sm, P, p, cta, ncta, len);
-        ++lk.next;
+__device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
+    Smem& sm = smem_ref();
+    const Ctx& c = P.c;
+    const int ph = 5 * c.L;  // the head's step
+    const uint32_t ebase = *P.base;
+    const int own0 = sm.rg[K_OUT].r0, own1 = sm.rg[K_OUT].r0 + sm.rg[K_OUT].n;
+    uint32_t seg = 0;  // global index of the next segment to consume
+    uint32_t rb = 0;
+    uint32_t agreements = 0;
+    for (int f = 0; f < P.steps; ++f) {
+        if (threadIdx.x == 0) {
+            if (sm.tron) trace_wall(P);  // end of the traced frame
+            sm.tron = P.trace != nullptr && cta == 0 && f == P.trace_frame;
+        }
+        trace_wall(P);
+        trace_mark(P, 1);
+        const uint32_t E = ebase + (uint32_t)f * kEpochsPerFrame + 1u;  // epoch of step 0
+        if (threadIdx.x == 0) {
+            uint32_t text = c.desc->text ? __ldcg(c.desc->text + f) : sm.st.last_text;
+            if (text >= (uint32_t)c.TV) {
+                raise_error(c.desc, -1);
+                text = 0;
+            }
+            sm.text = text;
+        }
+        if (threadIdx.x < (c.HD >> 1))
+            sm.rope[threadIdx.x] = c.rope[(int64_t)sm.st.offset * (c.HD >> 1) + threadIdx.x];
+        csync();
+        bool ok = true;
+        for (int l = 0; l < c.L && ok; ++l) {
+            const int p0 = 5 * l, par = l & 1;
+            // ---- QKV
+            {
+                const int n = phase_segs(sm, P, p0, cta);
+                if (n > 0) {
+                    ok = wait_seg(sm, P, seg) && ok;
+                    const float* alpha = reinterpret_cast<const float*>(sm.ring + sm.seg_off[seg % kNBar]);
+                    if (l == 0)
+                        ok = prep_any(P, nullptr, 0, c.D, alpha, rb, 1, P.xa + (int64_t)f * c.D, sm.text, own0, own1) && ok;
+                    else
+                        ok = prep_any(P, P.xb[par ^ 1][1], E + (uint32_t)(p0 - 1), c.D, alpha, rb, 0, nullptr, 0, 0, 0) && ok;
+                    rb ^= 1u;
+                    trace_mark(P, 11);
+                    ok = gemv_phase<EPI_QKV>(P, p0, seg + 1, P.qkvb[par], E + (uint32_t)p0, f) && ok;
+                    trace_mark(P, 12);
+                } else if (l == 0) {
+                    // no QKV rows here, but the residual still needs x0's own rows
+                    ok = prep_any(P, nullptr, 0, c.D, nullptr, rb, 1, P.xa + (int64_t)f * c.D, sm.text, own0, own1) && ok;
+                }
+                csync();
+                trace_mark(P, 13);
+                release_phase(sm, seg, n);
+                seg += (uint32_t)n;
+            }
+            // ---- attention
+            {
+                const int n = phase_segs(sm, P, p0 + K_ATT, cta);
+                if (n > 0) {
+                    if (c.kv_f32)
+                        ok = attention_phase<float>(P, l, seg, E + (uint32_t)(p0 + K_ATT), cta) && ok;
+                    else
+                        ok = attention_phase<__nv_bfloat16>(P, l, seg, E + (uint32_t)(p0 + K_ATT), cta) && ok;
+                }
+                csync();
+                trace_mark(P, 23);
+                release_phase(sm, seg, n);
+                seg += (uint32_t)n;
+            }
+            // ---- out_proj + residual
+            {
+                const int n = phase_segs(sm, P, p0 + K_OUT, cta);
+                if (n > 0) {
+                    ok = prep_any(P, P.attb[par], E + (uint32_t)(p0 + K_ATT), c.D, nullptr, rb, 0, nullptr, 0, 0, 0) && ok;
+                    trace_mark(P, 31);
+                    ok = gemv_phase<EPI_RESID>(P, p0 + K_OUT, seg, P.xb[par][0], E + (uint32_t)(p0 + K_OUT), f) && ok;
+                    trace_mark(P, 32);
+                }
+                csync();
+                trace_mark(P, 33);
+                release_phase(sm, seg, n);
+                seg += (uint32_t)n;
+            }
+            // ---- linear_in + silu gate
+            {
+                const int n = phase_segs(sm, P, p0 + K_IN, cta);
+                if (n > 0) {
+                    ok = wait_seg(sm, P, seg) && ok;
+                    const float* alpha = reinterpret_cast<const float*>(sm.ring + sm.seg_off[seg % kNBar]);
+                    ok = prep_any(P, P.xb[par][0], E + (uint32_t)(p0 + K_OUT), c.D, alpha, rb, 0, nullptr, 0, 0, 0) && ok;
+                    rb ^= 1u;
+                    trace_mark(P, 41);
+                    ok = gemv_phase<EPI_GATE>(P, p0 + K_IN, seg + 1, P.hidb[par], E + (uint32_t)(p0 + K_IN), f) && ok;
+                    trace_mark(P, 42);
+                }
+                csync();
+                trace_mark(P, 43);
+                release_phase(sm, seg, n);
+                seg += (uint32_t)n;
+            }
+            // ---- linear_out + residual
+            {
+                const int n = phase_segs(sm, P, p0 + K_DOWN, cta);
+                if (n > 0) {
+                    ok = prep_any(P, P.hidb[par], E + (uint32_t)(p0 + K_IN), c.F, nullptr, rb, 0, nullptr, 0, 0, 0) && ok;
+                    trace_mark(P, 51);
+                    ok = gemv_phase<EPI_RESID>(P, p0 + K_DOWN, seg, P.xb[par][1], E + (uint32_t)(p0 + K_DOWN), f) && ok;
+                    trace_mark(P, 52);
+                }
+                ok = agree(sm, P, ok, agreements);  // includes the phase-end barrier
+                trace_mark(P, 53);
+                release_phase(sm, seg, n);
+                seg += (uint32_t)n;
+            }
+        }
+        if (!ok) break;
+        // ---- head + this CTA's argmax partial
+        {
+            const int n = phase_segs(sm, P, ph, cta);
+            if (threadIdx.x < kCWarps) {
+                sm.wv[threadIdx.x] = -FLT_MAX;
+                sm.wi[threadIdx.x] = 0x7FFFFFFF;
+            }
+            csync();
+            if (n > 0) {
+                ok = wait_seg(sm, P, seg) && ok;
+                const float* alpha = reinterpret_cast<const float*>(sm.ring + sm.seg_off[seg % kNBar]);
+                ok = prep_any(P, P.xb[(c.L - 1) & 1][1], E + (uint32_t)(ph - 1), c.D, alpha, rb, 0, nullptr, 0, 0, 0) && ok;
+                rb ^= 1u;
+                trace_mark(P, 61);
+                ok = gemv_phase<EPI_LOGITS>(P, ph, seg + 1, nullptr, 0, f) && ok;
+                trace_mark(P, 62);
+            }
+            csync();
+            if (threadIdx.x == 0) {
+                float bv = -FLT_MAX;
+                int bi = 0x7FFFFFFF;
+                for (int w = 0; w < kCWarps; ++w)
+                    if (sm.wv[w] > bv || (sm.wv[w] == bv && sm.wi[w] < bi)) {
+                        bv = sm.wv[w];
+                        bi = sm.wi[w];
+                    }
+                uint64_t* d = P.argb[f & 1] + 2 * cta;
+                ll_store(d, bv, E + (uint32_t)ph);
+                ll_store(d + 1, __int_as_float(bi), E + (uint32_t)ph);
+            }
+            trace_mark(P, 63);
+            release_phase(sm, seg, n);
+            seg += (uint32_t)n;
+        }
+        ok = argmax_phase(P, f, E + (uint32_t)ph) && ok;
+        trace_mark(P, 7);
+        // this CTA's K/V writes of the frame are done: publish them to the producers
+        ok = agree(sm, P, ok, agreements);
+        if (threadIdx.x == 0) red_release_add(P.bar, 1u);
+        if (!ok) break;
+    }
+    if (threadIdx.x == 0) {
+        if (sm.tron) trace_wall(P);
+        // epochs of the next launch start after every epoch this one could have used
+        if (cta == 0) *P.base = ebase + (uint32_t)P.steps * kEpochsPerFrame;
     }
 }
 
@@ -917,206 +1212,46 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
     Smem& sm = smem_ref();
     const Ctx& c = P.c;
     const int cta = blockIdx.x, ncta = gridDim.x;
-    const int per_frame = 5 * c.L + 1;
-    uint32_t epoch = 0, parity = 0, rb = 0;
-    Tracer tr;
-    Look lk{0, per_frame * P.steps};
-    // rows of x this CTA owns: the out_proj / linear_out row range
-    const int own0 = (int)(2 * split_lo(c.D / 2, cta, ncta));
-    const int own1 = (int)(2 * split_lo(c.D / 2, cta + 1, ncta));
-
     for (int i = threadIdx.x; i < c.L; i += kThreads) sm.layers[i] = c.layers[i];
     if (threadIdx.x == 0) {
-        mbar_init(&sm.mbar, 1);
-        sm.staged = sm.waited = 0;
+        for (int i = 0; i < kNBar; ++i) {
+            mbar_init(&sm.full[i], 1);
+            mbar_init(&sm.empty[i], 1);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        sm.st = c.state[c.ids[0]];
+        sm.stop[0] = sm.stop[1] = 0;
+        sm.tslot = 0;
+        sm.tron = 0;
+        // row ranges of this CTA (the same for every layer)
+        auto pairs = [&](int rows, uint32_t row_bytes) {
+            Range r;
+            const int64_t U = (rows + 1) / 2;
+            r.r0 = (int)(2 * split_lo(U, cta, ncta));
+            r.n = max(0, (int)min((int64_t)rows, 2 * split_lo(U, cta + 1, ncta)) - r.r0);
+            r.units = (r.n + 1) / 2;
+            r.ups = max(1, (int)(kSegMax / (2u * row_bytes)));
+            return r;
+        };
+        const uint32_t rowD = (uint32_t)(c.D / 32) * 18u, rowF = (uint32_t)(c.F / 32) * 18u;
+        sm.rg[K_QKV] = pairs(3 * c.D, rowD);
+        sm.rg[K_ATT] = Range{0, 0, 0, 1};
+        sm.rg[K_OUT] = pairs(c.D, rowD);
+        sm.rg[K_DOWN] = pairs(c.D, rowF);
+        sm.rg[K_HEAD] = pairs(c.V, rowD);
+        Range g;
+        g.r0 = (int)split_lo(c.F, cta, ncta);
+        g.n = (int)split_lo(c.F, cta + 1, ncta) - g.r0;
+        g.units = g.n;
+        g.ups = max(1, (int)(kSegMax / (2u * rowD)));
+        sm.rg[K_IN] = g;
     }
     __syncthreads();
-    const int sid = c.ids[0];
-    StreamState st = c.state[sid];
-    StepDesc* desc = c.desc;
-    if (threadIdx.x == 0) stage_phase(sm, c, 0, cta, ncta);
-    if (threadIdx.x < 32) look_ahead(sm, P, lk, 0, per_frame, cta, ncta, min(st.len + 1, c.ML));
-
-    for (int f = 0; f < P.steps; ++f) {
-        if (tr.on) tr.wall(P);  // end of the traced frame
-        tr.on = P.trace != nullptr && cta == 0 && f == P.trace_frame;
-        tr.wall(P);
-        tr.mark(P, 1);
-        {
-            const int len_now = min(st.len + 1, c.ML);
-            uint32_t text = desc->text ? __ldcg(desc->text + f) : st.last_text;
-            if (text >= (uint32_t)c.TV) {
-                raise_error(desc, -1);
-                text = 0;
-            }
-            // x = audio sum + text row (model.rs:640-646): built whole by every CTA; the CTA keeps
-            // its own rows in xown and publishes them
-            const float* xa = P.xa + (int64_t)f * c.D;
-            for (int j = threadIdx.x; j < c.D; j += kThreads) {
-                const float v = __fadd_rn(__ldcg(xa + j), emb_val(c, c.emb_text, text, j));
-                sm.xf[j] = v;
-                if (j >= own0 && j < own1) {
-                    sm.xown[j - own0] = v;
-                    c.x[j] = v;
-                }
-            }
-            if (threadIdx.x < (c.HD >> 1)) sm.rope[threadIdx.x] = c.rope[(int64_t)st.offset * (c.HD >> 1) + threadIdx.x];
-            __syncthreads();
-            for (int l = 0; l < c.L; ++l) {
-                const int p0 = 5 * l, gp0 = f * per_frame + p0;
-                // ---- QKV: weights and norm1 were staged before the previous barrier
-                if (!wait_stage(sm, P, parity)) goto drain;
-                tr.mark(P, 11);
-                {
-                    const Rows r = rows_of(sm, c, p0 + K_QKV, cta, ncta);
-                    const Staged sg = staged_layout(r, true, c.D);
-                    prep_vector(sm, l == 0 ? nullptr : c.x, c.D, reinterpret_cast<const float*>(sm.wbuf + sg.alpha), rb);
-                    tr.mark(P, 10);
-                    gemv_phase<EPI_QKV>(P, sm, r, l, st, nullptr, f);
-                }
-                __syncthreads();
-                tr.mark(P, 12);
-                if (threadIdx.x == 0) stage_out_kv(sm, P, l, cta, ncta, len_now);
-                tr.mark(P, 70);
-                if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_OUT, per_frame, cta, ncta, len_now);
-                tr.mark(P, 71);
-                if (!grid_sync(P, epoch, sm, tr)) goto drain;
-                // ---- attention over the staged K/V slots (staged together with out_proj's rows)
-                if (!wait_stage(sm, P, parity)) goto drain;
-                tr.mark(P, 21);
-                if (c.kv_f32) attention_phase<float>(P, sm, l, st, cta, ncta);
-                else attention_phase<__nv_bfloat16>(P, sm, l, st, cta, ncta);
-                __syncthreads();
-                tr.mark(P, 22);
-                if (!grid_sync(P, epoch, sm, tr)) goto drain;
-                // ---- out_proj + residual (input: the combined attention partials)
-                if (P.nsplit <= 10) prep_attn<10>(sm, P);
-                else prep_attn<1>(sm, P);
-                tr.mark(P, 30);
-                gemv_phase<EPI_RESID>(P, sm, rows_of(sm, c, p0 + K_OUT, cta, ncta), l, st, nullptr, f);
-                __syncthreads();
-                tr.mark(P, 32);
-                if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_IN, cta, ncta);
-                tr.mark(P, 70);
-                if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_IN, per_frame, cta, ncta, len_now);
-                tr.mark(P, 71);
-                if (!grid_sync(P, epoch, sm, tr)) goto drain;
-                // ---- linear_in + silu gate
-                if (!wait_stage(sm, P, parity)) goto drain;
-                tr.mark(P, 41);
-                {
-                    const Rows r = rows_of(sm, c, p0 + K_IN, cta, ncta);
-                    const Staged sg = staged_layout(r, true, c.D);
-                    prep_vector(sm, c.x, c.D, reinterpret_cast<const float*>(sm.wbuf + sg.alpha), rb);
-                    tr.mark(P, 40);
-                    gemv_phase<EPI_GATE>(P, sm, r, l, st, nullptr, f);
-                }
-                __syncthreads();
-                tr.mark(P, 42);
-                if (threadIdx.x == 0) stage_phase(sm, c, p0 + K_DOWN, cta, ncta);
-                tr.mark(P, 70);
-                if (threadIdx.x < 32) look_ahead(sm, P, lk, gp0 + K_DOWN, per_frame, cta, ncta, len_now);
-                tr.mark(P, 71);
-                if (!grid_sync(P, epoch, sm, tr)) goto drain;
-                // ---- linear_out + residual
-                if (!wait_stage(sm, P, parity)) goto drain;
-                tr.mark(P, 51);
-                prep_vector(sm, c.hid, c.F, nullptr, rb);
-                tr.mark(P, 50);
-                gemv_phase<EPI_RESID>(P, sm, rows_of(sm, c, p0 + K_DOWN, cta, ncta), l, st, nullptr, f);
-                __syncthreads();
-                tr.mark(P, 52);
-                {  // next: QKV of layer l+1, or the head
-                    const int pn = l + 1 < c.L ? p0 + 5 : 5 * c.L;
-                    if (threadIdx.x == 0) stage_phase(sm, c, pn, cta, ncta);
-                    tr.mark(P, 70);
-                    if (threadIdx.x < 32) look_ahead(sm, P, lk, f * per_frame + pn, per_frame, cta, ncta, len_now);
-                    tr.mark(P, 71);
-                }
-                if (!grid_sync(P, epoch, sm, tr)) goto drain;
-            }
-            // ---- head + argmax partials
-            if (!wait_stage(sm, P, parity)) goto drain;
-            tr.mark(P, 61);
-            HeadBest best{-FLT_MAX, 0x7FFFFFFF};
-            {
-                const Rows r = rows_of(sm, c, 5 * c.L, cta, ncta);
-                const Staged sg = staged_layout(r, true, c.D);
-                prep_vector(sm, c.x, c.D, reinterpret_cast<const float*>(sm.wbuf + sg.alpha), rb);
-                tr.mark(P, 60);
-                gemv_phase<EPI_LOGITS>(P, sm, r, 0, st, &best, f);
-            }
-            {
-                const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-                if (lane == 0) {
-                    sm.wv[warp] = best.v;
-                    sm.wi[warp] = best.i;
-                }
-                __syncthreads();
-                if (threadIdx.x == 0) {
-                    float bv = -FLT_MAX;
-                    int bi = 0x7FFFFFFF;
-                    for (int w = 0; w < kWarps; ++w)
-                        if (sm.wv[w] > bv || (sm.wv[w] == bv && sm.wi[w] < bi)) {
-                            bv = sm.wv[w];
-                            bi = sm.wi[w];
-                        }
-                    P.amax_v[cta] = bv;
-                    P.amax_i[cta] = bi;
-                    if (f + 1 < P.steps) stage_phase(sm, c, 0, cta, ncta);  // next frame: layer 0's QKV
-                }
-                if (f + 1 < P.steps && threadIdx.x < 32)
-                    look_ahead(sm, P, lk, (f + 1) * per_frame, per_frame, cta, ncta, min(st.len + 2, c.ML));
-            }
-            tr.mark(P, 62);
-            if (!grid_sync(P, epoch, sm, tr)) goto drain;
-        }
-        // every CTA reduces the partials identically
-        {
-            float bv = -FLT_MAX;
-            int bi = 0x7FFFFFFF;
-            for (int t = 0; t < ncta; ++t) {
-                const float v = __ldcg(P.amax_v + t);
-                const int i = __ldcg(P.amax_i + t);
-                if (v > bv || (v == bv && i < bi)) {
-                    bv = v;
-                    bi = i;
-                }
-            }
-            const uint32_t token = (uint32_t)(bi == 0x7FFFFFFF ? 0 : bi);
-            st.write_pos = (st.write_pos + 1) % c.ML;
-            st.offset += 1;
-            st.len = min(st.len + 1, c.ML);
-            int32_t out = (int32_t)token;
-            if (desc->mode == 1) {
-                st.frame_count += 1;
-                if (st.frame_count >= c.text_delay) {
-                    st.last_text = token;
-                } else {
-                    const uint32_t p0 = st.prev0, p1 = st.prev1;
-                    st.prev0 = p1;
-                    st.prev1 = token;
-                    st.last_text = (token != c.pad_id && token != 0u && token == p0 && token != p1) ? c.pad_id : token;
-                    out = -1;
-                }
-            }
-            if (cta == 0 && threadIdx.x == 0) {
-                desc->tokens[f] = out;
-                c.state[sid] = st;
-                if (f + 1 == P.steps) desc->step = P.steps;
-            }
-        }
-    }
-    return;
-drain:
-    // stopping early: a staged copy that was issued but not yet waited for (stages and waits
-    // alternate, so one is pending exactly when the issue count exceeds the wait count) must land
-    // before the CTA's shared memory goes away
-    if (threadIdx.x == 0 && sm.staged != sm.waited) {
-        uint32_t spins = 0;
-        while (!mbar_try_wait(&sm.mbar, parity) && ++spins < kSpinLimit) {
-        }
+    if ((int)threadIdx.x >= kCThreads) {
+        const uint32_t issued = producer(P, cta);
+        producer_drain(sm, issued);
+    } else {
+        consumers(P, cta);
     }
     __syncthreads();
 }
@@ -1144,50 +1279,72 @@ __global__ void __launch_bounds__(256) audio_sum_kernel(Ctx c, float* __restrict
     xa[(int64_t)f * c.D + j] = acc;
 }
 
-// Grid-barrier latency probe: `iters` back-to-back barriers of the persistent kernel (mode 0),
-// or of a variant where the last arriver (atom.add.acq_rel) publishes a generation flag on a
-// separate line that the others poll (mode 1).
-__global__ void __launch_bounds__(kThreads, 1) barrier_probe_kernel(const __grid_constant__ MegaArgs P, int iters,
-                                                                    int mode) {
-    Smem& sm = smem_ref();
-    uint32_t epoch = 0;
-    Tracer tr;
-    if (mode == 0) {
-        for (int i = 0; i < iters; ++i)
-            if (!grid_sync(P, epoch, sm, tr)) return;
-        return;
-    }
-    uint32_t* flag = P.bar + 32;  // 128 bytes away from the counter
+// Grid-barrier latency probe: `iters` back-to-back grid barriers (mode 0: release add on one
+// counter + acquire poll; mode 1: the last arriver publishes a generation flag on another line).
+__global__ void __launch_bounds__(kThreads, 1) barrier_probe_kernel(uint32_t* bar, int iters, int mode) {
+    __shared__ int go;
+    uint32_t* flag = bar + 32;  // 128 bytes away from the counter
     for (int i = 0; i < iters; ++i) {
         __syncthreads();
         if (threadIdx.x == 0) {
             const uint32_t gen = (uint32_t)i + 1u;
-            uint32_t old;
-            asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(P.bar) : "memory");
-            if (old == gen * gridDim.x - 1u) {
-                asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(gen) : "memory");
+            int ok = 1;
+            uint32_t spins = 0;
+            if (mode == 0) {
+                red_release_add(bar, 1u);
+                while ((int32_t)(ld_acquire(bar) - gen * gridDim.x) < 0)
+                    if (++spins > kSpinLimit || *(volatile uint32_t*)(bar + 1)) {
+                        ok = 0;
+                        break;
+                    }
             } else {
-                uint32_t spins = 0;
-                while ((int32_t)(ld_acquire(flag) - gen) < 0 && ++spins < kSpinLimit) {
+                uint32_t old;
+                asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(bar) : "memory");
+                if (old == gen * gridDim.x - 1u) {
+                    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(gen) : "memory");
+                } else {
+                    while ((int32_t)(ld_acquire(flag) - gen) < 0)
+                        if (++spins > kSpinLimit || *(volatile uint32_t*)(bar + 1)) {
+                            ok = 0;
+                            break;
+                        }
                 }
             }
+            if (!ok) atomicExch(bar + 1, 1u);
+            go = ok;
         }
         __syncthreads();
+        if (!go) return;
     }
 }
 
-// Largest staged phase of one CTA in bytes (must fit kWBuf).
-size_t max_stage_bytes(int D, int F, int V, int ncta) {
-    auto rows_max = [&](int64_t units, int rows_per_unit) { return (units + ncta - 1) / ncta * rows_per_unit; };
-    auto bytes = [](int64_t rows, int k) {
-        return (size_t)rows * (k / 32) * 16 + (((size_t)rows * (k / 32) * 2 + 15) & ~(size_t)15);
-    };
-    size_t m = bytes(rows_max(3 * D / 2, 2), D);
-    m = std::max(m, bytes(rows_max(D / 2, 2), D));
-    m = std::max(m, 2 * bytes(rows_max(F, 1), D));
-    m = std::max(m, bytes(rows_max(D / 2, 2), F));
-    m = std::max(m, bytes(rows_max((V + 1) / 2, 2), D));
-    return m;
+// Scratch layout of the persistent kernel inside the stream set's scratch.
+struct ScratchLayout {
+    size_t bar, base, xb, qkvb, partb, attb, hidb, argb, total;
+};
+ScratchLayout scratch_layout(int num_sms, int D, int F, int H) {
+    auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+    const int ns = num_sms / (H > 0 ? H : 1);
+    ScratchLayout s;
+    size_t o = 0;
+    s.bar = o;
+    o += 256;
+    s.base = o;
+    o += 256;
+    s.xb = o;
+    o += up((size_t)4 * D * 8);
+    s.qkvb = o;
+    o += up((size_t)2 * 3 * D * 8);
+    s.partb = o;
+    o += up((size_t)2 * H * ns * kPartPairs * 8);
+    s.attb = o;
+    o += up((size_t)2 * D * 8);
+    s.hidb = o;
+    o += up((size_t)2 * F * 8);
+    s.argb = o;
+    o += up((size_t)2 * num_sms * 2 * 8);
+    s.total = o;
+    return s;
 }
 
 }  // namespace
@@ -1196,19 +1353,16 @@ cudaError_t mega_barrier_probe(void* scratch, int iters, int mode, float* ms_out
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(barrier_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem));
     if (e != cudaSuccess) return e;
-    MegaArgs P{};
-    P.bar = static_cast<uint32_t*>(scratch);
+    uint32_t* bar = static_cast<uint32_t*>(scratch);
     cudaEvent_t a, b;
     cudaEventCreate(&a);
     cudaEventCreate(&b);
-    e = cudaMemset(P.bar, 0, 256);
-    void* args[] = {(void*)&P, (void*)&iters, (void*)&mode};
+    e = cudaMemset(bar, 0, 256);
+    void* args[] = {(void*)&bar, (void*)&iters, (void*)&mode};
     if (e == cudaSuccess) e = cudaEventRecord(a, 0);
     if (e == cudaSuccess)
-        e = cudaLaunchCooperativeKernel((const void*)barrier_probe_kernel, dim3(sms), dim3(kThreads), args, sizeof(Smem), 0);
+        e = cudaLaunchCooperativeKernel((const void*)barrier_probe_kernel, dim3(sms), dim3(kThreads), args, 0, 0);
     if (e == cudaSuccess) e = cudaEventRecord(b, 0);
     if (e == cudaSuccess) e = cudaEventSynchronize(b);
     if (e == cudaSuccess) e = cudaEventElapsedTime(ms_out, a, b);
@@ -1218,25 +1372,35 @@ cudaError_t mega_barrier_probe(void* scratch, int iters, int mode, float* ms_out
 }
 
 bool mega_supported(int L, int D, int F, int HD, int V, int num_sms, int ML, int kv_f32) {
+    if (std::getenv("STT_DISABLE_MEGA") != nullptr) return false;
+    if (HD != 128 || D % 256 != 0 || D > 4096 || F % 256 != 0 || F > kMaxK || L < 1 || L > kMaxL) return false;
     const int H = D / HD;
-    const int nsplit = num_sms / (H > 0 ? H : 1);
-    if (nsplit < 1) return false;
-    // out_proj rows (plus alignment) and the K/V slots of one split share the staging buffer
-    const size_t kv = (size_t)((ML + nsplit - 1) / nsplit) * HD * (kv_f32 ? 4 : 2) * 2;
-    const size_t out_rows = (size_t)2 * ((D / 2 + num_sms - 1) / num_sms);
-    const size_t out_bytes = out_rows * (D / 32) * 16 + ((out_rows * (D / 32) * 2 + 15) & ~(size_t)15);
-    if (((out_bytes + 127) & ~(size_t)127) + kv > (size_t)kWBuf) return false;
-    if (max_stage_bytes(D, F, V, num_sms) + (size_t)D * 4 > (size_t)kWBuf) return false;
-    // head tickets live in the 64-word barrier block (2 + H <= 64); the layer table holds kMaxL;
-    // a CTA keeps its x rows (2 * ceil(D/2 / num_sms)) in xown
-    return HD == 128 && D % 256 == 0 && D <= 4096 && F % 128 == 0 && F <= kMaxK && L > 0 && L <= kMaxL &&
-           2 * ((D / 2 + num_sms - 1) / num_sms) <= kMaxOwnRows &&
-           D / HD <= 60 && max_stage_bytes(D, F, V, num_sms) <= (size_t)kWBuf &&
-           std::getenv("STT_DISABLE_MEGA") == nullptr;
+    if (H < 1 || H > num_sms || num_sms > kCThreads) return false;
+    if ((uint32_t)(5 * L + 2) > kEpochsPerFrame) return false;
+    const int nsplit = num_sms / H;
+    // a CTA keeps its x rows in xown
+    if (2 * ((D / 2 + num_sms - 1) / num_sms) > kMaxOwnRows) return false;
+    // every phase of one CTA must fit the ring at once (segments are released per phase), with
+    // room for the alignment of each segment and one wrap of the ring
+    auto phase_fits = [&](int units, uint32_t unit_bytes, uint32_t alpha_bytes) {
+        const uint32_t ups = std::max<uint32_t>(1u, kSegMax / unit_bytes);
+        const uint32_t segs = (uint32_t)(units + ups - 1) / ups;
+        const uint64_t bytes = (uint64_t)units * unit_bytes + alpha_bytes + (segs + 1) * 128u + (uint64_t)ups * unit_bytes;
+        return bytes <= kRing && segs + 1 <= (uint32_t)kNBar / 2;
+    };
+    const uint32_t rowD = (uint32_t)(D / 32) * 18u, rowF = (uint32_t)(F / 32) * 18u;
+    auto per = [&](int64_t units) { return (int)((units + num_sms - 1) / num_sms); };
+    if (!phase_fits(per(3 * D / 2), 2 * rowD, (uint32_t)D * 4)) return false;
+    if (!phase_fits(per(D / 2), 2 * rowD, 0)) return false;
+    if (!phase_fits(per(F), 2 * rowD, (uint32_t)D * 4)) return false;
+    if (!phase_fits(per(D / 2), 2 * rowF, 0)) return false;
+    if (!phase_fits(per((V + 1) / 2), 2 * rowD, (uint32_t)D * 4)) return false;
+    const uint64_t kv = (uint64_t)((ML + nsplit - 1) / nsplit) * HD * (kv_f32 ? 4 : 2) * 2 + 256;
+    return kv <= kRing;
 }
 
 size_t mega_scratch_bytes(int num_sms, int D, int F, int V, int H, int HD) {
-    return 256 + (size_t)D * 4 + (size_t)num_sms * 8 + 64 * 4;  // bar | (unused) | amax_v | amax_i
+    return scratch_layout(num_sms, D, F, H).total;
 }
 
 cudaError_t configure_mega() {
@@ -1250,19 +1414,26 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
     if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, mega_kernel, kThreads, sizeof(Smem));
     if (e != cudaSuccess) return e;
     if (occ < 1) return cudaErrorCooperativeLaunchTooLarge;
+    const ScratchLayout sl = scratch_layout(sms, c.D, c.F, c.H);
     uint8_t* s = static_cast<uint8_t*>(ms.scratch);
     MegaArgs P;
     P.c = c;
     P.steps = steps;
-    P.nsplit = sms / c.H;  // the stream set sizes its partials buffer for num_sms rows
-    P.bar = reinterpret_cast<uint32_t*>(s);
+    P.nsplit = sms / c.H;
+    if (P.nsplit < 1) return cudaErrorInvalidConfiguration;
+    P.bar = reinterpret_cast<uint32_t*>(s + sl.bar);
+    P.base = reinterpret_cast<uint32_t*>(s + sl.base);
     P.xa = ms.xa_all;
-    P.amax_v = reinterpret_cast<float*>(s + 256 + (size_t)c.D * 4);
-    P.amax_i = reinterpret_cast<int32_t*>(s + 256 + (size_t)c.D * 4 + (size_t)sms * 4);
-    P.pf_budget = 0;  // off by default: issuing the prefetches stalls warp 0 longer than it saves
-    if (const char* pb = std::getenv("STT_MEGA_PF_KB")) P.pf_budget = (uint32_t)std::atoi(pb) * 1024u;
-    P.pf_lines = 1;
-    if (const char* pm = std::getenv("STT_MEGA_PF_BULK")) P.pf_lines = std::atoi(pm) ? 0 : 1;
+    uint64_t* xb = reinterpret_cast<uint64_t*>(s + sl.xb);
+    for (int i = 0; i < 2; ++i) {
+        P.xb[i][0] = xb + (size_t)(2 * i) * c.D;
+        P.xb[i][1] = xb + (size_t)(2 * i + 1) * c.D;
+        P.qkvb[i] = reinterpret_cast<uint64_t*>(s + sl.qkvb) + (size_t)i * 3 * c.D;
+        P.partb[i] = reinterpret_cast<uint64_t*>(s + sl.partb) + (size_t)i * c.H * P.nsplit * kPartPairs;
+        P.attb[i] = reinterpret_cast<uint64_t*>(s + sl.attb) + (size_t)i * c.D;
+        P.hidb[i] = reinterpret_cast<uint64_t*>(s + sl.hidb) + (size_t)i * c.F;
+        P.argb[i] = reinterpret_cast<uint64_t*>(s + sl.argb) + (size_t)i * sms * 2;
+    }
     P.trace = nullptr;
     P.trace_frame = -1;
     P.trace_cap = 0;
@@ -1271,7 +1442,6 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
         P.trace_frame = ms.trace_frame;
         P.trace_cap = ms.trace_cap;
     }
-    if (P.nsplit < 1) return cudaErrorInvalidConfiguration;
     e = cudaMemsetAsync(P.bar, 0, 256, st);
     if (e != cudaSuccess) return e;
     audio_sum_kernel<<<dim3((c.D + 255) / 256, steps), 256, 0, st>>>(c, ms.xa_all);

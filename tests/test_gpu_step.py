@@ -238,12 +238,11 @@ def test_persistent_kernel_barrier_and_trace(full_model):
     buf = (C.c_uint64 * 1024)()
     n = C.c_int()
     assert lib().stt_debug_get_trace(cache._h, buf, 1024, C.byref(n)) == 0
-    # (tag, time) pairs: frame start; per layer 5 barriers (2 marks each), the phase marks (3 for
-    # qkv, linear_in and linear_out, 2 for attention and out_proj) and 2 after each of the 4
-    # stagings; the head's 3 marks and its barrier
+    # (tag, time) pairs: frame start; per layer 3 marks for each of the 4 GEMV phases and 4 for
+    # attention (CTA 0 merges the splits of head 0); the head's 3 marks and the argmax
     tags = list(buf[0:n.value:2])
     marks = [i for i, t in enumerate(tags) if t != 0]
-    assert len(marks) == 1 + 16 * (5 * 2 + 3 * 3 + 2 * 2 + 4 * 2) + 3 + 2, len(marks)
+    assert len(marks) == 1 + 16 * (4 * 3 + 4) + 3 + 1, len(marks)
     assert tags[0] == 0 and tags[-1] == 0  # wall-clock pairs around the frame
     t = np.array([buf[2 * i + 1] for i in marks], dtype=np.int64)
     assert np.all(np.diff(t) >= 0)
