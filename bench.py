@@ -56,11 +56,13 @@ TRACE_NAMES = {1: "frame_start", 11: "qkv_inputs", 12: "qkv_gemv", 13: "qkv_end"
 
 
 def trace_breakdown(raw):
-    """(tag, cycles) pairs of one traced frame, bracketed by (0, globaltimer ns) pairs ->
-    microseconds spent reaching each kind of mark."""
+    """(tag, cycles) pairs of one traced frame of CTA 0, bracketed by (0, globaltimer ns) pairs ->
+    microseconds spent reaching each kind of mark, plus the wait durations (tags >= 100: thread
+    0's cycles + 1 in segment waits, 100 + kind, and flagged-word waits, 110 + kind)."""
     pairs = [(raw[i], raw[i + 1]) for i in range(0, len(raw) - 1, 2)]
     walls = [v for t, v in pairs if t == 0]
-    marks = [(t, v) for t, v in pairs if t != 0]
+    marks = [(t, v) for t, v in pairs if 0 < t < 100]
+    durs = [(t, v - 1) for t, v in pairs if t >= 100]
     frame_ns = walls[-1] - walls[0] if len(walls) >= 2 else None
     cycles = marks[-1][1] - marks[0][1]
     ns_per_cycle = frame_ns / cycles if frame_ns and cycles else 1.0 / 1.965
@@ -68,8 +70,46 @@ def trace_breakdown(raw):
     for (t0, a), (t1, b) in zip(marks, marks[1:]):
         k = TRACE_NAMES.get(t1, str(t1))
         out[k] = out.get(k, 0.0) + (b - a) * ns_per_cycle / 1e3
+    kinds = {1: "qkv", 2: "attention", 3: "out_proj", 4: "linear_in", 5: "linear_out", 6: "head"}
+    waits = {}
+    for t, v in durs:
+        name = ("segment_wait_" if t < 110 else "input_wait_") + kinds.get(t % 10, str(t))
+        waits[name] = waits.get(name, 0.0) + v * ns_per_cycle / 1e3
     return {"frame_us": frame_ns / 1e3 if frame_ns else None, "sm_ghz": 1.0 / ns_per_cycle,
-            "trace_us": {k: round(v, 2) for k, v in out.items()}}
+            "trace_us": {k: round(v, 2) for k, v in out.items()},
+            "cta0_waits_us": {k: round(v, 2) for k, v in sorted(waits.items())}}
+
+
+LAYER_TAGS = [11, 12, 13, 21, 22, 24, 23, 31, 32, 33, 41, 42, 43, 51, 52, 53]
+HEAD_TAGS = [61, 62, 63, 7]
+
+
+def cta_breakdown(buf, n_ctas, n_slots, layers):
+    """Per-CTA %globaltimer stamps of one frame -> how far the latest CTA moves at each kind of
+    mark (critical path, us per frame) and how far it is ahead of the median CTA (lag)."""
+    import numpy as np
+    t = np.array(buf, dtype=np.int64).reshape(n_ctas, n_slots)
+    starts = t[:, 0][t[:, 0] > 0]
+    if starts.size == 0:
+        return {}
+    order = [(1 + 16 * l + i, tag) for l in range(layers) for i, tag in enumerate(LAYER_TAGS)]
+    order += [(1 + 16 * layers + i, tag) for i, tag in enumerate(HEAD_TAGS)]
+    prev = int(starts.max())
+    crit, lag = {}, {}
+    last = prev
+    for slot, tag in order:
+        v = t[:, slot][t[:, slot] > 0]
+        if v.size == 0:
+            continue
+        mx = int(v.max())
+        name = TRACE_NAMES.get(tag, str(tag))
+        crit[name] = crit.get(name, 0.0) + (mx - prev) / 1e3
+        lag[name] = lag.get(name, 0.0) + (mx - float(np.median(v))) / 1e3
+        prev = mx
+        last = mx
+    return {"frame_us_all_ctas": (last - int(starts.min())) / 1e3,
+            "critical_path_us": {k: round(v, 2) for k, v in crit.items()},
+            "lag_behind_median_us": {k: round(v, 2) for k, v in lag.items()}}
 
 
 class ClockSampler:
@@ -172,6 +212,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--frames", type=int, default=FRAMES,
+                    help="frames per utterance; only a shorter profiling case sets it (default 750)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -184,6 +226,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    nframes = args.frames
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
@@ -211,14 +254,14 @@ def main():
     g.close()
     cache = model.create_cache(1, "bf16")
     stream = stt_b200.SttStream(cfg, cache, 0)
-    audio = stt_b200.audio_tokens(SEED, rank, FRAMES)
+    audio = stt_b200.audio_tokens(SEED, rank, nframes)
     d_audio = torch.from_numpy(audio.astype(np.int32)).cuda()
-    d_tokens = torch.empty(FRAMES, dtype=torch.int32, device="cuda")
+    d_tokens = torch.empty(nframes, dtype=torch.int32, device="cuda")
     ts = torch.cuda.current_stream()
 
     def utterance_device():
         check(lib().stt_stream_reset_async(cache._h, 0, 0, C.c_void_p(ts.cuda_stream)), "reset_async")
-        check(lib().stt_stream_feed_frames_device(cache._h, 0, FRAMES, C.c_void_p(d_audio.data_ptr()),
+        check(lib().stt_stream_feed_frames_device(cache._h, 0, nframes, C.c_void_p(d_audio.data_ptr()),
                                                   C.c_void_p(d_tokens.data_ptr()), C.c_void_p(ts.cuda_stream)),
               "feed_frames_device")
 
@@ -239,7 +282,7 @@ def main():
     ms = max_over_ranks(ms)
     clocks = clk.summary()
     dev_tokens = d_tokens.cpu().numpy()
-    value = world * args.steps * FRAMES / (ms / 1000.0)
+    value = world * args.steps * nframes / (ms / 1000.0)
 
     # ---- e2e: the public per-frame call with host buffers
     audio_host = [np.ascontiguousarray(a) for a in audio]
@@ -250,12 +293,12 @@ def main():
     t0 = time.perf_counter()
     for _ in range(args.steps):
         stream.reset()
-        for f in range(FRAMES):
+        for f in range(nframes):
             stream.feed_frame(audio_host[f])
     e2e_s = time.perf_counter() - t0
     barrier()
     e2e_s = max_over_ranks(e2e_s)
-    e2e = world * args.steps * FRAMES / e2e_s
+    e2e = world * args.steps * nframes / e2e_s
 
     # ---- diagnostics: grid-barrier latency and a per-phase breakdown of one late frame
     diag = {}
@@ -264,35 +307,42 @@ def main():
         diag["grid_barrier_ns"] = ns.value
     if lib().stt_debug_barrier_ns(local, 2000, 1, C.byref(ns)) == 0:
         diag["grid_barrier_flag_ns"] = ns.value
-    lib().stt_debug_trace_frame(cache._h, FRAMES - 10)
+    lib().stt_debug_trace_frame(cache._h, nframes - 10)
     utterance_device()
     torch.cuda.synchronize()
     buf = (C.c_uint64 * 1024)()
     nt = C.c_int()
     if lib().stt_debug_get_trace(cache._h, buf, 1024, C.byref(nt)) == 0 and nt.value > 4:
         diag.update(trace_breakdown([buf[i] for i in range(nt.value)]))
-        diag["traced_frame"] = FRAMES - 10
+        diag["traced_frame"] = nframes - 10
+    cap = 148 * 1024
+    tb = (C.c_uint64 * cap)()
+    nc, ns_ = C.c_int(), C.c_int()
+    if lib().stt_debug_get_trace_ctas(cache._h, tb, cap, C.byref(nc), C.byref(ns_)) == 0:
+        diag.update(cta_breakdown(list(tb[:nc.value * ns_.value]), nc.value, ns_.value, 16))
     lib().stt_debug_trace_frame(cache._h, -1)
 
     # ---- roofline of the decode step (every kernel of a frame, device-timed above)
     pk, pk_kind = peaks()
-    algo = algorithmic_bytes_per_utterance()
+    algo = algorithmic_bytes_per_utterance(nframes)
     achieved = algo / (ms / args.steps / 1000.0) / 1e9
     line = {
         "metric": "decode frames/s per GPU (1 stream, 750-frame utterance)",
         "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "ms_per_frame": ms / args.steps / FRAMES,
+        "ms_per_step": ms / args.steps, "ms_per_frame": ms / args.steps / nframes,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "1 stream x 750 frames (config 2) per GPU, STT-1B Q4_0, 16 layers d2048, bf16 KV",
+        "config": {"workload": f"1 stream x {nframes} frames per GPU, STT-1B Q4_0, 16 layers d2048, bf16 KV",
                    "l2": "inputs larger than L2: 627 MB of Q4 weights streamed per frame",
                    "parallelism": f"{world} independent streams, one per GPU"},
         "roofline": {"bound": "hbm", "kernel": "decode step (all kernels of one frame)", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "peak_kind": pk_kind, "algorithmic_bytes_per_step": algo, "traffic": None},
-        "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": FRAMES * 32 * 4,
-                "d2h_bytes_per_step": FRAMES * (4 + 32)},
+        "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": nframes * 32 * 4,
+                "d2h_bytes_per_step": nframes * (4 + 32)},
         "clocks": clocks,
+        # our kernels per step: stream reset, step descriptor, audio-embedding sums, persistent kernel
+        "gpu_launches": 4 * args.steps,
         "diagnostics": diag,
         "tokens_checksum": int(np.int64(dev_tokens.astype(np.int64).sum())),
     }

@@ -240,6 +240,10 @@ int stt_synth_audio_tokens(uint64_t seed, int32_t stream, int32_t first_frame, i
 int stt_debug_trace_frame(stt_streams* streams, int frame);
 /* Copies the timestamps of the last traced frame (at most cap); *n receives the count. */
 int stt_debug_get_trace(stt_streams* streams, uint64_t* out, int cap, int* n);
+/* Copies every CTA's %globaltimer stamps of the last traced frame: out[cta * n_slots + slot],
+ * slot 0 the frame start, 1 + 16 l + i the i-th phase mark of layer l, 1 + 16 L + i the head's
+ * marks and the argmax (0 = not reached by that CTA).  cap must hold num_sms * n_slots values. */
+int stt_debug_get_trace_ctas(stt_streams* streams, uint64_t* out, int cap, int* n_ctas, int* n_slots);
 /* Mean time of one grid barrier over `iters` back-to-back barriers on device `device`, in
  * nanoseconds: mode 0 is the persistent kernel's barrier (release add, acquire poll of the
  * counter), mode 1 a variant in which the last arriver publishes a flag that the others poll. */

@@ -670,8 +670,11 @@ int run_steps(stt_streams* s, const int32_t* ids, int n, int steps, const uint32
     CUDA_TRY(launch_set_desc(s->d_desc, s->d_ids, init, st));
     if (use_mega) {
         // single-stream steps go through the persistent step kernel
-        if (s->mega.trace_frame >= 0)
+        if (s->mega.trace_frame >= 0) {
             CUDA_TRY(cudaMemsetAsync(s->mega.trace, 0, sizeof(unsigned long long) * s->mega.trace_cap, st));
+            CUDA_TRY(cudaMemsetAsync(s->mega.trace_ctas, 0,
+                                     sizeof(unsigned long long) * (size_t)m->num_sms * kTraceSlots, st));
+        }
         if ((size_t)steps * m->D * 4 > s->mega_xa.cap) {
             // growing reallocates: work still queued on another stream may read the old buffer
             CUDA_TRY(cudaDeviceSynchronize());
@@ -760,6 +763,7 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     const size_t o_desc = take(sizeof(StepDesc) + S * 4 + 64);
     const size_t o_mega = take(mega_scratch_bytes(m->num_sms, m->D, m->F, m->V, m->H, m->HD));
     const size_t o_trace = take(kTraceCap * sizeof(unsigned long long));
+    const size_t o_trace_ctas = take((size_t)m->num_sms * kTraceSlots * sizeof(unsigned long long));
     if (cudaMalloc(&s->d_scratch, off) != cudaSuccess) {
         cudaGetLastError();
         return set_error(STT_E_OOM, "cannot allocate %zu bytes of step scratch", off);
@@ -784,6 +788,8 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     s->mega.scratch_bytes = mega_scratch_bytes(m->num_sms, m->D, m->F, m->V, m->H, m->HD);
     s->mega.trace = reinterpret_cast<unsigned long long*>(b + o_trace);
     s->mega.trace_cap = kTraceCap;
+    s->mega.trace_ctas = reinterpret_cast<unsigned long long*>(b + o_trace_ctas);
+    s->mega.trace_slots = kTraceSlots;
     CUDA_TRY(cudaMemset(s->d_scratch, 0, off));
     CUDA_TRY(cudaMemset(s->d_kv, 0, s->kv_stream_bytes * S));
     s->h_state.assign(S, fresh_state(m));
@@ -1137,6 +1143,19 @@ extern "C" int stt_debug_get_trace(stt_streams* s, uint64_t* out, int cap, int* 
     while (k + 1 < (int)t.size() && t[k + 1] != 0) k += 2;
     *n = std::min(k, cap & ~1);
     for (int i = 0; i < *n; ++i) out[i] = t[i];
+    return STT_OK;
+}
+
+extern "C" int stt_debug_get_trace_ctas(stt_streams* s, uint64_t* out, int cap, int* n_ctas, int* n_slots) {
+    clear_error();
+    if (!s || !out || !n_ctas || !n_slots || cap < 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    DeviceScope ds(s->m->device);
+    const size_t total = (size_t)s->m->num_sms * kTraceSlots;
+    if ((size_t)cap < total) return set_error(STT_E_INVALID_ARG, "capacity %d below %zu", cap, total);
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(out, s->mega.trace_ctas, sizeof(unsigned long long) * total, cudaMemcpyDeviceToHost));
+    *n_ctas = s->m->num_sms;
+    *n_slots = kTraceSlots;
     return STT_OK;
 }
 

@@ -55,6 +55,7 @@ constexpr int kPartPairs = 132;            // attention partial: M, L, 2 unused,
 // up after roughly a second.
 constexpr uint32_t kSpinLimit = 1u << 21;    // mbarrier / counter polls
 constexpr uint32_t kLLSpinLimit = 1u << 20;  // flagged-word polls (each with a short sleep)
+constexpr uint32_t kSleepLimit = 1u << 20;   // mbarrier waits with a suspend-time hint
 
 enum Kind : int { K_QKV = 0, K_ATT = 1, K_OUT = 2, K_IN = 3, K_DOWN = 4, K_HEAD = 5 };
 
@@ -82,6 +83,8 @@ struct MegaArgs {
     unsigned long long* trace;  // optional: (tag, SM clock) pairs of one frame of CTA 0
     int32_t trace_frame;
     int32_t trace_cap;
+    unsigned long long* tctas;  // optional: [cta][slot] %globaltimer of every CTA's marks
+    int32_t tslots;
 };
 
 struct Smem {
@@ -105,6 +108,8 @@ struct Smem {
     alignas(8) unsigned long long empty[kNBar];
     int32_t stop[2];          // consumers: some thread saw an abort (by agreement parity)
     int32_t tslot, tron;      // trace cursor (consumer thread 0)
+    int32_t tall;             // every CTA records this frame's marks
+    long long wseg, wll;      // traced frame: thread 0's cycles in segment / flagged-word waits
 };
 static_assert(sizeof(Smem) <= 232448, "shared memory per CTA");
 
@@ -141,6 +146,19 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* m, uint32_t pa
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(smem_addr(m)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// The same with a suspend-time hint: the thread sleeps until the phase completes or about
+// `ns` nanoseconds pass, instead of spinning on the issue slots the working warps need.
+__device__ __forceinline__ bool mbar_wait_sleep(unsigned long long* m, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(m)), "r"(parity), "r"(ns)
         : "memory");
     return ok != 0;
 }
@@ -194,12 +212,36 @@ __device__ __noinline__ void give_up(const MegaArgs& P) {
 // kind of phase k (1 qkv, 2 attention, 3 out_proj, 4 linear_in, 5 linear_out, 6 head):
 // 10k+1 inputs ready, 10k+2 this thread's compute done, 10k+3 phase end; 24 the partials of the
 // other attention splits merged (split-0 CTAs); 7 argmax reduced.
-__device__ __forceinline__ void trace_mark(const MegaArgs& P, unsigned long long tag) {
+// Every CTA also records %globaltimer at the mark's fixed slot: 0 frame start, 1 + 16 l + i for
+// the i-th mark of layer l (11 12 13 21 22 24 23 31 32 33 41 42 43 51 52 53), 1 + 16 L + i for
+// 61 62 63 7.
+__device__ __forceinline__ void trace_mark(const MegaArgs& P, unsigned long long tag, int slot) {
     Smem& sm = smem_ref();
-    if (threadIdx.x == 0 && sm.tron && sm.tslot + 1 < P.trace_cap) {
-        P.trace[sm.tslot] = tag;
-        P.trace[sm.tslot + 1] = clock64();
-        sm.tslot += 2;
+    if (threadIdx.x == 0) {
+        if (sm.tron && sm.tslot + 1 < P.trace_cap) {
+            P.trace[sm.tslot] = tag;
+            P.trace[sm.tslot + 1] = clock64();
+            sm.tslot += 2;
+        }
+        if (sm.tall && slot < P.tslots) P.tctas[(int64_t)blockIdx.x * P.tslots + slot] = globaltimer();
+    }
+}
+__device__ __forceinline__ int lslot(int l, int i) { return 1 + 16 * l + i; }
+
+// Traced frame, CTA 0: thread 0's wait cycles of the phase that just ended, as (100 + kind,
+// cycles + 1) for segment waits and (110 + kind, cycles + 1) for flagged-word waits (the +1
+// keeps a zero duration from reading as the end of the trace).
+__device__ __forceinline__ void trace_waits(const MegaArgs& P, int kind) {
+    Smem& sm = smem_ref();
+    if (threadIdx.x == 0 && sm.tron) {
+        if (sm.tslot + 3 < P.trace_cap) {
+            P.trace[sm.tslot] = 100 + kind;
+            P.trace[sm.tslot + 1] = (unsigned long long)sm.wseg + 1;
+            P.trace[sm.tslot + 2] = 110 + kind;
+            P.trace[sm.tslot + 3] = (unsigned long long)sm.wll + 1;
+            sm.tslot += 4;
+        }
+        sm.wseg = sm.wll = 0;
     }
 }
 __device__ __forceinline__ void trace_wall(const MegaArgs& P) {
@@ -217,30 +259,49 @@ __device__ __forceinline__ void trace_wall(const MegaArgs& P) {
 __device__ __forceinline__ bool wait_seg(Smem& sm, const MegaArgs& P, uint32_t i) {
     unsigned long long* m = &sm.full[i % kNBar];
     const uint32_t par = (i / kNBar) & 1u;
+    if (mbar_try_wait(m, par)) return true;
+    const bool tr = threadIdx.x == 0 && sm.tron;
+    const long long t0 = tr ? clock64() : 0;
     uint32_t spins = 0;
-    while (!mbar_try_wait(m, par)) {
-        if ((++spins & 255u) == 0) {
-            if (aborted(P)) return false;
-            if (spins > kSpinLimit) {
+    bool ok = true;
+    while (!mbar_wait_sleep(m, par, 2000u)) {
+        if ((++spins & 15u) == 0) {
+            if (aborted(P)) {
+                ok = false;
+                break;
+            }
+            if (spins > kSleepLimit) {
                 give_up(P);
-                return false;
+                ok = false;
+                break;
             }
         }
     }
-    return true;
+    if (tr) sm.wseg += clock64() - t0;
+    return ok;
 }
 
-// Waits until the 2 * N words at p (16-byte aligned) all carry epoch ep.
-template <int N>
-__device__ __forceinline__ bool ll_wait(const MegaArgs& P, const uint64_t* p, uint32_t ep, uint64_t (&w)[2 * N]) {
-    uint32_t spins = 0;
+// Waits until the words of N 16-byte pieces (two words each, at addr(i)) all carry epoch ep.
+// All loads of a round are in flight together, so a wait costs one L2 round trip once the data
+// is there; between rounds the thread sleeps 32 .. 256 ns.  (Every address must be valid:
+// loads skipped under a condition make the compiler keep far more registers live.)
+template <int N, typename Addr>
+__device__ __forceinline__ bool ll_wait_n(const MegaArgs& P, Addr addr, uint32_t ep, uint64_t (&w)[N][2]) {
+    uint32_t spins = 0, nap = 32;
+    const bool tr = threadIdx.x == 0 && smem_ref().tron;
+    const long long t0 = tr ? clock64() : 0;
     for (;;) {
 #pragma unroll
-        for (int i = 0; i < N; ++i) ll_load2(p + 2 * i, w[2 * i], w[2 * i + 1]);
+        for (int i = 0; i < N; ++i) {
+            ll_load2(addr(i), w[i][0], w[i][1]);
+        }
         bool ok = true;
 #pragma unroll
-        for (int i = 0; i < 2 * N; ++i) ok = ok && ll_ep(w[i]) == ep;
-        if (ok) return true;
+        for (int i = 0; i < N; ++i) ok = ok && ll_ep(w[i][0]) == ep && ll_ep(w[i][1]) == ep;
+        if (ok) {
+            if (tr) smem_ref().wll += clock64() - t0;
+            return true;
+        }
         ++spins;
         if ((spins & 63u) == 0) {
             if (aborted(P)) return false;
@@ -249,7 +310,8 @@ __device__ __forceinline__ bool ll_wait(const MegaArgs& P, const uint64_t* p, ui
                 return false;
             }
         }
-        __nanosleep(64);
+        __nanosleep(nap);
+        nap = min(nap * 2u, 256u);
     }
 }
 
@@ -328,13 +390,13 @@ __device__ __forceinline__ bool prod_wait_release(Smem& sm, const MegaArgs& P, P
         unsigned long long* m = &sm.empty[j % kNBar];
         const uint32_t par = (j / kNBar) & 1u;
         uint32_t spins = 0;
-        while (!mbar_try_wait(m, par)) {
-            if ((++spins & 255u) == 0) {
+        while (!mbar_wait_sleep(m, par, 2000u)) {
+            if ((++spins & 15u) == 0) {
                 if (aborted(P)) {
                     ok = 0;
                     break;
                 }
-                if (spins > kSpinLimit) {
+                if (spins > kSleepLimit) {
                     give_up(P);
                     ok = 0;
                     break;
@@ -594,9 +656,10 @@ __device__ __noinline__ bool prep_vector(const MegaArgs& P, const uint64_t* ll, 
         v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (q < nq) {
             if (src == 0) {
-                uint64_t w[4];
-                ok = ll_wait<2>(P, ll + 4 * q, ep, w) && ok;
-                v[i] = make_float4(ll_val(w[0]), ll_val(w[1]), ll_val(w[2]), ll_val(w[3]));
+                uint64_t w[2][2];
+                const uint64_t* a = ll + 4 * q;
+                ok = ll_wait_n<2>(P, [=](int j) -> const uint64_t* { return a + 2 * j; }, ep, w) && ok;
+                v[i] = make_float4(ll_val(w[0][0]), ll_val(w[0][1]), ll_val(w[1][0]), ll_val(w[1][1]));
             } else {
                 const float4 a = __ldcg(reinterpret_cast<const float4*>(xa) + q);
                 const int j = 4 * q;
@@ -862,15 +925,14 @@ __device__ __noinline__ bool attention_phase(const MegaArgs& P, int layer, uint3
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int HD = c.HD, h = sp.h, par = layer & 1;
     bool ok = wait_seg(sm, P, seg);
-    uint64_t w[4];
-    const uint64_t* qb = P.qkvb[par];
-    ok = ll_wait<2>(P, qb + h * HD + 4 * lane, ep - 1u, w) && ok;
-    const float4 q = make_float4(ll_val(w[0]), ll_val(w[1]), ll_val(w[2]), ll_val(w[3]));
-    ok = ll_wait<2>(P, qb + c.D + h * HD + 4 * lane, ep - 1u, w) && ok;
-    const float4 kcur = make_float4(ll_val(w[0]), ll_val(w[1]), ll_val(w[2]), ll_val(w[3]));
-    ok = ll_wait<2>(P, qb + 2 * c.D + h * HD + 4 * lane, ep - 1u, w) && ok;
-    const float4 vcur = make_float4(ll_val(w[0]), ll_val(w[1]), ll_val(w[2]), ll_val(w[3]));
-    trace_mark(P, 21);
+    const uint64_t* qb = P.qkvb[par] + h * HD + 4 * lane;
+    const int D = c.D;
+    uint64_t w[6][2];
+    ok = ll_wait_n<6>(P, [=](int i) -> const uint64_t* { return qb + (i >> 1) * D + 2 * (i & 1); }, ep - 1u, w) && ok;
+    const float4 q = make_float4(ll_val(w[0][0]), ll_val(w[0][1]), ll_val(w[1][0]), ll_val(w[1][1]));
+    const float4 kcur = make_float4(ll_val(w[2][0]), ll_val(w[2][1]), ll_val(w[3][0]), ll_val(w[3][1]));
+    const float4 vcur = make_float4(ll_val(w[4][0]), ll_val(w[4][1]), ll_val(w[5][0]), ll_val(w[5][1]));
+    trace_mark(P, 21, lslot(layer, 3));
     const uint32_t base = sm.seg_off[seg % kNBar];
     const int n = sp.j1 - sp.j0;
     const KT* ks = reinterpret_cast<const KT*>(sm.ring + base);
@@ -920,7 +982,7 @@ __device__ __noinline__ bool attention_phase(const MegaArgs& P, int layer, uint3
         acc.m = mn;
     }
     const SoftAcc mine = merge_warps(sm, acc);
-    trace_mark(P, 22);
+    trace_mark(P, 22, lslot(layer, 4));
     uint64_t* pb = P.partb[par] + (int64_t)h * P.nsplit * kPartPairs;
     if (sp.s != 0) {
         if (warp == 0) {
@@ -941,14 +1003,13 @@ __device__ __noinline__ bool attention_phase(const MegaArgs& P, int layer, uint3
     if (warp == 0) a = mine;
     for (int s = warp == 0 ? kCWarps : warp; s < P.nsplit; s += kCWarps) {
         const uint64_t* d = pb + (int64_t)s * kPartPairs;
-        uint64_t ml[2], ov[4];
-        ok = ll_wait<1>(P, d, ep, ml) && ok;
-        ok = ll_wait<2>(P, d + 4 + 4 * lane, ep, ov) && ok;
-        soft_merge(a, ll_val(ml[0]), ll_val(ml[1]),
-                   make_float4(ll_val(ov[0]), ll_val(ov[1]), ll_val(ov[2]), ll_val(ov[3])));
+        uint64_t w[3][2];
+        ok = ll_wait_n<3>(P, [=](int i) -> const uint64_t* { return i == 0 ? d : d + 2 + 2 * i + 4 * lane; }, ep, w) && ok;
+        soft_merge(a, ll_val(w[0][0]), ll_val(w[0][1]),
+                   make_float4(ll_val(w[1][0]), ll_val(w[1][1]), ll_val(w[2][0]), ll_val(w[2][1])));
     }
     const SoftAcc all = merge_warps(sm, a);
-    trace_mark(P, 24);
+    trace_mark(P, 24, lslot(layer, 5));
     if (warp == 0) {
         uint64_t* d = P.attb[par] + h * HD + 4 * lane;
         ll_store(d, __fdiv_rn(all.o.x, all.l), ep);
@@ -989,10 +1050,11 @@ __device__ __noinline__ bool argmax_phase(const MegaArgs& P, int f, uint32_t ep)
     float bv = -FLT_MAX;
     int bi = 0x7FFFFFFF;
     if ((int)threadIdx.x < (int)gridDim.x) {
-        uint64_t w[2];
-        ok = ll_wait<1>(P, ab + 2 * threadIdx.x, ep, w);
-        bv = ll_val(w[0]);
-        bi = (int)(uint32_t)w[1];
+        const uint64_t* a = ab + 2 * threadIdx.x;
+        uint64_t w[1][2];
+        ok = ll_wait_n<1>(P, [=](int) -> const uint64_t* { return a; }, ep, w);
+        bv = ll_val(w[0][0]);
+        bi = (int)(uint32_t)w[0][1];
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -1058,9 +1120,10 @@ __device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
         if (threadIdx.x == 0) {
             if (sm.tron) trace_wall(P);  // end of the traced frame
             sm.tron = P.trace != nullptr && cta == 0 && f == P.trace_frame;
+            sm.tall = P.tctas != nullptr && f == P.trace_frame;
         }
         trace_wall(P);
-        trace_mark(P, 1);
+        trace_mark(P, 1, 0);
         const uint32_t E = ebase + (uint32_t)f * kEpochsPerFrame + 1u;  // epoch of step 0
         if (threadIdx.x == 0) {
             uint32_t text = c.desc->text ? __ldcg(c.desc->text + f) : sm.st.last_text;
@@ -1087,15 +1150,16 @@ __device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
                     else
                         ok = prep_any(P, P.xb[par ^ 1][1], E + (uint32_t)(p0 - 1), c.D, alpha, rb, 0, nullptr, 0, 0, 0) && ok;
                     rb ^= 1u;
-                    trace_mark(P, 11);
+                    trace_mark(P, 11, lslot(l, 0));
                     ok = gemv_phase<EPI_QKV>(P, p0, seg + 1, P.qkvb[par], E + (uint32_t)p0, f) && ok;
-                    trace_mark(P, 12);
+                    trace_mark(P, 12, lslot(l, 1));
                 } else if (l == 0) {
                     // no QKV rows here, but the residual still needs x0's own rows
                     ok = prep_any(P, nullptr, 0, c.D, nullptr, rb, 1, P.xa + (int64_t)f * c.D, sm.text, own0, own1) && ok;
                 }
                 csync();
-                trace_mark(P, 13);
+                trace_mark(P, 13, lslot(l, 2));
+                trace_waits(P, 1);
                 release_phase(sm, seg, n);
                 seg += (uint32_t)n;
             }
@@ -1109,7 +1173,8 @@ __device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
                         ok = attention_phase<__nv_bfloat16>(P, l, seg, E + (uint32_t)(p0 + K_ATT), cta) && ok;
                 }
                 csync();
-                trace_mark(P, 23);
+                trace_mark(P, 23, lslot(l, 6));
+                trace_waits(P, 2);
                 release_phase(sm, seg, n);
                 seg += (uint32_t)n;
             }
@@ -1118,12 +1183,13 @@ __device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
                 const int n = phase_segs(sm, P, p0 + K_OUT, cta);
                 if (n > 0) {
                     ok = prep_any(P, P.attb[par], E + (uint32_t)(p0 + K_ATT), c.D, nullptr, rb, 0, nullptr, 0, 0, 0) && ok;
-                    trace_mark(P, 31);
+                    trace_mark(P, 31, lslot(l, 7));
                     ok = gemv_phase<EPI_RESID>(P, p0 + K_OUT, seg, P.xb[par][0], E + (uint32_t)(p0 + K_OUT), f) && ok;
-                    trace_mark(P, 32);
+                    trace_mark(P, 32, lslot(l, 8));
                 }
                 csync();
-                trace_mark(P, 33);
+                trace_mark(P, 33, lslot(l, 9));
+                trace_waits(P, 3);
                 release_phase(sm, seg, n);
                 seg += (uint32_t)n;
             }
@@ -1135,12 +1201,13 @@ __device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
                     const float* alpha = reinterpret_cast<const float*>(sm.ring + sm.seg_off[seg % kNBar]);
                     ok = prep_any(P, P.xb[par][0], E + (uint32_t)(p0 + K_OUT), c.D, alpha, rb, 0, nullptr, 0, 0, 0) && ok;
                     rb ^= 1u;
-                    trace_mark(P, 41);
+                    trace_mark(P, 41, lslot(l, 10));
                     ok = gemv_phase<EPI_GATE>(P, p0 + K_IN, seg + 1, P.hidb[par], E + (uint32_t)(p0 + K_IN), f) && ok;
-                    trace_mark(P, 42);
+                    trace_mark(P, 42, lslot(l, 11));
                 }
                 csync();
-                trace_mark(P, 43);
+                trace_mark(P, 43, lslot(l, 12));
+                trace_waits(P, 4);
                 release_phase(sm, seg, n);
                 seg += (uint32_t)n;
             }
@@ -1149,12 +1216,13 @@ __device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
                 const int n = phase_segs(sm, P, p0 + K_DOWN, cta);
                 if (n > 0) {
                     ok = prep_any(P, P.hidb[par], E + (uint32_t)(p0 + K_IN), c.F, nullptr, rb, 0, nullptr, 0, 0, 0) && ok;
-                    trace_mark(P, 51);
+                    trace_mark(P, 51, lslot(l, 13));
                     ok = gemv_phase<EPI_RESID>(P, p0 + K_DOWN, seg, P.xb[par][1], E + (uint32_t)(p0 + K_DOWN), f) && ok;
-                    trace_mark(P, 52);
+                    trace_mark(P, 52, lslot(l, 14));
                 }
                 ok = agree(sm, P, ok, agreements);  // includes the phase-end barrier
-                trace_mark(P, 53);
+                trace_mark(P, 53, lslot(l, 15));
+                trace_waits(P, 5);
                 release_phase(sm, seg, n);
                 seg += (uint32_t)n;
             }
@@ -1173,9 +1241,9 @@ __device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
                 const float* alpha = reinterpret_cast<const float*>(sm.ring + sm.seg_off[seg % kNBar]);
                 ok = prep_any(P, P.xb[(c.L - 1) & 1][1], E + (uint32_t)(ph - 1), c.D, alpha, rb, 0, nullptr, 0, 0, 0) && ok;
                 rb ^= 1u;
-                trace_mark(P, 61);
+                trace_mark(P, 61, lslot(c.L, 0));
                 ok = gemv_phase<EPI_LOGITS>(P, ph, seg + 1, nullptr, 0, f) && ok;
-                trace_mark(P, 62);
+                trace_mark(P, 62, lslot(c.L, 1));
             }
             csync();
             if (threadIdx.x == 0) {
@@ -1190,12 +1258,13 @@ __device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
                 ll_store(d, bv, E + (uint32_t)ph);
                 ll_store(d + 1, __int_as_float(bi), E + (uint32_t)ph);
             }
-            trace_mark(P, 63);
+            trace_mark(P, 63, lslot(c.L, 2));
+                trace_waits(P, 6);
             release_phase(sm, seg, n);
             seg += (uint32_t)n;
         }
         ok = argmax_phase(P, f, E + (uint32_t)ph) && ok;
-        trace_mark(P, 7);
+        trace_mark(P, 7, lslot(c.L, 3));
         // this CTA's K/V writes of the frame are done: publish them to the producers
         ok = agree(sm, P, ok, agreements);
         if (threadIdx.x == 0) red_release_add(P.bar, 1u);
@@ -1223,6 +1292,8 @@ __global__ void __launch_bounds__(kThreads, 1) mega_kernel(const __grid_constant
         sm.stop[0] = sm.stop[1] = 0;
         sm.tslot = 0;
         sm.tron = 0;
+        sm.wseg = sm.wll = 0;
+        sm.tall = 0;
         // row ranges of this CTA (the same for every layer)
         auto pairs = [&](int rows, uint32_t row_bytes) {
             Range r;
@@ -1437,10 +1508,14 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
     P.trace = nullptr;
     P.trace_frame = -1;
     P.trace_cap = 0;
+    P.tctas = nullptr;
+    P.tslots = 0;
     if (ms.trace && ms.trace_frame >= 0) {
         P.trace = ms.trace;
         P.trace_frame = ms.trace_frame;
         P.trace_cap = ms.trace_cap;
+        P.tctas = ms.trace_ctas;
+        P.tslots = ms.trace_slots;
     }
     e = cudaMemsetAsync(P.bar, 0, 256, st);
     if (e != cudaSuccess) return e;

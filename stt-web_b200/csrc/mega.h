@@ -12,7 +12,12 @@ struct MegaState {
     unsigned long long* trace = nullptr;  // device buffer for phase timestamps (diagnostics)
     int trace_frame = -1;
     int trace_cap = 0;
+    unsigned long long* trace_ctas = nullptr;  // [num_sms][trace_slots] %globaltimer per CTA
+    int trace_slots = 0;
 };
+
+// Trace slots per CTA of one frame: 1 + 16 per layer + 4 (layers <= 32).
+constexpr int kTraceSlots = 1 + 16 * 32 + 4;
 
 bool mega_supported(int L, int D, int F, int HD, int V, int num_sms, int ML, int kv_f32);
 size_t mega_scratch_bytes(int num_sms, int D, int F, int V, int H, int HD);

@@ -132,6 +132,7 @@ SIGNATURES = {
     "stt_synth_audio_tokens": (C.c_int, [C.c_uint64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, U32P]),
     "stt_debug_trace_frame": (C.c_int, [P, C.c_int]),
     "stt_debug_get_trace": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int, I32P]),
+    "stt_debug_get_trace_ctas": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "stt_debug_barrier_ns": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "stt_last_error": (C.c_char_p, []),
 }

@@ -241,7 +241,7 @@ def test_persistent_kernel_barrier_and_trace(full_model):
     # (tag, time) pairs: frame start; per layer 3 marks for each of the 4 GEMV phases and 4 for
     # attention (CTA 0 merges the splits of head 0); the head's 3 marks and the argmax
     tags = list(buf[0:n.value:2])
-    marks = [i for i, t in enumerate(tags) if t != 0]
+    marks = [i for i, t in enumerate(tags) if 0 < t < 100]  # tags >= 100 carry wait durations
     assert len(marks) == 1 + 16 * (4 * 3 + 4) + 3 + 1, len(marks)
     assert tags[0] == 0 and tags[-1] == 0  # wall-clock pairs around the frame
     t = np.array([buf[2 * i + 1] for i in marks], dtype=np.int64)
