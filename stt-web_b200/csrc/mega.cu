@@ -650,17 +650,33 @@ __device__ __noinline__ bool prep_vector(const MegaArgs& P, const uint64_t* ll, 
     const int nq = K >> 2, NB = K >> 5;
     float4 v[QN];
     bool ok = true;
+    if (src == 0) {
+        // two quads a round: their loads are in flight together (slots past the end re-read the
+        // last quad and are dropped)
+        const int t = threadIdx.x;
 #pragma unroll
-    for (int i = 0; i < QN; ++i) {
-        const int q = threadIdx.x + i * kCThreads;
-        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q < nq) {
-            if (src == 0) {
-                uint64_t w[2][2];
-                const uint64_t* a = ll + 4 * q;
-                ok = ll_wait_n<2>(P, [=](int j) -> const uint64_t* { return a + 2 * j; }, ep, w) && ok;
-                v[i] = make_float4(ll_val(w[0][0]), ll_val(w[0][1]), ll_val(w[1][0]), ll_val(w[1][1]));
-            } else {
+        for (int i0 = 0; i0 < QN; i0 += 2) {
+            uint64_t w[4][2];
+            ok = ll_wait_n<4>(
+                     P,
+                     [=](int j) -> const uint64_t* {
+                         const int q = min(t + (i0 + (j >> 1)) * kCThreads, nq - 1);
+                         return ll + 4 * q + 2 * (j & 1);
+                     },
+                     ep, w) &&
+                 ok;
+            v[i0] = make_float4(ll_val(w[0][0]), ll_val(w[0][1]), ll_val(w[1][0]), ll_val(w[1][1]));
+            if (i0 + 1 < QN) v[i0 + 1] = make_float4(ll_val(w[2][0]), ll_val(w[2][1]), ll_val(w[3][0]), ll_val(w[3][1]));
+        }
+#pragma unroll
+        for (int i = 0; i < QN; ++i)
+            if (t + i * kCThreads >= nq) v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+#pragma unroll
+        for (int i = 0; i < QN; ++i) {
+            const int q = threadIdx.x + i * kCThreads;
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (q < nq) {
                 const float4 a = __ldcg(reinterpret_cast<const float4*>(xa) + q);
                 const int j = 4 * q;
                 v[i] = make_float4(__fadd_rn(a.x, emb_val(c, c.emb_text, text, j)),
@@ -669,8 +685,8 @@ __device__ __noinline__ bool prep_vector(const MegaArgs& P, const uint64_t* ll, 
                                    __fadd_rn(a.w, emb_val(c, c.emb_text, text, j + 3)));
                 const float vv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
-                for (int t = 0; t < 4; ++t)
-                    if (j + t >= own0 && j + t < own1) sm.xown[j + t - own0] = vv[t];
+                for (int u = 0; u < 4; ++u)
+                    if (j + u >= own0 && j + u < own1) sm.xown[j + u - own0] = vv[u];
             }
         }
     }
