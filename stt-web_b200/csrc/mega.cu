@@ -884,154 +884,266 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
 
 // ------------------------------------------------------------------------------ attention
 
-// Online-softmax state of a set of keys: max score, sum of exp, sum of exp * v (4 dims a lane).
-struct SoftAcc {
-    float m, l;
-    float4 o;
-};
-__device__ __forceinline__ void soft_merge(SoftAcc& a, float m, float l, float4 o) {
-    if (l == 0.0f) return;
-    if (a.l == 0.0f) {
-        a.m = m;
-        a.l = l;
-        a.o = o;
-        return;
-    }
-    const float M = fmaxf(a.m, m);
-    const float fa = expf(a.m - M), fb = expf(m - M);
-    a.l = __fmaf_rn(a.l, fa, __fmul_rn(l, fb));
-    a.o.x = __fmaf_rn(a.o.x, fa, __fmul_rn(o.x, fb));
-    a.o.y = __fmaf_rn(a.o.y, fa, __fmul_rn(o.y, fb));
-    a.o.z = __fmaf_rn(a.o.z, fa, __fmul_rn(o.z, fb));
-    a.o.w = __fmaf_rn(a.o.w, fa, __fmul_rn(o.w, fb));
-    a.m = M;
-}
-
-// Merges the 15 per-warp states through shared memory in warp order; the result is valid in
-// warp 0.  Two consumer barriers.
-__device__ __forceinline__ SoftAcc merge_warps(Smem& sm, const SoftAcc& mine) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float4* wo = reinterpret_cast<float4*>(sm.limbs);
-    float* wm = reinterpret_cast<float*>(wo + kCWarps * 32);
-    float* wl = wm + kCWarps;
-    if (lane == 0) {
-        wm[warp] = mine.m;
-        wl[warp] = mine.l;
-    }
-    wo[warp * 32 + lane] = mine.o;
-    csync();
-    SoftAcc a{-FLT_MAX, 0.0f, make_float4(0.f, 0.f, 0.f, 0.f)};
-    if (warp == 0)
-        for (int w = 0; w < kCWarps; ++w) soft_merge(a, wm[w], wl[w], wo[w * 32 + lane]);
-    csync();  // the scratch may be rewritten after this
-    return a;
-}
-
-// Split-KV attention of head h over ring slots [j0, j1) (model.rs:450-472): the K/V slots come
-// from the ring segment `seg`, the slot of this frame (write_pos) from the flagged qkv words.
-// Split 0 of each head then merges the partials of all splits (split order, then warp order)
-// into softmax(q.k^T * scale).v and publishes it.  Returns false after an abort.
+// Split-KV attention of head h over ring slots [j0, j1) (model.rs:450-472), HD = 128.
+//   - q, k and v of this frame (flagged qkv words) go to shared memory once;
+//   - a warp takes 4 keys at a time, one per group of 8 lanes; a lane holds 16 dimensions
+//     (interleaved so that the 16-byte loads of a group are contiguous) and keeps an
+//     online-softmax state (max, sum of exp, sum of exp * v) for its group's keys; the key slots
+//     come from the ring segment `seg`, the slot of this frame (write_pos) from q/k/v above;
+//   - the 4 groups of a warp merge by shuffles, the 15 warps through shared memory with one
+//     thread per dimension (warp order);
+//   - split 0 of each head then merges the partials of the other splits (three groups of
+//     threads over consecutive splits, then the groups in order) into
+//     softmax(q.k^T * scale).v and publishes it; the other splits publish their partials.
+// Returns false after an abort.
 template <typename KT>
 __device__ __noinline__ bool attention_phase(const MegaArgs& P, int layer, uint32_t seg, uint32_t ep, int cta) {
+    constexpr int HD = 128;
+    constexpr int EPL = 16 / (int)sizeof(KT);  // elements of one 16-byte load
+    constexpr int CH = 16 / EPL;               // 16-byte loads per lane for 16 dimensions
     Smem& sm = smem_ref();
     const Ctx& c = P.c;
     const int len = min(sm.st.len + 1, c.ML);
     const int wpos = sm.st.write_pos;
     const Split sp = split_of(cta, P.nsplit, c.H, len);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int HD = c.HD, h = sp.h, par = layer & 1;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int h = sp.h, par = layer & 1;
+    float* qs = reinterpret_cast<float*>(sm.limbs);  // [3][128]: q, k, v of this frame
+    float* wst = qs + 3 * HD;                        // [15][HD + 4]: m, l, unused, unused, o[HD]
     bool ok = wait_seg(sm, P, seg);
-    const uint64_t* qb = P.qkvb[par] + h * HD + 4 * lane;
-    const int D = c.D;
-    uint64_t w[6][2];
-    ok = ll_wait_n<6>(P, [=](int i) -> const uint64_t* { return qb + (i >> 1) * D + 2 * (i & 1); }, ep - 1u, w) && ok;
-    const float4 q = make_float4(ll_val(w[0][0]), ll_val(w[0][1]), ll_val(w[1][0]), ll_val(w[1][1]));
-    const float4 kcur = make_float4(ll_val(w[2][0]), ll_val(w[2][1]), ll_val(w[3][0]), ll_val(w[3][1]));
-    const float4 vcur = make_float4(ll_val(w[4][0]), ll_val(w[4][1]), ll_val(w[5][0]), ll_val(w[5][1]));
+    if (t < 3 * HD / 2) {
+        const int part = t / (HD / 2), i = (t % (HD / 2)) * 2;
+        const uint64_t* a = P.qkvb[par] + part * c.D + h * HD + i;
+        uint64_t w[1][2];
+        ok = ll_wait_n<1>(P, [=](int) -> const uint64_t* { return a; }, ep - 1u, w) && ok;
+        qs[part * HD + i] = ll_val(w[0][0]);
+        qs[part * HD + i + 1] = ll_val(w[0][1]);
+    }
+    csync();
     trace_mark(P, 21, lslot(layer, 3));
+    const int g = lane >> 3, sub = lane & 7;
+    // lane dimension i (0..15) is dims(i) = (i / EPL) * 8 * EPL + sub * EPL + i % EPL
+    float q[16], o[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        q[i] = qs[(i / EPL) * 8 * EPL + sub * EPL + i % EPL];
+        o[i] = 0.0f;
+    }
     const uint32_t base = sm.seg_off[seg % kNBar];
     const int n = sp.j1 - sp.j0;
-    const KT* ks = reinterpret_cast<const KT*>(sm.ring + base);
-    const KT* vs = reinterpret_cast<const KT*>(sm.ring + base + (uint32_t)n * HD * sizeof(KT));
-    SoftAcc acc{-FLT_MAX, 0.0f, make_float4(0.f, 0.f, 0.f, 0.f)};
-    for (int j = sp.j0 + warp; j < sp.j1; j += kCWarps) {
-        float4 k, v;
-        if (j == wpos) {
-            // this frame's K/V (the ring copy stores them rounded to the ring type)
-            if (sizeof(KT) == 4) {
-                k = kcur;
-                v = vcur;
-            } else {
-                k = make_float4(__bfloat162float(__float2bfloat16_rn(kcur.x)), __bfloat162float(__float2bfloat16_rn(kcur.y)),
-                                __bfloat162float(__float2bfloat16_rn(kcur.z)), __bfloat162float(__float2bfloat16_rn(kcur.w)));
-                v = make_float4(__bfloat162float(__float2bfloat16_rn(vcur.x)), __bfloat162float(__float2bfloat16_rn(vcur.y)),
-                                __bfloat162float(__float2bfloat16_rn(vcur.z)), __bfloat162float(__float2bfloat16_rn(vcur.w)));
+    const uint8_t* ks = sm.ring + base;
+    const uint8_t* vs = ks + (uint32_t)n * HD * sizeof(KT);
+    float m = -FLT_MAX, l = 0.0f;
+    for (int jb = sp.j0 + warp * 4; jb < sp.j1; jb += 4 * kCWarps) {
+        const int j = jb + g;
+        const bool valid = j < sp.j1;
+        const bool cur = j == wpos;
+        const int rr = valid && !cur ? j - sp.j0 : 0;
+        float kv[16];
+        if (cur) {
+            // this frame's key (the ring copy stores it rounded to the ring type)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float x = qs[HD + (i / EPL) * 8 * EPL + sub * EPL + i % EPL];
+                kv[i] = sizeof(KT) == 4 ? x : __bfloat162float(__float2bfloat16_rn(x));
             }
         } else {
-            const int rr = j - sp.j0;
-            if (sizeof(KT) == 4) {
-                k = reinterpret_cast<const float4*>(ks + (int64_t)rr * HD)[lane];
-                v = reinterpret_cast<const float4*>(vs + (int64_t)rr * HD)[lane];
-            } else {
-                const uint2 kr = reinterpret_cast<const uint2*>(ks + (int64_t)rr * HD)[lane];
-                const uint2 vr = reinterpret_cast<const uint2*>(vs + (int64_t)rr * HD)[lane];
-                k = make_float4(__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xFFFF0000u),
-                                __uint_as_float(kr.y << 16), __uint_as_float(kr.y & 0xFFFF0000u));
-                v = make_float4(__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xFFFF0000u),
-                                __uint_as_float(vr.y << 16), __uint_as_float(vr.y & 0xFFFF0000u));
+#pragma unroll
+            for (int ch = 0; ch < CH; ++ch) {
+                const uint4 r = *reinterpret_cast<const uint4*>(ks + ((size_t)rr * HD + ch * 8 * EPL + sub * EPL) * sizeof(KT));
+                if (sizeof(KT) == 4) {
+                    kv[ch * 4 + 0] = __uint_as_float(r.x);
+                    kv[ch * 4 + 1] = __uint_as_float(r.y);
+                    kv[ch * 4 + 2] = __uint_as_float(r.z);
+                    kv[ch * 4 + 3] = __uint_as_float(r.w);
+                } else {
+                    const uint32_t wv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        kv[ch * 8 + 2 * e] = __uint_as_float(wv[e] << 16);
+                        kv[ch * 8 + 2 * e + 1] = __uint_as_float(wv[e] & 0xFFFF0000u);
+                    }
+                }
             }
         }
-        float dot = __fmul_rn(q.x, k.x);
-        dot = __fmaf_rn(q.y, k.y, dot);
-        dot = __fmaf_rn(q.z, k.z, dot);
-        dot = __fmaf_rn(q.w, k.w, dot);
-        dot = warp_sum(dot);
+        float dot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dot = __fmaf_rn(q[i], kv[i], dot);
+        dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 1);
+        dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 2);
+        dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 4);
+        if (!valid) continue;
+        // value row
+        if (cur) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float x = qs[2 * HD + (i / EPL) * 8 * EPL + sub * EPL + i % EPL];
+                kv[i] = sizeof(KT) == 4 ? x : __bfloat162float(__float2bfloat16_rn(x));
+            }
+        } else {
+#pragma unroll
+            for (int ch = 0; ch < CH; ++ch) {
+                const uint4 r = *reinterpret_cast<const uint4*>(vs + ((size_t)rr * HD + ch * 8 * EPL + sub * EPL) * sizeof(KT));
+                if (sizeof(KT) == 4) {
+                    kv[ch * 4 + 0] = __uint_as_float(r.x);
+                    kv[ch * 4 + 1] = __uint_as_float(r.y);
+                    kv[ch * 4 + 2] = __uint_as_float(r.z);
+                    kv[ch * 4 + 3] = __uint_as_float(r.w);
+                } else {
+                    const uint32_t wv[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        kv[ch * 8 + 2 * e] = __uint_as_float(wv[e] << 16);
+                        kv[ch * 8 + 2 * e + 1] = __uint_as_float(wv[e] & 0xFFFF0000u);
+                    }
+                }
+            }
+        }
         const float score = __fmul_rn(dot, c.attn_scale);
-        const float mn = fmaxf(acc.m, score);
-        const float corr = expf(acc.m - mn);
+        const float mn = fmaxf(m, score);
+        const float corr = expf(m - mn);
         const float pr = expf(score - mn);
-        acc.l = __fmaf_rn(acc.l, corr, pr);
-        acc.o.x = __fmaf_rn(acc.o.x, corr, __fmul_rn(pr, v.x));
-        acc.o.y = __fmaf_rn(acc.o.y, corr, __fmul_rn(pr, v.y));
-        acc.o.z = __fmaf_rn(acc.o.z, corr, __fmul_rn(pr, v.z));
-        acc.o.w = __fmaf_rn(acc.o.w, corr, __fmul_rn(pr, v.w));
-        acc.m = mn;
+        l = __fmaf_rn(l, corr, pr);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[i] = __fmaf_rn(o[i], corr, __fmul_rn(pr, kv[i]));
+        m = mn;
     }
-    const SoftAcc mine = merge_warps(sm, acc);
+    // merge the 4 key groups of the warp (lanes with the same sub); the lower group keeps its
+    // terms first
+#pragma unroll
+    for (int x = 8; x <= 16; x <<= 1) {
+        const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, x), l2 = __shfl_xor_sync(0xFFFFFFFFu, l, x);
+        float o2[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o2[i] = __shfl_xor_sync(0xFFFFFFFFu, o[i], x);
+        const bool low = (lane & x) == 0;
+        const float ma = low ? m : m2, la = low ? l : l2, mb = low ? m2 : m, lb = low ? l2 : l;
+        if (lb != 0.0f) {
+            if (la == 0.0f) {
+                m = mb;
+                l = lb;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] = low ? o2[i] : o[i];
+            } else {
+                const float M = fmaxf(ma, mb);
+                const float fa = expf(ma - M), fb = expf(mb - M);
+                l = __fmaf_rn(la, fa, __fmul_rn(lb, fb));
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float oa = low ? o[i] : o2[i], ob = low ? o2[i] : o[i];
+                    o[i] = __fmaf_rn(oa, fa, __fmul_rn(ob, fb));
+                }
+                m = M;
+            }
+        } else if (la != 0.0f) {
+            m = ma;
+            l = la;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = low ? o[i] : o2[i];
+        }
+    }
+    if (g == 0) {
+        float* d = wst + warp * (HD + 4);
+        if (sub == 0) {
+            d[0] = m;
+            d[1] = l;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) d[4 + (i / EPL) * 8 * EPL + sub * EPL + i % EPL] = o[i];
+    }
+    csync();
+    // 128 threads: the warps' states merged per dimension (warp order)
+    float M = -FLT_MAX, L = 0.0f, O = 0.0f;
+    if (t < HD) {
+        for (int w = 0; w < kCWarps; ++w)
+            if (wst[w * (HD + 4) + 1] != 0.0f) M = fmaxf(M, wst[w * (HD + 4)]);
+        for (int w = 0; w < kCWarps; ++w) {
+            const float lw = wst[w * (HD + 4) + 1];
+            if (lw == 0.0f) continue;
+            const float f = expf(wst[w * (HD + 4)] - M);
+            L = __fmaf_rn(lw, f, L);
+            O = __fmaf_rn(wst[w * (HD + 4) + 4 + t], f, O);
+        }
+    }
     trace_mark(P, 22, lslot(layer, 4));
     uint64_t* pb = P.partb[par] + (int64_t)h * P.nsplit * kPartPairs;
     if (sp.s != 0) {
-        if (warp == 0) {
+        if (t < HD) {
             uint64_t* d = pb + (int64_t)sp.s * kPartPairs;
-            if (lane == 0) {
-                ll_store(d, mine.m, ep);
-                ll_store(d + 1, mine.l, ep);
+            if (t == 0) {
+                ll_store(d, M, ep);
+                ll_store(d + 1, L, ep);
             }
-            ll_store(d + 4 + 4 * lane, mine.o.x, ep);
-            ll_store(d + 5 + 4 * lane, mine.o.y, ep);
-            ll_store(d + 6 + 4 * lane, mine.o.z, ep);
-            ll_store(d + 7 + 4 * lane, mine.o.w, ep);
+            ll_store(d + 4 + t, O, ep);
         }
         return ok;
     }
-    // split 0: warp w merges splits w, w + 15, ...; warp 0 starts from its own partial (split 0)
-    SoftAcc a{-FLT_MAX, 0.0f, make_float4(0.f, 0.f, 0.f, 0.f)};
-    if (warp == 0) a = mine;
-    for (int s = warp == 0 ? kCWarps : warp; s < P.nsplit; s += kCWarps) {
-        const uint64_t* d = pb + (int64_t)s * kPartPairs;
-        uint64_t w[3][2];
-        ok = ll_wait_n<3>(P, [=](int i) -> const uint64_t* { return i == 0 ? d : d + 2 + 2 * i + 4 * lane; }, ep, w) && ok;
-        soft_merge(a, ll_val(w[0][0]), ll_val(w[0][1]),
-                   make_float4(ll_val(w[1][0]), ll_val(w[1][1]), ll_val(w[2][0]), ll_val(w[2][1])));
+    // split 0: threads 0-127, 128-255 and 256-383 (one dimension each) merge three consecutive
+    // ranges of the other splits, three splits a poll round; group 0 starts from this split's
+    // own state
+    const int grp = t / HD, dim = t % HD;
+    const int others = P.nsplit - 1;
+    const int per = (others + 2) / 3;
+    const int s_lo = 1 + min(others, grp * per), s_hi = 1 + min(others, (grp + 1) * per);
+    float gm = grp == 0 ? M : -FLT_MAX, gl = grp == 0 ? L : 0.0f, go = grp == 0 ? O : 0.0f;
+    if (grp < 3) {
+        for (int s0 = s_lo; s0 < s_hi; s0 += 3) {
+            uint64_t w[6][2];
+            ok = ll_wait_n<6>(
+                     P,
+                     [=](int i) -> const uint64_t* {
+                         const int s = min(s0 + (i >> 1), s_hi - 1);
+                         const uint64_t* d = pb + (int64_t)s * kPartPairs;
+                         return (i & 1) ? d + 4 + (dim & ~1) : d;
+                     },
+                     ep, w) &&
+                 ok;
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                if (s0 + i >= s_hi) break;
+                const float ms = ll_val(w[2 * i][0]), ls = ll_val(w[2 * i][1]);
+                const float os = ll_val(w[2 * i + 1][dim & 1]);
+                if (ls == 0.0f) continue;
+                if (gl == 0.0f) {
+                    gm = ms;
+                    gl = ls;
+                    go = os;
+                    continue;
+                }
+                const float Mx = fmaxf(gm, ms);
+                const float fa = expf(gm - Mx), fb = expf(ms - Mx);
+                gl = __fmaf_rn(gl, fa, __fmul_rn(ls, fb));
+                go = __fmaf_rn(go, fa, __fmul_rn(os, fb));
+                gm = Mx;
+            }
+        }
     }
-    const SoftAcc all = merge_warps(sm, a);
+    float* gst = wst;  // the warps' states are no longer needed: [grp][3] = m, l, o per dimension
+    csync();
+    if (grp >= 1 && grp < 3) {
+        gst[(grp - 1) * 3 * HD + dim] = gm;
+        gst[(grp - 1) * 3 * HD + HD + dim] = gl;
+        gst[(grp - 1) * 3 * HD + 2 * HD + dim] = go;
+    }
+    csync();
     trace_mark(P, 24, lslot(layer, 5));
-    if (warp == 0) {
-        uint64_t* d = P.attb[par] + h * HD + 4 * lane;
-        ll_store(d, __fdiv_rn(all.o.x, all.l), ep);
-        ll_store(d + 1, __fdiv_rn(all.o.y, all.l), ep);
-        ll_store(d + 2, __fdiv_rn(all.o.z, all.l), ep);
-        ll_store(d + 3, __fdiv_rn(all.o.w, all.l), ep);
+    if (t < HD) {
+        for (int k = 0; k < 2; ++k) {
+            const float ms = gst[k * 3 * HD + t], ls = gst[k * 3 * HD + HD + t], os = gst[k * 3 * HD + 2 * HD + t];
+            if (ls == 0.0f) continue;
+            if (gl == 0.0f) {
+                gm = ms;
+                gl = ls;
+                go = os;
+                continue;
+            }
+            const float Mx = fmaxf(gm, ms);
+            const float fa = expf(gm - Mx), fb = expf(ms - Mx);
+            gl = __fmaf_rn(gl, fa, __fmul_rn(ls, fb));
+            go = __fmaf_rn(go, fa, __fmul_rn(os, fb));
+            gm = Mx;
+        }
+        ll_store(P.attb[par] + h * HD + t, __fdiv_rn(go, gl), ep);
     }
     return ok;
 }
