@@ -276,6 +276,7 @@ __device__ __forceinline__ bool wait_seg(Smem& sm, const MegaArgs& P, uint32_t i
                 break;
             }
         }
+        __nanosleep(64);  // in case the hint returns early: keep waiting warps off the issue slots
     }
     if (tr) sm.wseg += clock64() - t0;
     return ok;
@@ -402,6 +403,7 @@ __device__ __forceinline__ bool prod_wait_release(Smem& sm, const MegaArgs& P, P
                     break;
                 }
             }
+            __nanosleep(256);  // the producer is ahead anyway: leave the issue slots to the consumers
         }
     }
     ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
