@@ -187,7 +187,10 @@ int stt_q4_tensor_destroy(stt_q4_tensor* t);
 /* out[rows, n] = input[rows, k] x W^T with f32 host buffers (rows = B*M of the reference). */
 int stt_q4_matmul(const stt_q4_tensor* w, const float* input, int rows, float* out);
 /* Device variant: d_input is f32 [rows, k] (in_dtype 0) or bf16 [rows, k] (in_dtype 1);
- * d_out is f32 [rows, n].  Queued on cuda_stream, no synchronisation. */
+ * d_out is f32 [rows, n].  Queued on cuda_stream, no synchronisation.
+ * in_dtype 2: f16 [rows, k] input (16-byte aligned, k a multiple of 64), computed on the tensor
+ * cores with the weights dequantised to f16 and f32 accumulation (the batched-stream product;
+ * its f16 operand rounding is the tolerance of the multi-stream path). */
 int stt_q4_matmul_device(const stt_q4_tensor* w, const void* d_input, int in_dtype, int rows,
                          float* d_out, void* cuda_stream);
 /* No counterpart in the reference.  Split-K form of stt_q4_matmul_device (same arguments plus

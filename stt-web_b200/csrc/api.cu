@@ -13,6 +13,7 @@
 #include "gguf.h"
 #include "kernels.h"
 #include "noalloc.h"
+#include "tc_gemm.h"
 #include "mega.h"
 
 namespace stt {
@@ -963,6 +964,7 @@ struct stt_q4_tensor {
     int num_sms = 148;
     Q4Dev w{};
     void* mem = nullptr;
+    int* d_err = nullptr;  // timeout flag of the tensor-core kernel (inside mem)
 };
 
 extern "C" int stt_q4_tensor_create(const uint8_t* bytes, size_t n_bytes, int n, int k, int device, stt_q4_tensor** out) {
@@ -986,7 +988,8 @@ extern "C" int stt_q4_tensor_create(const uint8_t* bytes, size_t n_bytes, int n,
     CUDA_TRY(cudaGetDeviceProperties(&prop, device));
     t->num_sms = prop.multiProcessorCount;
     const size_t nib_bytes = (nblk * 16 + 255) / 256 * 256;
-    if (cudaMalloc(&t->mem, nib_bytes + nblk * 2) != cudaSuccess) {
+    const size_t sc_bytes = (nblk * 2 + 255) / 256 * 256;
+    if (cudaMalloc(&t->mem, nib_bytes + sc_bytes + 256) != cudaSuccess) {
         cudaGetLastError();
         return set_error(STT_E_OOM, "cannot allocate Q4 tensor");
     }
@@ -994,6 +997,8 @@ extern "C" int stt_q4_tensor_create(const uint8_t* bytes, size_t n_bytes, int n,
     t->w.scale = reinterpret_cast<const uint16_t*>(static_cast<uint8_t*>(t->mem) + nib_bytes);
     t->w.n = n;
     t->w.k = k;
+    t->d_err = reinterpret_cast<int*>(static_cast<uint8_t*>(t->mem) + nib_bytes + sc_bytes);
+    CUDA_TRY(cudaMemset(t->d_err, 0, sizeof(int)));
     DevBuf staging;
     TRY(staging.ensure(n_bytes));
     CUDA_TRY(cudaMemcpy(staging.p, bytes, n_bytes, cudaMemcpyHostToDevice));
@@ -1017,10 +1022,19 @@ extern "C" int stt_q4_tensor_destroy(stt_q4_tensor* t) {
 
 extern "C" int stt_q4_matmul_device(const stt_q4_tensor* t, const void* d_in, int in_dtype, int rows, float* d_out,
                                     void* cuda_stream) {
-    if (!t || !d_in || !d_out || rows < 0 || (in_dtype != 0 && in_dtype != 1))
+    if (!t || !d_in || !d_out || rows < 0 || in_dtype < 0 || in_dtype > 2)
         return set_error(STT_E_INVALID_ARG, "bad arguments");
     if (rows == 0) return STT_OK;
     DeviceScope ds(t->device);
+    if (in_dtype == 2) {
+        if (!tc_gemm_supported(t->w))
+            return set_error(STT_E_INVALID_ARG, "f16 input needs in_features a multiple of 64, got %d", t->w.k);
+        if (reinterpret_cast<uintptr_t>(d_in) % 16 != 0)
+            return set_error(STT_E_INVALID_ARG, "f16 input must be 16-byte aligned");
+        CUDA_TRY(launch_q4_tc_gemm(t->w, static_cast<const __half*>(d_in), rows, d_out, t->w.n, t->d_err,
+                                   static_cast<cudaStream_t>(cuda_stream)));
+        return STT_OK;
+    }
     Ctx c{};
     GemvArgs a{};
     a.W = t->w;

@@ -100,3 +100,25 @@ def test_q4_matmul_bf16_input():
     torch.cuda.synchronize()
     ref = O.q4_matmul(raw, n, k, x.float().numpy())
     assert np.abs(out.cpu().numpy() - ref).max() <= 2e-6 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("n,k", SHAPES)
+@pytest.mark.parametrize("m", [1, 16, 64, 200])
+def test_q4_matmul_tensor_cores_f16_input(n, k, m):
+    """in_dtype 2: tcgen05 MMAs on f16 operands (weights dequantised to f16, f32 accumulation).
+    Each weight rounds by at most 2^-11 relative, so the dot products agree with the exact f32
+    product to ~1e-4 of their scale; the bound is 2e-3 of the largest output."""
+    import torch
+    from stt_b200._lib import lib
+    raw = q4_bytes(n, k, 3 * n + k + m)
+    t = stt_b200.Q4Tensor.from_q4_bytes(raw, (n, k))
+    x = torch.from_numpy(np.random.default_rng(m + n).standard_normal((m, k)).astype(np.float32)).to(torch.float16)
+    dx = x.cuda()
+    out = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    rc = lib().stt_q4_matmul_device(t._h, dx.data_ptr(), 2, m, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib().stt_last_error().decode()
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    ref = O.q4_matmul(raw, n, k, x.float().numpy())
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() <= 2e-3 * np.abs(ref).max(), np.abs(got - ref).max() / np.abs(ref).max()
