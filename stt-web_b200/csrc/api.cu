@@ -496,6 +496,8 @@ struct stt_streams {
     // scratch, sized for S batch rows
     float *d_x = nullptr, *d_qkv = nullptr, *d_attn = nullptr, *d_hid = nullptr, *d_logits = nullptr, *d_part = nullptr;
     uint32_t* d_tickets = nullptr;
+    __half* d_x16 = nullptr;  // f16 GEMM inputs of a batched step on the tensor cores
+    int* d_tc_err = nullptr;  // timeout word of the tensor-core kernels
     int32_t* d_ids = nullptr;
     StepDesc* d_desc = nullptr;
     DevBuf in_audio, in_text, out_tokens, out_logits, mega_xa;
@@ -560,29 +562,34 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
     stt_model* m = s->m;
     const Ctx c = make_ctx(s, n);
     const int grid = 2 * m->num_sms;
+    // batches of kTcMinBatch streams or more: layer products on the tensor cores (f16 operands)
+    const bool tc = n >= kTcMinBatch && m->D % 64 == 0 && m->F % 64 == 0 && std::getenv("STT_DISABLE_TC") == nullptr;
+    auto layer = [&](const GemvArgs& a, int epi) -> cudaError_t {
+        return tc ? launch_tc_layer(c, a, epi, n, s->d_x16, s->d_tc_err, st) : launch_gemv(c, a, epi, n, grid, st);
+    };
     CUDA_TRY(launch_embed(c, st));
     for (int l = 0; l < m->L; ++l) {
         const LayerDev& L = m->h_layers[l];
         GemvArgs a{};
         a.W = L.qkv; a.in = s->d_x; a.norm = L.norm1; a.out = s->d_qkv; a.ldo = 3 * m->D; a.layer = l;
         a.n_units = 3 * m->D / 2;
-        CUDA_TRY(launch_gemv(c, a, EPI_QKV, n, grid, st));
+        CUDA_TRY(layer(a, EPI_QKV));
         CUDA_TRY(launch_attention(c, l, st));
         a = GemvArgs{};
         a.W = L.out; a.in = s->d_attn; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
-        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, grid, st));
+        CUDA_TRY(layer(a, EPI_RESID));
         a = GemvArgs{};
         a.W = L.fin; a.in = s->d_x; a.norm = L.norm2; a.out = s->d_hid; a.ldo = m->F; a.n_units = m->F;
         a.half_n = m->F;
-        CUDA_TRY(launch_gemv(c, a, EPI_GATE, n, grid, st));
+        CUDA_TRY(layer(a, EPI_GATE));
         a = GemvArgs{};
         a.W = L.fout; a.in = s->d_hid; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
-        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, grid, st));
+        CUDA_TRY(layer(a, EPI_RESID));
     }
     GemvArgs a{};
     a.W = m->head; a.in = s->d_x; a.norm = m->out_norm; a.out = s->d_logits; a.ldo = m->V;
     a.n_units = (m->V + 1) / 2;
-    CUDA_TRY(launch_gemv(c, a, EPI_LOGITS, n, grid, st));
+    CUDA_TRY(layer(a, EPI_LOGITS));
     CUDA_TRY(launch_finish(c, st));
     return STT_OK;
 }
@@ -764,6 +771,8 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     const size_t o_desc = take(sizeof(StepDesc) + S * 4 + 64);
     const size_t o_mega = take(mega_scratch_bytes(m->num_sms, m->D, m->F, m->V, m->H, m->HD));
     const size_t o_trace = take(kTraceCap * sizeof(unsigned long long));
+    const size_t o_x16 = take(2 * S * (size_t)std::max(m->D, m->F) * sizeof(__half));  // hi and lo parts
+    const size_t o_tc_err = take(sizeof(int));
     const size_t o_trace_ctas = take((size_t)m->num_sms * kTraceSlots * sizeof(unsigned long long));
     if (cudaMalloc(&s->d_scratch, off) != cudaSuccess) {
         cudaGetLastError();
@@ -789,6 +798,8 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     s->mega.scratch_bytes = mega_scratch_bytes(m->num_sms, m->D, m->F, m->V, m->H, m->HD);
     s->mega.trace = reinterpret_cast<unsigned long long*>(b + o_trace);
     s->mega.trace_cap = kTraceCap;
+    s->d_x16 = reinterpret_cast<__half*>(b + o_x16);
+    s->d_tc_err = reinterpret_cast<int*>(b + o_tc_err);
     s->mega.trace_ctas = reinterpret_cast<unsigned long long*>(b + o_trace_ctas);
     s->mega.trace_slots = kTraceSlots;
     CUDA_TRY(cudaMemset(s->d_scratch, 0, off));

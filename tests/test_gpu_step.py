@@ -246,3 +246,85 @@ def test_persistent_kernel_barrier_and_trace(full_model):
     assert tags[0] == 0 and tags[-1] == 0  # wall-clock pairs around the frame
     t = np.array([buf[2 * i + 1] for i in marks], dtype=np.int64)
     assert np.all(np.diff(t) >= 0)
+
+
+TC_TIE = 5e-2  # near-ties below this margin may flip under f16 operand rounding
+
+
+@pytest.mark.parametrize("kv", ["bf16", "f32"])
+def test_batched_tensor_core_path_matches_oracle(tiny_ref_gguf, kv):
+    """Batches of 16+ streams run their layer products on the tensor cores with f16 operands:
+    logits within the 2e-2 bound of the oracle, tokens equal away from near-ties."""
+    cfg = tiny_cfg(sliding_window=12)
+    model = stt_b200.SttModel.from_shards([tiny_ref_gguf], config=cfg)
+    n = 20
+    cache = model.create_cache(n, kv)
+    om = oracle_for(tiny_ref_gguf, cfg)
+    refs = [om.stream(0 if kv == "f32" else O.KV_BF16) for _ in range(n)]
+    rng = np.random.default_rng(9)
+    for s in range(n):  # staggered positions, some past the ring size
+        for _ in range(s % 7 + (s // 7) * 6):
+            f = rng.integers(0, 300, 4)
+            model.forward(f, 5, cache, s)
+            refs[s].forward(f, 5)
+    order = list(rng.permutation(n))
+    texts = [1000] * n
+    worst = 0.0
+    for step in range(8):
+        audio = rng.integers(0, 300, (n, 4))
+        lg, am = cache.forward(order, audio, [texts[s] for s in order])
+        for i, s in enumerate(order):
+            lo, ao = refs[s].forward(audio[i], texts[s])
+            worst = max(worst, float(np.abs(lg[i] - lo).max()))
+            if margin(lo) > TC_TIE:
+                assert am[i] == ao
+            texts[s] = ao
+    assert worst < LOGIT_TOL, worst
+
+
+def test_full_size_batched_tensor_core_path(full_model):
+    g, model = full_model
+    n = 16
+    cache = model.create_cache(n, "bf16")
+    om = oracle_for(g.array, SttConfig())
+    refs = [om.stream(O.KV_BF16) for _ in range(n)]
+    ids = list(range(n))
+    texts = [0] * n
+    worst = 0.0
+    for step in range(3):
+        audio = np.stack([stt_b200.audio_tokens(11, s, 1, first_frame=step)[0] for s in ids])
+        lg, am = cache.forward(ids, audio, texts)
+        for s in ids:
+            lo, ao = refs[s].forward(audio[s], texts[s])
+            worst = max(worst, float(np.abs(lg[s] - lo).max()))
+            if margin(lo) > TC_TIE:
+                assert am[s] == ao
+            texts[s] = ao
+    assert worst < LOGIT_TOL, worst
+
+
+def test_tensor_core_and_gemv_batches_agree(monkeypatch):
+    """The same 16-stream batch through the tensor cores and through the GEMV (STT_DISABLE_TC)."""
+    spec = stt_b200.SynthSpec(seed=24, num_layers=2, hidden_size=256, num_heads=2, ffn_hidden=512, vocab_size=1000,
+                              text_in_vocab_size=1001, num_codebooks=4, audio_vocab_size=300)
+    g = stt_b200.synth_gguf(spec)
+    cfg = tiny_cfg()
+    model = stt_b200.SttModel.from_shards([g.array], config=cfg)
+    n = 16
+    frames = np.random.default_rng(12).integers(0, 300, (6, n, 4))
+    outs = []
+    for disable in (False, True):
+        if disable:
+            monkeypatch.setenv("STT_DISABLE_TC", "1")
+        cache = model.create_cache(n, "bf16")
+        toks, lgs = [], []
+        texts = [1000] * n
+        for f in frames:
+            lg, am = cache.forward(list(range(n)), f, texts)
+            lgs.append(lg)
+            toks.append(list(am))
+            texts = [int(a) for a in am]
+        outs.append((toks, np.stack(lgs)))
+        cache.close()
+    monkeypatch.delenv("STT_DISABLE_TC")
+    assert np.abs(outs[0][1] - outs[1][1]).max() < LOGIT_TOL
