@@ -79,6 +79,11 @@ typedef struct stt_model_info {
     int32_t device;
     uint64_t q4_weight_bytes;    /* Q4_0 bytes one decode step reads (all linear layers)   */
     uint64_t device_bytes;       /* total device memory held by the model                  */
+    int32_t tensor_core_min_batch; /* batches of at least this many streams run their Q4
+                                    * products on the tensor cores; 0 when the weights do not
+                                    * fit that path (in_features not a multiple of 256, or a
+                                    * Q4_0 scale of magnitude above 4) */
+    int32_t reserved;
 } stt_model_info;
 
 /* ---------------------------------------------------------------------------------------
@@ -188,9 +193,10 @@ int stt_q4_tensor_destroy(stt_q4_tensor* t);
 int stt_q4_matmul(const stt_q4_tensor* w, const float* input, int rows, float* out);
 /* Device variant: d_input is f32 [rows, k] (in_dtype 0) or bf16 [rows, k] (in_dtype 1);
  * d_out is f32 [rows, n].  Queued on cuda_stream, no synchronisation.
- * in_dtype 2: f16 [rows, k] input (16-byte aligned, k a multiple of 64), computed on the tensor
- * cores with the weights dequantised to f16 and f32 accumulation (the batched-stream product;
- * its f16 operand rounding is the tolerance of the multi-stream path). */
+ * in_dtype 2: f16 [rows, k] input (k a multiple of 256, Q4_0 scales of magnitude at most 4),
+ * computed on the tensor cores with each dequantised weight split exactly into two f16 parts and
+ * f32 accumulation (the batched-stream product).  Its scratch is kept with the tensor and grows
+ * on demand: a call with more rows than any before it may allocate (and so synchronise). */
 int stt_q4_matmul_device(const stt_q4_tensor* w, const void* d_input, int in_dtype, int rows,
                          float* d_out, void* cuda_stream);
 /* No counterpart in the reference.  Split-K form of stt_q4_matmul_device (same arguments plus

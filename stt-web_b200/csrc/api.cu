@@ -128,6 +128,7 @@ struct stt_model {
     Q4Dev head{};
     const float* out_norm = nullptr;
     const float2* rope = nullptr;
+    bool tc_ok = false;  // every layer product and the head fit the tensor-core path
     const uint8_t* emb_audio = nullptr;
     const uint8_t* emb_text = nullptr;
     float attn_scale = 0.0f;
@@ -401,9 +402,11 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
         TRY(staging.ensure(max_raw));
         std::vector<uint8_t> scratch;
         std::vector<Q4Dev> qd(q4s.size());
+        m->tc_ok = true;
         for (size_t i = 0; i < q4s.size(); ++i) {
             const uint8_t* src = g.tensor_data(*q4s[i], scratch);
             if (!src) return STT_E_FORMAT;
+            m->tc_ok = m->tc_ok && tc_gemm_scales_ok(src, (int64_t)(q4s[i]->numel / 32));
             CUDA_TRY(cudaMemcpy(staging.p, src, q4s[i]->nbytes, cudaMemcpyHostToDevice));
             const auto s = q4s[i]->shape();
             qd[i].nib = reinterpret_cast<const uint4*>(base + off_nib[i]);
@@ -426,6 +429,7 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
             L.norm2 = dn + (size_t)(2 * l + 1) * m->D;
         }
         m->head = qd.back();
+        for (const Q4Dev& w : qd) m->tc_ok = m->tc_ok && tc_gemm_supported(w);
         m->out_norm = dn + (size_t)(2 * m->L) * m->D;
     }
     CUDA_TRY(cudaMemcpy(base + off_norms, norms.data(), norms.size() * sizeof(float), cudaMemcpyHostToDevice));
@@ -479,6 +483,8 @@ extern "C" int stt_model_get_info(const stt_model* m, stt_model_info* o) {
     o->device = m->device;
     o->q4_weight_bytes = m->q4_bytes;
     o->device_bytes = m->device_bytes;
+    o->tensor_core_min_batch = m->tc_ok ? kTcMinBatch : 0;
+    o->reserved = 0;
     return STT_OK;
 }
 
@@ -496,8 +502,9 @@ struct stt_streams {
     // scratch, sized for S batch rows
     float *d_x = nullptr, *d_qkv = nullptr, *d_attn = nullptr, *d_hid = nullptr, *d_logits = nullptr, *d_part = nullptr;
     uint32_t* d_tickets = nullptr;
-    __half* d_x16 = nullptr;  // f16 GEMM inputs of a batched step on the tensor cores
-    int* d_tc_err = nullptr;  // timeout word of the tensor-core kernels
+    __half* d_x16 = nullptr;    // f16 GEMM inputs of a batched step on the tensor cores
+    float* d_tc_part = nullptr; // their K-slice partial sums
+    int* d_tc_err = nullptr;    // timeout word of the tensor-core kernels
     int32_t* d_ids = nullptr;
     StepDesc* d_desc = nullptr;
     DevBuf in_audio, in_text, out_tokens, out_logits, mega_xa;
@@ -563,9 +570,10 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
     const Ctx c = make_ctx(s, n);
     const int grid = 2 * m->num_sms;
     // batches of kTcMinBatch streams or more: layer products on the tensor cores (f16 operands)
-    const bool tc = n >= kTcMinBatch && m->D % 64 == 0 && m->F % 64 == 0 && std::getenv("STT_DISABLE_TC") == nullptr;
+    const bool tc = n >= kTcMinBatch && m->tc_ok && std::getenv("STT_DISABLE_TC") == nullptr;
     auto layer = [&](const GemvArgs& a, int epi) -> cudaError_t {
-        return tc ? launch_tc_layer(c, a, epi, n, s->d_x16, s->d_tc_err, st) : launch_gemv(c, a, epi, n, grid, st);
+        return tc ? launch_tc_layer(c, a, epi, n, s->d_x16, s->d_tc_part, s->d_tc_err, m->num_sms, st)
+                  : launch_gemv(c, a, epi, n, grid, st);
     };
     CUDA_TRY(launch_embed(c, st));
     for (int l = 0; l < m->L; ++l) {
@@ -771,7 +779,18 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     const size_t o_desc = take(sizeof(StepDesc) + S * 4 + 64);
     const size_t o_mega = take(mega_scratch_bytes(m->num_sms, m->D, m->F, m->V, m->H, m->HD));
     const size_t o_trace = take(kTraceCap * sizeof(unsigned long long));
-    const size_t o_x16 = take(2 * S * (size_t)std::max(m->D, m->F) * sizeof(__half));  // hi and lo parts
+    // tensor-core products of batches kTcMinBatch .. S: tiled f16 inputs and K-slice partial sums
+    size_t x16_bytes = 0, tc_part_bytes_max = 0;
+    if (m->tc_ok)
+        for (int rows = kTcMinBatch; rows <= n_streams; ++rows) {
+            x16_bytes = std::max(x16_bytes, tc_x16_bytes(std::max(m->D, m->F), rows));
+            for (const LayerDev& L : m->h_layers)
+                for (const Q4Dev* w : {&L.qkv, &L.out, &L.fin, &L.fout})
+                    tc_part_bytes_max = std::max(tc_part_bytes_max, tc_part_bytes(*w, rows, m->num_sms));
+            tc_part_bytes_max = std::max(tc_part_bytes_max, tc_part_bytes(m->head, rows, m->num_sms));
+        }
+    const size_t o_x16 = take(x16_bytes);
+    const size_t o_tc_part = take(tc_part_bytes_max);
     const size_t o_tc_err = take(sizeof(int));
     const size_t o_trace_ctas = take((size_t)m->num_sms * kTraceSlots * sizeof(unsigned long long));
     if (cudaMalloc(&s->d_scratch, off) != cudaSuccess) {
@@ -799,6 +818,7 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     s->mega.trace = reinterpret_cast<unsigned long long*>(b + o_trace);
     s->mega.trace_cap = kTraceCap;
     s->d_x16 = reinterpret_cast<__half*>(b + o_x16);
+    s->d_tc_part = reinterpret_cast<float*>(b + o_tc_part);
     s->d_tc_err = reinterpret_cast<int*>(b + o_tc_err);
     s->mega.trace_ctas = reinterpret_cast<unsigned long long*>(b + o_trace_ctas);
     s->mega.trace_slots = kTraceSlots;
@@ -976,6 +996,8 @@ struct stt_q4_tensor {
     Q4Dev w{};
     void* mem = nullptr;
     int* d_err = nullptr;  // timeout flag of the tensor-core kernel (inside mem)
+    bool tc_ok = false;    // shape and scales fit the tensor-core kernel
+    mutable DevBuf tc_x16, tc_part;  // its scratch, grown on demand
 };
 
 extern "C" int stt_q4_tensor_create(const uint8_t* bytes, size_t n_bytes, int n, int k, int device, stt_q4_tensor** out) {
@@ -1009,6 +1031,7 @@ extern "C" int stt_q4_tensor_create(const uint8_t* bytes, size_t n_bytes, int n,
     t->w.n = n;
     t->w.k = k;
     t->d_err = reinterpret_cast<int*>(static_cast<uint8_t*>(t->mem) + nib_bytes + sc_bytes);
+    t->tc_ok = tc_gemm_supported(t->w) && tc_gemm_scales_ok(bytes, (int64_t)nblk);
     CUDA_TRY(cudaMemset(t->d_err, 0, sizeof(int)));
     DevBuf staging;
     TRY(staging.ensure(n_bytes));
@@ -1039,11 +1062,16 @@ extern "C" int stt_q4_matmul_device(const stt_q4_tensor* t, const void* d_in, in
     DeviceScope ds(t->device);
     if (in_dtype == 2) {
         if (!tc_gemm_supported(t->w))
-            return set_error(STT_E_INVALID_ARG, "f16 input needs in_features a multiple of 64, got %d", t->w.k);
-        if (reinterpret_cast<uintptr_t>(d_in) % 16 != 0)
-            return set_error(STT_E_INVALID_ARG, "f16 input must be 16-byte aligned");
-        CUDA_TRY(launch_q4_tc_gemm(t->w, static_cast<const __half*>(d_in), rows, d_out, t->w.n, t->d_err,
-                                   static_cast<cudaStream_t>(cuda_stream)));
+            return set_error(STT_E_INVALID_ARG, "f16 input needs in_features a multiple of 256, got %d", t->w.k);
+        if (!t->tc_ok)
+            return set_error(STT_E_INVALID_ARG, "f16 input needs Q4_0 scales of magnitude at most 4");
+        if (reinterpret_cast<uintptr_t>(d_in) % 2 != 0)
+            return set_error(STT_E_INVALID_ARG, "f16 input must be 2-byte aligned");
+        TRY(t->tc_x16.ensure(tc_x16_bytes(t->w.k, rows)));
+        TRY(t->tc_part.ensure(tc_part_bytes(t->w, rows, t->num_sms)));
+        CUDA_TRY(launch_q4_tc_gemm(t->w, static_cast<const __half*>(d_in), rows, d_out, t->w.n,
+                                   static_cast<__half*>(t->tc_x16.p), static_cast<float*>(t->tc_part.p), t->d_err,
+                                   t->num_sms, static_cast<cudaStream_t>(cuda_stream)));
         return STT_OK;
     }
     Ctx c{};

@@ -11,6 +11,7 @@
 //   head       RMSNorm(out_norm) prologue                                  (model.rs:662-663)
 //   finish     argmax (lowest index on ties) and the stream-loop state update (stream.rs:90-107,
 //              231-266)
+#include <algorithm>
 #include <cfloat>
 
 #include "device.cuh"
@@ -284,6 +285,28 @@ __global__ void __launch_bounds__(256) gemv_kernel(Ctx c, GemvArgs a, int row0, 
                 if (lane == 0) epilogue<EPI>(c, a, row0 + m, ra, rb, va, vb);
             }
         }
+    }
+}
+
+// Epilogue of a tensor-core product: the K-slice partial sums part[z][m][W.n] of each output pair
+// are added in slice order (z = 0, 1, ...) and handed to the same epilogue as the GEMV's.
+template <int EPI>
+__global__ void __launch_bounds__(256) tc_epilogue_kernel(Ctx c, GemvArgs a, const float* __restrict__ part, int rows,
+                                                         int slices) {
+    const int64_t total = (int64_t)rows * a.n_units;
+    const int64_t plane = (int64_t)rows * a.W.n;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int m = (int)(i / a.n_units), u = (int)(i - (int64_t)m * a.n_units);
+        int ra, rb;
+        unit_rows<EPI>(a, u, &ra, &rb);
+        const float* p = part + (int64_t)m * a.W.n;
+        float va = p[ra], vb = rb >= 0 ? p[rb] : 0.0f;
+        for (int z = 1; z < slices; ++z) {
+            p += plane;
+            va = __fadd_rn(va, p[ra]);
+            if (rb >= 0) vb = __fadd_rn(vb, p[rb]);
+        }
+        epilogue<EPI>(c, a, m, ra, rb, va, vb);
     }
 }
 
@@ -592,6 +615,21 @@ cudaError_t launch_attention(const Ctx& c, int layer, cudaStream_t st) {
 
 cudaError_t launch_finish(const Ctx& c, cudaStream_t st) {
     finish_kernel<<<c.n, 1024, 0, st>>>(c);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tc_epilogue(const Ctx& c, const GemvArgs& a, int epi, int rows, const float* part, int slices,
+                               cudaStream_t st) {
+    const int64_t total = (int64_t)rows * a.n_units;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, 8192);
+    if (grid <= 0) return cudaSuccess;
+    switch (epi) {
+        case EPI_QKV: tc_epilogue_kernel<EPI_QKV><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
+        case EPI_GATE: tc_epilogue_kernel<EPI_GATE><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
+        case EPI_RESID: tc_epilogue_kernel<EPI_RESID><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
+        case EPI_LOGITS: tc_epilogue_kernel<EPI_LOGITS><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
+        default: tc_epilogue_kernel<EPI_PLAIN><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
+    }
     return cudaGetLastError();
 }
 

@@ -41,5 +41,9 @@ cudaError_t launch_gemv(const Ctx& c, const GemvArgs& a, int epi, int rows, int 
 cudaError_t launch_embed(const Ctx& c, cudaStream_t st);
 cudaError_t launch_attention(const Ctx& c, int layer, cudaStream_t st);
 cudaError_t launch_finish(const Ctx& c, cudaStream_t st);
+// Adds the K-slice partial sums part[slices][rows][a.W.n] of a tensor-core product in slice order
+// and applies the epilogue `epi` as launch_gemv does.
+cudaError_t launch_tc_epilogue(const Ctx& c, const GemvArgs& a, int epi, int rows, const float* part, int slices,
+                               cudaStream_t st);
 
 }  // namespace stt

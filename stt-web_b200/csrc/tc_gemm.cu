@@ -1,24 +1,43 @@
 // Q4_0 x f16 matmul on the 5th-generation tensor cores (tcgen05, accumulator in TMEM).
 //
-// out[m][n] = sum_k x[m][k] * w[n][k] for a batch of rows m (streams) and the Q4_0 weight rows n:
-// the product of q4_matmul (gguf.rs:517-578) on the f16 tensor cores with f32 accumulation.  Each
-// operand is split into two f16 parts, w = w_hi + w_lo and x = x_hi + x_lo, and three MMAs add
-// w_hi.x_hi + w_hi.x_lo + w_lo.x_hi: about 22 significant bits per product, close to the f32
-// reference.  The dequantised weight (nibble - 8) * scale is exact in f32; it is scaled by 2^10
-// (exact) before the split so that w_lo stays clear of f16 subnormals, and the accumulator is
-// scaled back in the epilogue.
+// part[z][m][n] = sum over the K slice z of x[m][k] * w[n][k], for a batch of rows m (streams)
+// and the Q4_0 weight rows n: the product of q4_matmul (gguf.rs:517-578) on the f16 tensor cores
+// with f32 accumulation.  An epilogue kernel (kernels.cu) then adds the slices in slice order and
+// applies the layer's epilogue, the same one the GEMV uses.
 //
-// One CTA computes 128 weight rows (the MMA's M, one TMEM lane each) for NT batch rows (the MMA's
-// N, one TMEM column each).  K advances in chunks of 64 (two Q4_0 blocks):
-//   - 128 threads dequantise one weight row each into shared memory (hi and lo parts), in the
-//     no-swizzle K-major "core matrix" layout of the MMA (8 rows x 16 bytes per 128-byte core
-//     matrix), and copy the chunk of the batch rows (hi and lo parts) the same way;
-//   - one thread issues 4 x 3 MMAs of 128 x NT x 16 and commits them to an mbarrier;
-//   - two buffers alternate, so the threads prepare chunk c+1 while the MMAs of chunk c run.
-// After the last chunk every warp reads its 32 TMEM lanes (tcgen05.ld 32x32b) and stores them.
-// Every wait is bounded; on a timeout the CTA records an error, waits (bounded) for its MMAs,
-// frees its TMEM and returns.
+// Precision.  Each operand is split into two f16 parts, w = w_hi + w_lo and x = x_hi + x_lo, and
+// three MMAs add w_hi.x_hi + w_hi.x_lo + w_lo.x_hi: about 22 significant bits per product, close
+// to the f32 reference.  The dequantised weight q * s (q = nibble - 8 in [-8, 7], s the block's
+// f16 scale) has at most 15 significant bits; it is formed in f16 as hi = rn(q * s') and
+// lo = rn(q * s' - hi) (one fused multiply-add), where s' = s * 2^10 keeps lo clear of f16
+// subnormals, so hi + lo = q * s' exactly.  The accumulator is scaled back by 2^-10 (exact).
+// Weights with |s| > 4 would overflow f16 and are not sent here (tc_gemm_scales_ok).
+//
+// K order.  A 16-byte word of four Q4_0 payload bytes yields, with one mask per nibble position,
+// the element pairs (4i, 4i+2), (4i+1, 4i+3), (16+4i, 16+4i+2), (16+4i+1, 16+4i+3) of its block;
+// those four pairs form one 8-element row piece of the MMA operand.  The MMA sums over K, so the
+// activations are stored in the same order (prep_f16_kernel) instead of shuffling the weights.
+//
+// Layout of the activations (x16): [part hi/lo][row tile of NT][64-wide chunk][NT x 64 f16 in the
+// MMA's no-swizzle K-major core-matrix order: 8 rows x 16 bytes per 128-byte core matrix, core
+// matrices along K 128 bytes apart, 8-row groups 1024 bytes apart], so one chunk of one part is a
+// single contiguous bulk copy of NT * 128 bytes.
+//
+// Grid: (weight-row tiles of 128, batch-row tiles of NT, K slices).  A CTA of 256 threads:
+//   - warp 7 bulk-copies (cp.async.bulk) its slice of the 128 weight rows into shared memory, one
+//     copy of nibbles and one of scales per row, all on one mbarrier;
+//   - thread 0 bulk-copies the activation chunks into a ring of B stages, two chunks ahead when
+//     the ring has four stages;
+//   - per 64-wide chunk, two threads per weight row dequantise one Q4_0 block each into the A
+//     operand (hi and lo parts, two buffers), and thread 0 issues 4 x 3 MMAs of 128 x NT x 16
+//     and commits them to an mbarrier;
+//   - each warp reads 32 TMEM lanes (tcgen05.ld 32x32b) for half of the batch columns and stores
+//     the partial sums.
+// Every wait is bounded; on a timeout the CTA stops issuing, records an error, waits (bounded) for
+// its MMAs and copies in flight, frees its TMEM and returns.
 #include "tc_gemm.h"
+
+#include <algorithm>
 
 #include "kernels.h"
 
@@ -26,12 +45,17 @@ namespace stt {
 
 namespace {
 
-constexpr int kTM = 128;          // weight rows per CTA (MMA M)
-constexpr int kKC = 64;           // K elements per chunk
-constexpr int kThreads = 128;     // one thread per weight row; warp w owns TMEM lanes 32w..32w+31
+constexpr int kTM = 128;            // weight rows per CTA (MMA M, one TMEM lane each)
+constexpr int kKC = 64;             // K elements per chunk (two Q4_0 blocks)
+constexpr int kQuad = 256;          // K granule of a slice: 8 blocks, so scale copies stay 16-byte sized
+constexpr int kMaxQuads = 4;        // quads per slice held in shared memory (1024 K)
+constexpr int kThreads = 256;
+constexpr int kNibStride = kMaxQuads * 8 * 16 + 16;  // bytes per weight row, padded against bank conflicts
+constexpr int kScStride = kMaxQuads * 8 * 2 + 16;
 constexpr uint32_t kSpin = 1u << 22;
-constexpr float kWScale = 1024.0f;          // weights enter the MMA scaled by 2^10
 constexpr float kWUnscale = 1.0f / 1024.0f;
+
+__host__ __device__ constexpr int b_stages(int nt) { return nt >= 128 ? 2 : 4; }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -75,6 +99,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity) {
         if (mbar_try(m, parity)) return true;
     return false;
 }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* m, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
+}
+// Bulk copy global -> this CTA's shared memory, completing `bytes` on the mbarrier (no multicast).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(m))
+        : "memory");
+}
 
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
     asm volatile(
@@ -89,7 +123,7 @@ __device__ __forceinline__ void mma_commit(uint64_t* m) {
                  : "memory");
 }
 
-// 16 consecutive f32 columns of this thread's TMEM lane.
+// 16 consecutive f32 columns of this thread's TMEM lane, scaled back by 2^-10.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
     asm volatile(
@@ -105,44 +139,84 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 
 template <int NT>
 struct TcSmem {
-    alignas(128) uint8_t a[2][2][kTM * kKC * 2];  // [buffer][hi, lo] dequantised weights, core-matrix layout
-    alignas(128) uint8_t b[2][2][NT * kKC * 2];   // [buffer][hi, lo] batch rows
-    alignas(8) uint64_t mbar[2];
+    alignas(128) uint8_t a[2][2][kTM * kKC * 2];           // [buffer][hi, lo] weights, core-matrix layout
+    alignas(128) uint8_t b[b_stages(NT)][2][NT * kKC * 2];  // [stage][hi, lo] activations, same layout
+    alignas(128) uint8_t nib[kTM * kNibStride];             // the slice's Q4_0 nibbles, row after row
+    alignas(128) uint8_t sc[kTM * kScStride];               // and its scales
+    alignas(8) uint64_t raw_bar;
+    alignas(8) uint64_t b_full[b_stages(NT)];
+    alignas(8) uint64_t mma_done[4];                        // chunk c commits to mma_done[c % 4]
     uint32_t tmem;
-    int32_t ok;
-    float gv[64][17];  // EPI_GATE: the value rows' results, handed to the gate rows
-    int2 pos[NT];      // EPI_QKV: (RoPE position, ring slot) of each batch row of the tile
 };
 
-// byte offset of element (row, k) of a [rows x 64] K-major chunk in the core-matrix layout:
-// core matrix (row / 8, k / 8) at ((row / 8) * 8 + k / 8) * 128, row % 8 at 16-byte steps
-__device__ __forceinline__ uint32_t core_off(int row, int k8) { return ((row >> 3) * 8 + k8) * 128 + (row & 7) * 16; }
-
-// Weight row of tile row t: consecutive rows, or for the gate epilogue 64 gate rows followed by
-// their 64 value rows (rows u and u + half_n of linear_in).
-template <int EPI>
-__device__ __forceinline__ int tile_row(int tile, int t, int half_n) {
-    if (EPI == EPI_GATE) return t < 64 ? tile * 64 + t : half_n + tile * 64 + (t - 64);
-    return tile * kTM + t;
+// byte offset of 8-element piece k8 of row `row` of a [rows x 64] K-major chunk in core-matrix
+// order: core matrix (row / 8, k8) at ((row / 8) * 8 + k8) * 128, row % 8 at 16-byte steps
+__host__ __device__ __forceinline__ uint32_t core_off(int row, int k8) {
+    return ((row >> 3) * 8 + k8) * 128 + (row & 7) * 16;
 }
 
-// x holds the hi parts [M][K], then (x_lo != 0) the lo parts [M][K]; without lo parts the input
-// is taken as exact f16 and the hi.lo product is skipped.
-template <int NT, int EPI>
-__global__ void __launch_bounds__(kThreads) q4_tc_kernel(Q4Dev w, const __half* __restrict__ x, int x_lo, int M,
-                                                       float* __restrict__ out, int64_t ldo, int* __restrict__ err, Ctx c,
-                                                       GemvArgs ga) {
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) {
+    __half2 h;
+    memcpy(&h, &u, 4);
+    return h;
+}
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) {
+    uint32_t u;
+    memcpy(&u, &h, 4);
+    return u;
+}
+
+// Dequantises one Q4_0 block (16 payload bytes, scale bits sbits) into four 8-element pieces of
+// hi parts and four of lo parts, in the K order described at the top of this file.
+__device__ __forceinline__ void dequant_block(uint4 q, uint16_t sbits, uint4 (&hi)[4], uint4 (&lo)[4]) {
+    // s * 2^10 is exact in f16 for every |s| <= 4
+    const __half2 s2 = __half2half2(__hmul(__ushort_as_half(sbits), __ushort_as_half(0x6400)));
+    const __half2 bias = u32_as_h2(0x64086408u);  // 1032 = 1024 + 8 in both halves
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi) {
+        const uint32_t w = words[wi];
+        // 0x6400 | n is the f16 value 1024 + n; minus 1032 gives n - 8 exactly
+        const uint32_t u[4] = {(w & 0x000F000Fu) | 0x64006400u, ((w >> 8) & 0x000F000Fu) | 0x64006400u,
+                               ((w >> 4) & 0x000F000Fu) | 0x64006400u, ((w >> 12) & 0x000F000Fu) | 0x64006400u};
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half2 qv = __hsub2(u32_as_h2(u[j]), bias);
+            const __half2 hv = __hmul2_rn(qv, s2);
+            h[j] = h2_as_u32(hv);
+            l[j] = h2_as_u32(__hfma2(qv, s2, __hneg2(hv)));  // the exact remainder q * s' - hi
+        }
+        hi[wi] = make_uint4(h[0], h[1], h[2], h[3]);
+        lo[wi] = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+// x16 holds the hi parts, then (x_lo != 0) the lo parts, in the tiled order above; without lo
+// parts the input is taken as exact f16 and the hi.lo product is skipped.  Slice z covers the
+// quads [z * nq / slices, (z + 1) * nq / slices) of K.  part: [slices][M][w.n].
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(Q4Dev w, const __half* __restrict__ x16, int x_lo, int M,
+                                                          int mtiles, int slices, float* __restrict__ part,
+                                                          int* __restrict__ err) {
     extern __shared__ __align__(128) uint8_t tc_raw[];
     TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(tc_raw);
+    constexpr int NBS = b_stages(NT);
     constexpr uint32_t kCols = NT < 32 ? 32 : NT;  // TMEM columns (a power of two >= 32)
+    constexpr uint32_t kBBytes = NT * kKC * 2;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int m0 = blockIdx.y * NT;
-    const int K = w.k, NB = K >> 5, nchunks = K / kKC;
+    const int n0 = blockIdx.x * kTM, mt = blockIdx.y, z = blockIdx.z;
+    const int K = w.k, NB = K >> 5, nch = K / kKC, nq = K / kQuad;
+    const int q0 = (int)((int64_t)z * nq / slices), q1 = (int)((int64_t)(z + 1) * nq / slices);
+    const int c0 = q0 * 4, nchunks = (q1 - q0) * 4, sb = (q1 - q0) * 8;
+    const int rows = min(kTM, w.n - n0);
+    const int64_t part_elems = (int64_t)mtiles * NT * K;  // f16 elements per part of x16
+    const __half* xb = x16 + ((int64_t)mt * nch + c0) * (NT * kKC);
     if (t == 0) {
-        mbar_init(&sm.mbar[0]);
-        mbar_init(&sm.mbar[1]);
+        mbar_init(&sm.raw_bar);
+        for (int i = 0; i < NBS; ++i) mbar_init(&sm.b_full[i]);
+        for (int i = 0; i < 4; ++i) mbar_init(&sm.mma_done[i]);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        sm.ok = 1;
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem)),
@@ -154,204 +228,173 @@ __global__ void __launch_bounds__(kThreads) q4_tc_kernel(Q4Dev w, const __half* 
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = sm.tmem;
+    // the weight slice: one nibble copy and one scale copy per row (both multiples of 16 bytes)
+    if (warp == 7) {
+        if (lane == 0) mbar_expect_tx(&sm.raw_bar, (uint32_t)rows * sb * 18u);
+        __syncwarp();
+        for (int r = lane; r < rows; r += 32) {
+            const int64_t blk = (int64_t)(n0 + r) * NB + q0 * 8;
+            bulk_g2s(sm.nib + r * kNibStride, w.nib + blk, (uint32_t)sb * 16u, &sm.raw_bar);
+            bulk_g2s(sm.sc + r * kScStride, w.scale + blk, (uint32_t)sb * 2u, &sm.raw_bar);
+        }
+    }
+    // thread 0: activation chunk j -> stage j % NBS
+    int issued = 0;
+    auto issue_b = [&](int j) {
+        uint64_t* fb = &sm.b_full[j % NBS];
+        mbar_expect_tx(fb, (1u + (x_lo ? 1u : 0u)) * kBBytes);
+        bulk_g2s(sm.b[j % NBS][0], xb + (int64_t)j * (NT * kKC), kBBytes, fb);
+        if (x_lo) bulk_g2s(sm.b[j % NBS][1], xb + part_elems + (int64_t)j * (NT * kKC), kBBytes, fb);
+        issued = j + 1;
+    };
+    if (t == 0)
+        for (int j = 0; j < NBS - 2 && j < nchunks; ++j) issue_b(j);
+    bool ok = mbar_wait(&sm.raw_bar, 0);
+    const int row = t & (kTM - 1), bb = t >> 7;  // this thread's weight row and block of each chunk
     const uint32_t idesc = instr_desc_f16(kTM, NT);
-    const int row = tile_row<EPI>(blockIdx.x, t, ga.half_n);  // this thread's weight row
-    bool ok = true;
+    int committed = 0;  // chunks whose MMAs are committed (tracked by every thread)
     for (int c = 0; c < nchunks; ++c) {
         const int buf = c & 1;
-        if (c >= 2 && !mbar_wait(&sm.mbar[buf], ((c >> 1) - 1) & 1)) ok = false;  // MMAs of chunk c-2 are done
-        // weights: two Q4_0 blocks of this row -> 64 values, each split into f16 hi and lo parts
+        // the A buffer and the B stage refilled now were read by the MMAs of chunk c - 2
+        if (c >= 2 && !mbar_wait(&sm.mma_done[(c - 2) & 3], ((c - 2) >> 2) & 1)) ok = false;
+        if (t == 0 && ok && c + NBS - 2 < nchunks && c + NBS - 2 >= issued) issue_b(c + NBS - 2);
         uint8_t* Ah = sm.a[buf][0];
         uint8_t* Al = sm.a[buf][1];
-        if (row < w.n) {
-            const int b0 = c * 2;
+        if (row < rows) {
+            const int blk = c * 2 + bb;  // block within the slice
+            const uint4 q = *reinterpret_cast<const uint4*>(sm.nib + row * kNibStride + blk * 16);
+            const uint16_t sbits = *reinterpret_cast<const uint16_t*>(sm.sc + row * kScStride + blk * 2);
+            uint4 hi[4], lo[4];
+            dequant_block(q, sbits, hi, lo);
 #pragma unroll
-            for (int bb = 0; bb < 2; ++bb) {
-                const uint4 q = __ldg(w.nib + (int64_t)row * NB + b0 + bb);
-                const float d = __fmul_rn(f16_to_f32_ieee(__ldg(w.scale + (int64_t)row * NB + b0 + bb)), kWScale);
-                const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-                // element e of the block: e < 16 low nibble of byte e, e >= 16 high nibble of byte e-16
-                __half hv[32], lv[32];
-#pragma unroll
-                for (int wi = 0; wi < 4; ++wi)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint32_t byte = (words[wi] >> (8 * i)) & 0xFFu;
-                        const float wl = __fmul_rn(nib_m8(byte & 0xFu), d), wh = __fmul_rn(nib_m8(byte >> 4), d);
-                        const __half hl = __float2half_rn(wl), hh = __float2half_rn(wh);
-                        hv[4 * wi + i] = hl;
-                        lv[4 * wi + i] = __float2half_rn(__fsub_rn(wl, __half2float(hl)));
-                        hv[16 + 4 * wi + i] = hh;
-                        lv[16 + 4 * wi + i] = __float2half_rn(__fsub_rn(wh, __half2float(hh)));
-                    }
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    *reinterpret_cast<uint4*>(Ah + core_off(t, 4 * bb + j)) = *reinterpret_cast<const uint4*>(&hv[8 * j]);
-                    *reinterpret_cast<uint4*>(Al + core_off(t, 4 * bb + j)) = *reinterpret_cast<const uint4*>(&lv[8 * j]);
-                }
+            for (int wi = 0; wi < 4; ++wi) {
+                *reinterpret_cast<uint4*>(Ah + core_off(row, 4 * bb + wi)) = hi[wi];
+                *reinterpret_cast<uint4*>(Al + core_off(row, 4 * bb + wi)) = lo[wi];
             }
         } else {
 #pragma unroll
-            for (int k8 = 0; k8 < 8; ++k8) {
-                *reinterpret_cast<uint4*>(Ah + core_off(t, k8)) = make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4*>(Al + core_off(t, k8)) = make_uint4(0, 0, 0, 0);
+            for (int wi = 0; wi < 4; ++wi) {
+                *reinterpret_cast<uint4*>(Ah + core_off(row, 4 * bb + wi)) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(Al + core_off(row, 4 * bb + wi)) = make_uint4(0, 0, 0, 0);
             }
         }
-        // batch rows, hi and lo: NT x 64 f16 each = NT * 8 pieces of 16 bytes; piece p -> (k8 = p / NT,
-        // r = p % NT)
-        for (int part = 0; part < 1 + x_lo; ++part) {
-            uint8_t* B = sm.b[buf][part];
-            const __half* xp = x + (int64_t)part * M * K;
-            for (int p = t; p < NT * 8; p += kThreads) {
-                const int k8 = p / NT, r = p % NT;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (m0 + r < M) v = __ldg(reinterpret_cast<const uint4*>(xp + (int64_t)(m0 + r) * K + c * kKC + k8 * 8));
-                *reinterpret_cast<uint4*>(B + core_off(r, k8)) = v;
-            }
-        }
-        // generic-proxy writes of the tiles -> visible to the tensor cores (async proxy)
+        // generic-proxy writes of A -> visible to the tensor cores (async proxy)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncthreads();
+        if (!__syncthreads_and(ok)) {
+            ok = false;
+            break;
+        }
         if (t == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t ah = smem_u32(sm.a[buf][0]), al = smem_u32(sm.a[buf][1]);
-            const uint32_t bh = smem_u32(sm.b[buf][0]), bl = smem_u32(sm.b[buf][1]);
+            if (mbar_wait(&sm.b_full[c % NBS], (c / NBS) & 1)) {
+                const uint32_t ah = smem_u32(sm.a[buf][0]), al = smem_u32(sm.a[buf][1]);
+                const uint32_t bh = smem_u32(sm.b[c % NBS][0]), bl = smem_u32(sm.b[c % NBS][1]);
 #pragma unroll
-            for (int k16 = 0; k16 < kKC / 16; ++k16) {
-                // K = 16 is two core matrices along K: LBO 128 bytes, 8-row groups 1024 bytes apart
-                const uint32_t o = k16 * 256;
-                mma_f16(tmem, smem_desc(ah + o, 128, 1024), smem_desc(bh + o, 128, 1024), idesc, (c > 0 || k16 > 0) ? 1u : 0u);
-                if (x_lo) mma_f16(tmem, smem_desc(ah + o, 128, 1024), smem_desc(bl + o, 128, 1024), idesc, 1u);
-                mma_f16(tmem, smem_desc(al + o, 128, 1024), smem_desc(bh + o, 128, 1024), idesc, 1u);
+                for (int k16 = 0; k16 < kKC / 16; ++k16) {
+                    // K = 16 is two core matrices along K: LBO 128 bytes, 8-row groups 1024 bytes apart
+                    const uint32_t o = k16 * 256;
+                    mma_f16(tmem, smem_desc(ah + o, 128, 1024), smem_desc(bh + o, 128, 1024), idesc,
+                            (c > 0 || k16 > 0) ? 1u : 0u);
+                    if (x_lo) mma_f16(tmem, smem_desc(ah + o, 128, 1024), smem_desc(bl + o, 128, 1024), idesc, 1u);
+                    mma_f16(tmem, smem_desc(al + o, 128, 1024), smem_desc(bh + o, 128, 1024), idesc, 1u);
+                }
+            } else {
+                ok = false;  // seen by every thread at the next __syncthreads_and
             }
-            mma_commit(&sm.mbar[buf]);
+            mma_commit(&sm.mma_done[c & 3]);  // arrives once the MMAs issued so far are done
         }
+        committed = c + 1;
     }
     // the last commit covers every MMA of the CTA
-    const int last = nchunks - 1;
-    if (!mbar_wait(&sm.mbar[last & 1], (last >> 1) & 1)) ok = false;
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (!ok) sm.ok = 0;
-    __syncthreads();
-    if (EPI == EPI_QKV) {
-        for (int j = t; j < NT; j += kThreads) {
-            int2 v = make_int2(0, 0);
-            if (m0 + j < M) {
-                const StreamState st = c.state[c.ids[m0 + j]];
-                v = make_int2(st.offset, st.write_pos);
-            }
-            sm.pos[j] = v;
-        }
-        __syncthreads();
+    if (committed > 0) {
+        const int lc = committed - 1;
+        if (!mbar_wait(&sm.mma_done[lc & 3], (lc >> 2) & 1)) ok = false;
     }
-    if (sm.ok) {
-        // tile row t = TMEM lane t = this thread (warp w reads lanes 32w .. 32w+31)
-        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const bool all_ok = __syncthreads_and(ok) && committed == nchunks;
+    if (all_ok) {
+        // tile row = TMEM lane: warp w reads lanes 32 (w % 4) .. +31, columns of its half
+        const int trow = (warp & 3) * 32 + lane;
+        const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        float* pz = part + (int64_t)z * M * w.n + n0 + trow;
 #pragma unroll 1
-        for (int j0 = 0; j0 < NT; j0 += 16) {
+        for (int j0 = (warp >> 2) * 16; j0 < NT; j0 += 32) {
             float v[16];
             tmem_ld16(lane_addr + j0, v);
-            if (EPI == EPI_GATE) {
-                // value rows hand their results to the gate rows
-                if (t >= 64)
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) sm.gv[t - 64][j] = v[j];
-                __syncthreads();
-                if (t < 64 && row < w.n)
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int m = m0 + j0 + j;
-                        if (m >= M) break;
-                        const float g = v[j];
-                        // silu(x) = x * (1 / (1 + exp(-x)))
-                        const float sg = __fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
-                        out[(int64_t)m * ldo + row] = __fmul_rn(sg, sm.gv[t][j]);
-                    }
-                __syncthreads();
-            } else if (EPI == EPI_QKV) {
+            if (trow < rows)
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const float other = __shfl_xor_sync(0xFFFFFFFFu, v[j], 1);  // the pair's odd row
-                    const int m = m0 + j0 + j;
-                    if ((t & 1) || m >= M || row >= w.n) continue;
-                    float va = v[j], vb = other;
-                    const int D = c.D, HD = c.HD;
-                    const int part = row / D, within = row - part * D;
-                    const int h = within / HD, d = within - h * HD;
-                    const int2 ps = sm.pos[j0 + j];
-                    if (part < 2) {
-                        // RoPE::apply_rotation (model.rs:114-116) on the pair (2i, 2i+1)
-                        const float2 cs = c.rope[(int64_t)ps.x * (HD >> 1) + (d >> 1)];
-                        const float re = __fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y));
-                        const float im = __fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x));
-                        va = re;
-                        vb = im;
-                    }
-                    out[(int64_t)m * ldo + row] = va;
-                    out[(int64_t)m * ldo + row + 1] = vb;
-                    if (part >= 1) {
-                        const int64_t off = (int64_t)c.ids[m] * c.kv_stream_stride + (int64_t)ga.layer * c.kv_layer_stride +
-                                            (part == 2 ? c.kv_half_stride : 0) + ((int64_t)h * c.ML + ps.y) * HD + d;
-                        if (c.kv_f32) {
-                            float* kv = reinterpret_cast<float*>(c.kv) + off;
-                            kv[0] = va;
-                            kv[1] = vb;
-                        } else {
-                            *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(c.kv) + off) =
-                                __floats2bfloat162_rn(va, vb);
-                        }
-                    }
+                    const int m = mt * NT + j0 + j;
+                    if (m < M) pz[(int64_t)m * w.n] = v[j];
                 }
-            } else if (row < w.n) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int m = m0 + j0 + j;
-                    if (m >= M) break;
-                    float* o = out + (int64_t)m * ldo + row;
-                    *o = EPI == EPI_RESID ? __fadd_rn(v[j], *o) : v[j];
-                }
-            }
         }
     } else if (t == 0) {
-        atomicCAS(err, 0, 1);
+        atomicExch(err, 1);
+        // copies still in flight land before the CTA's shared memory goes away
+        mbar_wait(&sm.raw_bar, 0);
+        for (int j = committed; j < issued; ++j) mbar_wait(&sm.b_full[j % NBS], (j / NBS) & 1);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
 }
 
-template <int NT, int EPI>
-cudaError_t launch_nt(const Q4Dev& w, const __half* x, int x_lo, int M, float* out, int64_t ldo, int* err, const Ctx& c,
-                      const GemvArgs& ga, cudaStream_t st) {
+int pick_nt(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+
+// Slices: at least enough to fit 4 quads each in shared memory, and up to one CTA per SM.
+TcPlan make_plan(int n, int k, int M, int num_sms) {
+    TcPlan p;
+    p.nt = pick_nt(M);
+    p.mtiles = (M + p.nt - 1) / p.nt;
+    p.tiles = (n + kTM - 1) / kTM;
+    const int nq = k / kQuad;
+    const int need = (nq + kMaxQuads - 1) / kMaxQuads;
+    const int fill = num_sms / std::max(1, p.tiles * p.mtiles);
+    p.slices = std::max(need, std::min(nq, fill));
+    return p;
+}
+
+template <int NT>
+cudaError_t launch_nt(const Q4Dev& w, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
+                      cudaStream_t st) {
     const size_t smem = sizeof(TcSmem<NT>);
-    cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const int tiles = EPI == EPI_GATE ? ga.half_n / 64 : (w.n + kTM - 1) / kTM;
-    dim3 grid(tiles, (M + NT - 1) / NT);
-    q4_tc_kernel<NT, EPI><<<grid, kThreads, smem, st>>>(w, x, x_lo, M, out, ldo, err, c, ga);
+    dim3 grid(p.tiles, p.mtiles, p.slices);
+    q4_tc_kernel<NT><<<grid, kThreads, smem, st>>>(w, x16, x_lo, M, p.mtiles, p.slices, part, err);
     return cudaGetLastError();
 }
 
-template <int EPI>
-cudaError_t launch_epi(const Q4Dev& w, const __half* x, int x_lo, int M, float* out, int64_t ldo, int* err, const Ctx& c,
-                       const GemvArgs& ga, cudaStream_t st) {
-    if (M <= 16) return launch_nt<16, EPI>(w, x, x_lo, M, out, ldo, err, c, ga, st);
-    if (M <= 32) return launch_nt<32, EPI>(w, x, x_lo, M, out, ldo, err, c, ga, st);
-    if (M <= 64) return launch_nt<64, EPI>(w, x, x_lo, M, out, ldo, err, c, ga, st);
-    if (M <= 128) return launch_nt<128, EPI>(w, x, x_lo, M, out, ldo, err, c, ga, st);
-    return launch_nt<256, EPI>(w, x, x_lo, M, out, ldo, err, c, ga, st);
+cudaError_t launch_gemm(const Q4Dev& w, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
+                        cudaStream_t st) {
+    switch (p.nt) {
+        case 16: return launch_nt<16>(w, x16, x_lo, M, p, part, err, st);
+        case 32: return launch_nt<32>(w, x16, x_lo, M, p, part, err, st);
+        case 64: return launch_nt<64>(w, x16, x_lo, M, p, part, err, st);
+        default: return launch_nt<128>(w, x16, x_lo, M, p, part, err, st);
+    }
 }
 
-// f16 GEMM input of a batch: row m of `in` (f32, or bf16 when in_bf16), with RMSNorm when alpha is
-// not NULL (the same arithmetic as the GEMV's prologue: x / rms * alpha), split into f16 hi and lo
-// parts: out[m][k] = hi, out[rows + m][k] = lo.
+// Position within a 32-element block of element e of an 8-element piece (see the K order above).
+__device__ __forceinline__ int piece_elem(int e) { return ((e & 1) << 1) | ((e >> 1) & 1) | ((e >> 2) << 4); }
+
+// f16 GEMM input of a batch, in the tiled K order of the kernel above.  One CTA per padded batch
+// row (mtiles * nt of them); row m < M is row m of `in` (f32, bf16 when in_bf16, f16 when in_f16),
+// with RMSNorm when alpha is not NULL (the same arithmetic as the GEMV's prologue: x / rms *
+// alpha); rows >= M are zero.  Writes the hi parts and, when lo != 0, the lo parts (x = hi + lo).
 __global__ void __launch_bounds__(256) prep_f16_kernel(const float* __restrict__ in, const __nv_bfloat16* __restrict__ in_bf16,
-                                                       const float* __restrict__ alpha, int K, __half* __restrict__ out) {
+                                                       const __half* __restrict__ in_f16, const float* __restrict__ alpha,
+                                                       int K, int M, int nt, int lo, __half* __restrict__ out) {
     __shared__ float red[32];
-    const int64_t base = (int64_t)blockIdx.x * K;
+    const int m = blockIdx.x, mt = m / nt, r = m - mt * nt;
+    const int nch = K / kKC;
+    const int64_t lo_off = (int64_t)gridDim.x * K;  // the lo parts follow the hi parts of all rows
+    uint8_t* const hi_base = reinterpret_cast<uint8_t*>(out + (int64_t)mt * nch * (nt * kKC));
+    uint8_t* const lo_base = reinterpret_cast<uint8_t*>(out + lo_off + (int64_t)mt * nch * (nt * kKC));
+    const int64_t base = (int64_t)m * K;
     float rms = 1.0f;
-    if (alpha) {
+    if (alpha && m < M) {
         float ss = 0.0f;
         for (int j = threadIdx.x; j < K; j += blockDim.x) {
             const float v = in[base + j];
@@ -368,35 +411,81 @@ __global__ void __launch_bounds__(256) prep_f16_kernel(const float* __restrict__
         __syncthreads();
         rms = sqrtf(__fadd_rn(__fdiv_rn(red[0], (float)K), 1e-8f));
     }
-    const int64_t lo_off = (int64_t)gridDim.x * K;  // the lo parts follow the hi parts of all rows
-    for (int j = threadIdx.x; j < K; j += blockDim.x) {
-        float v = in_bf16 ? __bfloat162float(in_bf16[base + j]) : in[base + j];
-        if (alpha) v = __fmul_rn(__fdiv_rn(v, rms), alpha[j]);
-        const __half h = __float2half_rn(v);
-        out[base + j] = h;
-        out[lo_off + base + j] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+    // piece pi: 8 elements of block pi / 4, word pi % 4; chunk pi / 8, piece pi % 8 of the chunk
+    for (int pi = threadIdx.x; pi < K / 8; pi += blockDim.x) {
+        const int blk = pi >> 2, wi = pi & 3;
+        const size_t off = (size_t)(pi >> 3) * (nt * kKC * 2) + core_off(r, pi & 7);
+        __align__(16) __half h[8], l[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float v = 0.0f;
+            if (m < M) {
+                const int64_t k = base + blk * 32 + 4 * wi + piece_elem(e);
+                v = in_f16 ? __half2float(in_f16[k]) : in_bf16 ? __bfloat162float(in_bf16[k]) : in[k];
+                if (alpha) v = __fmul_rn(__fdiv_rn(v, rms), alpha[blk * 32 + 4 * wi + piece_elem(e)]);
+            }
+            h[e] = __float2half_rn(v);
+            l[e] = __float2half_rn(__fsub_rn(v, __half2float(h[e])));
+        }
+        *reinterpret_cast<uint4*>(hi_base + off) = *reinterpret_cast<const uint4*>(h);
+        if (lo) *reinterpret_cast<uint4*>(lo_base + off) = *reinterpret_cast<const uint4*>(l);
     }
+}
+
+cudaError_t launch_prep(const float* in, const __nv_bfloat16* in_bf16, const __half* in_f16, const float* alpha, int K,
+                        int M, const TcPlan& p, int lo, __half* x16, cudaStream_t st) {
+    prep_f16_kernel<<<p.mtiles * p.nt, 256, 0, st>>>(in, in_bf16, in_f16, alpha, K, M, p.nt, lo, x16);
+    return cudaGetLastError();
 }
 
 }  // namespace
 
-bool tc_gemm_supported(const Q4Dev& w) { return w.k % kKC == 0 && w.k >= kKC; }
+bool tc_gemm_supported(const Q4Dev& w) { return w.k % kQuad == 0 && w.k > 0 && w.n > 0; }
 
-cudaError_t launch_q4_tc_gemm(const Q4Dev& w, const __half* x, int M, float* out, int64_t ldo, int* err, cudaStream_t st) {
-    return launch_epi<EPI_PLAIN>(w, x, 0, M, out, ldo, err, Ctx{}, GemvArgs{}, st);
+bool tc_gemm_scales_ok(const uint8_t* q4_blocks, int64_t nblocks) {
+    // Q4_0 block: f16 scale, then 16 payload bytes; |s| <= 4 keeps every q * s * 2^10 finite in f16
+    for (int64_t b = 0; b < nblocks; ++b) {
+        const uint16_t s = (uint16_t)(q4_blocks[b * 18] | (q4_blocks[b * 18 + 1] << 8));
+        if ((s & 0x7FFFu) > 0x4400u) return false;  // 0x4400 = 4.0; larger magnitudes, inf and nan fail
+    }
+    return true;
 }
 
-cudaError_t launch_tc_layer(const Ctx& c, const GemvArgs& a, int epi, int rows, __half* x16, int* err, cudaStream_t st) {
-    prep_f16_kernel<<<rows, 256, 0, st>>>(a.in, a.in_bf16, a.norm, a.W.k, x16);
-    cudaError_t e = cudaGetLastError();
+TcPlan tc_gemm_plan(const Q4Dev& w, int M, int num_sms) { return make_plan(w.n, w.k, M, num_sms); }
+
+size_t tc_x16_bytes(int k, int M) {
+    const TcPlan p = make_plan(1, k, M, 1);
+    return 2 * (size_t)p.mtiles * p.nt * k * sizeof(__half);
+}
+
+size_t tc_part_bytes(const Q4Dev& w, int M, int num_sms) {
+    const TcPlan p = make_plan(w.n, w.k, M, num_sms);
+    return (size_t)p.slices * M * w.n * sizeof(float);
+}
+
+cudaError_t launch_q4_tc_gemm(const Q4Dev& w, const __half* x, int M, float* out, int64_t ldo, __half* x16,
+                              float* part, int* err, int num_sms, cudaStream_t st) {
+    const TcPlan p = make_plan(w.n, w.k, M, num_sms);
+    cudaError_t e = launch_prep(nullptr, nullptr, x, nullptr, w.k, M, p, 0, x16, st);
     if (e != cudaSuccess) return e;
-    switch (epi) {
-        case EPI_QKV: return launch_epi<EPI_QKV>(a.W, x16, 1, rows, a.out, a.ldo, err, c, a, st);
-        case EPI_GATE: return launch_epi<EPI_GATE>(a.W, x16, 1, rows, a.out, a.ldo, err, c, a, st);
-        case EPI_RESID: return launch_epi<EPI_RESID>(a.W, x16, 1, rows, a.out, a.ldo, err, c, a, st);
-        case EPI_LOGITS: return launch_epi<EPI_LOGITS>(a.W, x16, 1, rows, a.out, a.ldo, err, c, a, st);
-        default: return launch_epi<EPI_PLAIN>(a.W, x16, 1, rows, a.out, a.ldo, err, c, a, st);
-    }
+    e = launch_gemm(w, x16, 0, M, p, part, err, st);
+    if (e != cudaSuccess) return e;
+    GemvArgs a{};
+    a.W = w;
+    a.out = out;
+    a.ldo = ldo;
+    a.n_units = (w.n + 1) / 2;
+    return launch_tc_epilogue(Ctx{}, a, EPI_PLAIN, M, part, p.slices, st);
+}
+
+cudaError_t launch_tc_layer(const Ctx& c, const GemvArgs& a, int epi, int rows, __half* x16, float* part, int* err,
+                            int num_sms, cudaStream_t st) {
+    const TcPlan p = make_plan(a.W.n, a.W.k, rows, num_sms);
+    cudaError_t e = launch_prep(a.in, a.in_bf16, nullptr, a.norm, a.W.k, rows, p, 1, x16, st);
+    if (e != cudaSuccess) return e;
+    e = launch_gemm(a.W, x16, 1, rows, p, part, err, st);
+    if (e != cudaSuccess) return e;
+    return launch_tc_epilogue(c, a, epi, rows, part, p.slices, st);
 }
 
 }  // namespace stt

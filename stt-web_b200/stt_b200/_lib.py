@@ -60,6 +60,8 @@ class stt_model_info(C.Structure):
         ("device", C.c_int32),
         ("q4_weight_bytes", C.c_uint64),
         ("device_bytes", C.c_uint64),
+        ("tensor_core_min_batch", C.c_int32),
+        ("reserved", C.c_int32),
     ]
 
 

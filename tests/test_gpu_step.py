@@ -251,13 +251,14 @@ def test_persistent_kernel_barrier_and_trace(full_model):
 TC_TIE = 5e-2  # near-ties below this margin may flip under f16 operand rounding
 
 
-@pytest.mark.parametrize("kv", ["bf16", "f32"])
-def test_batched_tensor_core_path_matches_oracle(tiny_ref_gguf, kv):
-    """Batches of 16+ streams run their layer products on the tensor cores with f16 operands:
-    logits within the 2e-2 bound of the oracle, tokens equal away from near-ties."""
+@pytest.mark.parametrize("kv,n", [("bf16", 20), ("f32", 20), ("bf16", 150)])
+def test_batched_tensor_core_path_matches_oracle(tiny_ref_gguf, kv, n):
+    """Batches of 16+ streams run their layer products on the tensor cores (f16 operand parts,
+    K-slice partial sums added in order; 150 streams span two batch tiles): logits within the
+    2e-2 bound of the oracle, tokens equal away from near-ties."""
     cfg = tiny_cfg(sliding_window=12)
     model = stt_b200.SttModel.from_shards([tiny_ref_gguf], config=cfg)
-    n = 20
+    assert model.info.tensor_core_min_batch == 16
     cache = model.create_cache(n, kv)
     om = oracle_for(tiny_ref_gguf, cfg)
     refs = [om.stream(0 if kv == "f32" else O.KV_BF16) for _ in range(n)]
@@ -284,6 +285,7 @@ def test_batched_tensor_core_path_matches_oracle(tiny_ref_gguf, kv):
 
 def test_full_size_batched_tensor_core_path(full_model):
     g, model = full_model
+    assert model.info.tensor_core_min_batch == 16
     n = 16
     cache = model.create_cache(n, "bf16")
     om = oracle_for(g.array, SttConfig())
@@ -310,6 +312,7 @@ def test_tensor_core_and_gemv_batches_agree(monkeypatch):
     g = stt_b200.synth_gguf(spec)
     cfg = tiny_cfg()
     model = stt_b200.SttModel.from_shards([g.array], config=cfg)
+    assert model.info.tensor_core_min_batch == 16
     n = 16
     frames = np.random.default_rng(12).integers(0, 300, (6, n, 4))
     outs = []
