@@ -129,6 +129,7 @@ struct stt_model {
     const float* out_norm = nullptr;
     const float2* rope = nullptr;
     bool tc_ok = false;  // every layer product and the head fit the tensor-core path
+    std::vector<TcWeight> tc_w;  // their TMA descriptors: 4 per layer (qkv, out, fin, fout), then the head
     const uint8_t* emb_audio = nullptr;
     const uint8_t* emb_text = nullptr;
     float attn_scale = 0.0f;
@@ -430,6 +431,11 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
         }
         m->head = qd.back();
         for (const Q4Dev& w : qd) m->tc_ok = m->tc_ok && tc_gemm_supported(w);
+        if (m->tc_ok) {
+            m->tc_w.resize(qd.size());
+            for (size_t i = 0; i < qd.size(); ++i)
+                if (tc_make_weight(qd[i], &m->tc_w[i]) != cudaSuccess) m->tc_ok = false;
+        }
         m->out_norm = dn + (size_t)(2 * m->L) * m->D;
     }
     CUDA_TRY(cudaMemcpy(base + off_norms, norms.data(), norms.size() * sizeof(float), cudaMemcpyHostToDevice));
@@ -571,8 +577,8 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
     const int grid = 2 * m->num_sms;
     // batches of kTcMinBatch streams or more: layer products on the tensor cores (f16 operands)
     const bool tc = n >= kTcMinBatch && m->tc_ok && std::getenv("STT_DISABLE_TC") == nullptr;
-    auto layer = [&](const GemvArgs& a, int epi) -> cudaError_t {
-        return tc ? launch_tc_layer(c, a, epi, n, s->d_x16, s->d_tc_part, s->d_tc_err, m->num_sms, st)
+    auto layer = [&](const GemvArgs& a, int w, int epi) -> cudaError_t {
+        return tc ? launch_tc_layer(c, a, m->tc_w[w], epi, n, s->d_x16, s->d_tc_part, s->d_tc_err, m->num_sms, st)
                   : launch_gemv(c, a, epi, n, grid, st);
     };
     CUDA_TRY(launch_embed(c, st));
@@ -581,23 +587,23 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
         GemvArgs a{};
         a.W = L.qkv; a.in = s->d_x; a.norm = L.norm1; a.out = s->d_qkv; a.ldo = 3 * m->D; a.layer = l;
         a.n_units = 3 * m->D / 2;
-        CUDA_TRY(layer(a, EPI_QKV));
+        CUDA_TRY(layer(a, 4 * l + 0, EPI_QKV));
         CUDA_TRY(launch_attention(c, l, st));
         a = GemvArgs{};
         a.W = L.out; a.in = s->d_attn; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
-        CUDA_TRY(layer(a, EPI_RESID));
+        CUDA_TRY(layer(a, 4 * l + 1, EPI_RESID));
         a = GemvArgs{};
         a.W = L.fin; a.in = s->d_x; a.norm = L.norm2; a.out = s->d_hid; a.ldo = m->F; a.n_units = m->F;
         a.half_n = m->F;
-        CUDA_TRY(layer(a, EPI_GATE));
+        CUDA_TRY(layer(a, 4 * l + 2, EPI_GATE));
         a = GemvArgs{};
         a.W = L.fout; a.in = s->d_hid; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
-        CUDA_TRY(layer(a, EPI_RESID));
+        CUDA_TRY(layer(a, 4 * l + 3, EPI_RESID));
     }
     GemvArgs a{};
     a.W = m->head; a.in = s->d_x; a.norm = m->out_norm; a.out = s->d_logits; a.ldo = m->V;
     a.n_units = (m->V + 1) / 2;
-    CUDA_TRY(layer(a, EPI_LOGITS));
+    CUDA_TRY(layer(a, 4 * m->L, EPI_LOGITS));
     CUDA_TRY(launch_finish(c, st));
     return STT_OK;
 }
@@ -997,6 +1003,7 @@ struct stt_q4_tensor {
     void* mem = nullptr;
     int* d_err = nullptr;  // timeout flag of the tensor-core kernel (inside mem)
     bool tc_ok = false;    // shape and scales fit the tensor-core kernel
+    TcWeight tc_w{};       // its TMA descriptors
     mutable DevBuf tc_x16, tc_part;  // its scratch, grown on demand
 };
 
@@ -1031,7 +1038,8 @@ extern "C" int stt_q4_tensor_create(const uint8_t* bytes, size_t n_bytes, int n,
     t->w.n = n;
     t->w.k = k;
     t->d_err = reinterpret_cast<int*>(static_cast<uint8_t*>(t->mem) + nib_bytes + sc_bytes);
-    t->tc_ok = tc_gemm_supported(t->w) && tc_gemm_scales_ok(bytes, (int64_t)nblk);
+    t->tc_ok = tc_gemm_supported(t->w) && tc_gemm_scales_ok(bytes, (int64_t)nblk) &&
+               tc_make_weight(t->w, &t->tc_w) == cudaSuccess;
     CUDA_TRY(cudaMemset(t->d_err, 0, sizeof(int)));
     DevBuf staging;
     TRY(staging.ensure(n_bytes));
@@ -1069,7 +1077,7 @@ extern "C" int stt_q4_matmul_device(const stt_q4_tensor* t, const void* d_in, in
             return set_error(STT_E_INVALID_ARG, "f16 input must be 2-byte aligned");
         TRY(t->tc_x16.ensure(tc_x16_bytes(t->w.k, rows)));
         TRY(t->tc_part.ensure(tc_part_bytes(t->w, rows, t->num_sms)));
-        CUDA_TRY(launch_q4_tc_gemm(t->w, static_cast<const __half*>(d_in), rows, d_out, t->w.n,
+        CUDA_TRY(launch_q4_tc_gemm(t->tc_w, t->w, static_cast<const __half*>(d_in), rows, d_out, t->w.n,
                                    static_cast<__half*>(t->tc_x16.p), static_cast<float*>(t->tc_part.p), t->d_err,
                                    t->num_sms, static_cast<cudaStream_t>(cuda_stream)));
         return STT_OK;

@@ -23,19 +23,24 @@
 // matrices along K 128 bytes apart, 8-row groups 1024 bytes apart], so one chunk of one part is a
 // single contiguous bulk copy of NT * 128 bytes.
 //
-// Grid: (weight-row tiles of 128, batch-row tiles of NT, K slices).  A CTA of 256 threads:
-//   - warp 7 bulk-copies (cp.async.bulk) its slice of the 128 weight rows into shared memory, one
-//     copy of nibbles and one of scales per row, all on one mbarrier;
-//   - thread 0 bulk-copies the activation chunks into a ring of B stages, two chunks ahead when
-//     the ring has four stages;
-//   - per 64-wide chunk, two threads per weight row dequantise one Q4_0 block each into the A
-//     operand (hi and lo parts, two buffers), and thread 0 issues 4 x 3 MMAs of 128 x NT x 16
-//     and commits them to an mbarrier;
-//   - each warp reads 32 TMEM lanes (tcgen05.ld 32x32b) for half of the batch columns and stores
-//     the partial sums.
-// Every wait is bounded; on a timeout the CTA stops issuing, records an error, waits (bounded) for
-// its MMAs and copies in flight, frees its TMEM and returns.
+// Grid: (weight-row tiles of 128, batch-row tiles of NT, K slices).  A CTA runs a warp-specialised
+// pipeline with mbarrier hand-offs and no CTA-wide barrier inside the K loop:
+//   - warp 0 (one lane) is the copy engine: per 256-wide quad of K it loads the 128 rows' Q4_0
+//     nibbles (16 KB, 128-byte swizzle) and scales (2 KB) with two 2-D TMA loads into a ring of
+//     raw stages, and per 64-wide chunk the activation tile (hi, lo) with bulk copies into a ring
+//     of B stages;
+//   - warps 2..9 dequantise: two threads per weight row, one Q4_0 block each per chunk, into a
+//     ring of A stages (hi and lo parts), then signal the stage with one arrive per warp;
+//   - warp 1 (one lane) issues, per chunk, 4 x 3 MMAs of 128 x NT x 16 into the TMEM accumulator
+//     and commits them to the barriers that free the A and B stages they read;
+//   - after the last commit, warps 2..9 read the accumulator (tcgen05.ld 32x32b; each warp its
+//     32 TMEM lanes and half of the batch columns) and store the partial sums.
+// Every wait is bounded and polls a shared abort word; a timeout sets it, every role stops
+// issuing, the copies and MMAs in flight are waited for (bounded), the CTA records an error,
+// frees its TMEM and returns without storing.
 #include "tc_gemm.h"
+
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 
@@ -45,13 +50,15 @@ namespace stt {
 
 namespace {
 
-constexpr int kTM = 128;            // weight rows per CTA (MMA M, one TMEM lane each)
-constexpr int kKC = 64;             // K elements per chunk (two Q4_0 blocks)
-constexpr int kQuad = 256;          // K granule of a slice: 8 blocks, so scale copies stay 16-byte sized
-constexpr int kMaxQuads = 4;        // quads per slice held in shared memory (1024 K)
-constexpr int kThreads = 256;
-constexpr int kNibStride = kMaxQuads * 8 * 16 + 16;  // bytes per weight row, padded against bank conflicts
-constexpr int kScStride = kMaxQuads * 8 * 2 + 16;
+constexpr int kTM = 128;        // weight rows per CTA (MMA M, one TMEM lane each)
+constexpr int kKC = 64;         // K elements per chunk (two Q4_0 blocks)
+constexpr int kQuad = 256;      // K elements per raw stage (8 blocks: 128 nibble bytes, 16 scale bytes per row)
+constexpr int kRS = 3;          // raw stages
+constexpr int kAS = 3;          // A stages
+constexpr int kDqWarps = 8;     // dequantising warps (2 .. 9)
+constexpr int kThreads = 64 + 32 * kDqWarps;
+constexpr uint32_t kRNib = kTM * 128;  // raw nibble bytes per stage
+constexpr uint32_t kRSc = kTM * 16;    // raw scale bytes per stage
 constexpr uint32_t kSpin = 1u << 22;
 constexpr float kWUnscale = 1.0f / 1024.0f;
 
@@ -80,8 +87,8 @@ __host__ __device__ constexpr uint32_t instr_desc_f16(int M, int N) {
            | ((uint32_t)(M >> 4) << 24); // M / 16
 }
 
-__device__ __forceinline__ void mbar_init(uint64_t* m) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(m)) : "memory");
+__device__ __forceinline__ void mbar_init(uint64_t* m, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(m)), "r"(count) : "memory");
 }
 __device__ __forceinline__ bool mbar_try(uint64_t* m, uint32_t parity) {
     uint32_t ok;
@@ -94,10 +101,23 @@ __device__ __forceinline__ bool mbar_try(uint64_t* m, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity) {
-    for (uint32_t i = 0; i < kSpin; ++i)
+// Bounded wait for the phase of parity `parity`; gives up when the CTA's abort word is set or
+// after kSpin polls (then sets it).
+__device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity, volatile int* abort) {
+    for (uint32_t i = 0; i < kSpin; ++i) {
         if (mbar_try(m, parity)) return true;
+        if ((i & 63u) == 63u && *abort) return false;
+    }
+    *abort = 1;
     return false;
+}
+// Bounded wait that ignores the abort word (draining copies and MMAs before exit).
+__device__ __forceinline__ void mbar_drain(uint64_t* m, uint32_t parity) {
+    for (uint32_t i = 0; i < kSpin; ++i)
+        if (mbar_try(m, parity)) return;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* m) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(m)) : "memory");
 }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* m, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(m)), "r"(bytes) : "memory");
@@ -109,6 +129,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(m))
         : "memory");
 }
+// 2-D TMA tile load (x = innermost coordinate in elements), completing on the mbarrier (no multicast).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* m) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(m))
+        : "memory");
+}
 
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
     asm volatile(
@@ -118,6 +146,7 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_
         ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
 }
+// Arrives on the mbarrier once every MMA issued so far by this thread has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* m) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(m))
                  : "memory");
@@ -139,15 +168,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 
 template <int NT>
 struct TcSmem {
-    alignas(128) uint8_t a[2][2][kTM * kKC * 2];           // [buffer][hi, lo] weights, core-matrix layout
-    alignas(128) uint8_t b[b_stages(NT)][2][NT * kKC * 2];  // [stage][hi, lo] activations, same layout
-    alignas(128) uint8_t nib[kTM * kNibStride];             // the slice's Q4_0 nibbles, row after row
-    alignas(128) uint8_t sc[kTM * kScStride];               // and its scales
-    alignas(8) uint64_t raw_bar;
-    alignas(8) uint64_t b_full[b_stages(NT)];
-    alignas(8) uint64_t mma_done[4];                        // chunk c commits to mma_done[c % 4]
+    uint8_t rnib[kRS][kRNib];                             // raw nibbles [128 rows][128 B], 128-byte swizzle
+    uint8_t rsc[kRS][kRSc];                               // raw scales [128 rows][8]
+    uint8_t a[kAS][2][kTM * kKC * 2];                     // [stage][hi, lo] weights, core-matrix layout
+    uint8_t b[b_stages(NT)][2][NT * kKC * 2];             // [stage][hi, lo] activations, same layout
+    uint64_t r_full[kRS], r_empty[kRS], a_full[kAS], a_empty[kAS];
+    uint64_t b_full[b_stages(NT)], b_empty[b_stages(NT)], done;
     uint32_t tmem;
+    int abort;
 };
+// the TMA's 128-byte swizzle repeats every 1024 bytes: the shared-memory block is aligned to that
+template <int NT>
+constexpr size_t smem_bytes() { return sizeof(TcSmem<NT>) + 1024; }
 
 // byte offset of 8-element piece k8 of row `row` of a [rows x 64] K-major chunk in core-matrix
 // order: core matrix (row / 8, k8) at ((row / 8) * 8 + k8) * 128, row % 8 at 16-byte steps
@@ -194,31 +226,41 @@ __device__ __forceinline__ void dequant_block(uint4 q, uint16_t sbits, uint4 (&h
 
 // x16 holds the hi parts, then (x_lo != 0) the lo parts, in the tiled order above; without lo
 // parts the input is taken as exact f16 and the hi.lo product is skipped.  Slice z covers the
-// quads [z * nq / slices, (z + 1) * nq / slices) of K.  part: [slices][M][w.n].
+// quads [z * nq / slices, (z + 1) * nq / slices) of K.  part: [slices][M][n].
 template <int NT>
-__global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(Q4Dev w, const __half* __restrict__ x16, int x_lo, int M,
-                                                          int mtiles, int slices, float* __restrict__ part,
-                                                          int* __restrict__ err) {
-    extern __shared__ __align__(128) uint8_t tc_raw[];
-    TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(tc_raw);
+__global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constant__ CUtensorMap tm_nib,
+                                                          const __grid_constant__ CUtensorMap tm_sc, int n, int K,
+                                                          const __half* __restrict__ x16, int x_lo, int M, int mtiles,
+                                                          int slices, float* __restrict__ part, int* __restrict__ err) {
+    extern __shared__ uint8_t tc_raw[];
+    TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(tc_raw + ((1024u - (smem_u32(tc_raw) & 1023u)) & 1023u));
     constexpr int NBS = b_stages(NT);
     constexpr uint32_t kCols = NT < 32 ? 32 : NT;  // TMEM columns (a power of two >= 32)
     constexpr uint32_t kBBytes = NT * kKC * 2;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int n0 = blockIdx.x * kTM, mt = blockIdx.y, z = blockIdx.z;
-    const int K = w.k, NB = K >> 5, nch = K / kKC, nq = K / kQuad;
+    const int nch = K / kKC, nq = K / kQuad;
     const int q0 = (int)((int64_t)z * nq / slices), q1 = (int)((int64_t)(z + 1) * nq / slices);
-    const int c0 = q0 * 4, nchunks = (q1 - q0) * 4, sb = (q1 - q0) * 8;
-    const int rows = min(kTM, w.n - n0);
-    const int64_t part_elems = (int64_t)mtiles * NT * K;  // f16 elements per part of x16
-    const __half* xb = x16 + ((int64_t)mt * nch + c0) * (NT * kKC);
+    const int nquads = q1 - q0, nchunks = 4 * nquads;
+    volatile int* abort = &sm.abort;
     if (t == 0) {
-        mbar_init(&sm.raw_bar);
-        for (int i = 0; i < NBS; ++i) mbar_init(&sm.b_full[i]);
-        for (int i = 0; i < 4; ++i) mbar_init(&sm.mma_done[i]);
+        for (int i = 0; i < kRS; ++i) {
+            mbar_init(&sm.r_full[i], 1);
+            mbar_init(&sm.r_empty[i], kDqWarps);
+        }
+        for (int i = 0; i < kAS; ++i) {
+            mbar_init(&sm.a_full[i], kDqWarps);
+            mbar_init(&sm.a_empty[i], 1);
+        }
+        for (int i = 0; i < NBS; ++i) {
+            mbar_init(&sm.b_full[i], 1);
+            mbar_init(&sm.b_empty[i], 1);
+        }
+        mbar_init(&sm.done, 1);
+        sm.abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem)),
                      "r"(kCols)
                      : "memory");
@@ -228,68 +270,47 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(Q4Dev w, const __hal
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = sm.tmem;
-    // the weight slice: one nibble copy and one scale copy per row (both multiples of 16 bytes)
-    if (warp == 7) {
-        if (lane == 0) mbar_expect_tx(&sm.raw_bar, (uint32_t)rows * sb * 18u);
-        __syncwarp();
-        for (int r = lane; r < rows; r += 32) {
-            const int64_t blk = (int64_t)(n0 + r) * NB + q0 * 8;
-            bulk_g2s(sm.nib + r * kNibStride, w.nib + blk, (uint32_t)sb * 16u, &sm.raw_bar);
-            bulk_g2s(sm.sc + r * kScStride, w.scale + blk, (uint32_t)sb * 2u, &sm.raw_bar);
-        }
-    }
-    // thread 0: activation chunk j -> stage j % NBS
-    int issued = 0;
-    auto issue_b = [&](int j) {
-        uint64_t* fb = &sm.b_full[j % NBS];
-        mbar_expect_tx(fb, (1u + (x_lo ? 1u : 0u)) * kBBytes);
-        bulk_g2s(sm.b[j % NBS][0], xb + (int64_t)j * (NT * kKC), kBBytes, fb);
-        if (x_lo) bulk_g2s(sm.b[j % NBS][1], xb + part_elems + (int64_t)j * (NT * kKC), kBBytes, fb);
-        issued = j + 1;
-    };
-    if (t == 0)
-        for (int j = 0; j < NBS - 2 && j < nchunks; ++j) issue_b(j);
-    bool ok = mbar_wait(&sm.raw_bar, 0);
-    const int row = t & (kTM - 1), bb = t >> 7;  // this thread's weight row and block of each chunk
-    const uint32_t idesc = instr_desc_f16(kTM, NT);
-    int committed = 0;  // chunks whose MMAs are committed (tracked by every thread)
-    for (int c = 0; c < nchunks; ++c) {
-        const int buf = c & 1;
-        // the A buffer and the B stage refilled now were read by the MMAs of chunk c - 2
-        if (c >= 2 && !mbar_wait(&sm.mma_done[(c - 2) & 3], ((c - 2) >> 2) & 1)) ok = false;
-        if (t == 0 && ok && c + NBS - 2 < nchunks && c + NBS - 2 >= issued) issue_b(c + NBS - 2);
-        uint8_t* Ah = sm.a[buf][0];
-        uint8_t* Al = sm.a[buf][1];
-        if (row < rows) {
-            const int blk = c * 2 + bb;  // block within the slice
-            const uint4 q = *reinterpret_cast<const uint4*>(sm.nib + row * kNibStride + blk * 16);
-            const uint16_t sbits = *reinterpret_cast<const uint16_t*>(sm.sc + row * kScStride + blk * 2);
-            uint4 hi[4], lo[4];
-            dequant_block(q, sbits, hi, lo);
-#pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
-                *reinterpret_cast<uint4*>(Ah + core_off(row, 4 * bb + wi)) = hi[wi];
-                *reinterpret_cast<uint4*>(Al + core_off(row, 4 * bb + wi)) = lo[wi];
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // copy engine: raw quad qi -> stage qi % kRS; activation chunk c -> stage c % NBS
+            const __half* xb = x16 + ((int64_t)mt * nch + 4 * q0) * (NT * kKC);
+            const int64_t part_elems = (int64_t)mtiles * NT * K;  // f16 elements per part of x16
+            int rq = 0, bc = 0;                                   // raw quads and chunks issued
+            bool ok = true;
+            for (int qi = 0; qi < nquads && ok; ++qi) {
+                const int s = qi % kRS;
+                if (qi >= kRS && !mbar_wait(&sm.r_empty[s], ((qi / kRS) - 1) & 1, abort)) break;
+                mbar_expect_tx(&sm.r_full[s], kRNib + kRSc);
+                tma_load_2d(sm.rnib[s], &tm_nib, (q0 + qi) * 128, n0, &sm.r_full[s]);
+                tma_load_2d(sm.rsc[s], &tm_sc, (q0 + qi) * 8, n0, &sm.r_full[s]);
+                rq = qi + 1;
+                for (int cq = 0; cq < 4; ++cq) {
+                    const int c = 4 * qi + cq, sb = c % NBS;
+                    if (c >= NBS && !mbar_wait(&sm.b_empty[sb], ((c / NBS) - 1) & 1, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&sm.b_full[sb], (x_lo ? 2u : 1u) * kBBytes);
+                    bulk_g2s(sm.b[sb][0], xb + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
+                    if (x_lo) bulk_g2s(sm.b[sb][1], xb + part_elems + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
+                    bc = c + 1;
+                }
             }
-        } else {
-#pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
-                *reinterpret_cast<uint4*>(Ah + core_off(row, 4 * bb + wi)) = make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4*>(Al + core_off(row, 4 * bb + wi)) = make_uint4(0, 0, 0, 0);
-            }
+            // the last copies of each stage have landed before the CTA can exit
+            for (int qi = std::max(0, rq - kRS); qi < rq; ++qi) mbar_drain(&sm.r_full[qi % kRS], (qi / kRS) & 1);
+            for (int c = std::max(0, bc - NBS); c < bc; ++c) mbar_drain(&sm.b_full[c % NBS], (c / NBS) & 1);
         }
-        // generic-proxy writes of A -> visible to the tensor cores (async proxy)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        if (!__syncthreads_and(ok)) {
-            ok = false;
-            break;
-        }
-        if (t == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            if (mbar_wait(&sm.b_full[c % NBS], (c / NBS) & 1)) {
-                const uint32_t ah = smem_u32(sm.a[buf][0]), al = smem_u32(sm.a[buf][1]);
-                const uint32_t bh = smem_u32(sm.b[c % NBS][0]), bl = smem_u32(sm.b[c % NBS][1]);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc_f16(kTM, NT);
+            for (int c = 0; c < nchunks; ++c) {
+                const int sa = c % kAS, sb = c % NBS;
+                if (!mbar_wait(&sm.a_full[sa], (c / kAS) & 1, abort)) break;
+                if (!mbar_wait(&sm.b_full[sb], (c / NBS) & 1, abort)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t ah = smem_u32(sm.a[sa][0]), al = smem_u32(sm.a[sa][1]);
+                const uint32_t bh = smem_u32(sm.b[sb][0]), bl = smem_u32(sm.b[sb][1]);
 #pragma unroll
                 for (int k16 = 0; k16 < kKC / 16; ++k16) {
                     // K = 16 is two core matrices along K: LBO 128 bytes, 8-row groups 1024 bytes apart
@@ -299,80 +320,103 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(Q4Dev w, const __hal
                     if (x_lo) mma_f16(tmem, smem_desc(ah + o, 128, 1024), smem_desc(bl + o, 128, 1024), idesc, 1u);
                     mma_f16(tmem, smem_desc(al + o, 128, 1024), smem_desc(bh + o, 128, 1024), idesc, 1u);
                 }
-            } else {
-                ok = false;  // seen by every thread at the next __syncthreads_and
+                mma_commit(&sm.a_empty[sa]);
+                mma_commit(&sm.b_empty[sb]);
             }
-            mma_commit(&sm.mma_done[c & 3]);  // arrives once the MMAs issued so far are done
+            mma_commit(&sm.done);  // also on abort: arrives once the MMAs issued so far are done
         }
-        committed = c + 1;
-    }
-    // the last commit covers every MMA of the CTA
-    if (committed > 0) {
-        const int lc = committed - 1;
-        if (!mbar_wait(&sm.mma_done[lc & 3], (lc >> 2) & 1)) ok = false;
-    }
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const bool all_ok = __syncthreads_and(ok) && committed == nchunks;
-    if (all_ok) {
-        // tile row = TMEM lane: warp w reads lanes 32 (w % 4) .. +31, columns of its half
-        const int trow = (warp & 3) * 32 + lane;
-        const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        float* pz = part + (int64_t)z * M * w.n + n0 + trow;
-#pragma unroll 1
-        for (int j0 = (warp >> 2) * 16; j0 < NT; j0 += 32) {
-            float v[16];
-            tmem_ld16(lane_addr + j0, v);
-            if (trow < rows)
+    } else {
+        // dequantisers: thread dt of 256 -> weight row dt % 128, block dt / 128 of each chunk
+        const int dt = t - 64, row = dt & (kTM - 1), bb = dt >> 7;
+        const uint32_t rsw = (uint32_t)(row & 7);  // the swizzle's XOR for this row
+        for (int c = 0; c < nchunks; ++c) {
+            const int qi = c >> 2, cq = c & 3, s = qi % kRS, sa = c % kAS;
+            bool ok = cq != 0 || mbar_wait(&sm.r_full[s], (qi / kRS) & 1, abort);
+            if (ok && c >= kAS) ok = mbar_wait(&sm.a_empty[sa], ((c / kAS) - 1) & 1, abort);
+            if (!__all_sync(0xFFFFFFFFu, ok)) break;  // the warp leaves together
+            const int j = 2 * cq + bb;  // block within the quad
+            const uint4 q = *reinterpret_cast<const uint4*>(sm.rnib[s] + row * 128 + (((uint32_t)j ^ rsw) << 4));
+            const uint16_t sbits = *reinterpret_cast<const uint16_t*>(sm.rsc[s] + row * 16 + j * 2);
+            // rows past the matrix were zero-filled by the TMA: scale 0 gives zero weights
+            uint4 hi[4], lo[4];
+            dequant_block(q, sbits, hi, lo);
+            uint8_t* Ah = sm.a[sa][0];
+            uint8_t* Al = sm.a[sa][1];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int m = mt * NT + j0 + j;
-                    if (m < M) pz[(int64_t)m * w.n] = v[j];
-                }
+            for (int wi = 0; wi < 4; ++wi) {
+                *reinterpret_cast<uint4*>(Ah + core_off(row, 4 * bb + wi)) = hi[wi];
+                *reinterpret_cast<uint4*>(Al + core_off(row, 4 * bb + wi)) = lo[wi];
+            }
+            // generic-proxy writes of A -> visible to the tensor cores (async proxy)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&sm.a_full[sa]);
+                if (cq == 3) mbar_arrive(&sm.r_empty[s]);
+            }
         }
-    } else if (t == 0) {
-        atomicExch(err, 1);
-        // copies still in flight land before the CTA's shared memory goes away
-        mbar_wait(&sm.raw_bar, 0);
-        for (int j = committed; j < issued; ++j) mbar_wait(&sm.b_full[j % NBS], (j / NBS) & 1);
+        // accumulator -> partial sums (the done barrier completes after the last MMAs)
+        mbar_drain(&sm.done, 0);
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (__shfl_sync(0xFFFFFFFFu, *abort, 0) == 0) {  // warp-uniform: tcgen05.ld is warp-collective
+            const int quarter = warp & 3, half = (warp - 2) >> 2;
+            const int trow = quarter * 32 + lane;
+            const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+            float* pz = part + (int64_t)z * M * n + n0 + trow;
+            const bool row_ok = n0 + trow < n;
+#pragma unroll 1
+            for (int j0 = half * 16; j0 < NT; j0 += 32) {
+                float v[16];
+                tmem_ld16(lane_addr + j0, v);
+                if (row_ok)
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const int m = mt * NT + j0 + jj;
+                        if (m < M) pz[(int64_t)m * n] = v[jj];
+                    }
+            }
+        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+    if (t == 0 && *abort) atomicExch(err, 1);
+    __syncwarp();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
 }
 
 int pick_nt(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
 
-// Slices: at least enough to fit 4 quads each in shared memory, and up to one CTA per SM.
+// K slices: up to one CTA per SM.
 TcPlan make_plan(int n, int k, int M, int num_sms) {
     TcPlan p;
     p.nt = pick_nt(M);
     p.mtiles = (M + p.nt - 1) / p.nt;
     p.tiles = (n + kTM - 1) / kTM;
     const int nq = k / kQuad;
-    const int need = (nq + kMaxQuads - 1) / kMaxQuads;
-    const int fill = num_sms / std::max(1, p.tiles * p.mtiles);
-    p.slices = std::max(need, std::min(nq, fill));
+    p.slices = std::max(1, std::min(nq, num_sms / std::max(1, p.tiles * p.mtiles)));
     return p;
 }
 
 template <int NT>
-cudaError_t launch_nt(const Q4Dev& w, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
+cudaError_t launch_nt(const TcWeight& tw, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
                       cudaStream_t st) {
-    const size_t smem = sizeof(TcSmem<NT>);
+    const size_t smem = smem_bytes<NT>();
     cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p.tiles, p.mtiles, p.slices);
-    q4_tc_kernel<NT><<<grid, kThreads, smem, st>>>(w, x16, x_lo, M, p.mtiles, p.slices, part, err);
+    q4_tc_kernel<NT><<<grid, kThreads, smem, st>>>(tw.nib, tw.sc, tw.n, tw.k, x16, x_lo, M, p.mtiles, p.slices, part,
+                                                   err);
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemm(const Q4Dev& w, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
+cudaError_t launch_gemm(const TcWeight& tw, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
                         cudaStream_t st) {
     switch (p.nt) {
-        case 16: return launch_nt<16>(w, x16, x_lo, M, p, part, err, st);
-        case 32: return launch_nt<32>(w, x16, x_lo, M, p, part, err, st);
-        case 64: return launch_nt<64>(w, x16, x_lo, M, p, part, err, st);
-        default: return launch_nt<128>(w, x16, x_lo, M, p, part, err, st);
+        case 16: return launch_nt<16>(tw, x16, x_lo, M, p, part, err, st);
+        case 32: return launch_nt<32>(tw, x16, x_lo, M, p, part, err, st);
+        case 64: return launch_nt<64>(tw, x16, x_lo, M, p, part, err, st);
+        default: return launch_nt<128>(tw, x16, x_lo, M, p, part, err, st);
     }
 }
 
@@ -451,6 +495,44 @@ bool tc_gemm_scales_ok(const uint8_t* q4_blocks, int64_t nblocks) {
     return true;
 }
 
+cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess) return e;
+        if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint64_t nb = (cuuint64_t)(w.k / 32);
+    // nibble plane: [n rows][k/32 * 16 bytes]; a box is one quad (128 bytes) of 128 rows
+    {
+        const cuuint64_t dims[2] = {nb * 16, (cuuint64_t)w.n};
+        const cuuint64_t strides[1] = {nb * 16};
+        const cuuint32_t box[2] = {128, (cuuint32_t)kTM};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&out->nib, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint4*>(w.nib), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    // scale plane: [n rows][k/32 scales]; a box is one quad (8 scales, 16 bytes) of 128 rows
+    {
+        const cuuint64_t dims[2] = {nb, (cuuint64_t)w.n};
+        const cuuint64_t strides[1] = {nb * 2};
+        const cuuint32_t box[2] = {8, (cuuint32_t)kTM};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&out->sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(w.scale), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    out->n = w.n;
+    out->k = w.k;
+    return cudaSuccess;
+}
+
 TcPlan tc_gemm_plan(const Q4Dev& w, int M, int num_sms) { return make_plan(w.n, w.k, M, num_sms); }
 
 size_t tc_x16_bytes(int k, int M) {
@@ -463,12 +545,12 @@ size_t tc_part_bytes(const Q4Dev& w, int M, int num_sms) {
     return (size_t)p.slices * M * w.n * sizeof(float);
 }
 
-cudaError_t launch_q4_tc_gemm(const Q4Dev& w, const __half* x, int M, float* out, int64_t ldo, __half* x16,
-                              float* part, int* err, int num_sms, cudaStream_t st) {
+cudaError_t launch_q4_tc_gemm(const TcWeight& tw, const Q4Dev& w, const __half* x, int M, float* out, int64_t ldo,
+                              __half* x16, float* part, int* err, int num_sms, cudaStream_t st) {
     const TcPlan p = make_plan(w.n, w.k, M, num_sms);
     cudaError_t e = launch_prep(nullptr, nullptr, x, nullptr, w.k, M, p, 0, x16, st);
     if (e != cudaSuccess) return e;
-    e = launch_gemm(w, x16, 0, M, p, part, err, st);
+    e = launch_gemm(tw, x16, 0, M, p, part, err, st);
     if (e != cudaSuccess) return e;
     GemvArgs a{};
     a.W = w;
@@ -478,12 +560,12 @@ cudaError_t launch_q4_tc_gemm(const Q4Dev& w, const __half* x, int M, float* out
     return launch_tc_epilogue(Ctx{}, a, EPI_PLAIN, M, part, p.slices, st);
 }
 
-cudaError_t launch_tc_layer(const Ctx& c, const GemvArgs& a, int epi, int rows, __half* x16, float* part, int* err,
-                            int num_sms, cudaStream_t st) {
+cudaError_t launch_tc_layer(const Ctx& c, const GemvArgs& a, const TcWeight& tw, int epi, int rows, __half* x16,
+                            float* part, int* err, int num_sms, cudaStream_t st) {
     const TcPlan p = make_plan(a.W.n, a.W.k, rows, num_sms);
     cudaError_t e = launch_prep(a.in, a.in_bf16, nullptr, a.norm, a.W.k, rows, p, 1, x16, st);
     if (e != cudaSuccess) return e;
-    e = launch_gemm(a.W, x16, 1, rows, p, part, err, st);
+    e = launch_gemm(tw, x16, 1, rows, p, part, err, st);
     if (e != cudaSuccess) return e;
     return launch_tc_epilogue(c, a, epi, rows, part, p.slices, st);
 }
