@@ -23,18 +23,26 @@
 // matrices along K 128 bytes apart, 8-row groups 1024 bytes apart], so one chunk of one part is a
 // single contiguous bulk copy of NT * 128 bytes.
 //
-// Grid: (weight-row tiles of 128, batch-row tiles of NT, K slices).  A CTA runs a warp-specialised
-// pipeline with mbarrier hand-offs and no CTA-wide barrier inside the K loop:
-//   - warp 0 (one lane) is the copy engine: per 256-wide quad of K it loads the 128 rows' Q4_0
-//     nibbles (16 KB, 128-byte swizzle) and scales (2 KB) with two 2-D TMA loads into a ring of
-//     raw stages, and per 64-wide chunk the activation tile (hi, lo) with bulk copies into a ring
-//     of B stages;
-//   - warps 2..9 dequantise: two threads per weight row, one Q4_0 block each per chunk, into a
-//     ring of A stages (hi and lo parts), then signal the stage with one arrive per warp;
-//   - warp 1 (one lane) issues, per chunk, 4 x 3 MMAs of 128 x NT x 16 into the TMEM accumulator
-//     and commits them to the barriers that free the A and B stages they read;
+// Grid: (weight-row tiles of 128, batch-row tiles of NT, K slices).  A CTA (one per SM: it takes
+// the SM's whole tensor memory) runs a warp-specialised pipeline with mbarrier hand-offs and no
+// CTA-wide barrier inside the K loop:
+//   - warp 0 loads, per 256-wide quad of K, the 128 rows' Q4_0 nibbles (16 KB, 128-byte swizzle)
+//     and scales (2 KB) with two 2-D TMA loads into a ring of raw stages;
+//   - warp 10 copies, per 64-wide chunk, the activation tile (hi, lo) with bulk copies into a
+//     ring of B stages;
+//   - warps 2..9 dequantise in two groups of four that take alternate chunks: one thread per
+//     weight row and chunk (two Q4_0 blocks), writing the hi and lo parts straight into a ring of
+//     A stages in tensor memory (tcgen05.st; weight row = TMEM lane), then signalling the stage
+//     with one arrive per warp;
+//   - warp 1 issues from one elected lane, per pair of chunks, 2 x 4 x 3 MMAs of 128 x NT x 16
+//     with A read from tensor memory and B from shared memory into the TMEM accumulator, and
+//     commits them to the barriers that free the A and B stages they read;
 //   - after the last commit, warps 2..9 read the accumulator (tcgen05.ld 32x32b; each warp its
 //     32 TMEM lanes and half of the batch columns) and store the partial sums.
+// The copy and MMA roles run as whole warps and issue from one elected lane (elect.sync).
+// Measured on the 16896 x 2048 product at 64 batch rows, the dequantisation sets the pace (the MMA
+// lane waits for the slowest dequantising warp) and its per-iteration overhead (waits, fences,
+// TMEM stores, index arithmetic) is a large share of it, hence whole chunks per thread.
 // Every wait is bounded and polls a shared abort word; a timeout sets it, every role stops
 // issuing, the copies and MMAs in flight are waited for (bounded), the CTA records an error,
 // frees its TMEM and returns without storing.
@@ -53,16 +61,21 @@ namespace {
 constexpr int kTM = 128;        // weight rows per CTA (MMA M, one TMEM lane each)
 constexpr int kKC = 64;         // K elements per chunk (two Q4_0 blocks)
 constexpr int kQuad = 256;      // K elements per raw stage (8 blocks: 128 nibble bytes, 16 scale bytes per row)
-constexpr int kRS = 3;          // raw stages
-constexpr int kAS = 3;          // A stages
-constexpr int kDqWarps = 8;     // dequantising warps (2 .. 9)
-constexpr int kThreads = 64 + 32 * kDqWarps;
+constexpr int kRS = 4;          // raw stages (a power of two)
+constexpr int kAS = 4;          // A stages in tensor memory (a power of two)
+constexpr uint32_t kACol = 128;      // TMEM column of A stage 0 (the accumulator uses columns 0 .. NT-1)
+constexpr uint32_t kAStageCols = 64; // per A stage: hi part in 32 columns (64 f16 per lane), then lo
+constexpr uint32_t kTmemCols = 512;  // allocated TMEM columns (the whole SM's; one CTA per SM)
+constexpr int kDqWarps = 8;     // dequantising warps (2 .. 9, two groups of 4); warp 10 copies the activations
+constexpr int kBWarp = 2 + kDqWarps;
+constexpr int kThreads = 32 * (kBWarp + 1);
 constexpr uint32_t kRNib = kTM * 128;  // raw nibble bytes per stage
 constexpr uint32_t kRSc = kTM * 16;    // raw scale bytes per stage
 constexpr uint32_t kSpin = 1u << 22;
+constexpr uint32_t kNap = 64;  // ns between polls of a wait off the critical path
 constexpr float kWUnscale = 1.0f / 1024.0f;
 
-__host__ __device__ constexpr int b_stages(int nt) { return nt >= 128 ? 2 : 4; }
+__host__ __device__ constexpr int b_stages(int) { return 4; }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -102,11 +115,13 @@ __device__ __forceinline__ bool mbar_try(uint64_t* m, uint32_t parity) {
     return ok != 0;
 }
 // Bounded wait for the phase of parity `parity`; gives up when the CTA's abort word is set or
-// after kSpin polls (then sets it).
-__device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity, volatile int* abort) {
+// after kSpin polls (then sets it).  Waits off the critical path back off by `nap` ns between
+// polls, so that they leave the barrier unit to the MMA-issuing warp.
+__device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity, volatile int* abort, uint32_t nap = 0) {
     for (uint32_t i = 0; i < kSpin; ++i) {
         if (mbar_try(m, parity)) return true;
         if ((i & 63u) == 63u && *abort) return false;
+        if (nap) __nanosleep(nap);
     }
     *abort = 1;
     return false;
@@ -146,6 +161,26 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_
         ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
 }
+// The same with A read from tensor memory: row i of A in TMEM lane i, two f16 per 32-bit column.
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// True in exactly one lane of the (converged) warp.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "elect.sync _|P, 0xFFFFFFFF;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
 // Arrives on the mbarrier once every MMA issued so far by this thread has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* m) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(m))
@@ -166,20 +201,35 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(__uint_as_float(r[i]), kWUnscale);  // exact: a power of two
 }
 
+// Consecutive 32-bit columns of this thread's TMEM lane (warp-collective): 16 or 8 of them.
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
 template <int NT>
 struct TcSmem {
     uint8_t rnib[kRS][kRNib];                             // raw nibbles [128 rows][128 B], 128-byte swizzle
     uint8_t rsc[kRS][kRSc];                               // raw scales [128 rows][8]
-    uint8_t a[kAS][2][kTM * kKC * 2];                     // [stage][hi, lo] weights, core-matrix layout
     uint8_t b[b_stages(NT)][2][NT * kKC * 2];             // [stage][hi, lo] activations, same layout
     uint64_t r_full[kRS], r_empty[kRS], a_full[kAS], a_empty[kAS];
     uint64_t b_full[b_stages(NT)], b_empty[b_stages(NT)], done;
     uint32_t tmem;
     int abort;
 };
-// the TMA's 128-byte swizzle repeats every 1024 bytes: the shared-memory block is aligned to that
+// the TMA's 128-byte swizzle repeats every 1024 bytes: the shared-memory block is aligned to that;
+// at least 120 KB, so that one CTA holds an SM (and all of its tensor memory) at a time
 template <int NT>
-constexpr size_t smem_bytes() { return sizeof(TcSmem<NT>) + 1024; }
+constexpr size_t smem_bytes() { return sizeof(TcSmem<NT>) + 1024 > 120 * 1024 ? sizeof(TcSmem<NT>) + 1024 : 120 * 1024; }
 
 // byte offset of 8-element piece k8 of row `row` of a [rows x 64] K-major chunk in core-matrix
 // order: core matrix (row / 8, k8) at ((row / 8) * 8 + k8) * 128, row % 8 at 16-byte steps
@@ -198,29 +248,27 @@ __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) {
     return u;
 }
 
-// Dequantises one Q4_0 block (16 payload bytes, scale bits sbits) into four 8-element pieces of
-// hi parts and four of lo parts, in the K order described at the top of this file.
-__device__ __forceinline__ void dequant_block(uint4 q, uint16_t sbits, uint4 (&hi)[4], uint4 (&lo)[4]) {
+// Dequantises W payload words of one Q4_0 block (scale bits sbits): each word gives one 8-element
+// piece (4 half2) of hi parts and one of lo parts, in the K order described at the top of this file.
+template <int W>
+__device__ __forceinline__ void dequant_words(const uint32_t (&words)[W], uint16_t sbits, uint32_t (&h)[4 * W],
+                                              uint32_t (&l)[4 * W]) {
     // s * 2^10 is exact in f16 for every |s| <= 4
     const __half2 s2 = __half2half2(__hmul(__ushort_as_half(sbits), __ushort_as_half(0x6400)));
     const __half2 bias = u32_as_h2(0x64086408u);  // 1032 = 1024 + 8 in both halves
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int wi = 0; wi < 4; ++wi) {
+    for (int wi = 0; wi < W; ++wi) {
         const uint32_t w = words[wi];
         // 0x6400 | n is the f16 value 1024 + n; minus 1032 gives n - 8 exactly
         const uint32_t u[4] = {(w & 0x000F000Fu) | 0x64006400u, ((w >> 8) & 0x000F000Fu) | 0x64006400u,
                                ((w >> 4) & 0x000F000Fu) | 0x64006400u, ((w >> 12) & 0x000F000Fu) | 0x64006400u};
-        uint32_t h[4], l[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const __half2 qv = __hsub2(u32_as_h2(u[j]), bias);
             const __half2 hv = __hmul2_rn(qv, s2);
-            h[j] = h2_as_u32(hv);
-            l[j] = h2_as_u32(__hfma2(qv, s2, __hneg2(hv)));  // the exact remainder q * s' - hi
+            h[4 * wi + j] = h2_as_u32(hv);
+            l[4 * wi + j] = h2_as_u32(__hfma2(qv, s2, __hneg2(hv)));  // the exact remainder q * s' - hi
         }
-        hi[wi] = make_uint4(h[0], h[1], h[2], h[3]);
-        lo[wi] = make_uint4(l[0], l[1], l[2], l[3]);
     }
 }
 
@@ -235,7 +283,6 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
     extern __shared__ uint8_t tc_raw[];
     TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(tc_raw + ((1024u - (smem_u32(tc_raw) & 1023u)) & 1023u));
     constexpr int NBS = b_stages(NT);
-    constexpr uint32_t kCols = NT < 32 ? 32 : NT;  // TMEM columns (a power of two >= 32)
     constexpr uint32_t kBBytes = NT * kKC * 2;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int n0 = blockIdx.x * kTM, mt = blockIdx.y, z = blockIdx.z;
@@ -249,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
             mbar_init(&sm.r_empty[i], kDqWarps);
         }
         for (int i = 0; i < kAS; ++i) {
-            mbar_init(&sm.a_full[i], kDqWarps);
+            mbar_init(&sm.a_full[i], kDqWarps / 2);  // one group of four warps fills a stage
             mbar_init(&sm.a_empty[i], 1);
         }
         for (int i = 0; i < NBS; ++i) {
@@ -262,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem)),
-                     "r"(kCols)
+                     "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -271,88 +318,120 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = sm.tmem;
 
+    // The copy and MMA roles run as whole warps (loop state warp-uniform, so the addresses and
+    // descriptors stay in uniform registers) and issue from one elected lane.
     if (warp == 0) {
-        if (lane == 0) {
-            // copy engine: raw quad qi -> stage qi % kRS; activation chunk c -> stage c % NBS
-            const __half* xb = x16 + ((int64_t)mt * nch + 4 * q0) * (NT * kKC);
-            const int64_t part_elems = (int64_t)mtiles * NT * K;  // f16 elements per part of x16
-            int rq = 0, bc = 0;                                   // raw quads and chunks issued
-            bool ok = true;
-            for (int qi = 0; qi < nquads && ok; ++qi) {
-                const int s = qi % kRS;
-                if (qi >= kRS && !mbar_wait(&sm.r_empty[s], ((qi / kRS) - 1) & 1, abort)) break;
+        // weight copies: raw quad qi -> stage qi % kRS
+        int rq = 0;  // quads issued
+        for (int qi = 0; qi < nquads; ++qi) {
+            const int s = qi % kRS;
+            if (qi >= kRS && !__all_sync(0xFFFFFFFFu, mbar_wait(&sm.r_empty[s], ((qi / kRS) - 1) & 1, abort, kNap)))
+                break;
+            if (elect_one()) {
                 mbar_expect_tx(&sm.r_full[s], kRNib + kRSc);
                 tma_load_2d(sm.rnib[s], &tm_nib, (q0 + qi) * 128, n0, &sm.r_full[s]);
                 tma_load_2d(sm.rsc[s], &tm_sc, (q0 + qi) * 8, n0, &sm.r_full[s]);
-                rq = qi + 1;
-                for (int cq = 0; cq < 4; ++cq) {
-                    const int c = 4 * qi + cq, sb = c % NBS;
-                    if (c >= NBS && !mbar_wait(&sm.b_empty[sb], ((c / NBS) - 1) & 1, abort)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_expect_tx(&sm.b_full[sb], (x_lo ? 2u : 1u) * kBBytes);
-                    bulk_g2s(sm.b[sb][0], xb + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
-                    if (x_lo) bulk_g2s(sm.b[sb][1], xb + part_elems + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
-                    bc = c + 1;
-                }
             }
-            // the last copies of each stage have landed before the CTA can exit
-            for (int qi = std::max(0, rq - kRS); qi < rq; ++qi) mbar_drain(&sm.r_full[qi % kRS], (qi / kRS) & 1);
-            for (int c = std::max(0, bc - NBS); c < bc; ++c) mbar_drain(&sm.b_full[c % NBS], (c / NBS) & 1);
+            __syncwarp();
+            rq = qi + 1;
         }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = instr_desc_f16(kTM, NT);
-            for (int c = 0; c < nchunks; ++c) {
-                const int sa = c % kAS, sb = c % NBS;
-                if (!mbar_wait(&sm.a_full[sa], (c / kAS) & 1, abort)) break;
-                if (!mbar_wait(&sm.b_full[sb], (c / NBS) & 1, abort)) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t ah = smem_u32(sm.a[sa][0]), al = smem_u32(sm.a[sa][1]);
-                const uint32_t bh = smem_u32(sm.b[sb][0]), bl = smem_u32(sm.b[sb][1]);
-#pragma unroll
-                for (int k16 = 0; k16 < kKC / 16; ++k16) {
-                    // K = 16 is two core matrices along K: LBO 128 bytes, 8-row groups 1024 bytes apart
-                    const uint32_t o = k16 * 256;
-                    mma_f16(tmem, smem_desc(ah + o, 128, 1024), smem_desc(bh + o, 128, 1024), idesc,
-                            (c > 0 || k16 > 0) ? 1u : 0u);
-                    if (x_lo) mma_f16(tmem, smem_desc(ah + o, 128, 1024), smem_desc(bl + o, 128, 1024), idesc, 1u);
-                    mma_f16(tmem, smem_desc(al + o, 128, 1024), smem_desc(bh + o, 128, 1024), idesc, 1u);
-                }
-                mma_commit(&sm.a_empty[sa]);
-                mma_commit(&sm.b_empty[sb]);
-            }
-            mma_commit(&sm.done);  // also on abort: arrives once the MMAs issued so far are done
-        }
-    } else {
-        // dequantisers: thread dt of 256 -> weight row dt % 128, block dt / 128 of each chunk
-        const int dt = t - 64, row = dt & (kTM - 1), bb = dt >> 7;
-        const uint32_t rsw = (uint32_t)(row & 7);  // the swizzle's XOR for this row
+        // the last copy of each stage has landed before the CTA can exit
+        for (int qi = std::max(0, rq - kRS); qi < rq; ++qi) mbar_drain(&sm.r_full[qi % kRS], (qi / kRS) & 1);
+    } else if (warp == kBWarp) {
+        // activation copies: chunk c -> stage c % NBS
+        const __half* xb = x16 + ((int64_t)mt * nch + 4 * q0) * (NT * kKC);
+        const int64_t part_elems = (int64_t)mtiles * NT * K;  // f16 elements per part of x16
+        int bc = 0;                                           // chunks issued
         for (int c = 0; c < nchunks; ++c) {
-            const int qi = c >> 2, cq = c & 3, s = qi % kRS, sa = c % kAS;
-            bool ok = cq != 0 || mbar_wait(&sm.r_full[s], (qi / kRS) & 1, abort);
-            if (ok && c >= kAS) ok = mbar_wait(&sm.a_empty[sa], ((c / kAS) - 1) & 1, abort);
-            if (!__all_sync(0xFFFFFFFFu, ok)) break;  // the warp leaves together
-            const int j = 2 * cq + bb;  // block within the quad
-            const uint4 q = *reinterpret_cast<const uint4*>(sm.rnib[s] + row * 128 + (((uint32_t)j ^ rsw) << 4));
-            const uint16_t sbits = *reinterpret_cast<const uint16_t*>(sm.rsc[s] + row * 16 + j * 2);
-            // rows past the matrix were zero-filled by the TMA: scale 0 gives zero weights
-            uint4 hi[4], lo[4];
-            dequant_block(q, sbits, hi, lo);
-            uint8_t* Ah = sm.a[sa][0];
-            uint8_t* Al = sm.a[sa][1];
-#pragma unroll
-            for (int wi = 0; wi < 4; ++wi) {
-                *reinterpret_cast<uint4*>(Ah + core_off(row, 4 * bb + wi)) = hi[wi];
-                *reinterpret_cast<uint4*>(Al + core_off(row, 4 * bb + wi)) = lo[wi];
+            const int sb = c % NBS;
+            if (c >= NBS && !__all_sync(0xFFFFFFFFu, mbar_wait(&sm.b_empty[sb], ((c / NBS) - 1) & 1, abort, kNap)))
+                break;
+            if (elect_one()) {
+                mbar_expect_tx(&sm.b_full[sb], (x_lo ? 2u : 1u) * kBBytes);
+                bulk_g2s(sm.b[sb][0], xb + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
+                if (x_lo) bulk_g2s(sm.b[sb][1], xb + part_elems + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
             }
-            // generic-proxy writes of A -> visible to the tensor cores (async proxy)
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            bc = c + 1;
+        }
+        for (int c = std::max(0, bc - NBS); c < bc; ++c) mbar_drain(&sm.b_full[c % NBS], (c / NBS) & 1);
+    } else if (warp == 1) {
+        // chunks in pairs: one round trip waits for both chunks' A and B stages (lanes 0-7, 8-15,
+        // 16-23 and 24-31 poll one barrier each), then 24 MMAs go out back to back, since the
+        // tensor cores idle whenever this warp does anything else
+        const uint32_t idesc = instr_desc_f16(kTM, NT);
+        for (int c = 0; c < nchunks; c += 2) {
+            const int cc = c + ((lane >> 3) & 1);  // lanes 8-15 and 24-31: the pair's second chunk
+            uint64_t* const bar = lane < 16 ? &sm.a_full[cc % kAS] : &sm.b_full[cc % NBS];
+            const uint32_t par = lane < 16 ? (uint32_t)(cc / kAS) & 1u : (uint32_t)(cc / NBS) & 1u;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(bar, par, abort))) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            if (elect_one()) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int sa = (c + h) % kAS, sb = (c + h) % NBS;
+                    const uint32_t ah = tmem + kACol + sa * kAStageCols, al = ah + 32;
+                    const uint32_t bh = smem_u32(sm.b[sb][0]), bl = smem_u32(sm.b[sb][1]);
+#pragma unroll
+                    for (int k16 = 0; k16 < kKC / 16; ++k16) {
+                        // A: 8 TMEM columns per K = 16; B: two core matrices along K (LBO 128
+                        // bytes, 8-row groups 1024 bytes apart)
+                        const uint32_t oa = k16 * 8, ob = k16 * 256;
+                        mma_f16_ts(tmem, ah + oa, smem_desc(bh + ob, 128, 1024), idesc,
+                                   (c + h > 0 || k16 > 0) ? 1u : 0u);
+                        if (x_lo) mma_f16_ts(tmem, ah + oa, smem_desc(bl + ob, 128, 1024), idesc, 1u);
+                        mma_f16_ts(tmem, al + oa, smem_desc(bh + ob, 128, 1024), idesc, 1u);
+                    }
+                }
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    mma_commit(&sm.a_empty[(c + h) % kAS]);
+                    mma_commit(&sm.b_empty[(c + h) % NBS]);
+                }
+            }
+            __syncwarp();
+        }
+        if (elect_one()) mma_commit(&sm.done);  // also on abort: arrives once the MMAs issued so far are done
+        __syncwarp();
+    } else if (warp >= 2) {
+        // dequantisers: two groups of four warps take alternate chunks (group 0 the even ones);
+        // a warp may only reach TMEM lanes 32 (warp % 4) .. +31, so thread -> weight row
+        // 32 (warp % 4) + lane, and a thread dequantises the row's whole chunk (2 blocks, 8 words)
+        const int grp = (warp - 2) >> 2;
+        const int row = 32 * (warp & 3) + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+        const uint32_t rsw = (uint32_t)(row & 7);  // the swizzle's XOR for this row
+        for (int c = grp; c < nchunks; c += 2) {
+            const int qi = c >> 2, cq = c & 3, s = qi & (kRS - 1), sa = c & (kAS - 1);
+            // lanes 0-15 poll the raw quad (this group's first chunk of a quad), lanes 16-31 the
+            // A stage, in one loop
+            const bool need = lane < 16 ? cq == grp : c >= kAS;
+            uint64_t* const bar = lane < 16 ? &sm.r_full[s] : &sm.a_empty[sa];
+            const uint32_t par = lane < 16 ? (uint32_t)(qi / kRS) & 1u : (uint32_t)((c / kAS) - 1) & 1u;
+            if (!__all_sync(0xFFFFFFFFu, !need || mbar_wait(bar, par, abort, kNap))) break;  // the warp leaves together
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            // blocks 2 cq and 2 cq + 1 of the quad; their two scales are adjacent
+            const uint8_t* rn = sm.rnib[s] + row * 128;
+            const uint4 q0 = *reinterpret_cast<const uint4*>(rn + (((uint32_t)(2 * cq) ^ rsw) << 4));
+            const uint4 q1 = *reinterpret_cast<const uint4*>(rn + (((uint32_t)(2 * cq + 1) ^ rsw) << 4));
+            const uint32_t sc2 = *reinterpret_cast<const uint32_t*>(sm.rsc[s] + row * 16 + cq * 4);
+            // rows past the matrix were zero-filled by the TMA: scale 0 gives zero weights
+            const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w}, w1[4] = {q1.x, q1.y, q1.z, q1.w};
+            uint32_t h0[16], l0[16], h1[16], l1[16];
+            dequant_words<4>(w0, (uint16_t)(sc2 & 0xFFFFu), h0, l0);
+            dequant_words<4>(w1, (uint16_t)(sc2 >> 16), h1, l1);
+            // the stage's hi part: block 0 in columns 0-15, block 1 in 16-31; its lo part the same + 32
+            const uint32_t col = lane_base + kACol + sa * kAStageCols;
+            tmem_st(col, h0);
+            tmem_st(col + 16, h1);
+            tmem_st(col + 32, l0);
+            tmem_st(col + 48, l1);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&sm.a_full[sa]);
-                if (cq == 3) mbar_arrive(&sm.r_empty[s]);
+                if (cq == 2 + grp) mbar_arrive(&sm.r_empty[s]);  // this group's last chunk of the quad
             }
         }
         // accumulator -> partial sums (the done barrier completes after the last MMAs)
@@ -360,13 +439,13 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (__shfl_sync(0xFFFFFFFFu, *abort, 0) == 0) {  // warp-uniform: tcgen05.ld is warp-collective
-            const int quarter = warp & 3, half = (warp - 2) >> 2;
+            const int quarter = warp & 3, grp = (warp - 2) >> 2;  // two column groups of 16
             const int trow = quarter * 32 + lane;
             const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
             float* pz = part + (int64_t)z * M * n + n0 + trow;
             const bool row_ok = n0 + trow < n;
 #pragma unroll 1
-            for (int j0 = half * 16; j0 < NT; j0 += 32) {
+            for (int j0 = grp * 16; j0 < NT; j0 += 32) {
                 float v[16];
                 tmem_ld16(lane_addr + j0, v);
                 if (row_ok)
@@ -382,7 +461,8 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
     __syncthreads();
     if (t == 0 && *abort) atomicExch(err, 1);
     __syncwarp();
-    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
 int pick_nt(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
@@ -420,13 +500,25 @@ cudaError_t launch_gemm(const TcWeight& tw, const __half* x16, int x_lo, int M, 
     }
 }
 
-// Position within a 32-element block of element e of an 8-element piece (see the K order above).
-__device__ __forceinline__ int piece_elem(int e) { return ((e & 1) << 1) | ((e >> 1) & 1) | ((e >> 2) << 4); }
+// Four consecutive input elements k .. k+3 of a row (f32 rows are 16-byte aligned: K % 256 == 0).
+__device__ __forceinline__ float4 load4(const float* __restrict__ in, const __nv_bfloat16* __restrict__ in_bf16,
+                                        const __half* __restrict__ in_f16, int64_t k) {
+    if (in_f16)
+        return make_float4(__half2float(in_f16[k]), __half2float(in_f16[k + 1]), __half2float(in_f16[k + 2]),
+                           __half2float(in_f16[k + 3]));
+    if (in_bf16)
+        return make_float4(__bfloat162float(in_bf16[k]), __bfloat162float(in_bf16[k + 1]),
+                           __bfloat162float(in_bf16[k + 2]), __bfloat162float(in_bf16[k + 3]));
+    return *reinterpret_cast<const float4*>(in + k);
+}
 
-// f16 GEMM input of a batch, in the tiled K order of the kernel above.  One CTA per padded batch
-// row (mtiles * nt of them); row m < M is row m of `in` (f32, bf16 when in_bf16, f16 when in_f16),
-// with RMSNorm when alpha is not NULL (the same arithmetic as the GEMV's prologue: x / rms *
-// alpha); rows >= M are zero.  Writes the hi parts and, when lo != 0, the lo parts (x = hi + lo).
+// f16 GEMM input of a batch, in the tiled K order of the kernel above.  Grid: (padded batch rows
+// = mtiles * nt, groups of 256 pieces); a thread writes one 8-element piece.  Row m < M is row m
+// of `in` (f32, bf16 when in_bf16, f16 when in_f16), with RMSNorm when alpha is not NULL: x / rms
+// * alpha, rms = sqrt(mean(x^2) + 1e-8) (burn::nn::RmsNorm behind RmsNormLayer::forward,
+// model.rs:369-373), every CTA of a row summing it in the same order.  Rows >= M are zero.
+// Writes the hi parts and, when lo != 0, the lo parts (x = hi + lo).  Piece pi holds block pi / 4, word pi % 4: elements 4w + {0, 2, 1, 3}
+// and 16 + 4w + {0, 2, 1, 3} of the block, i.e. two aligned runs of four.
 __global__ void __launch_bounds__(256) prep_f16_kernel(const float* __restrict__ in, const __nv_bfloat16* __restrict__ in_bf16,
                                                        const __half* __restrict__ in_f16, const float* __restrict__ alpha,
                                                        int K, int M, int nt, int lo, __half* __restrict__ out) {
@@ -434,15 +526,16 @@ __global__ void __launch_bounds__(256) prep_f16_kernel(const float* __restrict__
     const int m = blockIdx.x, mt = m / nt, r = m - mt * nt;
     const int nch = K / kKC;
     const int64_t lo_off = (int64_t)gridDim.x * K;  // the lo parts follow the hi parts of all rows
-    uint8_t* const hi_base = reinterpret_cast<uint8_t*>(out + (int64_t)mt * nch * (nt * kKC));
-    uint8_t* const lo_base = reinterpret_cast<uint8_t*>(out + lo_off + (int64_t)mt * nch * (nt * kKC));
     const int64_t base = (int64_t)m * K;
     float rms = 1.0f;
     if (alpha && m < M) {
         float ss = 0.0f;
-        for (int j = threadIdx.x; j < K; j += blockDim.x) {
-            const float v = in[base + j];
-            ss = __fmaf_rn(v, v, ss);
+        for (int j = threadIdx.x; j < K / 4; j += blockDim.x) {
+            const float4 v = *reinterpret_cast<const float4*>(in + base + 4 * j);
+            ss = __fmaf_rn(v.x, v.x, ss);
+            ss = __fmaf_rn(v.y, v.y, ss);
+            ss = __fmaf_rn(v.z, v.z, ss);
+            ss = __fmaf_rn(v.w, v.w, ss);
         }
         ss = warp_sum(ss);
         if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -455,30 +548,40 @@ __global__ void __launch_bounds__(256) prep_f16_kernel(const float* __restrict__
         __syncthreads();
         rms = sqrtf(__fadd_rn(__fdiv_rn(red[0], (float)K), 1e-8f));
     }
-    // piece pi: 8 elements of block pi / 4, word pi % 4; chunk pi / 8, piece pi % 8 of the chunk
-    for (int pi = threadIdx.x; pi < K / 8; pi += blockDim.x) {
-        const int blk = pi >> 2, wi = pi & 3;
-        const size_t off = (size_t)(pi >> 3) * (nt * kKC * 2) + core_off(r, pi & 7);
-        __align__(16) __half h[8], l[8];
+    const int pi = blockIdx.y * blockDim.x + threadIdx.x;
+    if (pi >= K / 8) return;
+    const int k0 = (pi >> 2) * 32 + 4 * (pi & 3);
+    float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    if (m < M) {
+        const float4 a = load4(in, in_bf16, in_f16, base + k0), b = load4(in, in_bf16, in_f16, base + k0 + 16);
+        const float x[8] = {a.x, a.z, a.y, a.w, b.x, b.z, b.y, b.w};
+        if (alpha) {
+            const float4 ga = *reinterpret_cast<const float4*>(alpha + k0);
+            const float4 gb = *reinterpret_cast<const float4*>(alpha + k0 + 16);
+            const float g[8] = {ga.x, ga.z, ga.y, ga.w, gb.x, gb.z, gb.y, gb.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            float v = 0.0f;
-            if (m < M) {
-                const int64_t k = base + blk * 32 + 4 * wi + piece_elem(e);
-                v = in_f16 ? __half2float(in_f16[k]) : in_bf16 ? __bfloat162float(in_bf16[k]) : in[k];
-                if (alpha) v = __fmul_rn(__fdiv_rn(v, rms), alpha[blk * 32 + 4 * wi + piece_elem(e)]);
-            }
-            h[e] = __float2half_rn(v);
-            l[e] = __float2half_rn(__fsub_rn(v, __half2float(h[e])));
+            for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fdiv_rn(x[e], rms), g[e]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = x[e];
         }
-        *reinterpret_cast<uint4*>(hi_base + off) = *reinterpret_cast<const uint4*>(h);
-        if (lo) *reinterpret_cast<uint4*>(lo_base + off) = *reinterpret_cast<const uint4*>(l);
     }
+    __align__(16) __half h[8], l[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        h[e] = __float2half_rn(v[e]);
+        l[e] = __float2half_rn(__fsub_rn(v[e], __half2float(h[e])));
+    }
+    // chunk pi / 8, piece pi % 8 of the chunk, in row tile mt
+    const size_t off = ((size_t)mt * nch + (pi >> 3)) * (nt * kKC * 2) + core_off(r, pi & 7);
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out) + off) = *reinterpret_cast<const uint4*>(h);
+    if (lo) *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + lo_off) + off) = *reinterpret_cast<const uint4*>(l);
 }
 
 cudaError_t launch_prep(const float* in, const __nv_bfloat16* in_bf16, const __half* in_f16, const float* alpha, int K,
                         int M, const TcPlan& p, int lo, __half* x16, cudaStream_t st) {
-    prep_f16_kernel<<<p.mtiles * p.nt, 256, 0, st>>>(in, in_bf16, in_f16, alpha, K, M, p.nt, lo, x16);
+    dim3 grid(p.mtiles * p.nt, (K / 8 + 255) / 256);
+    prep_f16_kernel<<<grid, 256, 0, st>>>(in, in_bf16, in_f16, alpha, K, M, p.nt, lo, x16);
     return cudaGetLastError();
 }
 
