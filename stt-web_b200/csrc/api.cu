@@ -575,35 +575,60 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
     stt_model* m = s->m;
     const Ctx c = make_ctx(s, n);
     const int grid = 2 * m->num_sms;
-    // batches of kTcMinBatch streams or more: layer products on the tensor cores (f16 operands)
-    const bool tc = n >= kTcMinBatch && m->tc_ok && std::getenv("STT_DISABLE_TC") == nullptr;
-    auto layer = [&](const GemvArgs& a, int w, int epi) -> cudaError_t {
-        return tc ? launch_tc_layer(c, a, m->tc_w[w], epi, n, s->d_x16, s->d_tc_part, s->d_tc_err, m->num_sms, st)
-                  : launch_gemv(c, a, epi, n, grid, st);
-    };
     CUDA_TRY(launch_embed(c, st));
+    // batches of kTcMinBatch streams or more: layer products on the tensor cores, each product's
+    // epilogue writing the next one's f16 input tiles
+    if (n >= kTcMinBatch && m->tc_ok && std::getenv("STT_DISABLE_TC") == nullptr) {
+        Ctx ca = c;
+        ca.x16 = s->d_x16;
+        tc_batch_tiles(n, &ca.x16_nt, &ca.x16_rows_pad);
+        float* part = s->d_tc_part;
+        int slices = 0;
+        CUDA_TRY(launch_tc_prep(s->d_x, m->h_layers[0].norm1, m->D, n, s->d_x16, st));
+        for (int l = 0; l < m->L; ++l) {
+            const LayerDev& L = m->h_layers[l];
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 0], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+            GemvArgs a{};
+            a.W = L.qkv; a.out = s->d_qkv; a.ldo = 3 * m->D; a.layer = l; a.n_units = 3 * m->D / 2;
+            CUDA_TRY(launch_tc_epilogue(c, a, EPI_QKV, n, part, slices, st));
+            CUDA_TRY(launch_attention(ca, l, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 1], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_resid_norm(s->d_x, part, slices, n, m->D, L.norm2, s->d_x16, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 2], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_gate(part, slices, n, m->F, s->d_x16, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 3], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+            const float* next_norm = l + 1 < m->L ? m->h_layers[l + 1].norm1 : m->out_norm;
+            CUDA_TRY(launch_tc_resid_norm(s->d_x, part, slices, n, m->D, next_norm, s->d_x16, st));
+        }
+        CUDA_TRY(launch_tc_product(m->tc_w[4 * m->L], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+        GemvArgs a{};
+        a.W = m->head; a.out = s->d_logits; a.ldo = m->V; a.n_units = (m->V + 1) / 2;
+        CUDA_TRY(launch_tc_epilogue(c, a, EPI_LOGITS, n, part, slices, st));
+        CUDA_TRY(launch_finish(c, st));
+        return STT_OK;
+    }
     for (int l = 0; l < m->L; ++l) {
         const LayerDev& L = m->h_layers[l];
         GemvArgs a{};
         a.W = L.qkv; a.in = s->d_x; a.norm = L.norm1; a.out = s->d_qkv; a.ldo = 3 * m->D; a.layer = l;
         a.n_units = 3 * m->D / 2;
-        CUDA_TRY(layer(a, 4 * l + 0, EPI_QKV));
+        CUDA_TRY(launch_gemv(c, a, EPI_QKV, n, grid, st));
         CUDA_TRY(launch_attention(c, l, st));
         a = GemvArgs{};
         a.W = L.out; a.in = s->d_attn; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
-        CUDA_TRY(layer(a, 4 * l + 1, EPI_RESID));
+        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, grid, st));
         a = GemvArgs{};
         a.W = L.fin; a.in = s->d_x; a.norm = L.norm2; a.out = s->d_hid; a.ldo = m->F; a.n_units = m->F;
         a.half_n = m->F;
-        CUDA_TRY(layer(a, 4 * l + 2, EPI_GATE));
+        CUDA_TRY(launch_gemv(c, a, EPI_GATE, n, grid, st));
         a = GemvArgs{};
         a.W = L.fout; a.in = s->d_hid; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
-        CUDA_TRY(layer(a, 4 * l + 3, EPI_RESID));
+        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, grid, st));
     }
     GemvArgs a{};
     a.W = m->head; a.in = s->d_x; a.norm = m->out_norm; a.out = s->d_logits; a.ldo = m->V;
     a.n_units = (m->V + 1) / 2;
-    CUDA_TRY(layer(a, 4 * m->L, EPI_LOGITS));
+    CUDA_TRY(launch_gemv(c, a, EPI_LOGITS, n, grid, st));
     CUDA_TRY(launch_finish(c, st));
     return STT_OK;
 }

@@ -97,6 +97,10 @@ struct Ctx {
     float* amax_val;    // [n][amax_ctas]
     int32_t* amax_idx;  // [n][amax_ctas]
     int32_t nsplit, chunk;
+    // tensor-core steps: the attention kernel also writes its output as the output projection's
+    // f16 input tiles (tc_layout.cuh); NULL otherwise
+    __half* x16;
+    int32_t x16_nt, x16_rows_pad;
 };
 
 // ---------------------------------------------------------------------------- helpers
@@ -124,6 +128,31 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ void raise_error(StepDesc* d, int32_t code) {
     if (d) atomicCAS(&d->error, 0, code);
+}
+
+// Programmatic dependent launch.  A kernel launched with launch_pdl may start while the previous
+// kernel of the stream is still running: it must call pdl_wait() before it touches anything that
+// kernel writes or reads (pdl_wait returns once that kernel has completed and its writes are
+// visible; it returns at once for a kernel launched the ordinary way), and every one of its CTAs
+// must call it before exiting, so that completion stays ordered along the stream.  pdl_trigger()
+// lets the next kernel's CTAs be scheduled before this one finishes.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 }  // namespace stt

@@ -16,6 +16,7 @@
 
 #include "device.cuh"
 #include "kernels.h"
+#include "tc_layout.cuh"
 
 namespace stt {
 
@@ -293,6 +294,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(Ctx c, GemvArgs a, int row0, 
 template <int EPI>
 __global__ void __launch_bounds__(256) tc_epilogue_kernel(Ctx c, GemvArgs a, const float* __restrict__ part, int rows,
                                                          int slices) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t total = (int64_t)rows * a.n_units;
     const int64_t plane = (int64_t)rows * a.W.n;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -317,6 +320,8 @@ __global__ void __launch_bounds__(256) tc_epilogue_kernel(Ctx c, GemvArgs a, con
 // combines the partials in split order and writes attn[row][head].
 template <typename KT>
 __global__ void __launch_bounds__(128) attn_kernel(Ctx c, int layer) {
+    pdl_trigger();
+    pdl_wait();
     const int s = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sid = c.ids[i];
@@ -423,6 +428,15 @@ __global__ void __launch_bounds__(128) attn_kernel(Ctx c, int layer) {
         }
         float4 r = make_float4(__fdiv_rn(O.x, L), __fdiv_rn(O.y, L), __fdiv_rn(O.z, L), __fdiv_rn(O.w, L));
         reinterpret_cast<float4*>(c.attn + (int64_t)i * c.D + h * HD)[lane] = r;
+        if (c.x16) {
+            // lane holds elements 4 lane .. +3 of the head: a piece of block h*4 + lane/8 takes
+            // word w = lane % 8 (< 4) from this lane and w + 16 from lane + 4
+            const float4 b = make_float4(__shfl_down_sync(0xFFFFFFFFu, r.x, 4), __shfl_down_sync(0xFFFFFFFFu, r.y, 4),
+                                         __shfl_down_sync(0xFFFFFFFFu, r.z, 4), __shfl_down_sync(0xFFFFFFFFu, r.w, 4));
+            if ((lane & 7) < 4)
+                x16_store_piece(c.x16, c.x16_nt, c.x16_rows_pad, c.D, i, (h * 4 + (lane >> 3)) * 4 + (lane & 7), r, b,
+                                true);
+        }
         if (lane == 0) c.tickets[i * c.H + h] = 0u;
     }
 }
@@ -608,9 +622,8 @@ cudaError_t launch_embed(const Ctx& c, cudaStream_t st) {
 
 cudaError_t launch_attention(const Ctx& c, int layer, cudaStream_t st) {
     dim3 grid(c.nsplit, c.H, c.n);
-    if (c.kv_f32) attn_kernel<float><<<grid, 128, 0, st>>>(c, layer);
-    else attn_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(c, layer);
-    return cudaGetLastError();
+    if (c.kv_f32) return launch_pdl(attn_kernel<float>, grid, dim3(128), 0, st, c, layer);
+    return launch_pdl(attn_kernel<__nv_bfloat16>, grid, dim3(128), 0, st, c, layer);
 }
 
 cudaError_t launch_finish(const Ctx& c, cudaStream_t st) {
@@ -624,13 +637,13 @@ cudaError_t launch_tc_epilogue(const Ctx& c, const GemvArgs& a, int epi, int row
     const int grid = (int)std::min<int64_t>((total + 255) / 256, 8192);
     if (grid <= 0) return cudaSuccess;
     switch (epi) {
-        case EPI_QKV: tc_epilogue_kernel<EPI_QKV><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
-        case EPI_GATE: tc_epilogue_kernel<EPI_GATE><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
-        case EPI_RESID: tc_epilogue_kernel<EPI_RESID><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
-        case EPI_LOGITS: tc_epilogue_kernel<EPI_LOGITS><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
-        default: tc_epilogue_kernel<EPI_PLAIN><<<grid, 256, 0, st>>>(c, a, part, rows, slices); break;
+        case EPI_QKV: return launch_pdl(tc_epilogue_kernel<EPI_QKV>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
+        case EPI_GATE: return launch_pdl(tc_epilogue_kernel<EPI_GATE>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
+        case EPI_RESID: return launch_pdl(tc_epilogue_kernel<EPI_RESID>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
+        case EPI_LOGITS:
+            return launch_pdl(tc_epilogue_kernel<EPI_LOGITS>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
+        default: return launch_pdl(tc_epilogue_kernel<EPI_PLAIN>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
     }
-    return cudaGetLastError();
 }
 
 }  // namespace stt

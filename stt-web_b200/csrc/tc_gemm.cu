@@ -53,6 +53,7 @@
 #include <algorithm>
 
 #include "kernels.h"
+#include "tc_layout.cuh"
 
 namespace stt {
 
@@ -231,12 +232,6 @@ struct TcSmem {
 template <int NT>
 constexpr size_t smem_bytes() { return sizeof(TcSmem<NT>) + 1024 > 120 * 1024 ? sizeof(TcSmem<NT>) + 1024 : 120 * 1024; }
 
-// byte offset of 8-element piece k8 of row `row` of a [rows x 64] K-major chunk in core-matrix
-// order: core matrix (row / 8, k8) at ((row / 8) * 8 + k8) * 128, row % 8 at 16-byte steps
-__host__ __device__ __forceinline__ uint32_t core_off(int row, int k8) {
-    return ((row >> 3) * 8 + k8) * 128 + (row & 7) * 16;
-}
-
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) {
     __half2 h;
     memcpy(&h, &u, 4);
@@ -335,10 +330,13 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
             __syncwarp();
             rq = qi + 1;
         }
+        pdl_trigger();
         // the last copy of each stage has landed before the CTA can exit
         for (int qi = std::max(0, rq - kRS); qi < rq; ++qi) mbar_drain(&sm.r_full[qi % kRS], (qi / kRS) & 1);
     } else if (warp == kBWarp) {
-        // activation copies: chunk c -> stage c % NBS
+        // activation copies: chunk c -> stage c % NBS.  The activations come from the previous
+        // kernel of the stream (launched as a programmatic dependent, this kernel may start first)
+        pdl_wait();
         const __half* xb = x16 + ((int64_t)mt * nch + 4 * q0) * (NT * kKC);
         const int64_t part_elems = (int64_t)mtiles * NT * K;  // f16 elements per part of x16
         int bc = 0;                                           // chunks issued
@@ -354,6 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
             __syncwarp();
             bc = c + 1;
         }
+        pdl_trigger();
         for (int c = std::max(0, bc - NBS); c < bc; ++c) mbar_drain(&sm.b_full[c % NBS], (c / NBS) & 1);
     } else if (warp == 1) {
         // chunks in pairs: one round trip waits for both chunks' A and B stages (lanes 0-7, 8-15,
@@ -393,6 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         }
         if (elect_one()) mma_commit(&sm.done);  // also on abort: arrives once the MMAs issued so far are done
         __syncwarp();
+        pdl_trigger();
     } else if (warp >= 2) {
         // dequantisers: two groups of four warps take alternate chunks (group 0 the even ones);
         // a warp may only reach TMEM lanes 32 (warp % 4) .. +31, so thread -> weight row
@@ -435,6 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
             }
         }
         // accumulator -> partial sums (the done barrier completes after the last MMAs)
+        pdl_trigger();
+        pdl_wait();
         mbar_drain(&sm.done, 0);
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -485,9 +487,8 @@ cudaError_t launch_nt(const TcWeight& tw, const __half* x16, int x_lo, int M, co
     cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p.tiles, p.mtiles, p.slices);
-    q4_tc_kernel<NT><<<grid, kThreads, smem, st>>>(tw.nib, tw.sc, tw.n, tw.k, x16, x_lo, M, p.mtiles, p.slices, part,
-                                                   err);
-    return cudaGetLastError();
+    return launch_pdl(q4_tc_kernel<NT>, grid, dim3(kThreads), smem, st, tw.nib, tw.sc, tw.n, tw.k, x16, x_lo, M,
+                      p.mtiles, p.slices, part, err);
 }
 
 cudaError_t launch_gemm(const TcWeight& tw, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
@@ -512,70 +513,138 @@ __device__ __forceinline__ float4 load4(const float* __restrict__ in, const __nv
     return *reinterpret_cast<const float4*>(in + k);
 }
 
-// f16 GEMM input of a batch, in the tiled K order of the kernel above.  Grid: (padded batch rows
-// = mtiles * nt, groups of 256 pieces); a thread writes one 8-element piece.  Row m < M is row m
-// of `in` (f32, bf16 when in_bf16, f16 when in_f16), with RMSNorm when alpha is not NULL: x / rms
-// * alpha, rms = sqrt(mean(x^2) + 1e-8) (burn::nn::RmsNorm behind RmsNormLayer::forward,
-// model.rs:369-373), every CTA of a row summing it in the same order.  Rows >= M are zero.
-// Writes the hi parts and, when lo != 0, the lo parts (x = hi + lo).  Piece pi holds block pi / 4, word pi % 4: elements 4w + {0, 2, 1, 3}
-// and 16 + 4w + {0, 2, 1, 3} of the block, i.e. two aligned runs of four.
+// Sum of squares of row[0 .. K) (K % 4 == 0), the same in every thread of the CTA: float4
+// loads, per-thread sums in order x, y, z, w, then warp and CTA sums.
+__device__ __forceinline__ float row_sumsq(const float* __restrict__ row, int K, float* red) {
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < K / 4; j += blockDim.x) {
+        const float4 v = *reinterpret_cast<const float4*>(row + 4 * j);
+        ss = __fmaf_rn(v.x, v.x, ss);
+        ss = __fmaf_rn(v.y, v.y, ss);
+        ss = __fmaf_rn(v.z, v.z, ss);
+        ss = __fmaf_rn(v.w, v.w, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+// RMSNorm of a row: x / rms * alpha, rms = sqrt(mean(x^2) + 1e-8) (burn::nn::RmsNorm behind
+// RmsNormLayer::forward, model.rs:369-373; the GEMV's prologue computes the same).
+__device__ __forceinline__ float4 rms_scale(float4 v, float rms, const float* __restrict__ alpha, int k) {
+    const float4 g = *reinterpret_cast<const float4*>(alpha + k);
+    return make_float4(__fmul_rn(__fdiv_rn(v.x, rms), g.x), __fmul_rn(__fdiv_rn(v.y, rms), g.y),
+                       __fmul_rn(__fdiv_rn(v.z, rms), g.z), __fmul_rn(__fdiv_rn(v.w, rms), g.w));
+}
+
+// f16 GEMM input of a batch (x16, layout in tc_layout.cuh).  Grid: (padded batch rows, groups of
+// 256 pieces); a thread writes one piece.  Row m < M is row m of `in` (f32, bf16 when in_bf16, f16
+// when in_f16), RMSNorm'd when alpha is not NULL; rows >= M are zero.  Writes the hi parts and,
+// when lo != 0, the lo parts.
 __global__ void __launch_bounds__(256) prep_f16_kernel(const float* __restrict__ in, const __nv_bfloat16* __restrict__ in_bf16,
                                                        const __half* __restrict__ in_f16, const float* __restrict__ alpha,
                                                        int K, int M, int nt, int lo, __half* __restrict__ out) {
     __shared__ float red[32];
-    const int m = blockIdx.x, mt = m / nt, r = m - mt * nt;
-    const int nch = K / kKC;
-    const int64_t lo_off = (int64_t)gridDim.x * K;  // the lo parts follow the hi parts of all rows
+    const int m = blockIdx.x;
     const int64_t base = (int64_t)m * K;
-    float rms = 1.0f;
-    if (alpha && m < M) {
-        float ss = 0.0f;
-        for (int j = threadIdx.x; j < K / 4; j += blockDim.x) {
-            const float4 v = *reinterpret_cast<const float4*>(in + base + 4 * j);
-            ss = __fmaf_rn(v.x, v.x, ss);
-            ss = __fmaf_rn(v.y, v.y, ss);
-            ss = __fmaf_rn(v.z, v.z, ss);
-            ss = __fmaf_rn(v.w, v.w, ss);
-        }
-        ss = warp_sum(ss);
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-        __syncthreads();
-        if (threadIdx.x < 32) {
-            float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-            v = warp_sum(v);
-            if (threadIdx.x == 0) red[0] = v;
-        }
-        __syncthreads();
-        rms = sqrtf(__fadd_rn(__fdiv_rn(red[0], (float)K), 1e-8f));
-    }
+    const float rms = alpha && m < M ? sqrtf(__fadd_rn(__fdiv_rn(row_sumsq(in + base, K, red), (float)K), 1e-8f)) : 1.0f;
     const int pi = blockIdx.y * blockDim.x + threadIdx.x;
     if (pi >= K / 8) return;
-    const int k0 = (pi >> 2) * 32 + 4 * (pi & 3);
-    float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    const int k0 = piece_k0(pi);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
     if (m < M) {
-        const float4 a = load4(in, in_bf16, in_f16, base + k0), b = load4(in, in_bf16, in_f16, base + k0 + 16);
-        const float x[8] = {a.x, a.z, a.y, a.w, b.x, b.z, b.y, b.w};
+        a = load4(in, in_bf16, in_f16, base + k0);
+        b = load4(in, in_bf16, in_f16, base + k0 + 16);
         if (alpha) {
-            const float4 ga = *reinterpret_cast<const float4*>(alpha + k0);
-            const float4 gb = *reinterpret_cast<const float4*>(alpha + k0 + 16);
-            const float g[8] = {ga.x, ga.z, ga.y, ga.w, gb.x, gb.z, gb.y, gb.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fdiv_rn(x[e], rms), g[e]);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = x[e];
+            a = rms_scale(a, rms, alpha, k0);
+            b = rms_scale(b, rms, alpha, k0 + 16);
         }
     }
-    __align__(16) __half h[8], l[8];
+    x16_store_piece(out, nt, gridDim.x, K, m, pi, a, b, lo != 0);
+}
+
+// Residual epilogue fused with the next product's input: one CTA per batch row m.
+// x[m] += sum over slices of part[z][m] (slices added in order, then the residual, as the GEMV's
+// residual epilogue does), then x16 row m = RMSNorm(x[m]) * alpha, hi and lo parts.
+__global__ void __launch_bounds__(512) resid_norm_kernel(float* __restrict__ x, const float* __restrict__ part, int slices,
+                                                         int rows, int D, const float* __restrict__ alpha,
+                                                         __half* __restrict__ x16, int nt, int rows_pad) {
+    extern __shared__ float4 vrow[];  // the updated row
+    __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
+    const int m = blockIdx.x;
+    float4* xr = reinterpret_cast<float4*>(x + (int64_t)m * D);
+    const float* pm = part + (int64_t)m * D;
+    const int64_t plane = (int64_t)rows * D;
+    for (int j = threadIdx.x; j < D / 4; j += blockDim.x) {
+        float4 sum = reinterpret_cast<const float4*>(pm)[j];
+        // slices 1 .. in groups of 4 loads issued together, added in slice order
+        for (int z0 = 1; z0 < slices; z0 += 4) {
+            float4 p[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        h[e] = __float2half_rn(v[e]);
-        l[e] = __float2half_rn(__fsub_rn(v[e], __half2float(h[e])));
+            for (int u = 0; u < 4; ++u)
+                if (z0 + u < slices) p[u] = reinterpret_cast<const float4*>(pm + (z0 + u) * plane)[j];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (z0 + u < slices)
+                    sum = make_float4(__fadd_rn(sum.x, p[u].x), __fadd_rn(sum.y, p[u].y), __fadd_rn(sum.z, p[u].z),
+                                      __fadd_rn(sum.w, p[u].w));
+        }
+        const float4 o = xr[j];
+        const float4 v = make_float4(__fadd_rn(sum.x, o.x), __fadd_rn(sum.y, o.y), __fadd_rn(sum.z, o.z), __fadd_rn(sum.w, o.w));
+        xr[j] = v;
+        vrow[j] = v;
     }
-    // chunk pi / 8, piece pi % 8 of the chunk, in row tile mt
-    const size_t off = ((size_t)mt * nch + (pi >> 3)) * (nt * kKC * 2) + core_off(r, pi & 7);
-    *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out) + off) = *reinterpret_cast<const uint4*>(h);
-    if (lo) *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out + lo_off) + off) = *reinterpret_cast<const uint4*>(l);
+    __syncthreads();
+    const float rms = sqrtf(__fadd_rn(__fdiv_rn(row_sumsq(reinterpret_cast<const float*>(vrow), D, red), (float)D), 1e-8f));
+    for (int pi = threadIdx.x; pi < D / 8; pi += blockDim.x) {
+        const int k0 = piece_k0(pi);
+        x16_store_piece(x16, nt, rows_pad, D, m, pi, rms_scale(vrow[k0 / 4], rms, alpha, k0),
+                        rms_scale(vrow[k0 / 4 + 4], rms, alpha, k0 + 16), true);
+    }
+}
+
+// silu(g) = g * (1 / (1 + exp(-g))), times the value: the GEMV's gate epilogue.
+__device__ __forceinline__ float gated(float g, float v) {
+    return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), v);
+}
+
+// Gate epilogue fused with the next product's input: part[z][m][0 .. 2F) holds the gate rows
+// (0 .. F) and value rows (F .. 2F) of linear_in; x16 row m = silu(gate) * value, hi and lo parts.
+// A thread writes one piece of one row.
+__global__ void __launch_bounds__(256) gate_kernel(const float* __restrict__ part, int slices, int rows, int F,
+                                                   __half* __restrict__ x16, int nt, int rows_pad) {
+    pdl_trigger();
+    pdl_wait();
+    const int npieces = F / 8;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= rows * npieces) return;
+    const int m = idx / npieces, pi = idx - m * npieces;
+    const int k0 = piece_k0(pi);
+    const int64_t plane = (int64_t)rows * 2 * F;
+    const float* pm = part + (int64_t)m * 2 * F;
+    float4 r[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+        const int k = k0 + 16 * hh;
+        float4 g = *reinterpret_cast<const float4*>(pm + k), v = *reinterpret_cast<const float4*>(pm + F + k);
+        for (int z = 1; z < slices; ++z) {
+            const float4 gz = *reinterpret_cast<const float4*>(pm + z * plane + k);
+            const float4 vz = *reinterpret_cast<const float4*>(pm + z * plane + F + k);
+            g = make_float4(__fadd_rn(g.x, gz.x), __fadd_rn(g.y, gz.y), __fadd_rn(g.z, gz.z), __fadd_rn(g.w, gz.w));
+            v = make_float4(__fadd_rn(v.x, vz.x), __fadd_rn(v.y, vz.y), __fadd_rn(v.z, vz.z), __fadd_rn(v.w, vz.w));
+        }
+        r[hh] = make_float4(gated(g.x, v.x), gated(g.y, v.y), gated(g.z, v.z), gated(g.w, v.w));
+    }
+    x16_store_piece(x16, nt, rows_pad, F, m, pi, r[0], r[1], true);
 }
 
 cudaError_t launch_prep(const float* in, const __nv_bfloat16* in_bf16, const __half* in_f16, const float* alpha, int K,
@@ -663,14 +732,36 @@ cudaError_t launch_q4_tc_gemm(const TcWeight& tw, const Q4Dev& w, const __half* 
     return launch_tc_epilogue(Ctx{}, a, EPI_PLAIN, M, part, p.slices, st);
 }
 
-cudaError_t launch_tc_layer(const Ctx& c, const GemvArgs& a, const TcWeight& tw, int epi, int rows, __half* x16,
-                            float* part, int* err, int num_sms, cudaStream_t st) {
-    const TcPlan p = make_plan(a.W.n, a.W.k, rows, num_sms);
-    cudaError_t e = launch_prep(a.in, a.in_bf16, nullptr, a.norm, a.W.k, rows, p, 1, x16, st);
-    if (e != cudaSuccess) return e;
-    e = launch_gemm(tw, x16, 1, rows, p, part, err, st);
-    if (e != cudaSuccess) return e;
-    return launch_tc_epilogue(c, a, epi, rows, part, p.slices, st);
+void tc_batch_tiles(int rows, int* nt, int* rows_pad) {
+    const TcPlan p = make_plan(1, kQuad, rows, 1);
+    *nt = p.nt;
+    *rows_pad = p.mtiles * p.nt;
+}
+
+cudaError_t launch_tc_prep(const float* in, const float* alpha, int K, int rows, __half* x16, cudaStream_t st) {
+    return launch_prep(in, nullptr, nullptr, alpha, K, rows, make_plan(1, K, rows, 1), 1, x16, st);
+}
+
+cudaError_t launch_tc_product(const TcWeight& tw, const __half* x16, int rows, float* part, int* err, int num_sms,
+                              int* slices, cudaStream_t st) {
+    const TcPlan p = make_plan(tw.n, tw.k, rows, num_sms);
+    *slices = p.slices;
+    return launch_gemm(tw, x16, 1, rows, p, part, err, st);
+}
+
+cudaError_t launch_tc_resid_norm(float* x, const float* part, int slices, int rows, int D, const float* alpha,
+                                 __half* x16, cudaStream_t st) {
+    int nt, rows_pad;
+    tc_batch_tiles(rows, &nt, &rows_pad);
+    return launch_pdl(resid_norm_kernel, dim3(rows), dim3(512), (size_t)D * sizeof(float), st, x, part, slices, rows, D,
+                      alpha, x16, nt, rows_pad);
+}
+
+cudaError_t launch_tc_gate(const float* part, int slices, int rows, int F, __half* x16, cudaStream_t st) {
+    int nt, rows_pad;
+    tc_batch_tiles(rows, &nt, &rows_pad);
+    const int total = rows * (F / 8);
+    return launch_pdl(gate_kernel, dim3((total + 255) / 256), dim3(256), 0, st, part, slices, rows, F, x16, nt, rows_pad);
 }
 
 }  // namespace stt

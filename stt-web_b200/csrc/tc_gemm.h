@@ -41,15 +41,24 @@ size_t tc_part_bytes(const Q4Dev& w, int M, int num_sms);
 cudaError_t launch_q4_tc_gemm(const TcWeight& tw, const Q4Dev& w, const __half* x, int M, float* out, int64_t ldo,
                               __half* x16, float* part, int* err, int num_sms, cudaStream_t st);
 
-struct Ctx;
-struct GemvArgs;
 // Smallest batch the step's layers run on the tensor cores (smaller batches use the GEMV).
 constexpr int kTcMinBatch = 16;
-// One layer product of a batched decode step on the tensor cores: the input rows (RMSNorm'd with
-// a.norm when set) are split into f16 hi and lo parts in x16, the GEMM writes K-slice partial sums
-// to part, and the epilogue kernel adds them in slice order and applies `epi` (EPI_QKV, EPI_RESID,
-// EPI_GATE, EPI_LOGITS or EPI_PLAIN) exactly as the GEMV does.
-cudaError_t launch_tc_layer(const Ctx& c, const GemvArgs& a, const TcWeight& tw, int epi, int rows, __half* x16,
-                            float* part, int* err, int num_sms, cudaStream_t st);
+
+// A batched decode step on the tensor cores keeps every product's input in x16 (tc_layout.cuh):
+// launch_tc_prep writes it for the first product, and each product's epilogue writes the next
+// one's (launch_tc_resid_norm, launch_tc_gate; the attention kernel for the output projection).
+// Batch rows per tile and padded rows of a batch of `rows`.
+void tc_batch_tiles(int rows, int* nt, int* rows_pad);
+// x16 = rows of `in` [rows][K], RMSNorm'd with alpha when set.
+cudaError_t launch_tc_prep(const float* in, const float* alpha, int K, int rows, __half* x16, cudaStream_t st);
+// The GEMM: K-slice partial sums part[slices][rows][tw.n] of the weight times the x16 rows; the
+// slice count is returned in *slices.
+cudaError_t launch_tc_product(const TcWeight& tw, const __half* x16, int rows, float* part, int* err, int num_sms,
+                              int* slices, cudaStream_t st);
+// x[rows][D] += the slices (in order); x16 = RMSNorm(x) * alpha.
+cudaError_t launch_tc_resid_norm(float* x, const float* part, int slices, int rows, int D, const float* alpha,
+                                 __half* x16, cudaStream_t st);
+// x16 = silu(gate) * value of the linear_in slices ([slices][rows][2F]: gate rows, then value rows).
+cudaError_t launch_tc_gate(const float* part, int slices, int rows, int F, __half* x16, cudaStream_t st);
 
 }  // namespace stt
