@@ -315,66 +315,128 @@ __global__ void __launch_bounds__(256) tc_epilogue_kernel(Ctx c, GemvArgs a, con
 
 // ------------------------------------------------------------------------------------ attention
 
-// One (split, head, batch row): keys [split*chunk, min(len, (split+1)*chunk)) of the ring.
+// One (split, head, batch row): keys [split*chunk, min(len, (split+1)*chunk)) of the ring
+// (model.rs:450-472; ring order does not matter to the softmax).  HD = 128.  A warp takes 4 keys at
+// a time, one per group of 8 lanes; a lane holds 16 dimensions of q, k, v and its group's
+// online-softmax state (max, sum of exp, sum of exp * v), and two key groups' loads are issued
+// before either is used.  The groups of a warp merge by shuffles, then the 4 warps in warp order.
 // Partial = (max score, sum exp, sum exp * v).  The CTA finishing last for a (row, head)
 // combines the partials in split order and writes attn[row][head].
+template <typename KT>
+__device__ __forceinline__ void load_row16(const KT* row, int sub, float (&x)[16]) {
+    constexpr int EPL = 16 / (int)sizeof(KT);  // elements of one 16-byte load
+    constexpr int CH = 16 / EPL;               // loads for 16 dimensions
+#pragma unroll
+    for (int ch = 0; ch < CH; ++ch) {
+        const uint4 r = *reinterpret_cast<const uint4*>(row + ch * 8 * EPL + sub * EPL);
+        if (sizeof(KT) == 4) {
+            x[ch * 4 + 0] = __uint_as_float(r.x);
+            x[ch * 4 + 1] = __uint_as_float(r.y);
+            x[ch * 4 + 2] = __uint_as_float(r.z);
+            x[ch * 4 + 3] = __uint_as_float(r.w);
+        } else {
+            const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                x[ch * 8 + 2 * e] = __uint_as_float(w[e] << 16);
+                x[ch * 8 + 2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
+            }
+        }
+    }
+}
+
 template <typename KT>
 __global__ void __launch_bounds__(128) attn_kernel(Ctx c, int layer) {
     pdl_trigger();
     pdl_wait();
+    constexpr int HD = 128;
+    constexpr int EPL = 16 / (int)sizeof(KT);
     const int s = blockIdx.x, h = blockIdx.y, i = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 3, sub = lane & 7;
     const int sid = c.ids[i];
     const StreamState st = c.state[sid];
     const int len = min(st.len + 1, c.ML);
     const int j0 = s * c.chunk, j1 = min(len, j0 + c.chunk);
-    const int HD = c.HD;  // 128: 4 dims per lane
-    const float4 q = reinterpret_cast<const float4*>(c.qkv + (int64_t)i * 3 * c.D + h * HD)[lane];
+    // lane dimension e (0..15) is dim(e) = (e / EPL) * 8 * EPL + sub * EPL + e % EPL
+    float q[16], o[16];
+    {
+        const float* qh = c.qkv + (int64_t)i * 3 * c.D + h * HD;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            q[e] = qh[(e / EPL) * 8 * EPL + sub * EPL + e % EPL];
+            o[e] = 0.0f;
+        }
+    }
     const KT* kbase = reinterpret_cast<const KT*>(c.kv) + (int64_t)sid * c.kv_stream_stride +
                       (int64_t)layer * c.kv_layer_stride + (int64_t)h * c.ML * HD;
     const KT* vbase = kbase + c.kv_half_stride;
     float m = -FLT_MAX, l = 0.0f;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    bool any = false;
-    for (int j = j0 + warp; j < j1; j += 4) {
-        float4 k, v;
-        if (sizeof(KT) == 4) {
-            k = reinterpret_cast<const float4*>(kbase + (int64_t)j * HD)[lane];
-            v = reinterpret_cast<const float4*>(vbase + (int64_t)j * HD)[lane];
-        } else {
-            const uint2 kr = reinterpret_cast<const uint2*>(kbase + (int64_t)j * HD)[lane];
-            const uint2 vr = reinterpret_cast<const uint2*>(vbase + (int64_t)j * HD)[lane];
-            k = make_float4(__uint_as_float(kr.x << 16), __uint_as_float(kr.x & 0xFFFF0000u),
-                            __uint_as_float(kr.y << 16), __uint_as_float(kr.y & 0xFFFF0000u));
-            v = make_float4(__uint_as_float(vr.x << 16), __uint_as_float(vr.x & 0xFFFF0000u),
-                            __uint_as_float(vr.y << 16), __uint_as_float(vr.y & 0xFFFF0000u));
+    // key groups of 16 per CTA step (4 per warp), two steps in flight
+    for (int jb = j0 + warp * 4; jb < j1; jb += 32) {
+        float k0[16], v0[16], k1[16], v1[16];
+        const int ja = jb + g, jc = jb + 16 + g;
+        const bool va = ja < j1, vc = jc < j1;
+        load_row16(kbase + (int64_t)(va ? ja : j0) * HD, sub, k0);
+        load_row16(vbase + (int64_t)(va ? ja : j0) * HD, sub, v0);
+        load_row16(kbase + (int64_t)(vc ? jc : j0) * HD, sub, k1);
+        load_row16(vbase + (int64_t)(vc ? jc : j0) * HD, sub, v1);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const float* kv = u == 0 ? k0 : k1;
+            const float* vv = u == 0 ? v0 : v1;
+            float dot = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) dot = __fmaf_rn(q[e], kv[e], dot);
+            dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 1);
+            dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 2);
+            dot += __shfl_xor_sync(0xFFFFFFFFu, dot, 4);
+            if (!(u == 0 ? va : vc)) continue;
+            const float score = __fmul_rn(dot, c.attn_scale);
+            const float mn = fmaxf(m, score);
+            const float corr = expf(m - mn);
+            const float p = expf(score - mn);
+            l = __fmaf_rn(l, corr, p);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = __fmaf_rn(o[e], corr, __fmul_rn(p, vv[e]));
+            m = mn;
         }
-        float dot = __fmul_rn(q.x, k.x);
-        dot = __fmaf_rn(q.y, k.y, dot);
-        dot = __fmaf_rn(q.z, k.z, dot);
-        dot = __fmaf_rn(q.w, k.w, dot);
-        dot = warp_sum(dot);
-        const float score = __fmul_rn(dot, c.attn_scale);
-        const float mn = fmaxf(m, score);
-        const float corr = any ? expf(m - mn) : 0.0f;
-        const float p = expf(score - mn);
-        l = __fmaf_rn(l, corr, p);
-        o.x = __fmaf_rn(o.x, corr, __fmul_rn(p, v.x));
-        o.y = __fmaf_rn(o.y, corr, __fmul_rn(p, v.y));
-        o.z = __fmaf_rn(o.z, corr, __fmul_rn(p, v.z));
-        o.w = __fmaf_rn(o.w, corr, __fmul_rn(p, v.w));
-        m = mn;
-        any = true;
     }
-    // combine the 4 warps in warp order
+    // the 4 key groups of the warp: groups g and g ^ 1, then g and g ^ 2
+#pragma unroll
+    for (int d = 8; d <= 16; d <<= 1) {
+        const float mo = __shfl_xor_sync(0xFFFFFFFFu, m, d), lo = __shfl_xor_sync(0xFFFFFFFFu, l, d);
+        const float mn = fmaxf(m, mo);
+        const float fa = l == 0.0f ? 0.0f : expf(m - mn), fb = lo == 0.0f ? 0.0f : expf(mo - mn);
+        // the lower group's terms first, so that both halves of a pair compute the same sums
+        const bool lower = (lane & d) == 0;
+        const float fl = lower ? fa : fb, fu = lower ? fb : fa;
+        const float ll = lower ? l : lo, lu = lower ? lo : l;
+        l = __fmaf_rn(lu, fu, __fmul_rn(ll, fl));
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const float oo = __shfl_xor_sync(0xFFFFFFFFu, o[e], d);
+            const float ol = lower ? o[e] : oo, ou = lower ? oo : o[e];
+            o[e] = __fmaf_rn(ou, fu, __fmul_rn(ol, fl));
+        }
+        m = mn;
+    }
+    // warp state -> shared memory in dimension order (group 0's lanes)
     __shared__ float sm_m[4], sm_l[4];
     __shared__ float4 sm_o[4][32];
-    if (lane == 0) {
-        sm_m[warp] = any ? m : -FLT_MAX;
-        sm_l[warp] = l;
+    {
+        float* od = reinterpret_cast<float*>(sm_o[warp]);
+        if (g == 0) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) od[(e / EPL) * 8 * EPL + sub * EPL + e % EPL] = o[e];
+        }
+        if (lane == 0) {
+            sm_m[warp] = l == 0.0f ? -FLT_MAX : m;
+            sm_l[warp] = l;
+        }
     }
-    sm_o[warp][lane] = o;
     __syncthreads();
+    // combine the 4 warps in warp order
     const int NS = c.nsplit;
     float* part = c.part + (((int64_t)i * c.H + h) * NS + s) * (HD + 4);
     if (warp == 0) {
