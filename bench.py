@@ -205,6 +205,77 @@ def run_reference(args):
     return 0
 
 
+def multi_stream(model, S, F, offsets, seed, torch, np, lib, check, stt_b200):
+    """Config 3 / 4 workload on this GPU: S streams, stream s pre-rolled alone to offsets[s] frames,
+    then F batched steps of all S streams (one frame each), device-timed.  Returns ms per step."""
+    cache = model.create_cache(S, "bf16")
+    ts = torch.cuda.current_stream()
+    for s_ in range(S):
+        if offsets[s_]:
+            a = torch.from_numpy(stt_b200.audio_tokens(seed, s_, offsets[s_]).astype(np.int32)).cuda()
+            tk = torch.empty(offsets[s_], dtype=torch.int32, device="cuda")
+            check(lib().stt_stream_feed_frames_device(cache._h, s_, offsets[s_], C.c_void_p(a.data_ptr()),
+                                                      C.c_void_p(tk.data_ptr()), C.c_void_p(ts.cuda_stream)), "pre-roll")
+    aud = np.stack([stt_b200.audio_tokens(seed, s_, F, first_frame=offsets[s_]) for s_ in range(S)], 1)
+    da = torch.from_numpy(aud.astype(np.int32)).cuda()
+    dt = torch.empty(F, S, dtype=torch.int32, device="cuda")
+    ids = (C.c_int32 * S)(*range(S))
+
+    def step(f):
+        check(lib().stt_streams_feed_frame_device(cache._h, ids, S, C.c_void_p(da[f].data_ptr()),
+                                                  C.c_void_p(dt[f].data_ptr()), C.c_void_p(ts.cuda_stream)), "step")
+    warm = min(3, F - 1)
+    for f in range(warm):
+        step(f)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ts)
+    for f in range(warm, F):
+        step(f)
+    e1.record(ts)
+    torch.cuda.synchronize()
+    cache.close()
+    return e0.elapsed_time(e1) / (F - warm), F - warm
+
+
+Q4_SHAPES = [(6144, 2048), (2048, 2048), (16896, 2048), (2048, 8448), (8001, 2048)]  # (N rows, K)
+
+
+def q4_sweep(torch, np, lib, stt_b200, device):
+    """Config 5: isolated Q4_0 products, weights N(0, 0.02) quantised, activations N(0, 1) bf16.
+    M = 1 and 4 run the GEMV (bf16 input); M >= 16 the tensor-core GEMM (the bf16 activations
+    converted to f16, exactly for these values).  Device-timed, 20 calls after 3 warm-up calls."""
+    out = []
+    rng = np.random.default_rng(5)
+    ts = torch.cuda.current_stream()
+    for n, k in Q4_SHAPES:
+        raw = stt_b200.quantize_q4_0((rng.standard_normal(n * k) * 0.02).astype(np.float32))
+        t = stt_b200.Q4Tensor.from_q4_bytes(raw, (n, k), device=device)
+        for m in (1, 4, 16, 64, 256):
+            x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+            dtype, xin = (1, x) if m < 16 else (2, x.to(torch.float16))
+            y = torch.empty(m, n, dtype=torch.float32, device="cuda")
+
+            def call():
+                rc = lib().stt_q4_matmul_device(t._h, xin.data_ptr(), dtype, m, y.data_ptr(), ts.cuda_stream)
+                assert rc == 0, lib().stt_last_error().decode()
+            for _ in range(3):
+                call()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(ts)
+            for _ in range(20):
+                call()
+            e1.record(ts)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / 20 * 1000.0
+            out.append({"n": n, "k": k, "m": m, "us": round(us, 2), "path": "gemv" if m < 16 else "tcgen05",
+                        "weight_gbs": round(n * k // 32 * 18 / us / 1e3, 1),
+                        "tflops": round(2.0 * n * k * m / us / 1e6, 2)})
+        t.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -214,6 +285,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--frames", type=int, default=FRAMES,
                     help="frames per utterance; only a shorter profiling case sets it (default 750)")
+    ap.add_argument("--no-multi", action="store_true", help="skip the 64- and 512-stream and matmul-sweep lines")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -346,6 +418,30 @@ def main():
         "diagnostics": diag,
         "tokens_checksum": int(np.int64(dev_tokens.astype(np.int64).sum())),
     }
+    if not args.no_multi:
+        # config 3: 64 streams per GPU at staggered offsets 0..374, 375 batched steps
+        offs = [round(i * 374 / 63) for i in range(64)]
+        ms64, k64 = multi_stream(model, 64, 375, offs, SEED + 1000 * rank, torch, np, lib, check, stt_b200)
+        barrier()
+        ms64 = max_over_ranks(ms64)
+        line["streams64"] = {"frames_per_s": world * 64 * 1000.0 / ms64, "ms_per_step": ms64, "timed_steps": k64,
+                             "real_time_streams_per_gpu_at_this_batch": 64 * 80.0 / ms64,
+                             "config": "64 streams per GPU, staggered offsets 0..374, 375 frames each, bf16 KV, "
+                                       "layer products on tcgen05 (M = 64)"}
+        # config 4: 512 streams split evenly over the GPUs, 250 frames each
+        per = 512 // world
+        ms512, k512 = multi_stream(model, per, 250, [0] * per, SEED + 2000 * rank, torch, np, lib, check, stt_b200)
+        barrier()
+        ms512 = max_over_ranks(ms512)
+        line["streams512"] = {"frames_per_s": world * per * 1000.0 / ms512, "ms_per_step": ms512,
+                              "timed_steps": k512, "config": f"{per} streams per GPU x {world} GPUs, 250 frames"}
+        if rank == 0:
+            sweep = q4_sweep(torch, np, lib, stt_b200, local)
+            m1 = [r for r in sweep if r["m"] == 1]
+            line["q4_matmul"] = {"gemv_m1_weight_gbs": {f"{r['n']}x{r['k']}": r["weight_gbs"] for r in m1},
+                                 "gemv_m1_frac_of_hbm": max(r["weight_gbs"] for r in m1) / pk["hbm_gbs"],
+                                 "sweep": sweep}
+        barrier()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         fps, n, cores = cpu_reference(20.0, 3, 1)
         line["cpu_baseline"] = {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",
