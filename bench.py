@@ -286,6 +286,8 @@ def main():
     ap.add_argument("--frames", type=int, default=FRAMES,
                     help="frames per utterance; only a shorter profiling case sets it (default 750)")
     ap.add_argument("--no-multi", action="store_true", help="skip the 64- and 512-stream and matmul-sweep lines")
+    ap.add_argument("--batched", type=int, default=0,
+                    help="profiling case: only S streams x --frames batched steps from position 0, one JSON line")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -324,6 +326,14 @@ def main():
     cfg = stt_b200.SttConfig(text_start_token=0)   # initial text token 0 (benchmark config)
     model = stt_b200.SttModel.from_buffer(g.address, g.length, device=local, config=cfg)
     g.close()
+    if args.batched:
+        ms_b, k_b = multi_stream(model, args.batched, nframes, [0] * args.batched, SEED, torch, np, lib, check,
+                                 stt_b200)
+        if rank == 0:
+            print(json.dumps({"batched_streams": args.batched, "frames": nframes, "timed_steps": k_b,
+                              "ms_per_step": ms_b, "frames_per_s": args.batched * 1000.0 / ms_b}))
+        model.close()
+        return 0
     cache = model.create_cache(1, "bf16")
     stream = stt_b200.SttStream(cfg, cache, 0)
     audio = stt_b200.audio_tokens(SEED, rank, nframes)
