@@ -296,10 +296,11 @@ __global__ void __launch_bounds__(256) tc_epilogue_kernel(Ctx c, GemvArgs a, con
                                                          int slices) {
     pdl_trigger();
     pdl_wait();
-    const int64_t total = (int64_t)rows * a.n_units;
+    // grid (unit groups of 256, batch rows): the row's stream id and state are the same in a CTA
     const int64_t plane = (int64_t)rows * a.W.n;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int m = (int)(i / a.n_units), u = (int)(i - (int64_t)m * a.n_units);
+    const int m = blockIdx.y;
+    const int u = blockIdx.x * blockDim.x + threadIdx.x;
+    if (u < a.n_units) {
         int ra, rb;
         unit_rows<EPI>(a, u, &ra, &rb);
         const float* p = part + (int64_t)m * a.W.n;
@@ -321,7 +322,8 @@ __global__ void __launch_bounds__(256) tc_epilogue_kernel(Ctx c, GemvArgs a, con
 // online-softmax state (max, sum of exp, sum of exp * v), and two key groups' loads are issued
 // before either is used.  The groups of a warp merge by shuffles, then the 4 warps in warp order.
 // Partial = (max score, sum exp, sum exp * v).  The CTA finishing last for a (row, head)
-// combines the partials in split order and writes attn[row][head].
+// combines the partials in split order and writes attn[row][head]; with a single split the CTA
+// writes it directly.
 template <typename KT>
 __device__ __forceinline__ void load_row16(const KT* row, int sub, float (&x)[16]) {
     constexpr int EPL = 16 / (int)sizeof(KT);  // elements of one 16-byte load
@@ -342,6 +344,19 @@ __device__ __forceinline__ void load_row16(const KT* row, int sub, float (&x)[16
                 x[ch * 8 + 2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
             }
         }
+    }
+}
+
+// Warp-collective: lane holds dims 4 lane .. +3 of head h of batch row i; writes attn and, on a
+// tensor-core step, the output projection's f16 input pieces (a piece of block h*4 + lane/8 takes
+// word w = lane % 8 (< 4) from this lane and w + 16 from lane + 4).
+__device__ __forceinline__ void write_head_output(const Ctx& c, int i, int h, int lane, float4 r) {
+    reinterpret_cast<float4*>(c.attn + (int64_t)i * c.D + h * 128)[lane] = r;
+    if (c.x16) {
+        const float4 b = make_float4(__shfl_down_sync(0xFFFFFFFFu, r.x, 4), __shfl_down_sync(0xFFFFFFFFu, r.y, 4),
+                                     __shfl_down_sync(0xFFFFFFFFu, r.z, 4), __shfl_down_sync(0xFFFFFFFFu, r.w, 4));
+        if ((lane & 7) < 4)
+            x16_store_piece(c.x16, c.x16_nt, c.x16_rows_pad, c.D, i, (h * 4 + (lane >> 3)) * 4 + (lane & 7), r, b, true);
     }
 }
 
@@ -439,6 +454,28 @@ __global__ void __launch_bounds__(128) attn_kernel(Ctx c, int layer) {
     // combine the 4 warps in warp order
     const int NS = c.nsplit;
     float* part = c.part + (((int64_t)i * c.H + h) * NS + s) * (HD + 4);
+    if (NS == 1) {
+        // one split: the warps' merge is the head's output
+        if (warp == 0) {
+            float M = -FLT_MAX;
+            for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w]);
+            float L = 0.0f;
+            float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int w = 0; w < 4; ++w) {
+                if (sm_l[w] == 0.0f) continue;
+                const float f = expf(sm_m[w] - M);
+                L = __fmaf_rn(sm_l[w], f, L);
+                const float4 ow = sm_o[w][lane];
+                O.x = __fmaf_rn(ow.x, f, O.x);
+                O.y = __fmaf_rn(ow.y, f, O.y);
+                O.z = __fmaf_rn(ow.z, f, O.z);
+                O.w = __fmaf_rn(ow.w, f, O.w);
+            }
+            write_head_output(c, i, h, lane,
+                              make_float4(__fdiv_rn(O.x, L), __fdiv_rn(O.y, L), __fdiv_rn(O.z, L), __fdiv_rn(O.w, L)));
+        }
+        return;
+    }
     if (warp == 0) {
         float M = -FLT_MAX;
         for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w]);
@@ -488,17 +525,8 @@ __global__ void __launch_bounds__(128) attn_kernel(Ctx c, int layer) {
             O.z = __fmaf_rn(ot.z, f, O.z);
             O.w = __fmaf_rn(ot.w, f, O.w);
         }
-        float4 r = make_float4(__fdiv_rn(O.x, L), __fdiv_rn(O.y, L), __fdiv_rn(O.z, L), __fdiv_rn(O.w, L));
-        reinterpret_cast<float4*>(c.attn + (int64_t)i * c.D + h * HD)[lane] = r;
-        if (c.x16) {
-            // lane holds elements 4 lane .. +3 of the head: a piece of block h*4 + lane/8 takes
-            // word w = lane % 8 (< 4) from this lane and w + 16 from lane + 4
-            const float4 b = make_float4(__shfl_down_sync(0xFFFFFFFFu, r.x, 4), __shfl_down_sync(0xFFFFFFFFu, r.y, 4),
-                                         __shfl_down_sync(0xFFFFFFFFu, r.z, 4), __shfl_down_sync(0xFFFFFFFFu, r.w, 4));
-            if ((lane & 7) < 4)
-                x16_store_piece(c.x16, c.x16_nt, c.x16_rows_pad, c.D, i, (h * 4 + (lane >> 3)) * 4 + (lane & 7), r, b,
-                                true);
-        }
+        write_head_output(c, i, h, lane,
+                          make_float4(__fdiv_rn(O.x, L), __fdiv_rn(O.y, L), __fdiv_rn(O.z, L), __fdiv_rn(O.w, L)));
         if (lane == 0) c.tickets[i * c.H + h] = 0u;
     }
 }
@@ -695,16 +723,15 @@ cudaError_t launch_finish(const Ctx& c, cudaStream_t st) {
 
 cudaError_t launch_tc_epilogue(const Ctx& c, const GemvArgs& a, int epi, int rows, const float* part, int slices,
                                cudaStream_t st) {
-    const int64_t total = (int64_t)rows * a.n_units;
-    const int grid = (int)std::min<int64_t>((total + 255) / 256, 8192);
-    if (grid <= 0) return cudaSuccess;
+    if (rows <= 0 || a.n_units <= 0) return cudaSuccess;
+    const dim3 grid((a.n_units + 255) / 256, rows);
     switch (epi) {
-        case EPI_QKV: return launch_pdl(tc_epilogue_kernel<EPI_QKV>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
-        case EPI_GATE: return launch_pdl(tc_epilogue_kernel<EPI_GATE>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
-        case EPI_RESID: return launch_pdl(tc_epilogue_kernel<EPI_RESID>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
+        case EPI_QKV: return launch_pdl(tc_epilogue_kernel<EPI_QKV>, grid, dim3(256), 0, st, c, a, part, rows, slices);
+        case EPI_GATE: return launch_pdl(tc_epilogue_kernel<EPI_GATE>, grid, dim3(256), 0, st, c, a, part, rows, slices);
+        case EPI_RESID: return launch_pdl(tc_epilogue_kernel<EPI_RESID>, grid, dim3(256), 0, st, c, a, part, rows, slices);
         case EPI_LOGITS:
-            return launch_pdl(tc_epilogue_kernel<EPI_LOGITS>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
-        default: return launch_pdl(tc_epilogue_kernel<EPI_PLAIN>, dim3(grid), dim3(256), 0, st, c, a, part, rows, slices);
+            return launch_pdl(tc_epilogue_kernel<EPI_LOGITS>, grid, dim3(256), 0, st, c, a, part, rows, slices);
+        default: return launch_pdl(tc_epilogue_kernel<EPI_PLAIN>, grid, dim3(256), 0, st, c, a, part, rows, slices);
     }
 }
 
