@@ -62,9 +62,6 @@ namespace {
 constexpr int kTM = 128;        // weight rows per CTA (MMA M, one TMEM lane each)
 constexpr int kKC = 64;         // K elements per chunk (two Q4_0 blocks)
 constexpr int kQuad = 256;      // K elements per raw stage (8 blocks: 128 nibble bytes, 16 scale bytes per row)
-constexpr int kRS = 4;          // raw stages (a power of two)
-constexpr int kAS = 4;          // A stages in tensor memory (a power of two)
-constexpr uint32_t kACol = 128;      // TMEM column of A stage 0 (the accumulator uses columns 0 .. NT-1)
 constexpr uint32_t kAStageCols = 64; // per A stage: hi part in 32 columns (64 f16 per lane), then lo
 constexpr uint32_t kTmemCols = 512;  // allocated TMEM columns (the whole SM's; one CTA per SM)
 constexpr int kDqWarps = 8;     // dequantising warps (2 .. 9, two groups of 4); warp 10 copies the activations
@@ -76,7 +73,20 @@ constexpr uint32_t kSpin = 1u << 22;
 constexpr uint32_t kNap = 64;  // ns between polls of a wait off the critical path
 constexpr float kWUnscale = 1.0f / 1024.0f;
 
-__host__ __device__ constexpr int b_stages(int) { return 4; }
+// Pipeline shape by batch tile.  Up to 128 batch rows: 4-stage rings, accumulator in TMEM columns
+// 0 .. 127, A stages from column 128, MMAs issued per chunk pair.  256 rows: a 32 KB B tile per
+// part, so 2 B stages and 3 raw stages fit in shared memory; accumulator in columns 0 .. 255, A
+// stages from 256; the 12 MMAs of one chunk already keep the tensor cores busy for about 1,700
+// cycles, so they go out per chunk.
+template <int NT>
+struct TcCfg {
+    static constexpr bool kWide = NT >= 256;
+    static constexpr int kRS = kWide ? 3 : 4;          // raw stages
+    static constexpr int kAS = 4;                      // A stages in tensor memory
+    static constexpr int NBS = kWide ? 2 : 4;          // B stages
+    static constexpr uint32_t kACol = kWide ? 256 : 128;
+    static constexpr int kStep = kWide ? 1 : 2;        // chunks per MMA round
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -219,11 +229,12 @@ __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&v)[8]) 
 
 template <int NT>
 struct TcSmem {
-    uint8_t rnib[kRS][kRNib];                             // raw nibbles [128 rows][128 B], 128-byte swizzle
-    uint8_t rsc[kRS][kRSc];                               // raw scales [128 rows][8]
-    uint8_t b[b_stages(NT)][2][NT * kKC * 2];             // [stage][hi, lo] activations, same layout
-    uint64_t r_full[kRS], r_empty[kRS], a_full[kAS], a_empty[kAS];
-    uint64_t b_full[b_stages(NT)], b_empty[b_stages(NT)], done;
+    using C = TcCfg<NT>;
+    uint8_t rnib[C::kRS][kRNib];                          // raw nibbles [128 rows][128 B], 128-byte swizzle
+    uint8_t rsc[C::kRS][kRSc];                            // raw scales [128 rows][8]
+    uint8_t b[C::NBS][2][NT * kKC * 2];                   // [stage][hi, lo] activations, same layout
+    uint64_t r_full[C::kRS], r_empty[C::kRS], a_full[C::kAS], a_empty[C::kAS];
+    uint64_t b_full[C::NBS], b_empty[C::NBS], done;
     uint32_t tmem;
     int abort;
 };
@@ -277,7 +288,9 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
                                                           int slices, float* __restrict__ part, int* __restrict__ err) {
     extern __shared__ uint8_t tc_raw[];
     TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(tc_raw + ((1024u - (smem_u32(tc_raw) & 1023u)) & 1023u));
-    constexpr int NBS = b_stages(NT);
+    using C = TcCfg<NT>;
+    constexpr int NBS = C::NBS, kRS = C::kRS, kAS = C::kAS, kStep = C::kStep;
+    constexpr uint32_t kACol = C::kACol;
     constexpr uint32_t kBBytes = NT * kKC * 2;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int n0 = blockIdx.x * kTM, mt = blockIdx.y, z = blockIdx.z;
@@ -355,19 +368,19 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         pdl_trigger();
         for (int c = std::max(0, bc - NBS); c < bc; ++c) mbar_drain(&sm.b_full[c % NBS], (c / NBS) & 1);
     } else if (warp == 1) {
-        // chunks in pairs: one round trip waits for both chunks' A and B stages (lanes 0-7, 8-15,
-        // 16-23 and 24-31 poll one barrier each), then 24 MMAs go out back to back, since the
-        // tensor cores idle whenever this warp does anything else
+        // chunks in pairs (kStep 2): one round trip waits for both chunks' A and B stages (lanes
+        // 0-7, 8-15, 16-23 and 24-31 poll one barrier each), then 24 MMAs go out back to back,
+        // since the tensor cores idle whenever this warp does anything else
         const uint32_t idesc = instr_desc_f16(kTM, NT);
-        for (int c = 0; c < nchunks; c += 2) {
-            const int cc = c + ((lane >> 3) & 1);  // lanes 8-15 and 24-31: the pair's second chunk
+        for (int c = 0; c < nchunks; c += kStep) {
+            const int cc = c + (kStep == 2 ? (lane >> 3) & 1 : 0);  // lanes 8-15 and 24-31: the pair's second chunk
             uint64_t* const bar = lane < 16 ? &sm.a_full[cc % kAS] : &sm.b_full[cc % NBS];
             const uint32_t par = lane < 16 ? (uint32_t)(cc / kAS) & 1u : (uint32_t)(cc / NBS) & 1u;
             if (!__all_sync(0xFFFFFFFFu, mbar_wait(bar, par, abort))) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             if (elect_one()) {
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < kStep; ++h) {
                     const int sa = (c + h) % kAS, sb = (c + h) % NBS;
                     const uint32_t ah = tmem + kACol + sa * kAStageCols, al = ah + 32;
                     const uint32_t bh = smem_u32(sm.b[sb][0]), bl = smem_u32(sm.b[sb][1]);
@@ -383,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
                     }
                 }
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < kStep; ++h) {
                     mma_commit(&sm.a_empty[(c + h) % kAS]);
                     mma_commit(&sm.b_empty[(c + h) % NBS]);
                 }
@@ -402,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
         const uint32_t rsw = (uint32_t)(row & 7);  // the swizzle's XOR for this row
         for (int c = grp; c < nchunks; c += 2) {
-            const int qi = c >> 2, cq = c & 3, s = qi & (kRS - 1), sa = c & (kAS - 1);
+            const int qi = c >> 2, cq = c & 3, s = qi % kRS, sa = c % kAS;
             // lanes 0-15 poll the raw quad (this group's first chunk of a quad), lanes 16-31 the
             // A stage, in one loop
             const bool need = lane < 16 ? cq == grp : c >= kAS;
@@ -467,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
-int pick_nt(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+int pick_nt(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
 
 // K slices: up to one CTA per SM.
 TcPlan make_plan(int n, int k, int M, int num_sms) {
@@ -497,7 +510,8 @@ cudaError_t launch_gemm(const TcWeight& tw, const __half* x16, int x_lo, int M, 
         case 16: return launch_nt<16>(tw, x16, x_lo, M, p, part, err, st);
         case 32: return launch_nt<32>(tw, x16, x_lo, M, p, part, err, st);
         case 64: return launch_nt<64>(tw, x16, x_lo, M, p, part, err, st);
-        default: return launch_nt<128>(tw, x16, x_lo, M, p, part, err, st);
+        case 128: return launch_nt<128>(tw, x16, x_lo, M, p, part, err, st);
+        default: return launch_nt<256>(tw, x16, x_lo, M, p, part, err, st);
     }
 }
 
