@@ -284,7 +284,7 @@ __device__ __forceinline__ bool wait_seg(Smem& sm, const MegaArgs& P, uint32_t i
 
 // Waits until the words of N 16-byte pieces (two words each, at addr(i)) all carry epoch ep.
 // All loads of a round are in flight together, so a wait costs one L2 round trip once the data
-// is there; between rounds the thread sleeps 32 .. 256 ns.  (Every address must be valid:
+// is there; between rounds the thread sleeps 32 .. 96 ns.  (Every address must be valid:
 // loads skipped under a condition make the compiler keep far more registers live.)
 template <int N, typename Addr>
 __device__ __forceinline__ bool ll_wait_n(const MegaArgs& P, Addr addr, uint32_t ep, uint64_t (&w)[N][2]) {
@@ -312,7 +312,7 @@ __device__ __forceinline__ bool ll_wait_n(const MegaArgs& P, Addr addr, uint32_t
             }
         }
         __nanosleep(nap);
-        nap = min(nap * 2u, 256u);
+        nap = min(nap * 2u, 96u);
     }
 }
 
