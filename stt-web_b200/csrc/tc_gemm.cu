@@ -480,6 +480,11 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
+// Launch shape of one product: batch rows per tile, batch tiles, weight-row tiles of 128, K slices.
+struct TcPlan {
+    int nt, mtiles, tiles, slices;
+};
+
 int pick_nt(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
 
 // K slices: up to one CTA per SM.
@@ -718,8 +723,6 @@ cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out) {
     out->k = w.k;
     return cudaSuccess;
 }
-
-TcPlan tc_gemm_plan(const Q4Dev& w, int M, int num_sms) { return make_plan(w.n, w.k, M, num_sms); }
 
 size_t tc_x16_bytes(int k, int M) {
     const TcPlan p = make_plan(1, k, M, 1);

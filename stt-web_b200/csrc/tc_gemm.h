@@ -24,12 +24,6 @@ struct TcWeight {
 };
 cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out);
 
-// Launch shape of one product: batch rows per tile, batch tiles, weight-row tiles of 128, K slices.
-struct TcPlan {
-    int nt, mtiles, tiles, slices;
-};
-TcPlan tc_gemm_plan(const Q4Dev& w, int M, int num_sms);
-
 // Scratch of one product of M batch rows: the tiled f16 input (hi and lo parts) and the K-slice
 // partial sums.
 size_t tc_x16_bytes(int k, int M);
