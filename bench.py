@@ -35,6 +35,9 @@ KV_BYTES_PER_TOKEN = 16 * 2 * 2048 * 2   # bf16 K+V of one cached position over 
 EMB_BYTES = 33 * 2048 * 2        # 33 bf16 embedding rows per frame
 
 
+MEGA_TRAFFIC_750 = 508_194_168_320 + 2_685_069_824  # dram__bytes_read.sum + dram__bytes_write.sum, one launch
+
+
 def algorithmic_bytes_per_utterance(frames=FRAMES, ring=751):
     kv_read = sum(min(p + 1, ring) for p in range(frames)) * KV_BYTES_PER_TOKEN
     kv_write = frames * KV_BYTES_PER_TOKEN
@@ -419,7 +422,10 @@ def main():
                    "parallelism": f"{world} independent streams, one per GPU"},
         "roofline": {"bound": "hbm", "kernel": "decode step (all kernels of one frame)", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                     "peak_kind": pk_kind, "algorithmic_bytes_per_step": algo, "traffic": None},
+                     "peak_kind": pk_kind, "algorithmic_bytes_per_step": algo,
+                     # DRAM read + write bytes of one 750-frame launch, from the ncu capture in
+                     # profiles/mega_kernel_dram_750frames.txt (not measured for other frame counts)
+                     "traffic": MEGA_TRAFFIC_750 if nframes == FRAMES else None},
         "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": nframes * 32 * 4,
                 "d2h_bytes_per_step": nframes * (4 + 32)},
         "clocks": clocks,
