@@ -44,6 +44,25 @@ def algorithmic_bytes_per_utterance(frames=FRAMES, ring=751):
     return frames * (WEIGHT_BYTES + EMB_BYTES) + kv_read + kv_write
 
 
+def algorithmic_bytes_batched(offsets, first, last, ring=751):
+    """Mean algorithmic bytes of the batched steps first .. last-1: the weights once per step, each
+    stream's K/V reads at its position (offset + step), its K/V write and its 33 embedding rows."""
+    total = 0
+    for f in range(first, last):
+        total += WEIGHT_BYTES + sum((min(o + f + 1, ring) + 1) * KV_BYTES_PER_TOKEN + EMB_BYTES for o in offsets)
+    return total / max(1, last - first)
+
+
+# Q4_0 weights of one step (16 layers + head), and the MMA work of a batched tensor-core step: three
+# f16 MMAs per product (w_hi.x_hi + w_hi.x_lo + w_lo.x_hi) over the batch rows padded to the tile.
+Q4_PARAMS = 16 * (6144 * 2048 + 2048 * 2048 + 16896 * 2048 + 2048 * 8448) + 8000 * 2048
+
+
+def mma_flops_batched(S):
+    nt = 16 if S <= 16 else 32 if S <= 32 else 64 if S <= 64 else 128 if S <= 128 else 256
+    return 3 * 2 * ((S + nt - 1) // nt * nt) * Q4_PARAMS
+
+
 def peaks():
     try:
         return json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))), "measured"
@@ -210,7 +229,8 @@ def run_reference(args):
 
 def multi_stream(model, S, F, offsets, seed, torch, np, lib, check, stt_b200):
     """Config 3 / 4 workload on this GPU: S streams, stream s pre-rolled alone to offsets[s] frames,
-    then F batched steps of all S streams (one frame each), device-timed.  Returns ms per step."""
+    then F batched steps of all S streams (one frame each), device-timed.  Returns ms per step and
+    the number of timed steps (the last F - warm of the F)."""
     cache = model.create_cache(S, "bf16")
     ts = torch.cuda.current_stream()
     for s_ in range(S):
@@ -440,8 +460,16 @@ def main():
         ms64, k64 = multi_stream(model, 64, 375, offs, SEED + 1000 * rank, torch, np, lib, check, stt_b200)
         barrier()
         ms64 = max_over_ranks(ms64)
+        b64 = algorithmic_bytes_batched(offs, 375 - k64, 375)
         line["streams64"] = {"frames_per_s": world * 64 * 1000.0 / ms64, "ms_per_step": ms64, "timed_steps": k64,
                              "real_time_streams_per_gpu_at_this_batch": 64 * 80.0 / ms64,
+                             "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": b64,
+                                          "achieved": b64 / (ms64 / 1000.0) / 1e9, "peak": pk["hbm_gbs"],
+                                          "unit": "GB/s", "frac": b64 / (ms64 / 1000.0) / 1e9 / pk["hbm_gbs"]},
+                             "tensor": {"mma_flops_per_step": mma_flops_batched(64),
+                                        "achieved_tflops_over_step": mma_flops_batched(64) / (ms64 / 1000.0) / 1e12,
+                                        "peak": pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")),
+                                        "peak_kind": "sustained bf16 (a seconds-long loop)", "unit": "TFLOP/s"},
                              "config": "64 streams per GPU, staggered offsets 0..374, 375 frames each, bf16 KV, "
                                        "layer products on tcgen05 (M = 64)"}
         # config 4: 512 streams split evenly over the GPUs, 250 frames each
@@ -449,8 +477,16 @@ def main():
         ms512, k512 = multi_stream(model, per, 250, [0] * per, SEED + 2000 * rank, torch, np, lib, check, stt_b200)
         barrier()
         ms512 = max_over_ranks(ms512)
+        b512 = algorithmic_bytes_batched([0] * per, 250 - k512, 250)
         line["streams512"] = {"frames_per_s": world * per * 1000.0 / ms512, "ms_per_step": ms512,
-                              "timed_steps": k512, "config": f"{per} streams per GPU x {world} GPUs, 250 frames"}
+                              "timed_steps": k512, "config": f"{per} streams per GPU x {world} GPUs, 250 frames",
+                              "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": b512,
+                                           "achieved": b512 / (ms512 / 1000.0) / 1e9, "peak": pk["hbm_gbs"],
+                                           "unit": "GB/s", "frac": b512 / (ms512 / 1000.0) / 1e9 / pk["hbm_gbs"]},
+                              "tensor": {"mma_flops_per_step": mma_flops_batched(per),
+                                         "achieved_tflops_over_step": mma_flops_batched(per) / (ms512 / 1000.0) / 1e12,
+                                         "peak": pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")),
+                                         "peak_kind": "sustained bf16 (a seconds-long loop)", "unit": "TFLOP/s"}}
         if rank == 0:
             sweep = q4_sweep(torch, np, lib, stt_b200, local)
             m1 = [r for r in sweep if r["m"] == 1]
