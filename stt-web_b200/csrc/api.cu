@@ -764,21 +764,18 @@ int run_host(stt_streams* s, const int32_t* ids, int n, int steps, const uint32_
     TRY(run_steps(s, ids, n, steps, static_cast<uint32_t*>(s->in_audio.p),
                   text ? static_cast<uint32_t*>(s->in_text.p) : nullptr, static_cast<int32_t*>(s->out_tokens.p),
                   logits_out ? static_cast<float*>(s->out_logits.p) : nullptr, mode, s->stream));
-    // read-backs on the same stream into pinned memory, then one synchronisation: the tokens, the
-    // step descriptor (its error word) and every stream's state
+    // read-backs on the same stream into pinned memory, then one synchronisation: the tokens and the
+    // step descriptor (its error word).  The host keeps the offsets itself (run_steps); the rest of
+    // the stream state is read lazily (refresh_state) by the calls that need it.
     CUDA_TRY(cudaMemcpyAsync(hb.p, s->out_tokens.p, (size_t)steps * n * 4, cudaMemcpyDeviceToHost, s->stream));
-    TRY(s->h_stage.ensure(sizeof(StepDesc) + sizeof(StreamState) * s->S));
+    TRY(s->h_stage.ensure(sizeof(StepDesc)));
     StepDesc* desc_stage = static_cast<StepDesc*>(s->h_stage.p);
-    StreamState* state_stage = reinterpret_cast<StreamState*>(desc_stage + 1);
     CUDA_TRY(cudaMemcpyAsync(desc_stage, s->d_desc, sizeof(StepDesc), cudaMemcpyDeviceToHost, s->stream));
-    CUDA_TRY(cudaMemcpyAsync(state_stage, s->d_state, sizeof(StreamState) * s->S, cudaMemcpyDeviceToHost, s->stream));
     if (logits_out)
         CUDA_TRY(cudaMemcpyAsync(logits_out, s->out_logits.p, (size_t)steps * n * m->V * 4, cudaMemcpyDeviceToHost,
                                  s->stream));
     CUDA_TRY(cudaStreamSynchronize(s->stream));
     if (tokens_out) std::memcpy(tokens_out, hb.p, (size_t)steps * n * 4);
-    std::memcpy(s->h_state.data(), state_stage, sizeof(StreamState) * s->S);
-    s->state_stale = false;
     const StepDesc desc_back = *desc_stage;
     if (desc_back.error != 0)
         return set_error(desc_back.error == STT_E_INVALID_ARG ? STT_E_INVALID_ARG : STT_E_DEVICE_FLAG,
