@@ -510,7 +510,6 @@ struct stt_streams {
     uint32_t* d_tickets = nullptr;
     __half* d_x16 = nullptr;    // f16 GEMM inputs of a batched step on the tensor cores
     float* d_tc_part = nullptr; // their K-slice partial sums
-    int* d_tc_err = nullptr;    // timeout word of the tensor-core kernels
     int32_t* d_ids = nullptr;
     StepDesc* d_desc = nullptr;
     DevBuf in_audio, in_text, out_tokens, out_logits, mega_xa;
@@ -584,24 +583,25 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
         ca.x16 = s->d_x16;
         tc_batch_tiles(n, &ca.x16_nt, &ca.x16_rows_pad);
         float* part = s->d_tc_part;
+        int* err = &s->d_desc->error;  // a GEMM timeout raises STT_E_DEVICE_FLAG like any step kernel
         int slices = 0;
         CUDA_TRY(launch_tc_prep(s->d_x, m->h_layers[0].norm1, m->D, n, s->d_x16, st));
         for (int l = 0; l < m->L; ++l) {
             const LayerDev& L = m->h_layers[l];
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 0], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 0], s->d_x16, n, part, err, m->num_sms, &slices, st));
             GemvArgs a{};
             a.W = L.qkv; a.out = s->d_qkv; a.ldo = 3 * m->D; a.layer = l; a.n_units = 3 * m->D / 2;
             CUDA_TRY(launch_tc_epilogue(c, a, EPI_QKV, n, part, slices, st));
             CUDA_TRY(launch_attention(ca, l, st));
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 1], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 1], s->d_x16, n, part, err, m->num_sms, &slices, st));
             CUDA_TRY(launch_tc_resid_norm(s->d_x, part, slices, n, m->D, L.norm2, s->d_x16, st));
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 2], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 2], s->d_x16, n, part, err, m->num_sms, &slices, st));
             CUDA_TRY(launch_tc_gate(part, slices, n, m->F, s->d_x16, st));
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 3], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 3], s->d_x16, n, part, err, m->num_sms, &slices, st));
             const float* next_norm = l + 1 < m->L ? m->h_layers[l + 1].norm1 : m->out_norm;
             CUDA_TRY(launch_tc_resid_norm(s->d_x, part, slices, n, m->D, next_norm, s->d_x16, st));
         }
-        CUDA_TRY(launch_tc_product(m->tc_w[4 * m->L], s->d_x16, n, part, s->d_tc_err, m->num_sms, &slices, st));
+        CUDA_TRY(launch_tc_product(m->tc_w[4 * m->L], s->d_x16, n, part, err, m->num_sms, &slices, st));
         GemvArgs a{};
         a.W = m->head; a.out = s->d_logits; a.ldo = m->V; a.n_units = (m->V + 1) / 2;
         CUDA_TRY(launch_tc_epilogue(c, a, EPI_LOGITS, n, part, slices, st));
@@ -825,7 +825,6 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
         }
     const size_t o_x16 = take(x16_bytes);
     const size_t o_tc_part = take(tc_part_bytes_max);
-    const size_t o_tc_err = take(sizeof(int));
     const size_t o_trace_ctas = take((size_t)m->num_sms * kTraceSlots * sizeof(unsigned long long));
     if (cudaMalloc(&s->d_scratch, off) != cudaSuccess) {
         cudaGetLastError();
@@ -853,7 +852,6 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     s->mega.trace_cap = kTraceCap;
     s->d_x16 = reinterpret_cast<__half*>(b + o_x16);
     s->d_tc_part = reinterpret_cast<float*>(b + o_tc_part);
-    s->d_tc_err = reinterpret_cast<int*>(b + o_tc_err);
     s->mega.trace_ctas = reinterpret_cast<unsigned long long*>(b + o_trace_ctas);
     s->mega.trace_slots = kTraceSlots;
     CUDA_TRY(cudaMemset(s->d_scratch, 0, off));

@@ -324,6 +324,46 @@ __global__ void __launch_bounds__(256) tc_epilogue_kernel(Ctx c, GemvArgs a, con
 // Partial = (max score, sum exp, sum exp * v).  The CTA finishing last for a (row, head)
 // combines the partials in split order and writes attn[row][head]; with a single split the CTA
 // writes it directly.
+// K/V staging of the batched attention: chunks of kAttnChunk keys, two stages of K and V.
+constexpr int kAttnChunk = 64;
+template <typename KT>
+constexpr size_t attn_smem_bytes() { return (size_t)2 * 2 * kAttnChunk * 128 * sizeof(KT); }
+
+// mbarrier and bulk-copy helpers of the attention kernel's K/V staging
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void attn_mbar_init(uint64_t* m) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(m)) : "memory");
+}
+__device__ __forceinline__ bool attn_mbar_wait(uint64_t* m, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 22); ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_addr(m)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+// Bulk copies of `bytes` (a multiple of 16) of K and of V into this CTA's shared memory, both
+// completing on the mbarrier (no multicast).
+__device__ __forceinline__ void attn_stage_kv(void* kd, const void* ks, void* vd, const void* vs, uint32_t bytes,
+                                              uint64_t* m) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(m)), "r"(2 * bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(kd)),
+                 "l"(ks), "r"(bytes), "r"(smem_addr(m))
+                 : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(vd)),
+                 "l"(vs), "r"(bytes), "r"(smem_addr(m))
+                 : "memory");
+}
+
 template <typename KT>
 __device__ __forceinline__ void load_row16(const KT* row, int sub, float (&x)[16]) {
     constexpr int EPL = 16 / (int)sizeof(KT);  // elements of one 16-byte load
@@ -386,16 +426,44 @@ __global__ void __launch_bounds__(128) attn_kernel(Ctx c, int layer) {
     const KT* kbase = reinterpret_cast<const KT*>(c.kv) + (int64_t)sid * c.kv_stream_stride +
                       (int64_t)layer * c.kv_layer_stride + (int64_t)h * c.ML * HD;
     const KT* vbase = kbase + c.kv_half_stride;
+    // K/V of the split stream through shared memory in chunks of kAttnChunk keys, two in flight
+    extern __shared__ __align__(128) uint8_t attn_stage[];  // [2 stages][K, V][kAttnChunk][HD] KT
+    __shared__ uint64_t full[2];
+    KT* const stage = reinterpret_cast<KT*>(attn_stage);
+    constexpr int kStageElems = kAttnChunk * HD;
+    const int nkeys = max(0, j1 - j0), nchunks = (nkeys + kAttnChunk - 1) / kAttnChunk;
+    int issued = 0;  // chunks whose copies thread 0 has issued
+    if (threadIdx.x == 0) {
+        attn_mbar_init(&full[0]);
+        attn_mbar_init(&full[1]);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int ci = 0; ci < 2 && ci < nchunks; ++ci) {
+            const int ka = j0 + ci * kAttnChunk, kn = min(kAttnChunk, j1 - ka);
+            attn_stage_kv(stage + (2 * ci) * kStageElems, kbase + (int64_t)ka * HD, stage + (2 * ci + 1) * kStageElems,
+                          vbase + (int64_t)ka * HD, (uint32_t)(kn * HD * sizeof(KT)), &full[ci]);
+            issued = ci + 1;
+        }
+    }
+    __syncthreads();
     float m = -FLT_MAX, l = 0.0f;
-    // key groups of 16 per CTA step (4 per warp), two steps in flight
-    for (int jb = j0 + warp * 4; jb < j1; jb += 32) {
+    bool staged_ok = true;
+    for (int ci = 0; ci < nchunks; ++ci) {
+        const int cs = ci & 1, kn = min(kAttnChunk, nkeys - ci * kAttnChunk);
+        if (!__syncthreads_and(attn_mbar_wait(&full[cs], (uint32_t)(ci >> 1) & 1u))) {
+            staged_ok = false;
+            break;
+        }
+        const KT* ks = stage + (2 * cs) * kStageElems;
+        const KT* vs = stage + (2 * cs + 1) * kStageElems;
+        // key groups of 16 per CTA step (4 per warp), two steps per iteration
+        for (int jb = warp * 4; jb < kn; jb += 32) {
         float k0[16], v0[16], k1[16], v1[16];
         const int ja = jb + g, jc = jb + 16 + g;
-        const bool va = ja < j1, vc = jc < j1;
-        load_row16(kbase + (int64_t)(va ? ja : j0) * HD, sub, k0);
-        load_row16(vbase + (int64_t)(va ? ja : j0) * HD, sub, v0);
-        load_row16(kbase + (int64_t)(vc ? jc : j0) * HD, sub, k1);
-        load_row16(vbase + (int64_t)(vc ? jc : j0) * HD, sub, v1);
+        const bool va = ja < kn, vc = jc < kn;
+        load_row16(ks + (va ? ja : 0) * HD, sub, k0);
+        load_row16(vs + (va ? ja : 0) * HD, sub, v0);
+        load_row16(ks + (vc ? jc : 0) * HD, sub, k1);
+        load_row16(vs + (vc ? jc : 0) * HD, sub, v1);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const float* kv = u == 0 ? k0 : k1;
@@ -416,6 +484,23 @@ __global__ void __launch_bounds__(128) attn_kernel(Ctx c, int layer) {
             for (int e = 0; e < 16; ++e) o[e] = __fmaf_rn(o[e], corr, __fmul_rn(p, vv[e]));
             m = mn;
         }
+        }
+        __syncthreads();  // every warp is done with stage cs
+        if (threadIdx.x == 0 && ci + 2 < nchunks) {
+            const int ka = j0 + (ci + 2) * kAttnChunk, kn2 = min(kAttnChunk, j1 - ka);
+            attn_stage_kv(stage + (2 * cs) * kStageElems, kbase + (int64_t)ka * HD, stage + (2 * cs + 1) * kStageElems,
+                          vbase + (int64_t)ka * HD, (uint32_t)(kn2 * HD * sizeof(KT)), &full[cs]);
+            issued = ci + 3;
+        }
+    }
+    if (!staged_ok) {
+        // a copy did not land in time: record it, let the copies in flight land, produce nothing
+        if (threadIdx.x == 0) {
+            raise_error(c.desc, -5);
+            for (int ci = max(0, issued - 2); ci < issued; ++ci) attn_mbar_wait(&full[ci & 1], (uint32_t)(ci >> 1) & 1u);
+        }
+        __syncthreads();
+        return;
     }
     // the 4 key groups of the warp: groups g and g ^ 1, then g and g ^ 2
 #pragma unroll
@@ -712,8 +797,17 @@ cudaError_t launch_embed(const Ctx& c, cudaStream_t st) {
 
 cudaError_t launch_attention(const Ctx& c, int layer, cudaStream_t st) {
     dim3 grid(c.nsplit, c.H, c.n);
-    if (c.kv_f32) return launch_pdl(attn_kernel<float>, grid, dim3(128), 0, st, c, layer);
-    return launch_pdl(attn_kernel<__nv_bfloat16>, grid, dim3(128), 0, st, c, layer);
+    if (c.kv_f32) {
+        const size_t smem = attn_smem_bytes<float>();
+        cudaError_t e = cudaFuncSetAttribute(attn_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(attn_kernel<float>, grid, dim3(128), smem, st, c, layer);
+    }
+    const size_t smem = attn_smem_bytes<__nv_bfloat16>();
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(attn_kernel<__nv_bfloat16>, grid, dim3(128), smem, st, c, layer);
 }
 
 cudaError_t launch_finish(const Ctx& c, cudaStream_t st) {

@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (t == 0 && *abort) atomicExch(err, 1);
+    if (t == 0 && *abort) atomicCAS(err, 0, -5);  // STT_E_DEVICE_FLAG, unless an earlier error is recorded
     __syncwarp();
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");

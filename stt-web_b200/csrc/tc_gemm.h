@@ -31,7 +31,7 @@ size_t tc_part_bytes(const Q4Dev& w, int M, int num_sms);
 
 // out[m][n] (row stride ldo floats) = x[m][:] . dequant(w)[n][:] for m < M, x f16 [M][w.k] taken
 // as exact; x16 and part are scratch of tc_x16_bytes / tc_part_bytes.  On a timeout a CTA sets
-// *err to 1 (device int, expected 0) and leaves its partial sums unwritten.
+// *err to -5 (STT_E_DEVICE_FLAG) if it was 0 and leaves its partial sums unwritten.
 cudaError_t launch_q4_tc_gemm(const TcWeight& tw, const Q4Dev& w, const __half* x, int M, float* out, int64_t ldo,
                               __half* x16, float* part, int* err, int num_sms, cudaStream_t st);
 
@@ -46,7 +46,7 @@ void tc_batch_tiles(int rows, int* nt, int* rows_pad);
 // x16 = rows of `in` [rows][K], RMSNorm'd with alpha when set.
 cudaError_t launch_tc_prep(const float* in, const float* alpha, int K, int rows, __half* x16, cudaStream_t st);
 // The GEMM: K-slice partial sums part[slices][rows][tw.n] of the weight times the x16 rows; the
-// slice count is returned in *slices.
+// slice count is returned in *slices.  A timeout records -5 in *err (a step descriptor's error word).
 cudaError_t launch_tc_product(const TcWeight& tw, const __half* x16, int rows, float* part, int* err, int num_sms,
                               int* slices, cudaStream_t st);
 // x[rows][D] += the slices (in order); x16 = RMSNorm(x) * alpha.
