@@ -251,12 +251,13 @@ def test_persistent_kernel_barrier_and_trace(full_model):
 TC_TIE = 5e-2  # near-ties below this margin may flip under f16 operand rounding
 
 
-@pytest.mark.parametrize("kv,n", [("bf16", 20), ("f32", 20), ("bf16", 40), ("bf16", 100), ("bf16", 150)])
+@pytest.mark.parametrize("kv,n", [("bf16", 20), ("f32", 20), ("bf16", 40), ("bf16", 100), ("bf16", 150),
+                                  ("bf16", 260), ("f32", 260)])
 def test_batched_tensor_core_path_matches_oracle(tiny_ref_gguf, kv, n):
     """Batches of 16+ streams run their layer products on the tensor cores (f16 operand parts,
     K-slice partial sums added in order; 20, 40, 100 and 150 streams take batch tiles of 32, 64,
-    128 and 256 rows): logits within the 2e-2 bound of the oracle, tokens equal away from
-    near-ties."""
+    128 and 256 rows, 260 streams two 256-row tiles and the attention's 32-key K/V chunks): logits
+    within the 2e-2 bound of the oracle, tokens equal away from near-ties."""
     cfg = tiny_cfg(sliding_window=12)
     model = stt_b200.SttModel.from_shards([tiny_ref_gguf], config=cfg)
     assert model.info.tensor_core_min_batch == 16
