@@ -81,11 +81,12 @@ constexpr float kWUnscale = 1.0f / 1024.0f;
 template <int NT>
 struct TcCfg {
     static constexpr bool kWide = NT >= 256;
+    static constexpr bool kNarrow = NT <= 64;          // accumulator in columns 0 .. 63: room for 6 A stages
     static constexpr int kRS = kWide ? 3 : 4;          // raw stages
-    static constexpr int kAS = 4;                      // A stages in tensor memory
-    static constexpr int NBS = kWide ? 2 : 4;          // B stages
-    static constexpr uint32_t kACol = kWide ? 256 : 128;
-    static constexpr int kStep = kWide ? 1 : 2;        // chunks per MMA round
+    static constexpr int kAS = kNarrow ? 6 : 4;        // A stages in tensor memory
+    static constexpr int NBS = kWide ? 2 : kNarrow ? 6 : 4;  // B stages
+    static constexpr uint32_t kACol = kWide ? 256 : kNarrow ? 64 : 128;
+    static constexpr int kStep = kWide ? 1 : kNarrow ? 3 : 2;  // chunks per MMA round
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -368,19 +369,23 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         pdl_trigger();
         for (int c = std::max(0, bc - NBS); c < bc; ++c) mbar_drain(&sm.b_full[c % NBS], (c / NBS) & 1);
     } else if (warp == 1) {
-        // chunks in pairs (kStep 2): one round trip waits for both chunks' A and B stages (lanes
-        // 0-7, 8-15, 16-23 and 24-31 poll one barrier each), then 24 MMAs go out back to back,
-        // since the tensor cores idle whenever this warp does anything else
+        // kStep chunks per round: one round trip waits for all of their A and B stages (lane
+        // L polls the A (L even) or B (L odd) stage of chunk c + (L / 2) % kStep), then the
+        // round's MMAs go out back to back, since the tensor cores idle whenever this warp does
+        // anything else
         const uint32_t idesc = instr_desc_f16(kTM, NT);
         for (int c = 0; c < nchunks; c += kStep) {
-            const int cc = c + (kStep == 2 ? (lane >> 3) & 1 : 0);  // lanes 8-15 and 24-31: the pair's second chunk
-            uint64_t* const bar = lane < 16 ? &sm.a_full[cc % kAS] : &sm.b_full[cc % NBS];
-            const uint32_t par = lane < 16 ? (uint32_t)(cc / kAS) & 1u : (uint32_t)(cc / NBS) & 1u;
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(bar, par, abort))) break;
+            const int nh = min(kStep, nchunks - c);  // chunks of this round
+            const int cc = c + (lane >> 1) % kStep;
+            const bool need = cc < nchunks;
+            uint64_t* const bar = (lane & 1) == 0 ? &sm.a_full[cc % kAS] : &sm.b_full[cc % NBS];
+            const uint32_t par = (lane & 1) == 0 ? (uint32_t)(cc / kAS) & 1u : (uint32_t)(cc / NBS) & 1u;
+            if (!__all_sync(0xFFFFFFFFu, !need || mbar_wait(bar, par, abort))) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             if (elect_one()) {
 #pragma unroll
                 for (int h = 0; h < kStep; ++h) {
+                    if (h >= nh) break;
                     const int sa = (c + h) % kAS, sb = (c + h) % NBS;
                     const uint32_t ah = tmem + kACol + sa * kAStageCols, al = ah + 32;
                     const uint32_t bh = smem_u32(sm.b[sb][0]), bl = smem_u32(sm.b[sb][1]);
@@ -397,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
                 }
 #pragma unroll
                 for (int h = 0; h < kStep; ++h) {
+                    if (h >= nh) break;
                     mma_commit(&sm.a_empty[(c + h) % kAS]);
                     mma_commit(&sm.b_empty[(c + h) % NBS]);
                 }
