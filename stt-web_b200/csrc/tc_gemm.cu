@@ -13,7 +13,7 @@
 // subnormals, so hi + lo = q * s' exactly.  The accumulator is scaled back by 2^-10 (exact).
 // Weights with |s| > 4 would overflow f16 and are not sent here (tc_gemm_scales_ok).
 //
-// K order.  A 16-byte word of four Q4_0 payload bytes yields, with one mask per nibble position,
+// K order.  A 32-bit word (four Q4_0 payload bytes) yields, with one mask per nibble position,
 // the element pairs (4i, 4i+2), (4i+1, 4i+3), (16+4i, 16+4i+2), (16+4i+1, 16+4i+3) of its block;
 // those four pairs form one 8-element row piece of the MMA operand.  The MMA sums over K, so the
 // activations are stored in the same order (prep_f16_kernel) instead of shuffling the weights.
@@ -34,9 +34,9 @@
 //     weight row and chunk (two Q4_0 blocks), writing the hi and lo parts straight into a ring of
 //     A stages in tensor memory (tcgen05.st; weight row = TMEM lane), then signalling the stage
 //     with one arrive per warp;
-//   - warp 1 issues from one elected lane, per pair of chunks, 2 x 4 x 3 MMAs of 128 x NT x 16
-//     with A read from tensor memory and B from shared memory into the TMEM accumulator, and
-//     commits them to the barriers that free the A and B stages they read;
+//   - warp 1 issues from one elected lane, per round of 1 to 3 chunks (TcCfg), 4 x 3 MMAs of
+//     128 x NT x 16 per chunk with A read from tensor memory and B from shared memory into the TMEM
+//     accumulator, and commits them to the barriers that free the A and B stages they read;
 //   - after the last commit, warps 2..9 read the accumulator (tcgen05.ld 32x32b; each warp its
 //     32 TMEM lanes and half of the batch columns) and store the partial sums.
 // The copy and MMA roles run as whole warps and issue from one elected lane (elect.sync).
@@ -73,11 +73,12 @@ constexpr uint32_t kSpin = 1u << 22;
 constexpr uint32_t kNap = 64;  // ns between polls of a wait off the critical path
 constexpr float kWUnscale = 1.0f / 1024.0f;
 
-// Pipeline shape by batch tile.  Up to 128 batch rows: 4-stage rings, accumulator in TMEM columns
-// 0 .. 127, A stages from column 128, MMAs issued per chunk pair.  256 rows: a 32 KB B tile per
-// part, so 2 B stages and 3 raw stages fit in shared memory; accumulator in columns 0 .. 255, A
-// stages from 256; the 12 MMAs of one chunk already keep the tensor cores busy for about 1,700
-// cycles, so they go out per chunk.
+// Pipeline shape by batch tile.  Up to 64 batch rows: the accumulator takes TMEM columns 0 .. 63,
+// leaving room for 6 A stages from column 64; 6 B stages; MMAs issued per round of 3 chunks.
+// 128 rows: 4-stage rings, accumulator in columns 0 .. 127, A stages from column 128, rounds of
+// 2 chunks.  256 rows: a 32 KB B tile per part, so 2 B stages and 3 raw stages fit in shared
+// memory; accumulator in columns 0 .. 255, A stages from 256; the 12 MMAs of one chunk already
+// keep the tensor cores busy for about 1,700 cycles, so they go out per chunk.
 template <int NT>
 struct TcCfg {
     static constexpr bool kWide = NT >= 256;
