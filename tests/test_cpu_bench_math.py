@@ -1,0 +1,54 @@
+"""The roofline arithmetic of bench.py: byte and FLOP counts against the model's shapes."""
+import importlib.util
+import os
+
+import pytest
+
+REPO = os.path.join(os.path.dirname(os.path.abspath(__file__)), "..")
+
+
+@pytest.fixture(scope="module")
+def bench():
+    spec = importlib.util.spec_from_file_location("bench_under_test", os.path.join(REPO, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def q4_bytes(n, k):
+    return n * k // 32 * 18
+
+
+def test_weight_bytes_and_params(bench):
+    # 16 x (in_proj 6144x2048, out_proj 2048x2048, linear_in 16896x2048, linear_out 2048x8448) + head 8000x2048
+    layer = [(6144, 2048), (2048, 2048), (16896, 2048), (2048, 8448)]
+    params = 16 * sum(n * k for n, k in layer) + 8000 * 2048
+    assert bench.Q4_PARAMS == params == 1_115_291_648
+    assert bench.WEIGHT_BYTES == 16 * sum(q4_bytes(n, k) for n, k in layer) + q4_bytes(8000, 2048)
+    assert bench.KV_BYTES_PER_TOKEN == 131_072
+
+
+def test_bytes_per_utterance(bench):
+    # 750 frames from position 0: weights and embeddings every frame, K/V of positions 0..t read at t
+    total = bench.algorithmic_bytes_per_utterance(750)
+    assert total == 750 * (bench.WEIGHT_BYTES + bench.EMB_BYTES) + (sum(range(1, 751)) + 750) * 131_072
+    assert abs(total / 750 / 1e6 - 676.8) < 0.1  # MB per frame
+
+
+def test_bytes_per_batched_step(bench):
+    # configuration 3: stream s pre-rolled to round(374 s / 63); 375 steps, 3 of them warm-up
+    offs = [round(s * 374 / 63) for s in range(64)]
+    per_step = bench.algorithmic_bytes_batched(offs, 3, 375)
+    assert 3.7e9 < per_step < 3.9e9
+    # one step of one stream at position p reads p + 1 slots and writes one
+    one = bench.algorithmic_bytes_batched([10], 0, 1)
+    assert one == bench.WEIGHT_BYTES + (11 + 1) * 131_072 + bench.EMB_BYTES
+    # the ring caps the slots read at 751
+    assert bench.algorithmic_bytes_batched([2000], 0, 1) == bench.WEIGHT_BYTES + (751 + 1) * 131_072 + bench.EMB_BYTES
+
+
+def test_mma_flops(bench):
+    # three MMAs per product over the batch rows padded to the tile (64 -> 64, 100 -> 128, 300 -> 512)
+    assert bench.mma_flops_batched(64) == 3 * 2 * 64 * bench.Q4_PARAMS
+    assert bench.mma_flops_batched(100) == 3 * 2 * 128 * bench.Q4_PARAMS
+    assert bench.mma_flops_batched(300) == 3 * 2 * 512 * bench.Q4_PARAMS
