@@ -94,6 +94,7 @@ struct Smem {
     LayerDev layers[kMaxL];
     float xown[kMaxOwnRows];  // this CTA's rows of the residual stream x
     float2 rope[64];          // (cos, sin) of this frame's position
+    float2 hpart[kWarps / 2]; // residual phases: the second half-row sums of each row pair
     float red[2][kWarps];
     float wv[kWarps];         // head: best logit of each warp
     int32_t wi[kWarps];
@@ -653,23 +654,21 @@ __device__ __noinline__ bool prep_vector(const MegaArgs& P, const uint64_t* ll, 
     float4 v[QN];
     bool ok = true;
     if (src == 0) {
-        // two quads a round: their loads are in flight together (slots past the end re-read the
-        // last quad and are dropped)
+        // all of a thread's quads in one wait: their loads are in flight together, so a K = 8448
+        // input costs one L2 round trip, not three (slots past the end re-read the last quad and
+        // are dropped)
         const int t = threadIdx.x;
+        uint64_t w[2 * QN][2];
+        ok = ll_wait_n<2 * QN>(
+            P,
+            [=](int j) -> const uint64_t* {
+                const int q = min(t + (j >> 1) * kCThreads, nq - 1);
+                return ll + 4 * q + 2 * (j & 1);
+            },
+            ep, w);
 #pragma unroll
-        for (int i0 = 0; i0 < QN; i0 += 2) {
-            uint64_t w[4][2];
-            ok = ll_wait_n<4>(
-                     P,
-                     [=](int j) -> const uint64_t* {
-                         const int q = min(t + (i0 + (j >> 1)) * kCThreads, nq - 1);
-                         return ll + 4 * q + 2 * (j & 1);
-                     },
-                     ep, w) &&
-                 ok;
-            v[i0] = make_float4(ll_val(w[0][0]), ll_val(w[0][1]), ll_val(w[1][0]), ll_val(w[1][1]));
-            if (i0 + 1 < QN) v[i0 + 1] = make_float4(ll_val(w[2][0]), ll_val(w[2][1]), ll_val(w[3][0]), ll_val(w[3][1]));
-        }
+        for (int i = 0; i < QN; ++i)
+            v[i] = make_float4(ll_val(w[2 * i][0]), ll_val(w[2 * i][1]), ll_val(w[2 * i + 1][0]), ll_val(w[2 * i + 1][1]));
 #pragma unroll
         for (int i = 0; i < QN; ++i)
             if (t + i * kCThreads >= nq) v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -779,6 +778,56 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
     float best_v = -FLT_MAX;
     int best_i = 0x7FFFFFFF;
     bool ok = true;
+    if (EPI == EPI_RESID && 2 * r.units <= kCWarps) {
+        // few row pairs (the residual phases own D / 148 rows): two warps per pair, each over
+        // alternate runs of 32 blocks, the halves added in shared memory
+        const int u = warp >> 1, h = warp & 1;
+        float va = 0.0f, vb = 0.0f;
+        int ra = 0, rb = -1;
+        if (u < r.units) {
+            const int k = u / r.ups;
+            ok = wait_seg(sm, P, seg0 + (uint32_t)k) && ok;
+            const WSeg g = wseg(r, false, k, NB);
+            const uint32_t base = sm.seg_off[(seg0 + (uint32_t)k) % kNBar];
+            const int la = 2 * (u - g.ua);
+            const bool two = la + 1 < g.nr;
+            const int lb = two ? la + 1 : la;
+            ra = r.r0 + 2 * u;
+            rb = two ? ra + 1 : -1;
+            const uint32_t na = (base + (uint32_t)la * NB * 16u) / 16u, nb = (base + (uint32_t)lb * NB * 16u) / 16u;
+            const uint32_t sa = (base + g.sc_base + (uint32_t)la * NB * 2u) / 2u;
+            const uint32_t sb = (base + g.sc_base + (uint32_t)lb * NB * 2u) / 2u;
+            float acc_a = 0.0f, acc_b = 0.0f;
+            for (int b = lane + 32 * h; b < NB; b += 64) {
+                const uint4 qa = nibs[na + b], qb = nibs[nb + b];
+                const float x = sm.xs[b];
+                const float da = __fmul_rn(f16_to_f32_ieee(scs[sa + b]), x);
+                const float db = __fmul_rn(f16_to_f32_ieee(scs[sb + b]), x);
+                uint4 L[6];
+#pragma unroll
+                for (int v = 0; v < 6; ++v) L[v] = sm.limbs[v * NB + b];
+                acc_a = __fmaf_rn(block_dp4a(qa, L), da, acc_a);
+                acc_b = __fmaf_rn(block_dp4a(qb, L), db, acc_b);
+            }
+            va = warp_sum(acc_a);
+            vb = warp_sum(acc_b);
+            if (h == 1 && lane == 0) sm.hpart[u] = make_float2(va, vb);
+        }
+        csync();
+        if (u < r.units && h == 0 && lane == 0) {
+            const float2 o = sm.hpart[u];
+            const int oi = ra - r.r0;
+            const float xa_ = __fadd_rn(__fadd_rn(va, o.x), sm.xown[oi]);
+            sm.xown[oi] = xa_;
+            ll_store(outb + ra, xa_, ep);
+            if (rb >= 0) {
+                const float xb_ = __fadd_rn(__fadd_rn(vb, o.y), sm.xown[oi + 1]);
+                sm.xown[oi + 1] = xb_;
+                ll_store(outb + rb, xb_, ep);
+            }
+        }
+        return ok;
+    }
     for (int u = warp; u < r.units; u += kCWarps) {
         const int k = u / r.ups;
         ok = wait_seg(sm, P, seg0 + (uint32_t)k) && ok;
