@@ -609,6 +609,13 @@ __device__ __forceinline__ void quad_limbs(Smem& sm, int q, int NB, float4 v) {
     if (g == 0) sm.xs[b] = __uint_as_float((uint32_t)(127 + e - 27) << 23);
 }
 
+// Sum over each half of a warp (lanes 0-15 and 16-31 separately).
+__device__ __forceinline__ float half_sum(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
 // Sum over the consumer threads in a fixed order; `rb` alternates the two scratch rows so
 // back-to-back sums need one barrier each.
 __device__ __forceinline__ float block_sum(float v, Smem& sm, uint32_t rb) {
@@ -757,9 +764,12 @@ __device__ __forceinline__ float block_dp4a(const uint4 q, const uint4* L) {
     return __fmaf_rn(i2f(s2), 65536.0f, __fmaf_rn(i2f(s1), 256.0f, i2f(s0)));
 }
 
-// One GEMV phase: unit u of this CTA's rows goes to consumer warp u % 15, in segment order; a
-// warp waits for the segment of its unit, its lanes split the unit's blocks.  `seg0` is the
-// global index of the phase's first weight segment.  Returns false after an abort.
+// One GEMV phase over this CTA's units (row pairs; linear_in: gate/value pairs), in segment
+// order.  The residual phases (7 units) give each unit two warps; the others give each unit a
+// half-warp, so a warp takes two units per round.  A unit's lanes wait for its segment and split
+// its blocks: every round ends in a shuffle reduction and an epilogue, so fewer rounds of longer
+// block loops measured faster.  `seg0` is the global index of the phase's first weight segment.
+// Returns false after an abort.
 //   EPI_QKV    RoPE on the q and k pairs, flagged qkv words, K/V ring write (model.rs:426-449)
 //   EPI_RESID  x rows += result (kept in xown), flagged x words               (model.rs:565, 570)
 //   EPI_GATE   silu(gate) * value, flagged hidden words                       (model.rs:517-524)
@@ -828,7 +838,15 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
         }
         return ok;
     }
-    for (int u = warp; u < r.units; u += kCWarps) {
+    // The other phases (K = D, 21 or more units per CTA): a half-warp per unit, so a warp takes
+    // two units at a time (lanes 0-15 the first, 16-31 the second); a missing second unit
+    // repeats the first and is dropped.
+    constexpr bool kHalf = EPI != EPI_RESID;
+    constexpr int kLanes = kHalf ? 16 : 32, kPer = kHalf ? 2 : 1;
+    const int hsel = kHalf ? lane >> 4 : 0, hl = kHalf ? lane & 15 : lane;
+    for (int u0 = warp * kPer; u0 < r.units; u0 += kCWarps * kPer) {
+        const bool mine = u0 + hsel < r.units;
+        const int u = mine ? u0 + hsel : u0;
         const int k = u / r.ups;
         ok = wait_seg(sm, P, seg0 + (uint32_t)k) && ok;
         const WSeg g = wseg(r, gate, k, NB);
@@ -855,7 +873,7 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
             sb = (base + g.sc_base + (uint32_t)lb * NB * 2u) / 2u;
         }
         float acc_a = 0.0f, acc_b = 0.0f;
-        for (int b = lane; b < NB; b += 32) {
+        for (int b = hl; b < NB; b += kLanes) {
             const uint4 qa = nibs[na + b], qb = nibs[nb + b];
             const float x = sm.xs[b];
             const float da = __fmul_rn(f16_to_f32_ieee(scs[sa + b]), x);
@@ -866,8 +884,8 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
             acc_a = __fmaf_rn(block_dp4a(qa, L), da, acc_a);
             acc_b = __fmaf_rn(block_dp4a(qb, L), db, acc_b);
         }
-        float va = warp_sum(acc_a), vb = warp_sum(acc_b);
-        if (lane != 0) continue;
+        float va = kHalf ? half_sum(acc_a) : warp_sum(acc_a), vb = kHalf ? half_sum(acc_b) : warp_sum(acc_b);
+        if (hl != 0 || !mine) continue;
         if (EPI == EPI_RESID) {
             const int o = ra - r.r0;
             const float xa_ = __fadd_rn(va, sm.xown[o]);
@@ -926,9 +944,18 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
             }
         }
     }
-    if (EPI == EPI_LOGITS && lane == 0) {
-        sm.wv[warp] = best_v;
-        sm.wi[warp] = best_i;
+    if (EPI == EPI_LOGITS) {
+        // the best of the two half-warps (lowest index on ties)
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, best_v, 16);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, best_i, 16);
+        if (ov > best_v || (ov == best_v && oi < best_i)) {
+            best_v = ov;
+            best_i = oi;
+        }
+        if (lane == 0) {
+            sm.wv[warp] = best_v;
+            sm.wi[warp] = best_i;
+        }
     }
     return ok;
 }
