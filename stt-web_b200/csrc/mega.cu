@@ -609,10 +609,11 @@ __device__ __forceinline__ void quad_limbs(Smem& sm, int q, int NB, float4 v) {
     if (g == 0) sm.xs[b] = __uint_as_float((uint32_t)(127 + e - 27) << 23);
 }
 
-// Sum over each half of a warp (lanes 0-15 and 16-31 separately).
-__device__ __forceinline__ float half_sum(float v) {
+// Sum over each group of W consecutive lanes.
+template <int W>
+__device__ __forceinline__ float group_sum(float v) {
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    for (int o = W / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
     return v;
 }
 
@@ -766,7 +767,7 @@ __device__ __forceinline__ float block_dp4a(const uint4 q, const uint4* L) {
 
 // One GEMV phase over this CTA's units (row pairs; linear_in: gate/value pairs), in segment
 // order.  The residual phases (7 units) give each unit two warps; the others give each unit a
-// half-warp, so a warp takes two units per round.  A unit's lanes wait for its segment and split
+// group of 16 lanes (linear_in: 8), so a warp takes two (four) units per round.  A unit's lanes wait for its segment and split
 // its blocks: every round ends in a shuffle reduction and an epilogue, so fewer rounds of longer
 // block loops measured faster.  `seg0` is the global index of the phase's first weight segment.
 // Returns false after an abort.
@@ -838,12 +839,12 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
         }
         return ok;
     }
-    // The other phases (K = D, 21 or more units per CTA): a half-warp per unit, so a warp takes
-    // two units at a time (lanes 0-15 the first, 16-31 the second); a missing second unit
-    // repeats the first and is dropped.
+    // The other phases (K = D, 21 or more units per CTA): a group of 16 lanes per unit (8 in
+    // linear_in, 57 units), so a warp takes kPer units at a time; a missing unit of a group
+    // repeats the first of the warp and is dropped.
     constexpr bool kHalf = EPI != EPI_RESID;
-    constexpr int kLanes = kHalf ? 16 : 32, kPer = kHalf ? 2 : 1;
-    const int hsel = kHalf ? lane >> 4 : 0, hl = kHalf ? lane & 15 : lane;
+    constexpr int kLanes = EPI == EPI_GATE ? 8 : kHalf ? 16 : 32, kPer = 32 / kLanes;
+    const int hsel = lane / kLanes, hl = lane % kLanes;
     for (int u0 = warp * kPer; u0 < r.units; u0 += kCWarps * kPer) {
         const bool mine = u0 + hsel < r.units;
         const int u = mine ? u0 + hsel : u0;
@@ -884,7 +885,7 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
             acc_a = __fmaf_rn(block_dp4a(qa, L), da, acc_a);
             acc_b = __fmaf_rn(block_dp4a(qb, L), db, acc_b);
         }
-        float va = kHalf ? half_sum(acc_a) : warp_sum(acc_a), vb = kHalf ? half_sum(acc_b) : warp_sum(acc_b);
+        float va = group_sum<kLanes>(acc_a), vb = group_sum<kLanes>(acc_b);
         if (hl != 0 || !mine) continue;
         if (EPI == EPI_RESID) {
             const int o = ra - r.r0;
@@ -945,7 +946,7 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
         }
     }
     if (EPI == EPI_LOGITS) {
-        // the best of the two half-warps (lowest index on ties)
+        // the best of the two 16-lane groups (lowest index on ties)
         const float ov = __shfl_xor_sync(0xFFFFFFFFu, best_v, 16);
         const int oi = __shfl_xor_sync(0xFFFFFFFFu, best_i, 16);
         if (ov > best_v || (ov == best_v && oi < best_i)) {
