@@ -35,7 +35,7 @@ KV_BYTES_PER_TOKEN = 16 * 2 * 2048 * 2   # bf16 K+V of one cached position over 
 EMB_BYTES = 33 * 2048 * 2        # 33 bf16 embedding rows per frame
 
 
-MEGA_TRAFFIC_750 = 508_194_168_320 + 2_685_069_824  # dram__bytes_read.sum + dram__bytes_write.sum, one launch
+MEGA_TRAFFIC_750 = 508_142_132_480 + 2_654_166_784  # dram__bytes_read.sum + dram__bytes_write.sum, one launch
 
 
 def algorithmic_bytes_per_utterance(frames=FRAMES, ring=751):
