@@ -849,8 +849,7 @@ __device__ __noinline__ bool gemv_phase(const MegaArgs& P, int p, uint32_t seg0,
     // The other phases (K = D, 21 or more units per CTA): a group of 16 lanes per unit (8 in
     // linear_in, 57 units), so a warp takes kPer units at a time; a missing unit of a group
     // repeats the first of the warp and is dropped.
-    constexpr bool kHalf = EPI != EPI_RESID;
-    constexpr int kLanes = EPI == EPI_GATE ? 8 : kHalf ? 16 : 32, kPer = 32 / kLanes;
+    constexpr int kLanes = EPI == EPI_GATE ? 8 : EPI == EPI_RESID ? 32 : 16, kPer = 32 / kLanes;
     const int hsel = lane / kLanes, hl = lane % kLanes;
     for (int u0 = warp * kPer; u0 < r.units; u0 += kCWarps * kPer) {
         const bool mine = u0 + hsel < r.units;
