@@ -227,19 +227,23 @@ def run_reference(args):
     return 0
 
 
-def multi_stream(model, S, F, offsets, seed, torch, np, lib, check, stt_b200):
-    """Config 3 / 4 workload on this GPU: S streams, stream s pre-rolled alone to offsets[s] frames,
-    then F batched steps of all S streams (one frame each), device-timed.  Returns ms per step and
-    the number of timed steps (the last F - warm of the F)."""
+def multi_stream(model, stream_ids, F, offsets, seed, torch, np, lib, check, stt_b200):
+    """Config 3 / 4 workload on this GPU: the S = len(stream_ids) streams of those global ids, the s-th
+    pre-rolled alone to offsets[s] frames, then F batched steps of all S streams (one frame each),
+    device-timed.  A stream's audio tokens follow from (seed, global id), so it decodes the same
+    frames whichever rank holds it.  Returns ms per step and the number of timed steps (the last
+    F - warm of the F)."""
+    S = len(stream_ids)
     cache = model.create_cache(S, "bf16")
     ts = torch.cuda.current_stream()
     for s_ in range(S):
         if offsets[s_]:
-            a = torch.from_numpy(stt_b200.audio_tokens(seed, s_, offsets[s_]).astype(np.int32)).cuda()
+            pre = stt_b200.audio_tokens(seed, stream_ids[s_], offsets[s_])
+            a = torch.from_numpy(pre.astype(np.int32)).cuda()
             tk = torch.empty(offsets[s_], dtype=torch.int32, device="cuda")
             check(lib().stt_stream_feed_frames_device(cache._h, s_, offsets[s_], C.c_void_p(a.data_ptr()),
                                                       C.c_void_p(tk.data_ptr()), C.c_void_p(ts.cuda_stream)), "pre-roll")
-    aud = np.stack([stt_b200.audio_tokens(seed, s_, F, first_frame=offsets[s_]) for s_ in range(S)], 1)
+    aud = np.stack([stt_b200.audio_tokens(seed, stream_ids[s_], F, first_frame=offsets[s_]) for s_ in range(S)], 1)
     da = torch.from_numpy(aud.astype(np.int32)).cuda()
     dt = torch.empty(F, S, dtype=torch.int32, device="cuda")
     ids = (C.c_int32 * S)(*range(S))
@@ -318,6 +322,7 @@ def main():
     import numpy as np
     import torch
     import stt_b200
+    from stt_b200 import shard
     from stt_b200._lib import lib, check
 
     rank = int(os.environ.get("RANK", "0"))
@@ -338,11 +343,7 @@ def main():
         torch.cuda.synchronize()
 
     def max_over_ranks(v):
-        if not dist:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(v, dist, "cuda")
 
     nthreads = max(1, (os.cpu_count() or 8) // max(1, world))
     g = stt_b200.synth_gguf(stt_b200.SynthSpec(seed=SEED, n_threads=nthreads))
@@ -350,8 +351,8 @@ def main():
     model = stt_b200.SttModel.from_buffer(g.address, g.length, device=local, config=cfg)
     g.close()
     if args.batched:
-        ms_b, k_b = multi_stream(model, args.batched, nframes, [0] * args.batched, SEED, torch, np, lib, check,
-                                 stt_b200)
+        ms_b, k_b = multi_stream(model, range(args.batched), nframes, [0] * args.batched, SEED, torch, np, lib,
+                                 check, stt_b200)
         if rank == 0:
             print(json.dumps({"batched_streams": args.batched, "frames": nframes, "timed_steps": k_b,
                               "ms_per_step": ms_b, "frames_per_s": args.batched * 1000.0 / ms_b}))
@@ -457,7 +458,8 @@ def main():
     if not args.no_multi:
         # config 3: 64 streams per GPU at staggered offsets 0..374, 375 batched steps
         offs = [round(i * 374 / 63) for i in range(64)]
-        ms64, k64 = multi_stream(model, 64, 375, offs, SEED + 1000 * rank, torch, np, lib, check, stt_b200)
+        ms64, k64 = multi_stream(model, range(64 * rank, 64 * rank + 64), 375, offs, SEED, torch, np, lib, check,
+                                 stt_b200)
         barrier()
         ms64 = max_over_ranks(ms64)
         b64 = algorithmic_bytes_batched(offs, 375 - k64, 375)
@@ -472,13 +474,15 @@ def main():
                                         "peak_kind": "sustained bf16 (a seconds-long loop)", "unit": "TFLOP/s"},
                              "config": "64 streams per GPU, staggered offsets 0..374, 375 frames each, bf16 KV, "
                                        "layer products on tcgen05 (M = 64)"}
-        # config 4: 512 streams split evenly over the GPUs, 250 frames each
-        per = 512 // world
-        ms512, k512 = multi_stream(model, per, 250, [0] * per, SEED + 2000 * rank, torch, np, lib, check, stt_b200)
+        # config 4: 512 streams split into contiguous blocks over the GPUs, 250 frames each
+        blk = shard.stream_block(512, world, rank)
+        per = len(blk)
+        ms512, k512 = multi_stream(model, blk, 250, [0] * per, SEED, torch, np, lib, check, stt_b200)
         barrier()
         ms512 = max_over_ranks(ms512)
+        total512 = shard.sum_over_ranks(per, dist, "cuda")
         b512 = algorithmic_bytes_batched([0] * per, 250 - k512, 250)
-        line["streams512"] = {"frames_per_s": world * per * 1000.0 / ms512, "ms_per_step": ms512,
+        line["streams512"] = {"frames_per_s": total512 * 1000.0 / ms512, "ms_per_step": ms512,
                               "timed_steps": k512, "config": f"{per} streams per GPU x {world} GPUs, 250 frames",
                               "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": b512,
                                            "achieved": b512 / (ms512 / 1000.0) / 1e9, "peak": pk["hbm_gbs"],
