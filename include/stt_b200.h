@@ -240,6 +240,31 @@ int stt_synth_audio_tokens(uint64_t seed, int32_t stream, int32_t first_frame, i
                            int32_t num_codebooks, uint32_t* out);
 
 /* ---------------------------------------------------------------------------------------
+ * SentencePiece detokeniser: the step after the decode path.  Replaces SpmDecoder
+ * (crates/stt-wasm/src/tokenizer.rs:7-38), which turns the emitted text-token ids into text.
+ * Host only: these calls touch no device.  A decoder is immutable after creation, so several
+ * threads may decode with one decoder at the same time.
+ * ------------------------------------------------------------------------------------- */
+typedef struct stt_spm_decoder stt_spm_decoder;
+/* SpmDecoder::from_bytes (tokenizer.rs:14-17, vocabulary walk :44-96): the pieces of a
+ * SentencePiece `.model` protobuf, token id = entry order.  A piece whose declared length runs
+ * past the buffer (a panic in the reference) is STT_E_FORMAT. */
+int stt_spm_decoder_create(const uint8_t* model_bytes, size_t n_bytes, stt_spm_decoder** out);
+int stt_spm_decoder_destroy(stt_spm_decoder* dec);
+/* SpmDecoder::vocab_len (tokenizer.rs:35-37). */
+int stt_spm_vocab_len(const stt_spm_decoder* dec, int64_t* out);
+/* The piece of token `id` as the decoder holds it (UTF-8; invalid bytes of the file replaced
+ * by U+FFFD as in tokenizer.rs:90).  Output convention of both calls below: *len receives the
+ * text's byte length; with out == NULL nothing is written (a size query), else out must hold
+ * *len + 1 bytes (the text and a NUL) or the call fails with STT_E_INVALID_ARG. */
+int stt_spm_piece(const stt_spm_decoder* dec, int64_t id, char* out, size_t cap, size_t* len);
+/* SpmDecoder::decode (tokenizer.rs:30-32, rules :150-192): ids 0 (end of stream) and 3
+ * (padding) and ids past the vocabulary are skipped; runs of byte-fallback pieces "<0xHH>"
+ * are emitted only when they form valid UTF-8; U+2581 becomes a space; nothing is trimmed. */
+int stt_spm_decode(const stt_spm_decoder* dec, const uint32_t* ids, size_t n, char* out, size_t cap,
+                   size_t* len);
+
+/* ---------------------------------------------------------------------------------------
  * Diagnostics (no counterpart in the reference): timing probes of the persistent
  * single-stream step kernel, used by the benchmarks and profiles of this library.
  * ------------------------------------------------------------------------------------- */

@@ -6,3 +6,4 @@ Add the directory holding this package (``stt-web_b200``) to ``sys.path`` and im
 from ._lib import LIB_PATH, SttError, lib  # noqa: F401
 from .model import LayerCaches, Q4Tensor, SttConfig, SttModel, SttStream, q4_matmul  # noqa: F401
 from .synth import SynthSpec, audio_tokens, quantize_q4_0, synth_gguf  # noqa: F401
+from .tokenizer import SpmDecoder  # noqa: F401

@@ -132,6 +132,11 @@ SIGNATURES = {
     "stt_synth_free": (None, [U8P]),
     "stt_synth_quantize_q4_0": (C.c_int, [F32P, C.c_size_t, U8P]),
     "stt_synth_audio_tokens": (C.c_int, [C.c_uint64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, U32P]),
+    "stt_spm_decoder_create": (C.c_int, [U8P, C.c_size_t, C.POINTER(P)]),
+    "stt_spm_decoder_destroy": (C.c_int, [P]),
+    "stt_spm_vocab_len": (C.c_int, [P, C.POINTER(C.c_int64)]),
+    "stt_spm_piece": (C.c_int, [P, C.c_int64, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "stt_spm_decode": (C.c_int, [P, U32P, C.c_size_t, C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]),
     "stt_debug_trace_frame": (C.c_int, [P, C.c_int]),
     "stt_debug_get_trace": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int, I32P]),
     "stt_debug_get_trace_ctas": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
