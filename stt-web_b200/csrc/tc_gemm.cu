@@ -166,15 +166,8 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
-        : "memory");
-}
-// The same with A read from tensor memory: row i of A in TMEM lane i, two f16 per 32-bit column.
+// D (+)= A * B, f16 operands, f32 accumulator in TMEM, with A read from tensor memory (row i of A
+// in TMEM lane i, two f16 per 32-bit column) and B from shared memory through its descriptor.
 __device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
                                            uint32_t acc) {
     asm volatile(
@@ -214,7 +207,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(__uint_as_float(r[i]), kWUnscale);  // exact: a power of two
 }
 
-// Consecutive 32-bit columns of this thread's TMEM lane (warp-collective): 16 or 8 of them.
+// 16 consecutive 32-bit columns of this thread's TMEM lane (warp-collective).
 __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&v)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -222,11 +215,6 @@ __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&v)[16])
         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
         "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
-}
-__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&v)[8]) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
-                 "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-                 : "memory");
 }
 
 template <int NT>
