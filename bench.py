@@ -35,6 +35,10 @@ KV_BYTES_PER_TOKEN = 16 * 2 * 2048 * 2   # bf16 K+V of one cached position over 
 EMB_BYTES = 33 * 2048 * 2        # 33 bf16 embedding rows per frame
 
 
+# The reference's published 1-stream step time over a 750-frame (60 s) utterance: 52.5 ms per frame
+# on an Apple M2 GPU through wgpu/Metal (BENCHMARKS.md:29 of stt-web).
+PUBLISHED_FPS_750 = 1000.0 / 52.5
+
 MEGA_TRAFFIC_750 = 508_142_132_480 + 2_654_166_784  # dram__bytes_read.sum + dram__bytes_write.sum, one launch
 
 
@@ -436,7 +440,11 @@ def main():
         "metric": "decode frames/s per GPU (1 stream, 750-frame utterance)",
         "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms / args.steps, "ms_per_frame": ms / args.steps / nframes,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak",
+        # against the published single-stream rate (other hardware), at the full 750 frames only
+        "vs_baseline": value / PUBLISHED_FPS_750 if nframes == FRAMES else None,
+        "vs_baseline_source": "stt-web BENCHMARKS.md:29: 52.5 ms/frame, 1 stream x 750 frames, Apple M2 wgpu/Metal",
+        "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": f"1 stream x {nframes} frames per GPU, STT-1B Q4_0, 16 layers d2048, bf16 KV",
                    "l2": "inputs larger than L2: 627 MB of Q4 weights streamed per frame",
