@@ -709,7 +709,10 @@ int run_steps(stt_streams* s, const int32_t* ids, int n, int steps, const uint32
               int32_t* d_tokens, float* d_logits, int mode, cudaStream_t st) {
     stt_model* m = s->m;
     if (n > kMaxBatch) return set_error(STT_E_INVALID_ARG, "batch of %d streams exceeds %d", n, kMaxBatch);
-    static DescInit init;  // large; filled under the caller's serialisation of this handle
+    // Large (16 KB), so not on the stack; one per host thread, since threads may drive different
+    // handles at the same time (one thread per GPU).  The launch copies it into the kernel's
+    // parameters, so it is free again when launch_set_desc returns.
+    static thread_local DescInit init;
     init.desc = StepDesc{d_audio, d_text, d_tokens, d_logits, 0, mode, 0, 0};
     init.n = n;
     std::memcpy(init.ids, ids, sizeof(int32_t) * n);

@@ -682,15 +682,23 @@ bool tc_gemm_scales_ok(const uint8_t* q4_blocks, int64_t nblocks) {
 }
 
 cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out) {
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    if (!encode) {
+    // The driver's encoder, looked up once; a function-local static is initialised exactly once
+    // even when threads load models on several devices at the same time.
+    struct EncodeFn {
+        PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+        cudaError_t err = cudaSuccess;
+    };
+    static const EncodeFn lookup = [] {
+        EncodeFn r;
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
-        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-        if (e != cudaSuccess) return e;
-        if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
-        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
+        r.err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (r.err == cudaSuccess && (q != cudaDriverEntryPointSuccess || !fn)) r.err = cudaErrorNotSupported;
+        if (r.err == cudaSuccess) r.fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        return r;
+    }();
+    if (lookup.err != cudaSuccess) return lookup.err;
+    const PFN_cuTensorMapEncodeTiled_v12000 encode = lookup.fn;
     const cuuint64_t nb = (cuuint64_t)(w.k / 32);
     // nibble plane: [n rows][k/32 * 16 bytes]; a box is one quad (128 bytes) of 128 rows
     {
