@@ -839,6 +839,13 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
         cudaFree(s->d_scratch);
         return set_error(STT_E_OOM, "cannot allocate the KV rings (%zu bytes)", s->kv_stream_bytes * S);
     }
+    // from here on a failing call releases everything allocated so far; success hands the set out
+    struct ReleaseOnError {
+        std::unique_ptr<stt_streams>& set;
+        ~ReleaseOnError() {
+            if (set) stt_streams_destroy(set.release());
+        }
+    } release_on_error{s};
     uint8_t* b = static_cast<uint8_t*>(s->d_scratch);
     s->d_state = reinterpret_cast<StreamState*>(b + o_state);
     s->d_x = reinterpret_cast<float*>(b + o_x);
