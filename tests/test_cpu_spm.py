@@ -190,3 +190,16 @@ def test_load_reads_the_file(model_bytes, tmp_path):
     d = stt_b200.SpmDecoder.load(str(f))
     assert d.vocab_len() == 400
     d.close()
+
+
+def test_per_token_decoding_concatenates(dec, golden):
+    # The reference keeps each piece's leading space so that a host decoding token by token, as the
+    # stream emits them, gets the same text as decoding the whole sequence (tokenizer.rs:187-190).
+    # That holds for every sequence without byte-fallback pieces; a multi-byte character split over
+    # byte pieces only decodes once its run is complete.
+    vocab = golden["pieces"]
+    for c in golden["cases"]:
+        ids = c["ids"]
+        if any(0 <= i < len(vocab) and S.byte_piece_value(vocab[i]) is not None for i in ids):
+            continue
+        assert "".join(dec.decode([i]) for i in ids) == dec.decode(ids) == c["text"]
