@@ -350,9 +350,14 @@ def main():
         return shard.max_over_ranks(v, dist, "cuda")
 
     nthreads = max(1, (os.cpu_count() or 8) // max(1, world))
+    t0 = time.perf_counter()
     g = stt_b200.synth_gguf(stt_b200.SynthSpec(seed=SEED, n_threads=nthreads))
+    t1 = time.perf_counter()
     cfg = stt_b200.SttConfig(text_start_token=0)   # initial text token 0 (benchmark config)
     model = stt_b200.SttModel.from_buffer(g.address, g.length, device=local, config=cfg)
+    t2 = time.perf_counter()   # the load synchronises the device before it returns
+    load = {"gguf_bytes": g.length, "synth_s": t1 - t0, "model_load_s": t2 - t1,
+            "model_load_gbs": g.length / (t2 - t1) / 1e9}
     g.close()
     if args.batched:
         ms_b, k_b = multi_stream(model, range(args.batched), nframes, [0] * args.batched, SEED, torch, np, lib,
@@ -458,6 +463,8 @@ def main():
         "e2e": {"value": e2e, "unit": "frames/s", "h2d_bytes_per_step": nframes * 32 * 4,
                 "d2h_bytes_per_step": nframes * (4 + 32)},
         "clocks": clocks,
+        # this rank's model load from a host buffer (parse, upload, repack), host wall clock
+        "load": load,
         # our kernels per step: stream reset, step descriptor, audio-embedding sums, persistent kernel
         "gpu_launches": 4 * args.steps,
         "diagnostics": diag,
