@@ -199,8 +199,10 @@ int stt_q4_matmul(const stt_q4_tensor* w, const float* input, int rows, float* o
  * on demand: a call with more rows than any before it may allocate (and so synchronise). */
 int stt_q4_matmul_device(const stt_q4_tensor* w, const void* d_input, int in_dtype, int rows,
                          float* d_out, void* cuda_stream);
-/* No counterpart in the reference.  Split-K form of stt_q4_matmul_device (same arguments plus
- * `splits`, 1..64 and at most k/32) that requests no device memory: partial sums and per-tile
+/* No counterpart in the reference.  Split-K form of stt_q4_matmul_device for f32 (in_dtype 0) and
+ * bf16 (in_dtype 1) input only, with `splits` (1..64 and at most k/32) added; in_dtype 2 (f16, the
+ * tensor-core product, whose scratch grows with the rows) is rejected with STT_E_INVALID_ARG.  It
+ * requests no device memory: partial sums and per-tile
  * counters live in a fixed 4 MiB + 16 KiB array of the library's device image, so
  * splits * rows * n * 4 must be at most 4 MiB and n at most 65536, else STT_E_INVALID_ARG.
  * The first call on a device looks up that array's address (make it before capturing a
@@ -211,33 +213,6 @@ int stt_q4_matmul_device_noalloc(const stt_q4_tensor* w, const void* d_input, in
 /* Dequantises the whole matrix to f32 on the device and copies it to out_host (n*k floats):
  * out[r*k + j] = (nibble - 8) * f16_to_f32(scale), bit-exact with gguf.rs:616-633. */
 int stt_q4_tensor_dequant(const stt_q4_tensor* w, float* out_host);
-
-/* ---------------------------------------------------------------------------------------
- * Synthetic model and inputs (no counterpart in the reference, which downloads the real
- * checkpoint).  Weights are drawn N(mean, std) from Philox-4x32-10 keyed by (seed, tensor
- * index) with a Box-Muller transform in f64, rounded to bf16, and Q4_0-quantised with the
- * exact rules of scripts/quantize.py:65-116; the file layout follows quantize.py:119-199.
- * ------------------------------------------------------------------------------------- */
-typedef struct stt_synth_params {
-    uint64_t seed;
-    int32_t num_layers, hidden_size, num_heads, ffn_hidden;
-    int32_t vocab_size, text_in_vocab_size, num_codebooks, audio_vocab_size;
-    int32_t embedding_dtype;     /* 30 = BF16 (default), 2 = Q4_0, 0 = F32                  */
-    float weight_std;            /* 0.02 */
-    float norm_mean, norm_std;   /* 1.0, 0.02 (alphas rounded to bf16, stored F32)          */
-    int32_t n_threads;           /* 0 = all host cores                                      */
-} stt_synth_params;
-void stt_synth_default(stt_synth_params* p);
-/* Writes a whole GGUF v3 file into a buffer allocated by the library (*out_buf, *out_len);
- * release it with stt_synth_free. */
-int stt_synth_gguf(const stt_synth_params* p, uint8_t** out_buf, size_t* out_len);
-void stt_synth_free(uint8_t* buf);
-/* Q4_0-quantises n floats (n % 32 == 0) with the rules of scripts/quantize.py:65-116. */
-int stt_synth_quantize_q4_0(const float* x, size_t n, uint8_t* out);
-/* Seeded uniform audio tokens in [0, 2048): out[f*num_codebooks + c] for frames
- * first_frame .. first_frame+n_frames-1 of stream `stream`. */
-int stt_synth_audio_tokens(uint64_t seed, int32_t stream, int32_t first_frame, int32_t n_frames,
-                           int32_t num_codebooks, uint32_t* out);
 
 /* ---------------------------------------------------------------------------------------
  * SentencePiece detokeniser: the step after the decode path.  Replaces SpmDecoder
@@ -282,6 +257,25 @@ int stt_debug_get_trace_ctas(stt_streams* streams, uint64_t* out, int cap, int* 
  * nanoseconds: mode 0 is the persistent kernel's barrier (release add, acquire poll of the
  * counter), mode 1 a variant in which the last arriver publishes a flag that the others poll. */
 int stt_debug_barrier_ns(int device, int iters, int mode, double* ns_per_barrier);
+
+/* Test of the persistent kernel's bounded waits.  Arms the next single-stream call on this set
+ * (one launch only): in its first frame, the CTAs that compute the first layer's output projection
+ * wait for an input epoch that no phase ever publishes.  That wait gives up after its limit (about
+ * a second), the launch stops through the same abort path as a real timeout, and the call returns
+ * STT_E_DEVICE_FLAG; the stream's state on the device is left as it was before the failed frame, so
+ * stt_stream_reset (or the next call) continues normally.  Nothing faults or hangs. */
+int stt_debug_arm_wait_timeout(stt_streams* streams);
+/* Number of kernels one batched step of n streams (n >= 2) launches: the nodes of the CUDA
+ * graph that the library captures for that batch size (captured on first use). */
+int stt_debug_graph_kernels(stt_streams* streams, int n, int* kernels);
+/* Mean device time of one launch of each of the five tensor-core products of a batched step of
+ * n streams (tensor_core_min_batch <= n <= the set's size): layer 0's in_proj, out_proj,
+ * linear_in and linear_out, then the text head, each timed over `iters` back-to-back launches
+ * with CUDA events on the set's own stream.  us_out[5] receives microseconds per launch and
+ * flops_out[5] (may be NULL) the useful work of one launch, 2 * n * rows * in_features.  The
+ * products read the set's current input tiles and overwrite its partial-sum scratch, so call
+ * this only between steps. */
+int stt_debug_time_products(stt_streams* streams, int n, int iters, double* us_out, double* flops_out);
 
 /* Text of the last error on the calling thread ("" if none). */
 const char* stt_last_error(void);

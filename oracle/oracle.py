@@ -67,6 +67,13 @@ def lib() -> C.CDLL:
         L.orc_forward.argtypes = [P, U32P, C.c_uint32, F32P]
         L.orc_feed_frame.restype = C.c_int64
         L.orc_feed_frame.argtypes = [P, U32P]
+        I64P = C.POINTER(C.c_int64)
+        L.orc_forward_batch.restype = C.c_int
+        L.orc_forward_batch.argtypes = [C.POINTER(P), C.c_int, U32P, U32P, F32P, I64P]
+        L.orc_feed_frame_batch.restype = C.c_int
+        L.orc_feed_frame_batch.argtypes = [C.POINTER(P), C.c_int, U32P, F32P, I64P]
+        L.orc_forward_gpu_token.restype = C.c_int64
+        L.orc_forward_gpu_token.argtypes = [P, U32P, C.c_int, C.c_uint32, C.c_uint32, F32P]
         L.orc_flush.restype = C.c_int
         L.orc_flush.argtypes = [P, U32P, C.c_int]
         L.orc_stream_state.argtypes = [P, C.POINTER(C.c_int64)]
@@ -160,6 +167,40 @@ class OracleModel:
             pass
 
 
+def _handles(streams):
+    hs = (C.c_void_p * len(streams))(*[s._h for s in streams])
+    return hs
+
+
+def forward_batch(streams, audio, texts, want_logits: bool = True):
+    """orc_forward for several streams of one model in one step (the same values each stream
+    would get alone).  Returns (logits [n, vocab] or None, argmax [n])."""
+    n = len(streams)
+    a = np.ascontiguousarray(np.asarray(audio, dtype=np.uint32).reshape(n, -1))
+    t = np.ascontiguousarray(np.asarray(texts, dtype=np.uint32).reshape(n))
+    lg = np.empty((n, streams[0].model.vocab), dtype=np.float32) if want_logits else None
+    am = np.empty(n, dtype=np.int64)
+    rc = lib().orc_forward_batch(_handles(streams), n, _p(a, C.c_uint32), _p(t, C.c_uint32),
+                                 _p(lg, C.c_float) if want_logits else None, _p(am, C.c_int64))
+    if rc != 0:
+        raise RuntimeError("oracle forward_batch failed: " + lib().orc_last_error().decode())
+    return lg, am
+
+
+def feed_frame_batch(streams, audio, want_logits: bool = False):
+    """SttStream::feed_frame for several streams in one batched step.  Returns (tokens as a list
+    with None for frames inside the delay, logits [n, vocab] or None)."""
+    n = len(streams)
+    a = np.ascontiguousarray(np.asarray(audio, dtype=np.uint32).reshape(n, -1))
+    lg = np.empty((n, streams[0].model.vocab), dtype=np.float32) if want_logits else None
+    tk = np.empty(n, dtype=np.int64)
+    rc = lib().orc_feed_frame_batch(_handles(streams), n, _p(a, C.c_uint32), _p(lg, C.c_float) if want_logits else None,
+                                    _p(tk, C.c_int64))
+    if rc != 0:
+        raise RuntimeError("oracle feed_frame_batch failed: " + lib().orc_last_error().decode())
+    return [None if t < 0 else int(t) for t in tk], lg
+
+
 class OracleStream:
     def __init__(self, model: OracleModel, flags: int = 0):
         self.model = model
@@ -172,6 +213,21 @@ class OracleStream:
         if r < 0:
             raise RuntimeError("oracle forward failed: " + lib().orc_last_error().decode())
         return lg, int(r)
+
+    def forward_gpu_token(self, audio, argmax, fallback_text: int):
+        """SttModel::forward_with_gpu_token: `argmax` is the previous frame's argmax or None."""
+        a = np.ascontiguousarray(np.asarray(audio, dtype=np.uint32))
+        lg = np.empty(self.model.vocab, dtype=np.float32)
+        r = lib().orc_forward_gpu_token(self._h, _p(a, C.c_uint32), 0 if argmax is None else 1,
+                                        0 if argmax is None else int(argmax), fallback_text, _p(lg, C.c_float))
+        if r < 0:
+            raise RuntimeError("oracle forward_gpu_token failed: " + lib().orc_last_error().decode())
+        return lg, int(r)
+
+    def feed_frame_logits(self, audio):
+        """feed_frame that also returns the step's logits: (token or None, logits)."""
+        toks, lg = feed_frame_batch([self], np.asarray(audio).reshape(1, -1), want_logits=True)
+        return toks[0], lg[0]
 
     def feed_frame(self, audio):
         a = np.ascontiguousarray(np.asarray(audio, dtype=np.uint32))

@@ -195,43 +195,103 @@ static inline float dot4(const float* a, const float* b) {
     return s;
 }
 
-/* One output of shader_naive.wgsl:main — the block loop :51-95. */
-static float q4_row_dot(const uint8_t* row, int64_t blocks_per_row, const float* input, uint32_t flags) {
-    float acc = 0.0f;
+/* Q4 matmul with the per-output summation order of shader_naive.wgsl:main (the block loop
+ * :51-95): for each block, for each of its 4 words, acc += dot(lo vec4) then acc += dot(hi vec4),
+ * with w = (nibble - 8) * scale in f32 (:64-81).  A weight row is dequantised once into `wrow`
+ * (element j of a block holds the low nibble of byte j, element j + 16 the high one) and applied
+ * to every input row, which gives the same values and the same order as a per-output loop. */
+static void q4_row_dequant(const uint8_t* row, int64_t blocks_per_row, uint32_t flags, float* wrow) {
     for (int64_t blk = 0; blk < blocks_per_row; ++blk) {
         const uint8_t* b = row + blk * 18;
         const float scale = orc_f16_to_f32_ieee((uint16_t)(b[0] | (b[1] << 8)));
-        const int64_t k_base = blk * 32;
-        for (int wi = 0; wi < 4; ++wi) {
-            const uint8_t* p = b + 2 + wi * 4;
-            float w_lo[4], w_hi[4], in_lo[4], in_hi[4];
-            for (int i = 0; i < 4; ++i) {
-                w_lo[i] = ((float)(p[i] & 0x0F) - 8.0f) * scale;
-                w_hi[i] = ((float)((p[i] >> 4) & 0x0F) - 8.0f) * scale;
-                in_lo[i] = input[k_base + wi * 4 + i];
-                in_hi[i] = input[k_base + 16 + wi * 4 + i];
-                if (flags & ORC_GEMM_BF16) {
-                    w_lo[i] = round_bf16(w_lo[i]);
-                    w_hi[i] = round_bf16(w_hi[i]);
-                    in_lo[i] = round_bf16(in_lo[i]);
-                    in_hi[i] = round_bf16(in_hi[i]);
-                }
+        float* w = wrow + blk * 32;
+        for (int j = 0; j < 16; ++j) {
+            w[j] = ((float)(b[2 + j] & 0x0F) - 8.0f) * scale;
+            w[16 + j] = ((float)((b[2 + j] >> 4) & 0x0F) - 8.0f) * scale;
+            if (flags & ORC_GEMM_BF16) {
+                w[j] = round_bf16(w[j]);
+                w[16 + j] = round_bf16(w[16 + j]);
             }
-            acc += dot4(w_lo, in_lo);
-            acc += dot4(w_hi, in_hi);
+        }
+    }
+}
+
+static float q4_row_dot(const float* wrow, int64_t blocks_per_row, const float* input) {
+    float acc = 0.0f;
+    for (int64_t blk = 0; blk < blocks_per_row; ++blk) {
+        const int64_t kb = blk * 32;
+        for (int wi = 0; wi < 4; ++wi) {
+            acc += dot4(wrow + kb + wi * 4, input + kb + wi * 4);
+            acc += dot4(wrow + kb + 16 + wi * 4, input + kb + 16 + wi * 4);
         }
     }
     return acc;
 }
 
+/* The same products for m input rows at once: the inputs are transposed to [k][m] so that the
+ * loop over rows runs across SIMD lanes, while each row keeps its own accumulator and exactly the
+ * operation order of q4_row_dot (dot4 products, then the two adds per word). */
+static void q4_rows_dot(const float* wrow, int64_t blocks_per_row, const float* xt, int64_t m, float* acc,
+                        float* s4) {
+    for (int64_t r = 0; r < m; ++r) acc[r] = 0.0f;
+    for (int64_t blk = 0; blk < blocks_per_row; ++blk) {
+        const int64_t kb = blk * 32;
+        for (int wi = 0; wi < 4; ++wi) {
+            for (int half = 0; half < 2; ++half) {
+                const int64_t k0 = kb + half * 16 + wi * 4;
+                const float w0 = wrow[k0], w1 = wrow[k0 + 1], w2 = wrow[k0 + 2], w3 = wrow[k0 + 3];
+                const float* x0 = xt + k0 * m;
+                const float* x1 = x0 + m;
+                const float* x2 = x1 + m;
+                const float* x3 = x2 + m;
+                for (int64_t r = 0; r < m; ++r) {
+                    float t = w0 * x0[r];
+                    t = t + w1 * x1[r];
+                    t = t + w2 * x2[r];
+                    t = t + w3 * x3[r];
+                    s4[r] = t;
+                }
+                for (int64_t r = 0; r < m; ++r) acc[r] = acc[r] + s4[r];
+            }
+        }
+    }
+}
+
 void orc_q4_matmul(const uint8_t* w, int64_t n, int64_t k, const float* in, int64_t m, float* out,
                    uint32_t flags) {
     const int64_t nb = k / 32;
-#pragma omp parallel for schedule(static)
-    for (int64_t i = 0; i < n * m; ++i) {
-        const int64_t r = i / n, c = i % n;
-        out[r * n + c] = q4_row_dot(w + c * nb * 18, nb, in + r * k, flags);
+    const float* x = in;
+    float* xr = NULL;
+    if (flags & ORC_GEMM_BF16) {
+        xr = (float*)malloc(sizeof(float) * (size_t)(m * k));
+        for (int64_t i = 0; i < m * k; ++i) xr[i] = round_bf16(in[i]);
+        x = xr;
     }
+    float* xt = NULL;
+    if (m > 1) {
+        xt = (float*)malloc(sizeof(float) * (size_t)(m * k));
+        for (int64_t r = 0; r < m; ++r)
+            for (int64_t j = 0; j < k; ++j) xt[j * m + r] = x[r * k + j];
+    }
+#pragma omp parallel
+    {
+        float* wrow = (float*)malloc(sizeof(float) * (size_t)k);
+        float* acc = (float*)malloc(sizeof(float) * (size_t)(2 * m));
+#pragma omp for schedule(static)
+        for (int64_t c = 0; c < n; ++c) {
+            q4_row_dequant(w + c * nb * 18, nb, flags, wrow);
+            if (m == 1) {
+                out[c] = q4_row_dot(wrow, nb, x);
+            } else {
+                q4_rows_dot(wrow, nb, xt, m, acc, acc + m);
+                for (int64_t r = 0; r < m; ++r) out[r * n + c] = acc[r];
+            }
+        }
+        free(acc);
+        free(wrow);
+    }
+    free(xt);
+    free(xr);
 }
 
 /* ------------------------------------------------------------------ GGUF (gguf.rs:193-311) */
@@ -315,8 +375,6 @@ struct orc_stream {
     int32_t frame_count;
     uint32_t last_text_token;
     uint32_t delay_prev[2];
-    /* scratch */
-    float *x, *xn, *qkv, *attn, *tmp, *hid, *gate, *scores, *logits;
 };
 
 static const orc_tensor* find_t(const orc_tensor* ts, uint64_t n, const char* name) {
@@ -467,23 +525,14 @@ orc_stream* orc_stream_new(const orc_model* m, uint32_t flags) {
     const size_t kv = (size_t)m->cfg.num_layers * m->H * s->max_len * m->HD;
     s->k = (float*)calloc(kv, sizeof(float));
     s->v = (float*)calloc(kv, sizeof(float));
-    s->x = (float*)calloc((size_t)m->D, 4);
-    s->xn = (float*)calloc((size_t)m->D, 4);
-    s->qkv = (float*)calloc((size_t)3 * m->D, 4);
-    s->attn = (float*)calloc((size_t)m->D, 4);
-    s->tmp = (float*)calloc((size_t)m->D, 4);
-    s->hid = (float*)calloc((size_t)2 * m->F, 4);
-    s->gate = (float*)calloc((size_t)m->F, 4);
-    s->scores = (float*)calloc((size_t)s->max_len, 4);
-    s->logits = (float*)calloc((size_t)m->V, 4);
     orc_stream_reset(s);
     return s;
 }
 
 void orc_stream_free(orc_stream* s) {
     if (!s) return;
-    free(s->k); free(s->v); free(s->x); free(s->xn); free(s->qkv); free(s->attn); free(s->tmp);
-    free(s->hid); free(s->gate); free(s->scores); free(s->logits);
+    free(s->k);
+    free(s->v);
     free(s);
 }
 
@@ -548,111 +597,251 @@ static void rope_rotate(const orc_model* m, float* x, int32_t pos) {
 
 static float silu(float x) { return x * (1.0f / (1.0f + expf(-x))); }
 
-/* Q4TransformerBlock::forward_with_cache (model.rs:556-571) with Q4Attention (model.rs:426-474)
- * and Q4FeedForward (model.rs:517-524) for one layer. */
-static void block_forward(orc_stream* s, int l) {
+/* Attention of head h of one stream at layer l (model.rs:426-474): RoPE on q and k at the
+ * stream's position, the K/V ring write at write_pos (KVCache::update, model.rs:176-222), then
+ * softmax(q . k^T * scale) . v over the len + 1 valid slots (masks are no-ops at q_len == 1,
+ * model.rs:309-311, 338-340).  `scores` holds max_len floats. */
+static void head_attention(orc_stream* s, int l, int h, float* qkv, float* out, float* scores) {
     const orc_model* m = s->m;
-    const orc_layer* L = &m->layers[l];
-    const int32_t D = m->D, H = m->H, HD = m->HD, F = m->F, ML = s->max_len;
-    const uint32_t gf = s->flags & ORC_GEMM_BF16;
-    float* x = s->x;
-
-    rmsnorm(x, L->norm1, D, s->xn);
-    orc_q4_matmul(L->in_proj, 3 * D, D, s->xn, 1, s->qkv, gf);
-    float *q = s->qkv, *k = s->qkv + D, *v = s->qkv + 2 * D;
-    const int32_t offset = s->offset;
-    for (int h = 0; h < H; ++h) {
-        rope_rotate(m, q + h * HD, offset);
-        rope_rotate(m, k + h * HD, offset);
-    }
-    /* KVCache::update (model.rs:176-222): write at write_pos, advance the ring. */
-    const int32_t pos = s->write_pos;
-    for (int h = 0; h < H; ++h) {
-        float* kd = s->k + (((size_t)l * H + h) * ML + pos) * HD;
-        float* vd = s->v + (((size_t)l * H + h) * ML + pos) * HD;
-        for (int d = 0; d < HD; ++d) {
-            kd[d] = (s->flags & ORC_KV_BF16) ? round_bf16(k[h * HD + d]) : k[h * HD + d];
-            vd[d] = (s->flags & ORC_KV_BF16) ? round_bf16(v[h * HD + d]) : v[h * HD + d];
-        }
+    const int32_t D = m->D, H = m->H, HD = m->HD, ML = s->max_len;
+    float *q = qkv + h * HD, *k = qkv + D + h * HD, *v = qkv + 2 * D + h * HD;
+    rope_rotate(m, q, s->offset);
+    rope_rotate(m, k, s->offset);
+    float* kd = s->k + (((size_t)l * H + h) * ML + s->write_pos) * HD;
+    float* vd = s->v + (((size_t)l * H + h) * ML + s->write_pos) * HD;
+    for (int d = 0; d < HD; ++d) {
+        kd[d] = (s->flags & ORC_KV_BF16) ? round_bf16(k[d]) : k[d];
+        vd[d] = (s->flags & ORC_KV_BF16) ? round_bf16(v[d]) : v[d];
     }
     const int32_t len = s->len + 1 < ML ? s->len + 1 : ML;
-    /* scores = (q . k^T) * scale; softmax; attn . v   (model.rs:455-469; masks are no-ops at
-     * q_len == 1, model.rs:309-311, 338-340) */
-    for (int h = 0; h < H; ++h) {
-        const float* qh = q + h * HD;
-        const float* kb = s->k + ((size_t)l * H + h) * ML * HD;
-        const float* vb = s->v + ((size_t)l * H + h) * ML * HD;
-        float mx = -INFINITY;
-        for (int32_t j = 0; j < len; ++j) {
-            float dot = 0.0f;
-            for (int d = 0; d < HD; ++d) dot += qh[d] * kb[(size_t)j * HD + d];
-            s->scores[j] = dot * m->attn_scale;
-            if (s->scores[j] > mx) mx = s->scores[j];
-        }
-        float sum = 0.0f;
-        for (int32_t j = 0; j < len; ++j) { s->scores[j] = expf(s->scores[j] - mx); sum += s->scores[j]; }
-        for (int32_t j = 0; j < len; ++j) s->scores[j] = s->scores[j] / sum;
-        for (int d = 0; d < HD; ++d) {
-            float acc = 0.0f;
-            for (int32_t j = 0; j < len; ++j) acc += s->scores[j] * vb[(size_t)j * HD + d];
-            s->attn[h * HD + d] = acc;
-        }
+    const float* kb = s->k + ((size_t)l * H + h) * ML * HD;
+    const float* vb = s->v + ((size_t)l * H + h) * ML * HD;
+    float mx = -INFINITY;
+    for (int32_t j = 0; j < len; ++j) {
+        float dot = 0.0f;
+        for (int d = 0; d < HD; ++d) dot += q[d] * kb[(size_t)j * HD + d];
+        scores[j] = dot * m->attn_scale;
+        if (scores[j] > mx) mx = scores[j];
     }
-    orc_q4_matmul(L->out_proj, D, D, s->attn, 1, s->tmp, gf);
-    for (int32_t i = 0; i < D; ++i) x[i] = s->tmp[i] + x[i];
-
-    rmsnorm(x, L->norm2, D, s->xn);
-    orc_q4_matmul(L->lin_in, 2 * F, D, s->xn, 1, s->hid, gf);
-    for (int32_t i = 0; i < F; ++i) s->gate[i] = silu(s->hid[i]) * s->hid[F + i];
-    orc_q4_matmul(L->lin_out, D, F, s->gate, 1, s->tmp, gf);
-    for (int32_t i = 0; i < D; ++i) x[i] = s->tmp[i] + x[i];
+    float sum = 0.0f;
+    for (int32_t j = 0; j < len; ++j) { scores[j] = expf(scores[j] - mx); sum += scores[j]; }
+    for (int32_t j = 0; j < len; ++j) scores[j] = scores[j] / sum;
+    for (int d = 0; d < HD; ++d) {
+        float acc = 0.0f;
+        for (int32_t j = 0; j < len; ++j) acc += scores[j] * vb[(size_t)j * HD + d];
+        out[h * HD + d] = acc;
+    }
 }
 
-int64_t orc_forward(orc_stream* s, const uint32_t* audio, uint32_t text, float* logits) {
-    const orc_model* m = s->m;
-    if (s->offset + 1 > m->cfg.max_seq_len)
-        return set_err(-6, "position %d beyond the RoPE table (%d)", s->offset, m->cfg.max_seq_len);
-    for (int i = 0; i < m->cfg.num_codebooks; ++i)
-        if (audio[i] >= (uint32_t)m->AV) return set_err(-1, "audio token %u out of range", audio[i]);
-    if (text >= (uint32_t)m->TV) return set_err(-1, "text token %u out of range", text);
-    /* embedding sum on the CPU in codebook order, then the text row (model.rs:640-646) */
-    memset(s->x, 0, sizeof(float) * (size_t)m->D);
-    for (int i = 0; i < m->cfg.num_codebooks; ++i) embed_add(m, m->emb_audio[i], audio[i], s->x);
-    embed_add(m, m->emb_text, text, s->x);
-    for (int l = 0; l < m->cfg.num_layers; ++l) block_forward(s, l);
-    s->write_pos = (s->write_pos + 1) % s->max_len;
-    s->offset += 1;
-    s->len = s->len + 1 < s->max_len ? s->len + 1 : s->max_len;
-    rmsnorm(s->x, m->out_norm, m->D, s->xn);
-    orc_q4_matmul(m->head, m->V, m->D, s->xn, 1, s->logits, s->flags & ORC_GEMM_BF16);
-    if (logits) memcpy(logits, s->logits, sizeof(float) * (size_t)m->V);
+/* Scratch of one batched step over n streams: the stacked rows of every stream. */
+typedef struct {
+    float *x, *xn, *qkv, *attn, *tmp, *hid, *gate, *logits;
+} orc_batch;
+
+static int batch_alloc(orc_batch* b, const orc_model* m, int n) {
+    const size_t N = (size_t)n;
+    b->x = (float*)calloc(N * m->D, 4);
+    b->xn = (float*)calloc(N * m->D, 4);
+    b->qkv = (float*)calloc(N * 3 * m->D, 4);
+    b->attn = (float*)calloc(N * m->D, 4);
+    b->tmp = (float*)calloc(N * m->D, 4);
+    b->hid = (float*)calloc(N * 2 * m->F, 4);
+    b->gate = (float*)calloc(N * m->F, 4);
+    b->logits = (float*)calloc(N * m->V, 4);
+    return b->x && b->xn && b->qkv && b->attn && b->tmp && b->hid && b->gate && b->logits;
+}
+
+static void batch_free(orc_batch* b) {
+    free(b->x); free(b->xn); free(b->qkv); free(b->attn); free(b->tmp); free(b->hid); free(b->gate);
+    free(b->logits);
+}
+
+/* Q4TransformerBlock::forward_with_cache (model.rs:556-571) with Q4Attention (model.rs:426-474)
+ * and Q4FeedForward (model.rs:517-524) for one layer, over the stacked rows of n streams.  Each
+ * stream's arithmetic is that of a lone stream: the matmuls give every row the per-output order
+ * of orc_q4_matmul, and attention reads only the stream's own ring. */
+static void block_forward(orc_stream* const* ss, int n, int l, orc_batch* b) {
+    const orc_model* m = ss[0]->m;
+    const orc_layer* L = &m->layers[l];
+    const int32_t D = m->D, H = m->H, F = m->F;
+    const uint32_t gf = ss[0]->flags & ORC_GEMM_BF16;
+
+    for (int i = 0; i < n; ++i) rmsnorm(b->x + (size_t)i * D, L->norm1, D, b->xn + (size_t)i * D);
+    orc_q4_matmul(L->in_proj, 3 * D, D, b->xn, n, b->qkv, gf);
+#pragma omp parallel
+    {
+        float* scores = (float*)malloc(sizeof(float) * (size_t)ss[0]->max_len);
+#pragma omp for schedule(dynamic)
+        for (int t = 0; t < n * H; ++t) {
+            const int i = t / H, h = t % H;
+            head_attention(ss[i], l, h, b->qkv + (size_t)i * 3 * D, b->attn + (size_t)i * D, scores);
+        }
+        free(scores);
+    }
+    orc_q4_matmul(L->out_proj, D, D, b->attn, n, b->tmp, gf);
+    for (size_t i = 0; i < (size_t)n * D; ++i) b->x[i] = b->tmp[i] + b->x[i];
+
+    for (int i = 0; i < n; ++i) rmsnorm(b->x + (size_t)i * D, L->norm2, D, b->xn + (size_t)i * D);
+    orc_q4_matmul(L->lin_in, 2 * F, D, b->xn, n, b->hid, gf);
+    for (int i = 0; i < n; ++i) {
+        const float* hd = b->hid + (size_t)i * 2 * F;
+        float* g = b->gate + (size_t)i * F;
+        for (int32_t j = 0; j < F; ++j) g[j] = silu(hd[j]) * hd[F + j];
+    }
+    orc_q4_matmul(L->lin_out, D, F, b->gate, n, b->tmp, gf);
+    for (size_t i = 0; i < (size_t)n * D; ++i) b->x[i] = b->tmp[i] + b->x[i];
+}
+
+/* Checks the inputs of one batched step the way the reference would panic on them (nothing is
+ * changed when a check fails). */
+static int check_batch(orc_stream* const* ss, int n, const uint32_t* audio, const uint32_t* texts) {
+    if (n <= 0 || !ss) return set_err(-1, "need at least one stream");
+    const orc_model* m = ss[0]->m;
+    for (int i = 0; i < n; ++i) {
+        if (ss[i]->m != m || ss[i]->flags != ss[0]->flags) return set_err(-1, "streams of one batch share a model and flags");
+        for (int j = 0; j < i; ++j)
+            if (ss[j] == ss[i]) return set_err(-1, "stream repeated in one batch");
+        if (ss[i]->offset + 1 > m->cfg.max_seq_len)
+            return set_err(-6, "position %d beyond the RoPE table (%d)", ss[i]->offset, m->cfg.max_seq_len);
+        for (int c = 0; c < m->cfg.num_codebooks; ++c)
+            if (audio[(size_t)i * m->cfg.num_codebooks + c] >= (uint32_t)m->AV)
+                return set_err(-1, "audio token %u out of range", audio[(size_t)i * m->cfg.num_codebooks + c]);
+        if (texts[i] >= (uint32_t)m->TV) return set_err(-1, "text token %u out of range", texts[i]);
+    }
+    return 0;
+}
+
+static int64_t argmax_row(const float* lg, int32_t V) {
     int64_t best = 0;
-    for (int32_t i = 1; i < m->V; ++i)
-        if (s->logits[i] > s->logits[best]) best = i;
+    for (int32_t i = 1; i < V; ++i)
+        if (lg[i] > lg[best]) best = i;
     return best;
 }
 
-int64_t orc_feed_frame(orc_stream* s, const uint32_t* audio) {
-    const orc_config* c = &s->m->cfg;
-    /* submit_frame (stream.rs:90-107) */
-    s->frame_count += 1;
-    const int emits = s->frame_count >= c->text_delay;
-    int64_t tok = orc_forward(s, audio, s->last_text_token, NULL);
-    if (tok < 0) return tok - 100; /* keep errors below -1 */
-    const uint32_t token = (uint32_t)tok;
-    /* resolve_pending_as_token (stream.rs:231-266) */
-    if (emits) {
-        s->last_text_token = token;
-        return token;
+int orc_forward_batch(orc_stream* const* ss, int n, const uint32_t* audio, const uint32_t* texts, float* logits,
+                      int64_t* argmax) {
+    const int rc = check_batch(ss, n, audio, texts);
+    if (rc) return rc;
+    const orc_model* m = ss[0]->m;
+    const int32_t D = m->D, NC = m->cfg.num_codebooks;
+    orc_batch b;
+    if (!batch_alloc(&b, m, n)) { batch_free(&b); return set_err(-3, "out of memory"); }
+    /* embedding sum on the CPU in codebook order, then the text row (model.rs:640-646) */
+    for (int i = 0; i < n; ++i) {
+        float* x = b.x + (size_t)i * D;
+        for (int c = 0; c < NC; ++c) embed_add(m, m->emb_audio[c], audio[(size_t)i * NC + c], x);
+        embed_add(m, m->emb_text, texts[i], x);
     }
-    const uint32_t prev0 = s->delay_prev[0], prev1 = s->delay_prev[1];
-    s->delay_prev[0] = prev1;
-    s->delay_prev[1] = token;
-    if (token != c->text_padding_id && token != 0 && token == prev0 && token != prev1)
-        s->last_text_token = c->text_padding_id;
-    else
-        s->last_text_token = token;
-    return -1;
+    for (int l = 0; l < m->cfg.num_layers; ++l) block_forward(ss, n, l, &b);
+    for (int i = 0; i < n; ++i) {
+        orc_stream* s = ss[i];
+        s->write_pos = (s->write_pos + 1) % s->max_len;
+        s->offset += 1;
+        s->len = s->len + 1 < s->max_len ? s->len + 1 : s->max_len;
+        rmsnorm(b.x + (size_t)i * D, m->out_norm, D, b.xn + (size_t)i * D);
+    }
+    orc_q4_matmul(m->head, m->V, m->D, b.xn, n, b.logits, ss[0]->flags & ORC_GEMM_BF16);
+    for (int i = 0; i < n; ++i) {
+        const float* lg = b.logits + (size_t)i * m->V;
+        if (logits) memcpy(logits + (size_t)i * m->V, lg, sizeof(float) * (size_t)m->V);
+        argmax[i] = argmax_row(lg, m->V);
+    }
+    batch_free(&b);
+    return 0;
+}
+
+int64_t orc_forward(orc_stream* s, const uint32_t* audio, uint32_t text, float* logits) {
+    int64_t am = 0;
+    const int rc = orc_forward_batch(&s, 1, audio, &text, logits, &am);
+    return rc ? rc : am;
+}
+
+/* SttModel::forward_with_gpu_token (model.rs:675-722): the audio rows are summed on the CPU
+ * (embed_id_add_cpu into a zero vector), the text row comes either from the f32 table that
+ * dequant_embedding_to_gpu (gguf.rs:697-738) builds, selected by the previous argmax, or (no
+ * argmax yet) from embed_id_add_cpu into a second zero vector; the two vectors are then added.
+ * The rest of the step is SttModel::forward's. */
+int64_t orc_forward_gpu_token(orc_stream* s, const uint32_t* audio, int has_argmax, uint32_t argmax,
+                              uint32_t fallback_text, float* logits) {
+    const orc_model* m = s->m;
+    const uint32_t text = has_argmax ? argmax : fallback_text;
+    const int rc = check_batch(&s, 1, audio, &text);
+    if (rc) return rc;
+    const int32_t D = m->D, NC = m->cfg.num_codebooks;
+    orc_batch b;
+    if (!batch_alloc(&b, m, 1)) { batch_free(&b); return set_err(-3, "out of memory"); }
+    float* audio_sum = b.x;
+    for (int c = 0; c < NC; ++c) embed_add(m, m->emb_audio[c], audio[c], audio_sum);
+    float* text_in = (float*)calloc((size_t)D, 4);
+    if (has_argmax && m->emb_dtype == 2) {
+        /* dequant_embedding_to_gpu: data[j] = (nib - 8) * d, assigned (gguf.rs:725-732) */
+        const uint8_t* row = m->emb_text + (size_t)argmax * (D / 32) * 18;
+        for (int32_t blk = 0; blk < D / 32; ++blk) {
+            const uint8_t* bo = row + blk * 18;
+            const float d = orc_f16_to_f32_gguf((uint16_t)(bo[0] | (bo[1] << 8)));
+            for (int j = 0; j < 16; ++j) {
+                text_in[blk * 32 + j] = ((float)(bo[2 + j] & 0x0F) - 8.0f) * d;
+                text_in[blk * 32 + j + 16] = ((float)((bo[2 + j] >> 4) & 0x0F) - 8.0f) * d;
+            }
+        }
+    } else {
+        embed_add(m, m->emb_text, text, text_in);
+    }
+    for (int32_t j = 0; j < D; ++j) audio_sum[j] = audio_sum[j] + text_in[j];
+    free(text_in);
+    for (int l = 0; l < m->cfg.num_layers; ++l) block_forward(&s, 1, l, &b);
+    s->write_pos = (s->write_pos + 1) % s->max_len;
+    s->offset += 1;
+    s->len = s->len + 1 < s->max_len ? s->len + 1 : s->max_len;
+    rmsnorm(b.x, m->out_norm, D, b.xn);
+    orc_q4_matmul(m->head, m->V, m->D, b.xn, 1, b.logits, s->flags & ORC_GEMM_BF16);
+    if (logits) memcpy(logits, b.logits, sizeof(float) * (size_t)m->V);
+    const int64_t am = argmax_row(b.logits, m->V);
+    batch_free(&b);
+    return am;
+}
+
+/* SttStream::feed_frame (stream.rs:70-81) for n streams at once: submit_frame (stream.rs:90-107)
+ * with each stream's last_text_token, one batched step, then resolve_pending_as_token
+ * (stream.rs:231-266) per stream.  tokens[i] is the emitted token or -1 (None). */
+int orc_feed_frame_batch(orc_stream* const* ss, int n, const uint32_t* audio, float* logits, int64_t* tokens) {
+    if (n <= 0 || !ss) return set_err(-1, "need at least one stream");
+    uint32_t* texts = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)n);
+    int64_t* am = (int64_t*)malloc(sizeof(int64_t) * (size_t)n);
+    for (int i = 0; i < n; ++i) texts[i] = ss[i]->last_text_token;
+    const int rc = orc_forward_batch(ss, n, audio, texts, logits, am);
+    if (rc == 0) {
+        for (int i = 0; i < n; ++i) {
+            orc_stream* s = ss[i];
+            const orc_config* c = &s->m->cfg;
+            s->frame_count += 1;
+            const int emits = s->frame_count >= c->text_delay;
+            const uint32_t token = (uint32_t)am[i];
+            if (emits) {
+                s->last_text_token = token;
+                tokens[i] = token;
+                continue;
+            }
+            const uint32_t prev0 = s->delay_prev[0], prev1 = s->delay_prev[1];
+            s->delay_prev[0] = prev1;
+            s->delay_prev[1] = token;
+            if (token != c->text_padding_id && token != 0 && token == prev0 && token != prev1)
+                s->last_text_token = c->text_padding_id;
+            else
+                s->last_text_token = token;
+            tokens[i] = -1;
+        }
+    }
+    free(texts);
+    free(am);
+    return rc;
+}
+
+int64_t orc_feed_frame(orc_stream* s, const uint32_t* audio) {
+    int64_t tok = 0;
+    const int rc = orc_feed_frame_batch(&s, 1, audio, NULL, &tok);
+    if (rc) return rc - 100; /* keep errors below -1 */
+    return tok;
 }
 
 int orc_flush(orc_stream* s, uint32_t* tokens, int capacity) {

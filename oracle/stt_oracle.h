@@ -64,9 +64,24 @@ void orc_stream_reset(orc_stream* s);
 /* SttModel::forward (model.rs:631-664): one step; logits (vocab floats) may be NULL; returns
  * the argmax (lowest index on ties) or a negative error. */
 int64_t orc_forward(orc_stream* s, const uint32_t* audio, uint32_t text, float* logits);
+/* orc_forward for n distinct streams of one model (same flags) in one step: audio holds
+ * n * num_codebooks ids, texts n ids; logits (n * vocab) may be NULL; argmax receives n values.
+ * Each stream gets exactly the values orc_forward would give it alone.  Returns 0 or a negative
+ * error (then no stream has changed). */
+int orc_forward_batch(orc_stream* const* ss, int n, const uint32_t* audio, const uint32_t* texts,
+                      float* logits, int64_t* argmax);
+/* SttModel::forward_with_gpu_token (model.rs:675-722): the audio sum, then the text row taken
+ * from the dequantised f32 table by the previous argmax (has_argmax != 0) or built on the CPU
+ * from fallback_text, added to it.  Returns the argmax or a negative error. */
+int64_t orc_forward_gpu_token(orc_stream* s, const uint32_t* audio, int has_argmax, uint32_t argmax,
+                              uint32_t fallback_text, float* logits);
 /* SttStream::feed_frame (stream.rs:70-81, 90-107, 231-266).  Returns the emitted token,
  * -1 for None, or < -1 on error. */
 int64_t orc_feed_frame(orc_stream* s, const uint32_t* audio);
+/* feed_frame for n distinct streams in one batched step; logits (n * vocab) may be NULL;
+ * tokens[i] receives the emitted token or -1.  Returns 0 or a negative error. */
+int orc_feed_frame_batch(orc_stream* const* ss, int n, const uint32_t* audio, float* logits,
+                         int64_t* tokens);
 /* SttStream::flush (stream.rs:315-338); returns the number of tokens written. */
 int orc_flush(orc_stream* s, uint32_t* tokens, int capacity);
 /* State: offset, len, write_pos, frame_count, last_text_token, delay_prev0, delay_prev1. */

@@ -517,6 +517,7 @@ struct stt_streams {
     void* d_scratch = nullptr;
     cudaStream_t stream = nullptr;
     std::map<int, cudaGraphExec_t> graphs;
+    std::map<int, int> graph_kernels;  // kernel nodes of each captured step graph
     MegaState mega;
 };
 
@@ -650,6 +651,13 @@ int graph_for(stt_streams* s, int n, cudaGraphExec_t* out) {
         return rc;
     }
     CUDA_TRY(e);
+    size_t nodes = 0;
+    e = cudaGraphGetNodes(graph, nullptr, &nodes);
+    if (e != cudaSuccess) {
+        cudaGraphDestroy(graph);
+        CUDA_TRY(e);
+    }
+    s->graph_kernels[n] = (int)nodes;
     cudaGraphExec_t exec;
     e = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
@@ -1149,8 +1157,12 @@ void* g_noalloc_addr[kNoAllocMaxDevices] = {};
 extern "C" int stt_q4_matmul_device_noalloc(const stt_q4_tensor* t, const void* d_in, int in_dtype, int rows,
                                             int splits, float* d_out, void* cuda_stream) {
     clear_error();
-    if (!t || !d_in || !d_out || rows < 0 || (in_dtype != 0 && in_dtype != 1))
-        return set_error(STT_E_INVALID_ARG, "bad arguments");
+    if (!t || !d_in || !d_out || rows < 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    if (in_dtype == 2)
+        return set_error(STT_E_INVALID_ARG,
+                         "in_dtype 2 (f16, the tensor-core product) is not available without allocation: "
+                         "use in_dtype 0 (f32) or 1 (bf16)");
+    if (in_dtype != 0 && in_dtype != 1) return set_error(STT_E_INVALID_ARG, "in_dtype %d unknown", in_dtype);
     const int NB = t->w.k / 32;
     if (splits < 1 || splits > kNoAllocMaxSplits || splits > NB)
         return set_error(STT_E_INVALID_ARG, "splits %d out of range [1, %d]", splits, std::min(kNoAllocMaxSplits, NB));
@@ -1255,6 +1267,61 @@ extern "C" int stt_debug_get_trace_ctas(stt_streams* s, uint64_t* out, int cap, 
     *n_ctas = s->m->num_sms;
     *n_slots = kTraceSlots;
     return STT_OK;
+}
+
+extern "C" int stt_debug_arm_wait_timeout(stt_streams* s) {
+    clear_error();
+    if (!s) return set_error(STT_E_INVALID_ARG, "NULL streams");
+    s->mega.stall_next = 1;
+    return STT_OK;
+}
+
+extern "C" int stt_debug_graph_kernels(stt_streams* s, int n, int* kernels) {
+    clear_error();
+    if (!s || !kernels || n <= 1 || n > s->S) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    DeviceScope ds(s->m->device);
+    cudaGraphExec_t exec;
+    TRY(graph_for(s, n, &exec));
+    *kernels = s->graph_kernels[n];
+    return STT_OK;
+}
+
+extern "C" int stt_debug_time_products(stt_streams* s, int n, int iters, double* us_out, double* flops_out) {
+    clear_error();
+    if (!s || !us_out || n < kTcMinBatch || n > s->S || iters <= 0) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    stt_model* m = s->m;
+    if (!m->tc_ok) return set_error(STT_E_INVALID_ARG, "the model's products do not run on the tensor cores");
+    DeviceScope ds(m->device);
+    cudaEvent_t a, b;
+    CUDA_TRY(cudaEventCreate(&a));
+    if (cudaEventCreate(&b) != cudaSuccess) {
+        cudaEventDestroy(a);
+        return set_error(STT_E_CUDA, "cudaEventCreate failed");
+    }
+    int rc = STT_OK;
+    const int which[5] = {0, 1, 2, 3, 4 * m->L};  // layer 0's four products, then the head
+    for (int i = 0; i < 5 && rc == STT_OK; ++i) {
+        const TcWeight& tw = m->tc_w[which[i]];
+        int slices = 0;
+        float ms = 0.0f;
+        cudaError_t e = launch_tc_product(tw, s->d_x16, n, s->d_tc_part, &s->d_desc->error, m->num_sms, &slices,
+                                          s->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(a, s->stream);
+        for (int t = 0; t < iters && e == cudaSuccess; ++t)
+            e = launch_tc_product(tw, s->d_x16, n, s->d_tc_part, &s->d_desc->error, m->num_sms, &slices, s->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(b, s->stream);
+        if (e == cudaSuccess) e = cudaEventSynchronize(b);
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+        if (e != cudaSuccess) {
+            rc = set_error(STT_E_CUDA, "timing product %d: %s", i, cudaGetErrorString(e));
+            break;
+        }
+        us_out[i] = (double)ms * 1000.0 / iters;
+        if (flops_out) flops_out[i] = 2.0 * n * (double)tw.n * (double)tw.k;
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return rc;
 }
 
 extern "C" int stt_debug_barrier_ns(int device, int iters, int mode, double* ns) {

@@ -85,6 +85,7 @@ struct MegaArgs {
     int32_t trace_cap;
     unsigned long long* tctas;  // optional: [cta][slot] %globaltimer of every CTA's marks
     int32_t tslots;
+    int32_t stall_test;    // test of the bounded waits: frame 0 waits for an epoch nobody writes
 };
 
 struct Smem {
@@ -1395,7 +1396,12 @@ __device__ __noinline__ void consumers(const MegaArgs& P, int cta) {
             {
                 const int n = phase_segs(sm, P, p0 + K_OUT, cta);
                 if (n > 0) {
-                    ok = prep_any(P, P.attb[par], E + (uint32_t)(p0 + K_ATT), c.D, nullptr, rb, 0, nullptr, 0, 0, 0) && ok;
+                    // stall_test: in frame 0 of a launch, layer 0's out_proj input is awaited at an
+                    // epoch that no phase publishes, so the bounded wait runs out and the launch ends
+                    // through the same abort path as a real timeout
+                    const uint32_t ep_att = E + (uint32_t)(p0 + K_ATT);
+                    const uint32_t ep_wait = (P.stall_test && f == 0 && l == 0) ? (ep_att ^ 0x80000000u) : ep_att;
+                    ok = prep_any(P, P.attb[par], ep_wait, c.D, nullptr, rb, 0, nullptr, 0, 0, 0) && ok;
                     trace_mark(P, 31, lslot(l, 7));
                     ok = gemv_phase<EPI_RESID>(P, p0 + K_OUT, seg, P.xb[par][0], E + (uint32_t)(p0 + K_OUT), f) && ok;
                     trace_mark(P, 32, lslot(l, 8));
@@ -1723,6 +1729,8 @@ cudaError_t launch_mega_steps(MegaState& ms, const Ctx& c, const LayerDev* h_lay
     P.trace_cap = 0;
     P.tctas = nullptr;
     P.tslots = 0;
+    P.stall_test = ms.stall_next;
+    ms.stall_next = 0;
     if (ms.trace && ms.trace_frame >= 0) {
         P.trace = ms.trace;
         P.trace_frame = ms.trace_frame;

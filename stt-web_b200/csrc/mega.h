@@ -14,6 +14,7 @@ struct MegaState {
     int trace_cap = 0;
     unsigned long long* trace_ctas = nullptr;  // [num_sms][trace_slots] %globaltimer per CTA
     int trace_slots = 0;
+    int stall_next = 0;  // the next launch runs the bounded-wait test (one launch only)
 };
 
 // Trace slots per CTA of one frame: 1 + 16 per layer + 4 (layers <= 32).

@@ -20,7 +20,22 @@
 #include <thread>
 #include <vector>
 
+#include "../../include/stt_synth.h"
 #include "common.h"
+
+namespace {
+thread_local std::string g_synth_error;
+
+int synth_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_synth_error = buf;
+    return code;
+}
+}  // namespace
 
 namespace stt {
 namespace {
@@ -187,7 +202,7 @@ extern "C" void stt_synth_default(stt_synth_params* p) {
 }
 
 extern "C" int stt_synth_quantize_q4_0(const float* x, size_t n, uint8_t* out) {
-    if (!x || !out || n % 32 != 0) return set_error(STT_E_INVALID_ARG, "quantize: n %% 32 != 0 or NULL");
+    if (!x || !out || n % 32 != 0) return synth_error(STT_E_INVALID_ARG, "quantize: n %% 32 != 0 or NULL");
     for (size_t b = 0; b < n / 32; ++b) quantize_block(x + b * 32, out + b * 18);
     return STT_OK;
 }
@@ -195,7 +210,7 @@ extern "C" int stt_synth_quantize_q4_0(const float* x, size_t n, uint8_t* out) {
 extern "C" int stt_synth_audio_tokens(uint64_t seed, int32_t stream, int32_t first_frame,
                                       int32_t n_frames, int32_t num_codebooks, uint32_t* out) {
     if (!out || n_frames < 0 || num_codebooks <= 0 || first_frame < 0)
-        return set_error(STT_E_INVALID_ARG, "audio_tokens: bad arguments");
+        return synth_error(STT_E_INVALID_ARG, "audio_tokens: bad arguments");
     const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32) ^ 0x80000000u ^ (uint32_t)stream};
     for (int32_t f = 0; f < n_frames; ++f) {
         for (int32_t g = 0; g < (num_codebooks + 3) / 4; ++g) {
@@ -210,17 +225,17 @@ extern "C" int stt_synth_audio_tokens(uint64_t seed, int32_t stream, int32_t fir
 }
 
 extern "C" int stt_synth_gguf(const stt_synth_params* p_in, uint8_t** out_buf, size_t* out_len) {
-    clear_error();
-    if (!out_buf || !out_len) return set_error(STT_E_INVALID_ARG, "synth: NULL output");
+    g_synth_error.clear();
+    if (!out_buf || !out_len) return synth_error(STT_E_INVALID_ARG, "synth: NULL output");
     stt_synth_params p;
     if (p_in) p = *p_in; else stt_synth_default(&p);
     const uint64_t D = (uint64_t)p.hidden_size, F = (uint64_t)p.ffn_hidden;
     if (p.num_layers <= 0 || D == 0 || D % 32 || F % 32 || p.num_heads <= 0 || p.vocab_size <= 0 ||
         p.text_in_vocab_size <= 0 || p.num_codebooks <= 0 || p.audio_vocab_size <= 0)
-        return set_error(STT_E_INVALID_ARG, "synth: bad dimensions");
+        return synth_error(STT_E_INVALID_ARG, "synth: bad dimensions");
     const uint32_t edt = (uint32_t)p.embedding_dtype;
     if (edt != GGML_BF16 && edt != GGML_Q4_0 && edt != GGML_F32)
-        return set_error(STT_E_INVALID_ARG, "synth: embedding dtype must be 30, 2 or 0");
+        return synth_error(STT_E_INVALID_ARG, "synth: embedding dtype must be 30, 2 or 0");
 
     std::vector<TensorSpec> ts;
     const float ws = p.weight_std;
@@ -283,7 +298,7 @@ extern "C" int stt_synth_gguf(const stt_synth_params* p_in, uint8_t** out_buf, s
     while (hdr.size() % 32) hdr.push_back(0);
     const size_t total = hdr.size() + off;
     uint8_t* buf = (uint8_t*)std::malloc(total);
-    if (!buf) return set_error(STT_E_OOM, "synth: cannot allocate %zu bytes", total);
+    if (!buf) return synth_error(STT_E_OOM, "synth: cannot allocate %zu bytes", total);
     std::memcpy(buf, hdr.data(), hdr.size());
     uint8_t* data = buf + hdr.size();
 
@@ -317,3 +332,5 @@ extern "C" int stt_synth_gguf(const stt_synth_params* p_in, uint8_t** out_buf, s
 }
 
 extern "C" void stt_synth_free(uint8_t* buf) { std::free(buf); }
+
+extern "C" const char* stt_synth_last_error(void) { return g_synth_error.c_str(); }

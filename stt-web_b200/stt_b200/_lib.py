@@ -76,25 +76,6 @@ class stt_stream_state(C.Structure):
     ]
 
 
-class stt_synth_params(C.Structure):
-    _fields_ = [
-        ("seed", C.c_uint64),
-        ("num_layers", C.c_int32),
-        ("hidden_size", C.c_int32),
-        ("num_heads", C.c_int32),
-        ("ffn_hidden", C.c_int32),
-        ("vocab_size", C.c_int32),
-        ("text_in_vocab_size", C.c_int32),
-        ("num_codebooks", C.c_int32),
-        ("audio_vocab_size", C.c_int32),
-        ("embedding_dtype", C.c_int32),
-        ("weight_std", C.c_float),
-        ("norm_mean", C.c_float),
-        ("norm_std", C.c_float),
-        ("n_threads", C.c_int32),
-    ]
-
-
 P = C.c_void_p
 U8P = C.POINTER(C.c_uint8)
 U32P = C.POINTER(C.c_uint32)
@@ -127,11 +108,6 @@ SIGNATURES = {
     "stt_q4_matmul_device": (C.c_int, [P, P, C.c_int, C.c_int, P, P]),
     "stt_q4_tensor_dequant": (C.c_int, [P, F32P]),
     "stt_q4_matmul_device_noalloc": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, P, P]),
-    "stt_synth_default": (None, [C.POINTER(stt_synth_params)]),
-    "stt_synth_gguf": (C.c_int, [C.POINTER(stt_synth_params), C.POINTER(U8P), C.POINTER(C.c_size_t)]),
-    "stt_synth_free": (None, [U8P]),
-    "stt_synth_quantize_q4_0": (C.c_int, [F32P, C.c_size_t, U8P]),
-    "stt_synth_audio_tokens": (C.c_int, [C.c_uint64, C.c_int32, C.c_int32, C.c_int32, C.c_int32, U32P]),
     "stt_spm_decoder_create": (C.c_int, [U8P, C.c_size_t, C.POINTER(P)]),
     "stt_spm_decoder_destroy": (C.c_int, [P]),
     "stt_spm_vocab_len": (C.c_int, [P, C.POINTER(C.c_int64)]),
@@ -141,6 +117,9 @@ SIGNATURES = {
     "stt_debug_get_trace": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int, I32P]),
     "stt_debug_get_trace_ctas": (C.c_int, [P, C.POINTER(C.c_uint64), C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "stt_debug_barrier_ns": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]),
+    "stt_debug_graph_kernels": (C.c_int, [P, C.c_int, C.POINTER(C.c_int)]),
+    "stt_debug_arm_wait_timeout": (C.c_int, [P]),
+    "stt_debug_time_products": (C.c_int, [P, C.c_int, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "stt_last_error": (C.c_char_p, []),
 }
 

@@ -1,9 +1,9 @@
 """Generates the committed golden fixtures of tests/golden/ from the stt-web reference.
 
-Run in a container where the reference checkout is readable (default /root/reference, or the
-STT_WEB_REFERENCE environment variable):
+Run where a checkout of the stt-web reference is readable, naming its root either as the first
+argument or in the STT_WEB_REFERENCE environment variable:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <path of the stt-web checkout>
 
 Fixtures written (all small):
   q4_quantize.npz     inputs and the bytes scripts/quantize.py:quantize_q4_0 produces for them
@@ -26,11 +26,18 @@ import tempfile
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("STT_WEB_REFERENCE", "/root/reference")
+
+
+def reference_root() -> str:
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("STT_WEB_REFERENCE")
+    if not root or not os.path.isfile(os.path.join(root, "scripts", "quantize.py")):
+        sys.exit("usage: make_golden.py <stt-web checkout> (or set STT_WEB_REFERENCE); "
+                 "the checkout must hold scripts/quantize.py")
+    return root
 
 
 def ref_quantize_module():
-    sys.path.insert(0, os.path.join(REF, "scripts"))
+    sys.path.insert(0, os.path.join(reference_root(), "scripts"))
     import quantize  # noqa: E402  (the reference's script, imported unmodified)
     return quantize
 

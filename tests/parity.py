@@ -1,0 +1,64 @@
+"""Token parity bookkeeping shared by the GPU tests.
+
+The GPU and the oracle compute the same f32 step in different summation orders, and with bf16 K/V
+a last-bit difference can move a K or V element across a bf16 rounding boundary.  Their logits
+therefore agree to about 1e-5 .. 1e-4, and an argmax can only differ where the oracle's top two
+logits are closer than that.  A Follower compares the GPU's tokens with the oracle's, stream by
+stream and frame by frame:
+
+  - equal tokens: counted;
+  - different tokens where the oracle's top-2 margin is below EXEMPT_MARGIN: a near-tie flip.  It
+    is counted as an exemption and the oracle stream takes the GPU's token as its next text token
+    (what feed_frame does with the token it emitted), so both sides decode the same frames from
+    then on and the comparison continues;
+  - any other difference: the test fails.
+
+Every test prints compared / near-tie / exemption counts; near-ties are comparisons with a margin
+below 5e-2, the bound the earlier tensor-core tests exempted wholesale."""
+from __future__ import annotations
+
+import numpy as np
+
+from oracle import oracle as O
+
+EXEMPT_MARGIN = 2e-3
+NEAR = 5e-2
+
+
+def margins(lg):
+    s = np.sort(np.atleast_2d(lg), axis=1)
+    return s[:, -1] - s[:, -2]
+
+
+class Follower:
+    def __init__(self, refs, text_delay=6):
+        self.refs = list(refs)
+        self.text_delay = text_delay
+        self.compared = self.near = self.exempt = 0
+        self.exemptions = []
+
+    def step(self, idx, audio, got, where=""):
+        """One feed_frame of the oracle streams refs[i] for i in idx (audio rows in that order);
+        `got` holds the GPU's emitted tokens in the same order (-1 or None = None)."""
+        streams = [self.refs[i] for i in idx]
+        exp, lg = O.feed_frame_batch(streams, np.asarray(audio).reshape(len(idx), -1), want_logits=True)
+        mg = margins(lg)
+        for j, i in enumerate(idx):
+            g = got[j]
+            g = None if g is None or int(g) < 0 else int(g)
+            self.compared += 1
+            self.near += int(mg[j] < NEAR)
+            if g == exp[j]:
+                continue
+            if g is not None and exp[j] is not None and mg[j] < EXEMPT_MARGIN:
+                self.exempt += 1
+                self.exemptions.append((i, where, float(mg[j])))
+                self.refs[i].set_last_text_token(g)
+                continue
+            raise AssertionError(f"{where} stream {i}: token {g} != oracle {exp[j]} "
+                                 f"(oracle top-2 margin {mg[j]:.3g})")
+        return exp, lg
+
+    def report(self, name):
+        return (f"{name}: {self.compared} token comparisons, oracle near-ties (margin < {NEAR}) {self.near}, "
+                f"exemptions (margin < {EXEMPT_MARGIN}) {self.exempt} {self.exemptions[:8]}")

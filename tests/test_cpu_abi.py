@@ -3,6 +3,7 @@
 import ctypes as C
 import os
 import re
+import subprocess
 
 import numpy as np
 import pytest
@@ -14,8 +15,8 @@ from stt_b200 import _lib
 from stt_b200.model import SttConfig
 
 
-def header_functions():
-    text = open(os.path.join(REPO, "include", "stt_b200.h")).read()
+def header_functions(header="stt_b200.h"):
+    text = open(os.path.join(REPO, "include", header)).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(stt_[a-z0-9_]+)\s*\(", text)))
 
@@ -27,6 +28,21 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(L, n), n
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_generator_library_is_separate_from_the_decode_library():
+    """The synthetic-checkpoint generator lives in its own host-only library: the decode library
+    neither exports it nor needs it, and the generator library has no CUDA dependency."""
+    from stt_b200 import synth
+    S = synth.synth_lib()
+    names = header_functions("stt_synth.h")
+    assert len(names) == 6
+    for n in names:
+        assert hasattr(S, n), n
+        assert n in synth.SYNTH_SIGNATURES, f"{n} has no ctypes signature"
+        assert not hasattr(_lib.lib(), n), f"{n} is exported by the decode library"
+    needed = subprocess.run(["readelf", "-d", synth.SYNTH_LIB_PATH], capture_output=True, text=True).stdout
+    assert "cuda" not in needed.lower()
 
 
 def test_oracle_is_not_linked_into_the_library():

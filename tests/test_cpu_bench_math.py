@@ -47,8 +47,37 @@ def test_bytes_per_batched_step(bench):
     assert bench.algorithmic_bytes_batched([2000], 0, 1) == bench.WEIGHT_BYTES + (751 + 1) * 131_072 + bench.EMB_BYTES
 
 
-def test_mma_flops(bench):
-    # three MMAs per product over the batch rows padded to the tile (64 -> 64, 100 -> 128, 300 -> 512)
-    assert bench.mma_flops_batched(64) == 3 * 2 * 64 * bench.Q4_PARAMS
-    assert bench.mma_flops_batched(100) == 3 * 2 * 128 * bench.Q4_PARAMS
-    assert bench.mma_flops_batched(300) == 3 * 2 * 512 * bench.Q4_PARAMS
+def test_both_arms_describe_one_workload(bench):
+    # the GPU arm and the reference arm print the same config object for a given GPU count
+    for n in (1, 2, 4, 8):
+        c = bench.job_config(n)
+        assert c == bench.job_config(n)
+        assert c["streams"] == 512 and c["frames_per_stream"] == 250
+        assert f"{512 // n} streams" in c["parallelism"]
+
+
+def test_reference_arm_loads_no_decode_library(tmp_path):
+    """--impl reference runs the oracle on a bounded sample of the job and maps no library of the
+    decode path (the synthetic checkpoint comes from the separate generator library)."""
+    import json
+    import subprocess
+    import sys
+    env = dict(os.environ, OMP_NUM_THREADS="1")   # as torchrun sets it: the arm must override it
+    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "0"], capture_output=True, text=True, env=env, timeout=600, check=True).stdout
+    line = json.loads(out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["steps"] == 1 and line["warmup"] == 0
+    assert line["config"] == json.loads(json.dumps(_bench_module().job_config(1)))
+    assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0)) > 0
+    libs = line["libraries"]
+    assert "oracle/liboracle.so" in libs
+    assert not any("libsttb200" in x for x in libs), libs
+    # the timed steps fit the run: ms_per_step x steps is the sample's own time
+    assert 0 < line["ms_per_step"] < 600_000
+
+
+def _bench_module():
+    spec = importlib.util.spec_from_file_location("bench_under_test2", os.path.join(REPO, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod

@@ -333,3 +333,33 @@ def test_tensor_core_and_gemv_batches_agree(monkeypatch):
         cache.close()
     monkeypatch.delenv("STT_DISABLE_TC")
     assert np.abs(outs[0][1] - outs[1][1]).max() < LOGIT_TOL
+
+
+def test_bounded_wait_runs_out_and_the_next_call_recovers():
+    """A persistent-kernel wait that nothing will satisfy gives up after its limit: the call returns
+    STT_E_DEVICE_FLAG within seconds instead of hanging, and the stream set stays usable: after a
+    reset the same frames decode exactly as the oracle's."""
+    import ctypes as C
+    import time
+    from stt_b200._lib import lib, STT_E_DEVICE_FLAG
+    spec = stt_b200.SynthSpec(seed=25, num_layers=2, hidden_size=256, num_heads=2, ffn_hidden=512, vocab_size=1000,
+                              text_in_vocab_size=1001, num_codebooks=4, audio_vocab_size=300)
+    g = stt_b200.synth_gguf(spec)
+    cfg = tiny_cfg()
+    model = stt_b200.SttModel.from_shards([g.array], config=cfg)
+    cache = model.create_cache(1, "bf16")
+    st = stt_b200.SttStream(cfg, cache)
+    frames = np.random.default_rng(6).integers(0, 300, (10, 4))
+    assert lib().stt_debug_arm_wait_timeout(cache._h) == 0
+    t0 = time.perf_counter()
+    with pytest.raises(stt_b200.SttError) as e:
+        st.feed_frames(frames[:3])
+    took = time.perf_counter() - t0
+    assert e.value.code == STT_E_DEVICE_FLAG, e.value
+    assert took < 30.0, took
+    assert cache.state(0)["offset"] == 0          # the failed frame changed no stream state
+    st.reset()
+    ref = oracle_for(g.array, cfg).stream(O.KV_BF16)
+    assert st.feed_frames(frames) == [ref.feed_frame(f) for f in frames]
+    # the hook was one-shot: a second call runs normally too
+    assert st.feed_frame(frames[0]) == ref.feed_frame(frames[0])

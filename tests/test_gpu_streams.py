@@ -1,0 +1,144 @@
+"""Stream semantics at scale on the GPU: the batched feed_frame (stream.rs:70-107, 231-266) for many
+streams at once, through the host-buffer call and the device-buffer call that the multi-stream
+benchmarks time, against the oracle stream by stream; with the text delay, the limit-cycle rule
+actually firing, flush (stream.rs:315-338) and both resets (stream.rs:341-362) per stream.
+
+Tokens must be identical.  Every comparison also records the oracle's top-2 logit margin: a token
+that differs where the margin is below 5e-2 would be a near-tie flip; the count of such
+exemptions is printed and must be zero on these seeds (no comparison is skipped)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+import stt_b200
+from stt_b200._lib import check, lib
+from stt_b200.model import SttConfig
+
+pytestmark = pytest.mark.gpu
+
+TIE = 5e-2
+V = 16   # a small vocabulary, so that the limit-cycle rule fires during the delay
+
+
+def small_model(seed=31):
+    spec = stt_b200.SynthSpec(seed=seed, num_layers=2, hidden_size=256, num_heads=2, ffn_hidden=512, vocab_size=V,
+                              text_in_vocab_size=V + 1, num_codebooks=4, audio_vocab_size=300, weight_std=0.2)
+    g = stt_b200.synth_gguf(spec)
+    cfg = SttConfig(num_layers=2, hidden_size=256, num_heads=2, num_kv_heads=2, num_codebooks=4, vocab_size=V,
+                    text_in_vocab_size=V + 1, audio_vocab_size=300, text_start_token=V, sliding_window=12)
+    model = stt_b200.SttModel.from_shards([g.array], config=cfg)
+    om = O.OracleModel(g.array, num_layers=2, num_heads=2, num_codebooks=4, text_start_token=V, sliding_window=12)
+    return g, cfg, model, om
+
+
+def margins(lg):
+    s = np.sort(lg, axis=1)
+    return s[:, -1] - s[:, -2]
+
+
+class Tally:
+    """Counts comparisons, near-ties among them and mismatches at near-ties (exemptions)."""
+
+    def __init__(self):
+        self.compared = self.near = self.exempt = 0
+
+    def check(self, got, exp, margin, where):
+        self.compared += 1
+        near = margin < TIE
+        self.near += int(near)
+        if got != exp:
+            self.exempt += int(near)
+            raise AssertionError(f"{where}: token {got} != oracle {exp} (oracle top-2 margin {margin:.3g})")
+
+
+def device_feed(cache, ids, audio):
+    """stt_streams_feed_frame_device with torch device buffers; returns the tokens (-1 = None)."""
+    import torch
+    n = len(ids)
+    da = torch.from_numpy(np.ascontiguousarray(audio, dtype=np.int32).reshape(n, -1)).cuda()
+    dt = torch.empty(n, dtype=torch.int32, device="cuda")
+    cids = (C.c_int32 * n)(*ids)
+    ts = torch.cuda.current_stream()
+    check(lib().stt_streams_feed_frame_device(cache._h, cids, n, C.c_void_p(da.data_ptr()), C.c_void_p(dt.data_ptr()),
+                                              C.c_void_p(ts.cuda_stream)), "stt_streams_feed_frame_device")
+    torch.cuda.synchronize()
+    return dt.cpu().numpy()
+
+
+def limit_cycles(refs, tokens_before, argmax, pad=3):
+    """How many streams had the limit-cycle rule replace their token this frame (stream.rs:240-262):
+    during the delay, the next text token is the pad id although the argmax was not."""
+    return sum(1 for r, a in zip(refs, argmax) if r.state()["last_text_token"] == pad and a != pad
+               and r.state()["frame_count"] < 6)
+
+
+@pytest.mark.parametrize("path", ["host", "device"])
+def test_batched_feed_frame_matches_oracle_per_stream(path):
+    g, cfg, model, om = small_model()
+    n = 24
+    cache = model.create_cache(n, "bf16")
+    refs = [om.stream(O.KV_BF16) for _ in range(n)]
+    rng = np.random.default_rng(7)
+    tally = Tally()
+    fired = 0
+    order = list(rng.permutation(n))          # batch rows in a different order than stream ids
+    for f in range(14):                       # through the delay (frames 1..5 emit nothing) and past it
+        audio = rng.integers(0, 300, (n, 4))
+        exp, lg = O.feed_frame_batch([refs[s] for s in order], audio, want_logits=True)
+        am = np.argmax(lg, axis=1)
+        fired += limit_cycles([refs[s] for s in order], None, am)
+        got = cache.feed_frame(order, audio) if path == "host" else device_feed(cache, order, audio)
+        mg = margins(lg)
+        for i, s in enumerate(order):
+            tally.check(None if got[i] < 0 else int(got[i]), exp[i], mg[i], f"frame {f} stream {s}")
+            st, rs = cache.state(s), refs[s].state()
+            assert (st["offset"], st["frame_count"], st["last_text_token"]) == \
+                   (rs["offset"], rs["frame_count"], rs["last_text_token"]), (f, s)
+            assert st["delay_prev"] == (rs["prev0"] & 0xFFFFFFFF, rs["prev1"] & 0xFFFFFFFF), (f, s)
+    print(f"compared {tally.compared}, near-ties {tally.near}, exemptions {tally.exempt}, limit cycles {fired}")
+    assert fired > 0, "the limit-cycle rule never fired on this seed"
+    assert tally.exempt == 0
+
+    # flush then both resets, per stream, interleaved with batched steps of the others
+    cfg_s = cfg
+    for s in (0, 5, 17):
+        assert stt_b200.SttStream(cfg_s, cache, s).flush() == refs[s].flush()
+    stt_b200.SttStream(cfg_s, cache, 5).reset()
+    refs[5].reset()
+    stt_b200.SttStream(cfg_s, cache, 17).reset_keep_buffers()
+    refs[17].reset()
+    stt_b200.SttStream(cfg_s, cache, 9).set_last_text_token(4)
+    refs[9].set_last_text_token(4)
+    for f in range(9):
+        audio = rng.integers(0, 300, (n, 4))
+        exp, lg = O.feed_frame_batch(refs, audio, want_logits=True)
+        got = cache.feed_frame(list(range(n)), audio) if path == "host" else device_feed(cache, list(range(n)), audio)
+        mg = margins(lg)
+        for s in range(n):
+            tally.check(None if got[s] < 0 else int(got[s]), exp[s], mg[s], f"after resets: frame {f} stream {s}")
+    for s in range(n):
+        st, rs = cache.state(s), refs[s].state()
+        assert (st["offset"], st["len"], st["write_pos"], st["frame_count"], st["last_text_token"]) == \
+               (rs["offset"], rs["len"], rs["write_pos"], rs["frame_count"], rs["last_text_token"]), s
+    assert tally.exempt == 0
+
+
+def test_subsets_of_streams_step_independently():
+    """Batches that name different subsets of a set, in any order, leave the other streams untouched,
+    and each stream's tokens are those of the oracle stream alone."""
+    g, cfg, model, om = small_model(seed=32)
+    n = 20
+    cache = model.create_cache(n, "bf16")
+    refs = [om.stream(O.KV_BF16) for _ in range(n)]
+    rng = np.random.default_rng(8)
+    for f in range(12):
+        k = int(rng.integers(16, n + 1))      # 16.. streams: the tensor-core batch path
+        ids = [int(x) for x in rng.permutation(n)[:k]]
+        audio = rng.integers(0, 300, (k, 4))
+        exp, _ = O.feed_frame_batch([refs[s] for s in ids], audio)
+        got = device_feed(cache, ids, audio)
+        assert [None if t < 0 else int(t) for t in got] == exp, f
+    for s in range(n):
+        assert cache.state(s)["offset"] == refs[s].state()["offset"]

@@ -107,6 +107,10 @@ def test_sizes_beyond_the_fixed_scratch_are_rejected():
     for bad in (0, 65, 65536):
         assert lib().stt_q4_matmul_device_noalloc(t._h, x.data_ptr(), 0, 1, bad, out.data_ptr(), s) == STT_E_INVALID_ARG
         assert "splits" in lib().stt_last_error().decode()
+    # the f16 tensor-core product needs scratch that grows with the rows: not offered here
+    rc = lib().stt_q4_matmul_device_noalloc(t._h, x.data_ptr(), 2, 1, 2, out.data_ptr(), s)
+    assert rc == STT_E_INVALID_ARG
+    assert "in_dtype 2" in lib().stt_last_error().decode()
     # misaligned input
     rc = lib().stt_q4_matmul_device_noalloc(t._h, C.c_void_p(x.data_ptr() + 4), 0, 1, 2, out.data_ptr(), s)
     assert rc == STT_E_INVALID_ARG
