@@ -381,10 +381,18 @@ def main():
     token_check = None
     fx = os.path.join(REPO, "tests", "golden", "bench_tokens.json")
     if rank == 0 and os.path.exists(fx) and F == JOB_FRAMES:
-        ref = json.load(open(fx))["streams16_250"]
+        fxd = json.load(open(fx))
+        ref = fxd["streams16_250"]
+        ties = {(t[0], t[1]): t[2] for t in fxd["near_ties"]}
         k = min(len(ref), S)
-        same = sum(int(np.array_equal(job_tokens[:, s], np.array(ref[s]))) for s in range(k))
-        token_check = {"streams_compared": k, "frames": F, "identical_streams": same}
+        first = {}
+        for s in range(k):
+            d = np.nonzero(job_tokens[:, s] != np.array(ref[s]))[0]
+            if d.size:
+                first[s] = int(d[0])
+        token_check = {"streams_compared": k, "frames": F, "identical_streams": k - len(first),
+                       # where a stream first differs, and the oracle's top-2 logit margin there
+                       "first_difference": {str(s): [f, ties.get((s, f))] for s, f in first.items()}}
 
     # e2e: the same job through the public host-buffer call, one call per batched frame
     e2e_steps = min(args.steps, 3)

@@ -151,6 +151,27 @@ int stt_streams_feed_frame_device(stt_streams* streams, const int32_t* stream_id
                                   const uint32_t* d_audio, int32_t* d_tokens,
                                   void* cuda_stream);
 
+/* Asynchronous batched frames — replaces SttStream::submit_frame_gpu (stream.rs:117-138) with
+ * take_batch_pending / resolve_batch (stream.rs:146-183) as the WASM bindings drive them
+ * (web/bindings.rs:432-489): frames are queued with the text token fed back on the device, and
+ * their tokens are read back later, without stalling the submitting thread.
+ *
+ * stt_streams_submit_frame queues one feed_frame step (the delay gating and the limit-cycle rule
+ * included) for the n streams stream_ids, with host audio (n*num_codebooks ids, copied before the
+ * call returns), on the set's own CUDA stream, and returns without waiting; the step's emitted
+ * tokens will land in pinned host memory behind an event.  *ticket identifies the frame.  At most
+ * 64 submitted frames may be outstanding: a 65th submit without taking the oldest one's tokens
+ * fails with STT_E_STATE.  Frames of one set run in submission order, and after any other call on
+ * the set.
+ * stt_streams_poll_frame takes the tokens of `ticket` if its step has completed (*ready = 1,
+ * tokens_out[i] for stream_ids[i], -1 = None) and returns at once otherwise (*ready = 0).
+ * stt_streams_wait_frame blocks until they are there.  Tokens are taken once per ticket, in any
+ * order; a kernel error of that step is returned by the call that takes them. */
+int stt_streams_submit_frame(stt_streams* streams, const int32_t* stream_ids, int n,
+                             const uint32_t* audio_tokens, int64_t* ticket);
+int stt_streams_poll_frame(stt_streams* streams, int64_t ticket, int32_t* tokens_out, int* ready);
+int stt_streams_wait_frame(stt_streams* streams, int64_t ticket, int32_t* tokens_out);
+
 /* Replaces SttStream::flush (stream.rs:315-338): text_delay frames of zero audio through
  * feed_frame, collecting the emitted tokens (at most text_delay).  *n_tokens receives the
  * count written to tokens_out (capacity entries available). */

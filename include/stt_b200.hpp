@@ -10,6 +10,8 @@
  *   SttModel::forward + argmax(2)         model.rs:631-664, stream.rs:104     LayerCaches::forward
  *   SttStream::new / feed_frame / flush /  stream.rs:53-81, 315-362           SttStream
  *     reset / reset_keep_buffers / set_last_text_token
+ *   submit_frame_gpu + take_batch_pending  stream.rs:117-183                  LayerCaches::submit_frame,
+ *     (async readback, web/bindings.rs:432-489)                                 PendingFrame::poll / wait
  *   Q4Tensor::from_q4_bytes, q4_matmul    gguf.rs:418-451, 517-578            Q4Tensor, q4_matmul
  *   SpmDecoder                            tokenizer.rs:7-38                   SpmDecoder
  *
@@ -81,6 +83,44 @@ public:
         check(stt_forward(h_.get(), &id, 1, audio.data(), &text, logits.data(), &am), "stt_forward");
         if (argmax) *argmax = am;
         return logits;
+    }
+
+    /* A submitted batched frame (the PendingFrames of take_batch_pending, stream.rs:146-183):
+     * poll() gives its tokens once its step has completed (std::nullopt before), wait() blocks.
+     * A token is -1 where the stream is inside the text delay.  Tokens are taken once. */
+    class PendingFrame {
+    public:
+        std::optional<std::vector<int32_t>> poll() {
+            std::vector<int32_t> t((size_t)n_);
+            int ready = 0;
+            check(stt_streams_poll_frame(h_, ticket_, t.data(), &ready), "stt_streams_poll_frame");
+            if (!ready) return std::nullopt;
+            return t;
+        }
+        std::vector<int32_t> wait() {
+            std::vector<int32_t> t((size_t)n_);
+            check(stt_streams_wait_frame(h_, ticket_, t.data()), "stt_streams_wait_frame");
+            return t;
+        }
+        int64_t ticket() const { return ticket_; }
+
+    private:
+        friend class LayerCaches;
+        PendingFrame(stt_streams* h, int64_t ticket, int n) : h_(h), ticket_(ticket), n_(n) {}
+        stt_streams* h_;
+        int64_t ticket_;
+        int n_;
+    };
+
+    /* SttStream::submit_frame_gpu (stream.rs:117-138) for the streams `ids` at once: one frame of
+     * audio per stream (ids.size() * codebooks tokens), the text token fed back on the device,
+     * queued without waiting. */
+    PendingFrame submit_frame(const std::vector<int32_t>& ids, const std::vector<uint32_t>& audio) {
+        check_audio(audio.size(), ids.size());
+        int64_t t = 0;
+        check(stt_streams_submit_frame(h_.get(), ids.data(), (int)ids.size(), audio.data(), &t),
+              "stt_streams_submit_frame");
+        return PendingFrame(h_.get(), t, (int)ids.size());
     }
 
 private:

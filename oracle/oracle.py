@@ -78,6 +78,7 @@ def lib() -> C.CDLL:
         L.orc_flush.argtypes = [P, U32P, C.c_int]
         L.orc_stream_state.argtypes = [P, C.POINTER(C.c_int64)]
         L.orc_stream_set_last_text_token.argtypes = [P, C.c_uint32]
+        L.orc_stream_set_delay_state.argtypes = [P, C.c_uint32, C.c_uint32, C.c_uint32]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         L.orc_last_error.restype = C.c_char_p
@@ -248,6 +249,9 @@ class OracleStream:
 
     def set_last_text_token(self, t: int):
         lib().orc_stream_set_last_text_token(self._h, t)
+
+    def set_delay_state(self, last_text_token: int, prev0: int, prev1: int):
+        lib().orc_stream_set_delay_state(self._h, last_text_token, prev0 & 0xFFFFFFFF, prev1 & 0xFFFFFFFF)
 
     def state(self) -> dict:
         out = (C.c_int64 * 7)()

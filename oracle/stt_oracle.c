@@ -551,6 +551,11 @@ void orc_stream_state(const orc_stream* s, int64_t out[7]) {
     out[4] = s->last_text_token; out[5] = s->delay_prev[0]; out[6] = s->delay_prev[1];
 }
 void orc_stream_set_last_text_token(orc_stream* s, uint32_t token) { s->last_text_token = token; }
+void orc_stream_set_delay_state(orc_stream* s, uint32_t last_text_token, uint32_t prev0, uint32_t prev1) {
+    s->last_text_token = last_text_token;
+    s->delay_prev[0] = prev0;
+    s->delay_prev[1] = prev1;
+}
 
 /* RmsNorm (burn::nn::RmsNorm via model.rs:365-373): (x / sqrt(mean(x^2) + eps)) * alpha. */
 static void rmsnorm(const float* x, const float* alpha, int32_t n, float* y) {

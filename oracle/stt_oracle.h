@@ -87,6 +87,9 @@ int orc_flush(orc_stream* s, uint32_t* tokens, int capacity);
 /* State: offset, len, write_pos, frame_count, last_text_token, delay_prev0, delay_prev1. */
 void orc_stream_state(const orc_stream* s, int64_t out[7]);
 void orc_stream_set_last_text_token(orc_stream* s, uint32_t token);
+/* Sets the next text token and the limit-cycle history (stream.rs:20-41) together, so that a
+ * test can make the oracle continue from a state the device reached. */
+void orc_stream_set_delay_state(orc_stream* s, uint32_t last_text_token, uint32_t prev0, uint32_t prev1);
 
 /* Number of worker threads used by the matmuls (OpenMP); <= 0 leaves the default. */
 void orc_set_threads(int n);

@@ -2,11 +2,13 @@
 // The entry points and the reference interfaces they replace are listed in include/stt_b200.h.
 #include <algorithm>
 #include <cmath>
+#include <condition_variable>
 #include <cstdarg>
 #include <map>
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "common.h"
@@ -106,6 +108,150 @@ struct HostBuf {
     ~HostBuf() {
         if (p) cudaFreeHost(p);
     }
+};
+
+// Parallel host copy of a byte range of a (possibly sharded) GGUF file: a few worker threads each
+// copy one contiguous slice of every request.
+class CopyPool {
+public:
+    explicit CopyPool(int n) {
+        for (int i = 0; i < n; ++i) workers_.emplace_back([this, i, n] { loop(i, n); });
+    }
+    ~CopyPool() {
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            stop_ = true;
+            ++gen_;
+        }
+        cv_.notify_all();
+        for (auto& t : workers_) t.join();
+    }
+    // Copies bytes [pos, pos + n) of the file to dst; returns false if they run past its end.
+    bool read(const GgufFile& f, uint64_t pos, void* dst, uint64_t n) {
+        std::unique_lock<std::mutex> lk(mu_);
+        file_ = &f;
+        pos_ = pos;
+        dst_ = static_cast<uint8_t*>(dst);
+        n_ = n;
+        ok_ = true;
+        pending_ = (int)workers_.size();
+        ++gen_;
+        cv_.notify_all();
+        done_.wait(lk, [this] { return pending_ == 0; });
+        return ok_;
+    }
+
+private:
+    void loop(int id, int nw) {
+        uint64_t seen = 0;
+        for (;;) {
+            std::unique_lock<std::mutex> lk(mu_);
+            cv_.wait(lk, [&] { return gen_ != seen; });
+            seen = gen_;
+            if (stop_) return;
+            const GgufFile* f = file_;
+            const uint64_t pos = pos_, n = n_;
+            uint8_t* dst = dst_;
+            lk.unlock();
+            // slices on 4 KB boundaries: each worker touches whole pages of the destination
+            const uint64_t pages = (n + 4095) / 4096;
+            const uint64_t a = std::min(n, pages * id / nw * 4096), b = std::min(n, pages * (id + 1) / nw * 4096);
+            const bool ok = b <= a || f->read_range(pos + a, dst + a, b - a);
+            lk.lock();
+            if (!ok) ok_ = false;
+            if (--pending_ == 0) done_.notify_all();
+        }
+    }
+    std::vector<std::thread> workers_;
+    std::mutex mu_;
+    std::condition_variable cv_, done_;
+    uint64_t gen_ = 0;
+    bool stop_ = false, ok_ = true;
+    int pending_ = 0;
+    const GgufFile* file_ = nullptr;
+    uint64_t pos_ = 0, n_ = 0;
+    uint8_t* dst_ = nullptr;
+};
+
+// Pipelined upload of a checkpoint: the host copies the next piece of the file into one of a few
+// pinned staging buffers (several threads) while the copy engine moves the previous pieces to the
+// device and the repack kernels split Q4_0 pieces into their planes, all on one stream.  A staging
+// buffer is refilled once the event recorded after its last use has completed.
+class Uploader {
+public:
+    static constexpr size_t kPiece = (size_t)16 << 20;       // bytes per staging buffer
+    static constexpr size_t kQ4Piece = kPiece / 18 * 18;     // whole Q4_0 blocks per piece
+    static constexpr int kStages = 3;
+
+    Uploader() : pool_(std::max(1, std::min(8, (int)std::thread::hardware_concurrency()))) {}
+    ~Uploader() {
+        if (st_) cudaStreamSynchronize(st_);
+        for (auto& e : ev_)
+            if (e) cudaEventDestroy(e);
+        if (pinned_) cudaFreeHost(pinned_);
+        if (draw_) cudaFree(draw_);
+        if (st_) cudaStreamDestroy(st_);
+    }
+    int init() {
+        CUDA_TRY(cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking));
+        CUDA_TRY(cudaHostAlloc(&pinned_, kPiece * kStages, cudaHostAllocDefault));
+        CUDA_TRY(cudaMalloc(&draw_, kPiece * kStages));
+        for (auto& e : ev_) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        return STT_OK;
+    }
+    // File bytes [pos, pos + n) to device memory dst.
+    int to_device(const GgufFile& f, uint64_t pos, uint64_t n, void* dst) {
+        for (uint64_t o = 0; o < n; o += kPiece) {
+            const uint64_t take = std::min<uint64_t>(kPiece, n - o);
+            uint8_t* h;
+            TRY(stage(f, pos + o, take, &h));
+            CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(dst) + o, h, take, cudaMemcpyHostToDevice, st_));
+            CUDA_TRY(cudaEventRecord(ev_[cur_], st_));
+        }
+        return STT_OK;
+    }
+    // A Q4_0 matrix of nblocks raw blocks at file offset pos, repacked into its planes; big_scale
+    // (device) is set when a scale is too large for the tensor-core product.
+    int q4(const GgufFile& f, uint64_t pos, int64_t nblocks, uint4* nib, uint16_t* scale, int* big_scale) {
+        const int64_t per = (int64_t)(kQ4Piece / 18);
+        for (int64_t b0 = 0; b0 < nblocks; b0 += per) {
+            const int64_t nb = std::min<int64_t>(per, nblocks - b0);
+            uint8_t* h;
+            TRY(stage(f, pos + (uint64_t)b0 * 18, (uint64_t)nb * 18, &h));
+            uint8_t* d = static_cast<uint8_t*>(draw_) + (size_t)cur_ * kPiece;
+            CUDA_TRY(cudaMemcpyAsync(d, h, (size_t)nb * 18, cudaMemcpyHostToDevice, st_));
+            CUDA_TRY(launch_repack_q4(d, nb, nib + b0, scale + b0, st_, big_scale));
+            CUDA_TRY(cudaEventRecord(ev_[cur_], st_));
+        }
+        return STT_OK;
+    }
+    int finish() {
+        CUDA_TRY(cudaStreamSynchronize(st_));
+        return STT_OK;
+    }
+    cudaStream_t stream() const { return st_; }
+
+private:
+    // Next staging buffer, filled with file bytes [pos, pos + n) (n <= kPiece).
+    int stage(const GgufFile& f, uint64_t pos, uint64_t n, uint8_t** out) {
+        cur_ = next_;
+        next_ = (next_ + 1) % kStages;
+        if (used_[cur_]) CUDA_TRY(cudaEventSynchronize(ev_[cur_]));
+        used_[cur_] = true;
+        uint8_t* h = static_cast<uint8_t*>(pinned_) + (size_t)cur_ * kPiece;
+        if (!pool_.read(f, pos, h, n))
+            return set_error(STT_E_FORMAT, "tensor data (%llu bytes at %llu) runs past the end of the file",
+                             (unsigned long long)n, (unsigned long long)pos);
+        *out = h;
+        return STT_OK;
+    }
+    CopyPool pool_;
+    cudaStream_t st_ = nullptr;
+    void* pinned_ = nullptr;
+    void* draw_ = nullptr;
+    cudaEvent_t ev_[kStages] = {};
+    bool used_[kStages] = {};
+    int next_ = 0, cur_ = 0;
 };
 
 }  // namespace stt
@@ -333,7 +479,6 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
     q4s.push_back(head_t);
     size_t off = 0;
     std::vector<size_t> off_nib(q4s.size()), off_sc(q4s.size());
-    size_t max_raw = 0;
     for (size_t i = 0; i < q4s.size(); ++i) {
         const size_t nblk = q4s[i]->numel / 32;
         off_nib[i] = off;
@@ -341,7 +486,6 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
         off_sc[i] = off;
         off = align_up(off + nblk * 2, 256);
         m->q4_bytes += q4s[i]->nbytes;
-        max_raw = std::max<size_t>(max_raw, q4s[i]->nbytes);
     }
     const size_t off_norms = off;
     off = align_up(off + norms.size() * sizeof(float), 256);
@@ -354,6 +498,8 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
     off = align_up(off + (size_t)m->TV * m->emb_row_bytes, 256);
     const size_t off_layers = off;
     off = align_up(off + sizeof(LayerDev) * m->L, 256);
+    const size_t off_flag = off;  // the loader's scale-range flag
+    off = align_up(off + sizeof(int), 256);
     m->device_bytes = off;
 
     // Every tensor's bytes must lie inside the input (tensor_data, gguf.rs:298-310).
@@ -397,27 +543,30 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
         }
     } cleanup{m.get()};
 
-    // Q4 matrices: raw bytes -> staging -> repack into the two planes
+    // Upload: every Q4 matrix (repacked into its planes on the device, its scales checked there for
+    // the tensor-core product's range), then the embedding tables as they are in the file; the
+    // small host-built tables (norms, RoPE, layer table) go last.
     {
-        DevBuf staging;
-        TRY(staging.ensure(max_raw));
-        std::vector<uint8_t> scratch;
+        Uploader up;
+        TRY(up.init());
+        int* big_scale = reinterpret_cast<int*>(base + off_flag);
+        CUDA_TRY(cudaMemsetAsync(big_scale, 0, sizeof(int), up.stream()));
         std::vector<Q4Dev> qd(q4s.size());
-        m->tc_ok = true;
         for (size_t i = 0; i < q4s.size(); ++i) {
-            const uint8_t* src = g.tensor_data(*q4s[i], scratch);
-            if (!src) return STT_E_FORMAT;
-            m->tc_ok = m->tc_ok && tc_gemm_scales_ok(src, (int64_t)(q4s[i]->numel / 32));
-            CUDA_TRY(cudaMemcpy(staging.p, src, q4s[i]->nbytes, cudaMemcpyHostToDevice));
             const auto s = q4s[i]->shape();
             qd[i].nib = reinterpret_cast<const uint4*>(base + off_nib[i]);
             qd[i].scale = reinterpret_cast<const uint16_t*>(base + off_sc[i]);
             qd[i].n = (int32_t)s[0];
             qd[i].k = (int32_t)s[1];
-            CUDA_TRY(launch_repack_q4(static_cast<const uint8_t*>(staging.p), (int64_t)(q4s[i]->numel / 32),
-                                      const_cast<uint4*>(qd[i].nib), const_cast<uint16_t*>(qd[i].scale), 0));
-            CUDA_TRY(cudaDeviceSynchronize());
+            TRY(up.q4(g, g.data_offset() + q4s[i]->offset, (int64_t)(q4s[i]->numel / 32), const_cast<uint4*>(qd[i].nib),
+                      const_cast<uint16_t*>(qd[i].scale), big_scale));
         }
+        for (int i = 0; i < m->NC; ++i)
+            TRY(up.to_device(g, g.data_offset() + audio[i]->offset, audio_table, base + off_emb + audio_table * i));
+        TRY(up.to_device(g, g.data_offset() + text_emb->offset, (size_t)m->TV * m->emb_row_bytes, base + off_text));
+        int big = 0;
+        CUDA_TRY(cudaMemcpyAsync(&big, big_scale, sizeof(int), cudaMemcpyDeviceToHost, up.stream()));
+        TRY(up.finish());
         m->h_layers.resize(m->L);
         const float* dn = reinterpret_cast<const float*>(base + off_norms);
         for (int l = 0; l < m->L; ++l) {
@@ -430,6 +579,7 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
             L.norm2 = dn + (size_t)(2 * l + 1) * m->D;
         }
         m->head = qd.back();
+        m->tc_ok = big == 0;
         for (const Q4Dev& w : qd) m->tc_ok = m->tc_ok && tc_gemm_supported(w);
         if (m->tc_ok) {
             m->tc_w.resize(qd.size());
@@ -440,17 +590,6 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
     }
     CUDA_TRY(cudaMemcpy(base + off_norms, norms.data(), norms.size() * sizeof(float), cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(base + off_rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice));
-    {
-        std::vector<uint8_t> scratch;
-        for (int i = 0; i < m->NC; ++i) {
-            const uint8_t* src = g.tensor_data(*audio[i], scratch);
-            if (!src) return STT_E_FORMAT;
-            CUDA_TRY(cudaMemcpy(base + off_emb + audio_table * i, src, audio_table, cudaMemcpyHostToDevice));
-        }
-        const uint8_t* src = g.tensor_data(*text_emb, scratch);
-        if (!src) return STT_E_FORMAT;
-        CUDA_TRY(cudaMemcpy(base + off_text, src, (size_t)m->TV * m->emb_row_bytes, cudaMemcpyHostToDevice));
-    }
     CUDA_TRY(cudaMemcpy(base + off_layers, m->h_layers.data(), sizeof(LayerDev) * m->L, cudaMemcpyHostToDevice));
     m->d_layers = reinterpret_cast<LayerDev*>(base + off_layers);
     m->rope = reinterpret_cast<const float2*>(base + off_rope);
@@ -519,6 +658,17 @@ struct stt_streams {
     std::map<int, cudaGraphExec_t> graphs;
     std::map<int, int> graph_kernels;  // kernel nodes of each captured step graph
     MegaState mega;
+    // submitted batched frames whose tokens the caller has not taken yet (stt_streams_submit_frame)
+    struct Pending {
+        int64_t ticket = -1;
+        int n = 0;
+        bool taken = true;
+        cudaEvent_t ev = nullptr;
+    };
+    std::vector<Pending> pend;
+    HostBuf pend_in, pend_out;    // pinned: per slot the audio ids in, the tokens and step descriptor out
+    DevBuf pend_audio, pend_tok;  // device: per slot the audio ids and the emitted tokens
+    int64_t next_ticket = 0;
 };
 
 namespace {
@@ -615,23 +765,23 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
         GemvArgs a{};
         a.W = L.qkv; a.in = s->d_x; a.norm = L.norm1; a.out = s->d_qkv; a.ldo = 3 * m->D; a.layer = l;
         a.n_units = 3 * m->D / 2;
-        CUDA_TRY(launch_gemv(c, a, EPI_QKV, n, grid, st));
+        CUDA_TRY(launch_gemv(c, a, EPI_QKV, n, st));
         CUDA_TRY(launch_attention(c, l, st));
         a = GemvArgs{};
         a.W = L.out; a.in = s->d_attn; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
-        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, grid, st));
+        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, st));
         a = GemvArgs{};
         a.W = L.fin; a.in = s->d_x; a.norm = L.norm2; a.out = s->d_hid; a.ldo = m->F; a.n_units = m->F;
         a.half_n = m->F;
-        CUDA_TRY(launch_gemv(c, a, EPI_GATE, n, grid, st));
+        CUDA_TRY(launch_gemv(c, a, EPI_GATE, n, st));
         a = GemvArgs{};
         a.W = L.fout; a.in = s->d_hid; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
-        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, grid, st));
+        CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, st));
     }
     GemvArgs a{};
     a.W = m->head; a.in = s->d_x; a.norm = m->out_norm; a.out = s->d_logits; a.ldo = m->V;
     a.n_units = (m->V + 1) / 2;
-    CUDA_TRY(launch_gemv(c, a, EPI_LOGITS, n, grid, st));
+    CUDA_TRY(launch_gemv(c, a, EPI_LOGITS, n, st));
     CUDA_TRY(launch_finish(c, st));
     return STT_OK;
 }
@@ -887,6 +1037,12 @@ extern "C" int stt_streams_destroy(stt_streams* s) {
     {
         DeviceScope ds(s->m->device);
         if (s->stream) cudaStreamSynchronize(s->stream);
+        for (auto& p : s->pend)
+            if (p.ev) cudaEventDestroy(p.ev);
+        s->pend_in.release();
+        s->pend_out.release();
+        s->pend_audio.release();
+        s->pend_tok.release();
         for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
         s->graphs.clear();
         if (s->stream) cudaStreamDestroy(s->stream);
@@ -962,6 +1118,121 @@ extern "C" int stt_streams_feed_frame_device(stt_streams* s, const int32_t* ids,
     TRY(run_steps(s, ids, n, 1, d_audio, nullptr, d_tokens, nullptr, 1, static_cast<cudaStream_t>(cuda_stream)));
     s->state_stale = true;
     return STT_OK;
+}
+
+// ------------------------------------------------------------------------------------ submitted frames
+
+namespace {
+constexpr int kPendSlots = 64;  // submitted frames whose tokens may be outstanding at once
+
+size_t pend_out_stride(const stt_streams* s) {
+    return ((size_t)s->S * sizeof(int32_t) + sizeof(StepDesc) + 15) / 16 * 16;
+}
+
+int pend_setup(stt_streams* s) {
+    if (!s->pend.empty()) return STT_OK;
+    const size_t nc = (size_t)s->m->NC;
+    TRY(s->pend_in.ensure((size_t)kPendSlots * s->S * nc * sizeof(uint32_t)));
+    TRY(s->pend_out.ensure((size_t)kPendSlots * pend_out_stride(s)));
+    TRY(s->pend_audio.ensure((size_t)kPendSlots * s->S * nc * sizeof(uint32_t)));
+    TRY(s->pend_tok.ensure((size_t)kPendSlots * s->S * sizeof(int32_t)));
+    std::vector<stt_streams::Pending> p(kPendSlots);
+    for (auto& x : p) {
+        if (cudaEventCreateWithFlags(&x.ev, cudaEventDisableTiming) != cudaSuccess) {
+            for (auto& y : p)
+                if (y.ev) cudaEventDestroy(y.ev);
+            return set_error(STT_E_CUDA, "cudaEventCreate failed");
+        }
+    }
+    s->pend = std::move(p);
+    return STT_OK;
+}
+
+// The slot of `ticket` if it is a submitted frame whose tokens are still to be taken.
+int pend_slot(stt_streams* s, int64_t ticket, int* slot) {
+    if (ticket < 0 || ticket >= s->next_ticket || s->pend.empty())
+        return set_error(STT_E_INVALID_ARG, "ticket %lld was not issued by this stream set", (long long)ticket);
+    const int k = (int)(ticket % kPendSlots);
+    if (s->pend[k].ticket != ticket || s->pend[k].taken)
+        return set_error(STT_E_INVALID_ARG, "the tokens of ticket %lld were already taken", (long long)ticket);
+    *slot = k;
+    return STT_OK;
+}
+
+int pend_take(stt_streams* s, int k, int32_t* tokens_out) {
+    stt_streams::Pending& p = s->pend[k];
+    const uint8_t* o = static_cast<const uint8_t*>(s->pend_out.p) + (size_t)k * pend_out_stride(s);
+    StepDesc desc;
+    std::memcpy(&desc, o + (size_t)s->S * sizeof(int32_t), sizeof desc);
+    if (tokens_out) std::memcpy(tokens_out, o, (size_t)p.n * sizeof(int32_t));
+    p.taken = true;
+    if (desc.error != 0)
+        return set_error(desc.error == STT_E_INVALID_ARG ? STT_E_INVALID_ARG : STT_E_DEVICE_FLAG,
+                         "a kernel raised error %d in submitted frame %lld", desc.error, (long long)p.ticket);
+    return STT_OK;
+}
+}  // namespace
+
+extern "C" int stt_streams_submit_frame(stt_streams* s, const int32_t* ids, int n, const uint32_t* audio,
+                                        int64_t* ticket) {
+    clear_error();
+    if (!s || !audio || !ticket) return set_error(STT_E_INVALID_ARG, "NULL argument");
+    stt_model* m = s->m;
+    DeviceScope ds(m->device);
+    TRY(check_ids(s, ids, n));
+    const size_t nc = (size_t)m->NC;
+    TRY(check_tokens(m, audio, (size_t)n * nc, nullptr, 0));
+    TRY(check_positions(s, ids, n, 1));
+    TRY(pend_setup(s));
+    const int k = (int)(s->next_ticket % kPendSlots);
+    stt_streams::Pending& p = s->pend[k];
+    if (!p.taken)
+        return set_error(STT_E_STATE, "%d submitted frames are outstanding; take the tokens of ticket %lld first",
+                         kPendSlots, (long long)p.ticket);
+    // the slot's previous copies have completed (its event passed when its tokens were taken)
+    uint32_t* hin = static_cast<uint32_t*>(s->pend_in.p) + (size_t)k * s->S * nc;
+    std::memcpy(hin, audio, (size_t)n * nc * sizeof(uint32_t));
+    uint32_t* din = static_cast<uint32_t*>(s->pend_audio.p) + (size_t)k * s->S * nc;
+    int32_t* dtok = static_cast<int32_t*>(s->pend_tok.p) + (size_t)k * s->S;
+    uint8_t* hout = static_cast<uint8_t*>(s->pend_out.p) + (size_t)k * pend_out_stride(s);
+    CUDA_TRY(cudaMemcpyAsync(din, hin, (size_t)n * nc * sizeof(uint32_t), cudaMemcpyHostToDevice, s->stream));
+    TRY(run_steps(s, ids, n, 1, din, nullptr, dtok, nullptr, 1, s->stream));
+    CUDA_TRY(cudaMemcpyAsync(hout, dtok, (size_t)n * sizeof(int32_t), cudaMemcpyDeviceToHost, s->stream));
+    CUDA_TRY(cudaMemcpyAsync(hout + (size_t)s->S * sizeof(int32_t), s->d_desc, sizeof(StepDesc), cudaMemcpyDeviceToHost,
+                             s->stream));
+    CUDA_TRY(cudaEventRecord(p.ev, s->stream));
+    p.ticket = s->next_ticket;
+    p.n = n;
+    p.taken = false;
+    *ticket = s->next_ticket++;
+    return STT_OK;
+}
+
+extern "C" int stt_streams_poll_frame(stt_streams* s, int64_t ticket, int32_t* tokens_out, int* ready) {
+    clear_error();
+    if (!s || !tokens_out || !ready) return set_error(STT_E_INVALID_ARG, "NULL argument");
+    *ready = 0;
+    DeviceScope ds(s->m->device);
+    int k;
+    TRY(pend_slot(s, ticket, &k));
+    const cudaError_t e = cudaEventQuery(s->pend[k].ev);
+    if (e == cudaErrorNotReady) {
+        (void)cudaGetLastError();
+        return STT_OK;
+    }
+    CUDA_TRY(e);
+    *ready = 1;
+    return pend_take(s, k, tokens_out);
+}
+
+extern "C" int stt_streams_wait_frame(stt_streams* s, int64_t ticket, int32_t* tokens_out) {
+    clear_error();
+    if (!s || !tokens_out) return set_error(STT_E_INVALID_ARG, "NULL argument");
+    DeviceScope ds(s->m->device);
+    int k;
+    TRY(pend_slot(s, ticket, &k));
+    CUDA_TRY(cudaEventSynchronize(s->pend[k].ev));
+    return pend_take(s, k, tokens_out);
 }
 
 extern "C" int stt_stream_flush(stt_streams* s, int stream_id, uint32_t* tokens_out, int capacity, int* n_tokens) {
@@ -1135,7 +1406,7 @@ extern "C" int stt_q4_matmul_device(const stt_q4_tensor* t, const void* d_in, in
     a.out = d_out;
     a.ldo = t->w.n;
     a.n_units = (t->w.n + 1) / 2;
-    CUDA_TRY(launch_gemv(c, a, EPI_PLAIN, rows, 2 * t->num_sms, static_cast<cudaStream_t>(cuda_stream)));
+    CUDA_TRY(launch_gemv(c, a, EPI_PLAIN, rows, static_cast<cudaStream_t>(cuda_stream)));
     return STT_OK;
 }
 

@@ -37,6 +37,10 @@ public:
     // tensor runs past the end of the input.
     const uint8_t* tensor_data(const GgufTensor& t, std::vector<uint8_t>& scratch) const;
 
+    // Copies n bytes of the logical file (the shards back to back) from byte pos; false past the
+    // end.  Safe to call from several threads at once.
+    bool read_range(uint64_t pos, void* dst, uint64_t n) const { return read(pos, dst, n); }
+
     uint32_t version() const { return version_; }
     uint64_t tensor_count() const { return tensor_count_; }
     uint64_t data_offset() const { return data_offset_; }

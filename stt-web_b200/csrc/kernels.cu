@@ -15,6 +15,7 @@
 #include <cfloat>
 
 #include "device.cuh"
+#include "dp4a.cuh"
 #include "kernels.h"
 #include "tc_layout.cuh"
 
@@ -22,13 +23,17 @@ namespace stt {
 
 // ------------------------------------------------------------------------------------ Q4 layout
 
-// Splits raw Q4_0 blocks (18 bytes: f16 scale, 16 nibble bytes) into the two device planes.
+// Splits raw Q4_0 blocks (18 bytes: f16 scale, 16 nibble bytes) into the two device planes.  When
+// big_scale is set, a block whose scale has magnitude above 4 (or is inf / nan) sets it to 1: such
+// weights overflow the f16 parts of the tensor-core product (tc_gemm.cu).
 __global__ void repack_q4_kernel(const uint8_t* __restrict__ raw, int64_t nblocks, uint4* __restrict__ nib,
-                                 uint16_t* __restrict__ scale) {
+                                 uint16_t* __restrict__ scale, int* __restrict__ big_scale) {
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= nblocks) return;
     const uint8_t* p = raw + b * 18;
-    scale[b] = (uint16_t)(p[0] | (p[1] << 8));
+    const uint16_t sb = (uint16_t)(p[0] | (p[1] << 8));
+    scale[b] = sb;
+    if (big_scale && (sb & 0x7FFFu) > 0x4400u) *big_scale = 1;
     uint32_t w[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -109,14 +114,6 @@ __global__ void __launch_bounds__(256) embed_kernel(Ctx c) {
 
 // ------------------------------------------------------------------------------------ GEMV
 
-// Input vector layout in shared memory: element j of batch row m sits at
-//   m*K + ((q*NB + b) << 2) + e,   b = j/32, q = (j%32)/4, e = j%4
-// so lane l reading quad q of block b = l + 32t touches consecutive 16-byte chunks.
-__device__ __forceinline__ int xs_index(int j, int NB) {
-    const int b = j >> 5, w = j & 31;
-    return (((w >> 2) * NB + b) << 2) + (w & 3);
-}
-
 // Deterministic block reduction (fixed order) of one value per thread; all threads get the sum.
 __device__ __forceinline__ float block_sum(float v, float* red) {
     v = warp_sum(v);
@@ -129,11 +126,14 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     return s;
 }
 
-// Loads batch rows [row0, row0+mb) of `in` into the shared layout above, applying RMSNorm
-// (burn::nn::RmsNorm: (x / sqrt(mean(x^2) + 1e-8)) * alpha) when alpha != NULL.
-__device__ void load_vectors(const float* __restrict__ in, const __nv_bfloat16* __restrict__ in_bf16, int K,
-                             int row0, int mb, const float* __restrict__ alpha, float* xs, float* red) {
-    const int NB = K >> 5;
+// The GEMV input: batch rows [row0, row0 + mb) of `in` (f32, or bf16 when in_bf16 is set),
+// RMSNorm'd with alpha when alpha != NULL (burn::nn::RmsNorm: (x / sqrt(mean(x^2) + 1e-8)) * alpha),
+// as dp4a limbs L[m] ([6][NB] uint4) and block exponents xs[m] ([NB]).  Every thread of the CTA
+// takes part; ends with a CTA barrier.
+__device__ void load_limbs(const float* __restrict__ in, const __nv_bfloat16* __restrict__ in_bf16, int K, int row0,
+                           int mb, const float* __restrict__ alpha, uint4* L, float* xs, float* red) {
+    const int NB = K >> 5, nq = K >> 2;
+    const int nq_pad = (nq + 31) & ~31;  // whole warps join the shuffles of quad_limbs_store
     for (int m = 0; m < mb; ++m) {
         const int64_t base = (int64_t)(row0 + m) * K;
         float rms = 1.0f;
@@ -146,33 +146,29 @@ __device__ void load_vectors(const float* __restrict__ in, const __nv_bfloat16* 
             ss = block_sum(ss, red);
             rms = sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-8f));
         }
-        for (int j = threadIdx.x; j < K; j += blockDim.x) {
-            float v = in_bf16 ? __bfloat162float(in_bf16[base + j]) : in[base + j];
-            if (alpha) v = __fmul_rn(__fdiv_rn(v, rms), alpha[j]);
-            xs[m * K + xs_index(j, NB)] = v;
+        for (int q = threadIdx.x; q < nq_pad; q += blockDim.x) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            const bool valid = q < nq;
+            if (valid) {
+                if (in_bf16) {
+                    const uint2 r = *reinterpret_cast<const uint2*>(in_bf16 + base + 4 * q);
+                    v = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
+                                    __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
+                } else {
+                    v = *reinterpret_cast<const float4*>(in + base + 4 * q);
+                }
+                if (alpha) {
+                    const float4 al = reinterpret_cast<const float4*>(alpha)[q];
+                    v.x = __fmul_rn(__fdiv_rn(v.x, rms), al.x);
+                    v.y = __fmul_rn(__fdiv_rn(v.y, rms), al.y);
+                    v.z = __fmul_rn(__fdiv_rn(v.z, rms), al.z);
+                    v.w = __fmul_rn(__fdiv_rn(v.w, rms), al.w);
+                }
+            }
+            quad_limbs_store(L + (size_t)m * 6 * NB, xs + (size_t)m * NB, q, NB, v, valid);
         }
     }
-}
-
-// Sum over one 32-element block of (nibble - 8) * x for the 4 words of a Q4_0 payload.
-__device__ __forceinline__ float block_dot(const uint4 q, const float4* __restrict__ xq, int NB) {
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-    float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-    for (int wi = 0; wi < 4; ++wi) {
-        const float4 lo = xq[wi * NB];
-        const float4 hi = xq[(4 + wi) * NB];
-        const uint32_t w = words[wi];
-        s0 = __fmaf_rn(nib_m8(w & 0xFu), lo.x, s0);
-        s1 = __fmaf_rn(nib_m8((w >> 4) & 0xFu), hi.x, s1);
-        s0 = __fmaf_rn(nib_m8((w >> 8) & 0xFu), lo.y, s0);
-        s1 = __fmaf_rn(nib_m8((w >> 12) & 0xFu), hi.y, s1);
-        s0 = __fmaf_rn(nib_m8((w >> 16) & 0xFu), lo.z, s0);
-        s1 = __fmaf_rn(nib_m8((w >> 20) & 0xFu), hi.z, s1);
-        s0 = __fmaf_rn(nib_m8((w >> 24) & 0xFu), lo.w, s0);
-        s1 = __fmaf_rn(nib_m8(w >> 28), hi.w, s1);
-    }
-    return s0 + s1;
+    __syncthreads();
 }
 
 template <int EPI>
@@ -233,59 +229,115 @@ __device__ __forceinline__ void epilogue(const Ctx& c, const GemvArgs& a, int bm
     }
 }
 
+// The batched Q4 GEMV (batches of fewer than 16 streams, and the isolated f32 / bf16 matmul): for
+// each unit (a row pair; EPI_GATE: a gate row and its value row) and each batch row m < mb,
+// sum over blocks of scale * dot(block, x[m]) with the exact dp4a block dot of dp4a.cuh, then the
+// epilogue.  A unit is reduced by a team of `team` consecutive threads (8 .. 256, a power of two;
+// past 32 the team spans warps), each taking blocks tl, tl + team, ... (at most kBPL of them), so
+// that all of a unit's weight bytes are in flight at once and one launch keeps about 128 K lanes
+// busy.  The CTA first issues its first unit's weight loads, then converts the input rows to limbs
+// in shared memory while they are in flight.  Deterministic: the team sums its lanes, then its
+// warps, in a fixed order.
+constexpr int kBPL = 4;           // blocks per team lane and row, at most
+constexpr int kGemvThreads = 256;
+
 template <int MB, int EPI>
-__global__ void __launch_bounds__(256) gemv_kernel(Ctx c, GemvArgs a, int row0, int mb) {
-    extern __shared__ float4 smem4[];
-    float* xs = reinterpret_cast<float*>(smem4);
-    __shared__ float red[32];
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(Ctx c, GemvArgs a, int row0, int mb, int team) {
+    extern __shared__ uint4 gemv_smem[];
     const int K = a.W.k, NB = K >> 5;
-    load_vectors(a.in, a.in_bf16, K, row0, mb, a.norm, xs, red);
-    __syncthreads();
-    const int64_t u0 = (int64_t)a.n_units * blockIdx.x / gridDim.x;
-    const int64_t u1 = (int64_t)a.n_units * (blockIdx.x + 1) / gridDim.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    const float4* xq = reinterpret_cast<const float4*>(xs);
-    for (int64_t u = u0 + warp; u < u1; u += nwarps) {
-        int ra, rb;
-        unit_rows<EPI>(a, (int)u, &ra, &rb);
-        float acc[2][MB];
+    uint4* L = gemv_smem;                                           // [MB][6][NB]
+    float* xs = reinterpret_cast<float*>(gemv_smem + (size_t)MB * 6 * NB);  // [MB][NB]
+    __shared__ float red[32];
+    __shared__ float tpart[2][kGemvThreads / 32][2 * MB];          // cross-warp team partials
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int teams = kGemvThreads / team, my_team = tid / team, tl = tid % team;
+    const int64_t nteams = (int64_t)gridDim.x * teams;
+
+    uint4 qa[kBPL], qb[kBPL];
+    uint32_t sa[kBPL], sb[kBPL];
+    auto load_unit = [&](int64_t u, int* ra, int* rb) {
+        unit_rows<EPI>(a, (int)u, ra, rb);
+        const uint4* na = a.W.nib + (int64_t)*ra * NB;
+        const uint4* nb_ = a.W.nib + (int64_t)(*rb >= 0 ? *rb : *ra) * NB;
+        const uint16_t* s_a = a.W.scale + (int64_t)*ra * NB;
+        const uint16_t* s_b = a.W.scale + (int64_t)(*rb >= 0 ? *rb : *ra) * NB;
 #pragma unroll
-        for (int m = 0; m < MB; ++m) acc[0][m] = acc[1][m] = 0.0f;
-        const uint4* na = a.W.nib + (int64_t)ra * NB;
-        const uint4* nb_ = a.W.nib + (int64_t)(rb >= 0 ? rb : ra) * NB;
-        const uint16_t* sa = a.W.scale + (int64_t)ra * NB;
-        const uint16_t* sb = a.W.scale + (int64_t)(rb >= 0 ? rb : ra) * NB;
-        for (int b0 = lane; b0 < NB; b0 += 64) {
-            const int b1 = b0 + 32;
-            const bool has1 = b1 < NB;
-            const uint4 qa0 = __ldg(na + b0), qb0 = __ldg(nb_ + b0);
-            const uint4 qa1 = has1 ? __ldg(na + b1) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-            const uint4 qb1 = has1 ? __ldg(nb_ + b1) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-            const float da0 = f16_to_f32_ieee(__ldg(sa + b0)), db0 = f16_to_f32_ieee(__ldg(sb + b0));
-            const float da1 = has1 ? f16_to_f32_ieee(__ldg(sa + b1)) : 0.0f;
-            const float db1 = has1 ? f16_to_f32_ieee(__ldg(sb + b1)) : 0.0f;
+        for (int i = 0; i < kBPL; ++i) {
+            const int b = tl + i * team;
+            if (b < NB) {
+                qa[i] = __ldg(na + b);
+                qb[i] = __ldg(nb_ + b);
+                sa[i] = __ldg(s_a + b);
+                sb[i] = __ldg(s_b + b);
+            }
+        }
+    };
+
+    int64_t u = (int64_t)blockIdx.x * teams + my_team;
+    int ra = 0, rb = -1;
+    if (u < a.n_units) load_unit(u, &ra, &rb);  // weights first: they do not depend on the input
+    load_limbs(a.in, a.in_bf16, K, row0, mb, a.norm, L, xs, red);
+    int parity = 0;
+    for (; u < a.n_units; u += nteams) {
+        float acc[MB][2];
 #pragma unroll
-            for (int m = 0; m < MB; ++m) {
-                if (m < mb) {
-                    const float4* x0 = xq + (m * K >> 2) + b0;
-                    acc[0][m] = __fmaf_rn(da0, block_dot(qa0, x0, NB), acc[0][m]);
-                    acc[1][m] = __fmaf_rn(db0, block_dot(qb0, x0, NB), acc[1][m]);
-                    if (has1) {
-                        const float4* x1 = xq + (m * K >> 2) + b1;
-                        acc[0][m] = __fmaf_rn(da1, block_dot(qa1, x1, NB), acc[0][m]);
-                        acc[1][m] = __fmaf_rn(db1, block_dot(qb1, x1, NB), acc[1][m]);
+        for (int m = 0; m < MB; ++m) acc[m][0] = acc[m][1] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kBPL; ++i) {
+            const int b = tl + i * team;
+            if (b < NB) {
+                const float fa = f16_to_f32_ieee((uint16_t)sa[i]), fb = f16_to_f32_ieee((uint16_t)sb[i]);
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    if (m < mb) {
+                        const uint4* Lm = L + (size_t)m * 6 * NB;
+                        uint4 Lb[6];
+#pragma unroll
+                        for (int v = 0; v < 6; ++v) Lb[v] = Lm[v * NB + b];
+                        const float x = xs[m * NB + b];
+                        acc[m][0] = __fmaf_rn(block_dp4a(qa[i], Lb), __fmul_rn(fa, x), acc[m][0]);
+                        acc[m][1] = __fmaf_rn(block_dp4a(qb[i], Lb), __fmul_rn(fb, x), acc[m][1]);
                     }
                 }
             }
         }
+        const int cra = ra, crb = rb;
+        const int64_t next = u + nteams;
+        if (next < a.n_units) load_unit(next, &ra, &rb);  // the next unit's bytes fly during the reduction
+        // team reduction: lanes of the team inside a warp, then (teams past 32 lanes) its warps
+        const int span = team < 32 ? team : 32;
 #pragma unroll
-        for (int m = 0; m < MB; ++m) {
-            if (m < mb) {
-                const float va = warp_sum(acc[0][m]);
-                const float vb = warp_sum(acc[1][m]);
-                if (lane == 0) epilogue<EPI>(c, a, row0 + m, ra, rb, va, vb);
+        for (int m = 0; m < MB; ++m)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                for (int o = span >> 1; o > 0; o >>= 1) acc[m][h] += __shfl_xor_sync(0xFFFFFFFFu, acc[m][h], o);
+        if (team > 32) {
+            if (lane == 0)
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    tpart[parity][warp][2 * m] = acc[m][0];
+                    tpart[parity][warp][2 * m + 1] = acc[m][1];
+                }
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + my_team), "r"(team) : "memory");
+            if (tl == 0) {
+                const int w0 = warp, nw = team >> 5;
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    float s0 = tpart[parity][w0][2 * m], s1 = tpart[parity][w0][2 * m + 1];
+                    for (int w = 1; w < nw; ++w) {
+                        s0 += tpart[parity][w0 + w][2 * m];
+                        s1 += tpart[parity][w0 + w][2 * m + 1];
+                    }
+                    acc[m][0] = s0;
+                    acc[m][1] = s1;
+                }
             }
+            parity ^= 1;
         }
+        if (tl == 0)
+#pragma unroll
+            for (int m = 0; m < MB; ++m)
+                if (m < mb) epilogue<EPI>(c, a, row0 + m, cra, crb, acc[m][0], acc[m][1]);
     }
 }
 
@@ -728,10 +780,16 @@ cudaError_t launch_set_desc(StepDesc* d_desc, int32_t* d_ids, const DescInit& p,
     return cudaGetLastError();
 }
 
+// Dynamic shared memory of a GEMV launch: the limbs (96 bytes) and exponent (4 bytes) of every
+// block of every batch row of the pass.
+constexpr size_t gemv_smem_bytes(int mb, int k) { return (size_t)mb * (k / 32) * (6 * 16 + 4); }
+constexpr int kGemvMaxRowsLongK = 4;   // rows per pass when K > 4096 (the limbs of 8 rows would not fit)
+
 template <int MB, int EPI>
 static cudaError_t configure_gemv_t() {
+    const int k = MB > kGemvMaxRowsLongK ? 4096 : kMaxGemvK;
     return cudaFuncSetAttribute(gemv_kernel<MB, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)(MB * kMaxGemvK * sizeof(float)));
+                                (int)gemv_smem_bytes(MB, k));
 }
 
 template <int EPI>
@@ -739,6 +797,7 @@ static cudaError_t configure_gemv_e() {
     cudaError_t e = configure_gemv_t<1, EPI>();
     if (e == cudaSuccess) e = configure_gemv_t<2, EPI>();
     if (e == cudaSuccess) e = configure_gemv_t<4, EPI>();
+    if (e == cudaSuccess) e = configure_gemv_t<8, EPI>();
     return e;
 }
 
@@ -752,36 +811,53 @@ cudaError_t configure_kernels() {
     return e;
 }
 
+// Team size of a GEMV launch: at most kBPL blocks per lane and row, then doubled (up to 256 lanes,
+// and not past one lane per block) until the launch has about 96 K lanes, so that a matrix with
+// few units still spreads its bytes over the whole GPU.
+int gemv_team(int64_t units, int NB) {
+    int team = 8;
+    while (team * kBPL < NB) team *= 2;
+    while (team < 256 && team < NB && units * team < 96 * 1024) team *= 2;
+    return team;
+}
+
 template <int MB, int EPI>
-static cudaError_t launch_gemv_t(const Ctx& c, const GemvArgs& a, int rows, int grid, cudaStream_t st) {
-    const size_t smem = (size_t)MB * a.W.k * sizeof(float);
+static cudaError_t launch_gemv_t(const Ctx& c, const GemvArgs& a, int rows, cudaStream_t st) {
+    const int team = gemv_team(a.n_units, a.W.k / 32);
+    const int teams = kGemvThreads / team;
+    const int grid = (int)((a.n_units + teams - 1) / teams);
+    const size_t smem = gemv_smem_bytes(MB, a.W.k);
     for (int r0 = 0; r0 < rows; r0 += MB) {
         const int mb = rows - r0 < MB ? rows - r0 : MB;
-        gemv_kernel<MB, EPI><<<grid, 256, smem, st>>>(c, a, r0, mb);
+        gemv_kernel<MB, EPI><<<grid, kGemvThreads, smem, st>>>(c, a, r0, mb, team);
     }
     return cudaGetLastError();
 }
 
 template <int EPI>
-static cudaError_t launch_gemv_e(const Ctx& c, const GemvArgs& a, int rows, int grid, cudaStream_t st) {
-    if (rows <= 1) return launch_gemv_t<1, EPI>(c, a, rows, grid, st);
-    if (rows == 2) return launch_gemv_t<2, EPI>(c, a, rows, grid, st);
-    return launch_gemv_t<4, EPI>(c, a, rows, grid, st);
+static cudaError_t launch_gemv_e(const Ctx& c, const GemvArgs& a, int rows, cudaStream_t st) {
+    if (rows <= 1) return launch_gemv_t<1, EPI>(c, a, rows, st);
+    if (rows == 2) return launch_gemv_t<2, EPI>(c, a, rows, st);
+    if (rows <= 4 || a.W.k > 4096) return launch_gemv_t<4, EPI>(c, a, rows, st);
+    return launch_gemv_t<8, EPI>(c, a, rows, st);
 }
 
-cudaError_t launch_gemv(const Ctx& c, const GemvArgs& a, int epi, int rows, int grid, cudaStream_t st) {
+cudaError_t launch_gemv(const Ctx& c, const GemvArgs& a, int epi, int rows, cudaStream_t st) {
+    if (rows <= 0 || a.n_units <= 0) return cudaSuccess;
     switch (epi) {
-        case EPI_PLAIN: return launch_gemv_e<EPI_PLAIN>(c, a, rows, grid, st);
-        case EPI_QKV: return launch_gemv_e<EPI_QKV>(c, a, rows, grid, st);
-        case EPI_GATE: return launch_gemv_e<EPI_GATE>(c, a, rows, grid, st);
-        case EPI_RESID: return launch_gemv_e<EPI_RESID>(c, a, rows, grid, st);
-        default: return launch_gemv_e<EPI_LOGITS>(c, a, rows, grid, st);
+        case EPI_PLAIN: return launch_gemv_e<EPI_PLAIN>(c, a, rows, st);
+        case EPI_QKV: return launch_gemv_e<EPI_QKV>(c, a, rows, st);
+        case EPI_GATE: return launch_gemv_e<EPI_GATE>(c, a, rows, st);
+        case EPI_RESID: return launch_gemv_e<EPI_RESID>(c, a, rows, st);
+        default: return launch_gemv_e<EPI_LOGITS>(c, a, rows, st);
     }
 }
 
-cudaError_t launch_repack_q4(const uint8_t* raw, int64_t nblocks, uint4* nib, uint16_t* scale, cudaStream_t st) {
+cudaError_t launch_repack_q4(const uint8_t* raw, int64_t nblocks, uint4* nib, uint16_t* scale, cudaStream_t st,
+                             int* big_scale) {
+    if (nblocks <= 0) return cudaSuccess;
     const int64_t grid = (nblocks + 255) / 256;
-    repack_q4_kernel<<<(unsigned)grid, 256, 0, st>>>(raw, nblocks, nib, scale);
+    repack_q4_kernel<<<(unsigned)grid, 256, 0, st>>>(raw, nblocks, nib, scale, big_scale);
     return cudaGetLastError();
 }
 

@@ -35,9 +35,14 @@ struct DescInit {
 cudaError_t configure_kernels();
 cudaError_t launch_set_state(StreamState* dst, const StreamState& value, cudaStream_t st);
 cudaError_t launch_set_desc(StepDesc* d_desc, int32_t* d_ids, const DescInit& p, cudaStream_t st);
-cudaError_t launch_repack_q4(const uint8_t* raw, int64_t nblocks, uint4* nib, uint16_t* scale, cudaStream_t st);
+// Raw Q4_0 blocks -> the nibble and scale planes; big_scale (may be NULL) is set to 1 when a scale's
+// magnitude is above 4 (the tensor-core product's limit).
+cudaError_t launch_repack_q4(const uint8_t* raw, int64_t nblocks, uint4* nib, uint16_t* scale, cudaStream_t st,
+                             int* big_scale = nullptr);
 cudaError_t launch_dequant_q4(const Q4Dev& w, float* out, cudaStream_t st);
-cudaError_t launch_gemv(const Ctx& c, const GemvArgs& a, int epi, int rows, int grid, cudaStream_t st);
+// The batched Q4 GEMV of the step (and of the isolated f32 / bf16 matmul): one launch per pass of
+// up to 8 batch rows (4 when K > 4096), each pass reading the weights once.
+cudaError_t launch_gemv(const Ctx& c, const GemvArgs& a, int epi, int rows, cudaStream_t st);
 cudaError_t launch_embed(const Ctx& c, cudaStream_t st);
 cudaError_t launch_attention(const Ctx& c, int layer, cudaStream_t st);
 cudaError_t launch_finish(const Ctx& c, cudaStream_t st);

@@ -32,6 +32,7 @@
 #include <cstdlib>
 
 #include "kernels.h"
+#include "dp4a.cuh"
 #include "mega.h"
 
 namespace stt {
@@ -183,19 +184,6 @@ __device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((ui
 
 // consumer-only CTA barrier (the producer warp never joins it)
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory"); }
-
-__device__ __forceinline__ int dp4a_su(int a, uint32_t b, int c) {
-    int d;
-    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-__device__ __forceinline__ int dp4a_ss(int a, uint32_t b, int c) {
-    int d;
-    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-// exact int -> float for |v| < 2^22
-__device__ __forceinline__ float i2f(int v) { return __int_as_float(0x4B400000 + v) - 12582912.0f; }
 
 __device__ __forceinline__ unsigned long long globaltimer() {
     unsigned long long t;
@@ -585,34 +573,10 @@ __device__ void producer_drain(Smem& sm, uint32_t issued) {
 
 // ------------------------------------------------------------------------------ input vectors
 
-// dp4a limbs of one quad (elements 4q .. 4q+3) of block b = q / 8; called by all 32 lanes of a
-// warp with 8 consecutive lanes holding the 8 quads of a block.
+// dp4a limbs of one quad (elements 4q .. 4q+3) of block b = q / 8 into the CTA's input vector;
+// called by all 32 lanes of a warp with 8 consecutive lanes holding the 8 quads of a block.
 __device__ __forceinline__ void quad_limbs(Smem& sm, int q, int NB, float4 v) {
-    const int b = q >> 3, g = q & 7;
-    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
-    // max < 2^e with e = biased exponent - 126; scale the block by 2^(23 - e)
-    int e = m > 0.0f ? (int)((__float_as_uint(m) >> 23) & 0xFF) - 126 : 0;
-    e = max(-96, min(e, 120));
-    const float up = __uint_as_float((uint32_t)(127 + 23 - e) << 23);
-    const float vals[4] = {v.x, v.y, v.z, v.w};
-    uint32_t w0 = 0, w1 = 0, w2 = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        int X = __float2int_rn(vals[i] * up);
-        X = max(-(1 << 23), min(X, (1 << 23) - 1));
-        w0 |= (uint32_t)(X & 0xFF) << (8 * i);
-        w1 |= (uint32_t)((X >> 8) & 0xFF) << (8 * i);
-        w2 |= (uint32_t)((X >> 16) & 0xFF) << (8 * i);
-    }
-    uint32_t* L = reinterpret_cast<uint32_t*>(sm.limbs);
-    const int base = g < 4 ? 0 : 3;
-    L[((base + 0) * NB + b) * 4 + (g & 3)] = w0;
-    L[((base + 1) * NB + b) * 4 + (g & 3)] = w1;
-    L[((base + 2) * NB + b) * 4 + (g & 3)] = w2;
-    if (g == 0) sm.xs[b] = __uint_as_float((uint32_t)(127 + e - 27) << 23);
+    quad_limbs_store(sm.limbs, sm.xs, q, NB, v, true);
 }
 
 // Sum over each group of W consecutive lanes.
@@ -750,28 +714,6 @@ __device__ __forceinline__ bool prep_any(const MegaArgs& P, const uint64_t* ll, 
 }
 
 // ------------------------------------------------------------------------------ GEMV
-
-// 16 * sum over one Q4_0 block of (nibble - 8) * X in fixed point (S0 + 256 S1 + 65536 S2)
-__device__ __forceinline__ float block_dp4a(const uint4 q, const uint4* L) {
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-    const uint32_t l0[4] = {L[0].x, L[0].y, L[0].z, L[0].w}, l1[4] = {L[1].x, L[1].y, L[1].z, L[1].w};
-    const uint32_t l2[4] = {L[2].x, L[2].y, L[2].z, L[2].w}, h0[4] = {L[3].x, L[3].y, L[3].z, L[3].w};
-    const uint32_t h1[4] = {L[4].x, L[4].y, L[4].z, L[4].w}, h2[4] = {L[5].x, L[5].y, L[5].z, L[5].w};
-    int s0 = 0, s1 = 0, s2 = 0;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        // 16 * (nibble - 8) as signed bytes: low nibbles shifted up, high nibbles in place
-        const int lo = (int)(((words[w] << 4) & 0xF0F0F0F0u) ^ 0x80808080u);
-        const int hi = (int)((words[w] & 0xF0F0F0F0u) ^ 0x80808080u);
-        s0 = dp4a_su(lo, l0[w], s0);
-        s1 = dp4a_su(lo, l1[w], s1);
-        s2 = dp4a_ss(lo, l2[w], s2);
-        s0 = dp4a_su(hi, h0[w], s0);
-        s1 = dp4a_su(hi, h1[w], s1);
-        s2 = dp4a_ss(hi, h2[w], s2);
-    }
-    return __fmaf_rn(i2f(s2), 65536.0f, __fmaf_rn(i2f(s1), 256.0f, i2f(s0)));
-}
 
 // One GEMV phase over this CTA's units (row pairs; linear_in: gate/value pairs), in segment
 // order.  The residual phases (7 units) give each unit two warps; the others give each unit a

@@ -97,6 +97,9 @@ SIGNATURES = {
     "stt_stream_feed_frames": (C.c_int, [P, C.c_int, C.c_int, U32P, I32P]),
     "stt_stream_feed_frames_device": (C.c_int, [P, C.c_int, C.c_int, P, P, P]),
     "stt_streams_feed_frame_device": (C.c_int, [P, I32P, C.c_int, P, P, P]),
+    "stt_streams_submit_frame": (C.c_int, [P, I32P, C.c_int, U32P, C.POINTER(C.c_int64)]),
+    "stt_streams_poll_frame": (C.c_int, [P, C.c_int64, I32P, C.POINTER(C.c_int)]),
+    "stt_streams_wait_frame": (C.c_int, [P, C.c_int64, I32P]),
     "stt_stream_flush": (C.c_int, [P, C.c_int, U32P, C.c_int, I32P]),
     "stt_stream_reset": (C.c_int, [P, C.c_int, C.c_int]),
     "stt_stream_reset_async": (C.c_int, [P, C.c_int, C.c_int, P]),

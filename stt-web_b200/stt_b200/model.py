@@ -158,6 +158,16 @@ class LayerCaches:
                                            _ptr(out, C.c_int32)), "stt_streams_feed_frame")
         return out
 
+    def submit_frame(self, stream_ids: Sequence[int], audio: np.ndarray) -> "PendingFrame":
+        """Queues one batched feed_frame step without waiting (SttStream::submit_frame_gpu,
+        stream.rs:117-138); its tokens are taken later from the returned PendingFrame."""
+        ids = np.ascontiguousarray(np.asarray(stream_ids, dtype=np.int32))
+        a = _u32(audio).reshape(ids.size, -1)
+        t = C.c_int64()
+        check(lib().stt_streams_submit_frame(self._h, _ptr(ids, C.c_int32), ids.size, _ptr(a, C.c_uint32),
+                                             C.byref(t)), "stt_streams_submit_frame")
+        return PendingFrame(self, t.value, ids.size)
+
     def state(self, stream_id: int) -> dict:
         st = stt_stream_state()
         check(lib().stt_stream_get_state(self._h, stream_id, C.byref(st)), "stt_stream_get_state")
@@ -166,6 +176,27 @@ class LayerCaches:
 
     def reset(self, stream_id: int = 0, keep_buffers: bool = False) -> None:
         check(lib().stt_stream_reset(self._h, stream_id, 1 if keep_buffers else 0), "stt_stream_reset")
+
+
+class PendingFrame:
+    """A submitted batched frame (the analogue of a PendingFrame of take_batch_pending,
+    stream.rs:146-183): poll() returns its tokens once its step has completed (None before),
+    wait() blocks for them.  Tokens are -1 where a stream is still inside the text delay."""
+
+    def __init__(self, cache: "LayerCaches", ticket: int, n: int):
+        self.cache, self.ticket, self.n = cache, ticket, n
+
+    def poll(self) -> Optional[np.ndarray]:
+        out = np.empty(self.n, dtype=np.int32)
+        ready = C.c_int()
+        check(lib().stt_streams_poll_frame(self.cache._h, self.ticket, _ptr(out, C.c_int32), C.byref(ready)),
+              "stt_streams_poll_frame")
+        return out if ready.value else None
+
+    def wait(self) -> np.ndarray:
+        out = np.empty(self.n, dtype=np.int32)
+        check(lib().stt_streams_wait_frame(self.cache._h, self.ticket, _ptr(out, C.c_int32)), "stt_streams_wait_frame")
+        return out
 
 
 class SttStream:

@@ -14,8 +14,9 @@ initial text token 0, the benchmark's seed and audio).
                    stream checked
 
 Token comparison and the near-tie accounting are those of tests/parity.py: a difference is only
-excused where the oracle's top-2 logit margin is below 2e-3, the excused flips are counted and
-printed, and the oracle then follows the GPU's token."""
+excused where the oracle's top-2 logit margin is below the measured logit agreement (1e-2 with bf16
+K/V, 2e-3 with f32 K/V), the excused flips are counted and printed, and the oracle then follows the
+GPU's token."""
 import ctypes as C
 import json
 import os
@@ -25,7 +26,7 @@ import pytest
 
 from conftest import GOLDEN
 from oracle import oracle as O
-from parity import EXEMPT_MARGIN, Follower, margins
+from parity import EXEMPT_MARGIN, EXEMPT_MARGIN_BF16_KV, Follower, margins
 import stt_b200
 from stt_b200._lib import check, lib
 from stt_b200.model import SttConfig
@@ -79,7 +80,7 @@ def test_config2_utterance_through_the_persistent_kernel(bench_model):
     audio = stt_b200.audio_tokens(SEED, 0, 750)
     cache = model.create_cache(1, "bf16")
     got = feed_frames_device(cache, 0, audio)      # one call: the benchmark's timed entry point
-    fol = Follower([om.stream(O.KV_BF16)])
+    fol = Follower([om.stream(O.KV_BF16)], exempt_margin=EXEMPT_MARGIN_BF16_KV)
     for f in range(750):
         fol.step([0], audio[f:f + 1], [got[f]], f"frame {f}")
     print(fol.report("configuration 2"))
@@ -102,7 +103,7 @@ def test_config2_utterance_through_the_persistent_kernel(bench_model):
         d = float(np.abs(lg[0] - ref).max())
         worst = max(worst, d)
         assert d < LOGIT_TOL, (p, d)
-        assert int(am[0]) == int(np.argmax(ref)) or margins(ref)[0] < EXEMPT_MARGIN, p
+        assert int(am[0]) == int(np.argmax(ref)) or margins(ref)[0] < EXEMPT_MARGIN_BF16_KV, p
         stt_b200.SttStream(cfg, c2, 0).set_last_text_token(int(am[0]))  # feed_frame's update past the delay
         pos = p + 1
     print(f"max |logit - oracle| at frames {[int(x) for x in z['frames']]}: {worst:.3g}")
@@ -113,7 +114,7 @@ def test_config3_staggered_streams(bench_model):
     offs = [round(i * 374 / 63) for i in range(64)]
     checked = [0, 9, 18, 27, 36, 45, 54, 63]           # offsets 0, 53, 107, 160, 214, 267, 321, 374
     cache = model.create_cache(64, "bf16")
-    fol = Follower([om.stream(O.KV_BF16) for _ in range(64)])
+    fol = Follower([om.stream(O.KV_BF16) for _ in range(64)], exempt_margin=EXEMPT_MARGIN_BF16_KV)
     pre = {}
     # pre-roll every stream alone through the persistent kernel, as the benchmark does
     for s in range(64):
@@ -155,7 +156,7 @@ def test_config4_job_first_streams(bench_model):
                                                   C.c_void_p(dt[f].data_ptr()), C.c_void_p(ts.cuda_stream)), "step")
     torch.cuda.synchronize()
     got = dt.cpu().numpy()
-    fol = Follower([om.stream(O.KV_BF16) for _ in range(K)])
+    fol = Follower([om.stream(O.KV_BF16) for _ in range(K)], exempt_margin=EXEMPT_MARGIN_BF16_KV)
     for f in range(F):
         fol.step(list(range(K)), aud[f, :K], got[f, :K], f"frame {f}")
     print(fol.report("configuration 4, streams 0..15"))
@@ -165,18 +166,21 @@ def test_config4_job_first_streams(bench_model):
     cache.close()
 
 
-def test_config4_two_full_tiles_every_stream(bench_model):
+@pytest.mark.parametrize("kv", ["bf16", "f32"])
+def test_config4_two_full_tiles_every_stream(bench_model, kv):
     """260 streams, 8 frames from position 0 (the delay, then emitted tokens): every stream's
-    tokens, and its next text token (the argmax after the limit-cycle rule) after every frame."""
+    tokens, and its next text token (the argmax after the limit-cycle rule) after every frame.
+    With f32 K/V no K or V element can land on the other side of a bf16 rounding, so the GPU
+    follows the oracle more closely still."""
     g, cfg, model, om = bench_model
     S = 260
-    cache = model.create_cache(S, "bf16")
-    fol = Follower([om.stream(O.KV_BF16) for _ in range(S)])
+    cache = model.create_cache(S, kv)
+    fol = Follower([om.stream(O.KV_BF16 if kv == "bf16" else 0) for _ in range(S)],
+                   exempt_margin=EXEMPT_MARGIN_BF16_KV if kv == "bf16" else EXEMPT_MARGIN)
     for f in range(8):
         audio = np.stack([stt_b200.audio_tokens(SEED, 1000 + s, 1, first_frame=f)[0] for s in range(S)])
         got = feed_frame_device(cache, list(range(S)), audio)
-        fol.step(list(range(S)), audio, got, f"frame {f}")
-        if f < 5:   # inside the delay nothing is emitted: compare the next text token itself
-            for s in range(S):
-                assert cache.state(s)["last_text_token"] == fol.refs[s].state()["last_text_token"], (f, s)
-    print(fol.report("260 streams x 8 frames"))
+        # inside the delay nothing is emitted: the next text token and the limit-cycle history
+        # are compared instead
+        fol.step(list(range(S)), audio, got, f"frame {f}", states=cache.state)
+    print(fol.report(f"260 streams x 8 frames, {kv} K/V"))

@@ -142,3 +142,42 @@ def test_subsets_of_streams_step_independently():
         assert [None if t < 0 else int(t) for t in got] == exp, f
     for s in range(n):
         assert cache.state(s)["offset"] == refs[s].state()["offset"]
+
+
+def test_submitted_frames_resolve_later_in_any_order():
+    """stt_streams_submit_frame queues frames with the token fed back on the device and returns at
+    once; the tokens are taken later (poll or wait, in any order), as take_batch_pending and the
+    bindings' asynchronous readback do (stream.rs:117-183, web/bindings.rs:432-489)."""
+    from stt_b200._lib import STT_E_INVALID_ARG, STT_E_STATE
+    g, cfg, model, om = small_model(seed=33)
+    n = 18
+    cache = model.create_cache(n, "bf16")
+    refs = [om.stream(O.KV_BF16) for _ in range(n)]
+    rng = np.random.default_rng(9)
+    frames = [rng.integers(0, 300, (n, 4)) for _ in range(12)]
+    ids = list(range(n))
+    pending = [cache.submit_frame(ids, a) for a in frames]    # nothing waits here
+    exp = [O.feed_frame_batch(refs, a)[0] for a in frames]
+    # take them back out of order: the last by wait, the others by polling
+    last = pending[-1].wait()
+    assert [None if t < 0 else int(t) for t in last] == exp[-1]
+    for p, e in zip(pending[:-1], exp[:-1]):
+        got = None
+        while got is None:
+            got = p.poll()
+        assert [None if t < 0 else int(t) for t in got] == e
+    # a ticket is taken once
+    with pytest.raises(stt_b200.SttError) as err:
+        pending[0].wait()
+    assert err.value.code == STT_E_INVALID_ARG
+    # 64 frames may be outstanding; the 65th waits for the caller to take the oldest
+    sub = [cache.submit_frame([0], rng.integers(0, 300, (1, 4))) for _ in range(64)]
+    with pytest.raises(stt_b200.SttError) as err:
+        cache.submit_frame([0], rng.integers(0, 300, (1, 4)))
+    assert err.value.code == STT_E_STATE
+    sub[0].wait()
+    cache.submit_frame([0], rng.integers(0, 300, (1, 4))).wait()
+    for p in sub[1:]:
+        p.wait()
+    for s in range(1, n):
+        assert cache.state(s)["offset"] == refs[s].state()["offset"] == 12
