@@ -435,6 +435,24 @@ def main():
                     "us_per_product": {"in_proj": us[0], "out_proj": us[1], "linear_in": us[2], "linear_out": us[3],
                                        "head": us[4]},
                     "gemm_share_of_step": per_step_us / (ms / args.steps / F * 1000.0)}
+    # the same job with the two-product precision of the tensor-core layer products (activations
+    # rounded to f16): a third less tensor work (stt_streams_set_product_precision)
+    f16x2 = None
+    if roofline is not None and not args.no_extras:
+        check(lib().stt_streams_set_product_precision(cache._h, 1), "set_product_precision")
+        batched_job(model, cache, S, F, da, dt, lib, check, ts)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(ts)
+        for _ in range(2):
+            batched_job(model, cache, S, F, da, dt, lib, check, ts)
+        e1.record(ts)
+        torch.cuda.synchronize()
+        ms2 = max_over_ranks(e0.elapsed_time(e1))
+        barrier()
+        check(lib().stt_streams_set_product_precision(cache._h, 0), "set_product_precision")
+        f16x2 = {"frames_per_s": total_streams * F * 2 / (ms2 / 1000.0), "ms_per_step": ms2 / 2,
+                 "note": "two f16 products per weight (activation rounded to f16) instead of three"}
     step_bytes = algorithmic_bytes_batched([0] * S, 0, F)
     step_ms = ms / args.steps / F
     line = {
@@ -451,6 +469,7 @@ def main():
                           "hbm_frac": step_bytes / (step_ms / 1000.0) / 1e9 / pk["hbm_gbs"],
                           "real_time_streams_per_gpu": S * 80.0 / step_ms},
         "tokens_vs_oracle": token_check,
+        "products_f16x2": f16x2,
         "load": load,
     }
     cache.close()

@@ -187,6 +187,18 @@ int stt_stream_reset(stt_streams* streams, int stream_id, int keep_buffers);
  * legacy default stream) behind work already queued there, without waiting for the device. */
 int stt_stream_reset_async(stt_streams* streams, int stream_id, int keep_buffers, void* cuda_stream);
 
+/* Precision of the layer products of batched steps on the tensor cores (batches of at least
+ * tensor_core_min_batch streams; no counterpart in the reference, whose f32 shader has one).  Each
+ * dequantised weight is split exactly into two f16 parts, w = w_hi + w_lo, and accumulated in f32:
+ *   STT_PRODUCTS_F16X3 (default): the activation is split too, x = x_hi + x_lo, and three MMAs add
+ *     w_hi.x_hi + w_hi.x_lo + w_lo.x_hi: about 22 significant bits per product, close to f32;
+ *   STT_PRODUCTS_F16X2: the activation is rounded to f16 (11 bits) and two MMAs add
+ *     w_hi.x + w_lo.x: a third less tensor work, about 2^-12 relative error per activation.
+ * Applies to the set's later batched steps (their CUDA graphs are captured again). */
+#define STT_PRODUCTS_F16X3 0
+#define STT_PRODUCTS_F16X2 1
+int stt_streams_set_product_precision(stt_streams* streams, int precision);
+
 /* Replaces SttStream::set_last_text_token (stream.rs:190-192). */
 int stt_stream_set_last_text_token(stt_streams* streams, int stream_id, uint32_t token);
 

@@ -669,6 +669,7 @@ struct stt_streams {
     HostBuf pend_in, pend_out;    // pinned: per slot the audio ids in, the tokens and step descriptor out
     DevBuf pend_audio, pend_tok;  // device: per slot the audio ids and the emitted tokens
     int64_t next_ticket = 0;
+    int product_precision = STT_PRODUCTS_F16X3;  // batched tensor-core products
 };
 
 namespace {
@@ -737,23 +738,24 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
         float* part = s->d_tc_part;
         int* err = &s->d_desc->error;  // a GEMM timeout raises STT_E_DEVICE_FLAG like any step kernel
         int slices = 0;
+        const bool x_lo = s->product_precision == STT_PRODUCTS_F16X3;
         CUDA_TRY(launch_tc_prep(s->d_x, m->h_layers[0].norm1, m->D, n, s->d_x16, st));
         for (int l = 0; l < m->L; ++l) {
             const LayerDev& L = m->h_layers[l];
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 0], s->d_x16, n, part, err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 0], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
             GemvArgs a{};
             a.W = L.qkv; a.out = s->d_qkv; a.ldo = 3 * m->D; a.layer = l; a.n_units = 3 * m->D / 2;
             CUDA_TRY(launch_tc_epilogue(c, a, EPI_QKV, n, part, slices, st));
             CUDA_TRY(launch_attention(ca, l, st));
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 1], s->d_x16, n, part, err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 1], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
             CUDA_TRY(launch_tc_resid_norm(s->d_x, part, slices, n, m->D, L.norm2, s->d_x16, st));
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 2], s->d_x16, n, part, err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 2], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
             CUDA_TRY(launch_tc_gate(part, slices, n, m->F, s->d_x16, st));
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 3], s->d_x16, n, part, err, m->num_sms, &slices, st));
+            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 3], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
             const float* next_norm = l + 1 < m->L ? m->h_layers[l + 1].norm1 : m->out_norm;
             CUDA_TRY(launch_tc_resid_norm(s->d_x, part, slices, n, m->D, next_norm, s->d_x16, st));
         }
-        CUDA_TRY(launch_tc_product(m->tc_w[4 * m->L], s->d_x16, n, part, err, m->num_sms, &slices, st));
+        CUDA_TRY(launch_tc_product(m->tc_w[4 * m->L], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
         GemvArgs a{};
         a.W = m->head; a.out = s->d_logits; a.ldo = m->V; a.n_units = (m->V + 1) / 2;
         CUDA_TRY(launch_tc_epilogue(c, a, EPI_LOGITS, n, part, slices, st));
@@ -1278,6 +1280,21 @@ extern "C" int stt_stream_reset_async(stt_streams* s, int stream_id, int keep_bu
     // the offset mirror is exact; the other host fields are refreshed on the next synchronous call
     s->h_state[stream_id] = fresh;
     s->state_stale = true;
+    return STT_OK;
+}
+
+extern "C" int stt_streams_set_product_precision(stt_streams* s, int precision) {
+    clear_error();
+    if (!s) return set_error(STT_E_INVALID_ARG, "NULL streams");
+    if (precision != STT_PRODUCTS_F16X3 && precision != STT_PRODUCTS_F16X2)
+        return set_error(STT_E_INVALID_ARG, "precision %d unknown", precision);
+    if (precision == s->product_precision) return STT_OK;
+    DeviceScope ds(s->m->device);
+    CUDA_TRY(cudaStreamSynchronize(s->stream));
+    for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);  // recaptured with the new products
+    s->graphs.clear();
+    s->graph_kernels.clear();
+    s->product_precision = precision;
     return STT_OK;
 }
 

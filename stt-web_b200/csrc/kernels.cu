@@ -236,8 +236,9 @@ __device__ __forceinline__ void epilogue(const Ctx& c, const GemvArgs& a, int bm
 // past 32 the team spans warps), each taking blocks tl, tl + team, ... (at most kBPL of them), so
 // that all of a unit's weight bytes are in flight at once and one launch keeps about 128 K lanes
 // busy.  The CTA first issues its first unit's weight loads, then converts the input rows to limbs
-// in shared memory while they are in flight.  Deterministic: the team sums its lanes, then its
-// warps, in a fixed order.
+// in shared memory while they are in flight; launched as a programmatic dependent, those weight
+// loads also overlap the end of the previous kernel.  Deterministic: the team sums its lanes, then
+// its warps, in a fixed order.
 constexpr int kBPL = 4;           // blocks per team lane and row, at most
 constexpr int kGemvThreads = 256;
 
@@ -275,7 +276,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(Ctx c, GemvArgs a, i
 
     int64_t u = (int64_t)blockIdx.x * teams + my_team;
     int ra = 0, rb = -1;
+    pdl_trigger();
     if (u < a.n_units) load_unit(u, &ra, &rb);  // weights first: they do not depend on the input
+    // launched as a programmatic dependent: the input (and, for EPI_RESID, the output) belong to the
+    // previous kernel of the stream until this wait returns
+    pdl_wait();
     load_limbs(a.in, a.in_bf16, K, row0, mb, a.norm, L, xs, red);
     int parity = 0;
     for (; u < a.n_units; u += nteams) {
@@ -829,9 +834,11 @@ static cudaError_t launch_gemv_t(const Ctx& c, const GemvArgs& a, int rows, cuda
     const size_t smem = gemv_smem_bytes(MB, a.W.k);
     for (int r0 = 0; r0 < rows; r0 += MB) {
         const int mb = rows - r0 < MB ? rows - r0 : MB;
-        gemv_kernel<MB, EPI><<<grid, kGemvThreads, smem, st>>>(c, a, r0, mb, team);
+        const cudaError_t e = launch_pdl(gemv_kernel<MB, EPI>, dim3(grid), dim3(kGemvThreads), smem, st, c, a, r0, mb,
+                                         team);
+        if (e != cudaSuccess) return e;
     }
-    return cudaGetLastError();
+    return cudaSuccess;
 }
 
 template <int EPI>

@@ -763,10 +763,10 @@ cudaError_t launch_tc_prep(const float* in, const float* alpha, int K, int rows,
 }
 
 cudaError_t launch_tc_product(const TcWeight& tw, const __half* x16, int rows, float* part, int* err, int num_sms,
-                              int* slices, cudaStream_t st) {
+                              int* slices, cudaStream_t st, bool x_lo) {
     const TcPlan p = make_plan(tw.n, tw.k, rows, num_sms);
     *slices = p.slices;
-    return launch_gemm(tw, x16, 1, rows, p, part, err, st);
+    return launch_gemm(tw, x16, x_lo ? 1 : 0, rows, p, part, err, st);
 }
 
 cudaError_t launch_tc_resid_norm(float* x, const float* part, int slices, int rows, int D, const float* alpha,

@@ -47,8 +47,10 @@ void tc_batch_tiles(int rows, int* nt, int* rows_pad);
 cudaError_t launch_tc_prep(const float* in, const float* alpha, int K, int rows, __half* x16, cudaStream_t st);
 // The GEMM: K-slice partial sums part[slices][rows][tw.n] of the weight times the x16 rows; the
 // slice count is returned in *slices.  A timeout records -5 in *err (a step descriptor's error word).
+// x_lo: the activations' lo parts take part (three products, about 22 significant bits); without
+// them the activations count as their f16 hi parts (two products).
 cudaError_t launch_tc_product(const TcWeight& tw, const __half* x16, int rows, float* part, int* err, int num_sms,
-                              int* slices, cudaStream_t st);
+                              int* slices, cudaStream_t st, bool x_lo = true);
 // x[rows][D] += the slices (in order); x16 = RMSNorm(x) * alpha.
 cudaError_t launch_tc_resid_norm(float* x, const float* part, int slices, int rows, int D, const float* alpha,
                                  __half* x16, cudaStream_t st);

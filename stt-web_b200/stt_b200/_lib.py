@@ -22,6 +22,9 @@ STT_E_STATE = -6
 STT_KV_BF16 = 0
 STT_KV_F32 = 1
 
+STT_PRODUCTS_F16X3 = 0
+STT_PRODUCTS_F16X2 = 1
+
 GGML_F32, GGML_F16, GGML_Q4_0, GGML_BF16 = 0, 1, 2, 30
 
 
@@ -104,6 +107,7 @@ SIGNATURES = {
     "stt_stream_reset": (C.c_int, [P, C.c_int, C.c_int]),
     "stt_stream_reset_async": (C.c_int, [P, C.c_int, C.c_int, P]),
     "stt_stream_set_last_text_token": (C.c_int, [P, C.c_int, C.c_uint32]),
+    "stt_streams_set_product_precision": (C.c_int, [P, C.c_int]),
     "stt_stream_get_state": (C.c_int, [P, C.c_int, C.POINTER(stt_stream_state)]),
     "stt_q4_tensor_create": (C.c_int, [U8P, C.c_size_t, C.c_int, C.c_int, C.c_int, C.POINTER(P)]),
     "stt_q4_tensor_destroy": (C.c_int, [P]),

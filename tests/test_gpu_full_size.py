@@ -184,3 +184,65 @@ def test_config4_two_full_tiles_every_stream(bench_model, kv):
         # are compared instead
         fol.step(list(range(S)), audio, got, f"frame {f}", states=cache.state)
     print(fol.report(f"260 streams x 8 frames, {kv} K/V"))
+
+
+def test_full_size_q4_0_embeddings_from_shards():
+    """The reference's real checkpoint format at full size: Q4_0 embedding tables (as
+    scripts/quantize.py writes them) and the file split over shards at arbitrary byte boundaries,
+    one of them a single byte (ShardedCursor, gguf.rs:321-397).  The pipelined upload must give a
+    model that decodes like the oracle on the contiguous file, through the persistent kernel and
+    through a 16-stream tensor-core batch."""
+    import time
+    g = stt_b200.synth_gguf(stt_b200.SynthSpec(seed=77, embedding_dtype=2))
+    buf = g.array
+    cuts = [0, 123_456_789, 400_000_001, 400_000_002, 777_777_777, buf.size]
+    shards = [buf[a:b] for a, b in zip(cuts, cuts[1:])]
+    cfg = SttConfig(text_start_token=0)
+    t0 = time.perf_counter()
+    model = stt_b200.SttModel.from_shards(shards, config=cfg)
+    dt = time.perf_counter() - t0
+    print(f"loaded {buf.size / 1e9:.3f} GB from {len(shards)} shards in {dt * 1e3:.1f} ms ({buf.size / dt / 1e9:.1f} GB/s)")
+    assert model.info.embedding_dtype == 2 and model.info.q4_weight_bytes == 627_351_552
+    assert model.info.tensor_core_min_batch == 16
+    om = O.OracleModel(buf, text_start_token=0)
+    audio = stt_b200.audio_tokens(5, 0, 12)
+    cache = model.create_cache(16, "bf16")
+    got = stt_b200.SttStream(cfg, cache, 0).feed_frames(audio)
+    fol = Follower([om.stream(O.KV_BF16) for _ in range(16)], exempt_margin=EXEMPT_MARGIN_BF16_KV)
+    for f in range(12):
+        fol.step([0], audio[f:f + 1], [got[f]], f"stream 0 frame {f}")
+    ids = list(range(1, 16))
+    for f in range(8):
+        a = np.stack([stt_b200.audio_tokens(5, s, 1, first_frame=f)[0] for s in [0] + ids])
+        got = feed_frame_device(cache, [0] + ids, a)
+        fol.step([0] + ids, a, got, f"batched frame {f}", states=cache.state)
+    print(fol.report("Q4_0 embeddings, sharded file"))
+    model.close()
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+def test_batched_product_precision_logits(bench_model, precision):
+    """Raw batched steps of 64 full-size streams on the tensor cores, logits against the oracle,
+    for both product precisions: three f16 products per weight (the default, activation split into
+    two f16 parts) and two (activation rounded to f16).  Both must stay inside the 2e-2 bound;
+    the printed maxima show what the third product buys."""
+    g, cfg, model, om = bench_model
+    from stt_b200._lib import lib as L
+    n = 64
+    cache = model.create_cache(n, "bf16")
+    assert L().stt_streams_set_product_precision(cache._h, precision) == 0
+    refs = [om.stream(O.KV_BF16) for _ in range(n)]
+    texts = [0] * n
+    worst = 0.0
+    flips = 0
+    for step in range(4):
+        audio = np.stack([stt_b200.audio_tokens(21, s, 1, first_frame=step)[0] for s in range(n)])
+        lg, am = cache.forward(list(range(n)), audio, texts)
+        lo, ao = O.forward_batch(refs, audio, texts)
+        worst = max(worst, float(np.abs(lg - lo).max()))
+        mg = margins(lo)
+        flips += int(((am != ao) & (mg >= EXEMPT_MARGIN_BF16_KV)).sum())
+        texts = [int(x) for x in ao]            # both sides continue from the oracle's tokens
+    print(f"product precision {precision}: max |logit - oracle| over 64 streams x 4 steps = {worst:.3g}")
+    assert worst < LOGIT_TOL
+    assert flips == 0
