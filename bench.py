@@ -310,6 +310,15 @@ def main():
                     help="frames per stream of the headline job; only a shorter profiling case sets it")
     ap.add_argument("--streams", type=int, default=JOB_STREAMS,
                     help="streams of the headline job; only a smaller profiling case sets it")
+    ap.add_argument("--only", default="all", choices=["all", "job", "stream1", "streams64", "sweep", "frame"],
+                    help="profiling cases: run one workload alone and print what it measured; 'frame' pre-rolls "
+                         "--streams streams to --position with one persistent-kernel launch each, then times two "
+                         "batched frames (few launches before them, for a profiler's launch list)")
+    ap.add_argument("--position", type=int, default=129, help="position of the streams in the 'frame' case")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the per-call end-to-end timings (profiling cases)")
+    ap.add_argument("--window", type=int, default=750,
+                    help="sliding window of the model (K/V ring = window + 1 slots); only a profiling case "
+                         "that must hold little device memory lowers it")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -345,137 +354,169 @@ def main():
     t0 = time.perf_counter()
     g = synth.synth_gguf(synth.SynthSpec(seed=SEED, n_threads=nthreads))
     t1 = time.perf_counter()
-    cfg = stt_b200.SttConfig(text_start_token=0)   # initial text token 0 (benchmark config)
+    cfg = stt_b200.SttConfig(text_start_token=0, sliding_window=args.window)   # initial text token 0
     model = stt_b200.SttModel.from_buffer(g.address, g.length, device=local, config=cfg)
     t2 = time.perf_counter()   # the load synchronises the device before it returns
     load = {"gguf_bytes": g.length, "synth_s": round(t1 - t0, 3), "model_load_s": round(t2 - t1, 3),
             "model_load_gbs": round(g.length / (t2 - t1) / 1e9, 3)}
     g.close()
 
-    # ---------------------------------------------------------------- headline: configuration 4
-    total_streams, F = args.streams, args.frames
-    blk = shard.stream_block(total_streams, world, rank)
-    S = len(blk)
-    cache = model.create_cache(S, "bf16")
-    aud = np.stack([synth.audio_tokens(SEED, s, F) for s in blk], 1)   # [frame][stream][32]
-    da = torch.from_numpy(aud.astype(np.int32)).cuda()
-    dt = torch.empty(F, S, dtype=torch.int32, device="cuda")
-    for _ in range(args.warmup):
-        batched_job(model, cache, S, F, da, dt, lib, check, ts)
-    barrier()
-    with ClockSampler(local) as clk:
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ev0.record(ts)
-        for _ in range(args.steps):
+    line = {}
+    if args.only in ("all", "job"):
+        # ---------------------------------------------------------------- headline: configuration 4
+        total_streams, F = args.streams, args.frames
+        blk = shard.stream_block(total_streams, world, rank)
+        S = len(blk)
+        cache = model.create_cache(S, "bf16")
+        aud = np.stack([synth.audio_tokens(SEED, s, F) for s in blk], 1)   # [frame][stream][32]
+        da = torch.from_numpy(aud.astype(np.int32)).cuda()
+        dt = torch.empty(F, S, dtype=torch.int32, device="cuda")
+        for _ in range(args.warmup):
             batched_job(model, cache, S, F, da, dt, lib, check, ts)
-        ev1.record(ts)
-        torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    barrier()
-    ms = max_over_ranks(ms)
-    clocks = clk.summary()
-    job_tokens = dt.cpu().numpy()     # [frame][stream] of the last step
-    value = total_streams * F * args.steps / (ms / 1000.0)
-
-    # tokens of the job's first streams against the oracle's (tests/golden/bench_tokens.json)
-    token_check = None
-    fx = os.path.join(REPO, "tests", "golden", "bench_tokens.json")
-    if rank == 0 and os.path.exists(fx) and F == JOB_FRAMES:
-        fxd = json.load(open(fx))
-        ref = fxd["streams16_250"]
-        ties = {(t[0], t[1]): t[2] for t in fxd["near_ties"]}
-        k = min(len(ref), S)
-        first = {}
-        for s in range(k):
-            d = np.nonzero(job_tokens[:, s] != np.array(ref[s]))[0]
-            if d.size:
-                first[s] = int(d[0])
-        token_check = {"streams_compared": k, "frames": F, "identical_streams": k - len(first),
-                       # where a stream first differs, and the oracle's top-2 logit margin there
-                       "first_difference": {str(s): [f, ties.get((s, f))] for s, f in first.items()}}
-
-    # e2e: the same job through the public host-buffer call, one call per batched frame
-    e2e_steps = min(args.steps, 3)
-    audio_host = [np.ascontiguousarray(aud[f]) for f in range(F)]
-    ids = list(range(S))
-    for s in ids:                       # one untimed frame warms the host staging buffers
-        cache.reset(s)
-    cache.feed_frame(ids, audio_host[0])
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        for s in ids:
-            cache.reset(s)
-        for f in range(F):
-            cache.feed_frame(ids, audio_host[f])
-    e2e_s = time.perf_counter() - t0
-    barrier()
-    e2e_s = max_over_ranks(e2e_s)
-    e2e = total_streams * F * e2e_steps / e2e_s
-
-    # the step's kernels and its dominant kernel, the tcgen05 GEMM, timed per launch
-    nk = C.c_int()
-    check(lib().stt_debug_graph_kernels(cache._h, S, C.byref(nk)), "graph_kernels")
-    launches_per_step = S + F * (1 + nk.value)   # resets, then per frame the descriptor + the graph
-    roofline = None
-    if model.info.tensor_core_min_batch and S >= model.info.tensor_core_min_batch:
-        us = (C.c_double * 5)()
-        fl = (C.c_double * 5)()
-        check(lib().stt_debug_time_products(cache._h, S, 20, us, fl), "time_products")
-        per_step_us = 16 * (us[0] + us[1] + us[2] + us[3]) + us[4]
-        per_step_flops = 16 * (fl[0] + fl[1] + fl[2] + fl[3]) + fl[4]
-        achieved = per_step_flops / (per_step_us * 1e-6) / 1e12
-        peak_t = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
-        roofline = {"bound": "tensor", "kernel": "q4_tc_kernel (tcgen05 Q4_0 x f16 GEMM), the 65 products of a step",
-                    "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s", "frac": achieved / peak_t,
-                    "peak_kind": f"{pk_kind} sustained bf16", "traffic": TC_TRAFFIC_LINEAR_IN_512,
-                    "traffic_kernel": "one linear_in launch (16896 x 2048) at 512 rows",
-                    "useful_flops_per_launch": per_step_flops / 65, "us_per_launch": per_step_us / 65,
-                    "executed_mma_factor": 3,
-                    "us_per_product": {"in_proj": us[0], "out_proj": us[1], "linear_in": us[2], "linear_out": us[3],
-                                       "head": us[4]},
-                    "gemm_share_of_step": per_step_us / (ms / args.steps / F * 1000.0)}
-    # the same job with the two-product precision of the tensor-core layer products (activations
-    # rounded to f16): a third less tensor work (stt_streams_set_product_precision)
-    f16x2 = None
-    if roofline is not None and not args.no_extras:
-        check(lib().stt_streams_set_product_precision(cache._h, 1), "set_product_precision")
-        batched_job(model, cache, S, F, da, dt, lib, check, ts)
         barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(ts)
-        for _ in range(2):
+        with ClockSampler(local) as clk:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(ts)
+            for _ in range(args.steps):
+                batched_job(model, cache, S, F, da, dt, lib, check, ts)
+            ev1.record(ts)
+            torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        barrier()
+        ms = max_over_ranks(ms)
+        clocks = clk.summary()
+        job_tokens = dt.cpu().numpy()     # [frame][stream] of the last step
+        value = total_streams * F * args.steps / (ms / 1000.0)
+
+        # tokens of the job's first streams against the oracle's (tests/golden/bench_tokens.json)
+        token_check = None
+        fx = os.path.join(REPO, "tests", "golden", "bench_tokens.json")
+        if rank == 0 and os.path.exists(fx) and F == JOB_FRAMES:
+            fxd = json.load(open(fx))
+            ref = fxd["streams16_250"]
+            ties = {(t[0], t[1]): t[2] for t in fxd["near_ties"]}
+            k = min(len(ref), S)
+            first = {}
+            for s in range(k):
+                d = np.nonzero(job_tokens[:, s] != np.array(ref[s]))[0]
+                if d.size:
+                    first[s] = int(d[0])
+            token_check = {"streams_compared": k, "frames": F, "identical_streams": k - len(first),
+                           # where a stream first differs, and the oracle's top-2 logit margin there
+                           "first_difference": {str(s): [f, ties.get((s, f))] for s, f in first.items()}}
+
+        # e2e: the same job through the public host-buffer call, one call per batched frame
+        e2e_steps = 0 if args.no_e2e else min(args.steps, 3)
+        audio_host = [np.ascontiguousarray(aud[f]) for f in range(F)]
+        ids = list(range(S))
+        if e2e_steps:
+            for s in ids:                   # one untimed frame warms the host staging buffers
+                cache.reset(s)
+            cache.feed_frame(ids, audio_host[0])
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            for s in ids:
+                cache.reset(s)
+            for f in range(F):
+                cache.feed_frame(ids, audio_host[f])
+        e2e_s = time.perf_counter() - t0
+        barrier()
+        e2e_s = max_over_ranks(e2e_s)
+        e2e = total_streams * F * e2e_steps / e2e_s if e2e_steps else None
+
+        # the step's kernels and its dominant kernel, the tcgen05 GEMM, timed per launch
+        nk = C.c_int()
+        check(lib().stt_debug_graph_kernels(cache._h, S, C.byref(nk)), "graph_kernels")
+        launches_per_step = S + F * (1 + nk.value)   # resets, then per frame the descriptor + the graph
+        roofline = None
+        if model.info.tensor_core_min_batch and S >= model.info.tensor_core_min_batch:
+            us = (C.c_double * 5)()
+            fl = (C.c_double * 5)()
+            check(lib().stt_debug_time_products(cache._h, S, 20, us, fl), "time_products")
+            per_step_us = 16 * (us[0] + us[1] + us[2] + us[3]) + us[4]
+            per_step_flops = 16 * (fl[0] + fl[1] + fl[2] + fl[3]) + fl[4]
+            achieved = per_step_flops / (per_step_us * 1e-6) / 1e12
+            peak_t = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+            roofline = {"bound": "tensor", "kernel": "q4_tc_kernel (tcgen05 Q4_0 x f16 GEMM), the 65 products of a step",
+                        "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s", "frac": achieved / peak_t,
+                        "peak_kind": f"{pk_kind} sustained bf16", "traffic": TC_TRAFFIC_LINEAR_IN_512,
+                        "traffic_kernel": "one linear_in launch (16896 x 2048) at 512 rows",
+                        "useful_flops_per_launch": per_step_flops / 65, "us_per_launch": per_step_us / 65,
+                        "executed_mma_factor": 3,
+                        "us_per_product": {"in_proj": us[0], "out_proj": us[1], "linear_in": us[2], "linear_out": us[3],
+                                           "head": us[4]},
+                        "gemm_share_of_step": per_step_us / (ms / args.steps / F * 1000.0)}
+        # the same job with the two-product precision of the tensor-core layer products (activations
+        # rounded to f16): a third less tensor work (stt_streams_set_product_precision)
+        f16x2 = None
+        if roofline is not None and not args.no_extras and args.only == "all":
+            check(lib().stt_streams_set_product_precision(cache._h, 1), "set_product_precision")
             batched_job(model, cache, S, F, da, dt, lib, check, ts)
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(ts)
+            for _ in range(2):
+                batched_job(model, cache, S, F, da, dt, lib, check, ts)
+            e1.record(ts)
+            torch.cuda.synchronize()
+            ms2 = max_over_ranks(e0.elapsed_time(e1))
+            barrier()
+            check(lib().stt_streams_set_product_precision(cache._h, 0), "set_product_precision")
+            f16x2 = {"frames_per_s": total_streams * F * 2 / (ms2 / 1000.0), "ms_per_step": ms2 / 2,
+                     "note": "two f16 products per weight (activation rounded to f16) instead of three"}
+        step_bytes = algorithmic_bytes_batched([0] * S, 0, F)
+        step_ms = ms / args.steps / F
+        line = {
+            "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": job_config(world),
+            "roofline": roofline,
+            "e2e": {"value": e2e, "unit": "frames/s", "steps": e2e_steps,
+                    "h2d_bytes_per_step": F * S * 32 * 4 + S * 32, "d2h_bytes_per_step": F * (S * 4 + 48)},
+            "clocks": clocks,
+            "gpu_launches": launches_per_step * args.steps,
+            "batched_frame": {"ms": step_ms, "algorithmic_bytes": step_bytes,
+                              "hbm_gbs": step_bytes / (step_ms / 1000.0) / 1e9,
+                              "hbm_frac": step_bytes / (step_ms / 1000.0) / 1e9 / pk["hbm_gbs"],
+                              "real_time_streams_per_gpu": S * 80.0 / step_ms},
+            "tokens_vs_oracle": token_check,
+            "products_f16x2": f16x2,
+            "load": load,
+        }
+        cache.close()
+        del da, dt
+
+    if args.only == "frame":
+        # one batched frame of S streams at position P, reached by one persistent-kernel launch per
+        # stream (instead of P batched frames), then two batched frames
+        S, P = args.streams, args.position
+        cache = model.create_cache(S, "bf16")
+        for s_ in range(S):
+            pre = torch.from_numpy(synth.audio_tokens(SEED, s_, P).astype(np.int32)).cuda()
+            tk = torch.empty(P, dtype=torch.int32, device="cuda")
+            check(lib().stt_stream_feed_frames_device(cache._h, s_, P, C.c_void_p(pre.data_ptr()),
+                                                      C.c_void_p(tk.data_ptr()), C.c_void_p(ts.cuda_stream)), "pre-roll")
+        aud = np.stack([synth.audio_tokens(SEED, s_, 2, first_frame=P) for s_ in range(S)], 1)
+        da = torch.from_numpy(aud.astype(np.int32)).cuda()
+        dt = torch.empty(2, S, dtype=torch.int32, device="cuda")
+        ids = (C.c_int32 * S)(*range(S))
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for f in range(2):
+            if f == 1:
+                e0.record(ts)
+            check(lib().stt_streams_feed_frame_device(cache._h, ids, S, C.c_void_p(da[f].data_ptr()),
+                                                      C.c_void_p(dt[f].data_ptr()), C.c_void_p(ts.cuda_stream)), "step")
         e1.record(ts)
         torch.cuda.synchronize()
-        ms2 = max_over_ranks(e0.elapsed_time(e1))
-        barrier()
-        check(lib().stt_streams_set_product_precision(cache._h, 0), "set_product_precision")
-        f16x2 = {"frames_per_s": total_streams * F * 2 / (ms2 / 1000.0), "ms_per_step": ms2 / 2,
-                 "note": "two f16 products per weight (activation rounded to f16) instead of three"}
-    step_bytes = algorithmic_bytes_batched([0] * S, 0, F)
-    step_ms = ms / args.steps / F
-    line = {
-        "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": job_config(world),
-        "roofline": roofline,
-        "e2e": {"value": e2e, "unit": "frames/s", "steps": e2e_steps,
-                "h2d_bytes_per_step": F * S * 32 * 4 + S * 32, "d2h_bytes_per_step": F * (S * 4 + 48)},
-        "clocks": clocks,
-        "gpu_launches": launches_per_step * args.steps,
-        "batched_frame": {"ms": step_ms, "algorithmic_bytes": step_bytes,
-                          "hbm_gbs": step_bytes / (step_ms / 1000.0) / 1e9,
-                          "hbm_frac": step_bytes / (step_ms / 1000.0) / 1e9 / pk["hbm_gbs"],
-                          "real_time_streams_per_gpu": S * 80.0 / step_ms},
-        "tokens_vs_oracle": token_check,
-        "products_f16x2": f16x2,
-        "load": load,
-    }
-    cache.close()
-    del da, dt
-
-    if not args.no_extras:
+        nk = C.c_int()
+        check(lib().stt_debug_graph_kernels(cache._h, S, C.byref(nk)), "graph_kernels")
+        line["frame"] = {"streams": S, "position": P, "ms": e0.elapsed_time(e1), "launches_before_second_frame":
+                         3 * S + 1 + nk.value, "graph_kernels": nk.value}
+        cache.close()
+    extras = not args.no_extras
+    if extras and args.only in ("all", "stream1"):
         # ------------------------------------------------------------ configuration 2: one stream
         c1 = model.create_cache(1, "bf16")
         st1 = stt_b200.SttStream(cfg, c1, 0)
@@ -501,16 +542,18 @@ def main():
         ms1 = max_over_ranks(e0.elapsed_time(e1))
         toks1 = d_tokens.cpu().numpy()
         audio_host = [np.ascontiguousarray(a) for a in audio]
-        st1.reset()
-        for f in range(3):
-            st1.feed_frame(audio_host[f])
-        barrier()
-        t0 = time.perf_counter()
-        for _ in range(2):
+        e2e1 = float("nan")
+        if not args.no_e2e:
             st1.reset()
-            for f in range(UTT_FRAMES):
+            for f in range(3):
                 st1.feed_frame(audio_host[f])
-        e2e1 = max_over_ranks(time.perf_counter() - t0)
+            barrier()
+            t0 = time.perf_counter()
+            for _ in range(2):
+                st1.reset()
+                for f in range(UTT_FRAMES):
+                    st1.feed_frame(audio_host[f])
+            e2e1 = max_over_ranks(time.perf_counter() - t0)
         algo = algorithmic_bytes_per_utterance(UTT_FRAMES)
         ach = algo / (ms1 / n_utt / 1000.0) / 1e9
         s1 = {"config": "1 stream x 750 frames per GPU (the persistent kernel)",
@@ -526,6 +569,7 @@ def main():
         c1.close()
         line["stream1"] = s1
 
+    if extras and args.only in ("all", "streams64"):
         # ------------------------------------------------ configuration 3: 64 staggered streams
         offs = [round(i * 374 / 63) for i in range(64)]
         ms64, k64 = staggered(model, range(64 * rank, 64 * rank + 64), 375, offs, SEED, torch, np, lib, check, synth)
@@ -536,13 +580,14 @@ def main():
                              "frames_per_s": world * 64 * 1000.0 / ms64, "ms_per_step": ms64,
                              "real_time_streams_per_gpu": 64 * 80.0 / ms64,
                              "hbm_frac": b64 / (ms64 / 1000.0) / 1e9 / pk["hbm_gbs"]}
+    if extras and args.only in ("all", "sweep"):
         if rank == 0:
             sweep = q4_sweep(torch, np, lib, stt_b200, local)
             gbs = {f"{n}x{k}": round(n * k // 32 * 18 / us / 1e3, 1) for n, k, m, us, _ in sweep if m == 1}
             line["q4_matmul"] = {"gemv_m1_weight_gbs": gbs, "gemv_m1_frac_of_hbm": max(gbs.values()) / pk["hbm_gbs"],
                                  "sweep_n_k_m_us_path": sweep}
         barrier()
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.only == "all":
         job = CpuJob()
         job.step()
         t0 = time.perf_counter()

@@ -291,6 +291,11 @@ int stt_debug_get_trace_ctas(stt_streams* streams, uint64_t* out, int cap, int* 
  * counter), mode 1 a variant in which the last arriver publishes a flag that the others poll. */
 int stt_debug_barrier_ns(int device, int iters, int mode, double* ns_per_barrier);
 
+/* Allocation-failure injection for tests of the error paths: after `after` more successful
+ * allocations of device or pinned host memory by this library (any thread, any device), the next
+ * one fails as if memory had run out, so the call making it returns STT_E_OOM having released
+ * whatever it had allocated; the countdown then stops.  after < 0 disarms it. */
+int stt_debug_fail_allocation(int after);
 /* Test of the persistent kernel's bounded waits.  Arms the next single-stream call on this set
  * (one launch only): in its first frame, the CTAs that compute the first layer's output projection
  * wait for an input epoch that no phase ever publishes.  That wait gives up after its limit (about

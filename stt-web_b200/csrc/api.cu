@@ -1,6 +1,7 @@
 // C ABI of libsttb200: model loading, stream sets, decode steps and the isolated Q4 matmul.
 // The entry points and the reference interfaces they replace are listed in include/stt_b200.h.
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <condition_variable>
 #include <cstdarg>
@@ -52,6 +53,43 @@ void clear_error() {
         if (rc_ != STT_OK) return rc_; \
     } while (0)
 
+// Allocation-failure injection for tests (stt_debug_fail_allocation): a countdown over the library's
+// device and pinned-host allocations; the one that brings it to zero fails as if memory had run out.
+std::atomic<int64_t> g_fail_after{-1};
+
+bool injected_failure() {
+    int64_t v = g_fail_after.load();
+    while (v >= 0)
+        if (g_fail_after.compare_exchange_weak(v, v - 1)) return v == 0;
+    return false;
+}
+cudaError_t dev_alloc(void** p, size_t bytes) {
+    if (injected_failure()) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaMalloc(p, bytes);
+}
+cudaError_t host_alloc(void** p, size_t bytes) {
+    if (injected_failure()) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaHostAlloc(p, bytes, cudaHostAllocDefault);
+}
+
+// An allocation: out of memory is STT_E_OOM, any other failure STT_E_CUDA.
+#define ALLOC_TRY(expr)                                                                             \
+    do {                                                                                            \
+        cudaError_t e_ = (expr);                                                                    \
+        if (e_ != cudaSuccess) {                                                                    \
+            (void)cudaGetLastError();                                                               \
+            return set_error(e_ == cudaErrorMemoryAllocation ? STT_E_OOM : STT_E_CUDA,              \
+                             "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__,      \
+                             __LINE__);                                                             \
+        }                                                                                           \
+    } while (0)
+
 // Restores the calling thread's current device on scope exit.
 struct DeviceScope {
     int prev = 0;
@@ -78,7 +116,7 @@ struct DevBuf {
         if (p) cudaFree(p);
         p = nullptr;
         cap = 0;
-        CUDA_TRY(cudaMalloc(&p, bytes));
+        ALLOC_TRY(dev_alloc(&p, bytes));
         cap = bytes;
         return STT_OK;
     }
@@ -101,7 +139,7 @@ struct HostBuf {
         if (p) cudaFreeHost(p);
         p = nullptr;
         cap = 0;
-        CUDA_TRY(cudaHostAlloc(&p, bytes, cudaHostAllocDefault));
+        ALLOC_TRY(host_alloc(&p, bytes));
         cap = bytes;
         return STT_OK;
     }
@@ -194,8 +232,8 @@ public:
     }
     int init() {
         CUDA_TRY(cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking));
-        CUDA_TRY(cudaHostAlloc(&pinned_, kPiece * kStages, cudaHostAllocDefault));
-        CUDA_TRY(cudaMalloc(&draw_, kPiece * kStages));
+        ALLOC_TRY(host_alloc(&pinned_, kPiece * kStages));
+        ALLOC_TRY(dev_alloc(&draw_, kPiece * kStages));
         for (auto& e : ev_) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         return STT_OK;
     }
@@ -530,7 +568,7 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
     cudaDeviceProp prop;
     CUDA_TRY(cudaGetDeviceProperties(&prop, device));
     m->num_sms = prop.multiProcessorCount;
-    if (cudaMalloc(&m->d_mem, off) != cudaSuccess) {
+    if (dev_alloc(&m->d_mem, off) != cudaSuccess) {
         cudaGetLastError();
         return set_error(STT_E_OOM, "cannot allocate %zu bytes on device %d", off, device);
     }
@@ -990,11 +1028,11 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     const size_t o_x16 = take(x16_bytes);
     const size_t o_tc_part = take(tc_part_bytes_max);
     const size_t o_trace_ctas = take((size_t)m->num_sms * kTraceSlots * sizeof(unsigned long long));
-    if (cudaMalloc(&s->d_scratch, off) != cudaSuccess) {
+    if (dev_alloc(&s->d_scratch, off) != cudaSuccess) {
         cudaGetLastError();
         return set_error(STT_E_OOM, "cannot allocate %zu bytes of step scratch", off);
     }
-    if (cudaMalloc(&s->d_kv, s->kv_stream_bytes * S) != cudaSuccess) {
+    if (dev_alloc(&s->d_kv, s->kv_stream_bytes * S) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(s->d_scratch);
         return set_error(STT_E_OOM, "cannot allocate the KV rings (%zu bytes)", s->kv_stream_bytes * S);
@@ -1362,7 +1400,7 @@ extern "C" int stt_q4_tensor_create(const uint8_t* bytes, size_t n_bytes, int n,
     t->num_sms = prop.multiProcessorCount;
     const size_t nib_bytes = (nblk * 16 + 255) / 256 * 256;
     const size_t sc_bytes = (nblk * 2 + 255) / 256 * 256;
-    if (cudaMalloc(&t->mem, nib_bytes + sc_bytes + 256) != cudaSuccess) {
+    if (dev_alloc(&t->mem, nib_bytes + sc_bytes + 256) != cudaSuccess) {
         cudaGetLastError();
         return set_error(STT_E_OOM, "cannot allocate Q4 tensor");
     }
@@ -1423,6 +1461,7 @@ extern "C" int stt_q4_matmul_device(const stt_q4_tensor* t, const void* d_in, in
     a.out = d_out;
     a.ldo = t->w.n;
     a.n_units = (t->w.n + 1) / 2;
+    a.err = t->d_err;
     CUDA_TRY(launch_gemv(c, a, EPI_PLAIN, rows, static_cast<cudaStream_t>(cuda_stream)));
     return STT_OK;
 }
@@ -1554,6 +1593,12 @@ extern "C" int stt_debug_get_trace_ctas(stt_streams* s, uint64_t* out, int cap, 
     CUDA_TRY(cudaMemcpy(out, s->mega.trace_ctas, sizeof(unsigned long long) * total, cudaMemcpyDeviceToHost));
     *n_ctas = s->m->num_sms;
     *n_slots = kTraceSlots;
+    return STT_OK;
+}
+
+extern "C" int stt_debug_fail_allocation(int after) {
+    clear_error();
+    g_fail_after.store(after < 0 ? -1 : after);
     return STT_OK;
 }
 

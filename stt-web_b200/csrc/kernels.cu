@@ -13,6 +13,8 @@
 //              231-266)
 #include <algorithm>
 #include <cfloat>
+#include <map>
+#include <mutex>
 
 #include "device.cuh"
 #include "dp4a.cuh"
@@ -20,6 +22,8 @@
 #include "tc_layout.cuh"
 
 namespace stt {
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 // ------------------------------------------------------------------------------------ Q4 layout
 
@@ -346,6 +350,223 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(Ctx c, GemvArgs a, i
     }
 }
 
+// The streamed GEMV: the same products as gemv_kernel, for K a multiple of 256, with the weights
+// moved by bulk copies instead of register loads.  A CTA owns a contiguous range of units; its
+// producer warp copies them, a few units per stage, into a ring of shared-memory stages
+// (cp.async.bulk, one full mbarrier per stage), so the CTA's whole share of the matrix can be in
+// flight at once without holding registers, and the consumer warps take the units of each stage
+// as it lands: a warp per unit, the lanes splitting its blocks, the dp4a block dot on the limbs,
+// a shuffle reduction and the epilogue.  Stage layout: the units' nibble rows (pairs: rows 2u and
+// 2u + 1 of each unit; EPI_GATE: the gate rows, then the value rows), then their scale rows.  Every
+// wait is bounded; a wait that gives up records STT_E_DEVICE_FLAG in the step descriptor (or in
+// a.err) and the CTA stops, waiting (bounded) for its copies in flight before it exits.
+constexpr int kSCWarps = 8;                        // consumer warps
+constexpr int kSThreads = 32 * (kSCWarps + 1);     // + the producer warp
+constexpr int kSStages = 6;
+constexpr uint32_t kSStageBytes = 24 * 1024;
+constexpr uint32_t kSSpin = 1u << 22;
+constexpr size_t kSmemLimit = 226 * 1024;     // dynamic shared memory of one CTA (227 KB on sm_100, less the static part)
+
+__device__ __forceinline__ bool gemv_mbar_wait(uint64_t* m, uint32_t parity, volatile int* stop) {
+    for (uint32_t i = 0; i < kSSpin; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_addr(m)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((i & 255u) == 255u && *stop) return false;
+    }
+    return false;
+}
+
+template <int MB, int EPI>
+__global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(Ctx c, GemvArgs a, int row0, int mb, int ups,
+                                                                int stages, int* err) {
+    extern __shared__ __align__(128) uint8_t gs_smem[];
+    const int K = a.W.k, NB = K >> 5;
+    uint8_t* ring = gs_smem;                                                   // [stages][kSStageBytes]
+    uint4* L = reinterpret_cast<uint4*>(gs_smem + (size_t)stages * kSStageBytes);  // [MB][6][NB]
+    float* xs = reinterpret_cast<float*>(L + (size_t)MB * 6 * NB);            // [MB][NB]
+    __shared__ __align__(8) uint64_t full[kSStages], empty[kSStages];  // the first `stages` are used
+    __shared__ float red[32];
+    __shared__ int stop;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t u0 = (int64_t)a.n_units * blockIdx.x / gridDim.x;
+    const int64_t u1 = (int64_t)a.n_units * (blockIdx.x + 1) / gridDim.x;
+    const int nchunks = (int)((u1 - u0 + ups - 1) / ups);
+    if (tid == 0) {
+        for (int i = 0; i < stages; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[i])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(&empty[i])), "r"(kSCWarps) : "memory");
+        }
+        stop = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    pdl_trigger();
+    const bool gate = EPI == EPI_GATE;
+    const uint32_t row_nib = (uint32_t)NB * 16u, row_sc = (uint32_t)NB * 2u;
+    if (warp == kSCWarps) {
+        // producer: the weights are constant, so their copies start before the previous kernel ends
+        int issued = 0;
+        for (int k = 0; k < nchunks; ++k) {
+            const int s = k % stages;
+            if (k >= stages) {
+                bool ok = true;
+                if (lane == 0) ok = gemv_mbar_wait(&empty[s], ((k / stages) - 1) & 1, &stop);
+                if (!__shfl_sync(0xFFFFFFFFu, (int)ok, 0)) break;
+            }
+            if (lane == 0) {
+                const int64_t ua = u0 + (int64_t)k * ups;
+                const int nu = (int)((int64_t)ups < u1 - ua ? (int64_t)ups : u1 - ua);
+                const uint32_t dst = smem_addr(ring + (size_t)s * kSStageBytes);
+                const uint32_t nr = gate ? (uint32_t)nu : (uint32_t)((int64_t)(2 * nu) < (int64_t)a.W.n - 2 * ua ? (int64_t)(2 * nu) : (int64_t)a.W.n - 2 * ua);
+                const uint32_t bytes = gate ? 2u * nr * (row_nib + row_sc) : nr * (row_nib + row_sc);
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(&full[s])),
+                             "r"(bytes)
+                             : "memory");
+                const int64_t r0 = gate ? ua : 2 * ua;
+                const uint8_t* nib = reinterpret_cast<const uint8_t*>(a.W.nib);
+                const uint8_t* sc = reinterpret_cast<const uint8_t*>(a.W.scale);
+                const uint32_t nib_bytes = gate ? 2u * nr * row_nib : nr * row_nib;
+                auto copy = [&](uint32_t d, const void* src, uint32_t b) {
+                    asm volatile(
+                        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                            d),
+                        "l"(src), "r"(b), "r"(smem_addr(&full[s]))
+                        : "memory");
+                };
+                copy(dst, nib + r0 * row_nib, nr * row_nib);
+                if (gate) copy(dst + nr * row_nib, nib + (r0 + a.half_n) * row_nib, nr * row_nib);
+                copy(dst + nib_bytes, sc + r0 * row_sc, nr * row_sc);
+                if (gate) copy(dst + nib_bytes + nr * row_sc, sc + (r0 + a.half_n) * row_sc, nr * row_sc);
+            }
+            __syncwarp();
+            issued = k + 1;
+        }
+        // every copy must land before the CTA's shared memory goes away
+        if (lane == 0)
+            for (int k = max(0, issued - stages); k < issued; ++k) {
+                const int s = k % stages;
+                for (uint32_t i = 0; i < kSSpin; ++i) {
+                    uint32_t ok;
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\t"
+                        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                        "selp.u32 %0, 1, 0, p;\n\t}"
+                        : "=r"(ok)
+                        : "r"(smem_addr(&full[s])), "r"((uint32_t)(k / stages) & 1u)
+                        : "memory");
+                    if (ok) break;
+                }
+            }
+        pdl_wait();
+        return;
+    }
+    // consumers: the input rows become limbs (the producer's copies are already in flight)
+    pdl_wait();
+    {
+        const int nq = K >> 2;
+        for (int m = 0; m < mb; ++m) {
+            const int64_t base = (int64_t)(row0 + m) * K;
+            float rms = 1.0f;
+            if (a.norm) {
+                float ss = 0.0f;
+                for (int j = tid; j < K; j += 32 * kSCWarps) {
+                    const float v = a.in[base + j];
+                    ss = __fmaf_rn(v, v, ss);
+                }
+                ss = warp_sum(ss);
+                asm volatile("bar.sync 1, %0;" ::"n"(32 * kSCWarps) : "memory");
+                if (lane == 0) red[warp] = ss;
+                asm volatile("bar.sync 1, %0;" ::"n"(32 * kSCWarps) : "memory");
+                float t = 0.0f;
+                for (int w = 0; w < kSCWarps; ++w) t += red[w];
+                rms = sqrtf(__fadd_rn(__fdiv_rn(t, (float)K), 1e-8f));
+            }
+            for (int q = tid; q < nq; q += 32 * kSCWarps) {  // nq is a multiple of 64: whole warps
+                float4 v;
+                if (a.in_bf16) {
+                    const uint2 r = *reinterpret_cast<const uint2*>(a.in_bf16 + base + 4 * q);
+                    v = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
+                                    __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
+                } else {
+                    v = *reinterpret_cast<const float4*>(a.in + base + 4 * q);
+                }
+                if (a.norm) {
+                    const float4 al = reinterpret_cast<const float4*>(a.norm)[q];
+                    v.x = __fmul_rn(__fdiv_rn(v.x, rms), al.x);
+                    v.y = __fmul_rn(__fdiv_rn(v.y, rms), al.y);
+                    v.z = __fmul_rn(__fdiv_rn(v.z, rms), al.z);
+                    v.w = __fmul_rn(__fdiv_rn(v.w, rms), al.w);
+                }
+                quad_limbs_store(L + (size_t)m * 6 * NB, xs + (size_t)m * NB, q, NB, v, true);
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kSCWarps) : "memory");
+    }
+    for (int k = 0; k < nchunks; ++k) {
+        const int s = k % stages;
+        bool ok = true;
+        if (lane == 0) ok = gemv_mbar_wait(&full[s], (k / stages) & 1, &stop);
+        if (!__shfl_sync(0xFFFFFFFFu, (int)ok, 0)) {
+            if (lane == 0) {
+                stop = 1;
+                if (c.desc) raise_error(c.desc, -5);  // STT_E_DEVICE_FLAG
+                if (err) atomicCAS(err, 0, -5);
+            }
+            break;
+        }
+        const int64_t ua = u0 + (int64_t)k * ups;
+        const int nu = (int)((int64_t)ups < u1 - ua ? (int64_t)ups : u1 - ua);
+        const uint8_t* st = ring + (size_t)s * kSStageBytes;
+        const uint32_t nr = gate ? (uint32_t)nu : (uint32_t)((int64_t)(2 * nu) < (int64_t)a.W.n - 2 * ua ? (int64_t)(2 * nu) : (int64_t)a.W.n - 2 * ua);
+        const uint4* nibs = reinterpret_cast<const uint4*>(st);
+        const uint16_t* scs = reinterpret_cast<const uint16_t*>(st + (gate ? 2u * nr * row_nib : nr * row_nib));
+        for (int j = warp; j < nu; j += kSCWarps) {
+            int ra, rb;
+            unit_rows<EPI>(a, (int)(ua + j), &ra, &rb);
+            // stage rows of the unit's two rows
+            const int la = gate ? j : 2 * j;
+            const int lb = gate ? (int)nr + j : (rb >= 0 ? 2 * j + 1 : 2 * j);
+            float acc[MB][2];
+#pragma unroll
+            for (int m = 0; m < MB; ++m) acc[m][0] = acc[m][1] = 0.0f;
+            for (int b = lane; b < NB; b += 32) {
+                const uint4 qa = nibs[(size_t)la * NB + b], qb = nibs[(size_t)lb * NB + b];
+                const float fa = f16_to_f32_ieee(scs[(size_t)la * NB + b]), fb = f16_to_f32_ieee(scs[(size_t)lb * NB + b]);
+#pragma unroll
+                for (int m = 0; m < MB; ++m) {
+                    if (m < mb) {
+                        const uint4* Lm = L + (size_t)m * 6 * NB;
+                        uint4 Lb[6];
+#pragma unroll
+                        for (int v = 0; v < 6; ++v) Lb[v] = Lm[v * NB + b];
+                        const float x = xs[m * NB + b];
+                        acc[m][0] = __fmaf_rn(block_dp4a(qa, Lb), __fmul_rn(fa, x), acc[m][0]);
+                        acc[m][1] = __fmaf_rn(block_dp4a(qb, Lb), __fmul_rn(fb, x), acc[m][1]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < MB; ++m) {
+                acc[m][0] = warp_sum(acc[m][0]);
+                acc[m][1] = warp_sum(acc[m][1]);
+            }
+            if (lane == 0)
+#pragma unroll
+                for (int m = 0; m < MB; ++m)
+                    if (m < mb) epilogue<EPI>(c, a, row0 + m, ra, rb, acc[m][0], acc[m][1]);
+        }
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&empty[s])) : "memory");
+    }
+}
+
 // Epilogue of a tensor-core product: the K-slice partial sums part[z][m][W.n] of each output pair
 // are added in slice order (z = 0, 1, ...) and handed to the same epilogue as the GEMV's.
 template <int EPI>
@@ -388,7 +609,6 @@ template <typename KT, int CH>
 constexpr size_t attn_smem_bytes() { return (size_t)2 * 2 * CH * 128 * sizeof(KT); }
 
 // mbarrier and bulk-copy helpers of the attention kernel's K/V staging
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void attn_mbar_init(uint64_t* m) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(m)) : "memory");
 }
@@ -793,8 +1013,12 @@ constexpr int kGemvMaxRowsLongK = 4;   // rows per pass when K > 4096 (the limbs
 template <int MB, int EPI>
 static cudaError_t configure_gemv_t() {
     const int k = MB > kGemvMaxRowsLongK ? 4096 : kMaxGemvK;
-    return cudaFuncSetAttribute(gemv_kernel<MB, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)gemv_smem_bytes(MB, k));
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<MB, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)gemv_smem_bytes(MB, k));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemv_stream_kernel<MB, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmemLimit);
+    return e;
 }
 
 template <int EPI>
@@ -826,12 +1050,82 @@ int gemv_team(int64_t units, int NB) {
     return team;
 }
 
+// CTAs of one GEMV launch: one per team-sized group of units, but no more than fit on the GPU at
+// once, so that a CTA converts its input rows once and its teams then loop over units (each
+// team's next unit in flight while it reduces the current one).
+template <int MB, int EPI>
+static int gemv_grid(int64_t units, int teams, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, int> resident;  // (device, smem) -> CTAs per GPU
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    int fit = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = resident.find({dev, smem});
+        if (it != resident.end()) {
+            fit = it->second;
+        } else {
+            int sms = 0, occ = 0;
+            if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_kernel<MB, EPI>, kGemvThreads, smem) ==
+                    cudaSuccess)
+                fit = sms * std::max(occ, 1);
+            (void)cudaGetLastError();
+            resident[{dev, smem}] = fit;
+        }
+    }
+    const int64_t want = (units + teams - 1) / teams;
+    return (int)(fit > 0 ? std::min<int64_t>(want, fit) : want);
+}
+
+// Shared memory of the streamed GEMV: `stages` weight stages, then the limbs and exponents of MB
+// rows; stages as many as fit (at most kSStages, at least 2).
+static int gemv_stream_stages(int mb, int k) {
+    const size_t limbs = gemv_smem_bytes(mb, k) + 1024;
+    const int fit = (int)((kSmemLimit - std::min(kSmemLimit, limbs)) / kSStageBytes);
+    return std::min(kSStages, fit);
+}
+static bool gemv_streamed(const GemvArgs& a, int mb) {
+    const int64_t row_bytes = (int64_t)(a.W.k / 32) * 18;
+    return a.W.k % 256 == 0 && 2 * row_bytes <= kSStageBytes && gemv_stream_stages(mb, a.W.k) >= 2;
+}
+
+template <int MB, int EPI>
+static cudaError_t launch_gemv_stream(const Ctx& c, const GemvArgs& a, int rows, int* err, cudaStream_t st) {
+    static std::mutex mu;
+    static std::map<int, int> sms_of;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = sms_of.find(dev);
+        if (it == sms_of.end()) {
+            if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+            sms_of[dev] = sms;
+        } else {
+            sms = it->second;
+        }
+    }
+    const int stages = gemv_stream_stages(MB, a.W.k);
+    const size_t smem = (size_t)stages * kSStageBytes + gemv_smem_bytes(MB, a.W.k);
+    const int ups = (int)(kSStageBytes / (2u * (uint32_t)(a.W.k / 32) * 18u));
+    const int grid = (int)std::min<int64_t>(sms, a.n_units);
+    for (int r0 = 0; r0 < rows; r0 += MB) {
+        const int mb = rows - r0 < MB ? rows - r0 : MB;
+        const cudaError_t e = launch_pdl(gemv_stream_kernel<MB, EPI>, dim3(grid), dim3(kSThreads), smem, st, c, a, r0,
+                                         mb, ups, stages, err);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 template <int MB, int EPI>
 static cudaError_t launch_gemv_t(const Ctx& c, const GemvArgs& a, int rows, cudaStream_t st) {
+    if (gemv_streamed(a, MB)) return launch_gemv_stream<MB, EPI>(c, a, rows, a.err, st);
     const int team = gemv_team(a.n_units, a.W.k / 32);
     const int teams = kGemvThreads / team;
-    const int grid = (int)((a.n_units + teams - 1) / teams);
     const size_t smem = gemv_smem_bytes(MB, a.W.k);
+    const int grid = gemv_grid<MB, EPI>(a.n_units, teams, smem);
     for (int r0 = 0; r0 < rows; r0 += MB) {
         const int mb = rows - r0 < MB ? rows - r0 : MB;
         const cudaError_t e = launch_pdl(gemv_kernel<MB, EPI>, dim3(grid), dim3(kGemvThreads), smem, st, c, a, r0, mb,

@@ -20,6 +20,7 @@ struct GemvArgs {
     int32_t layer;                   // layer of the K/V ring (EPI_QKV)
     int32_t n_units;                 // pairs of output rows
     int32_t half_n;                  // EPI_GATE: value rows start here (= ffn width)
+    int* err;                        // where a kernel records a timeout when there is no step descriptor
 };
 
 // Per-call descriptor and batch ids, written on the device from launch parameters so that

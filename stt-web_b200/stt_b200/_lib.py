@@ -126,6 +126,7 @@ SIGNATURES = {
     "stt_debug_barrier_ns": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "stt_debug_graph_kernels": (C.c_int, [P, C.c_int, C.POINTER(C.c_int)]),
     "stt_debug_arm_wait_timeout": (C.c_int, [P]),
+    "stt_debug_fail_allocation": (C.c_int, [C.c_int]),
     "stt_debug_time_products": (C.c_int, [P, C.c_int, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "stt_last_error": (C.c_char_p, []),
 }

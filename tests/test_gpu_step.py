@@ -363,3 +363,48 @@ def test_bounded_wait_runs_out_and_the_next_call_recovers():
     assert st.feed_frames(frames) == [ref.feed_frame(f) for f in frames]
     # the hook was one-shot: a second call runs normally too
     assert st.feed_frame(frames[0]) == ref.feed_frame(frames[0])
+
+
+def test_allocation_failures_release_everything():
+    """An allocation that fails part-way through loading a model, creating a stream set or a step's
+    first use of its staging buffers is reported as STT_E_OOM, and whatever the call had already
+    allocated is released: after each failure, device memory is back where it started, and a later
+    attempt succeeds and decodes like the oracle.  (The failure is injected on the host, where the
+    library asks for memory.)"""
+    import torch
+    from stt_b200._lib import lib, STT_E_OOM
+    spec = stt_b200.SynthSpec(seed=26, num_layers=2, hidden_size=256, num_heads=2, ffn_hidden=512, vocab_size=1000,
+                              text_in_vocab_size=1001, num_codebooks=4, audio_vocab_size=300)
+    g = stt_b200.synth_gguf(spec)
+    cfg = tiny_cfg()
+    frames = np.random.default_rng(10).integers(0, 300, (3, 20, 4))
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    failures = 0
+    for k in range(40):
+        assert lib().stt_debug_fail_allocation(k) == 0
+        model = cache = None
+        try:
+            model = stt_b200.SttModel.from_shards([g.array], config=cfg)
+            cache = model.create_cache(20, "bf16")
+            toks = [cache.feed_frame(list(range(20)), f) for f in frames]
+            ok = True
+        except stt_b200.SttError as e:
+            assert e.code == STT_E_OOM, e
+            ok = False
+            failures += 1
+        finally:
+            lib().stt_debug_fail_allocation(-1)
+            if cache is not None:
+                cache.close()
+            if model is not None:
+                model.close()
+        torch.cuda.synchronize()
+        assert abs(torch.cuda.mem_get_info()[0] - free0) < (64 << 20), k
+        if ok:
+            break
+    assert failures >= 3 and ok
+    om = oracle_for(g.array, cfg)
+    refs = [om.stream(O.KV_BF16) for _ in range(20)]
+    exp = [O.feed_frame_batch(refs, f)[0] for f in frames]
+    assert [[None if t < 0 else int(t) for t in row] for row in toks] == exp
