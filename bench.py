@@ -50,11 +50,10 @@ Q4_PARAMS = 16 * (6144 * 2048 + 2048 * 2048 + 16896 * 2048 + 2048 * 8448) + 8000
 PUBLISHED_FPS_750 = 1000.0 / 52.5
 # DRAM read + write bytes of one 750-frame launch of the persistent kernel (ncu, single pass):
 # profiles/mega_kernel_dram_750frames.txt
-MEGA_TRAFFIC_750 = 508_142_132_480 + 2_654_166_784
+MEGA_TRAFFIC_750 = 508_170_845_440 + 2_636_432_128
 # DRAM read + write bytes of one launch of the tcgen05 GEMM on linear_in (16896 x 2048) at 512 batch
-# rows, K-slice partial sums included: profiles/q4_tc_kernel_linear_in_512rows.txt (None until
-# captured)
-TC_TRAFFIC_LINEAR_IN_512 = None
+# rows (ncu): profiles/q4_tc_kernel_linear_in_512rows.txt
+TC_TRAFFIC_LINEAR_IN_512 = 23_689_472 + 393_728
 METRIC = "decode frames/s, whole job (512 streams x 250 frames split over the GPUs)"
 
 
@@ -268,11 +267,12 @@ Q4_SHAPES = [(6144, 2048), (2048, 2048), (16896, 2048), (2048, 8448), (8001, 204
 def q4_sweep(torch, np, lib, stt_b200, device):
     """Configuration 5: isolated Q4_0 products, weights N(0, 0.02) quantised, activations N(0, 1)
     bf16.  M = 1 and 4 run the GEMV (bf16 input); M >= 16 the tensor-core GEMM (the bf16 activations
-    converted to f16, exactly for these values).  Device-timed, 20 calls after 3 warm-up calls.
-    Returns [n, k, m, microseconds per call, path] rows."""
+    converted to f16, exactly for these values).  After 3 warm-up calls, 20 back-to-back calls are
+    captured in a CUDA graph and the graph is replayed 3 times between CUDA events: the device time
+    per call, without the host's launch rate (a few microseconds per launch, as long as the smaller
+    products themselves).  Returns [n, k, m, microseconds per call, path] rows."""
     out = []
     rng = np.random.default_rng(5)
-    ts = torch.cuda.current_stream()
     for n, k in Q4_SHAPES:
         raw = stt_b200.quantize_q4_0((rng.standard_normal(n * k) * 0.02).astype(np.float32))
         t = stt_b200.Q4Tensor.from_q4_bytes(raw, (n, k), device=device)
@@ -281,19 +281,31 @@ def q4_sweep(torch, np, lib, stt_b200, device):
             dtype, xin = (1, x) if m < 16 else (2, x.to(torch.float16))
             y = torch.empty(m, n, dtype=torch.float32, device="cuda")
 
-            def call():
-                rc = lib().stt_q4_matmul_device(t._h, xin.data_ptr(), dtype, m, y.data_ptr(), ts.cuda_stream)
+            def call(stream):
+                rc = lib().stt_q4_matmul_device(t._h, xin.data_ptr(), dtype, m, y.data_ptr(), stream.cuda_stream)
                 assert rc == 0, lib().stt_last_error().decode()
-            for _ in range(3):
-                call()
+            side = torch.cuda.Stream()
+            with torch.cuda.stream(side):
+                for _ in range(3):
+                    call(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                cs = torch.cuda.current_stream()
+                for _ in range(20):
+                    call(cs)
+            torch.cuda.synchronize()
+            ts = torch.cuda.current_stream()
+            graph.replay()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(ts)
-            for _ in range(20):
-                call()
+            for _ in range(3):
+                graph.replay()
             e1.record(ts)
             torch.cuda.synchronize()
-            out.append([n, k, m, round(e0.elapsed_time(e1) / 20 * 1000.0, 2), "gemv" if m < 16 else "tcgen05"])
+            out.append([n, k, m, round(e0.elapsed_time(e1) / 60 * 1000.0, 2), "gemv" if m < 16 else "tcgen05"])
+            del graph
         t.close()
     return out
 

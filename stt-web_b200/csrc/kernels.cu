@@ -360,8 +360,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(Ctx c, GemvArgs a, i
 // 2u + 1 of each unit; EPI_GATE: the gate rows, then the value rows), then their scale rows.  Every
 // wait is bounded; a wait that gives up records STT_E_DEVICE_FLAG in the step descriptor (or in
 // a.err) and the CTA stops, waiting (bounded) for its copies in flight before it exits.
-constexpr int kSCWarps = 8;                        // consumer warps
-constexpr int kSThreads = 32 * (kSCWarps + 1);     // + the producer warp
+// consumer warps of the streamed GEMV: 16, or 8 for 8 batch rows (register budget)
+template <int MB>
+constexpr int stream_cwarps() { return MB >= 8 ? 8 : 16; }
 constexpr int kSStages = 6;
 constexpr uint32_t kSStageBytes = 24 * 1024;
 constexpr uint32_t kSSpin = 1u << 22;
@@ -384,8 +385,10 @@ __device__ __forceinline__ bool gemv_mbar_wait(uint64_t* m, uint32_t parity, vol
 }
 
 template <int MB, int EPI>
-__global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(Ctx c, GemvArgs a, int row0, int mb, int ups,
-                                                                int stages, int* err) {
+__global__ void __launch_bounds__(32 * (stream_cwarps<MB>() + 1)) gemv_stream_kernel(Ctx c, GemvArgs a, int row0,
+                                                                                      int mb, int ups, int stages,
+                                                                                      int* err) {
+    constexpr int kSCWarps = stream_cwarps<MB>();
     extern __shared__ __align__(128) uint8_t gs_smem[];
     const int K = a.W.k, NB = K >> 5;
     uint8_t* ring = gs_smem;                                                   // [stages][kSStageBytes]
@@ -401,7 +404,7 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(Ctx c, GemvArgs 
     if (tid == 0) {
         for (int i = 0; i < stages; ++i) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[i])) : "memory");
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(&empty[i])), "r"(kSCWarps) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(&empty[i])), "r"(ups) : "memory");
         }
         stop = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -509,8 +512,11 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(Ctx c, GemvArgs 
         }
         asm volatile("bar.sync 1, %0;" ::"n"(32 * kSCWarps) : "memory");
     }
-    for (int k = 0; k < nchunks; ++k) {
-        const int s = k % stages;
+    // each warp takes the CTA's units j = warp, warp + kSCWarps, ... as their stages land; a stage is
+    // free again once all of its units are done (every unit arrives once)
+    const int64_t cta_units = u1 - u0;
+    for (int64_t j = warp; j < cta_units; j += kSCWarps) {
+        const int k = (int)(j / ups), s = k % stages;
         bool ok = true;
         if (lane == 0) ok = gemv_mbar_wait(&full[s], (k / stages) & 1, &stop);
         if (!__shfl_sync(0xFFFFFFFFu, (int)ok, 0)) {
@@ -523,47 +529,45 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(Ctx c, GemvArgs 
         }
         const int64_t ua = u0 + (int64_t)k * ups;
         const int nu = (int)((int64_t)ups < u1 - ua ? (int64_t)ups : u1 - ua);
+        const int jl = (int)(j - (int64_t)k * ups);  // the unit's place in its stage
         const uint8_t* st = ring + (size_t)s * kSStageBytes;
         const uint32_t nr = gate ? (uint32_t)nu : (uint32_t)((int64_t)(2 * nu) < (int64_t)a.W.n - 2 * ua ? (int64_t)(2 * nu) : (int64_t)a.W.n - 2 * ua);
         const uint4* nibs = reinterpret_cast<const uint4*>(st);
         const uint16_t* scs = reinterpret_cast<const uint16_t*>(st + (gate ? 2u * nr * row_nib : nr * row_nib));
-        for (int j = warp; j < nu; j += kSCWarps) {
-            int ra, rb;
-            unit_rows<EPI>(a, (int)(ua + j), &ra, &rb);
-            // stage rows of the unit's two rows
-            const int la = gate ? j : 2 * j;
-            const int lb = gate ? (int)nr + j : (rb >= 0 ? 2 * j + 1 : 2 * j);
-            float acc[MB][2];
+        int ra, rb;
+        unit_rows<EPI>(a, (int)(ua + jl), &ra, &rb);
+        const int la = gate ? jl : 2 * jl;
+        const int lb = gate ? (int)nr + jl : (rb >= 0 ? 2 * jl + 1 : 2 * jl);
+        float acc[MB][2];
 #pragma unroll
-            for (int m = 0; m < MB; ++m) acc[m][0] = acc[m][1] = 0.0f;
-            for (int b = lane; b < NB; b += 32) {
-                const uint4 qa = nibs[(size_t)la * NB + b], qb = nibs[(size_t)lb * NB + b];
-                const float fa = f16_to_f32_ieee(scs[(size_t)la * NB + b]), fb = f16_to_f32_ieee(scs[(size_t)lb * NB + b]);
-#pragma unroll
-                for (int m = 0; m < MB; ++m) {
-                    if (m < mb) {
-                        const uint4* Lm = L + (size_t)m * 6 * NB;
-                        uint4 Lb[6];
-#pragma unroll
-                        for (int v = 0; v < 6; ++v) Lb[v] = Lm[v * NB + b];
-                        const float x = xs[m * NB + b];
-                        acc[m][0] = __fmaf_rn(block_dp4a(qa, Lb), __fmul_rn(fa, x), acc[m][0]);
-                        acc[m][1] = __fmaf_rn(block_dp4a(qb, Lb), __fmul_rn(fb, x), acc[m][1]);
-                    }
-                }
-            }
+        for (int m = 0; m < MB; ++m) acc[m][0] = acc[m][1] = 0.0f;
+        for (int b = lane; b < NB; b += 32) {
+            const uint4 qa = nibs[(size_t)la * NB + b], qb = nibs[(size_t)lb * NB + b];
+            const float fa = f16_to_f32_ieee(scs[(size_t)la * NB + b]), fb = f16_to_f32_ieee(scs[(size_t)lb * NB + b]);
 #pragma unroll
             for (int m = 0; m < MB; ++m) {
-                acc[m][0] = warp_sum(acc[m][0]);
-                acc[m][1] = warp_sum(acc[m][1]);
-            }
-            if (lane == 0)
+                if (m < mb) {
+                    const uint4* Lm = L + (size_t)m * 6 * NB;
+                    uint4 Lb[6];
 #pragma unroll
-                for (int m = 0; m < MB; ++m)
-                    if (m < mb) epilogue<EPI>(c, a, row0 + m, ra, rb, acc[m][0], acc[m][1]);
+                    for (int v = 0; v < 6; ++v) Lb[v] = Lm[v * NB + b];
+                    const float x = xs[m * NB + b];
+                    acc[m][0] = __fmaf_rn(block_dp4a(qa, Lb), __fmul_rn(fa, x), acc[m][0]);
+                    acc[m][1] = __fmaf_rn(block_dp4a(qb, Lb), __fmul_rn(fb, x), acc[m][1]);
+                }
+            }
         }
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&empty[s])) : "memory");
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+            acc[m][0] = warp_sum(acc[m][0]);
+            acc[m][1] = warp_sum(acc[m][1]);
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int m = 0; m < MB; ++m)
+                if (m < mb) epilogue<EPI>(c, a, row0 + m, ra, rb, acc[m][0], acc[m][1]);
     }
 }
 
@@ -1106,14 +1110,18 @@ static cudaError_t launch_gemv_stream(const Ctx& c, const GemvArgs& a, int rows,
             sms = it->second;
         }
     }
-    const int stages = gemv_stream_stages(MB, a.W.k);
-    const size_t smem = (size_t)stages * kSStageBytes + gemv_smem_bytes(MB, a.W.k);
     const int ups = (int)(kSStageBytes / (2u * (uint32_t)(a.W.k / 32) * 18u));
     const int grid = (int)std::min<int64_t>(sms, a.n_units);
+    // no more stages than a CTA's share needs: a smaller CTA leaves room on the SM for the next kernel
+    // of the stream (launched as a programmatic dependent) while this one finishes
+    const int64_t per_cta = (a.n_units + grid - 1) / grid;
+    const int stages = (int)std::max<int64_t>(
+        2, std::min<int64_t>((int64_t)gemv_stream_stages(MB, a.W.k), (per_cta + ups - 1) / ups));
+    const size_t smem = (size_t)stages * kSStageBytes + gemv_smem_bytes(MB, a.W.k);
     for (int r0 = 0; r0 < rows; r0 += MB) {
         const int mb = rows - r0 < MB ? rows - r0 : MB;
-        const cudaError_t e = launch_pdl(gemv_stream_kernel<MB, EPI>, dim3(grid), dim3(kSThreads), smem, st, c, a, r0,
-                                         mb, ups, stages, err);
+        const cudaError_t e = launch_pdl(gemv_stream_kernel<MB, EPI>, dim3(grid), dim3(32 * (stream_cwarps<MB>() + 1)),
+                                         smem, st, c, a, r0, mb, ups, stages, err);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
