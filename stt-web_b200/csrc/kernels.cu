@@ -1090,9 +1090,14 @@ static int gemv_stream_stages(int mb, int k) {
     const int fit = (int)((kSmemLimit - std::min(kSmemLimit, limbs)) / kSStageBytes);
     return std::min(kSStages, fit);
 }
+// Which GEMV a launch takes.  The streamed kernel needs K a multiple of 256; it is the faster one
+// except for one batch row over a large matrix (more than 40 units per SM: the 16896-row linear_in),
+// where the register kernel's two resident CTAs per SM keep more loads in flight than one CTA's
+// chain of stages (measured on B200: 6.5 against 7.7 us for 16896 x 2048, device time).
 static bool gemv_streamed(const GemvArgs& a, int mb) {
     const int64_t row_bytes = (int64_t)(a.W.k / 32) * 18;
-    return a.W.k % 256 == 0 && 2 * row_bytes <= kSStageBytes && gemv_stream_stages(mb, a.W.k) >= 2;
+    if (a.W.k % 256 != 0 || 2 * row_bytes > kSStageBytes || gemv_stream_stages(mb, a.W.k) < 2) return false;
+    return !(mb == 1 && a.n_units > 40 * 148);
 }
 
 template <int MB, int EPI>

@@ -28,17 +28,17 @@
 // CTA-wide barrier inside the K loop:
 //   - warp 0 loads, per 256-wide quad of K, the 128 rows' Q4_0 nibbles (16 KB, 128-byte swizzle)
 //     and scales (2 KB) with two 2-D TMA loads into a ring of raw stages;
-//   - warp 10 copies, per 64-wide chunk, the activation tile (hi, lo) with bulk copies into a
+//   - warp 14 copies, per 64-wide chunk, the activation tile (hi, lo) with bulk copies into a
 //     ring of B stages;
-//   - warps 2..9 dequantise in two groups of four that take alternate chunks: one thread per
+//   - warps 2..13 dequantise in three groups of four that take the chunks in turn: one thread per
 //     weight row and chunk (two Q4_0 blocks), writing the hi and lo parts straight into a ring of
 //     A stages in tensor memory (tcgen05.st; weight row = TMEM lane), then signalling the stage
 //     with one arrive per warp;
 //   - warp 1 issues from one elected lane, per round of 1 to 3 chunks (TcCfg), 4 x 3 MMAs of
 //     128 x NT x 16 per chunk with A read from tensor memory and B from shared memory into the TMEM
 //     accumulator, and commits them to the barriers that free the A and B stages they read;
-//   - after the last commit, warps 2..9 read the accumulator (tcgen05.ld 32x32b; each warp its
-//     32 TMEM lanes and half of the batch columns) and store the partial sums.
+//   - after the last commit, warps 2..13 read the accumulator (tcgen05.ld 32x32b; each warp its
+//     32 TMEM lanes and a third of the batch columns) and store the partial sums.
 // The copy and MMA roles run as whole warps and issue from one elected lane (elect.sync).
 // Measured on the 16896 x 2048 product at 64 batch rows, the dequantisation sets the pace (the MMA
 // lane waits for the slowest dequantising warp) and its per-iteration overhead (waits, fences,
@@ -64,7 +64,8 @@ constexpr int kKC = 64;         // K elements per chunk (two Q4_0 blocks)
 constexpr int kQuad = 256;      // K elements per raw stage (8 blocks: 128 nibble bytes, 16 scale bytes per row)
 constexpr uint32_t kAStageCols = 64; // per A stage: hi part in 32 columns (64 f16 per lane), then lo
 constexpr uint32_t kTmemCols = 512;  // allocated TMEM columns (the whole SM's; one CTA per SM)
-constexpr int kDqWarps = 8;     // dequantising warps (2 .. 9, two groups of 4); warp 10 copies the activations
+constexpr int kDqGroups = 3;    // groups of four dequantising warps, taking chunks in turn
+constexpr int kDqWarps = 4 * kDqGroups;  // warps 2 .. 13; warp 14 copies the activations
 constexpr int kBWarp = 2 + kDqWarps;
 constexpr int kThreads = 32 * (kBWarp + 1);
 constexpr uint32_t kRNib = kTM * 128;  // raw nibble bytes per stage
@@ -291,10 +292,10 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
     if (t == 0) {
         for (int i = 0; i < kRS; ++i) {
             mbar_init(&sm.r_full[i], 1);
-            mbar_init(&sm.r_empty[i], kDqWarps);
+            mbar_init(&sm.r_empty[i], 16);  // each of a quad's 4 chunks is released by the 4 warps of its group
         }
         for (int i = 0; i < kAS; ++i) {
-            mbar_init(&sm.a_full[i], kDqWarps / 2);  // one group of four warps fills a stage
+            mbar_init(&sm.a_full[i], 4);  // one group of four warps fills a stage
             mbar_init(&sm.a_empty[i], 1);
         }
         for (int i = 0; i < NBS; ++i) {
@@ -402,18 +403,18 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         __syncwarp();
         pdl_trigger();
     } else if (warp >= 2) {
-        // dequantisers: two groups of four warps take alternate chunks (group 0 the even ones);
+        // dequantisers: kDqGroups groups of four warps take the chunks in turn (group g the chunks
+        // c = g mod kDqGroups);
         // a warp may only reach TMEM lanes 32 (warp % 4) .. +31, so thread -> weight row
         // 32 (warp % 4) + lane, and a thread dequantises the row's whole chunk (2 blocks, 8 words)
         const int grp = (warp - 2) >> 2;
         const int row = 32 * (warp & 3) + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
         const uint32_t rsw = (uint32_t)(row & 7);  // the swizzle's XOR for this row
-        for (int c = grp; c < nchunks; c += 2) {
+        for (int c = grp; c < nchunks; c += kDqGroups) {
             const int qi = c >> 2, cq = c & 3, s = qi % kRS, sa = c % kAS;
-            // lanes 0-15 poll the raw quad (this group's first chunk of a quad), lanes 16-31 the
-            // A stage, in one loop
-            const bool need = lane < 16 ? cq == grp : c >= kAS;
+            // lanes 0-15 poll the raw quad, lanes 16-31 the A stage, in one loop
+            const bool need = lane < 16 ? true : c >= kAS;
             uint64_t* const bar = lane < 16 ? &sm.r_full[s] : &sm.a_empty[sa];
             const uint32_t par = lane < 16 ? (uint32_t)(qi / kRS) & 1u : (uint32_t)((c / kAS) - 1) & 1u;
             if (!__all_sync(0xFFFFFFFFu, !need || mbar_wait(bar, par, abort, kNap))) break;  // the warp leaves together
@@ -439,7 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&sm.a_full[sa]);
-                if (cq == 2 + grp) mbar_arrive(&sm.r_empty[s]);  // this group's last chunk of the quad
+                mbar_arrive(&sm.r_empty[s]);  // this warp is done with the chunk's rows of the raw quad
             }
         }
         // accumulator -> partial sums (the done barrier completes after the last MMAs)
@@ -449,13 +450,13 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (__shfl_sync(0xFFFFFFFFu, *abort, 0) == 0) {  // warp-uniform: tcgen05.ld is warp-collective
-            const int quarter = warp & 3, grp = (warp - 2) >> 2;  // two column groups of 16
+            const int quarter = warp & 3, grp = (warp - 2) >> 2;  // kDqGroups column groups of 16
             const int trow = quarter * 32 + lane;
             const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
             float* pz = part + (int64_t)z * M * n + n0 + trow;
             const bool row_ok = n0 + trow < n;
 #pragma unroll 1
-            for (int j0 = grp * 16; j0 < NT; j0 += 32) {
+            for (int j0 = grp * 16; j0 < NT; j0 += 16 * kDqGroups) {
                 float v[16];
                 tmem_ld16(lane_addr + j0, v);
                 if (row_ok)
