@@ -160,7 +160,9 @@ class CpuJob:
 
     def __init__(self, streams=16, frames=2):
         from oracle import oracle as O
-        from stt_b200 import synth   # the generator library only: no decode library is loaded
+        from stt_b200 import synth   # the generator's Python wrapper only: no decode library is loaded
+        if synth._slib is None:      # the oracle's own build of the generator (same source and flags)
+            synth.SYNTH_LIB_PATH = os.path.join(REPO, "oracle", "libsynth.so")
         self.O = O
         self.cores = len(os.sched_getaffinity(0))
         O.set_threads(self.cores)    # torchrun sets OMP_NUM_THREADS=1; the baseline uses every core

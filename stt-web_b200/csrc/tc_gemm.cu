@@ -223,9 +223,11 @@ struct TcSmem {
     using C = TcCfg<NT>;
     uint8_t rnib[C::kRS][kRNib];                          // raw nibbles [128 rows][128 B], 128-byte swizzle
     uint8_t rsc[C::kRS][kRSc];                            // raw scales [128 rows][8]
-    uint8_t b[C::NBS][2][NT * kKC * 2];                   // [stage][hi, lo] activations, same layout
+    uint8_t b[2 * C::NBS][NT * kKC * 2];                  // activation parts, same layout: with lo parts
+                                                          // NBS stages of (hi, lo), without them 2 NBS
+                                                          // stages of hi parts only
     uint64_t r_full[C::kRS], r_empty[C::kRS], a_full[C::kAS], a_empty[C::kAS];
-    uint64_t b_full[C::NBS], b_empty[C::NBS], done;
+    uint64_t b_full[2 * C::NBS], b_empty[2 * C::NBS], done;
     uint32_t tmem;
     int abort;
 };
@@ -272,15 +274,19 @@ __device__ __forceinline__ void dequant_words(const uint32_t (&words)[W], uint16
 // x16 holds the hi parts, then (x_lo != 0) the lo parts, in the tiled order above; without lo
 // parts the input is taken as exact f16 and the hi.lo product is skipped.  Slice z covers the
 // quads [z * nq / slices, (z + 1) * nq / slices) of K.  part: [slices][M][n].
-template <int NT>
+template <int NT, bool XLO>
 __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constant__ CUtensorMap tm_nib,
                                                           const __grid_constant__ CUtensorMap tm_sc, int n, int K,
-                                                          const __half* __restrict__ x16, int x_lo, int M, int mtiles,
-                                                          int slices, float* __restrict__ part, int* __restrict__ err) {
+                                                          const __half* __restrict__ x16, int M, int mtiles, int slices,
+                                                          float* __restrict__ part, int* __restrict__ err) {
+    constexpr bool x_lo = XLO;
     extern __shared__ uint8_t tc_raw[];
     TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(tc_raw + ((1024u - (smem_u32(tc_raw) & 1023u)) & 1023u));
     using C = TcCfg<NT>;
-    constexpr int NBS = C::NBS, kRS = C::kRS, kAS = C::kAS, kStep = C::kStep;
+    constexpr int kRS = C::kRS, kAS = C::kAS, kStep = C::kStep;
+    // activation stages: without lo parts each stage holds one part, so there are twice as many
+    // (more copies in flight ahead of the MMAs in the same shared memory)
+    constexpr int NBS = XLO ? C::NBS : 2 * C::NBS;
     constexpr uint32_t kACol = C::kACol;
     constexpr uint32_t kBBytes = NT * kKC * 2;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -350,8 +356,9 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
                 break;
             if (elect_one()) {
                 mbar_expect_tx(&sm.b_full[sb], (x_lo ? 2u : 1u) * kBBytes);
-                bulk_g2s(sm.b[sb][0], xb + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
-                if (x_lo) bulk_g2s(sm.b[sb][1], xb + part_elems + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
+                uint8_t* const bh = x_lo ? sm.b[2 * sb] : sm.b[sb];
+                bulk_g2s(bh, xb + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
+                if (x_lo) bulk_g2s(sm.b[2 * sb + 1], xb + part_elems + (int64_t)c * (NT * kKC), kBBytes, &sm.b_full[sb]);
             }
             __syncwarp();
             bc = c + 1;
@@ -378,7 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
                     if (h >= nh) break;
                     const int sa = (c + h) % kAS, sb = (c + h) % NBS;
                     const uint32_t ah = tmem + kACol + sa * kAStageCols, al = ah + 32;
-                    const uint32_t bh = smem_u32(sm.b[sb][0]), bl = smem_u32(sm.b[sb][1]);
+                    const uint32_t bh = smem_u32(x_lo ? sm.b[2 * sb] : sm.b[sb]), bl = smem_u32(sm.b[2 * sb + 1]);
 #pragma unroll
                     for (int k16 = 0; k16 < kKC / 16; ++k16) {
                         // A: 8 TMEM columns per K = 16; B: two core matrices along K (LBO 128
@@ -494,15 +501,21 @@ TcPlan make_plan(int n, int k, int M, int num_sms) {
     return p;
 }
 
+template <int NT, bool XLO>
+cudaError_t launch_nt_x(const TcWeight& tw, const __half* x16, int M, const TcPlan& p, float* part, int* err,
+                        cudaStream_t st) {
+    const size_t smem = smem_bytes<NT>();
+    cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT, XLO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(p.tiles, p.mtiles, p.slices);
+    return launch_pdl(q4_tc_kernel<NT, XLO>, grid, dim3(kThreads), smem, st, tw.nib, tw.sc, tw.n, tw.k, x16, M,
+                      p.mtiles, p.slices, part, err);
+}
+
 template <int NT>
 cudaError_t launch_nt(const TcWeight& tw, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
                       cudaStream_t st) {
-    const size_t smem = smem_bytes<NT>();
-    cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid(p.tiles, p.mtiles, p.slices);
-    return launch_pdl(q4_tc_kernel<NT>, grid, dim3(kThreads), smem, st, tw.nib, tw.sc, tw.n, tw.k, x16, x_lo, M,
-                      p.mtiles, p.slices, part, err);
+    return x_lo ? launch_nt_x<NT, true>(tw, x16, M, p, part, err, st) : launch_nt_x<NT, false>(tw, x16, M, p, part, err, st);
 }
 
 cudaError_t launch_gemm(const TcWeight& tw, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,

@@ -13,6 +13,8 @@ from dataclasses import dataclass
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
+# The generator library this module loads (on first use).  A program that must not map anything of
+# the decode package (the CPU baseline) points it at another build of the same source first.
 SYNTH_LIB_PATH = os.path.join(_HERE, "libsttsynth.so")
 
 GGML_F32, GGML_Q4_0, GGML_BF16 = 0, 2, 30
