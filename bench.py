@@ -102,6 +102,41 @@ def loaded_libraries():
     return sorted(out)
 
 
+TRACE_NAMES = {1: "frame_start", 11: "qkv_inputs", 12: "qkv_gemv", 13: "qkv_end", 21: "attention_inputs",
+               22: "attention", 24: "attention_merge", 23: "attention_end", 31: "out_proj_inputs",
+               32: "out_proj_gemv", 33: "out_proj_end", 41: "linear_in_inputs", 42: "linear_in_gemv",
+               43: "linear_in_end", 51: "linear_out_inputs", 52: "linear_out_gemv", 53: "linear_out_end",
+               61: "head_inputs", 62: "head_gemv", 63: "head_partial", 7: "argmax"}
+LAYER_TAGS = [11, 12, 13, 21, 22, 24, 23, 31, 32, 33, 41, 42, 43, 51, 52, 53]
+HEAD_TAGS = [61, 62, 63, 7]
+
+
+def critical_path(buf, n_ctas, n_slots, layers):
+    """Every CTA's %globaltimer stamps of one traced frame of the persistent kernel -> how far the
+    latest CTA moves at each kind of mark (the frame's critical path), in microseconds per frame."""
+    import numpy as np
+    t = np.array(buf, dtype=np.int64).reshape(n_ctas, n_slots)
+    starts = t[:, 0][t[:, 0] > 0]
+    if starts.size == 0:
+        return {}
+    order = [(1 + 16 * l + i, tag) for l in range(layers) for i, tag in enumerate(LAYER_TAGS)]
+    order += [(1 + 16 * layers + i, tag) for i, tag in enumerate(HEAD_TAGS)]
+    prev = int(starts.max())
+    crit = {}
+    last = prev
+    for slot, tag in order:
+        v = t[:, slot][t[:, slot] > 0]
+        if v.size == 0:
+            continue
+        mx = int(v.max())
+        name = TRACE_NAMES.get(tag, str(tag))
+        crit[name] = crit.get(name, 0.0) + (mx - prev) / 1e3
+        prev = mx
+        last = mx
+    return {"frame_us_all_ctas": round((last - int(starts.min())) / 1e3, 1),
+            "critical_path_us": {k: round(v, 1) for k, v in crit.items()}}
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -580,6 +615,16 @@ def main():
         fx = os.path.join(REPO, "tests", "golden", "bench_tokens.json")
         if rank == 0 and os.path.exists(fx):
             s1["tokens_identical_to_oracle"] = bool(np.array_equal(toks1, np.array(json.load(open(fx))["stream0_750"])))
+        # where a late frame's time goes: every CTA's stamps of frame 740 (stt_debug_trace_frame)
+        check(lib().stt_debug_trace_frame(c1._h, UTT_FRAMES - 10), "trace_frame")
+        utterance()
+        torch.cuda.synchronize()
+        cap = 148 * 1024
+        tb = (C.c_uint64 * cap)()
+        n_ctas, n_slots = C.c_int(), C.c_int()
+        if lib().stt_debug_get_trace_ctas(c1._h, tb, cap, C.byref(n_ctas), C.byref(n_slots)) == 0:
+            s1["trace_frame_740"] = critical_path(list(tb[:n_ctas.value * n_slots.value]), n_ctas.value, n_slots.value, 16)
+        check(lib().stt_debug_trace_frame(c1._h, -1), "trace_frame")
         c1.close()
         line["stream1"] = s1
 
