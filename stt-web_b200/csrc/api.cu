@@ -314,6 +314,7 @@ struct stt_model {
     const float2* rope = nullptr;
     bool tc_ok = false;  // every layer product and the head fit the tensor-core path
     std::vector<TcWeight> tc_w;  // their TMA descriptors: 4 per layer (qkv, out, fin, fout), then the head
+    std::vector<GemvMaps> gemv_maps;  // the GEMV's TMA descriptors, in the same order
     const uint8_t* emb_audio = nullptr;
     const uint8_t* emb_text = nullptr;
     float attn_scale = 0.0f;
@@ -617,6 +618,9 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
             L.norm2 = dn + (size_t)(2 * l + 1) * m->D;
         }
         m->head = qd.back();
+        m->gemv_maps.resize(qd.size());
+        for (size_t i = 0; i < qd.size(); ++i)
+            if (gemv_make_maps(qd[i], &m->gemv_maps[i]) != cudaSuccess) m->gemv_maps[i].ok = false;
         m->tc_ok = big == 0;
         for (const Q4Dev& w : qd) m->tc_ok = m->tc_ok && tc_gemm_supported(w);
         if (m->tc_ok) {
@@ -800,27 +804,28 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
         CUDA_TRY(launch_finish(c, st));
         return STT_OK;
     }
+    const GemvMaps* gm = m->gemv_maps.data();
     for (int l = 0; l < m->L; ++l) {
         const LayerDev& L = m->h_layers[l];
         GemvArgs a{};
         a.W = L.qkv; a.in = s->d_x; a.norm = L.norm1; a.out = s->d_qkv; a.ldo = 3 * m->D; a.layer = l;
-        a.n_units = 3 * m->D / 2;
+        a.n_units = 3 * m->D / 2; a.maps = &gm[4 * l + 0];
         CUDA_TRY(launch_gemv(c, a, EPI_QKV, n, st));
         CUDA_TRY(launch_attention(c, l, st));
         a = GemvArgs{};
-        a.W = L.out; a.in = s->d_attn; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
+        a.W = L.out; a.in = s->d_attn; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2; a.maps = &gm[4 * l + 1];
         CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, st));
         a = GemvArgs{};
         a.W = L.fin; a.in = s->d_x; a.norm = L.norm2; a.out = s->d_hid; a.ldo = m->F; a.n_units = m->F;
-        a.half_n = m->F;
+        a.half_n = m->F; a.maps = &gm[4 * l + 2];
         CUDA_TRY(launch_gemv(c, a, EPI_GATE, n, st));
         a = GemvArgs{};
-        a.W = L.fout; a.in = s->d_hid; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2;
+        a.W = L.fout; a.in = s->d_hid; a.out = s->d_x; a.ldo = m->D; a.n_units = m->D / 2; a.maps = &gm[4 * l + 3];
         CUDA_TRY(launch_gemv(c, a, EPI_RESID, n, st));
     }
     GemvArgs a{};
     a.W = m->head; a.in = s->d_x; a.norm = m->out_norm; a.out = s->d_logits; a.ldo = m->V;
-    a.n_units = (m->V + 1) / 2;
+    a.n_units = (m->V + 1) / 2; a.maps = &gm[4 * m->L];
     CUDA_TRY(launch_gemv(c, a, EPI_LOGITS, n, st));
     CUDA_TRY(launch_finish(c, st));
     return STT_OK;
@@ -1375,6 +1380,7 @@ struct stt_q4_tensor {
     int* d_err = nullptr;  // timeout flag of the tensor-core kernel (inside mem)
     bool tc_ok = false;    // shape and scales fit the tensor-core kernel
     TcWeight tc_w{};       // its TMA descriptors
+    GemvMaps gemv_maps{};  // the GEMV's TMA descriptors
     mutable DevBuf tc_x16, tc_part;  // its scratch, grown on demand
 };
 
@@ -1411,6 +1417,7 @@ extern "C" int stt_q4_tensor_create(const uint8_t* bytes, size_t n_bytes, int n,
     t->d_err = reinterpret_cast<int*>(static_cast<uint8_t*>(t->mem) + nib_bytes + sc_bytes);
     t->tc_ok = tc_gemm_supported(t->w) && tc_gemm_scales_ok(bytes, (int64_t)nblk) &&
                tc_make_weight(t->w, &t->tc_w) == cudaSuccess;
+    if (gemv_make_maps(t->w, &t->gemv_maps) != cudaSuccess) t->gemv_maps.ok = false;
     CUDA_TRY(cudaMemset(t->d_err, 0, sizeof(int)));
     DevBuf staging;
     TRY(staging.ensure(n_bytes));
@@ -1462,6 +1469,7 @@ extern "C" int stt_q4_matmul_device(const stt_q4_tensor* t, const void* d_in, in
     a.ldo = t->w.n;
     a.n_units = (t->w.n + 1) / 2;
     a.err = t->d_err;
+    a.maps = &t->gemv_maps;
     CUDA_TRY(launch_gemv(c, a, EPI_PLAIN, rows, static_cast<cudaStream_t>(cuda_stream)));
     return STT_OK;
 }

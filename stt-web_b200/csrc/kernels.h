@@ -1,11 +1,21 @@
 // Host-side launchers of the step kernels (kernels.cu).
 #pragma once
 
+#include <cuda.h>
+
 #include "device.cuh"
 
 namespace stt {
 
 constexpr int kMaxGemvK = 8448;  // largest reduction length the GEMV stages in shared memory
+
+// TMA descriptors of one Q4 weight for the tensor-core GEMV (gemv_mma_kernel): boxes of 8 rows of
+// one quad of nibbles (128 bytes) and of 64 scales (128 bytes), both with the 128-byte swizzle.
+struct GemvMaps {
+    CUtensorMap nib, sc;
+    bool ok = false;  // K a multiple of 256 and both descriptors built
+};
+cudaError_t gemv_make_maps(const Q4Dev& w, GemvMaps* out);
 
 enum Epi : int { EPI_PLAIN = 0, EPI_QKV = 1, EPI_GATE = 2, EPI_RESID = 3, EPI_LOGITS = 4 };
 
@@ -21,6 +31,7 @@ struct GemvArgs {
     int32_t n_units;                 // pairs of output rows
     int32_t half_n;                  // EPI_GATE: value rows start here (= ffn width)
     int* err;                        // where a kernel records a timeout when there is no step descriptor
+    const GemvMaps* maps;            // host copy of W's GEMV descriptors, or NULL (host side only)
 };
 
 // Per-call descriptor and batch ids, written on the device from launch parameters so that

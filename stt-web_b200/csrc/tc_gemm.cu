@@ -695,7 +695,8 @@ bool tc_gemm_scales_ok(const uint8_t* q4_blocks, int64_t nblocks) {
     return true;
 }
 
-cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out) {
+cudaError_t tma_encode(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank, const uint64_t* dims,
+                       const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle) {
     // The driver's encoder, looked up once; a function-local static is initialised exactly once
     // even when threads load models on several devices at the same time.
     struct EncodeFn {
@@ -712,30 +713,39 @@ cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out) {
         return r;
     }();
     if (lookup.err != cudaSuccess) return lookup.err;
-    const PFN_cuTensorMapEncodeTiled_v12000 encode = lookup.fn;
-    const cuuint64_t nb = (cuuint64_t)(w.k / 32);
+    if (rank < 1 || rank > 5) return cudaErrorInvalidValue;
+    cuuint64_t d[5], st[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+        es[i] = 1;
+        if (i + 1 < rank) st[i] = strides[i];
+    }
+    if (lookup.fn(map, type, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    return cudaSuccess;
+}
+
+cudaError_t tma_encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner,
+                          uint64_t rows, uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows,
+                          CUtensorMapSwizzle swizzle) {
+    const uint64_t dims[2] = {inner, rows};
+    const uint32_t box[2] = {box_inner, box_rows};
+    return tma_encode(map, type, base, 2, dims, &row_bytes, box, swizzle);
+}
+
+cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out) {
+    const uint64_t nb = (uint64_t)(w.k / 32);
     // nibble plane: [n rows][k/32 * 16 bytes]; a box is one quad (128 bytes) of 128 rows
-    {
-        const cuuint64_t dims[2] = {nb * 16, (cuuint64_t)w.n};
-        const cuuint64_t strides[1] = {nb * 16};
-        const cuuint32_t box[2] = {128, (cuuint32_t)kTM};
-        const cuuint32_t estr[2] = {1, 1};
-        if (encode(&out->nib, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint4*>(w.nib), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
+    cudaError_t e = tma_encode_2d(&out->nib, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, nb * 16, (uint64_t)w.n, nb * 16,
+                                  128, (uint32_t)kTM, CU_TENSOR_MAP_SWIZZLE_128B);
     // scale plane: [n rows][k/32 scales]; a box is one quad (8 scales, 16 bytes) of 128 rows
-    {
-        const cuuint64_t dims[2] = {nb, (cuuint64_t)w.n};
-        const cuuint64_t strides[1] = {nb * 2};
-        const cuuint32_t box[2] = {8, (cuuint32_t)kTM};
-        const cuuint32_t estr[2] = {1, 1};
-        if (encode(&out->sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(w.scale), dims, strides, box,
-                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
+    if (e == cudaSuccess)
+        e = tma_encode_2d(&out->sc, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.scale, nb, (uint64_t)w.n, nb * 2, 8,
+                          (uint32_t)kTM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (e != cudaSuccess) return e;
     out->n = w.n;
     out->k = w.k;
     return cudaSuccess;

@@ -24,6 +24,16 @@ struct TcWeight {
 };
 cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out);
 
+// A TMA descriptor of `rank` dimensions (dims[0] contiguous; strides[i] = byte stride of dimension
+// i + 1) with a box of box[i] elements per dimension; loads outside the array read zeros.
+cudaError_t tma_encode(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank, const uint64_t* dims,
+                       const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle);
+// A 2-D TMA descriptor of a row-major [rows][inner] array of `type` (rows row_bytes apart) with a
+// box of box_inner x box_rows elements; loads outside the array read zeros.
+cudaError_t tma_encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner,
+                          uint64_t rows, uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows,
+                          CUtensorMapSwizzle swizzle);
+
 // Scratch of one product of M batch rows: the tiled f16 input (hi and lo parts) and the K-slice
 // partial sums.
 size_t tc_x16_bytes(int k, int M);

@@ -12,6 +12,8 @@ initial text token 0, the benchmark's seed and audio).
   configuration 4  the 512-stream, 250-frame job itself: streams 0..15 checked at every frame; and
                    260 streams (two 256-row tiles of the tensor-core GEMM) over 8 frames, every
                    stream checked
+  small batches    9 streams at staggered positions through the GEMV path (batches under 16
+                   streams): raw batched steps, logits against the oracle
 
 Token comparison and the near-tie accounting are those of tests/parity.py: a difference is only
 excused where the oracle's top-2 logit margin is below the measured logit agreement (1e-2 with bf16
@@ -184,6 +186,39 @@ def test_config4_two_full_tiles_every_stream(bench_model, kv):
         # are compared instead
         fol.step(list(range(S)), audio, got, f"frame {f}", states=cache.state)
     print(fol.report(f"260 streams x 8 frames, {kv} K/V"))
+
+
+def test_full_size_small_batch_gemv_path(bench_model):
+    """Batches under 16 streams run every layer product on the GEMV with its fused prologues and
+    epilogues (RMSNorm, RoPE and the K/V write, the gate, the residuals, the head): 9 streams take
+    one pass of 8 batch rows and one of 1 (4 + 4 + 1 for the K = 8448 product), the integer-MMA
+    kernel for the passes of several rows.  Streams pre-rolled to staggered positions, then raw
+    batched steps with f32 K/V: logits within 1e-3 of the oracle, the argmax equal away from
+    near-ties; both sides continue from the oracle's tokens."""
+    g, cfg, model, om = bench_model
+    n = 9
+    cache = model.create_cache(n, "f32")
+    refs = [om.stream(0) for _ in range(n)]
+    for s in range(1, n):  # stream s starts at position 2s
+        a = stt_b200.audio_tokens(31, s, 2 * s)
+        for f in range(2 * s):
+            model.forward(a[f], 0, cache, s)
+            refs[s].forward(a[f], 0, want_logits=False)
+    order = [4, 0, 8, 2, 7, 1, 5, 3, 6]
+    texts = [0] * n
+    worst = 0.0
+    for step in range(4):
+        audio = np.stack([stt_b200.audio_tokens(31, s, 1, first_frame=2 * s + step)[0] for s in order])
+        lg, am = cache.forward(order, audio, [texts[s] for s in order])
+        lo, ao = O.forward_batch([refs[s] for s in order], audio, [texts[s] for s in order])
+        worst = max(worst, float(np.abs(lg - lo).max()))
+        mg = margins(lo)
+        assert all(int(am[i]) == int(ao[i]) or mg[i] < EXEMPT_MARGIN for i in range(n)), step
+        for i, s in enumerate(order):
+            texts[s] = int(ao[i])
+    print(f"9 streams through the GEMV path: max |logit - oracle| = {worst:.3g}")
+    assert worst < 1e-3
+    cache.close()
 
 
 def test_full_size_q4_0_embeddings_from_shards():

@@ -49,8 +49,10 @@ def test_dequant_subnormal_and_edge_scales():
 
 
 @pytest.mark.parametrize("n,k", SHAPES)
-@pytest.mark.parametrize("m", [1, 4, 16])
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 7, 16])
 def test_q4_matmul_matches_oracle(n, k, m):
+    """Batches of 1 to 8 rows take one pass of the GEMV (16 rows: two passes of 8, or four of 4
+    when K > 4096); 3 and 7 rows leave batch columns of the pass unused."""
     raw = q4_bytes(n, k, 7 * n + k)
     x = np.random.default_rng(m).standard_normal((1, m, k)).astype(np.float32)
     t = stt_b200.Q4Tensor.from_q4_bytes(raw, (n, k))
