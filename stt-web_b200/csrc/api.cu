@@ -313,6 +313,7 @@ struct stt_model {
     const float* out_norm = nullptr;
     const float2* rope = nullptr;
     bool tc_ok = false;  // every layer product and the head fit the tensor-core path
+    bool tc_gate_ok = false;  // and every linear_in can take the gate into its epilogue
     std::vector<TcWeight> tc_w;  // their TMA descriptors: 4 per layer (qkv, out, fin, fout), then the head
     std::vector<GemvMaps> gemv_maps;  // the GEMV's TMA descriptors, in the same order
     const uint8_t* emb_audio = nullptr;
@@ -627,6 +628,10 @@ extern "C" int stt_model_load_gguf(const uint8_t* const* shards, const size_t* s
             m->tc_w.resize(qd.size());
             for (size_t i = 0; i < qd.size(); ++i)
                 if (tc_make_weight(qd[i], &m->tc_w[i]) != cudaSuccess) m->tc_ok = false;
+            m->tc_gate_ok = m->tc_ok;
+            for (int l = 0; l < m->L && m->tc_gate_ok; ++l)
+                m->tc_gate_ok = tc_make_gate_maps(qd[4 * l + 2], &m->tc_w[4 * l + 2]) == cudaSuccess &&
+                                m->tc_w[4 * l + 2].gate_ok;
         }
         m->out_norm = dn + (size_t)(2 * m->L) * m->D;
     }
@@ -690,6 +695,7 @@ struct stt_streams {
     float *d_x = nullptr, *d_qkv = nullptr, *d_attn = nullptr, *d_hid = nullptr, *d_logits = nullptr, *d_part = nullptr;
     uint32_t* d_tickets = nullptr;
     __half* d_x16 = nullptr;    // f16 GEMM inputs of a batched step on the tensor cores
+    __half* d_x16b = nullptr;   // linear_out's inputs when the gate is fused into linear_in
     float* d_tc_part = nullptr; // their K-slice partial sums
     int32_t* d_ids = nullptr;
     StepDesc* d_desc = nullptr;
@@ -781,6 +787,9 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
         int* err = &s->d_desc->error;  // a GEMM timeout raises STT_E_DEVICE_FLAG like any step kernel
         int slices = 0;
         const bool x_lo = s->product_precision == STT_PRODUCTS_F16X3;
+        // STT_UNFUSED_GATE (read when a batch size's graph is built) keeps linear_in and the gate
+        // as two kernels, for the test that compares them
+        const bool gate_fused = m->tc_gate_ok && std::getenv("STT_UNFUSED_GATE") == nullptr;
         CUDA_TRY(launch_tc_prep(s->d_x, m->h_layers[0].norm1, m->D, n, s->d_x16, st));
         for (int l = 0; l < m->L; ++l) {
             const LayerDev& L = m->h_layers[l];
@@ -791,9 +800,14 @@ int enqueue_step(stt_streams* s, int n, cudaStream_t st) {
             CUDA_TRY(launch_attention(ca, l, st));
             CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 1], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
             CUDA_TRY(launch_tc_resid_norm(s->d_x, part, slices, n, m->D, L.norm2, s->d_x16, st));
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 2], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
-            CUDA_TRY(launch_tc_gate(part, slices, n, m->F, s->d_x16, st));
-            CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 3], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
+            if (gate_fused) {  // the gate in linear_in's epilogue, its output in the second input buffer
+                CUDA_TRY(launch_tc_product_gate(m->tc_w[4 * l + 2], s->d_x16, n, s->d_x16b, err, st, x_lo));
+                CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 3], s->d_x16b, n, part, err, m->num_sms, &slices, st, x_lo));
+            } else {
+                CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 2], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
+                CUDA_TRY(launch_tc_gate(part, slices, n, m->F, s->d_x16, st));
+                CUDA_TRY(launch_tc_product(m->tc_w[4 * l + 3], s->d_x16, n, part, err, m->num_sms, &slices, st, x_lo));
+            }
             const float* next_norm = l + 1 < m->L ? m->h_layers[l + 1].norm1 : m->out_norm;
             CUDA_TRY(launch_tc_resid_norm(s->d_x, part, slices, n, m->D, next_norm, s->d_x16, st));
         }
@@ -1031,6 +1045,7 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
             tc_part_bytes_max = std::max(tc_part_bytes_max, tc_part_bytes(m->head, rows, m->num_sms));
         }
     const size_t o_x16 = take(x16_bytes);
+    const size_t o_x16b = take(m->tc_gate_ok ? x16_bytes : 0);
     const size_t o_tc_part = take(tc_part_bytes_max);
     const size_t o_trace_ctas = take((size_t)m->num_sms * kTraceSlots * sizeof(unsigned long long));
     if (dev_alloc(&s->d_scratch, off) != cudaSuccess) {
@@ -1065,6 +1080,7 @@ extern "C" int stt_streams_create(stt_model* m, int n_streams, int kv_dtype, stt
     s->mega.trace = reinterpret_cast<unsigned long long*>(b + o_trace);
     s->mega.trace_cap = kTraceCap;
     s->d_x16 = reinterpret_cast<__half*>(b + o_x16);
+    s->d_x16b = reinterpret_cast<__half*>(b + o_x16b);
     s->d_tc_part = reinterpret_cast<float*>(b + o_tc_part);
     s->mega.trace_ctas = reinterpret_cast<unsigned long long*>(b + o_trace_ctas);
     s->mega.trace_slots = kTraceSlots;

@@ -69,15 +69,14 @@ __device__ __forceinline__ void quad_limbs_store(uint4* L, float* xs, int q, int
     e = max(-96, min(e, 120));
     const float up = __uint_as_float((uint32_t)(127 + 23 - e) << 23);
     const float vals[4] = {v.x, v.y, v.z, v.w};
-    uint32_t w0 = 0, w1 = 0, w2 = 0;
+    uint32_t X[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        int X = __float2int_rn(vals[i] * up);
-        X = max(-(1 << 23), min(X, (1 << 23) - 1));
-        w0 |= (uint32_t)(X & 0xFF) << (8 * i);
-        w1 |= (uint32_t)((X >> 8) & 0xFF) << (8 * i);
-        w2 |= (uint32_t)((X >> 16) & 0xFF) << (8 * i);
-    }
+    for (int i = 0; i < 4; ++i) X[i] = (uint32_t)max(-(1 << 23), min(__float2int_rn(vals[i] * up), (1 << 23) - 1));
+    // limb v of the four elements = byte v of each X (two's complement: byte 2 is the signed top)
+    const uint32_t t01 = __byte_perm(X[0], X[1], 0x5140), t23 = __byte_perm(X[2], X[3], 0x5140);
+    const uint32_t u01 = __byte_perm(X[0], X[1], 0x0062), u23 = __byte_perm(X[2], X[3], 0x0062);
+    const uint32_t w0 = __byte_perm(t01, t23, 0x5410), w1 = __byte_perm(t01, t23, 0x7632);
+    const uint32_t w2 = __byte_perm(u01, u23, 0x5410);
     if (!store) return;
     uint32_t* W = reinterpret_cast<uint32_t*>(L);
     const int base = g < 4 ? 0 : 3;

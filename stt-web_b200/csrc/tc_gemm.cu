@@ -178,6 +178,27 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uin
         ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
 }
+// Named barrier of `count` threads; bar_any also returns whether any of them passed cond.
+__device__ __forceinline__ void bar_sync_n(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool bar_any(int id, int count, bool cond) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)cond), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+// silu(g) = g * (1 / (1 + exp(-g))), times the value: the GEMV's gate epilogue.
+__device__ __forceinline__ float gated(float g, float v) {
+    return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), v);
+}
+
 // True in exactly one lane of the (converged) warp.
 __device__ __forceinline__ bool elect_one() {
     uint32_t pred;
@@ -274,11 +295,18 @@ __device__ __forceinline__ void dequant_words(const uint32_t (&words)[W], uint16
 // x16 holds the hi parts, then (x_lo != 0) the lo parts, in the tiled order above; without lo
 // parts the input is taken as exact f16 and the hi.lo product is skipped.  Slice z covers the
 // quads [z * nq / slices, (z + 1) * nq / slices) of K.  part: [slices][M][n].
-template <int NT, bool XLO>
+//
+// GATE (linear_in, one slice): the maps' boxes are 64 rows high, and CTA x loads the gate rows
+// 64x .. 64x+63 into tile rows 0..63 and their value rows gate_f + 64x .. into tile rows 64..127;
+// instead of partial sums the epilogue writes silu(gate) * value of its 64 units straight into the
+// next product's input x16_out (gate_f columns, hi and lo parts; rows_pad = mtiles * NT), the
+// gate_kernel's arithmetic.
+template <int NT, bool XLO, bool GATE>
 __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constant__ CUtensorMap tm_nib,
                                                           const __grid_constant__ CUtensorMap tm_sc, int n, int K,
                                                           const __half* __restrict__ x16, int M, int mtiles, int slices,
-                                                          float* __restrict__ part, int* __restrict__ err) {
+                                                          float* __restrict__ part, int* __restrict__ err,
+                                                          __half* __restrict__ x16_out, int gate_f) {
     constexpr bool x_lo = XLO;
     extern __shared__ uint8_t tc_raw[];
     TcSmem<NT>& sm = *reinterpret_cast<TcSmem<NT>*>(tc_raw + ((1024u - (smem_u32(tc_raw) & 1023u)) & 1023u));
@@ -334,8 +362,16 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
                 break;
             if (elect_one()) {
                 mbar_expect_tx(&sm.r_full[s], kRNib + kRSc);
-                tma_load_2d(sm.rnib[s], &tm_nib, (q0 + qi) * 128, n0, &sm.r_full[s]);
-                tma_load_2d(sm.rsc[s], &tm_sc, (q0 + qi) * 8, n0, &sm.r_full[s]);
+                if (GATE) {
+                    const int g0 = blockIdx.x * (kTM / 2);
+                    tma_load_2d(sm.rnib[s], &tm_nib, (q0 + qi) * 128, g0, &sm.r_full[s]);
+                    tma_load_2d(sm.rnib[s] + kRNib / 2, &tm_nib, (q0 + qi) * 128, gate_f + g0, &sm.r_full[s]);
+                    tma_load_2d(sm.rsc[s], &tm_sc, (q0 + qi) * 8, g0, &sm.r_full[s]);
+                    tma_load_2d(sm.rsc[s] + kRSc / 2, &tm_sc, (q0 + qi) * 8, gate_f + g0, &sm.r_full[s]);
+                } else {
+                    tma_load_2d(sm.rnib[s], &tm_nib, (q0 + qi) * 128, n0, &sm.r_full[s]);
+                    tma_load_2d(sm.rsc[s], &tm_sc, (q0 + qi) * 8, n0, &sm.r_full[s]);
+                }
             }
             __syncwarp();
             rq = qi + 1;
@@ -456,7 +492,41 @@ __global__ void __launch_bounds__(kThreads, 1) q4_tc_kernel(const __grid_constan
         mbar_drain(&sm.done, 0);
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (__shfl_sync(0xFFFFFFFFu, *abort, 0) == 0) {  // warp-uniform: tcgen05.ld is warp-collective
+        if (GATE) {
+            // gate rows are tile rows 0..63 (quarters 0 and 1), their value rows 64..127 (quarters 2
+            // and 3).  Per 16 columns, the group's value warps hand their sums to its gate warps through
+            // shared memory (the raw weight stages are idle now), the gate warps form silu(g) * v, and
+            // the group's 128 threads write one 8-element piece of x16_out each.  The group agrees on
+            // the abort word first, so that its warps meet the same barriers.
+            const int quarter = warp & 3, grp = (warp - 2) >> 2;
+            const int trow = quarter * 32 + lane, gt = trow;  // gt: thread of the group, 0..127
+            const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+            float* S = reinterpret_cast<float*>(sm.rnib[0]) + grp * (16 * 64);  // [16 columns][64 units]
+            const int rows_pad = mtiles * NT;
+            if (!bar_any(1 + grp, 128, *abort != 0)) {
+                for (int j0 = grp * 16; j0 < NT; j0 += 16 * kDqGroups) {
+                    float v[16];
+                    tmem_ld16(lane_addr + j0, v);
+                    if (quarter >= 2)
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) S[jj * 64 + trow - 64] = v[jj];
+                    bar_sync_n(1 + grp, 128);
+                    if (quarter < 2)
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) S[jj * 64 + trow] = gated(v[jj], S[jj * 64 + trow]);
+                    bar_sync_n(1 + grp, 128);
+                    const int jj = gt >> 3, pw = gt & 7;  // column, and piece of the tile's 64 units
+                    const int m = mt * NT + j0 + jj;
+                    if (m < M) {
+                        const float* sp = S + jj * 64 + (pw >> 2) * 32 + 4 * (pw & 3);
+                        x16_store_piece(x16_out, NT, rows_pad, gate_f, m, 8 * blockIdx.x + pw,
+                                        make_float4(sp[0], sp[1], sp[2], sp[3]),
+                                        make_float4(sp[16], sp[17], sp[18], sp[19]), true);
+                    }
+                    bar_sync_n(1 + grp, 128);
+                }
+            }
+        } else if (__shfl_sync(0xFFFFFFFFu, *abort, 0) == 0) {  // warp-uniform: tcgen05.ld is warp-collective
             const int quarter = warp & 3, grp = (warp - 2) >> 2;  // kDqGroups column groups of 16
             const int trow = quarter * 32 + lane;
             const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
@@ -501,31 +571,42 @@ TcPlan make_plan(int n, int k, int M, int num_sms) {
     return p;
 }
 
-template <int NT, bool XLO>
+// Gate mode: the descriptors are tw's 64-row ones and x16_out receives silu(gate) * value.
+struct TcGate {
+    __half* x16_out;
+    int f;
+};
+
+template <int NT, bool XLO, bool GATE>
 cudaError_t launch_nt_x(const TcWeight& tw, const __half* x16, int M, const TcPlan& p, float* part, int* err,
-                        cudaStream_t st) {
+                        const TcGate& gt, cudaStream_t st) {
     const size_t smem = smem_bytes<NT>();
-    cudaError_t e = cudaFuncSetAttribute(q4_tc_kernel<NT, XLO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e =
+        cudaFuncSetAttribute(q4_tc_kernel<NT, XLO, GATE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p.tiles, p.mtiles, p.slices);
-    return launch_pdl(q4_tc_kernel<NT, XLO>, grid, dim3(kThreads), smem, st, tw.nib, tw.sc, tw.n, tw.k, x16, M,
-                      p.mtiles, p.slices, part, err);
+    return launch_pdl(q4_tc_kernel<NT, XLO, GATE>, grid, dim3(kThreads), smem, st, GATE ? tw.nib64 : tw.nib,
+                      GATE ? tw.sc64 : tw.sc, tw.n, tw.k, x16, M, p.mtiles, p.slices, part, err, gt.x16_out, gt.f);
 }
 
 template <int NT>
 cudaError_t launch_nt(const TcWeight& tw, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
-                      cudaStream_t st) {
-    return x_lo ? launch_nt_x<NT, true>(tw, x16, M, p, part, err, st) : launch_nt_x<NT, false>(tw, x16, M, p, part, err, st);
+                      const TcGate* gt, cudaStream_t st) {
+    const TcGate none{nullptr, 0};
+    if (gt) return x_lo ? launch_nt_x<NT, true, true>(tw, x16, M, p, part, err, *gt, st)
+                        : launch_nt_x<NT, false, true>(tw, x16, M, p, part, err, *gt, st);
+    return x_lo ? launch_nt_x<NT, true, false>(tw, x16, M, p, part, err, none, st)
+                : launch_nt_x<NT, false, false>(tw, x16, M, p, part, err, none, st);
 }
 
 cudaError_t launch_gemm(const TcWeight& tw, const __half* x16, int x_lo, int M, const TcPlan& p, float* part, int* err,
-                        cudaStream_t st) {
+                        cudaStream_t st, const TcGate* gt = nullptr) {
     switch (p.nt) {
-        case 16: return launch_nt<16>(tw, x16, x_lo, M, p, part, err, st);
-        case 32: return launch_nt<32>(tw, x16, x_lo, M, p, part, err, st);
-        case 64: return launch_nt<64>(tw, x16, x_lo, M, p, part, err, st);
-        case 128: return launch_nt<128>(tw, x16, x_lo, M, p, part, err, st);
-        default: return launch_nt<256>(tw, x16, x_lo, M, p, part, err, st);
+        case 16: return launch_nt<16>(tw, x16, x_lo, M, p, part, err, gt, st);
+        case 32: return launch_nt<32>(tw, x16, x_lo, M, p, part, err, gt, st);
+        case 64: return launch_nt<64>(tw, x16, x_lo, M, p, part, err, gt, st);
+        case 128: return launch_nt<128>(tw, x16, x_lo, M, p, part, err, gt, st);
+        default: return launch_nt<256>(tw, x16, x_lo, M, p, part, err, gt, st);
     }
 }
 
@@ -640,11 +721,6 @@ __global__ void __launch_bounds__(512) resid_norm_kernel(float* __restrict__ x, 
     }
 }
 
-// silu(g) = g * (1 / (1 + exp(-g))), times the value: the GEMV's gate epilogue.
-__device__ __forceinline__ float gated(float g, float v) {
-    return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), v);
-}
-
 // Gate epilogue fused with the next product's input: part[z][m][0 .. 2F) holds the gate rows
 // (0 .. F) and value rows (F .. 2F) of linear_in; x16 row m = silu(gate) * value, hi and lo parts.
 // A thread writes one piece of one row.
@@ -748,7 +824,21 @@ cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out) {
     if (e != cudaSuccess) return e;
     out->n = w.n;
     out->k = w.k;
+    out->gate_ok = false;
     return cudaSuccess;
+}
+
+cudaError_t tc_make_gate_maps(const Q4Dev& w, TcWeight* out) {
+    out->gate_ok = false;
+    if (w.n % 128 != 0) return cudaSuccess;  // gate and value halves of 64-row multiples
+    const uint64_t nb = (uint64_t)(w.k / 32);
+    cudaError_t e = tma_encode_2d(&out->nib64, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, nb * 16, (uint64_t)w.n, nb * 16,
+                                  128, (uint32_t)(kTM / 2), CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e == cudaSuccess)
+        e = tma_encode_2d(&out->sc64, CU_TENSOR_MAP_DATA_TYPE_UINT16, w.scale, nb, (uint64_t)w.n, nb * 2, 8,
+                          (uint32_t)(kTM / 2), CU_TENSOR_MAP_SWIZZLE_NONE);
+    out->gate_ok = e == cudaSuccess;
+    return e;
 }
 
 size_t tc_x16_bytes(int k, int M) {
@@ -791,6 +881,15 @@ cudaError_t launch_tc_product(const TcWeight& tw, const __half* x16, int rows, f
     const TcPlan p = make_plan(tw.n, tw.k, rows, num_sms);
     *slices = p.slices;
     return launch_gemm(tw, x16, x_lo ? 1 : 0, rows, p, part, err, st);
+}
+
+cudaError_t launch_tc_product_gate(const TcWeight& tw, const __half* x16, int rows, __half* x16_out, int* err,
+                                   cudaStream_t st, bool x_lo) {
+    if (!tw.gate_ok) return cudaErrorInvalidValue;
+    TcPlan p = make_plan(tw.n, tw.k, rows, 1);
+    p.slices = 1;  // the epilogue needs each unit's whole sum
+    const TcGate gt{x16_out, tw.n / 2};
+    return launch_gemm(tw, x16, x_lo ? 1 : 0, rows, p, nullptr, err, st, &gt);
 }
 
 cudaError_t launch_tc_resid_norm(float* x, const float* part, int slices, int rows, int D, const float* alpha,

@@ -20,9 +20,14 @@ bool tc_gemm_scales_ok(const uint8_t* q4_blocks, int64_t nblocks);
 // TMA descriptors of a Q4 weight's nibble and scale planes (built once per weight on the host).
 struct TcWeight {
     CUtensorMap nib, sc;
+    CUtensorMap nib64, sc64;  // boxes of 64 rows, for the gate product (tc_make_gate_maps)
     int n, k;
+    bool gate_ok;
 };
 cudaError_t tc_make_weight(const Q4Dev& w, TcWeight* out);
+// The 64-row descriptors of linear_in ([2F][K]: gate rows, then value rows), for
+// launch_tc_product_gate; leaves gate_ok false when 2F is not a multiple of 128.
+cudaError_t tc_make_gate_maps(const Q4Dev& w, TcWeight* out);
 
 // A TMA descriptor of `rank` dimensions (dims[0] contiguous; strides[i] = byte stride of dimension
 // i + 1) with a box of box[i] elements per dimension; loads outside the array read zeros.
@@ -61,6 +66,11 @@ cudaError_t launch_tc_prep(const float* in, const float* alpha, int K, int rows,
 // them the activations count as their f16 hi parts (two products).
 cudaError_t launch_tc_product(const TcWeight& tw, const __half* x16, int rows, float* part, int* err, int num_sms,
                               int* slices, cudaStream_t st, bool x_lo = true);
+// linear_in ([2F][K], gate rows then value rows) with the gate fused into its epilogue: x16_out (the
+// linear_out input, F columns) = silu(gate) * value, the values launch_tc_product followed by
+// launch_tc_gate give.  x16_out must not be x16.
+cudaError_t launch_tc_product_gate(const TcWeight& tw, const __half* x16, int rows, __half* x16_out, int* err,
+                                   cudaStream_t st, bool x_lo = true);
 // x[rows][D] += the slices (in order); x16 = RMSNorm(x) * alpha.
 cudaError_t launch_tc_resid_norm(float* x, const float* part, int slices, int rows, int D, const float* alpha,
                                  __half* x16, cudaStream_t st);

@@ -307,6 +307,31 @@ def test_full_size_batched_tensor_core_path(full_model):
     assert worst < LOGIT_TOL, worst
 
 
+@pytest.mark.parametrize("n", [20, 150])
+def test_gate_fused_into_linear_in_is_bit_identical(monkeypatch, n):
+    """linear_in with the SiLU gate in its epilogue (writing the linear_out input directly) gives
+    the same logits, bit for bit, as linear_in followed by the separate gate kernel."""
+    spec = stt_b200.SynthSpec(seed=25, num_layers=2, hidden_size=256, num_heads=2, ffn_hidden=512, vocab_size=1000,
+                              text_in_vocab_size=1001, num_codebooks=4, audio_vocab_size=300)
+    g = stt_b200.synth_gguf(spec)
+    model = stt_b200.SttModel.from_shards([g.array], config=tiny_cfg())
+    frames = np.random.default_rng(13).integers(0, 300, (5, n, 4))
+    outs = []
+    for unfused in (False, True):
+        if unfused:
+            monkeypatch.setenv("STT_UNFUSED_GATE", "1")
+        cache = model.create_cache(n, "bf16")
+        texts = [1000] * n
+        lgs = []
+        for f in frames:
+            lg, am = cache.forward(list(range(n)), f, texts)
+            lgs.append(lg)
+            texts = [int(t) for t in am]
+        outs.append(np.stack(lgs))
+        cache.close()
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+
+
 def test_tensor_core_and_gemv_batches_agree(monkeypatch):
     """The same 16-stream batch through the tensor cores and through the GEMV (STT_DISABLE_TC)."""
     spec = stt_b200.SynthSpec(seed=24, num_layers=2, hidden_size=256, num_heads=2, ffn_hidden=512, vocab_size=1000,
