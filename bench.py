@@ -404,10 +404,17 @@ def main():
     g = synth.synth_gguf(synth.SynthSpec(seed=SEED, n_threads=nthreads))
     t1 = time.perf_counter()
     cfg = stt_b200.SttConfig(text_start_token=0, sliding_window=args.window)   # initial text token 0
+    # the first load of a process also pays its one-time set-up (kernel attributes, the pinned staging
+    # ring, the copy threads); the rate reported is that of a second load, the first beside it
     model = stt_b200.SttModel.from_buffer(g.address, g.length, device=local, config=cfg)
     t2 = time.perf_counter()   # the load synchronises the device before it returns
-    load = {"gguf_bytes": g.length, "synth_s": round(t1 - t0, 3), "model_load_s": round(t2 - t1, 3),
-            "model_load_gbs": round(g.length / (t2 - t1) / 1e9, 3)}
+    model.close()
+    t3 = time.perf_counter()
+    model = stt_b200.SttModel.from_buffer(g.address, g.length, device=local, config=cfg)
+    t4 = time.perf_counter()
+    load = {"gguf_bytes": g.length, "synth_s": round(t1 - t0, 3), "model_load_s": round(t4 - t3, 3),
+            "model_load_gbs": round(g.length / (t4 - t3) / 1e9, 3),
+            "first_load_in_process_s": round(t2 - t1, 3)}
     g.close()
 
     line = {}
