@@ -188,6 +188,45 @@ __device__ __forceinline__ void unit_rows(const GemvArgs& a, int u, int* ra, int
     }
 }
 
+// The QKV epilogue's RoPE factors of output pair (ra, ra + 1) at the stream's position (unused for
+// the v rows).
+__device__ __forceinline__ float2 qkv_rope(const Ctx& c, const StreamState& st, int ra) {
+    const int within = ra % c.D, d = within % c.HD;
+    return ra < 2 * c.D ? c.rope[(int64_t)st.offset * (c.HD >> 1) + (d >> 1)] : make_float2(0.0f, 0.0f);
+}
+
+// The QKV epilogue of output pair (ra, rb = ra + 1) of batch row bm (stream sid, state st): RoPE
+// on q and k, the row's q, k, v to the step's buffer and k, v to the stream's K/V ring.
+__device__ __forceinline__ void qkv_store(const Ctx& c, const GemvArgs& a, int bm, int sid, const StreamState& st,
+                                          float2 cs, int ra, int rb, float va, float vb) {
+    const int D = c.D, HD = c.HD;
+    float* o = a.out + (int64_t)bm * a.ldo;
+    int part = ra / D;            // 0 q, 1 k, 2 v
+    const int within = ra - part * D;
+    const int h = within / HD, d = within - h * HD;
+    if (part < 2) {
+        // RoPE::apply_rotation (model.rs:114-116) on the pair (2i, 2i+1), no fma contraction
+        const float r = __fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y));
+        const float im = __fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x));
+        va = r;
+        vb = im;
+    }
+    o[ra] = va;
+    o[rb] = vb;
+    if (part >= 1) {
+        const int64_t off = (int64_t)sid * c.kv_stream_stride + (int64_t)a.layer * c.kv_layer_stride +
+                            (part == 2 ? c.kv_half_stride : 0) + ((int64_t)h * c.ML + st.write_pos) * HD + d;
+        if (c.kv_f32) {
+            float* kv = reinterpret_cast<float*>(c.kv) + off;
+            kv[0] = va;
+            kv[1] = vb;
+        } else {
+            __nv_bfloat162* kv = reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(c.kv) + off);
+            *kv = __floats2bfloat162_rn(va, vb);
+        }
+    }
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue(const Ctx& c, const GemvArgs& a, int bm, int ra, int rb, float va, float vb) {
     if (EPI == EPI_PLAIN || EPI == EPI_LOGITS) {
@@ -205,33 +244,7 @@ __device__ __forceinline__ void epilogue(const Ctx& c, const GemvArgs& a, int bm
     } else {  // EPI_QKV
         const int sid = c.ids[bm];
         const StreamState st = c.state[sid];
-        const int D = c.D, HD = c.HD;
-        float* o = a.out + (int64_t)bm * a.ldo;
-        int part = ra / D;            // 0 q, 1 k, 2 v
-        const int within = ra - part * D;
-        const int h = within / HD, d = within - h * HD;
-        if (part < 2) {
-            // RoPE::apply_rotation (model.rs:114-116) on the pair (2i, 2i+1), no fma contraction
-            const float2 cs = c.rope[(int64_t)st.offset * (HD >> 1) + (d >> 1)];
-            const float r = __fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y));
-            const float im = __fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x));
-            va = r;
-            vb = im;
-        }
-        o[ra] = va;
-        o[rb] = vb;
-        if (part >= 1) {
-            const int64_t off = (int64_t)sid * c.kv_stream_stride + (int64_t)a.layer * c.kv_layer_stride +
-                                (part == 2 ? c.kv_half_stride : 0) + ((int64_t)h * c.ML + st.write_pos) * HD + d;
-            if (c.kv_f32) {
-                float* kv = reinterpret_cast<float*>(c.kv) + off;
-                kv[0] = va;
-                kv[1] = vb;
-            } else {
-                __nv_bfloat162* kv = reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(c.kv) + off);
-                *kv = __floats2bfloat162_rn(va, vb);
-            }
-        }
+        qkv_store(c, a, bm, sid, st, qkv_rope(c, st, ra), ra, rb, va, vb);
     }
 }
 
@@ -1066,27 +1079,67 @@ __global__ void __launch_bounds__(mg::kThreads, 1)
 }
 
 // Epilogue of a tensor-core product: the K-slice partial sums part[z][m][W.n] of each output pair
-// are added in slice order (z = 0, 1, ...) and handed to the same epilogue as the GEMV's.
-template <int EPI>
+// are added in slice order (z = 0, 1, ...) and handed to the same epilogue as the GEMV's.  Grid
+// (groups of kEpiUnits * 256 units, batch rows); a thread takes units u0 + 256 j, j < kEpiUnits, and
+// issues all of their loads before it uses any (4 units from 128 batch rows up; below, one, which
+// keeps more CTAs in flight).  The step's stream ids and states are written by kernels launched the
+// ordinary way before any tensor-core product of the step, and the RoPE table is constant, so the
+// QKV epilogue reads them before it waits for the product.
+template <int EPI, int kEpiUnits>
 __global__ void __launch_bounds__(256) tc_epilogue_kernel(Ctx c, GemvArgs a, const float* __restrict__ part, int rows,
                                                          int slices) {
     pdl_trigger();
-    pdl_wait();
-    // grid (unit groups of 256, batch rows): the row's stream id and state are the same in a CTA
-    const int64_t plane = (int64_t)rows * a.W.n;
     const int m = blockIdx.y;
-    const int u = blockIdx.x * blockDim.x + threadIdx.x;
-    if (u < a.n_units) {
-        int ra, rb;
-        unit_rows<EPI>(a, u, &ra, &rb);
-        const float* p = part + (int64_t)m * a.W.n;
-        float va = p[ra], vb = rb >= 0 ? p[rb] : 0.0f;
-        for (int z = 1; z < slices; ++z) {
-            p += plane;
-            va = __fadd_rn(va, p[ra]);
-            if (rb >= 0) vb = __fadd_rn(vb, p[rb]);
+    const int u0 = blockIdx.x * (256 * kEpiUnits) + threadIdx.x;
+    int sid = 0;
+    StreamState st{};
+    float2 cs[kEpiUnits];
+    if (EPI == EPI_QKV) {
+        sid = c.ids[m];
+        st = c.state[sid];
+#pragma unroll
+        for (int j = 0; j < kEpiUnits; ++j) {
+            const int u = u0 + 256 * j;
+            cs[j] = u < a.n_units ? qkv_rope(c, st, 2 * u) : make_float2(0.0f, 0.0f);
         }
-        epilogue<EPI>(c, a, m, ra, rb, va, vb);
+    }
+    pdl_wait();
+    const int64_t plane = (int64_t)rows * a.W.n;
+    const float* pm = part + (int64_t)m * a.W.n;
+    int ra[kEpiUnits], rb[kEpiUnits];
+    float va[kEpiUnits], vb[kEpiUnits];
+#pragma unroll
+    for (int j = 0; j < kEpiUnits; ++j) {
+        const int u = u0 + 256 * j;
+        ra[j] = 0, rb[j] = -1, va[j] = vb[j] = 0.0f;
+        if (u < a.n_units) {
+            unit_rows<EPI>(a, u, &ra[j], &rb[j]);
+            va[j] = pm[ra[j]];
+            if (rb[j] >= 0) vb[j] = pm[rb[j]];
+        }
+    }
+    for (int z = 1; z < slices; ++z) {
+        const float* p = pm + z * plane;
+        float wa[kEpiUnits], wb[kEpiUnits];
+#pragma unroll
+        for (int j = 0; j < kEpiUnits; ++j) {
+            wa[j] = wb[j] = 0.0f;
+            if (u0 + 256 * j < a.n_units) {
+                wa[j] = p[ra[j]];
+                if (rb[j] >= 0) wb[j] = p[rb[j]];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kEpiUnits; ++j) {
+            va[j] = __fadd_rn(va[j], wa[j]);
+            if (rb[j] >= 0) vb[j] = __fadd_rn(vb[j], wb[j]);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kEpiUnits; ++j) {
+        if (u0 + 256 * j >= a.n_units) continue;
+        if (EPI == EPI_QKV) qkv_store(c, a, m, sid, st, cs[j], ra[j], rb[j], va[j], vb[j]);
+        else epilogue<EPI>(c, a, m, ra[j], rb[j], va[j], vb[j]);
     }
 }
 
@@ -1773,18 +1826,26 @@ cudaError_t launch_finish(const Ctx& c, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+template <int U>
+static cudaError_t launch_tc_epilogue_u(const Ctx& c, const GemvArgs& a, int epi, int rows, const float* part,
+                                        int slices, cudaStream_t st) {
+    const dim3 grid((a.n_units + 256 * U - 1) / (256 * U), rows);
+    switch (epi) {
+        case EPI_QKV: return launch_pdl(tc_epilogue_kernel<EPI_QKV, U>, grid, dim3(256), 0, st, c, a, part, rows, slices);
+        case EPI_GATE: return launch_pdl(tc_epilogue_kernel<EPI_GATE, U>, grid, dim3(256), 0, st, c, a, part, rows, slices);
+        case EPI_RESID:
+            return launch_pdl(tc_epilogue_kernel<EPI_RESID, U>, grid, dim3(256), 0, st, c, a, part, rows, slices);
+        case EPI_LOGITS:
+            return launch_pdl(tc_epilogue_kernel<EPI_LOGITS, U>, grid, dim3(256), 0, st, c, a, part, rows, slices);
+        default: return launch_pdl(tc_epilogue_kernel<EPI_PLAIN, U>, grid, dim3(256), 0, st, c, a, part, rows, slices);
+    }
+}
+
 cudaError_t launch_tc_epilogue(const Ctx& c, const GemvArgs& a, int epi, int rows, const float* part, int slices,
                                cudaStream_t st) {
     if (rows <= 0 || a.n_units <= 0) return cudaSuccess;
-    const dim3 grid((a.n_units + 255) / 256, rows);
-    switch (epi) {
-        case EPI_QKV: return launch_pdl(tc_epilogue_kernel<EPI_QKV>, grid, dim3(256), 0, st, c, a, part, rows, slices);
-        case EPI_GATE: return launch_pdl(tc_epilogue_kernel<EPI_GATE>, grid, dim3(256), 0, st, c, a, part, rows, slices);
-        case EPI_RESID: return launch_pdl(tc_epilogue_kernel<EPI_RESID>, grid, dim3(256), 0, st, c, a, part, rows, slices);
-        case EPI_LOGITS:
-            return launch_pdl(tc_epilogue_kernel<EPI_LOGITS>, grid, dim3(256), 0, st, c, a, part, rows, slices);
-        default: return launch_pdl(tc_epilogue_kernel<EPI_PLAIN>, grid, dim3(256), 0, st, c, a, part, rows, slices);
-    }
+    return rows >= 128 ? launch_tc_epilogue_u<4>(c, a, epi, rows, part, slices, st)
+                       : launch_tc_epilogue_u<1>(c, a, epi, rows, part, slices, st);
 }
 
 }  // namespace stt
