@@ -20,6 +20,7 @@
 #include "device.cuh"
 #include "dp4a.cuh"
 #include "kernels.h"
+#include "qkv.cuh"
 #include "tc_gemm.h"
 #include "tc_layout.cuh"
 
@@ -188,34 +189,22 @@ __device__ __forceinline__ void unit_rows(const GemvArgs& a, int u, int* ra, int
     }
 }
 
-// The QKV epilogue's RoPE factors of output pair (ra, ra + 1) at the stream's position (unused for
-// the v rows).
-__device__ __forceinline__ float2 qkv_rope(const Ctx& c, const StreamState& st, int ra) {
-    const int within = ra % c.D, d = within % c.HD;
-    return ra < 2 * c.D ? c.rope[(int64_t)st.offset * (c.HD >> 1) + (d >> 1)] : make_float2(0.0f, 0.0f);
-}
-
-// The QKV epilogue of output pair (ra, rb = ra + 1) of batch row bm (stream sid, state st): RoPE
-// on q and k, the row's q, k, v to the step's buffer and k, v to the stream's K/V ring.
+// The QKV epilogue of output pair (ra, rb = ra + 1) of batch row bm (stream sid, state st, RoPE
+// factors cs): RoPE on q and k, the row's q, k, v to the step's buffer and k, v to the stream's K/V
+// ring.
 __device__ __forceinline__ void qkv_store(const Ctx& c, const GemvArgs& a, int bm, int sid, const StreamState& st,
                                           float2 cs, int ra, int rb, float va, float vb) {
-    const int D = c.D, HD = c.HD;
     float* o = a.out + (int64_t)bm * a.ldo;
-    int part = ra / D;            // 0 q, 1 k, 2 v
-    const int within = ra - part * D;
-    const int h = within / HD, d = within - h * HD;
+    const int part = ra / c.D;  // 0 q, 1 k, 2 v
     if (part < 2) {
-        // RoPE::apply_rotation (model.rs:114-116) on the pair (2i, 2i+1), no fma contraction
-        const float r = __fsub_rn(__fmul_rn(va, cs.x), __fmul_rn(vb, cs.y));
-        const float im = __fadd_rn(__fmul_rn(va, cs.y), __fmul_rn(vb, cs.x));
+        const float r = qkv_rotate(va, vb, cs, false), im = qkv_rotate(va, vb, cs, true);
         va = r;
         vb = im;
     }
     o[ra] = va;
     o[rb] = vb;
     if (part >= 1) {
-        const int64_t off = (int64_t)sid * c.kv_stream_stride + (int64_t)a.layer * c.kv_layer_stride +
-                            (part == 2 ? c.kv_half_stride : 0) + ((int64_t)h * c.ML + st.write_pos) * HD + d;
+        const int64_t off = qkv_kv_offset(c, a.layer, sid, st, ra);
         if (c.kv_f32) {
             float* kv = reinterpret_cast<float*>(c.kv) + off;
             kv[0] = va;
