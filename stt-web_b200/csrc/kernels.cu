@@ -237,8 +237,10 @@ __device__ __forceinline__ void epilogue(const Ctx& c, const GemvArgs& a, int bm
     }
 }
 
-// The batched Q4 GEMV (batches of fewer than 16 streams, and the isolated f32 / bf16 matmul): for
-// each unit (a row pair; EPI_GATE: a gate row and its value row) and each batch row m < mb,
+// The register GEMV, for the passes that neither the integer-MMA GEMV (passes of several rows, K a
+// multiple of 256) nor the streamed GEMV takes: K not a multiple of 256, or one row over more than
+// 40 units per SM.  For each unit (a row pair; EPI_GATE: a gate row and its value row) and each
+// batch row m < mb,
 // sum over blocks of scale * dot(block, x[m]) with the exact dp4a block dot of dp4a.cuh, then the
 // epilogue.  A unit is reduced by a team of `team` consecutive threads (8 .. 256, a power of two;
 // past 32 the team spans warps), each taking blocks tl, tl + team, ... (at most kBPL of them), so

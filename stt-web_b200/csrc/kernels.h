@@ -53,7 +53,8 @@ cudaError_t launch_repack_q4(const uint8_t* raw, int64_t nblocks, uint4* nib, ui
                              int* big_scale = nullptr);
 cudaError_t launch_dequant_q4(const Q4Dev& w, float* out, cudaStream_t st);
 // The batched Q4 GEMV of the step (and of the isolated f32 / bf16 matmul): one launch per pass of
-// up to 8 batch rows (4 when K > 4096), each pass reading the weights once.
+// up to 8 batch rows (4 when K > 4096), each pass reading the weights once; passes of several rows
+// take the integer-MMA kernel when a.maps holds W's descriptors, single rows the dp4a kernels.
 cudaError_t launch_gemv(const Ctx& c, const GemvArgs& a, int epi, int rows, cudaStream_t st);
 cudaError_t launch_embed(const Ctx& c, cudaStream_t st);
 cudaError_t launch_attention(const Ctx& c, int layer, cudaStream_t st);

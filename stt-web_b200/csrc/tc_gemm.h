@@ -14,7 +14,7 @@ namespace stt {
 bool tc_gemm_supported(const Q4Dev& w);
 
 // True when every f16 scale of the raw Q4_0 blocks (18 bytes each) has |s| <= 4, the range in
-// which the kernel's f16 weight parts stay finite; other weights use the f32 GEMV.
+// which the kernel's f16 weight parts stay finite; other weights use the GEMV.
 bool tc_gemm_scales_ok(const uint8_t* q4_blocks, int64_t nblocks);
 
 // TMA descriptors of a Q4 weight's nibble and scale planes (built once per weight on the host).
