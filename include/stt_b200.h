@@ -243,6 +243,10 @@ int stt_q4_matmul_device(const stt_q4_tensor* w, const void* d_input, int in_dty
  * cuda_stream, no synchronisation; d_input 16-byte aligned (f32) or 8-byte aligned (bf16). */
 int stt_q4_matmul_device_noalloc(const stt_q4_tensor* w, const void* d_input, int in_dtype, int rows,
                                  int splits, float* d_out, void* cuda_stream);
+/* No counterpart in the reference.  Waits for the device, then reports whether a device-side wait
+ * of any matmul on this tensor since the last check ran out (STT_E_DEVICE_FLAG: that call's output
+ * is invalid; the flag is cleared) or not (STT_OK).  stt_q4_matmul checks it itself. */
+int stt_q4_tensor_status(const stt_q4_tensor* w);
 /* Dequantises the whole matrix to f32 on the device and copies it to out_host (n*k floats):
  * out[r*k + j] = (nibble - 8) * f16_to_f32(scale), bit-exact with gguf.rs:616-633. */
 int stt_q4_tensor_dequant(const stt_q4_tensor* w, float* out_host);
@@ -303,6 +307,12 @@ int stt_debug_fail_allocation(int after);
  * STT_E_DEVICE_FLAG; the stream's state on the device is left as it was before the failed frame, so
  * stt_stream_reset (or the next call) continues normally.  Nothing faults or hangs. */
 int stt_debug_arm_wait_timeout(stt_streams* streams);
+/* Test of the integer-MMA GEMV's bounded waits.  Arms the next matmul call on this tensor that
+ * takes that kernel (f32 or bf16 input, 2 to 8 rows per pass, k a multiple of 256; one launch
+ * only): its first weight stage is never loaded, so the warps waiting for it give up after their
+ * limit (about a second) and the kernel stops through the same path as a real timeout, recording
+ * STT_E_DEVICE_FLAG for stt_q4_tensor_status (stt_q4_matmul returns it).  Nothing faults or hangs. */
+int stt_debug_q4_arm_wait_timeout(stt_q4_tensor* w);
 /* Number of kernels one batched step of n streams (n >= 2) launches: the nodes of the CUDA
  * graph that the library captures for that batch size (captured on first use). */
 int stt_debug_graph_kernels(stt_streams* streams, int n, int* kernels);

@@ -239,6 +239,9 @@ public:
         return Q4Tensor(t, n, k);
     }
     /* (nibble - 8) * scale for every weight, bit-exact with gguf.rs:616-633. */
+    // Waits for the device; throws Error(STT_E_DEVICE_FLAG) if a device-side wait of a matmul on
+    // this tensor ran out since the last check.
+    void status() const { check(stt_q4_tensor_status(h_.get()), "stt_q4_tensor_status"); }
     std::vector<float> dequant() const {
         std::vector<float> out((size_t)n_ * (size_t)k_);
         check(stt_q4_tensor_dequant(h_.get(), out.data()), "stt_q4_tensor_dequant");

@@ -1393,7 +1393,8 @@ struct stt_q4_tensor {
     int num_sms = 148;
     Q4Dev w{};
     void* mem = nullptr;
-    int* d_err = nullptr;  // timeout flag of the tensor-core kernel (inside mem)
+    int* d_err = nullptr;  // timeout flag of the tensor's kernels (inside mem)
+    int stall_next = 0;    // test hook: the next integer-MMA GEMV launch waits for a stage never loaded
     bool tc_ok = false;    // shape and scales fit the tensor-core kernel
     TcWeight tc_w{};       // its TMA descriptors
     GemvMaps gemv_maps{};  // the GEMV's TMA descriptors
@@ -1486,6 +1487,8 @@ extern "C" int stt_q4_matmul_device(const stt_q4_tensor* t, const void* d_in, in
     a.n_units = (t->w.n + 1) / 2;
     a.err = t->d_err;
     a.maps = &t->gemv_maps;
+    a.stall_test = t->stall_next;
+    const_cast<stt_q4_tensor*>(t)->stall_next = 0;
     CUDA_TRY(launch_gemv(c, a, EPI_PLAIN, rows, static_cast<cudaStream_t>(cuda_stream)));
     return STT_OK;
 }
@@ -1567,6 +1570,25 @@ extern "C" int stt_q4_matmul(const stt_q4_tensor* t, const float* input, int row
     TRY(stt_q4_matmul_device(t, din.p, 0, rows, static_cast<float*>(dout.p), nullptr));
     CUDA_TRY(cudaDeviceSynchronize());
     CUDA_TRY(cudaMemcpy(out, dout.p, (size_t)rows * t->w.n * 4, cudaMemcpyDeviceToHost));
+    return stt_q4_tensor_status(t);
+}
+
+extern "C" int stt_q4_tensor_status(const stt_q4_tensor* t) {
+    clear_error();
+    if (!t) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    DeviceScope ds(t->device);
+    CUDA_TRY(cudaDeviceSynchronize());
+    int flag = 0;
+    CUDA_TRY(cudaMemcpy(&flag, t->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag == 0) return STT_OK;
+    CUDA_TRY(cudaMemset(t->d_err, 0, sizeof(int)));
+    return set_error(STT_E_DEVICE_FLAG, "a device-side wait of a matmul on this tensor timed out; its output is invalid");
+}
+
+extern "C" int stt_debug_q4_arm_wait_timeout(stt_q4_tensor* t) {
+    clear_error();
+    if (!t) return set_error(STT_E_INVALID_ARG, "bad arguments");
+    t->stall_next = 1;
     return STT_OK;
 }
 

@@ -807,6 +807,10 @@ __global__ void __launch_bounds__(mg::kThreads, 1)
                         ok = false;
                         break;
                     }
+                    if (k == 0 && a.stall_test && blockIdx.x == 0) {  // test hook: stage 0 never lands
+                        issued = 1;
+                        continue;
+                    }
                     uint8_t* st = smem + (size_t)s * mg::kStageBytes;
                     // whole boxes, quads past the end read as zeros
                     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(&full[s])),
@@ -824,8 +828,10 @@ __global__ void __launch_bounds__(mg::kThreads, 1)
                 if (c.desc) raise_error(c.desc, -5);  // STT_E_DEVICE_FLAG
                 if (err) atomicCAS(err, 0, -5);
             }
-            // every load must land before the CTA's shared memory goes away
+            // every load must land before the CTA's shared memory goes away (the stage the test hook
+            // skipped has none)
             for (int k = max(0, issued - stages); k < issued; ++k) {
+                if (k == 0 && a.stall_test && blockIdx.x == 0) continue;
                 const int s = k % stages;
                 for (uint32_t i = 0; i < kSSpin; ++i) {
                     uint32_t done;

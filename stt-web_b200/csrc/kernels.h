@@ -32,6 +32,8 @@ struct GemvArgs {
     int32_t half_n;                  // EPI_GATE: value rows start here (= ffn width)
     int* err;                        // where a kernel records a timeout when there is no step descriptor
     const GemvMaps* maps;            // host copy of W's GEMV descriptors, or NULL (host side only)
+    int32_t stall_test;              // test hook: the integer-MMA GEMV's first stage is never loaded, so
+                                     // its waits run out and report STT_E_DEVICE_FLAG
 };
 
 // Per-call descriptor and batch ids, written on the device from launch parameters so that

@@ -114,6 +114,7 @@ SIGNATURES = {
     "stt_q4_matmul": (C.c_int, [P, F32P, C.c_int, F32P]),
     "stt_q4_matmul_device": (C.c_int, [P, P, C.c_int, C.c_int, P, P]),
     "stt_q4_tensor_dequant": (C.c_int, [P, F32P]),
+    "stt_q4_tensor_status": (C.c_int, [P]),
     "stt_q4_matmul_device_noalloc": (C.c_int, [P, P, C.c_int, C.c_int, C.c_int, P, P]),
     "stt_spm_decoder_create": (C.c_int, [U8P, C.c_size_t, C.POINTER(P)]),
     "stt_spm_decoder_destroy": (C.c_int, [P]),
@@ -126,6 +127,7 @@ SIGNATURES = {
     "stt_debug_barrier_ns": (C.c_int, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double)]),
     "stt_debug_graph_kernels": (C.c_int, [P, C.c_int, C.POINTER(C.c_int)]),
     "stt_debug_arm_wait_timeout": (C.c_int, [P]),
+    "stt_debug_q4_arm_wait_timeout": (C.c_int, [P]),
     "stt_debug_fail_allocation": (C.c_int, [C.c_int]),
     "stt_debug_time_products": (C.c_int, [P, C.c_int, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "stt_last_error": (C.c_char_p, []),

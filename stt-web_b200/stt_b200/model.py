@@ -286,6 +286,11 @@ class Q4Tensor:
         except Exception:
             pass
 
+    def status(self) -> None:
+        """Waits for the device; raises SttError (STT_E_DEVICE_FLAG) if a device-side wait of a
+        matmul on this tensor ran out since the last check (that output is invalid)."""
+        check(lib().stt_q4_tensor_status(self._h), "stt_q4_tensor_status")
+
     def dequant(self) -> np.ndarray:
         out = np.empty(self.shape, dtype=np.float32)
         check(lib().stt_q4_tensor_dequant(self._h, _ptr(out, C.c_float)), "stt_q4_tensor_dequant")

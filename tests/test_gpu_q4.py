@@ -141,3 +141,26 @@ def test_q4_matmul_tensor_cores_rejects_unsupported():
         rc = lib().stt_q4_matmul_device(t._h, dx.data_ptr(), 2, m, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
         assert rc != 0
         assert ("256" if not big else "at most 4") in lib().stt_last_error().decode()
+
+
+def test_mma_gemv_bounded_wait_runs_out_and_the_next_call_recovers():
+    """The test hook leaves the integer-MMA GEMV's first weight stage unloaded for one launch: the
+    warps waiting for it give up after their limit, the kernel stops through its timeout path, and
+    the call reports STT_E_DEVICE_FLAG (nothing faults or hangs).  The next call is exact again."""
+    import time
+    from stt_b200._lib import STT_E_DEVICE_FLAG, lib
+    n, k, m = 2048, 2048, 4
+    raw = q4_bytes(n, k, 17)
+    x = np.random.default_rng(4).standard_normal((1, m, k)).astype(np.float32)
+    t = stt_b200.Q4Tensor.from_q4_bytes(raw, (n, k))
+    ref = O.q4_matmul(raw, n, k, x[0])
+    assert lib().stt_debug_q4_arm_wait_timeout(t._h) == 0
+    t0 = time.perf_counter()
+    with pytest.raises(stt_b200.SttError) as err:
+        stt_b200.q4_matmul(x, t)
+    assert err.value.code == STT_E_DEVICE_FLAG
+    print(f"timed out and returned in {time.perf_counter() - t0:.2f} s")
+    t.status()  # the flag was cleared by the failed call
+    got = stt_b200.q4_matmul(x, t)[0]
+    assert np.abs(got - ref).max() <= 2e-6 * np.abs(ref).max()
+
