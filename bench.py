@@ -53,7 +53,7 @@ PUBLISHED_FPS_750 = 1000.0 / 52.5
 MEGA_TRAFFIC_750 = 508_170_845_440 + 2_636_432_128
 # DRAM read + write bytes of one launch of the tcgen05 GEMM on linear_in (16896 x 2048) at 512 batch
 # rows (ncu): profiles/q4_tc_kernel_linear_in_512rows.txt
-TC_TRAFFIC_LINEAR_IN_512 = 23_689_472 + 393_728
+TC_TRAFFIC_LINEAR_IN_512 = 23_695_360 + 194_048
 METRIC = "decode frames/s, whole job (512 streams x 250 frames split over the GPUs)"
 
 
