@@ -734,32 +734,36 @@ __device__ __forceinline__ bool mg_wait(uint64_t* m, uint32_t parity, volatile i
     return false;
 }
 
-// Digits of one block (32 elements of batch row m) and ex[m][b] = 2^(e - 26), by one thread.  With
-// |X| <= 2^22, Y = X + 0x808080 lies in [0, 2^24) and its three bytes are the balanced digits plus
-// 128, so the digits are Y's bytes with the top bit flipped.
-__device__ __forceinline__ void mg_block_digits(uint32_t* DW, float* ex, int MB, int NB, int m, int b,
-                                                const float (&x)[32]) {
+// Digits of one half block (16 elements: half h of block b of batch row m) and, from half 0,
+// ex[m][b] = 2^(e - 26).  The two halves of a block are neighbouring lanes (h = lane & 1), which
+// share the block's maximum by a shuffle, so every lane of the warp calls this (`valid` false: no
+// stores; both halves of a block are valid or neither is).  With |X| <= 2^22, Y = X + 0x808080
+// lies in [0, 2^24) and its three bytes are the balanced digits plus 128, so the digits are Y's
+// bytes with the top bit flipped.
+__device__ __forceinline__ void mg_half_digits(uint32_t* DW, float* ex, int MB, int NB, int m, int b, int h,
+                                               const float (&x)[16], bool valid) {
     float mx = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(x[i]));
+    for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(x[i]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+    if (!valid) return;
     // mx < 2^e; e >= -96 keeps 2^(e - 26) normal, and e <= 128 for every finite mx
     const int e = max(-96, mx > 0.0f ? (int)((__float_as_uint(mx) >> 23) & 0xFF) - 126 : 0);
     const float up = __uint_as_float((uint32_t)(127 + 22 - e) << 23);
-    uint32_t* rec = DW + mg_digit_word(MB, b, 0, 0, m, 0);
+    uint32_t* rec = DW + mg_digit_word(MB, b, h, 0, m, 0);
 #pragma unroll
-    for (int gq = 0; gq < 8; ++gq) {  // quad gq: elements 4gq .. 4gq+3
-        const uint32_t y0 = (uint32_t)(__float2int_rn(__fmul_rn(x[4 * gq + 0], up)) + 0x808080);
-        const uint32_t y1 = (uint32_t)(__float2int_rn(__fmul_rn(x[4 * gq + 1], up)) + 0x808080);
-        const uint32_t y2 = (uint32_t)(__float2int_rn(__fmul_rn(x[4 * gq + 2], up)) + 0x808080);
-        const uint32_t y3 = (uint32_t)(__float2int_rn(__fmul_rn(x[4 * gq + 3], up)) + 0x808080);
+    for (int t = 0; t < 4; ++t) {  // elements 4t .. 4t+3 of the half
+        const uint32_t y0 = (uint32_t)(__float2int_rn(__fmul_rn(x[4 * t + 0], up)) + 0x808080);
+        const uint32_t y1 = (uint32_t)(__float2int_rn(__fmul_rn(x[4 * t + 1], up)) + 0x808080);
+        const uint32_t y2 = (uint32_t)(__float2int_rn(__fmul_rn(x[4 * t + 2], up)) + 0x808080);
+        const uint32_t y3 = (uint32_t)(__float2int_rn(__fmul_rn(x[4 * t + 3], up)) + 0x808080);
         const uint32_t t01 = __byte_perm(y0, y1, 0x5140), t23 = __byte_perm(y2, y3, 0x5140);  // bytes 0, 1
         const uint32_t u01 = __byte_perm(y0, y1, 0x0062), u23 = __byte_perm(y2, y3, 0x0062);  // byte 2
-        const int half = gq >> 2, t = gq & 3;
-        rec[((half * 3 + 0) * MB) * 4 + t] = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
-        rec[((half * 3 + 1) * MB) * 4 + t] = __byte_perm(t01, t23, 0x7632) ^ 0x80808080u;
-        rec[((half * 3 + 2) * MB) * 4 + t] = __byte_perm(u01, u23, 0x5410) ^ 0x80808080u;
+        rec[(0 * MB) * 4 + t] = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
+        rec[(1 * MB) * 4 + t] = __byte_perm(t01, t23, 0x7632) ^ 0x80808080u;
+        rec[(2 * MB) * 4 + t] = __byte_perm(u01, u23, 0x5410) ^ 0x80808080u;
     }
-    ex[m * NB + b] = __uint_as_float((uint32_t)(127 + e - 26) << 23);
+    if (h == 0) ex[m * NB + b] = __uint_as_float((uint32_t)(127 + e - 26) << 23);
 }
 
 template <int MB, int EPI>
@@ -851,26 +855,33 @@ __global__ void __launch_bounds__(mg::kThreads, 1)
         return;
     }
 
-    // consumers: the input rows become digits while the first loads fly, a block (32 elements of
-    // one row) per thread at a time; the CTAs start at different blocks so that they do not all
-    // read the same lines at once
+    // consumers: the input rows become digits while the first loads fly.  A thread converts half a
+    // block (16 elements of one row) at a time while the loads of its next half block fly; the two
+    // halves of a block are neighbouring threads, and the CTAs start at different blocks so that
+    // they do not all read the same lines at once.
     pdl_wait();
     {
         constexpr int kT = 32 * mg::kCWarps;
-        const int total = mb * NB;
+        const int total = mb * NB, total2 = 2 * total;  // blocks, half blocks
         const float inv_nb = 1.0f / (float)NB;
         // row of block item i: (i + 1/2) / NB is at least 1/(2 NB) from an integer, far more than
         // the rounding of the product
         auto row_of = [&](int i) { return __float2int_rz(__fmul_rn((float)i + 0.5f, inv_nb)); };
         const int rot = (int)((blockIdx.x * 37u) % (uint32_t)total);
-        auto item = [&](int j) { const int i = j + rot; return i >= total ? i - total : i; };
-        auto load = [&](int i, float (&x)[32]) {
-            const int m = row_of(i), b = i - m * NB;
-            const int64_t off = (int64_t)(row0 + m) * K + 32 * b;
+        // half block j: half j & 1 of block item (j / 2 + rot) mod total
+        auto half_item = [&](int j, int& m, int& b, int& h) {
+            int i = (j >> 1) + rot;
+            if (i >= total) i -= total;
+            m = row_of(i);
+            b = i - m * NB;
+            h = j & 1;
+        };
+        auto load = [&](int m, int b, int h, float (&x)[16]) {
+            const int64_t off = (int64_t)(row0 + m) * K + 32 * b + 16 * h;
             if (a.in_bf16) {
                 const uint4* p = reinterpret_cast<const uint4*>(a.in_bf16 + off);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < 2; ++c) {
                     const uint4 r = p[c];
                     x[8 * c + 0] = __uint_as_float(r.x << 16), x[8 * c + 1] = __uint_as_float(r.x & 0xFFFF0000u);
                     x[8 * c + 2] = __uint_as_float(r.y << 16), x[8 * c + 3] = __uint_as_float(r.y & 0xFFFF0000u);
@@ -880,7 +891,7 @@ __global__ void __launch_bounds__(mg::kThreads, 1)
             } else {
                 const float4* p = reinterpret_cast<const float4*>(a.in + off);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < 4; ++c) {
                     const float4 v = p[c];
                     x[4 * c + 0] = v.x, x[4 * c + 1] = v.y, x[4 * c + 2] = v.z, x[4 * c + 3] = v.w;
                 }
@@ -894,14 +905,14 @@ __global__ void __launch_bounds__(mg::kThreads, 1)
             float ss[MB];
 #pragma unroll
             for (int m = 0; m < MB; ++m) ss[m] = 0.0f;
-            for (int j = tid; j < total; j += kT) {
-                float x[32];
-                const int i = item(j);
-                load(i, x);
+            for (int j = tid; j < total2; j += kT) {
+                float x[16];
+                int m, b, h;
+                half_item(j, m, b, h);
+                load(m, b, h, x);
                 float q2 = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) q2 = __fmaf_rn(x[c], x[c], q2);
-                const int m = row_of(i);
+                for (int c = 0; c < 16; ++c) q2 = __fmaf_rn(x[c], x[c], q2);
 #pragma unroll
                 for (int mm = 0; mm < MB; ++mm)
                     if (mm == m) ss[mm] += q2;
@@ -920,26 +931,43 @@ __global__ void __launch_bounds__(mg::kThreads, 1)
                     rms[m] = sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), 1e-8f));
                 }
         }
-        for (int j = tid; j < total; j += kT) {
-            float x[32];
-            const int i = item(j), m = row_of(i), b = i - m * NB;
-            load(i, x);
-            if (a.norm) {
-                float r = 1.0f;
+        // every thread runs the same rounds: the halves of a block share a shuffle
+        const int rounds = (total2 + kT - 1) / kT;
+        float xn[16];
+        int mn = 0, bn = 0, hn = 0;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) xn[c] = 0.0f;
+        if (tid < total2) {
+            half_item(tid, mn, bn, hn);
+            load(mn, bn, hn, xn);
+        }
+        for (int r = 0; r < rounds; ++r) {
+            const int j = tid + r * kT;
+            const bool valid = j < total2;
+            float x[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) x[c] = xn[c];
+            const int m = mn, b = bn, h = hn;
+            if (j + kT < total2) {  // the next half block's loads fly while this one is converted
+                half_item(j + kT, mn, bn, hn);
+                load(mn, bn, hn, xn);
+            }
+            if (valid && a.norm) {
+                float rr = 1.0f;
 #pragma unroll
                 for (int mm = 0; mm < MB; ++mm)
-                    if (mm == m) r = rms[mm];
-                const float4* al = reinterpret_cast<const float4*>(a.norm + 32 * b);
+                    if (mm == m) rr = rms[mm];
+                const float4* al = reinterpret_cast<const float4*>(a.norm + 32 * b + 16 * h);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                for (int c = 0; c < 4; ++c) {
                     const float4 w = al[c];
-                    x[4 * c + 0] = __fmul_rn(__fdiv_rn(x[4 * c + 0], r), w.x);
-                    x[4 * c + 1] = __fmul_rn(__fdiv_rn(x[4 * c + 1], r), w.y);
-                    x[4 * c + 2] = __fmul_rn(__fdiv_rn(x[4 * c + 2], r), w.z);
-                    x[4 * c + 3] = __fmul_rn(__fdiv_rn(x[4 * c + 3], r), w.w);
+                    x[4 * c + 0] = __fmul_rn(__fdiv_rn(x[4 * c + 0], rr), w.x);
+                    x[4 * c + 1] = __fmul_rn(__fdiv_rn(x[4 * c + 1], rr), w.y);
+                    x[4 * c + 2] = __fmul_rn(__fdiv_rn(x[4 * c + 2], rr), w.z);
+                    x[4 * c + 3] = __fmul_rn(__fdiv_rn(x[4 * c + 3], rr), w.w);
                 }
             }
-            mg_block_digits(DW, EX, MB, NB, m, b, x);
+            mg_half_digits(DW, EX, MB, NB, m, b, h, x, valid);
         }
         asm volatile("bar.sync 15, %0;" ::"n"(32 * mg::kCWarps) : "memory");
         // column factors: 2^(e - 26 + 8 v) for the columns in use, 0 for the others (and for batch
