@@ -58,6 +58,11 @@ cudaError_t launch_dequant_q4(const Q4Dev& w, float* out, cudaStream_t st);
 // up to 8 batch rows (4 when K > 4096), each pass reading the weights once; passes of several rows
 // take the integer-MMA kernel when a.maps holds W's descriptors, single rows the dp4a kernels.
 cudaError_t launch_gemv(const Ctx& c, const GemvArgs& a, int epi, int rows, cudaStream_t st);
+// The integer-MMA GEMV (gemv_mma.cu) for passes of up to mb in {2, 4, 8} rows: whether it takes a
+// pass of mb rows of this product, and its launch (one launch per pass).
+bool gemv_mma_ok(const GemvArgs& a, int mb);
+cudaError_t launch_gemv_mma(const Ctx& c, const GemvArgs& a, int epi, int mb, int rows, cudaStream_t st);
+cudaError_t configure_gemv_mma();
 cudaError_t launch_embed(const Ctx& c, cudaStream_t st);
 cudaError_t launch_attention(const Ctx& c, int layer, cudaStream_t st);
 cudaError_t launch_finish(const Ctx& c, cudaStream_t st);
